@@ -1,0 +1,385 @@
+// Flash attention forward for sm_100a (head_dim 128, bf16 in/out, fp32 softmax).
+//
+// One CTA per (128-query tile, head, batch).  Warp roles:
+//   warp 0      TMA producer: Q once, then K_j / V_j tiles into a 2-stage ring
+//   warp 1      MMA issuer: S_j = Q K_j^T into a double-buffered TMEM tile,
+//               O += P_{j-1} V_{j-1} (V read as an MN-major operand)
+//   warps 2..5  softmax: one query row per thread; S from TMEM, running max in
+//               log2 units, P = exp2(s - m) written to a 128B-swizzled smem
+//               tile for the PV MMA.  O is rescaled in TMEM only when the max
+//               grew by more than 2^8 (the stale max keeps P <= 256, exact
+//               after the final 1/l), then normalised and stored.
+// Optional per-batch key window [kv_lo, kv_hi) and natural-log LSE output
+// (for ring / context-parallel merges).
+//
+// Reference parity: attention contract of difflet/ops/attention.py:4-128 and
+// the CUDA SDPA path difflet/backends/cuda/ops_impl/attention.py:41-86 (scale
+// given explicitly, bounded key windows as in
+// difflet/backends/neuron/ops_impl/attention.py:212-249, LSE as in :280-301).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+using namespace dfl;
+
+constexpr int kBM = 128;   // queries per CTA
+constexpr int kBN = 128;   // keys per tile
+constexpr int kD = 128;    // head dim
+constexpr int kNS = 2;     // K/V ring depth
+constexpr int kThreads = 192;
+constexpr int kTileBytes = kBM * kD * 2;  // 32 KB (two 16 KB swizzle chunks)
+constexpr int kChunk = 16384;
+
+struct AttnSmem {
+  static constexpr int kQ = 0;
+  static constexpr int kP = kQ + kTileBytes;
+  static constexpr int kK = kP + kTileBytes;
+  static constexpr int kV = kK + kNS * kTileBytes;
+  static constexpr int kBar = kV + kNS * kTileBytes;
+  // q_full, k_full[NS], v_full[NS], k_empty[NS], v_empty[NS], s_full[2], s_empty[2],
+  // p_full, pv_done, o_full
+  static constexpr int kNumBars = 1 + 4 * kNS + 4 + 3;
+  static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
+};
+
+// 2^x on the SFU (PTX ex2.approx.ftz.f32); inputs here are <= 8 after the max shift.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+struct AttnParams {
+  long long o_bs, o_hs, o_ss;
+  float* lse;
+  int B, H, Sq, Sk;
+  float scale_log2;
+  const int* kv_lo;
+  const int* kv_hi;
+  __nv_bfloat16* o;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, AttnParams p, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnSmem::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + kNS;
+  uint64_t* k_empty = v_full + kNS;
+  uint64_t* v_empty = k_empty + kNS;
+  uint64_t* s_full = v_empty + kNS;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* o_full = pv_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AttnSmem::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qt * kBM;
+  const int lo = p.kv_lo ? max(0, p.kv_lo[b]) : 0;
+  const int hi = p.kv_hi ? min(p.Sk, p.kv_hi[b]) : p.Sk;
+  const int t_first = lo / kBN;
+  const int n_tiles = hi > lo ? (hi + kBN - 1) / kBN - t_first : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < AttnSmem::kNumBars; ++i) {
+      uint64_t* bar = &bars[i];
+      const bool softmax_arrivals = (bar == s_empty) || (bar == s_empty + 1) || (bar == p_full);
+      mbar_init(bar, softmax_arrivals ? 128 : 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_shared();
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_o = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0 && n_tiles > 0) {
+      uint8_t* sq = smem + AttnSmem::kQ;
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      // Q: two 64-wide d chunks
+      for (int c = 0; c < 2; ++c) {
+        asm volatile(
+            "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(sq + c * kChunk)),
+            "l"(reinterpret_cast<uint64_t>(&tq)), "r"(smem_u32(q_full)), "r"(c * 64), "r"(q0),
+            "r"(h), "r"(b)
+            : "memory");
+      }
+      bool issued_k[kNS] = {false, false}, issued_v[kNS] = {false, false};
+      uint32_t par_k[kNS] = {0, 0}, par_v[kNS] = {0, 0};
+      bool ok = true;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % kNS;
+        const uint32_t par = (j / kNS) & 1;
+        const int k0 = (t_first + j) * kBN;
+        for (int which = 0; which < 2; ++which) {
+          uint64_t* empty = which == 0 ? &k_empty[st] : &v_empty[st];
+          uint64_t* full = which == 0 ? &k_full[st] : &v_full[st];
+          if (!mbar_wait(empty, par ^ 1u, err, kKidAttn, 100 + which, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + (which == 0 ? AttnSmem::kK : AttnSmem::kV) + st * kTileBytes;
+          const CUtensorMap* map = which == 0 ? &tk : &tv;
+          mbar_arrive_expect_tx(full, kTileBytes);
+          for (int c = 0; c < 2; ++c) {
+            asm volatile(
+                "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst + c * kChunk)),
+                "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(full)), "r"(c * 64), "r"(k0),
+                "r"(h), "r"(b)
+                : "memory");
+          }
+          if (which == 0) issued_k[st] = true, par_k[st] = par;
+          else issued_v[st] = true, par_v[st] = par;
+        }
+      }
+      if (!ok) {
+        mbar_wait(q_full, 0, nullptr, 0, 0, nullptr, 200000000LL);
+        for (int s = 0; s < kNS; ++s) {
+          if (issued_k[s]) mbar_wait(&k_full[s], par_k[s], nullptr, 0, 0, nullptr, 200000000LL);
+          if (issued_v[s]) mbar_wait(&v_full[s], par_v[s], nullptr, 0, 0, nullptr, 200000000LL);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_qk = make_idesc_bf16_f32(kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_pv = make_idesc_bf16_f32(kBM, kD, 0, 1);
+      const uint32_t q_addr = smem_u32(smem + AttnSmem::kQ);
+      const uint32_t p_addr = smem_u32(smem + AttnSmem::kP);
+      bool ok = mbar_wait(q_full, 0, err, kKidAttn, 110, abort_flag);
+      auto issue_pv = [&](int jj) -> bool {
+        const int st = jj % kNS;
+        if (!mbar_wait(p_full, jj & 1, err, kKidAttn, 111, abort_flag)) return false;
+        if (!mbar_wait(&v_full[st], (jj / kNS) & 1, err, kKidAttn, 112, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + AttnSmem::kV + st * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          uint64_t ad = make_sdesc_sw128(p_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
+          uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, kChunk, 1024);
+          umma_f16_ss(tmem_o, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(pv_done);
+        umma_commit(&v_empty[st]);
+        return true;
+      };
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % kNS;
+        const int sb = j & 1;
+        if (!mbar_wait(&k_full[st], (j / kNS) & 1, err, kKidAttn, 113, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1u, err, kKidAttn, 114, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + AttnSmem::kK + st * kTileBytes);
+        const uint32_t s_tmem = tmem + sb * 128;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          uint64_t ad = make_sdesc_sw128(q_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
+          uint64_t bd = make_sdesc_sw128(k_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
+          umma_f16_ss(s_tmem, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[st]);
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && issue_pv(n_tiles - 1)) umma_commit(o_full);
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue ----------------
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;  // TMEM lane == query row within the tile
+    const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
+    float m = -INFINITY;  // running max (log2 domain)
+    float l = 0.f;
+    bool ok = true;
+    uint8_t* p_smem = smem + AttnSmem::kP;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, err, kKidAttn, 120, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]);
+        tmem_ld_32x32b_x32(tmem + lane_base + sb * 128 + c * 32, chunk);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+      const int k0 = (t_first + j) * kBN;
+      const bool edge = (k0 < lo) || (k0 + kBN > hi);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float v = s[c] * p.scale_log2;
+        if (edge) {
+          int key = k0 + c;
+          if (key < lo || key >= hi) v = -INFINITY;
+        }
+        s[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m, mx);
+      // Rescale decision is warp-uniform (tcgen05.ld/st are warp-collective).
+      const bool need = (j > 0) && __any_sync(0xffffffffu, m_new > m + 8.0f);
+      const float m_old = m;
+      if (j == 0 || need) m = m_new;
+      const float m_use = (m == -INFINITY) ? 0.f : m;
+      // exp2 into packed bf16 registers before waiting on the previous PV, so
+      // the exponentials overlap the tensor-core work.
+      uint32_t pk[64];
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        float e0 = fast_exp2(s[2 * c] - m_use);
+        float e1 = fast_exp2(s[2 * c + 1] - m_use);
+        rs += e0 + e1;
+        pk[c] = pack_bf16x2(e0, e1);
+      }
+      if (j > 0) {
+        // PV_{j-1} must finish before P is overwritten or O is rescaled.
+        if (!mbar_wait(pv_done, (j - 1) & 1, err, kKidAttn, 121, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        if (need) {
+          const float f = (m_old == -INFINITY) ? 0.f : fast_exp2(m_old - m);
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            uint32_t o_raw[16];
+            tmem_ld_32x32b_x16(tmem_o + lane_base + c * 16, o_raw);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * f);
+            tmem_st_32x32b_x16(tmem_o + lane_base + c * 16, o_raw);
+          }
+          tmem_wait_st();
+          l *= f;
+        }
+      }
+      // P -> smem, 128B swizzle: 16B unit u of row r sits at (u ^ (r & 7)) * 16
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint8_t* rowp = p_smem + c * kChunk + row * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int b0 = c * 32 + u * 4;
+          uint4 w = make_uint4(pk[b0], pk[b0 + 1], pk[b0 + 2], pk[b0 + 3]);
+          *reinterpret_cast<uint4*>(rowp + ((u ^ (row & 7)) * 16)) = w;
+        }
+      }
+      l += rs;
+      fence_proxy_async_shared();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ---------------- epilogue ----------------
+    const int qrow = q0 + row;
+    if (ok && n_tiles > 0 && mbar_wait(o_full, 0, err, kKidAttn, 122, abort_flag)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* op = p.o + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)qrow * p.o_ss;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o_raw[32];
+        tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o_raw);
+        tmem_wait_ld();
+        if (qrow < p.Sq) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o_raw[8 * q + 0]) * inv, __uint_as_float(o_raw[8 * q + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o_raw[8 * q + 2]) * inv, __uint_as_float(o_raw[8 * q + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o_raw[8 * q + 4]) * inv, __uint_as_float(o_raw[8 * q + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o_raw[8 * q + 6]) * inv, __uint_as_float(o_raw[8 * q + 7]) * inv);
+            reinterpret_cast<uint4*>(op + c * 32)[q] = w;
+          }
+        }
+      }
+      if (p.lse && qrow < p.Sq)
+        p.lse[((long long)b * p.H + h) * p.Sq + qrow] =
+            l > 0.f ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+    } else if (n_tiles == 0 && qrow < p.Sq) {
+      __nv_bfloat16* op = p.o + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)qrow * p.o_ss;
+      for (int d = 0; d < kD; ++d) op[d] = __float2bfloat16(0.f);
+      if (p.lse) p.lse[((long long)b * p.H + h) * p.Sq + qrow] = -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+int make_tmap_4d(CUtensorMap* map, const void* base, long long S, int H, int B, long long ss,
+                 long long hs, long long bs) {
+  dfl_host::EncodeTiledFn fn = dfl_host::get_encode_tiled();
+  if (!fn) return 999;
+  cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ss * 2, (cuuint64_t)hs * 2, (cuuint64_t)bs * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace
+
+extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
+  if (a->dh != kD) return -2;
+  if (a->B <= 0 || a->H <= 0 || a->Sq <= 0 || a->Sk <= 0) return -3;
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->o)) return -4;
+  if ((a->q_ss | a->q_hs | a->q_bs | a->k_ss | a->k_hs | a->k_bs | a->v_ss | a->v_hs | a->v_bs |
+       a->o_ss) % 8)
+    return -5;
+  CUtensorMap tq, tk, tv;
+  int rc = make_tmap_4d(&tq, a->q, a->Sq, a->H, a->B, a->q_ss, a->q_hs, a->q_bs);
+  if (rc) return 1000 + rc;
+  rc = make_tmap_4d(&tk, a->k, a->Sk, a->H, a->B, a->k_ss, a->k_hs, a->k_bs);
+  if (rc) return 2000 + rc;
+  rc = make_tmap_4d(&tv, a->v, a->Sk, a->H, a->B, a->v_ss, a->v_hs, a->v_bs);
+  if (rc) return 3000 + rc;
+  AttnParams p;
+  p.o_bs = a->o_bs;
+  p.o_hs = a->o_hs;
+  p.o_ss = a->o_ss;
+  p.lse = a->lse;
+  p.B = a->B;
+  p.H = a->H;
+  p.Sq = a->Sq;
+  p.Sk = a->Sk;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.kv_lo = a->kv_lo;
+  p.kv_hi = a->kv_hi;
+  p.o = reinterpret_cast<__nv_bfloat16*>(a->o);
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnSmem::kTotal);
+    if (e != cudaSuccess) return (int)e;
+    attr = true;
+  }
+  dim3 grid((a->Sq + kBM - 1) / kBM, a->H, a->B);
+  attn_fwd_kernel<<<grid, kThreads, AttnSmem::kTotal, stream>>>(tq, tk, tv, p, a->err);
+  return (int)cudaGetLastError();
+}

@@ -1,0 +1,322 @@
+// torch bindings for the difflet_b200 sm_100a kernels.
+//
+// The kernels live in torch-free .cu translation units behind the C interface
+// in kernels.h; this file only validates tensors, picks strides and streams,
+// and forwards.  Every entry point raises on a non-zero launcher status.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "kernels.h"
+
+namespace {
+
+#define DFL_CHECK_RC(rc, what) TORCH_CHECK((rc) == 0, what, " launch failed with status ", (rc))
+
+void check_bf16_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+}
+
+void check_rowmajor(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have a unit inner stride");
+}
+
+// Per-device 4-int error word (see common.cuh).
+at::Tensor& error_buffer(int device) {
+  static at::Tensor bufs[16];
+  TORCH_CHECK(device >= 0 && device < 16, "device index out of range");
+  if (!bufs[device].defined()) {
+    bufs[device] = at::zeros({4}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
+  }
+  return bufs[device];
+}
+
+int* err_ptr() {
+  int dev = c10::cuda::current_device();
+  return error_buffer(dev).data_ptr<int>();
+}
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+const void* opt_ptr(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
+}
+
+// ---------------------------------------------------------------------------
+at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at::Tensor>& bias,
+                c10::optional<at::Tensor> out, int64_t epi, int64_t act_lo, int64_t act_hi,
+                const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
+                const c10::optional<at::Tensor>& resid, double alpha, bool out_f32) {
+  check_bf16_cuda(A, "A");
+  check_bf16_cuda(B, "B");
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  TORCH_CHECK(A.size(1) == B.size(1), "K mismatch: A ", A.sizes(), " B ", B.sizes());
+  const c10::cuda::CUDAGuard guard(A.device());
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  at::Tensor D;
+  if (out.has_value() && out->defined()) {
+    D = *out;
+    check_rowmajor(D, "out");
+    TORCH_CHECK(D.size(0) == M && D.size(1) == N, "out shape mismatch");
+    TORCH_CHECK(D.scalar_type() == (out_f32 ? at::kFloat : at::kBFloat16), "out dtype mismatch");
+  } else {
+    D = at::empty({M, N}, A.options().dtype(out_f32 ? at::kFloat : at::kBFloat16));
+  }
+  GemmArgs a{};
+  a.A = A.data_ptr();
+  a.B = B.data_ptr();
+  a.D = D.data_ptr();
+  a.lda = A.stride(0);
+  a.ldb = B.stride(0);
+  a.ldd = D.stride(0);
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.out_f32 = out_f32 ? 1 : 0;
+  if (bias.has_value() && bias->defined()) {
+    check_bf16_cuda(*bias, "bias");
+    TORCH_CHECK(bias->numel() == N && bias->is_contiguous(), "bias must be contiguous [N]");
+    a.bias = bias->data_ptr();
+  }
+  a.epi = (int)epi;
+  a.act_lo = (int)act_lo;
+  a.act_hi = act_hi < 0 ? (int)N : (int)act_hi;
+  if (epi == kEpiGateResid) {
+    TORCH_CHECK(gate.has_value() && resid.has_value(), "gate/resid required");
+    TORCH_CHECK(gate->scalar_type() == at::kFloat, "gate must be float32");
+    TORCH_CHECK(gate->dim() == 2 && gate->stride(1) == 1 && gate->size(1) >= N, "gate must be [B, >=N]");
+    check_bf16_cuda(*resid, "resid");
+    check_rowmajor(*resid, "resid");
+    a.gate = gate->data_ptr<float>();
+    a.gate_bstride = gate->stride(0);
+    a.resid = resid->data_ptr();
+    a.ldr = resid->stride(0);
+    a.rows_per_batch = (int)(rows_per_batch > 0 ? rows_per_batch : M);
+  }
+  a.alpha = (float)alpha;
+  a.err = err_ptr();
+  int rc = dfl_gemm_bf16(&a, cur_stream());
+  DFL_CHECK_RC(rc, "gemm");
+  return D;
+}
+
+at::Tensor ln_modulate(const at::Tensor& x, c10::optional<at::Tensor> out,
+                       const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b,
+                       const c10::optional<at::Tensor>& shift, const c10::optional<at::Tensor>& scale,
+                       int64_t rows_per_batch, double eps, bool rms) {
+  check_bf16_cuda(x, "x");
+  check_rowmajor(x, "x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor y = (out.has_value() && out->defined()) ? *out : at::empty_like(x);
+  check_rowmajor(y, "out");
+  LnModArgs a{};
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.y = y.data_ptr();
+  a.ldy = y.stride(0);
+  a.w = opt_ptr(w);
+  a.b = opt_ptr(b);
+  long long bstride = 0;
+  if (shift.has_value() && shift->defined()) {
+    TORCH_CHECK(shift->scalar_type() == at::kFloat && shift->dim() == 2 && shift->stride(1) == 1, "shift must be f32 [B, D]");
+    a.shift = shift->data_ptr<float>();
+    bstride = shift->stride(0);
+  }
+  if (scale.has_value() && scale->defined()) {
+    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->dim() == 2 && scale->stride(1) == 1, "scale must be f32 [B, D]");
+    a.scale = scale->data_ptr<float>();
+    TORCH_CHECK(bstride == 0 || bstride == scale->stride(0), "shift/scale batch strides differ");
+    bstride = scale->stride(0);
+  }
+  a.mod_bstride = bstride;
+  a.rows_per_batch = (int)(rows_per_batch > 0 ? rows_per_batch : x.size(0));
+  a.M = (int)x.size(0);
+  a.D = (int)x.size(1);
+  a.eps = (float)eps;
+  a.rms = rms ? 1 : 0;
+  DFL_CHECK_RC(dfl_ln_modulate(&a, cur_stream()), "ln_modulate");
+  return y;
+}
+
+void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_off, int64_t S_src,
+                 int64_t H, int64_t dh, int64_t norm_mode, const c10::optional<at::Tensor>& wq,
+                 const c10::optional<at::Tensor>& wk, double eps,
+                 const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t,
+                 int64_t rope_pos_off, bool rope_half, int64_t heads_per_rank,
+                 std::vector<int64_t> q_dst, std::vector<int64_t> k_dst, std::vector<int64_t> v_dst,
+                 int64_t S_dst, int64_t seq_off, bool out_token_major) {
+  check_bf16_cuda(qkv, "qkv");
+  check_rowmajor(qkv, "qkv");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const int world = (int)q_dst.size();
+  TORCH_CHECK(world >= 1 && world <= DFL_MAX_PEERS, "1..8 destinations");
+  TORCH_CHECK(k_dst.size() == q_dst.size() && v_dst.size() == q_dst.size(), "dst tables differ");
+  QkvScatterArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.ld = qkv.stride(0);
+  a.q_off = (int)q_off;
+  a.k_off = (int)k_off;
+  a.v_off = (int)v_off;
+  a.rows = (int)qkv.size(0);
+  a.S_src = (int)S_src;
+  a.H = (int)H;
+  a.dh = (int)dh;
+  a.norm_mode = (int)norm_mode;
+  a.wq = opt_ptr(wq);
+  a.wk = opt_ptr(wk);
+  a.eps = (float)eps;
+  if (cos_t.has_value() && cos_t->defined()) {
+    TORCH_CHECK(cos_t->scalar_type() == at::kFloat && cos_t->is_contiguous(), "cos must be f32 contiguous");
+    TORCH_CHECK(sin_t.has_value() && sin_t->scalar_type() == at::kFloat && sin_t->is_contiguous(), "sin must be f32 contiguous");
+    a.cos_t = cos_t->data_ptr<float>();
+    a.sin_t = sin_t->data_ptr<float>();
+  }
+  a.rope_pos_off = (int)rope_pos_off;
+  a.rope_half = rope_half ? 1 : 0;
+  a.world = world;
+  a.heads_per_rank = (int)heads_per_rank;
+  for (int r = 0; r < world; ++r) {
+    a.q_dst[r] = reinterpret_cast<void*>(q_dst[r]);
+    a.k_dst[r] = reinterpret_cast<void*>(k_dst[r]);
+    a.v_dst[r] = reinterpret_cast<void*>(v_dst[r]);
+  }
+  a.S_dst = (int)S_dst;
+  a.seq_off = (int)seq_off;
+  a.out_token_major = out_token_major ? 1 : 0;
+  DFL_CHECK_RC(dfl_qkv_scatter(&a, cur_stream()), "qkv_scatter");
+}
+
+at::Tensor gemv(const at::Tensor& W, const at::Tensor& x, const c10::optional<at::Tensor>& bias,
+                c10::optional<at::Tensor> out, bool silu_in, bool silu_out) {
+  check_bf16_cuda(W, "W");
+  check_rowmajor(W, "W");
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.dim() == 2 && x.is_contiguous(), "x must be f32 [B, K]");
+  TORCH_CHECK(x.size(1) == W.size(1), "K mismatch");
+  const c10::cuda::CUDAGuard guard(W.device());
+  at::Tensor y = (out.has_value() && out->defined()) ? *out
+                                                     : at::empty({x.size(0), W.size(0)}, x.options());
+  TORCH_CHECK(y.scalar_type() == at::kFloat && y.dim() == 2 && y.stride(1) == 1, "out must be f32 [B, N]");
+  GemvArgs a{};
+  a.W = W.data_ptr();
+  a.ldw = W.stride(0);
+  a.x = x.data_ptr<float>();
+  a.batch = (int)x.size(0);
+  a.bias = opt_ptr(bias);
+  a.y = y.data_ptr<float>();
+  a.ldy = y.stride(0);
+  a.N = (int)W.size(0);
+  a.K = (int)W.size(1);
+  a.silu_in = silu_in ? 1 : 0;
+  a.silu_out = silu_out ? 1 : 0;
+  DFL_CHECK_RC(dfl_gemv(&a, cur_stream()), "gemv");
+  return y;
+}
+
+void euler_step(at::Tensor x32, const c10::optional<at::Tensor>& x16, const at::Tensor& v,
+                const c10::optional<at::Tensor>& cond, double dt, double guidance) {
+  TORCH_CHECK(x32.scalar_type() == at::kFloat && x32.is_contiguous(), "x32 must be f32 contiguous");
+  check_bf16_cuda(v, "v");
+  TORCH_CHECK(v.is_contiguous() && v.numel() == x32.numel(), "v must match x32");
+  const c10::cuda::CUDAGuard guard(x32.device());
+  SchedArgs a{};
+  a.x32 = x32.data_ptr<float>();
+  a.x16 = nullptr;
+  if (x16.has_value() && x16->defined()) {
+    check_bf16_cuda(*x16, "x16");
+    TORCH_CHECK(x16->is_contiguous() && x16->numel() == x32.numel(), "x16 must match x32");
+    a.x16 = x16->data_ptr();
+  }
+  a.v = v.data_ptr();
+  a.cond = nullptr;
+  if (cond.has_value() && cond->defined()) {
+    check_bf16_cuda(*cond, "cond");
+    TORCH_CHECK(cond->is_contiguous() && cond->numel() == x32.numel(), "cond must match x32");
+    a.cond = cond->data_ptr();
+  }
+  a.n = x32.numel();
+  a.dt = (float)dt;
+  a.guidance = (float)guidance;
+  DFL_CHECK_RC(dfl_euler_step(&a, cur_stream()), "euler_step");
+}
+
+at::Tensor timestep_embed(const at::Tensor& t, int64_t dim, double max_period, bool flip_sin_to_cos,
+                          double downscale_freq_shift, double scale) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.dim() == 1 && t.is_contiguous(), "t must be f32 [B]");
+  const c10::cuda::CUDAGuard guard(t.device());
+  at::Tensor out = at::empty({t.size(0), dim}, t.options());
+  int rc = dfl_timestep_embed(t.data_ptr<float>(), (int)t.size(0), (int)dim, (float)max_period,
+                              flip_sin_to_cos ? 1 : 0, (float)downscale_freq_shift, (float)scale,
+                              out.data_ptr<float>(), cur_stream());
+  DFL_CHECK_RC(rc, "timestep_embed");
+  return out;
+}
+
+// q, k, v: [B, H, S, dh] views (any strides with unit inner stride).
+at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
+                     c10::optional<at::Tensor> out, const c10::optional<at::Tensor>& lse,
+                     const c10::optional<at::Tensor>& kv_lo, const c10::optional<at::Tensor>& kv_hi) {
+  check_bf16_cuda(q, "q");
+  check_bf16_cuda(k, "k");
+  check_bf16_cuda(v, "v");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "q/k/v must be [B, H, S, dh]");
+  TORCH_CHECK(q.stride(3) == 1 && k.stride(3) == 1 && v.stride(3) == 1, "unit inner stride required");
+  const c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor o = (out.has_value() && out->defined()) ? *out : at::empty_like(q);
+  TORCH_CHECK(o.dim() == 4 && o.stride(3) == 1, "out must be [B, H, S, dh] with unit inner stride");
+  AttnArgs a{};
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.o = o.data_ptr();
+  a.q_bs = q.stride(0); a.q_hs = q.stride(1); a.q_ss = q.stride(2);
+  a.k_bs = k.stride(0); a.k_hs = k.stride(1); a.k_ss = k.stride(2);
+  a.v_bs = v.stride(0); a.v_hs = v.stride(1); a.v_ss = v.stride(2);
+  a.o_bs = o.stride(0); a.o_hs = o.stride(1); a.o_ss = o.stride(2);
+  a.B = (int)q.size(0);
+  a.H = (int)q.size(1);
+  a.Sq = (int)q.size(2);
+  a.Sk = (int)k.size(2);
+  a.dh = (int)q.size(3);
+  a.scale = (float)scale;
+  if (lse.has_value() && lse->defined()) {
+    TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->is_contiguous(), "lse must be f32 [B, H, Sq]");
+    a.lse = lse->data_ptr<float>();
+  }
+  if (kv_lo.has_value() && kv_lo->defined()) a.kv_lo = kv_lo->data_ptr<int>();
+  if (kv_hi.has_value() && kv_hi->defined()) a.kv_hi = kv_hi->data_ptr<int>();
+  a.err = err_ptr();
+  DFL_CHECK_RC(dfl_attention(&a, cur_stream()), "attention");
+  return o;
+}
+
+at::Tensor error_word(int64_t device) { return error_buffer((int)device); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "difflet_b200 native sm_100a kernels";
+  m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("B"),
+        py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,
+        py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),
+        py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("alpha") = 1.0,
+        py::arg("out_f32") = false);
+  m.def("ln_modulate", &ln_modulate, py::arg("x"), py::arg("out") = py::none(),
+        py::arg("w") = py::none(), py::arg("b") = py::none(), py::arg("shift") = py::none(),
+        py::arg("scale") = py::none(), py::arg("rows_per_batch") = 0, py::arg("eps") = 1e-6,
+        py::arg("rms") = false);
+  m.def("qkv_scatter", &qkv_scatter);
+  m.def("gemv", &gemv, py::arg("W"), py::arg("x"), py::arg("bias") = py::none(),
+        py::arg("out") = py::none(), py::arg("silu_in") = false, py::arg("silu_out") = false);
+  m.def("euler_step", &euler_step, py::arg("x32"), py::arg("x16"), py::arg("v"),
+        py::arg("cond") = py::none(), py::arg("dt") = 0.0, py::arg("guidance") = 1.0);
+  m.def("timestep_embed", &timestep_embed);
+  m.def("attention", &attention, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"),
+        py::arg("out") = py::none(), py::arg("lse") = py::none(), py::arg("kv_lo") = py::none(),
+        py::arg("kv_hi") = py::none());
+  m.def("error_word", &error_word);
+}

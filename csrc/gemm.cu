@@ -1,0 +1,458 @@
+// Persistent tcgen05 GEMM for sm_100a:  D[M,N] = epi(A[M,K] . B[N,K]^T + bias)
+//
+// A is the activation (row-major, K contiguous), B is an nn.Linear weight
+// ([out, in], K contiguous): both operands are K-major, bf16, fp32 accumulate
+// in tensor memory.  One CTA per SM, warp-specialised:
+//   warp 0      TMA producer (one lane): A/B tiles -> smem ring (128B swizzle)
+//   warp 1      MMA issuer (one lane) + TMEM owner; tcgen05.mma 128xBNx16
+//   warps 2..5  epilogue: tcgen05.ld the accumulator, fuse bias, GELU-tanh /
+//               SiLU on a column window, or residual + gate * y, store bf16/f32
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the main loop of tile i+1.
+//
+// Reference parity: every projection that the reference runs through
+// F.linear (difflet/backends/_torch_megatron/linear.py:123,193), the fused
+// GELU of NeuronGELU (difflet/layers/activations.py:62-65) and the gated
+// residual of the FLUX blocks (difflet/models/flux/modeling_flux.py:712,
+// 721-729, 844-867).
+#include <cstdio>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+using namespace dfl;
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;  // tile raster: 16 M-blocks per group for L2 reuse
+
+struct EpiParams {
+  void* D;
+  long long ldd;
+  const __nv_bfloat16* bias;
+  int act_lo, act_hi;
+  const float* gate;
+  long long gate_bstride;
+  int rows_per_batch;
+  const __nv_bfloat16* resid;
+  long long ldr;
+  float alpha;
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], then tmem addr + abort flag
+  static constexpr int kTotal = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;  // + align slack
+};
+
+DFL_DEVICE void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  int group_tiles = kGroupM * num_n;
+  int g = t / group_tiles;
+  int first_m = g * kGroupM;
+  int gm = min(kGroupM, num_m - first_m);
+  int r = t - g * group_tiles;
+  mb = first_m + (r % gm);
+  nb = r / gm;
+}
+
+template <int EPI, bool OUT_F32>
+DFL_DEVICE void epilogue_chunk(const uint32_t (&r)[32], int row, int col0, int M, int N,
+                               const EpiParams& p) {
+  if (row >= M) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+  const bool full = (col0 + 32 <= N);
+  if (p.bias != nullptr) {
+    if (full) {
+      const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w = __ldg(b4 + q);
+        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float2 f = unpack_bf16x2(ws[h]);
+          v[q * 8 + 2 * h] += f.x;
+          v[q * 8 + 2 * h + 1] += f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] += __bfloat162float(p.bias[col0 + j]);
+    }
+  }
+  if constexpr (EPI == kEpiGelu || EPI == kEpiSilu) {
+    if (col0 + 32 > p.act_lo && col0 < p.act_hi) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        int c = col0 + j;
+        if (c >= p.act_lo && c < p.act_hi) v[j] = (EPI == kEpiGelu) ? gelu_tanh(v[j]) : silu(v[j]);
+      }
+    }
+  }
+  if constexpr (EPI == kEpiGateResid) {
+    int b = row / p.rows_per_batch;
+    const float* g = p.gate + (long long)b * p.gate_bstride;
+    const __nv_bfloat16* rs = p.resid + (long long)row * p.ldr;
+    if (full) {
+      const float4* g4 = reinterpret_cast<const float4*>(g + col0);
+      const uint4* r4 = reinterpret_cast<const uint4*>(rs + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float4 ga = __ldg(g4 + 2 * q);
+        float4 gb = __ldg(g4 + 2 * q + 1);
+        float gs[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        uint4 rw = r4[q];
+        uint32_t rr[4] = {rw.x, rw.y, rw.z, rw.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float2 rf = unpack_bf16x2(rr[h]);
+          v[q * 8 + 2 * h] = rf.x + gs[2 * h] * v[q * 8 + 2 * h];
+          v[q * 8 + 2 * h + 1] = rf.y + gs[2 * h + 1] * v[q * 8 + 2 * h + 1];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] = __bfloat162float(rs[col0 + j]) + g[col0 + j] * v[j];
+    }
+  }
+  if constexpr (OUT_F32) {
+    float* d = reinterpret_cast<float*>(p.D) + (long long)row * p.ldd + col0;
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(d)[q] =
+            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) d[j] = v[j];
+    }
+  } else {
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd + col0;
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+        w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+        w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+        w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+        reinterpret_cast<uint4*>(d)[q] = w;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) d[j] = __float2bfloat16(v[j]);
+    }
+  }
+}
+
+template <int BN, int STAGES, int EPI, bool OUT_F32>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                        const __grid_constant__ CUtensorMap tmap_b, int M, int N, int K,
+                        EpiParams ep, int* err) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzle atoms
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (K + BK - 1) / BK;
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_shared();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_parity[STAGES];
+      bool issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kKidGemm, 10 + stage, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
+          tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, mb * BM);
+          tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, nb * BN);
+          issued[stage] = true;
+          issued_parity[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: our own bulk copies must land before the CTA exits.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) mbar_wait(&full_bar[s], issued_parity[s], nullptr, 0, 0, nullptr, 200000000LL);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, err, kKidGemm, 20 + acc, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, err, kKidGemm, 30 + stage, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * S::kStageBytes);
+          const uint32_t b_addr = a_addr + S::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t ad = make_sdesc_sw128(a_addr + k * 32, 16, 1024);
+            uint64_t bd = make_sdesc_sw128(b_addr + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4)
+    const int sub = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, err, kKidGemm, 40 + acc, abort_flag)) break;
+      tc_fence_after();
+      const int row = mb * BM + sub * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = nb * BN + c * 32;
+        if (col0 >= N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, r);
+        tmem_wait_ld();
+        epilogue_chunk<EPI, OUT_F32>(r, row, col0, M, N, ep);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+template <int BN, int STAGES, int EPI, bool OUT_F32>
+int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                   const EpiParams& ep, int* err, cudaStream_t stream, int device) {
+  using S = Smem<BN, STAGES>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI, OUT_F32>;
+  static bool attr_set[16] = {false};
+  if (!attr_set[device & 15]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    if (e != cudaSuccess) return (int)e;
+    attr_set[device & 15] = true;
+  }
+  int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  int grid = tiles < dfl_host::num_sms(device) ? tiles : dfl_host::num_sms(device);
+  kern<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, M, N, K, ep, err);
+  return (int)cudaGetLastError();
+}
+
+template <int BN, int STAGES>
+int dispatch_epi(int epi, bool out_f32, const CUtensorMap& ta, const CUtensorMap& tb, int M,
+                 int N, int K, const EpiParams& ep, int* err, cudaStream_t s, int dev) {
+  switch (epi) {
+    case kEpiNone:
+      return out_f32 ? launch_variant<BN, STAGES, kEpiNone, true>(ta, tb, M, N, K, ep, err, s, dev)
+                     : launch_variant<BN, STAGES, kEpiNone, false>(ta, tb, M, N, K, ep, err, s, dev);
+    case kEpiGelu:
+      return launch_variant<BN, STAGES, kEpiGelu, false>(ta, tb, M, N, K, ep, err, s, dev);
+    case kEpiSilu:
+      return launch_variant<BN, STAGES, kEpiSilu, false>(ta, tb, M, N, K, ep, err, s, dev);
+    case kEpiGateResid:
+      return launch_variant<BN, STAGES, kEpiGateResid, false>(ta, tb, M, N, K, ep, err, s, dev);
+    default:
+      return -1;
+  }
+}
+
+}  // namespace
+
+extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
+  // Host-side argument checks (TMA: 16-byte aligned bases and row strides).
+  if (a->M <= 0 || a->N <= 0 || a->K <= 0) return -2;
+  if ((reinterpret_cast<uintptr_t>(a->A) & 15) || (reinterpret_cast<uintptr_t>(a->B) & 15)) return -3;
+  if ((a->lda * 2) % 16 || (a->ldb * 2) % 16) return -4;
+  if (a->K % 8) return -5;
+  if (!a->out_f32 && ((a->ldd % 8) || (reinterpret_cast<uintptr_t>(a->D) & 15))) return -6;
+  if (a->out_f32 && ((a->ldd % 4) || (reinterpret_cast<uintptr_t>(a->D) & 15))) return -6;
+  if (a->bias && (reinterpret_cast<uintptr_t>(a->bias) & 15)) return -7;
+  if (a->epi == kEpiGateResid) {
+    if (!a->gate || !a->resid || a->rows_per_batch <= 0) return -8;
+    if ((reinterpret_cast<uintptr_t>(a->gate) & 15) || (reinterpret_cast<uintptr_t>(a->resid) & 15) ||
+        (a->ldr % 8) || (a->gate_bstride % 4))
+      return -8;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const bool wide = a->N >= 1024;
+  CUtensorMap ta, tb;
+  int rc = dfl_host::make_tmap_2d_bf16(&ta, a->A, a->K, a->M, a->lda, BK, BM, true);
+  if (rc) return 1000 + rc;
+  rc = dfl_host::make_tmap_2d_bf16(&tb, a->B, a->K, a->N, a->ldb, BK, wide ? 256 : 128, true);
+  if (rc) return 2000 + rc;
+  EpiParams ep;
+  ep.D = a->D;
+  ep.ldd = a->ldd;
+  ep.bias = reinterpret_cast<const __nv_bfloat16*>(a->bias);
+  ep.act_lo = a->act_lo;
+  ep.act_hi = a->act_hi;
+  ep.gate = a->gate;
+  ep.gate_bstride = a->gate_bstride;
+  ep.rows_per_batch = a->rows_per_batch > 0 ? a->rows_per_batch : a->M;
+  ep.resid = reinterpret_cast<const __nv_bfloat16*>(a->resid);
+  ep.ldr = a->ldr;
+  ep.alpha = a->alpha;
+  if (wide)
+    return dispatch_epi<256, 4>(a->epi, a->out_f32, ta, tb, a->M, a->N, a->K, ep, a->err, stream, dev);
+  return dispatch_epi<128, 6>(a->epi, a->out_f32, ta, tb, a->M, a->N, a->K, ep, a->err, stream, dev);
+}
+
+// ---------------------------------------------------------------------------
+// Host helpers shared by every TMA user in this library.
+// ---------------------------------------------------------------------------
+namespace dfl_host {
+
+EncodeTiledFn get_encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                      uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                      bool swizzle128) {
+  EncodeTiledFn fn = get_encode_tiled();
+  if (!fn) return 999;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return (int)r;
+}
+
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                      uint64_t stride1_elems, uint64_t stride2_elems, uint32_t b0, uint32_t b1,
+                      uint32_t b2, bool swizzle128) {
+  EncodeTiledFn fn = get_encode_tiled();
+  if (!fn) return 999;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_elems * 2, stride2_elems * 2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return (int)r;
+}
+
+int num_sms(int device) {
+  static int cache[16] = {0};
+  int d = device & 15;
+  if (cache[d] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    cache[d] = n > 0 ? n : 148;
+  }
+  return cache[d];
+}
+
+}  // namespace dfl_host

@@ -1,0 +1,117 @@
+// C interface between the sm_100a kernels (plain CUDA translation units, no
+// torch headers) and the torch bindings.  Every launcher returns 0 on success
+// and a non-zero code otherwise; device-side failures land in `err` (see
+// common.cuh for the error-word protocol).
+#pragma once
+#include <cuda_runtime_api.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { kEpiNone = 0, kEpiGelu = 1, kEpiGateResid = 2, kEpiSilu = 3 };
+
+typedef struct GemmArgs {
+  const void* A;   // bf16 [M, K], row stride lda (elements)
+  const void* B;   // bf16 [N, K], row stride ldb
+  void* D;         // bf16 or f32 [M, N], row stride ldd
+  long long lda, ldb, ldd;
+  int M, N, K;
+  int out_f32;
+  const void* bias;  // bf16 [N] or NULL
+  int epi;           // kEpi*
+  int act_lo, act_hi;  // activation column window for GELU / SiLU
+  const float* gate;   // f32 [batch, gate_bstride] for kEpiGateResid
+  long long gate_bstride;
+  int rows_per_batch;
+  const void* resid;   // bf16 [M, ldr] (may alias D)
+  long long ldr;
+  float alpha;         // scales the accumulator before bias
+  int* err;
+} GemmArgs;
+
+int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream);
+
+// y = (LN(x) [* w + b]) [* (1 + scale[b]) + shift[b]]      (fp32 statistics)
+typedef struct LnModArgs {
+  const void* x; long long ldx;      // bf16 [M, D]
+  void* y; long long ldy;            // bf16 [M, D]
+  const void* w; const void* b;      // bf16 [D] affine or NULL
+  const float* shift; const float* scale;  // f32 [batch, mod_bstride] or NULL
+  long long mod_bstride;
+  int rows_per_batch;
+  int M, D;
+  float eps;
+  int rms;                           // 1: RMSNorm (no mean subtraction, no bias)
+} LnModArgs;
+int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream);
+
+// q/k RMSNorm + RoPE + scatter to head-major [B, H_local, S_dst, dh] buffers.
+// Source rows are tokens; destination tables hold one pointer per rank so the
+// same pass performs the Ulysses sequence->head all-to-all over NVLink stores.
+#define DFL_MAX_PEERS 8
+typedef struct QkvScatterArgs {
+  const void* qkv; long long ld;     // bf16 [rows, ld]
+  int q_off, k_off, v_off;           // column offsets of the q / k / v blocks
+  int rows, S_src;                   // rows = B * S_src
+  int H, dh;                         // heads in the source row, head dim
+  int norm_mode;                     // 0 none, 1 per-head RMS, 2 across-heads RMS
+  const void* wq; const void* wk;    // bf16 [dh] (mode 1) or [H*dh] (mode 2), may be NULL
+  float eps;
+  const float* cos_t; const float* sin_t;  // f32 [pos, dh/2] or NULL (no RoPE)
+  int rope_pos_off;                  // table row = rope_pos_off + s
+  int rope_half;                     // 0 interleaved pairs, 1 half-split
+  int world, heads_per_rank;
+  void* q_dst[DFL_MAX_PEERS]; void* k_dst[DFL_MAX_PEERS]; void* v_dst[DFL_MAX_PEERS];
+  int S_dst, seq_off;                // destination seq length / offset of row 0
+  int out_token_major;               // 1: dst is [B, S_dst, H_local*dh] instead
+} QkvScatterArgs;
+int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream);
+
+// y[b, n] = act_in(x[b, :]) . W[n, :] + bias[n]   (bf16 W, f32 x / y; batch <= 8)
+typedef struct GemvArgs {
+  const void* W; long long ldw;      // bf16 [N, K]
+  const float* x; int batch;         // f32 [batch, K]
+  const void* bias;                  // bf16 [N] or NULL
+  float* y; long long ldy;           // f32 [batch, ldy]
+  int N, K;
+  int silu_in;                       // apply SiLU to x first
+  int silu_out;                      // apply SiLU to y
+} GemvArgs;
+int dfl_gemv(const GemvArgs* a, cudaStream_t stream);
+
+// Flow-matching Euler with optional CFG combine:
+//   v = u + s (c - u)  (when cond != NULL), x32 += dt * v, x16 = bf16(x32)
+typedef struct SchedArgs {
+  float* x32; void* x16;             // f32 master latents, optional bf16 mirror
+  const void* v;                     // bf16 prediction (uncond when cond != NULL)
+  const void* cond;                  // bf16 cond prediction or NULL
+  long long n;
+  float dt, guidance;
+} SchedArgs;
+int dfl_euler_step(const SchedArgs* a, cudaStream_t stream);
+
+// Sinusoidal timestep features: out[b, :] = [cos(t f) | sin(t f)] (flip) or [sin | cos].
+int dfl_timestep_embed(const float* t, int batch, int dim, float max_period, int flip_sin_to_cos,
+                       float downscale_freq_shift, float scale, float* out, cudaStream_t stream);
+
+// Flash attention forward, bf16 in / bf16 out, fp32 softmax.
+typedef struct AttnArgs {
+  const void* q; const void* k; const void* v;  // [B, H, S, dh] (strides below)
+  void* o;                                      // output
+  long long q_bs, q_hs, q_ss;                   // element strides (batch, head, seq)
+  long long k_bs, k_hs, k_ss;
+  long long v_bs, v_hs, v_ss;
+  long long o_bs, o_hs, o_ss;
+  float* lse;                                   // f32 [B, H, Sq] natural-log LSE or NULL
+  int B, H, Sq, Sk, dh;
+  float scale;
+  const int* kv_lo; const int* kv_hi;           // per-batch key window [lo, hi) or NULL
+  int* err;
+} AttnArgs;
+int dfl_attention(const AttnArgs* a, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif

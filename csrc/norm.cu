@@ -1,0 +1,422 @@
+// Memory-bound fused kernels for sm_100a:
+//   * adaLN LayerNorm / RMSNorm with optional affine and (1 + scale) / shift
+//     modulation (fp32 statistics, one warp per row, 16-byte vector IO)
+//   * q/k RMSNorm (per head or across heads) + RoPE + scatter of q/k/v to a
+//     head-major layout; with a table of per-rank destination pointers the
+//     same pass is the Ulysses sequence->head all-to-all (NVLink stores)
+//   * GEMV for adaLN / timestep-embedding linears (M <= 8)
+//   * flow-matching Euler update with optional CFG combine
+//   * sinusoidal timestep features
+//
+// Reference parity: adaLN-Zero / Single / Continuous
+// (difflet/layers/normalization.py:38-190), q/k CustomRMSNorm + RoPE
+// (difflet/models/flux/modeling_flux.py:1083-1084,1249-1252;
+// difflet/backends/_torch_megatron/embeddings.py:13-33), Wan across-heads RMS
+// (difflet/models/wan/modeling_wan.py:564-590), Ulysses seq_to_heads
+// (difflet/backends/neuron/ops_impl/collectives.py:276-289), timestep
+// projection (difflet/layers/embeddings.py:247-420), Euler / CFG combine
+// (difflet/models/flux/pipeline.py:370-420).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+using namespace dfl;
+
+// ---------------------------------------------------------------------------
+// LayerNorm / RMSNorm + modulation.  One warp per row; D <= 32 * 8 * kMaxVec.
+// ---------------------------------------------------------------------------
+constexpr int kMaxVec = 24;  // 24 x 8 bf16 per lane -> D <= 6144
+
+template <int kMaxVec>
+__global__ void __launch_bounds__(256) ln_modulate_kernel(LnModArgs a) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (warp >= a.M) return;
+  const int row = warp;
+  const int nvec = a.D / 8;  // 16-byte vectors per row
+  const uint4* x4 = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) +
+                                                   (long long)row * a.ldx);
+  float xs[kMaxVec][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    int vi = lane + 32 * i;
+    if (vi < nvec) {
+      uint4 w = x4[vi];
+      uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float2 f = unpack_bf16x2(ws[h]);
+        xs[i][2 * h] = f.x;
+        xs[i][2 * h + 1] = f.y;
+        sum += f.x + f.y;
+      }
+    }
+  }
+  float mean = 0.f;
+  if (!a.rms) mean = warp_sum(sum) / (float)a.D;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    int vi = lane + 32 * i;
+    if (vi < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float d = xs[i][j] - mean;
+        sq += d * d;
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(sq) / (float)a.D + a.eps);
+  const int b = row / a.rows_per_batch;
+  const float* sh = a.shift ? a.shift + (long long)b * a.mod_bstride : nullptr;
+  const float* sc = a.scale ? a.scale + (long long)b * a.mod_bstride : nullptr;
+  const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(a.w);
+  const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(a.b);
+  uint4* y4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + (long long)row * a.ldy);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    int vi = lane + 32 * i;
+    if (vi < nvec) {
+      int c0 = vi * 8;
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (xs[i][j] - mean) * rstd;
+      if (w) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] *= __bfloat162float(w[c0 + j]);
+      }
+      if (bb) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += __bfloat162float(bb[c0 + j]);
+      }
+      if (sc) {
+        float4 s0 = *reinterpret_cast<const float4*>(sc + c0);
+        float4 s1 = *reinterpret_cast<const float4*>(sc + c0 + 4);
+        float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] *= (1.f + s[j]);
+      }
+      if (sh) {
+        float4 s0 = *reinterpret_cast<const float4*>(sh + c0);
+        float4 s1 = *reinterpret_cast<const float4*>(sh + c0 + 4);
+        float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += s[j];
+      }
+      uint4 out;
+      out.x = pack_bf16x2(o[0], o[1]);
+      out.y = pack_bf16x2(o[2], o[3]);
+      out.z = pack_bf16x2(o[4], o[5]);
+      out.w = pack_bf16x2(o[6], o[7]);
+      y4[vi] = out;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// q/k norm + RoPE + head-major scatter.  One block of 128 threads per token;
+// warp w handles heads w, w + 4, ...; lane holds DH/32 consecutive elements.
+// ---------------------------------------------------------------------------
+template <int DH>
+__device__ __forceinline__ void load_head(const __nv_bfloat16* src, int lane, float (&x)[DH / 32]) {
+  constexpr int E = DH / 32;
+  if constexpr (E == 4) {
+    uint2 w = *reinterpret_cast<const uint2*>(src + lane * 4);
+    float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y);
+    x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+  } else {
+    uint32_t w = *reinterpret_cast<const uint32_t*>(src + lane * 2);
+    float2 a = unpack_bf16x2(w);
+    x[0] = a.x; x[1] = a.y;
+  }
+}
+
+template <int DH>
+__device__ __forceinline__ void store_head(__nv_bfloat16* dst, int lane, const float (&x)[DH / 32]) {
+  constexpr int E = DH / 32;
+  if constexpr (E == 4) {
+    uint2 w;
+    w.x = pack_bf16x2(x[0], x[1]);
+    w.y = pack_bf16x2(x[2], x[3]);
+    *reinterpret_cast<uint2*>(dst + lane * 4) = w;
+  } else {
+    *reinterpret_cast<uint32_t*>(dst + lane * 2) = pack_bf16x2(x[0], x[1]);
+  }
+}
+
+template <int DH>
+__device__ __forceinline__ void rope_apply(float (&x)[DH / 32], int lane, const float* cos_row,
+                                           const float* sin_row, int half) {
+  constexpr int E = DH / 32;
+  if (!half) {
+    // interleaved pairs (2i, 2i+1) live in one lane
+#pragma unroll
+    for (int p = 0; p < E / 2; ++p) {
+      int fi = lane * (E / 2) + p;
+      float c = cos_row[fi], s = sin_row[fi];
+      float x0 = x[2 * p], x1 = x[2 * p + 1];
+      x[2 * p] = x0 * c - x1 * s;
+      x[2 * p + 1] = x1 * c + x0 * s;
+    }
+  } else {
+    // half-split: element i pairs with i + DH/2, which sits in lane ^ 16
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+      int i = lane * E + e;
+      int fi = i % (DH / 2);
+      float c = cos_row[fi], s = sin_row[fi];
+      x[e] = (i < DH / 2) ? (x[e] * c - other * s) : (x[e] * c + other * s);
+    }
+  }
+}
+
+template <int DH>
+__global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
+  constexpr int E = DH / 32;
+  const int row = blockIdx.x;
+  if (row >= a.rows) return;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int b = row / a.S_src;
+  const int s = row % a.S_src;
+  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + (long long)row * a.ld;
+  const int H_local = a.heads_per_rank;
+  const int dpos = a.seq_off + s;
+  const float* cos_row = a.cos_t ? a.cos_t + (long long)(a.rope_pos_off + s) * (DH / 2) : nullptr;
+  const float* sin_row = a.sin_t ? a.sin_t + (long long)(a.rope_pos_off + s) * (DH / 2) : nullptr;
+  __shared__ float red[2][4];
+
+  // Across-heads RMS (mode 2): sum of squares over the whole q (and k) row.
+  float rq = 1.f, rk = 1.f;
+  if (a.norm_mode == 2) {
+    float sq = 0.f, sk = 0.f;
+    for (int h = warp; h < a.H; h += 4) {
+      float xq[E], xk[E];
+      load_head<DH>(src + a.q_off + h * DH, lane, xq);
+      load_head<DH>(src + a.k_off + h * DH, lane, xk);
+#pragma unroll
+      for (int e = 0; e < E; ++e) sq += xq[e] * xq[e], sk += xk[e] * xk[e];
+    }
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    if (lane == 0) red[0][warp] = sq, red[1][warp] = sk;
+    __syncthreads();
+    float tq = red[0][0] + red[0][1] + red[0][2] + red[0][3];
+    float tk = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+    rq = rsqrtf(tq / (float)(a.H * DH) + a.eps);
+    rk = rsqrtf(tk / (float)(a.H * DH) + a.eps);
+  }
+
+  for (int h = warp; h < a.H; h += 4) {
+    const int r = h / H_local;
+    const int hl = h % H_local;
+    const long long dst_off =
+        a.out_token_major
+            ? ((long long)b * a.S_dst + dpos) * (long long)(H_local * DH) + (long long)hl * DH
+            : (((long long)b * H_local + hl) * a.S_dst + dpos) * DH;
+    // q and k
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      float x[E];
+      const int off = which == 0 ? a.q_off : a.k_off;
+      load_head<DH>(src + off + h * DH, lane, x);
+      const __nv_bfloat16* wn = reinterpret_cast<const __nv_bfloat16*>(which == 0 ? a.wq : a.wk);
+      if (a.norm_mode == 1) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+        float rr = rsqrtf(warp_sum(ss) / (float)DH + a.eps);
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] *= rr;
+        if (wn) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) x[e] *= __bfloat162float(wn[lane * E + e]);
+        }
+      } else if (a.norm_mode == 2) {
+        float rr = which == 0 ? rq : rk;
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] *= rr;
+        if (wn) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) x[e] *= __bfloat162float(wn[h * DH + lane * E + e]);
+        }
+      }
+      if (cos_row) rope_apply<DH>(x, lane, cos_row, sin_row, a.rope_half);
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(which == 0 ? a.q_dst[r] : a.k_dst[r]);
+      store_head<DH>(dst + dst_off, lane, x);
+    }
+    // v: plain copy into the destination layout
+    {
+      float x[E];
+      load_head<DH>(src + a.v_off + h * DH, lane, x);
+      store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.v_dst[r]) + dst_off, lane, x);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// GEMV: one warp per output row, x staged in shared memory (f32).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
+  extern __shared__ float xs[];  // [batch, K]
+  for (int i = threadIdx.x; i < a.batch * a.K; i += blockDim.x) {
+    float v = a.x[i];
+    xs[i] = a.silu_in ? silu(v) : v;
+  }
+  __syncthreads();
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x % 32;
+  const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  for (int n = blockIdx.x * warps + threadIdx.x / 32; n < a.N; n += gridDim.x * warps) {
+    const uint4* w4 = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.W) +
+                                                     (long long)n * a.ldw);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int v = lane; v < a.K / 8; v += 32) {
+      uint4 w = __ldg(w4 + v);
+      uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      float wf[8];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float2 f = unpack_bf16x2(ws[h]);
+        wf[2 * h] = f.x;
+        wf[2 * h + 1] = f.y;
+      }
+#pragma unroll
+      for (int bi = 0; bi < 8; ++bi) {
+        if (bi < a.batch) {
+          const float4* xr = reinterpret_cast<const float4*>(xs + bi * a.K + v * 8);
+          float4 x0 = xr[0], x1 = xr[1];
+          acc[bi] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
+                     wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int bi = 0; bi < 8; ++bi) {
+      if (bi >= a.batch) break;
+      float s = warp_sum(acc[bi]);
+      if (lane == 0) {
+        if (bias) s += __bfloat162float(bias[n]);
+        if (a.silu_out) s = silu(s);
+        a.y[(long long)bi * a.ldy + n] = s;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Euler / CFG
+// ---------------------------------------------------------------------------
+__global__ void euler_kernel(SchedArgs a) {
+  long long i0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  long long stride = (long long)gridDim.x * blockDim.x * 4;
+  const __nv_bfloat16* v = reinterpret_cast<const __nv_bfloat16*>(a.v);
+  const __nv_bfloat16* c = reinterpret_cast<const __nv_bfloat16*>(a.cond);
+  __nv_bfloat16* x16 = reinterpret_cast<__nv_bfloat16*>(a.x16);
+  for (long long i = i0; i < a.n; i += stride) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      long long k = i + j;
+      if (k < a.n) {
+        float pred = __bfloat162float(v[k]);
+        if (c) pred = pred + a.guidance * (__bfloat162float(c[k]) - pred);
+        float x = a.x32[k] + a.dt * pred;
+        a.x32[k] = x;
+        if (x16) x16[k] = __float2bfloat16(x);
+      }
+    }
+  }
+}
+
+__global__ void timestep_kernel(const float* t, int batch, int dim, float max_period, int flip,
+                                float shift, float scale, float* out) {
+  int half = dim / 2;
+  int b = blockIdx.x;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    float expo = -logf(max_period) * (float)i / ((float)half - shift);
+    float f = expf(expo);
+    float arg = scale * t[b] * f;
+    float s = sinf(arg), c = cosf(arg);
+    if (flip) {
+      out[(long long)b * dim + i] = c;
+      out[(long long)b * dim + half + i] = s;
+    } else {
+      out[(long long)b * dim + i] = s;
+      out[(long long)b * dim + half + i] = c;
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream) {
+  if (a->D % 8 || a->D > 32 * 8 * kMaxVec) return -2;
+  if ((a->ldx % 8) || (a->ldy % 8)) return -3;
+  if ((a->shift || a->scale) && (a->mod_bstride % 4)) return -4;
+  if (a->M == 0) return 0;
+  LnModArgs c = *a;
+  if (c.rows_per_batch <= 0) c.rows_per_batch = c.M;
+  int threads = 256;
+  int blocks = (int)((c.M * 32LL + threads - 1) / threads);
+  int nv = (c.D / 8 + 31) / 32;
+  if (nv <= 1) ln_modulate_kernel<1><<<blocks, threads, 0, stream>>>(c);
+  else if (nv <= 2) ln_modulate_kernel<2><<<blocks, threads, 0, stream>>>(c);
+  else if (nv <= 4) ln_modulate_kernel<4><<<blocks, threads, 0, stream>>>(c);
+  else if (nv <= 8) ln_modulate_kernel<8><<<blocks, threads, 0, stream>>>(c);
+  else if (nv <= 12) ln_modulate_kernel<12><<<blocks, threads, 0, stream>>>(c);
+  else if (nv <= 16) ln_modulate_kernel<16><<<blocks, threads, 0, stream>>>(c);
+  else if (nv <= 20) ln_modulate_kernel<20><<<blocks, threads, 0, stream>>>(c);
+  else ln_modulate_kernel<24><<<blocks, threads, 0, stream>>>(c);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream) {
+  if (a->rows == 0) return 0;
+  if (a->world < 1 || a->world > DFL_MAX_PEERS) return -2;
+  if (a->heads_per_rank * a->world != a->H) return -3;
+  if (a->ld % 8) return -4;
+  if (a->dh == 128)
+    qkv_scatter_kernel<128><<<a->rows, 128, 0, stream>>>(*a);
+  else if (a->dh == 64)
+    qkv_scatter_kernel<64><<<a->rows, 128, 0, stream>>>(*a);
+  else
+    return -5;
+  return (int)cudaGetLastError();
+}
+
+extern "C" int dfl_gemv(const GemvArgs* a, cudaStream_t stream) {
+  if (a->batch < 1 || a->batch > 8) return -2;
+  if (a->K % 8 || a->ldw % 8) return -3;
+  size_t smem = (size_t)a->batch * a->K * sizeof(float);
+  if (smem > 200 * 1024) return -4;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int blocks = (a->N + 7) / 8;
+  int cap = dfl_host::num_sms(dev) * 4;
+  if (blocks > cap) blocks = cap;
+  gemv_kernel<<<blocks, 256, smem, stream>>>(*a);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int dfl_euler_step(const SchedArgs* a, cudaStream_t stream) {
+  if (a->n == 0) return 0;
+  long long blocks = (a->n / 4 + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  euler_kernel<<<(int)blocks, 256, 0, stream>>>(*a);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int dfl_timestep_embed(const float* t, int batch, int dim, float max_period,
+                                  int flip_sin_to_cos, float downscale_freq_shift, float scale,
+                                  float* out, cudaStream_t stream) {
+  if (dim % 2) return -2;
+  timestep_kernel<<<batch, 128, 0, stream>>>(t, batch, dim, max_period, flip_sin_to_cos,
+                                             downscale_freq_shift, scale, out);
+  return (int)cudaGetLastError();
+}

@@ -1,0 +1,169 @@
+"""Build and load the in-tree sm_100a extension (``difflet_b200/_build/_difflet_C*.so``).
+
+The CUDA sources under ``csrc/`` are plain CUDA translation units (no torch
+headers) plus one torch binding file.  ``build()`` compiles them for
+``sm_100a`` with ``torch.utils.cpp_extension`` into ``difflet_b200/_build``;
+``load()`` imports the built module straight from that directory when the
+source hash matches, so a machine that received the built ``.so`` (a GPU box)
+does not rebuild.  On a machine with a GPU the native module is mandatory:
+``require()`` raises instead of silently falling back to eager PyTorch.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import importlib.machinery
+import importlib.util
+import os
+import sys
+import threading
+from pathlib import Path
+
+_PKG_DIR = Path(__file__).resolve().parent
+_REPO = _PKG_DIR.parent
+CSRC = _REPO / "csrc"
+BUILD_DIR = _PKG_DIR / "_build"
+EXT_NAME = "_difflet_C"
+
+CUDA_SOURCES = [
+    "gemm.cu",
+    "norm.cu",
+    "attention.cu",
+    "comm.cu",
+    "mx.cu",
+    "conv.cu",
+]
+CPP_SOURCES = ["bindings.cpp"]
+HEADERS = ["common.cuh", "kernels.h"]
+
+NVCC_FLAGS = [
+    "-gencode",
+    "arch=compute_100a,code=sm_100a",
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-U__CUDA_NO_HALF_OPERATORS__",
+    "-U__CUDA_NO_HALF_CONVERSIONS__",
+    "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
+]
+CXX_FLAGS = ["-O3", "-std=c++17"]
+
+_lock = threading.Lock()
+_module = None
+_load_error: Exception | None = None
+
+
+def _sources() -> list[Path]:
+    out = []
+    for name in CUDA_SOURCES + CPP_SOURCES:
+        p = CSRC / name
+        if p.exists():
+            out.append(p)
+    return out
+
+
+def source_hash() -> str:
+    h = hashlib.sha256()
+    for p in sorted(_sources() + [CSRC / n for n in HEADERS if (CSRC / n).exists()]):
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    h.update(" ".join(NVCC_FLAGS + CXX_FLAGS).encode())
+    return h.hexdigest()[:24]
+
+
+def _so_path() -> Path | None:
+    for suffix in importlib.machinery.EXTENSION_SUFFIXES + [".so"]:
+        p = BUILD_DIR / f"{EXT_NAME}{suffix}"
+        if p.exists():
+            return p
+    return None
+
+
+def _stamp() -> Path:
+    return BUILD_DIR / f"{EXT_NAME}.hash"
+
+
+def build(verbose: bool = False, force: bool = False):
+    """Compile every CUDA source for sm_100a and return the loaded module."""
+    global _module
+    from torch.utils import cpp_extension
+
+    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    want = source_hash()
+    if not force and _so_path() is not None and _stamp().exists() and _stamp().read_text() == want:
+        return load()
+    os.environ.setdefault("MAX_JOBS", str(min(8, os.cpu_count() or 4)))
+    # torch's own arch list must not add other targets: the -gencode above is the only one.
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    mod = cpp_extension.load(
+        name=EXT_NAME,
+        sources=[str(p) for p in _sources()],
+        extra_cflags=CXX_FLAGS,
+        extra_cuda_cflags=NVCC_FLAGS,
+        extra_include_paths=[str(CSRC)],
+        build_directory=str(BUILD_DIR),
+        verbose=verbose,
+        with_cuda=True,
+    )
+    _stamp().write_text(want)
+    _module = mod
+    return mod
+
+
+def load():
+    """Import the built extension (building it first if it is missing or stale)."""
+    global _module, _load_error
+    if _module is not None:
+        return _module
+    with _lock:
+        if _module is not None:
+            return _module
+        try:
+            so = _so_path()
+            if so is None or not _stamp().exists() or _stamp().read_text() != source_hash():
+                return build()
+            import torch  # noqa: F401  (libtorch symbols must be loaded first)
+
+            spec = importlib.util.spec_from_file_location(EXT_NAME, str(so))
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            sys.modules[EXT_NAME] = mod
+            _module = mod
+            return mod
+        except Exception as exc:  # pragma: no cover - surfaced by require()
+            _load_error = exc
+            raise
+
+
+def available() -> bool:
+    try:
+        load()
+        return True
+    except Exception:
+        return False
+
+
+def require():
+    """Return the native module; raise loudly when it cannot be loaded."""
+    try:
+        return load()
+    except Exception as exc:
+        raise RuntimeError(
+            "difflet_b200 native extension (sm_100a) is not available; build it with "
+            "`python -c 'import difflet_b200._native as n; n.build(verbose=True)'`"
+        ) from exc
+
+
+def check_device_errors(device=None) -> None:
+    """Raise if any kernel recorded an error in the per-device error word."""
+    import torch
+
+    mod = require()
+    dev = torch.cuda.current_device() if device is None else int(device)
+    word = mod.error_word(dev).cpu().tolist()
+    if word[0] != 0:
+        mod.error_word(dev).zero_()
+        from difflet_b200.utils.errors import DeviceError
+
+        raise DeviceError(code=word[0], kernel=word[1], detail=(word[2], word[3]))

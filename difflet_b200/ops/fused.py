@@ -1,0 +1,258 @@
+"""Fused device ops used by every model: one entry point, two implementations.
+
+CUDA tensors go to the sm_100a kernels in ``csrc/`` (through ``_native``);
+CPU tensors go to a plain PyTorch implementation of the same math, which is
+the oracle the kernel tests compare against and which also runs in float64 for
+the tiny-model parity check.  There is no silent fallback: a CUDA tensor with a
+missing extension raises.
+
+Ops:
+  linear        y = epi(x W^T + b): epi in {none, gelu (column window), silu,
+                gate_resid (resid + gate[b] * y)}; strided outputs allowed
+  ln_modulate   LayerNorm / RMSNorm (+affine) (* (1 + scale) + shift)
+  qkv_scatter   per-head / across-heads q,k RMSNorm + RoPE + scatter to
+                head-major (or token-major) destinations, one per rank
+  attention     softmax(scale q k^T) v with key window and LSE
+  gemv          modulation linears (M <= 8), f32 in/out, optional SiLU
+  euler_step    x += dt * (u + s (c - u)) on f32 latents (+ bf16 mirror)
+  timestep_embed sinusoidal features
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from difflet_b200 import envs
+
+EPI_NONE, EPI_GELU, EPI_GATE_RESID, EPI_SILU = 0, 1, 2, 3
+_ACT = {None: EPI_NONE, "none": EPI_NONE, "gelu": EPI_GELU, "gelu_tanh": EPI_GELU, "silu": EPI_SILU}
+
+_nat = None
+
+
+def native():
+    global _nat
+    if _nat is None:
+        from difflet_b200 import _native
+
+        _nat = _native.require()
+    return _nat
+
+
+def _rows2d(x: torch.Tensor) -> torch.Tensor:
+    return x if x.dim() == 2 else x.reshape(-1, x.shape[-1])
+
+
+# ---------------------------------------------------------------------------
+def linear(x, w, b=None, *, out=None, act=None, act_lo=0, act_hi=None, gate=None, resid=None,
+           rows_per_batch=0, alpha=1.0, out_f32=False):
+    """``act(alpha * x @ w.T + b)`` or ``resid + gate * (...)``.
+
+    x: [M, K]; w: [N, K]; b: [N]; gate: f32 [B, N] (rows_per_batch rows each);
+    resid: [M, N] (may be ``out``).  ``act`` applies to columns [act_lo, act_hi).
+    """
+    x2 = _rows2d(x)
+    N = w.shape[0]
+    act_hi = N if act_hi is None else act_hi
+    if x2.is_cuda and envs.DIFFLET_KERNEL_GEMM != "cublas":
+        epi = EPI_GATE_RESID if gate is not None else _ACT[act]
+        return native().gemm(x2, w, b, out, epi, act_lo, act_hi, gate, rows_per_batch, resid, alpha, out_f32)
+    # reference path: the CPU oracle (any dtype), or the cuBLAS A/B baseline on CUDA
+    if x2.is_cuda:
+        y = torch.matmul(x2, w.t()).float()
+    else:
+        y = x2 @ w.t().to(x2.dtype)
+    y = y * alpha
+    if b is not None:
+        y = y + b.to(y.dtype)
+    if act in ("gelu", "gelu_tanh"):
+        y[:, act_lo:act_hi] = F.gelu(y[:, act_lo:act_hi], approximate="tanh")
+    elif act == "silu":
+        y[:, act_lo:act_hi] = F.silu(y[:, act_lo:act_hi])
+    if gate is not None:
+        M = y.shape[0]
+        rpb = rows_per_batch if rows_per_batch > 0 else M
+        g = gate[:, :N].to(y.dtype).repeat_interleave(rpb, 0)[:M]
+        y = resid.to(y.dtype) + g * y
+    dt = torch.float32 if out_f32 else (x2.dtype if not x2.is_cuda else torch.bfloat16)
+    if out is not None:
+        out.copy_(y.to(out.dtype))
+        return out
+    return y.to(dt)
+
+
+def ln_modulate(x, *, shift=None, scale=None, w=None, b=None, eps=1e-6, rms=False, rows_per_batch=0,
+                out=None):
+    x2 = _rows2d(x)
+    if x2.is_cuda:
+        return native().ln_modulate(x2, out, w, b, shift, scale, rows_per_batch, eps, rms)
+    xf = x2.to(torch.float64 if x2.dtype == torch.float64 else torch.float32)
+    if rms:
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    else:
+        y = F.layer_norm(xf, (xf.shape[-1],), eps=eps)
+    if w is not None:
+        y = y * w.to(y.dtype)
+    if b is not None:
+        y = y + b.to(y.dtype)
+    M = y.shape[0]
+    rpb = rows_per_batch if rows_per_batch > 0 else M
+    if scale is not None:
+        y = y * (1 + scale.to(y.dtype).repeat_interleave(rpb, 0)[:M])
+    if shift is not None:
+        y = y + shift.to(y.dtype).repeat_interleave(rpb, 0)[:M]
+    y = y.to(x2.dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def _rope_cpu(x, cos, sin, half):
+    # x [..., S, dh]; cos/sin [S, dh/2]
+    if half:
+        d2 = x.shape[-1] // 2
+        x1, x2 = x[..., :d2], x[..., d2:]
+        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1)
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    return torch.stack([x0 * cos - x1 * sin, x1 * cos + x0 * sin], -1).flatten(-2)
+
+
+def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, S_dst, seq_off=0,
+                norm_mode=1, wq=None, wk=None, eps=1e-6, cos=None, sin=None, rope_pos_off=0,
+                rope_half=False, heads_per_rank=None, token_major=False):
+    """Normalise + rotate q/k of a token-major qkv buffer and scatter q/k/v by head.
+
+    ``q_dst`` etc. are lists (one tensor per destination rank; a single-GPU call
+    passes one).  Destination layout [B, H_local, S_dst, dh] (or [B, S_dst,
+    H_local*dh] when ``token_major``); row ``s`` of the source lands at
+    position ``seq_off + s``.  ``heads_per_rank`` splits heads over the list.
+    """
+    qkv2 = _rows2d(qkv)
+    world = len(q_dst)
+    hpr = heads_per_rank or (H // world)
+    if qkv2.is_cuda:
+        ptr = lambda ts: [t if isinstance(t, int) else t.data_ptr() for t in ts]  # noqa: E731
+        native().qkv_scatter(qkv2, q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos, sin,
+                             rope_pos_off, rope_half, hpr, ptr(q_dst), ptr(k_dst), ptr(v_dst), S_dst,
+                             seq_off, token_major)
+        return
+    rows = qkv2.shape[0]
+    B = rows // S_src
+    ct = torch.float64 if qkv2.dtype == torch.float64 else torch.float32
+    x = qkv2.to(ct).view(B, S_src, -1)
+    q = x[..., q_off:q_off + H * dh].reshape(B, S_src, H, dh)
+    k = x[..., k_off:k_off + H * dh].reshape(B, S_src, H, dh)
+    v = x[..., v_off:v_off + H * dh].reshape(B, S_src, H, dh)
+    if norm_mode == 1:
+        q = q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + eps)
+        k = k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + eps)
+        if wq is not None:
+            q = q * wq.to(ct)
+        if wk is not None:
+            k = k * wk.to(ct)
+    elif norm_mode == 2:
+        qf = q.reshape(B, S_src, H * dh)
+        kf = k.reshape(B, S_src, H * dh)
+        qf = qf * torch.rsqrt(qf.pow(2).mean(-1, keepdim=True) + eps)
+        kf = kf * torch.rsqrt(kf.pow(2).mean(-1, keepdim=True) + eps)
+        if wq is not None:
+            qf = qf * wq.to(ct)
+        if wk is not None:
+            kf = kf * wk.to(ct)
+        q, k = qf.view(B, S_src, H, dh), kf.view(B, S_src, H, dh)
+    q, k, v = (t.permute(0, 2, 1, 3) for t in (q, k, v))  # B, H, S, dh
+    if cos is not None:
+        c = cos[rope_pos_off:rope_pos_off + S_src].to(ct)
+        s_ = sin[rope_pos_off:rope_pos_off + S_src].to(ct)
+        q = _rope_cpu(q, c, s_, rope_half)
+        k = _rope_cpu(k, c, s_, rope_half)
+    for r in range(world):
+        hs = slice(r * hpr, (r + 1) * hpr)
+        for src, dst in ((q, q_dst[r]), (k, k_dst[r]), (v, v_dst[r])):
+            part = src[:, hs]
+            if token_major:
+                dst.view(B, S_dst, hpr, dh)[:, seq_off:seq_off + S_src] = part.permute(0, 2, 1, 3).to(dst.dtype)
+            else:
+                dst[:, :, seq_off:seq_off + S_src] = part.to(dst.dtype)
+
+
+def attention(q, k, v, scale, *, out=None, lse=None, kv_lo=None, kv_hi=None):
+    """softmax(scale * q k^T) v over [B, H, S, dh]; key window [kv_lo[b], kv_hi[b])."""
+    if q.is_cuda and envs.DIFFLET_KERNEL_ATTN != "sdpa" and q.shape[-1] == 128:
+        return native().attention(q, k, v, float(scale), out, lse, kv_lo, kv_hi)
+    ct = torch.float64 if q.dtype == torch.float64 else torch.float32
+    if q.is_cuda and lse is None and kv_lo is None:
+        o = F.scaled_dot_product_attention(q, k, v, scale=float(scale))
+        if out is not None:
+            out.copy_(o)
+            return out
+        return o
+    s = torch.einsum("bhqd,bhkd->bhqk", q.to(ct), k.to(ct)) * scale
+    if kv_lo is not None or kv_hi is not None:
+        Sk = k.shape[2]
+        idx = torch.arange(Sk, device=q.device)
+        lo = kv_lo if kv_lo is not None else torch.zeros(q.shape[0], dtype=torch.long, device=q.device)
+        hi = kv_hi if kv_hi is not None else torch.full((q.shape[0],), Sk, dtype=torch.long, device=q.device)
+        mask = (idx[None] >= lo[:, None].to(idx.dtype)) & (idx[None] < hi[:, None].to(idx.dtype))
+        s = s.masked_fill(~mask[:, None, None, :], float("-inf"))
+    m = torch.logsumexp(s, -1)
+    p = torch.exp(s - m[..., None])
+    p = torch.nan_to_num(p, nan=0.0)
+    o = torch.einsum("bhqk,bhkd->bhqd", p, v.to(ct))
+    if lse is not None:
+        lse.copy_(m.to(lse.dtype))
+    o = o.to(q.dtype)
+    if out is not None:
+        out.copy_(o)
+        return out
+    return o
+
+
+def gemv(W, x, bias=None, *, silu_in=False, silu_out=False, out=None):
+    if W.is_cuda:
+        return native().gemv(W, x.float().contiguous(), bias, out, silu_in, silu_out)
+    ct = torch.float64 if x.dtype == torch.float64 else torch.float32
+    xx = F.silu(x.to(ct)) if silu_in else x.to(ct)
+    y = xx @ W.to(ct).t()
+    if bias is not None:
+        y = y + bias.to(ct)
+    if silu_out:
+        y = F.silu(y)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def euler_step(x32, v, dt, *, x16=None, cond=None, guidance=1.0):
+    """x32 += dt * pred, pred = v or v + guidance * (cond - v) (CFG); optional bf16 mirror."""
+    if x32.is_cuda:
+        native().euler_step(x32, x16, v, cond, float(dt), float(guidance))
+        return x32
+    pred = v.to(x32.dtype)
+    if cond is not None:
+        pred = pred + guidance * (cond.to(x32.dtype) - pred)
+    x32.add_(pred, alpha=dt)
+    if x16 is not None:
+        x16.copy_(x32.to(x16.dtype))
+    return x32
+
+
+def timestep_embed(t, dim, *, max_period=10000.0, flip_sin_to_cos=True, downscale_freq_shift=0.0,
+                   scale=1.0):
+    """Sinusoidal timestep features (diffusers ``get_timestep_embedding`` semantics)."""
+    if t.is_cuda:
+        return native().timestep_embed(t.float().contiguous(), dim, max_period, flip_sin_to_cos,
+                                       downscale_freq_shift, scale)
+    ct = torch.float64 if t.dtype == torch.float64 else torch.float32
+    half = dim // 2
+    ex = -math.log(max_period) * torch.arange(half, dtype=ct) / (half - downscale_freq_shift)
+    arg = scale * t.to(ct)[:, None] * torch.exp(ex)[None]
+    emb = torch.cat([torch.sin(arg), torch.cos(arg)], -1)
+    if flip_sin_to_cos:
+        emb = torch.cat([emb[:, half:], emb[:, :half]], -1)
+    return emb

@@ -1,0 +1,222 @@
+"""Numerics of every sm_100a kernel against a plain fp32 PyTorch reference."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(out, ref, tol=2e-2):
+    out = out.float()
+    ref = ref.float()
+    scale = ref.abs().max().item() + 1e-6
+    err = (out - ref).abs().max().item()
+    assert err <= tol * scale, f"max abs err {err:.4g} vs scale {scale:.4g}"
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 384, 200), (1024, 2048, 512), (128, 64, 64), (4608, 3072, 3072)])
+def test_gemm_plain_bias(native, M, N, K):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    bias = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    out = native.gemm(a, b, bias)
+    ref = a.float() @ b.float().t() + bias.float()
+    torch.cuda.synchronize()
+    _close(out, ref)
+    out32 = native.gemm(a, b, None, out_f32=True)
+    _close(out32, a.float() @ b.float().t(), tol=1e-3)
+
+
+def test_gemm_gelu_window_and_strided_out(native):
+    torch.manual_seed(1)
+    M, N, K = 512, 1536, 256
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    bias = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    big = torch.zeros(M, N + 256, device="cuda", dtype=torch.bfloat16)
+    view = big[:, 128 : 128 + N]
+    native.gemm(a, b, bias, out=view, epi=1, act_lo=512, act_hi=1024)
+    ref = a.float() @ b.float().t() + bias.float()
+    ref[:, 512:1024] = torch.nn.functional.gelu(ref[:, 512:1024], approximate="tanh")
+    torch.cuda.synchronize()
+    _close(view, ref)
+    assert big[:, :128].abs().max().item() == 0 and big[:, 128 + N :].abs().max().item() == 0
+
+
+def test_gemm_gate_residual(native):
+    torch.manual_seed(2)
+    B, S, N, K = 2, 200, 768, 384
+    M = B * S
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    bias = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    gate = torch.randn(B, N, device="cuda", dtype=torch.float32)
+    resid = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    ref = resid.float() + gate.repeat_interleave(S, 0) * (a.float() @ w.float().t() + bias.float())
+    native.gemm(a, w, bias, out=resid, epi=2, gate=gate, rows_per_batch=S, resid=resid)
+    torch.cuda.synchronize()
+    _close(resid, ref)
+
+
+@pytest.mark.parametrize("D", [256, 3072, 5120])
+def test_ln_modulate(native, D):
+    torch.manual_seed(3)
+    B, S = 2, 77
+    x = torch.randn(B * S, D, device="cuda", dtype=torch.bfloat16) * 3 + 1
+    shift = torch.randn(B, D, device="cuda")
+    scale = torch.randn(B, D, device="cuda") * 0.1
+    y = native.ln_modulate(x, shift=shift, scale=scale, rows_per_batch=S, eps=1e-6)
+    xf = x.float()
+    ref = torch.nn.functional.layer_norm(xf, (D,), eps=1e-6)
+    ref = ref * (1 + scale.repeat_interleave(S, 0)) + shift.repeat_interleave(S, 0)
+    torch.cuda.synchronize()
+    _close(y, ref)
+    w = torch.randn(D, device="cuda", dtype=torch.bfloat16)
+    y2 = native.ln_modulate(x, w=w, rms=True, eps=1e-6)
+    ref2 = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    _close(y2, ref2)
+
+
+def _rope_ref(x, cos, sin):
+    # x [..., S, dh] fp32, interleaved pairs
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    o0 = x0 * cos - x1 * sin
+    o1 = x1 * cos + x0 * sin
+    return torch.stack([o0, o1], -1).flatten(-2)
+
+
+@pytest.mark.parametrize("dh", [64, 128])
+def test_qkv_scatter_norm_rope(native, dh):
+    torch.manual_seed(4)
+    B, S, H = 2, 50, 4
+    D = H * dh
+    qkv = torch.randn(B * S, 3 * D, device="cuda", dtype=torch.bfloat16)
+    wq = torch.randn(dh, device="cuda", dtype=torch.bfloat16)
+    wk = torch.randn(dh, device="cuda", dtype=torch.bfloat16)
+    S_dst, off = S + 10, 10
+    pos = torch.arange(S_dst, device="cuda", dtype=torch.float32)[:, None]
+    freqs = 1.0 / (10000 ** (torch.arange(0, dh, 2, device="cuda").float() / dh))
+    ang = pos * freqs[None]
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    q = torch.zeros(B, H, S_dst, dh, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros_like(q)
+    v = torch.zeros_like(q)
+    native.qkv_scatter(qkv, 0, D, 2 * D, S, H, dh, 1, wq, wk, 1e-6, cos, sin, off, False, H,
+                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S_dst, off, False)
+    torch.cuda.synchronize()
+    x = qkv.float().view(B, S, 3, H, dh).permute(2, 0, 3, 1, 4)  # 3,B,H,S,dh
+
+    def norm(t, w):
+        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+
+    c, s_ = cos[off:], sin[off:]
+    _close(q[:, :, off:], _rope_ref(norm(x[0], wq), c, s_))
+    _close(k[:, :, off:], _rope_ref(norm(x[1], wk), c, s_))
+    _close(v[:, :, off:], x[2])
+    assert q[:, :, :off].abs().max().item() == 0
+
+
+def test_qkv_scatter_across_heads_half_rope(native):
+    torch.manual_seed(5)
+    B, S, H, dh = 1, 33, 8, 128
+    D = H * dh
+    qkv = torch.randn(B * S, 3 * D, device="cuda", dtype=torch.bfloat16)
+    wq = torch.randn(D, device="cuda", dtype=torch.bfloat16)
+    wk = torch.randn(D, device="cuda", dtype=torch.bfloat16)
+    ang = torch.rand(S, dh // 2, device="cuda") * 6
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    q = torch.empty(B, S, D, device="cuda", dtype=torch.bfloat16)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q)
+    native.qkv_scatter(qkv, 0, D, 2 * D, S, H, dh, 2, wq, wk, 1e-6, cos, sin, 0, True, H,
+                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S, 0, True)
+    torch.cuda.synchronize()
+    x = qkv.float().view(S, 3, D)
+    qn = x[:, 0] * torch.rsqrt(x[:, 0].pow(2).mean(-1, keepdim=True) + 1e-6) * wq.float()
+    qn = qn.view(S, H, dh)
+    x1, x2 = qn[..., : dh // 2], qn[..., dh // 2 :]
+    c, s_ = cos[:, None], sin[:, None]
+    ref = torch.cat([x1 * c - x2 * s_, x2 * c + x1 * s_], -1).reshape(S, D)
+    _close(q[0], ref)
+
+
+def test_gemv_and_timestep(native):
+    torch.manual_seed(6)
+    N, K, Bt = 3000, 3072, 2
+    W = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    x = torch.randn(Bt, K, device="cuda")
+    bias = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    y = native.gemv(W, x, bias, silu_in=True)
+    ref = torch.nn.functional.silu(x) @ W.float().t() + bias.float()
+    _close(y, ref, tol=1e-3)
+    t = torch.tensor([999.0, 0.5], device="cuda")
+    e = native.timestep_embed(t, 256, 10000.0, True, 0.0, 1.0)
+    half = 128
+    ex = -math.log(10000.0) * torch.arange(half, device="cuda", dtype=torch.float32) / half
+    arg = t[:, None] * torch.exp(ex)[None]
+    ref = torch.cat([arg.cos(), arg.sin()], -1)
+    assert (e - ref).abs().max().item() < 2e-3
+
+
+def test_euler_cfg(native):
+    n = 16 * 4096
+    x = torch.randn(n, device="cuda")
+    x16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    u = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    c = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    ref = x + (-0.03) * (u.float() + 4.0 * (c.float() - u.float()))
+    native.euler_step(x, x16, u, c, -0.03, 4.0)
+    torch.cuda.synchronize()
+    assert (x - ref).abs().max().item() < 1e-5
+    assert (x16.float() - ref).abs().max().item() < 0.05
+
+
+def _attn_ref(q, k, v, scale, lo=None, hi=None):
+    s = torch.einsum("bhqd,bhkd->bhqk", q.float(), k.float()) * scale
+    if lo is not None:
+        idx = torch.arange(k.shape[2], device=q.device)
+        mask = (idx[None, :] >= lo[:, None]) & (idx[None, :] < hi[:, None])  # B, Sk
+        s = s.masked_fill(~mask[:, None, None, :], float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    p = torch.softmax(s, -1)
+    return torch.einsum("bhqk,bhkd->bhqd", p, v.float()), lse
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk", [(1, 2, 128, 128), (2, 3, 300, 333), (1, 4, 1024, 2048)])
+def test_attention(native, B, H, Sq, Sk):
+    torch.manual_seed(7)
+    q = torch.randn(B, H, Sq, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, H, Sk, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, H, Sk, 128, device="cuda", dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(128)
+    lse = torch.empty(B, H, Sq, device="cuda")
+    o = native.attention(q, k, v, scale, lse=lse)
+    ref, ref_lse = _attn_ref(q, k, v, scale)
+    torch.cuda.synchronize()
+    _close(o, ref)
+    assert (lse - ref_lse).abs().max().item() < 2e-2
+
+
+def test_attention_bounds_large_logits_token_major(native):
+    torch.manual_seed(8)
+    B, H, S = 2, 2, 384
+    q = torch.randn(B, H, S, 128, device="cuda", dtype=torch.bfloat16) * 4
+    k = torch.randn(B, H, S, 128, device="cuda", dtype=torch.bfloat16) * 4
+    v = torch.randn(B, H, S, 128, device="cuda", dtype=torch.bfloat16)
+    lo = torch.tensor([0, 70], device="cuda", dtype=torch.int32)
+    hi = torch.tensor([300, 201], device="cuda", dtype=torch.int32)
+    out = torch.empty(B, S, H * 128, device="cuda", dtype=torch.bfloat16)
+    o_view = out.view(B, S, H, 128).permute(0, 2, 1, 3)
+    scale = 1 / math.sqrt(128)
+    native.attention(q, k, v, scale, out=o_view, kv_lo=lo, kv_hi=hi)
+    ref, _ = _attn_ref(q, k, v, scale, lo, hi)
+    torch.cuda.synchronize()
+    _close(o_view, ref)
+
+
+def test_error_word_clean(native):
+    torch.cuda.synchronize()
+    assert native.error_word(torch.cuda.current_device()).cpu().tolist() == [0, 0, 0, 0]
