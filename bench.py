@@ -1,0 +1,256 @@
+"""Headline benchmark: FLUX.1-dev 1024x1024 DiT denoise step (and e2e s/image) on N B200s.
+
+Contract (one rank per GPU; the driver launches N > 1 under torch.distributed.run):
+  python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+* ``value``: DiT denoise-step latency in ms (one full FLUX.1-dev step at 1024^2:
+  timestep/guidance/pooled embedders, all-block adaLN GEMV, 19 double + 38 single
+  blocks, final layer, Euler update), timed with CUDA events over exactly K steps
+  after W warm-up steps, bracketed by barrier + synchronize, max over ranks.
+  Strong scaling: the one image's token sequence is split over the N GPUs with
+  Ulysses sequence parallelism (fused peer-memory all-to-alls).
+* ``e2e``: seconds per image through the public API (``DiffletPipeline`` ->
+  28-step generate -> VAE decode), including every run's host->device copy of
+  the inputs (T5-shaped text states, CLIP pooled vector, initial noise, from
+  pinned memory) and the device->host read of the decoded uint8 image.
+* Weights are random-init bf16 of the FLUX.1-dev architecture (12B); inputs are
+  synthetic N(0, 1) (no network).  The 24 GB of weights stream from HBM every
+  step, far larger than the 126 MB L2, so no extra L2 flush is needed.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+REF_PUBLISHED_STEP_MS = 134.1  # reference FLUX.1-dev 1024^2 DiT per-step (1x B300, stock diffusers)
+REF_PUBLISHED_E2E_S = 7.9      # reference FLUX.1-dev e2e warm (1x B300)
+
+
+def _log(msg: str) -> None:
+    print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
+def _dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=600))
+    return world, rank, local
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    import torch
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the unmodified reference from baseline/_ref through its own API."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    ref = os.path.join(here, "baseline", "_ref")
+    reason = None
+    if not os.path.isdir(os.path.join(ref, "difflet")):
+        reason = "reference not installed under baseline/_ref"
+    else:
+        sys.path.insert(0, ref)
+        try:
+            import difflet.backends.cuda.flux.transformer  # noqa: F401  (its CUDA FLUX path)
+        except Exception as exc:  # diffusers is a hard dependency of the reference CUDA path
+            reason = (f"reference CUDA FLUX path cannot import ({type(exc).__name__}: {exc}); "
+                      "diffusers==0.38.0 is not installed in this image and has no offline wheel")
+    if reason is not None:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": reason}))
+        return 0
+    raise RuntimeError("unreachable: reference CUDA path imported but no runner is defined")
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--height", type=int, default=1024)
+    ap.add_argument("--width", type=int, default=1024)
+    ap.add_argument("--e2e-images", type=int, default=1)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    args = ap.parse_args(argv)
+    import faulthandler
+
+    faulthandler.enable()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+
+    world, rank, local = _dist_setup()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+
+    from difflet_b200.bench.clocks import ClockSampler
+    from difflet_b200.ops import fused as F
+    from difflet_b200.pipeline.difflet_pipeline import DiffletPipeline
+    from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
+
+    par = DiffletParallelConfig(cp_degree=world, cp_mode="ulysses") if world > 1 else DiffletParallelConfig()
+    t_load = time.time()
+    pipe = DiffletPipeline.from_pretrained(
+        "black-forest-labs/FLUX.1-dev", parallel=par, height=args.height, width=args.width, random_init=True,
+        skip_warmup=True, application_kwargs={"cuda_graph": not args.no_graph})
+    load_s = time.time() - t_load
+    _log(f"pipeline loaded in {load_s:.1f}s")
+    app = pipe.app.app
+    dit = app.dit
+    cfg = dit.cfg
+    dev = dit.device
+    B = 1
+    h_tok, w_tok = args.height // 16, args.width // 16
+    S_img, S_txt = h_tok * w_tok, 512
+    S_img_l, S_txt_l = S_img // world, S_txt // world
+
+    # ---------------- DiT step (device-timed) ----------------
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    x32 = torch.randn(B, S_img_l, cfg.in_channels, device=dev, generator=g)
+    x16 = x32.to(torch.bfloat16)
+    txt = torch.randn(B, S_txt_l, cfg.text_dim, device=dev, generator=g).to(torch.bfloat16)
+    pooled = torch.randn(B, cfg.pooled_dim, device=dev, generator=g)
+    t_buf = torch.full((B,), 0.75, device=dev)
+    gvec = torch.full((B,), 3.5, device=dev)
+    step_fn = app._step_fn(("bench", B, S_txt_l, S_img_l), x16, txt, pooled, t_buf, gvec, None, (h_tok, w_tok))
+    dt = -1.0 / 28
+
+    def one_step():
+        v = step_fn()
+        F.euler_step(x32, v, dt, x16=x16)
+
+    _log("capturing / warming the DiT step")
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    _log("warm-up done")
+    # kernel launches per step, counted on an eager forward
+    n0 = F.LAUNCHES[0]
+    v = dit(x16, txt, pooled, t_buf, gvec, img_hw=(h_tok, w_tok))
+    F.euler_step(x32, v, 0.0, x16=x16)
+    launches_per_step = F.LAUNCHES[0] - n0
+    _barrier(world)
+    gpu_ids = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()]
+    gpu_ids = gpu_ids[:world] if gpu_ids else list(range(world))
+    sampler = ClockSampler(gpu_ids if rank == 0 else [])
+    with sampler:
+        _barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            one_step()
+        end.record()
+        _barrier(world)
+    ms = start.elapsed_time(end) / args.steps
+    ms = _max_over_ranks(ms, world)
+    _log(f"timed {args.steps} steps: {ms:.3f} ms/step")
+    clocks = sampler.summary() if rank == 0 else {}
+    from difflet_b200 import _native
+
+    _native.check_device_errors()
+
+    # ---------------- end to end through the public API ----------------
+    e2e = None
+    if not args.no_e2e:
+        gen = torch.Generator().manual_seed(7)
+        emb = torch.randn(B, S_txt, cfg.text_dim, generator=gen).to(torch.bfloat16).pin_memory()
+        pool = torch.randn(B, cfg.pooled_dim, generator=gen).pin_memory()
+        noise = torch.randn(B, cfg.latent_channels, args.height // 8, args.width // 8, generator=gen).pin_memory()
+        h2d = emb.numel() * emb.element_size() + pool.numel() * pool.element_size() + noise.numel() * noise.element_size()
+        d2h = 0
+
+        def one_image():
+            nonlocal d2h
+            img = pipe(prompt_embeds=emb, pooled_prompt_embeds=pool, latents=noise, num_inference_steps=28,
+                       guidance_scale=3.5, height=args.height, width=args.width)
+            if img is not None:
+                host = img.to("cpu")
+                d2h = host.numel() * host.element_size()
+            return img
+
+        _log("e2e warm-up image")
+        one_image()  # warm-up (captures the graph for the pipeline shapes)
+        _barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_images):
+            one_image()
+        _barrier(world)
+        e2e_s = (time.perf_counter() - t0) / args.e2e_images
+        e2e_s = _max_over_ranks(e2e_s, world)
+        e2e = {"value": round(e2e_s, 4), "unit": "s/image", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "steps_per_image": 28,
+               "vs_published_reference_s": round(e2e_s / REF_PUBLISHED_E2E_S, 4)}
+        _native.check_device_errors()
+
+    if rank == 0:
+        out = {
+            "metric": "FLUX.1-dev 1024x1024 DiT denoise step latency (max over ranks)",
+            "value": round(ms, 3),
+            "unit": "ms/step",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 3),
+            "higher_is_better": False,
+            "scaling": "strong",
+            "vs_baseline": round(ms / REF_PUBLISHED_STEP_MS, 4),
+            "dtype": "bf16",
+            "data": "synthetic (random-init FLUX.1-dev weights, N(0,1) text states / pooled / latents)",
+            "config": {"model": "FLUX.1-dev", "global_batch": B, "seq_len": S_img + S_txt,
+                       "height": args.height, "width": args.width,
+                       "parallelism": f"ulysses{world}" if world > 1 else "single",
+                       "l2": "weights (24 GB) stream from HBM every step, larger than L2; no flush",
+                       "cuda_graph": not args.no_graph, "load_s": round(load_s, 1)},
+            "clocks": clocks,
+            "gpu_launches": int(launches_per_step * args.steps),
+            "e2e": e2e,
+        }
+        print(json.dumps(out), flush=True)
+    # release CUDA graphs (and any NCCL work they hold) before tearing anything down
+    app._graphs.clear()
+    del step_fn
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    _log("done")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,87 @@
+"""FLUX application factory (registry entry ``flux``).
+
+Lifecycle as in the reference GPU flow (``difflet/backends/gpu/application.py:84-481``):
+``compile()`` builds / verifies the native kernels and records the kernel hash
+in the manifest; ``load()`` materialises the weights on this rank's GPU
+(checkpoint or seeded random init), sets up the sequence-parallel context,
+and warms up (capturing the DiT step in a CUDA graph); ``generate()`` /
+``__call__`` run text-to-image.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from difflet_b200.models.flux.config import FluxConfig, get_config
+from difflet_b200.models.flux.model import FluxTransformer
+from difflet_b200.models.flux.pipeline import FluxApplication
+from difflet_b200.models.vae.autoencoder_kl import KLDecoder, KLDecoderConfig
+
+
+class FluxEngine:
+    def __init__(self, *, entry, model_path, parallel, dtype, shape, backend, application_kwargs):
+        self.entry = entry
+        self.model_path = model_path
+        self.parallel = parallel
+        self.dtype = dtype
+        self.shape = shape
+        self.backend = backend
+        self.kw = dict(application_kwargs or {})
+        preset = self.kw.get("preset") or ("flux-schnell" if "schnell" in str(model_path).lower() else "flux-dev")
+        self.cfg: FluxConfig = get_config(preset)
+        self.app: FluxApplication | None = None
+
+    def compile(self, compiled_path):
+        info = {"backend": self.backend}
+        if self.backend == "cuda":
+            from difflet_b200 import _native
+
+            _native.require()
+            info["kernels"] = _native.source_hash()
+        return info
+
+    def _device(self):
+        if self.backend == "cuda":
+            return torch.device("cuda", torch.cuda.current_device())
+        return torch.device("cpu")
+
+    def load(self, compiled_path=None, skip_warmup=False):
+        dev = self._device()
+        if self.kw.get("random_init") or not self.model_path:
+            dit = FluxTransformer.random_init(self.cfg, device=dev, dtype=self.dtype, seed=int(self.kw.get("seed", 0)))
+            vae = KLDecoder.random_init(KLDecoderConfig(), device=dev, dtype=self.dtype, seed=1)
+        else:
+            from difflet_b200.utils.checkpoint import load_component
+
+            sd = load_component(self.model_path, "transformer", dtype=self.dtype)
+            dit = FluxTransformer.from_diffusers_state_dict(self.cfg, sd, device=dev, dtype=self.dtype)
+            vsd = load_component(self.model_path, "vae", dtype=self.dtype, device=dev)
+            vae = KLDecoder(KLDecoderConfig(), vsd)
+        if self.parallel.world_size > 1:
+            from difflet_b200.parallel.ulysses import make_sequence_parallel
+
+            dit.par = make_sequence_parallel(self.parallel, dev)
+        self.app = FluxApplication(dit, vae, use_cuda_graph=(self.backend == "cuda" and self.kw.get("cuda_graph", True)))
+        if self.kw.get("teacache_speedup"):
+            from difflet_b200.pipeline.teacache import build_controller
+
+            self.app.teacache = build_controller(self.kw)
+        if not skip_warmup and self.backend == "cuda":
+            h = self.shape.get("height") or 1024
+            w = self.shape.get("width") or 1024
+            self.app.generate(prompt="warmup", height=h, width=w, num_inference_steps=2, output_type="latent")
+            torch.cuda.synchronize()
+
+    def generate(self, **kw):
+        kw.setdefault("height", self.shape.get("height") or 1024)
+        kw.setdefault("width", self.shape.get("width") or 1024)
+        return self.app.generate(**kw)
+
+    def __call__(self, *args, **kw):
+        if args and isinstance(args[0], str):
+            kw["prompt"] = args[0]
+        return self.generate(**kw)
+
+
+def create_application(**kw):
+    return FluxEngine(**kw)

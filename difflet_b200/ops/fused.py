@@ -31,6 +31,8 @@ EPI_NONE, EPI_GELU, EPI_GATE_RESID, EPI_SILU = 0, 1, 2, 3
 _ACT = {None: EPI_NONE, "none": EPI_NONE, "gelu": EPI_GELU, "gelu_tanh": EPI_GELU, "silu": EPI_SILU}
 
 _nat = None
+# Host-side count of native kernel launches (each fused-op call is one launch).
+LAUNCHES = [0]
 
 
 def native():
@@ -39,6 +41,7 @@ def native():
         from difflet_b200 import _native
 
         _nat = _native.require()
+    LAUNCHES[0] += 1
     return _nat
 
 
@@ -214,7 +217,14 @@ def attention(q, k, v, scale, *, out=None, lse=None, kv_lo=None, kv_hi=None):
 
 def gemv(W, x, bias=None, *, silu_in=False, silu_out=False, out=None):
     if W.is_cuda:
-        return native().gemv(W, x.float().contiguous(), bias, out, silu_in, silu_out)
+        x = x.float().contiguous()
+        if x.shape[0] <= 8:
+            return native().gemv(W, x, bias, out, silu_in, silu_out)
+        # the kernel stages at most 8 input rows in shared memory: chunk larger batches
+        y = out if out is not None else torch.empty(x.shape[0], W.shape[0], device=x.device)
+        for i in range(0, x.shape[0], 8):
+            native().gemv(W, x[i:i + 8], bias, y[i:i + 8], silu_in, silu_out)
+        return y
     ct = torch.float64 if x.dtype == torch.float64 else torch.float32
     xx = F.silu(x.to(ct)) if silu_in else x.to(ct)
     y = xx @ W.to(ct).t()
