@@ -57,7 +57,25 @@ struct AttnParams {
   const int* kv_lo;
   const int* kv_hi;
   __nv_bfloat16* o;
+  __nv_bfloat16* o_peer[DFL_MAX_PEERS];
+  int o_world, seg0_len, seg0_per, seg1_per;
 };
+
+// Output row address: local, or (Ulysses) the owning rank's buffer.
+__device__ __forceinline__ __nv_bfloat16* out_row(const AttnParams& p, int b, int h, int s) {
+  if (p.o_world <= 1)
+    return p.o + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)s * p.o_ss;
+  int owner, lrow;
+  if (s < p.seg0_len) {
+    owner = s / p.seg0_per;
+    lrow = s - owner * p.seg0_per;
+  } else {
+    const int s2 = s - p.seg0_len;
+    owner = s2 / p.seg1_per;
+    lrow = p.seg0_per + (s2 - owner * p.seg1_per);
+  }
+  return p.o_peer[owner] + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)lrow * p.o_ss;
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -295,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && n_tiles > 0 && mbar_wait(o_full, 0, err, kKidAttn, 122, abort_flag)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* op = p.o + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)qrow * p.o_ss;
+      __nv_bfloat16* op = out_row(p, b, h, qrow);
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o_raw[32];
@@ -317,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         p.lse[((long long)b * p.H + h) * p.Sq + qrow] =
             l > 0.f ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
     } else if (n_tiles == 0 && qrow < p.Sq) {
-      __nv_bfloat16* op = p.o + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)qrow * p.o_ss;
+      __nv_bfloat16* op = out_row(p, b, h, qrow);
       for (int d = 0; d < kD; ++d) op[d] = __float2bfloat16(0.f);
       if (p.lse) p.lse[((long long)b * p.H + h) * p.Sq + qrow] = -INFINITY;
     }
@@ -372,6 +390,19 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   p.kv_lo = a->kv_lo;
   p.kv_hi = a->kv_hi;
   p.o = reinterpret_cast<__nv_bfloat16*>(a->o);
+  p.o_world = a->o_world;
+  p.seg0_len = a->seg0_len;
+  p.seg0_per = a->seg0_per > 0 ? a->seg0_per : 1;
+  p.seg1_per = a->seg1_per > 0 ? a->seg1_per : 1;
+  for (int r = 0; r < DFL_MAX_PEERS; ++r)
+    p.o_peer[r] = reinterpret_cast<__nv_bfloat16*>(r < a->o_world ? a->o_peer[r] : nullptr);
+  if (a->o_world > 1) {
+    if (a->o_world > DFL_MAX_PEERS) return -6;
+    if (a->seg0_len > 0 && a->seg0_per * a->o_world != a->seg0_len) return -7;
+    if (a->seg1_per * a->o_world != a->Sq - a->seg0_len) return -7;
+    for (int r = 0; r < a->o_world; ++r)
+      if (!a->o_peer[r] || (reinterpret_cast<uintptr_t>(a->o_peer[r]) & 15)) return -8;
+  }
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

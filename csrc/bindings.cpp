@@ -259,15 +259,18 @@ at::Tensor timestep_embed(const at::Tensor& t, int64_t dim, double max_period, b
 // q, k, v: [B, H, S, dh] views (any strides with unit inner stride).
 at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
                      c10::optional<at::Tensor> out, const c10::optional<at::Tensor>& lse,
-                     const c10::optional<at::Tensor>& kv_lo, const c10::optional<at::Tensor>& kv_hi) {
+                     const c10::optional<at::Tensor>& kv_lo, const c10::optional<at::Tensor>& kv_hi,
+                     std::vector<int64_t> o_peer, int64_t seg0_len, int64_t seg0_per, int64_t seg1_per, std::vector<int64_t> o_strides) {
   check_bf16_cuda(q, "q");
   check_bf16_cuda(k, "k");
   check_bf16_cuda(v, "v");
   TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "q/k/v must be [B, H, S, dh]");
   TORCH_CHECK(q.stride(3) == 1 && k.stride(3) == 1 && v.stride(3) == 1, "unit inner stride required");
   const c10::cuda::CUDAGuard guard(q.device());
-  at::Tensor o = (out.has_value() && out->defined()) ? *out : at::empty_like(q);
-  TORCH_CHECK(o.dim() == 4 && o.stride(3) == 1, "out must be [B, H, S, dh] with unit inner stride");
+  const bool scatter = !o_peer.empty();
+  at::Tensor o = (out.has_value() && out->defined()) ? *out : (scatter ? at::empty({0}, q.options()) : at::empty_like(q));
+  TORCH_CHECK(scatter || (o.dim() == 4 && o.stride(3) == 1), "out must be [B, H, S, dh] with unit inner stride");
+  TORCH_CHECK(!scatter || o_strides.size() == 3, "o_strides (batch, head, seq) required with o_peer");
   AttnArgs a{};
   a.q = q.data_ptr();
   a.k = k.data_ptr();
@@ -276,7 +279,12 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   a.q_bs = q.stride(0); a.q_hs = q.stride(1); a.q_ss = q.stride(2);
   a.k_bs = k.stride(0); a.k_hs = k.stride(1); a.k_ss = k.stride(2);
   a.v_bs = v.stride(0); a.v_hs = v.stride(1); a.v_ss = v.stride(2);
-  a.o_bs = o.stride(0); a.o_hs = o.stride(1); a.o_ss = o.stride(2);
+  if (scatter) {
+    a.o_bs = o_strides[0]; a.o_hs = o_strides[1]; a.o_ss = o_strides[2];
+    a.o = reinterpret_cast<void*>(o_peer[0]);
+  } else {
+    a.o_bs = o.stride(0); a.o_hs = o.stride(1); a.o_ss = o.stride(2);
+  }
   a.B = (int)q.size(0);
   a.H = (int)q.size(1);
   a.Sq = (int)q.size(2);
@@ -290,11 +298,78 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   if (kv_lo.has_value() && kv_lo->defined()) a.kv_lo = kv_lo->data_ptr<int>();
   if (kv_hi.has_value() && kv_hi->defined()) a.kv_hi = kv_hi->data_ptr<int>();
   a.err = err_ptr();
+  TORCH_CHECK(o_peer.size() <= DFL_MAX_PEERS, "at most 8 output peers");
+  a.o_world = (int)o_peer.size();
+  for (size_t r = 0; r < o_peer.size(); ++r) a.o_peer[r] = reinterpret_cast<void*>(o_peer[r]);
+  a.seg0_len = (int)seg0_len;
+  a.seg0_per = (int)seg0_per;
+  a.seg1_per = (int)seg1_per;
   DFL_CHECK_RC(dfl_attention(&a, cur_stream()), "attention");
   return o;
 }
 
 at::Tensor error_word(int64_t device) { return error_buffer((int)device); }
+
+// ---------------------------------------------------------------- comm runtime
+at::Tensor symm_alloc(int64_t nbytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)nbytes);
+  TORCH_CHECK(e == cudaSuccess, "cudaMalloc(", nbytes, ") failed: ", cudaGetErrorString(e));
+  cudaMemset(p, 0, (size_t)nbytes);
+  cudaDeviceSynchronize();
+  return torch::from_blob(p, {nbytes}, [](void* ptr) { cudaFree(ptr); },
+                          at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device));
+}
+
+at::Tensor from_ptr(int64_t ptr, int64_t nbytes, int64_t device) {
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {nbytes}, [](void*) {},
+                          at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device));
+}
+
+py::bytes ipc_handle(const at::Tensor& t) {
+  char buf[64];
+  int rc = dfl_ipc_handle(t.data_ptr(), buf);
+  TORCH_CHECK(rc == 0, "cudaIpcGetMemHandle failed: ", rc);
+  return py::bytes(buf, 64);
+}
+
+int64_t ipc_open(py::bytes handle, int64_t device) {
+  const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  std::string h = handle;
+  TORCH_CHECK(h.size() == 64, "IPC handle must be 64 bytes");
+  void* p = nullptr;
+  int rc = dfl_ipc_open(h.data(), &p);
+  TORCH_CHECK(rc == 0, "cudaIpcOpenMemHandle failed: ", rc);
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr) { dfl_ipc_close(reinterpret_cast<void*>(ptr)); }
+
+void peer_barrier(std::vector<int64_t> flags, const at::Tensor& counter, int64_t rank, int64_t timeout_cycles) {
+  TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == at::kInt, "counter must be a CUDA int32 tensor");
+  const c10::cuda::CUDAGuard guard(counter.device());
+  BarrierArgs a{};
+  a.world = (int)flags.size();
+  for (size_t r = 0; r < flags.size(); ++r) a.flags[r] = reinterpret_cast<int*>(flags[r]);
+  a.counter = counter.data_ptr<int>();
+  a.rank = (int)rank;
+  a.timeout_cycles = timeout_cycles;
+  a.err = err_ptr();
+  DFL_CHECK_RC(dfl_peer_barrier(&a, cur_stream()), "peer_barrier");
+}
+
+void peer_put_f32(const at::Tensor& src, std::vector<int64_t> dst, int64_t dst_offset) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kFloat && src.is_contiguous(), "src must be f32 contiguous");
+  const c10::cuda::CUDAGuard guard(src.device());
+  PeerPutArgs a{};
+  a.src = src.data_ptr<float>();
+  a.n = src.numel();
+  a.world = (int)dst.size();
+  for (size_t r = 0; r < dst.size(); ++r) a.dst[r] = reinterpret_cast<float*>(dst[r]);
+  a.dst_offset = dst_offset;
+  DFL_CHECK_RC(dfl_peer_put_f32(&a, cur_stream()), "peer_put_f32");
+}
 
 }  // namespace
 
@@ -317,6 +392,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("timestep_embed", &timestep_embed);
   m.def("attention", &attention, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"),
         py::arg("out") = py::none(), py::arg("lse") = py::none(), py::arg("kv_lo") = py::none(),
-        py::arg("kv_hi") = py::none());
+        py::arg("kv_hi") = py::none(), py::arg("o_peer") = std::vector<int64_t>{},
+        py::arg("seg0_len") = 0, py::arg("seg0_per") = 0, py::arg("seg1_per") = 0,
+        py::arg("o_strides") = std::vector<int64_t>{});
   m.def("error_word", &error_word);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("from_ptr", &from_ptr);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("peer_barrier", &peer_barrier);
+  m.def("peer_put_f32", &peer_put_f32);
 }

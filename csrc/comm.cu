@@ -1,0 +1,102 @@
+// Communication runtime for NVLink / NVSwitch peer memory (sm_100a).
+//
+//   * symmetric buffers: every rank cudaMalloc's the same sizes and exports a
+//     CUDA IPC handle; peers open it, giving each kernel a table of peer
+//     pointers (plain P2P loads / stores over NVLink, no multicast objects)
+//   * peer barrier: one tiny kernel; each rank release-stores an epoch into
+//     every peer's flag slot and acquire-polls its own slots.  The epoch is a
+//     device-side counter, so the barrier stays correct across CUDA-graph
+//     replays.  Every wait is bounded: on timeout the kernel records
+//     kErrPeerTimeout in the error word and returns (no trap, no hang)
+//   * peer all-gather of a small f32 vector (sharded GEMV results)
+//
+// Reference parity: the NCCL bootstrap / groups of
+// difflet/backends/cuda/ops_impl/parallel_mesh.py:80-118 and the collectives
+// of difflet/backends/neuron/ops_impl/collectives.py:115-368, whose data
+// movement the fused kernels (attention epilogue, q/k/v scatter) now perform.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+using namespace dfl;
+
+DFL_DEVICE void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+DFL_DEVICE int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void peer_barrier_kernel(BarrierArgs a) {
+  __shared__ int epoch;
+  // A peer already timed out on this device: fail fast instead of waiting again.
+  if (a.err != nullptr && *(volatile int*)a.err == kErrPeerTimeout) return;
+  if (threadIdx.x == 0) epoch = *a.counter + 1;
+  __syncthreads();
+  const int e = epoch;
+  const int t = threadIdx.x;
+  if (t < a.world) {
+    __threadfence_system();
+    st_release_sys(a.flags[t] + a.rank, e);
+  }
+  if (t < a.world) {
+    const int* mine = a.flags[a.rank] + t;
+    long long t0 = clock64();
+    unsigned it = 0;
+    while ((int)(ld_acquire_sys(mine) - e) < 0) {
+      if ((++it & 63u) == 0 && clock64() - t0 > a.timeout_cycles) {
+        record_error(a.err, kErrPeerTimeout, kKidComm, t, e);
+        break;
+      }
+    }
+    __threadfence_system();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *a.counter = e;
+}
+
+// dst[r] + offset <- src (this rank's slice) for every peer r, f32 vectors.
+__global__ void peer_put_f32_kernel(PeerPutArgs a) {
+  const long long n = a.n;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    float v = a.src[i];
+    for (int r = 0; r < a.world; ++r) a.dst[r][a.dst_offset + i] = v;
+  }
+}
+
+}  // namespace
+
+extern "C" int dfl_ipc_handle(const void* ptr, void* out64) {
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return (int)e;
+  memcpy(out64, &h, sizeof(h));
+  return 0;
+}
+
+extern "C" int dfl_ipc_open(const void* handle64, void** out) {
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess);
+  return (int)e;
+}
+
+extern "C" int dfl_ipc_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
+
+extern "C" int dfl_peer_barrier(const BarrierArgs* a, cudaStream_t stream) {
+  if (a->world < 1 || a->world > DFL_MAX_PEERS || a->rank < 0 || a->rank >= a->world) return -2;
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(*a);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int dfl_peer_put_f32(const PeerPutArgs* a, cudaStream_t stream) {
+  if (a->world < 1 || a->world > DFL_MAX_PEERS) return -2;
+  if (a->n == 0) return 0;
+  long long blocks = (a->n + 255) / 256;
+  if (blocks > 1024) blocks = 1024;
+  peer_put_f32_kernel<<<(int)blocks, 256, 0, stream>>>(*a);
+  return (int)cudaGetLastError();
+}

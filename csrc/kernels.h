@@ -109,8 +109,40 @@ typedef struct AttnArgs {
   float scale;
   const int* kv_lo; const int* kv_hi;           // per-batch key window [lo, hi) or NULL
   int* err;
+  // Output scatter (Ulysses head->sequence all-to-all in the epilogue): when
+  // o_world > 1, query row s is stored at o_peer[owner(s)] + b*o_bs + h*o_hs +
+  // local_row(s)*o_ss.  Rows form two segments: the first seg0_len rows are
+  // split seg0_per per rank and land first in each owner's local layout; the
+  // remaining rows are split seg1_per per rank and land after them.
+  void* o_peer[DFL_MAX_PEERS];
+  int o_world;
+  int seg0_len, seg0_per, seg1_per;
 } AttnArgs;
 int dfl_attention(const AttnArgs* a, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Peer-memory communication runtime (comm.cu)
+// ---------------------------------------------------------------------------
+int dfl_ipc_handle(const void* ptr, void* out64);
+int dfl_ipc_open(const void* handle64, void** out);
+int dfl_ipc_close(void* ptr);
+
+typedef struct BarrierArgs {
+  int* flags[DFL_MAX_PEERS];  // flags[r] = rank r's flag array (world ints), peer-mapped
+  int* counter;               // this rank's device epoch counter
+  int rank, world;
+  long long timeout_cycles;
+  int* err;
+} BarrierArgs;
+int dfl_peer_barrier(const BarrierArgs* a, cudaStream_t stream);
+
+typedef struct PeerPutArgs {
+  const float* src; long long n;
+  float* dst[DFL_MAX_PEERS];  // every rank's destination buffer
+  long long dst_offset;       // element offset of this rank's slice
+  int world;
+} PeerPutArgs;
+int dfl_peer_put_f32(const PeerPutArgs* a, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -155,16 +155,17 @@ class FluxTransformer:
         ws["qkv_img"] = e(B * S_img, 3 * D)
         ws["qkv_txt"] = e(B * S_txt, 3 * D)
         ws["mlp"] = e(B * max(S_img, S_txt), F_)
-        ws["fused"] = e(B * S_loc, 3 * D + F_)
         Hl = H // world
+        # buffers that peers store into (q/k/v, attention outputs) come from the
+        # sequence-parallel context's symmetric heap
+        pe = (lambda *shape: par.empty(shape, dt)) if par is not None else e  # noqa: E731
         if par is not None:
-            bufs = par.buffers(B, Hl, S, dh, S_loc, D, dt)
-            ws.update(bufs)
-        else:
-            ws["q"] = e(B, Hl, S, dh)
-            ws["k"] = e(B, Hl, S, dh)
-            ws["v"] = e(B, Hl, S, dh)
-            ws["attn"] = e(B, S_loc, D)
+            par.check_heads(H)
+        ws["fused"] = pe(B * S_loc, 3 * D + F_)
+        ws["q"] = pe(B, Hl, S, dh)
+        ws["k"] = pe(B, Hl, S, dh)
+        ws["v"] = pe(B, Hl, S, dh)
+        ws["attn"] = pe(B, S_loc, D)
         self._ws[key] = ws
         return ws
 
@@ -311,7 +312,8 @@ class FluxTransformer:
         q, k, v = ws["q"], ws["k"], ws["v"]
         scale = 1.0 / math.sqrt(dh)
         if par is not None:
-            par.attention(q, k, v, scale, ws, out_rows, B, S_txt, S_img, D)
+            target = ws["attn"].view(B * (S_txt + S_img), D) if out_rows is None else out_rows
+            par.attention(q, k, v, scale, target, B, S_txt, S_img, target.shape[1])
             return
         S = q.shape[2]
         if out_rows is None:

@@ -1,0 +1,179 @@
+"""Ulysses sequence parallelism for MMDiT models (joint ``[text ; image]`` attention).
+
+Semantics of the reference's ``ulysses_attention`` / joint variants
+(``difflet/backends/neuron/ops_impl/attention.py:622-713``,
+``difflet/backends/neuron/ops_impl/collectives.py:276-348``): every rank holds
+``1/N`` of the text rows and ``1/N`` of the image rows; attention needs all
+rows for ``H/N`` heads, so q/k/v go sequence->heads and the output goes
+heads->sequence.  ``heads % N == 0`` is required.
+
+Two transports with one interface:
+
+``PeerUlysses`` (B200 path)
+    q/k/v and attention-output buffers live in symmetric peer memory.  The
+    fused q/k-norm + RoPE kernel stores each head block straight into the
+    owning rank's q/k/v buffer (the seq->heads all-to-all is its store
+    pattern), and the attention kernel's epilogue stores each output row into
+    the owning rank's buffer (heads->seq).  Two device barriers per attention
+    order the traffic.  No separate collective kernels, no staging copies.
+
+``CollectiveUlysses`` (baseline / CPU)
+    The same math with ``torch.distributed.all_to_all`` (NCCL on GPU, gloo on
+    CPU) plus pack / unpack copies: the measured NCCL baseline of the fused
+    path, and the multi-rank oracle that runs on CPU gloo ranks in the tests.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from difflet_b200 import envs
+from difflet_b200.ops import fused as F
+
+
+def all_to_all(recv: list, send: list, group) -> None:
+    """``dist.all_to_all`` (NCCL), or point-to-point pairs where the backend lacks it (gloo)."""
+    if dist.get_backend(group) != "gloo":
+        dist.all_to_all(recv, send, group=group)
+        return
+    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+    me = dist.get_rank()
+    reqs = []
+    for i, r in enumerate(ranks):
+        if r == me:
+            recv[i].copy_(send[i])
+            continue
+        reqs.append(dist.isend(send[i].contiguous(), r, group=group))
+        reqs.append(dist.irecv(recv[i], r, group=group))
+    for q in reqs:
+        q.wait()
+
+
+class _Base:
+    def __init__(self, group, ranks, device):
+        self.group = group
+        self.ranks = list(ranks)
+        self.world = len(ranks)
+        self.rank = self.ranks.index(dist.get_rank())
+        self.device = device
+        self.decode_on_all_ranks = False
+
+    # token sharding of the model inputs / outputs
+    def shard_tokens(self, x: torch.Tensor) -> torch.Tensor:
+        n = x.shape[1] // self.world
+        return x[:, self.rank * n:(self.rank + 1) * n]
+
+    def gather_tokens(self, x_loc: torch.Tensor) -> torch.Tensor:
+        parts = [torch.empty_like(x_loc) for _ in range(self.world)]
+        dist.all_gather(parts, x_loc.contiguous(), group=self.group)
+        return torch.cat(parts, 1)
+
+    def check_heads(self, H: int) -> None:
+        if H % self.world:
+            raise ValueError(f"Ulysses needs heads % world == 0, got {H} heads on {self.world} ranks")
+
+
+class PeerUlysses(_Base):
+    def __init__(self, group, ranks, device):
+        super().__init__(group, ranks, device)
+        from difflet_b200.parallel.symm import SymmetricHeap
+
+        self.heap = SymmetricHeap(group, ranks, device)
+
+    def empty(self, shape, dtype):
+        return self.heap.empty(shape, dtype)
+
+    def peer_views(self, t: torch.Tensor):
+        return self.heap.peer_ptrs(t)
+
+    def before_attention(self):
+        self.heap.barrier()
+
+    def attention(self, q, k, v, scale, target, B, S_txt, S_img, ld):
+        """q/k/v: this rank's heads over the full sequence; ``target``: local [B*S_loc, ld]
+        buffer whose columns [rank*Hl*dh, (rank+1)*Hl*dh) receive this rank's heads."""
+        Hl, dh = q.shape[1], q.shape[3]
+        S_loc = S_txt + S_img
+        self.heap.barrier()  # every rank's q/k/v stores have landed
+        col = self.rank * Hl * dh * target.element_size()
+        peers = [p + col for p in self.heap.peer_ptrs(target)]
+        F.native().attention(q, k, v, float(scale), None, None, None, None, peers, S_txt * self.world, S_txt,
+                             S_img, [S_loc * ld, dh, ld])
+        self.heap.barrier()  # every output row has landed at its owner
+
+    def close(self):
+        self.heap.close()
+
+
+class CollectiveUlysses(_Base):
+    """All-to-all transport (NCCL / gloo).  ``peer_views`` returns per-destination
+    staging buffers of the full sequence; the exchange packs this rank's rows."""
+
+    def __init__(self, group, ranks, device):
+        super().__init__(group, ranks, device)
+        self._stage = {}
+        self._seg = None
+
+    def empty(self, shape, dtype):
+        return torch.zeros(shape, dtype=dtype, device=self.device)
+
+    def peer_views(self, t: torch.Tensor):
+        key = (t.data_ptr(), tuple(t.shape), tuple(t.stride()))
+        if key not in self._stage:
+            self._stage[key] = (t, [torch.zeros_like(t) for _ in range(self.world)])
+        return self._stage[key][1]
+
+    def before_attention(self):
+        pass
+
+    def _rows(self, S_txt, S_img, r):
+        """Global row indices owned by rank r: its text rows then its image rows."""
+        Tg = S_txt * self.world
+        txt = torch.arange(r * S_txt, (r + 1) * S_txt)
+        img = Tg + torch.arange(r * S_img, (r + 1) * S_img)
+        return torch.cat([txt, img]).to(self.device)
+
+    def _exchange_qkv(self, S_txt, S_img):
+        for t, stages in list(self._stage.values()):
+            # staging[r] holds this rank's rows for destination r's heads
+            mine = self._rows(S_txt, S_img, self.rank)
+            send = [s[:, :, mine].contiguous() for s in stages]
+            recv = [torch.empty_like(send[0]) for _ in range(self.world)]
+            all_to_all(recv, send, self.group)
+            for src in range(self.world):
+                t[:, :, self._rows(S_txt, S_img, src)] = recv[src]
+            for s in stages:
+                s.zero_()
+
+    def attention(self, q, k, v, scale, target, B, S_txt, S_img, ld):
+        Hl, S, dh = q.shape[1], q.shape[2], q.shape[3]
+        self._exchange_qkv(S_txt, S_img)
+        o = torch.empty(B, S, Hl * dh, dtype=q.dtype, device=q.device)
+        F.attention(q, k, v, scale, out=o.view(B, S, Hl, dh).permute(0, 2, 1, 3))
+        send = [o[:, self._rows(S_txt, S_img, r)].contiguous() for r in range(self.world)]
+        recv = [torch.empty_like(send[0]) for _ in range(self.world)]
+        all_to_all(recv, send, self.group)
+        S_loc = S_txt + S_img
+        tv = target.view(B, S_loc, ld)
+        for src in range(self.world):
+            tv[:, :, src * Hl * dh:(src + 1) * Hl * dh] = recv[src]
+
+    def close(self):
+        self._stage.clear()
+
+
+def make_sequence_parallel(parallel, device, transport: str | None = None):
+    """Ulysses context over the cp axis of ``parallel`` (cp_mode='ulysses')."""
+    from difflet_b200.parallel import groups
+
+    if not dist.is_initialized():
+        raise RuntimeError("sequence parallelism needs an initialised process group (run under torchrun)")
+    if parallel.tp_degree != 1 or parallel.cfg_parallel_enabled or parallel.dp_degree != 1:
+        raise NotImplementedError("this build's FLUX path composes Ulysses CP only (tp=1, no cfg/dp)")
+    groups.init_mesh(parallel.mesh_spec)
+    group, ranks = groups.get_group("cp"), groups.get_group_ranks("cp")
+    transport = transport or envs.DIFFLET_KERNEL_COMM
+    if device.type == "cuda" and transport == "fused":
+        return PeerUlysses(group, ranks, device)
+    return CollectiveUlysses(group, ranks, device)
