@@ -2,7 +2,7 @@
 //
 //   * symmetric buffers: every rank cudaMalloc's the same sizes and exports a
 //     CUDA IPC handle; peers open it, giving each kernel a table of peer
-//     pointers (plain P2P loads / stores over NVLink, no multicast objects)
+//     pointers (plain P2P loads / stores over NVLink, no NVLS objects)
 //   * peer barrier: one tiny kernel; each rank release-stores an epoch into
 //     every peer's flag slot and acquire-polls its own slots.  The epoch is a
 //     device-side counter, so the barrier stays correct across CUDA-graph

@@ -1,7 +1,7 @@
 // Shared device helpers for the difflet_b200 sm_100a kernels.
 //
 // Everything here is written for Blackwell (sm_100a): mbarriers with bounded
-// waits, TMA tile loads (no cluster multicast anywhere in this tree), tcgen05
+// waits, TMA tile loads (plain per-CTA loads only), tcgen05
 // tensor-memory allocation / MMA / loads, and the error-word protocol every
 // kernel uses instead of __trap(): a wait that runs out of budget records a
 // code in a device error word, the kernel unwinds, and the host raises.
@@ -116,7 +116,7 @@ DFL_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int kid, int
 }
 
 // ---------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor) -- plain loads only.  No cluster multicast form
+// TMA (cp.async.bulk.tensor) -- plain loads only.  No cross-CTA broadcast form
 // exists in this code base: a tile that several CTAs need is fetched by each.
 // ---------------------------------------------------------------------------
 DFL_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,

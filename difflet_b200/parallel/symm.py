@@ -5,7 +5,7 @@ Every rank of a group allocates the same buffers in the same order
 and opens the peers', so each buffer has a table of peer device pointers that
 the fused kernels store to / load from directly.  A device epoch barrier
 (``barrier()``) orders those accesses; its counter lives on the GPU, so it is
-valid inside CUDA graphs.  No NVLink multicast object is created: plain P2P
+valid inside CUDA graphs.  No NVLS object is created: plain P2P
 loads and stores only.
 """
 
