@@ -113,7 +113,7 @@ class CollectiveUlysses(_Base):
     def __init__(self, group, ranks, device):
         super().__init__(group, ranks, device)
         self._stage = {}
-        self._seg = None
+        self._row_cache = {}
 
     def empty(self, shape, dtype):
         return torch.zeros(shape, dtype=dtype, device=self.device)
@@ -128,11 +128,15 @@ class CollectiveUlysses(_Base):
         pass
 
     def _rows(self, S_txt, S_img, r):
-        """Global row indices owned by rank r: its text rows then its image rows."""
-        Tg = S_txt * self.world
-        txt = torch.arange(r * S_txt, (r + 1) * S_txt)
-        img = Tg + torch.arange(r * S_img, (r + 1) * S_img)
-        return torch.cat([txt, img]).to(self.device)
+        """Global row indices owned by rank r: its text rows then its image rows (cached on
+        the device, so the first, eager call fills the cache before any graph capture)."""
+        key = (S_txt, S_img, r)
+        if key not in self._row_cache:
+            Tg = S_txt * self.world
+            txt = torch.arange(r * S_txt, (r + 1) * S_txt)
+            img = Tg + torch.arange(r * S_img, (r + 1) * S_img)
+            self._row_cache[key] = torch.cat([txt, img]).to(self.device)
+        return self._row_cache[key]
 
     def _exchange_qkv(self, S_txt, S_img):
         for t, stages in list(self._stage.values()):

@@ -143,7 +143,7 @@ def write_manifest(path: Path, spec: CacheSpec, extra: dict | None = None) -> Pa
     path.mkdir(parents=True, exist_ok=True)
     doc = {"key": cache_key(spec), "inputs": _normalize(spec.cache_inputs()),
            "metadata": spec.manifest_metadata(), **(extra or {})}
-    tmp = path / (MANIFEST_FILENAME + ".tmp")
+    tmp = path / f"{MANIFEST_FILENAME}.{os.getpid()}.tmp"  # unique per writer; rename is atomic
     tmp.write_text(json.dumps(doc, indent=2, sort_keys=True))
     os.replace(tmp, path / MANIFEST_FILENAME)
     return path / MANIFEST_FILENAME

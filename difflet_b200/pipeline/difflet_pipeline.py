@@ -87,8 +87,16 @@ class DiffletPipeline:
         pipe = cls(app=app, model_id=model_id, model_path=model_path, model_entry=entry,
                    compiled_path=compiled_path, cache_spec=spec, shape=shape, parallel=par, dtype=dtype,
                    backend=platform.name)
-        if not skip_compile and (force_compile or not has_valid_manifest(compiled_path, spec)):
-            pipe.compile(force=True)
+        if not skip_compile:
+            # one writer per node: local rank 0 builds and writes the manifest, the rest wait
+            import torch.distributed as dist
+
+            from difflet_b200 import envs
+
+            if envs.LOCAL_RANK == 0 and (force_compile or not has_valid_manifest(compiled_path, spec)):
+                pipe.compile(force=True)
+            if dist.is_initialized():
+                dist.barrier()
         if load:
             pipe.load(skip_warmup=skip_warmup)
         return pipe
