@@ -1,16 +1,23 @@
 // Flash attention forward for sm_100a (head_dim 128, bf16 in/out, fp32 softmax).
 //
-// One CTA per (128-query tile, head, batch).  Warp roles:
-//   warp 0      TMA producer: Q once, then K_j / V_j tiles into a 2-stage ring
-//   warp 1      MMA issuer: S_j = Q K_j^T into a double-buffered TMEM tile,
-//               O += P_{j-1} V_{j-1} (V read as an MN-major operand)
-//   warps 2..5  softmax: one query row per thread; S from TMEM, running max in
-//               log2 units, P = exp2(s - m) written to a 128B-swizzled smem
-//               tile for the PV MMA.  O is rescaled in TMEM only when the max
-//               grew by more than 2^8 (the stale max keeps P <= 256, exact
-//               after the final 1/l), then normalised and stored.
-// Optional per-batch key window [kv_lo, kv_hi) and natural-log LSE output
-// (for ring / context-parallel merges).
+// One CTA per (256-query block, head, batch), two 128-row Q tiles in ping-pong:
+//   warp 0      TMA producer: Q0/Q1 once, then K_j / V_j tiles (2-stage ring,
+//               shared by both Q tiles)
+//   warp 1      MMA issuer, in the order  PV0(j-1), QK0(j), PV1(j-1), QK1(j):
+//               S_g = Q_g K_j^T into TMEM; P_g (bf16) is written back over S_g
+//               by the softmax warps and consumed as the A operand straight
+//               from TMEM (tcgen05.mma ... [a_tmem]); O_g += P_g V (V read from
+//               smem as an MN-major operand).  tcgen05 operations of one thread
+//               complete in order, so when S_g(j) is ready the previous PV_g
+//               has finished: no extra barrier guards P reuse or O rescaling.
+//   warps 2..5  softmax for Q tile 0; warps 6..9 for Q tile 1: one query row per
+//               thread, running max in log2 units, exp2 on the SFU, P packed to
+//               bf16x2 and stored to TMEM; O_g is rescaled in TMEM only when the
+//               max grew by more than 2^8 (a stale max keeps P <= 256, exact
+//               after the final 1/l); epilogue normalises and stores rows.
+// Optional per-batch key window [kv_lo, kv_hi), natural-log LSE output (ring /
+// context-parallel merges), and an output-row scatter into peer ranks' buffers
+// (the Ulysses head->sequence all-to-all done by the epilogue's stores).
 //
 // Reference parity: attention contract of difflet/ops/attention.py:4-128 and
 // the CUDA SDPA path difflet/backends/cuda/ops_impl/attention.py:41-86 (scale
@@ -22,31 +29,58 @@
 namespace {
 using namespace dfl;
 
-constexpr int kBM = 128;   // queries per CTA
+constexpr int kBM = 128;   // queries per Q tile
+constexpr int kQT = 2;     // Q tiles per CTA
 constexpr int kBN = 128;   // keys per tile
 constexpr int kD = 128;    // head dim
 constexpr int kNS = 2;     // K/V ring depth
-constexpr int kThreads = 192;
-constexpr int kTileBytes = kBM * kD * 2;  // 32 KB (two 16 KB swizzle chunks)
+constexpr int kThreads = 320;
+constexpr int kTileBytes = 128 * kD * 2;  // 32 KB (two 16 KB swizzle chunks)
 constexpr int kChunk = 16384;
 
 struct AttnSmem {
-  static constexpr int kQ = 0;
-  static constexpr int kP = kQ + kTileBytes;
-  static constexpr int kK = kP + kTileBytes;
-  static constexpr int kV = kK + kNS * kTileBytes;
+  static constexpr int kQ = 0;                              // kQT tiles
+  static constexpr int kK = kQ + kQT * kTileBytes;          // kNS tiles
+  static constexpr int kV = kK + kNS * kTileBytes;          // kNS tiles
   static constexpr int kBar = kV + kNS * kTileBytes;
-  // q_full, k_full[NS], v_full[NS], k_empty[NS], v_empty[NS], s_full[2], s_empty[2],
-  // p_full, pv_done, o_full
-  static constexpr int kNumBars = 1 + 4 * kNS + 4 + 3;
+  // q_full, k_full[NS], v_full[NS], k_empty[NS], v_empty[NS], s_full[2], p_full[2], o_full
+  static constexpr int kNumBars = 1 + 4 * kNS + 2 + 2 + 1;
   static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
 };
+
+// TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512)
+__device__ __forceinline__ uint32_t tmem_s_col(int g) { return g == 0 ? 0u : 128u; }
+__device__ __forceinline__ uint32_t tmem_o_col(int g) { return g == 0 ? 256u : 384u; }
 
 // 2^x on the SFU (PTX ex2.approx.ftz.f32); inputs here are <= 8 after the max shift.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]  (A: M x K, one row per lane, 2 bf16 per column)
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
 
 struct AttnParams {
@@ -77,6 +111,15 @@ __device__ __forceinline__ __nv_bfloat16* out_row(const AttnParams& p, int b, in
   return p.o_peer[owner] + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)lrow * p.o_ss;
 }
 
+__device__ __forceinline__ void tma_load_4d(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, AttnParams p, int* err) {
@@ -90,16 +133,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = v_full + kNS;
   uint64_t* v_empty = k_empty + kNS;
   uint64_t* s_full = v_empty + kNS;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* pv_done = p_full + 1;
-  uint64_t* o_full = pv_done + 1;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AttnSmem::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qt * kBM;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = blockIdx.x * (kQT * kBM);
   const int lo = p.kv_lo ? max(0, p.kv_lo[b]) : 0;
   const int hi = p.kv_hi ? min(p.Sk, p.kv_hi[b]) : p.Sk;
   const int t_first = lo / kBN;
@@ -108,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < AttnSmem::kNumBars; ++i) {
       uint64_t* bar = &bars[i];
-      const bool softmax_arrivals = (bar == s_empty) || (bar == s_empty + 1) || (bar == p_full);
+      const bool softmax_arrivals = (bar == p_full) || (bar == p_full + 1);
       mbar_init(bar, softmax_arrivals ? 128 : 1);
     }
     *abort_flag = 0;
@@ -126,21 +167,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem + 256;
 
   if (warp == 0) {
+    // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
-      uint8_t* sq = smem + AttnSmem::kQ;
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      // Q: two 64-wide d chunks
-      for (int c = 0; c < 2; ++c) {
-        asm volatile(
-            "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
-            " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(sq + c * kChunk)),
-            "l"(reinterpret_cast<uint64_t>(&tq)), "r"(smem_u32(q_full)), "r"(c * 64), "r"(q0),
-            "r"(h), "r"(b)
-            : "memory");
-      }
+      mbar_arrive_expect_tx(q_full, kQT * kTileBytes);
+      for (int g = 0; g < kQT; ++g)
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d(smem + AttnSmem::kQ + g * kTileBytes + c * kChunk, &tq, q_full, c * 64,
+                      q0 + g * kBM, h, b);
       bool issued_k[kNS] = {false, false}, issued_v[kNS] = {false, false};
       uint32_t par_k[kNS] = {0, 0}, par_v[kNS] = {0, 0};
       bool ok = true;
@@ -158,19 +193,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* dst = smem + (which == 0 ? AttnSmem::kK : AttnSmem::kV) + st * kTileBytes;
           const CUtensorMap* map = which == 0 ? &tk : &tv;
           mbar_arrive_expect_tx(full, kTileBytes);
-          for (int c = 0; c < 2; ++c) {
-            asm volatile(
-                "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst + c * kChunk)),
-                "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(full)), "r"(c * 64), "r"(k0),
-                "r"(h), "r"(b)
-                : "memory");
-          }
+          for (int c = 0; c < 2; ++c) tma_load_4d(dst + c * kChunk, map, full, c * 64, k0, h, b);
           if (which == 0) issued_k[st] = true, par_k[st] = par;
           else issued_v[st] = true, par_v[st] = par;
         }
       }
-      if (!ok) {
+      if (!ok) {  // our own bulk copies must land before the CTA exits
         mbar_wait(q_full, 0, nullptr, 0, 0, nullptr, 200000000LL);
         for (int s = 0; s < kNS; ++s) {
           if (issued_k[s]) mbar_wait(&k_full[s], par_k[s], nullptr, 0, 0, nullptr, 200000000LL);
@@ -179,147 +207,151 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_bf16_f32(kBM, kD, 0, 1);
-      const uint32_t q_addr = smem_u32(smem + AttnSmem::kQ);
-      const uint32_t p_addr = smem_u32(smem + AttnSmem::kP);
       bool ok = mbar_wait(q_full, 0, err, kKidAttn, 110, abort_flag);
-      auto issue_pv = [&](int jj) -> bool {
-        const int st = jj % kNS;
-        if (!mbar_wait(p_full, jj & 1, err, kKidAttn, 111, abort_flag)) return false;
-        if (!mbar_wait(&v_full[st], (jj / kNS) & 1, err, kKidAttn, 112, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + AttnSmem::kV + st * kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          uint64_t ad = make_sdesc_sw128(p_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
-          uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, kChunk, 1024);
-          umma_f16_ss(tmem_o, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(pv_done);
-        umma_commit(&v_empty[st]);
-        return true;
-      };
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j % kNS;
-        const int sb = j & 1;
-        if (!mbar_wait(&k_full[st], (j / kNS) & 1, err, kKidAttn, 113, abort_flag)) { ok = false; break; }
-        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1u, err, kKidAttn, 114, abort_flag)) { ok = false; break; }
-        tc_fence_after();
+      auto issue_qk = [&](int g, int st) {
+        const uint32_t q_addr = smem_u32(smem + AttnSmem::kQ + g * kTileBytes);
         const uint32_t k_addr = smem_u32(smem + AttnSmem::kK + st * kTileBytes);
-        const uint32_t s_tmem = tmem + sb * 128;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           uint64_t ad = make_sdesc_sw128(q_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
           uint64_t bd = make_sdesc_sw128(k_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
-          umma_f16_ss(s_tmem, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + tmem_s_col(g), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[sb]);
+        umma_commit(&s_full[g]);
+      };
+      auto issue_pv = [&](int g, int jj) -> bool {
+        if (!mbar_wait(&p_full[g], jj & 1, err, kKidAttn, 111 + g, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + AttnSmem::kV + (jj % kNS) * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, kChunk, 1024);
+          umma_f16_ts(tmem + tmem_o_col(g), tmem + tmem_s_col(g) + kk * 8, bd, idesc_pv,
+                      (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        return true;
+      };
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % kNS;
+        if (!mbar_wait(&k_full[st], (j / kNS) & 1, err, kKidAttn, 113, abort_flag)) { ok = false; break; }
+        const int pst = (j + kNS - 1) % kNS;
+        if (j > 0) {
+          if (!mbar_wait(&v_full[pst], ((j - 1) / kNS) & 1, err, kKidAttn, 114, abort_flag)) { ok = false; break; }
+          if (!issue_pv(0, j - 1)) { ok = false; break; }
+        }
+        tc_fence_after();
+        issue_qk(0, st);
+        if (j > 0) {
+          if (!issue_pv(1, j - 1)) { ok = false; break; }
+          umma_commit(&v_empty[pst]);
+        }
+        issue_qk(1, st);
         umma_commit(&k_empty[st]);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
       }
-      if (ok && issue_pv(n_tiles - 1)) umma_commit(o_full);
+      if (ok) {
+        const int jl = n_tiles - 1;
+        const int pst = jl % kNS;
+        if (mbar_wait(&v_full[pst], (jl / kNS) & 1, err, kKidAttn, 115, abort_flag) && issue_pv(0, jl) &&
+            issue_pv(1, jl)) {
+          umma_commit(&v_empty[pst]);
+          umma_commit(o_full);
+        }
+      }
     }
   } else {
-    // ---------------- softmax / correction / epilogue ----------------
-    const int sub = warp & 3;
-    const int row = sub * 32 + lane;  // TMEM lane == query row within the tile
+    // ------------------------------------------------------------ softmax groups
+    const int g = (warp - 2) / 4;           // Q tile of this warpgroup
+    const int sub = warp & 3;               // TMEM lane quarter of this warp
+    const int row = sub * 32 + lane;        // row within the Q tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
+    const uint32_t s_t = tmem + lane_base + tmem_s_col(g);
+    const uint32_t o_t = tmem + lane_base + tmem_o_col(g);
     float m = -INFINITY;  // running max (log2 domain)
     float l = 0.f;
     bool ok = true;
-    uint8_t* p_smem = smem + AttnSmem::kP;
     for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, err, kKidAttn, 120, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&s_full[g], j & 1, err, kKidAttn, 120 + g, abort_flag)) { ok = false; break; }
       tc_fence_after();
       float s[128];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]);
-        tmem_ld_32x32b_x32(tmem + lane_base + sb * 128 + c * 32, chunk);
-      }
+      for (int c = 0; c < 4; ++c)
+        tmem_ld_32x32b_x32(s_t + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
       const int k0 = (t_first + j) * kBN;
-      const bool edge = (k0 < lo) || (k0 + kBN > hi);
-      float mx = -INFINITY;
+      if ((k0 < lo) || (k0 + kBN > hi)) {  // edge tile: mask keys outside [lo, hi)
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float v = s[c] * p.scale_log2;
-        if (edge) {
-          int key = k0 + c;
-          if (key < lo || key >= hi) v = -INFINITY;
+        for (int c = 0; c < 128; ++c) {
+          const int key = k0 + c;
+          if (key < lo || key >= hi) s[c] = -INFINITY;
         }
-        s[c] = v;
-        mx = fmaxf(mx, v);
       }
-      const float m_new = fmaxf(m, mx);
-      // Rescale decision is warp-uniform (tcgen05.ld/st are warp-collective).
+      // row max over raw scores: 8 independent chains (short dependency depth)
+      float mxa[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mxa[t] = s[t];
+#pragma unroll
+      for (int c = 8; c < 128; c += 8) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) mxa[t] = fmaxf(mxa[t], s[c + t]);
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+      const float m_new = fmaxf(m, mx * p.scale_log2);  // scale > 0: max commutes with it
+      // the rescale decision is warp-uniform: tcgen05.ld / st are warp-collective
       const bool need = (j > 0) && __any_sync(0xffffffffu, m_new > m + 8.0f);
       const float m_old = m;
       if (j == 0 || need) m = m_new;
       const float m_use = (m == -INFINITY) ? 0.f : m;
-      // exp2 into packed bf16 registers before waiting on the previous PV, so
-      // the exponentials overlap the tensor-core work.
-      uint32_t pk[64];
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        float e0 = fast_exp2(s[2 * c] - m_use);
-        float e1 = fast_exp2(s[2 * c + 1] - m_use);
-        rs += e0 + e1;
-        pk[c] = pack_bf16x2(e0, e1);
-      }
-      if (j > 0) {
-        // PV_{j-1} must finish before P is overwritten or O is rescaled.
-        if (!mbar_wait(pv_done, (j - 1) & 1, err, kKidAttn, 121, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        if (need) {
-          const float f = (m_old == -INFINITY) ? 0.f : fast_exp2(m_old - m);
+      if (need) {
+        // O_g is stable: PV_g(j-1) completed before S_g(j) (in-order tcgen05)
+        const float f = (m_old == -INFINITY) ? 0.f : fast_exp2(m_old - m);
 #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
-            uint32_t o_raw[16];
-            tmem_ld_32x32b_x16(tmem_o + lane_base + c * 16, o_raw);
-            tmem_wait_ld();
+        for (int c = 0; c < 8; ++c) {
+          uint32_t o_raw[16];
+          tmem_ld_32x32b_x16(o_t + c * 16, o_raw);
+          tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * f);
-            tmem_st_32x32b_x16(tmem_o + lane_base + c * 16, o_raw);
-          }
-          tmem_wait_st();
-          l *= f;
+          for (int e = 0; e < 16; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * f);
+          tmem_st_32x32b_x16(o_t + c * 16, o_raw);
         }
+        l *= f;
       }
-      // P -> smem, 128B swizzle: 16B unit u of row r sits at (u ^ (r & 7)) * 16
+      // p = 2^(s * scale_log2 - m): one FFMA + one SFU op per element; 4 sum chains
+      const float sc = p.scale_log2, neg_m = -m_use;
+      float rsa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint8_t* rowp = p_smem + c * kChunk + row * 128;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int b0 = c * 32 + u * 4;
-          uint4 w = make_uint4(pk[b0], pk[b0 + 1], pk[b0 + 2], pk[b0 + 3]);
-          *reinterpret_cast<uint4*>(rowp + ((u ^ (row & 7)) * 16)) = w;
+        for (int c = 0; c < 32; ++c) {
+          const float e0 = fast_exp2(fmaf(s[half * 64 + 2 * c], sc, neg_m));
+          const float e1 = fast_exp2(fmaf(s[half * 64 + 2 * c + 1], sc, neg_m));
+          rsa[c & 3] += e0 + e1;
+          pk[c] = pack_bf16x2(e0, e1);
         }
+        tmem_st_32x32b_x32(s_t + half * 32, pk);
       }
-      l += rs;
-      fence_proxy_async_shared();
+      l += (rsa[0] + rsa[1]) + (rsa[2] + rsa[3]);
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[g]);
     }
-    // ---------------- epilogue ----------------
-    const int qrow = q0 + row;
+    // ------------------------------------------------------------ epilogue
+    const int qrow = q0 + g * kBM + row;
     if (ok && n_tiles > 0 && mbar_wait(o_full, 0, err, kKidAttn, 122, abort_flag)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* op = out_row(p, b, h, qrow);
+      __nv_bfloat16* op = qrow < p.Sq ? out_row(p, b, h, qrow) : nullptr;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o_raw[32];
-        tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o_raw);
+        tmem_ld_32x32b_x32(o_t + c * 32, o_raw);
         tmem_wait_ld();
-        if (qrow < p.Sq) {
+        if (op != nullptr) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 w;
@@ -410,7 +442,7 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
     if (e != cudaSuccess) return (int)e;
     attr = true;
   }
-  dim3 grid((a->Sq + kBM - 1) / kBM, a->H, a->B);
+  dim3 grid((a->Sq + kQT * kBM - 1) / (kQT * kBM), a->H, a->B);
   attn_fwd_kernel<<<grid, kThreads, AttnSmem::kTotal, stream>>>(tq, tk, tv, p, a->err);
   return (int)cudaGetLastError();
 }

@@ -4,7 +4,11 @@ Every number is a CUDA-event time on the launching stream after warm-up, with
 an L2 flush (a 256 MB write) before each timed launch, reported as the median
 of the timed launches.  Usage::
 
-    python -m difflet_b200.bench.kernels [--only gemm,attn,ln] [--iters 20]
+    python -m difflet_b200.bench.kernels [--only gemm,attn,ln] [--cases flux_1gpu,...]
+                                         [--iters 20] [--no-ref]
+
+``--no-ref`` skips the library comparison (used for ncu captures so the
+profiled process launches only our kernels).
 """
 
 from __future__ import annotations
@@ -15,9 +19,18 @@ import math
 
 import torch
 
-
-def _flush(buf):
-    buf.zero_()
+GEMM_SHAPES = [
+    ("flux_qkv_img", 4096, 9216, 3072),
+    ("flux_single_fused", 4608, 21504, 3072),
+    ("flux_single_proj_out", 4608, 3072, 15360),
+    ("flux_mlp_up", 4096, 12288, 3072),
+    ("flux_mlp_down", 4096, 3072, 12288),
+    ("flux_sp8_fused", 576, 21504, 3072),
+    ("wan_ffn_up_sp4", 18900, 13824, 5120),
+    ("square_8192", 8192, 8192, 8192),
+]
+ATTN_CASES = [("flux_1gpu", 1, 24, 4608), ("flux_sp8_heads", 1, 3, 4608), ("wan_ulysses4", 1, 10, 75600 // 4)]
+LN_CASES = [("flux_ln", 4608, 3072), ("wan_ln_sp4", 18900, 5120)]
 
 
 def time_fn(fn, iters=20, warmup=3, flush=None):
@@ -27,7 +40,7 @@ def time_fn(fn, iters=20, warmup=3, flush=None):
     times = []
     for _ in range(iters):
         if flush is not None:
-            _flush(flush)
+            flush.zero_()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
@@ -38,58 +51,53 @@ def time_fn(fn, iters=20, warmup=3, flush=None):
     return times[len(times) // 2]
 
 
-def bench_gemm(nat, iters, flush, peaks):
+def _sel(items, cases):
+    return [it for it in items if not cases or it[0] in cases]
+
+
+def bench_gemm(nat, iters, flush, peaks, cases, ref):
     rows = []
-    shapes = [
-        ("flux_qkv_img", 4096, 9216, 3072),
-        ("flux_single_fused", 4608, 21504, 3072),
-        ("flux_single_proj_out", 4608, 3072, 15360),
-        ("flux_mlp_up", 4096, 12288, 3072),
-        ("flux_mlp_down", 4096, 3072, 12288),
-        ("wan_ffn_up_sp4", 18900, 13824, 5120),
-        ("square_8192", 8192, 8192, 8192),
-    ]
-    for name, M, N, K in shapes:
+    for name, M, N, K in _sel(GEMM_SHAPES, cases):
         a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
         b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
         out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         t_ours = time_fn(lambda: nat.gemm(a, b, None, out=out), iters, flush=flush)
-        t_ref = time_fn(lambda: torch.matmul(a, b.t(), out=out), iters, flush=flush)
         fl = 2.0 * M * N * K
-        rows.append({
-            "kernel": "gemm_tcgen05", "shape": name, "M": M, "N": N, "K": K,
-            "ms": round(t_ours, 4), "tflops": round(fl / t_ours / 1e9, 1),
-            "cublas_ms": round(t_ref, 4), "cublas_tflops": round(fl / t_ref / 1e9, 1),
-            "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3),
-        })
+        r = {"kernel": "gemm_tcgen05", "shape": name, "M": M, "N": N, "K": K, "ms": round(t_ours, 4),
+             "tflops": round(fl / t_ours / 1e9, 1),
+             "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3)}
+        if ref:
+            t_ref = time_fn(lambda: torch.matmul(a, b.t(), out=out), iters, flush=flush)
+            r.update({"cublas_ms": round(t_ref, 4), "cublas_tflops": round(fl / t_ref / 1e9, 1)})
+        rows.append(r)
         del a, b, out
     return rows
 
 
-def bench_attn(nat, iters, flush, peaks):
+def bench_attn(nat, iters, flush, peaks, cases, ref):
     rows = []
-    cases = [("flux_1gpu", 1, 24, 4608), ("flux_sp8_heads", 1, 3, 4608), ("wan_ulysses4", 1, 10, 75600 // 4)]
-    for name, B, H, S in cases:
+    for name, B, H, S in _sel(ATTN_CASES, cases):
         q = torch.randn(B, H, S, 128, device="cuda", dtype=torch.bfloat16)
         k = torch.randn_like(q)
         v = torch.randn_like(q)
         o = torch.empty_like(q)
         sc = 1 / math.sqrt(128)
         t_ours = time_fn(lambda: nat.attention(q, k, v, sc, out=o), iters, flush=flush)
-        t_ref = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=sc), iters, flush=flush)
         fl = 4.0 * B * H * S * S * 128
-        rows.append({
-            "kernel": "attn_tcgen05", "shape": name, "B": B, "H": H, "S": S,
-            "ms": round(t_ours, 4), "tflops": round(fl / t_ours / 1e9, 1),
-            "sdpa_ms": round(t_ref, 4), "sdpa_tflops": round(fl / t_ref / 1e9, 1),
-            "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3),
-        })
+        r = {"kernel": "attn_tcgen05", "shape": name, "B": B, "H": H, "S": S, "ms": round(t_ours, 4),
+             "tflops": round(fl / t_ours / 1e9, 1),
+             "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3)}
+        if ref:
+            t_ref = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=sc), iters,
+                            flush=flush)
+            r.update({"sdpa_ms": round(t_ref, 4), "sdpa_tflops": round(fl / t_ref / 1e9, 1)})
+        rows.append(r)
     return rows
 
 
-def bench_ln(nat, iters, flush, peaks):
+def bench_ln(nat, iters, flush, peaks, cases, ref):
     rows = []
-    for name, M, D in [("flux_ln", 4608, 3072), ("wan_ln_sp4", 18900, 5120)]:
+    for name, M, D in _sel(LN_CASES, cases):
         x = torch.randn(M, D, device="cuda", dtype=torch.bfloat16)
         y = torch.empty_like(x)
         sh = torch.randn(1, D, device="cuda")
@@ -105,7 +113,9 @@ def bench_ln(nat, iters, flush, peaks):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,ln")
+    ap.add_argument("--cases", default="")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--no-ref", action="store_true")
     args = ap.parse_args(argv)
     from difflet_b200 import _native
     from difflet_b200.utils.peaks import load_peaks
@@ -114,13 +124,15 @@ def main(argv=None):
     peaks = load_peaks()
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
     only = set(args.only.split(","))
+    cases = set(c for c in args.cases.split(",") if c)
+    ref = not args.no_ref
     rows = []
     if "gemm" in only:
-        rows += bench_gemm(nat, args.iters, flush, peaks)
+        rows += bench_gemm(nat, args.iters, flush, peaks, cases, ref)
     if "attn" in only:
-        rows += bench_attn(nat, args.iters, flush, peaks)
+        rows += bench_attn(nat, args.iters, flush, peaks, cases, ref)
     if "ln" in only:
-        rows += bench_ln(nat, args.iters, flush, peaks)
+        rows += bench_ln(nat, args.iters, flush, peaks, cases, ref)
     _native.check_device_errors()
     for r in rows:
         print(json.dumps(r))
