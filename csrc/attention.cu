@@ -30,17 +30,19 @@ namespace {
 using namespace dfl;
 
 constexpr int kBM = 128;   // queries per Q tile
-constexpr int kQT = 2;     // Q tiles per CTA
 constexpr int kBN = 128;   // keys per tile
 constexpr int kD = 128;    // head dim
 constexpr int kNS = 2;     // K/V ring depth
-constexpr int kThreads = 320;
 constexpr int kTileBytes = 128 * kD * 2;  // 32 KB (two 16 KB swizzle chunks)
 constexpr int kChunk = 16384;
 
+// QT = Q tiles per CTA: 2 (ping-pong, default) or 1 (small grids: twice the CTAs)
+template <int QT>
 struct AttnSmem {
-  static constexpr int kQ = 0;                              // kQT tiles
-  static constexpr int kK = kQ + kQT * kTileBytes;          // kNS tiles
+  static constexpr int kThreads = 64 + 128 * QT;
+  static constexpr uint32_t kTmemCols = QT == 2 ? 512 : 256;
+  static constexpr int kQ = 0;                              // QT tiles
+  static constexpr int kK = kQ + QT * kTileBytes;           // kNS tiles
   static constexpr int kV = kK + kNS * kTileBytes;          // kNS tiles
   static constexpr int kBar = kV + kNS * kTileBytes;
   // q_full, k_full[NS], v_full[NS], k_empty[NS], v_empty[NS], s_full[2], p_full[2], o_full
@@ -48,9 +50,11 @@ struct AttnSmem {
   static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
 };
 
-// TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512)
-__device__ __forceinline__ uint32_t tmem_s_col(int g) { return g == 0 ? 0u : 128u; }
-__device__ __forceinline__ uint32_t tmem_o_col(int g) { return g == 0 ? 256u : 384u; }
+// TMEM columns: S_g/P_g at [128 g, 128 g + 128), O_g after all S tiles
+// (QT=2: S0 0, S1 128, O0 256, O1 384; QT=1: S0 0, O0 128)
+__device__ __forceinline__ uint32_t tmem_s_col(int g) { return 128u * g; }
+template <int QT>
+__device__ __forceinline__ uint32_t tmem_o_col(int g) { return 128u * (QT + g); }
 
 // 2^x on the SFU (PTX ex2.approx.ftz.f32); inputs here are <= 8 after the max shift.
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -120,13 +124,14 @@ __device__ __forceinline__ void tma_load_4d(uint8_t* dst, const CUtensorMap* map
       : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <int QT>
+__global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, AttnParams p, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnSmem::kBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnSmem<QT>::kBar);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + kNS;
@@ -135,19 +140,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = v_empty + kNS;
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AttnSmem::kNumBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AttnSmem<QT>::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * (kQT * kBM);
+  const int q0 = blockIdx.x * (QT * kBM);
   const int lo = p.kv_lo ? max(0, p.kv_lo[b]) : 0;
   const int hi = p.kv_hi ? min(p.Sk, p.kv_hi[b]) : p.Sk;
   const int t_first = lo / kBN;
   const int n_tiles = hi > lo ? (hi + kBN - 1) / kBN - t_first : 0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < AttnSmem::kNumBars; ++i) {
+    for (int i = 0; i < AttnSmem<QT>::kNumBars; ++i) {
       uint64_t* bar = &bars[i];
       const bool softmax_arrivals = (bar == p_full) || (bar == p_full + 1);
       mbar_init(bar, softmax_arrivals ? 128 : 1);
@@ -160,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tv);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, AttnSmem<QT>::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -171,10 +176,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
-      mbar_arrive_expect_tx(q_full, kQT * kTileBytes);
-      for (int g = 0; g < kQT; ++g)
+      mbar_arrive_expect_tx(q_full, QT * kTileBytes);
+      for (int g = 0; g < QT; ++g)
         for (int c = 0; c < 2; ++c)
-          tma_load_4d(smem + AttnSmem::kQ + g * kTileBytes + c * kChunk, &tq, q_full, c * 64,
+          tma_load_4d(smem + AttnSmem<QT>::kQ + g * kTileBytes + c * kChunk, &tq, q_full, c * 64,
                       q0 + g * kBM, h, b);
       bool issued_k[kNS] = {false, false}, issued_v[kNS] = {false, false};
       uint32_t par_k[kNS] = {0, 0}, par_v[kNS] = {0, 0};
@@ -190,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          uint8_t* dst = smem + (which == 0 ? AttnSmem::kK : AttnSmem::kV) + st * kTileBytes;
+          uint8_t* dst = smem + (which == 0 ? AttnSmem<QT>::kK : AttnSmem<QT>::kV) + st * kTileBytes;
           const CUtensorMap* map = which == 0 ? &tk : &tv;
           mbar_arrive_expect_tx(full, kTileBytes);
           for (int c = 0; c < 2; ++c) tma_load_4d(dst + c * kChunk, map, full, c * 64, k0, h, b);
@@ -213,8 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_pv = make_idesc_bf16_f32(kBM, kD, 0, 1);
       bool ok = mbar_wait(q_full, 0, err, kKidAttn, 110, abort_flag);
       auto issue_qk = [&](int g, int st) {
-        const uint32_t q_addr = smem_u32(smem + AttnSmem::kQ + g * kTileBytes);
-        const uint32_t k_addr = smem_u32(smem + AttnSmem::kK + st * kTileBytes);
+        const uint32_t q_addr = smem_u32(smem + AttnSmem<QT>::kQ + g * kTileBytes);
+        const uint32_t k_addr = smem_u32(smem + AttnSmem<QT>::kK + st * kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           uint64_t ad = make_sdesc_sw128(q_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
@@ -226,11 +231,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_pv = [&](int g, int jj) -> bool {
         if (!mbar_wait(&p_full[g], jj & 1, err, kKidAttn, 111 + g, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + AttnSmem::kV + (jj % kNS) * kTileBytes);
+        const uint32_t v_addr = smem_u32(smem + AttnSmem<QT>::kV + (jj % kNS) * kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, kChunk, 1024);
-          umma_f16_ts(tmem + tmem_o_col(g), tmem + tmem_s_col(g) + kk * 8, bd, idesc_pv,
+          umma_f16_ts(tmem + tmem_o_col<QT>(g), tmem + tmem_s_col(g) + kk * 8, bd, idesc_pv,
                       (jj > 0 || kk > 0) ? 1u : 0u);
         }
         return true;
@@ -246,17 +251,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         issue_qk(0, st);
         if (j > 0) {
-          if (!issue_pv(1, j - 1)) { ok = false; break; }
+          if (QT == 2 && !issue_pv(1, j - 1)) { ok = false; break; }
           umma_commit(&v_empty[pst]);
         }
-        issue_qk(1, st);
+        if (QT == 2) issue_qk(1, st);
         umma_commit(&k_empty[st]);
       }
       if (ok) {
         const int jl = n_tiles - 1;
         const int pst = jl % kNS;
         if (mbar_wait(&v_full[pst], (jl / kNS) & 1, err, kKidAttn, 115, abort_flag) && issue_pv(0, jl) &&
-            issue_pv(1, jl)) {
+            (QT == 1 || issue_pv(1, jl))) {
           umma_commit(&v_empty[pst]);
           umma_commit(o_full);
         }
@@ -269,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = sub * 32 + lane;        // row within the Q tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
     const uint32_t s_t = tmem + lane_base + tmem_s_col(g);
-    const uint32_t o_t = tmem + lane_base + tmem_o_col(g);
+    const uint32_t o_t = tmem + lane_base + tmem_o_col<QT>(g);
     float m = -INFINITY;  // running max (log2 domain)
     float l = 0.f;
     bool ok = true;
@@ -376,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == 1) tmem_dealloc(tmem, AttnSmem<QT>::kTmemCols);
 }
 
 int make_tmap_4d(CUtensorMap* map, const void* base, long long S, int H, int B, long long ss,
@@ -390,6 +395,23 @@ int make_tmap_4d(CUtensorMap* map, const void* base, long long S, int H, int B, 
   return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int QT>
+int launch_attn(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
+                const CUtensorMap& tv, cudaStream_t stream) {
+  static bool attr[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 15]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnSmem<QT>::kTotal);
+    if (e != cudaSuccess) return (int)e;
+    attr[dev & 15] = true;
+  }
+  dim3 grid((a->Sq + QT * kBM - 1) / (QT * kBM), a->H, a->B);
+  attn_fwd_kernel<QT><<<grid, AttnSmem<QT>::kThreads, AttnSmem<QT>::kTotal, stream>>>(tq, tk, tv, p, a->err);
+  return (int)cudaGetLastError();
 }
 
 }  // namespace
@@ -435,14 +457,12 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
     for (int r = 0; r < a->o_world; ++r)
       if (!a->o_peer[r] || (reinterpret_cast<uintptr_t>(a->o_peer[r]) & 15)) return -8;
   }
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         AttnSmem::kTotal);
-    if (e != cudaSuccess) return (int)e;
-    attr = true;
-  }
-  dim3 grid((a->Sq + kQT * kBM - 1) / (kQT * kBM), a->H, a->B);
-  attn_fwd_kernel<<<grid, kThreads, AttnSmem::kTotal, stream>>>(tq, tk, tv, p, a->err);
-  return (int)cudaGetLastError();
+  // Two ping-pong Q tiles per CTA unless that leaves more than half the SMs idle:
+  // then one Q tile per CTA doubles the CTA count while still fitting one wave.
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = dfl_host::num_sms(dev);
+  const long long ctas2 = (long long)((a->Sq + 2 * kBM - 1) / (2 * kBM)) * a->H * a->B;
+  if (ctas2 * 2 <= sms) return launch_attn<1>(a, p, tq, tk, tv, stream);
+  return launch_attn<2>(a, p, tq, tk, tv, stream);
 }

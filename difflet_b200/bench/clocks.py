@@ -15,7 +15,7 @@ QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
 
 
 class ClockSampler:
-    def __init__(self, gpu_indices=None, period_ms: int = 200):
+    def __init__(self, gpu_indices=None, period_ms: int = 50):
         self.gpus = None if gpu_indices is None else {int(i) for i in gpu_indices}
         self.period_ms = period_ms
         self.proc = None
@@ -30,6 +30,18 @@ class ClockSampler:
                                          stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # do not start the timed region before the sampler is producing rows
+        import time
+
+        t0 = time.time()
+        while time.time() - t0 < 5.0:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):

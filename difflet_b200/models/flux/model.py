@@ -200,6 +200,11 @@ class FluxTransformer:
 
     def modulation(self, temb: torch.Tensor) -> torch.Tensor:
         """All blocks' adaLN vectors in one GEMV: f32 [B, N_mod] = W_mod silu(temb) + b."""
+        par = self.par
+        if par is not None and hasattr(par, "shard_gemv") and temb.is_cuda:
+            out = par.shard_gemv(self.w["mod.w"], temb, self.w["mod.b"], silu_in=True)
+            if out is not None:
+                return out
         return F.gemv(self.w["mod.w"], temb, self.w["mod.b"], silu_in=True)
 
     # ------------------------------------------------------------------ forward

@@ -87,6 +87,28 @@ class PeerUlysses(_Base):
     def peer_views(self, t: torch.Tensor):
         return self.heap.peer_ptrs(t)
 
+    def shard_gemv(self, W, x, bias, *, silu_in=False, silu_out=False):
+        """Row-sharded GEMV + all-gather by peer stores: each rank reads 1/N of W
+        (the adaLN modulation matrix is 6.5 GB for FLUX) and writes its slice of
+        the f32 result into every rank's symmetric copy.  Returns None when the
+        shape does not shard (the caller then runs the full GEMV)."""
+        N = W.shape[0]
+        if x.shape[0] != 1 or N % self.world or (N // self.world) % 4:
+            return None
+        if not hasattr(self, "_gemv_out"):
+            self._gemv_out = {}
+        out = self._gemv_out.get(N)
+        if out is None:
+            out = self._gemv_out[N] = self.heap.empty((1, N), torch.float32)
+        n = N // self.world
+        r0 = self.rank * n
+        F.gemv(W[r0:r0 + n], x, None if bias is None else bias[r0:r0 + n], silu_in=silu_in, silu_out=silu_out,
+               out=out[:, r0:r0 + n])
+        self.heap.barrier()  # every rank is done reading its copy from the previous step
+        F.native().peer_put_f32(out[0, r0:r0 + n], self.heap.peer_ptrs(out), r0)
+        self.heap.barrier()  # every slice has landed everywhere
+        return out
+
     def before_attention(self):
         self.heap.barrier()
 
