@@ -48,3 +48,27 @@ def video_ids(t_tokens: int, h_tokens: int, w_tokens: int) -> torch.Tensor:
     h = torch.arange(h_tokens)[None, :, None].expand(t_tokens, h_tokens, w_tokens)
     w = torch.arange(w_tokens)[None, None, :].expand(t_tokens, h_tokens, w_tokens)
     return torch.stack([t, h, w], -1).reshape(-1, 3)
+
+
+def joint_ids(family: str, S_txt: int, grid, order: str = "txt_img") -> torch.Tensor:
+    """Position ids of the joint sequence for an MMDiT family.
+
+    * ``flux`` / ``hunyuan_video``: image/video tokens get (t, h, w); text gets 0
+      on every axis (an identity rotation, i.e. text is not rotated).
+    * ``qwen_image`` (centred "MSRoPE"): image rows / columns are centred
+      (positions -(n - n//2) .. n//2 - 1); text tokens get position
+      max(h//2, w//2) + i on all three axes.
+    """
+    t, h, w = grid
+    if family == "qwen_image":
+        tt = torch.arange(t)[:, None, None].expand(t, h, w)
+        hh = (torch.arange(h) - (h - h // 2))[None, :, None].expand(t, h, w)
+        ww = (torch.arange(w) - (w - w // 2))[None, None, :].expand(t, h, w)
+        img = torch.stack([tt, hh, ww], -1).reshape(-1, 3)
+        m = max(h // 2, w // 2)
+        txt = torch.arange(m, m + S_txt)[:, None].expand(S_txt, 3)
+    else:
+        img = video_ids(t, h, w)
+        txt = torch.zeros(S_txt, 3, dtype=img.dtype)
+    parts = [txt, img] if order == "txt_img" else [img, txt]
+    return torch.cat(parts, 0)

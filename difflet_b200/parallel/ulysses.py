@@ -112,16 +112,18 @@ class PeerUlysses(_Base):
     def before_attention(self):
         self.heap.barrier()
 
-    def attention(self, q, k, v, scale, target, B, S_txt, S_img, ld):
-        """q/k/v: this rank's heads over the full sequence; ``target``: local [B*S_loc, ld]
-        buffer whose columns [rank*Hl*dh, (rank+1)*Hl*dh) receive this rank's heads."""
+    def attention(self, q, k, v, scale, target, B, n0, n1, ld, kv_lo=None, kv_hi=None):
+        """q/k/v: this rank's heads over the full sequence ``[seg0 ; seg1]``; each rank
+        owns ``n0`` rows of seg0 and ``n1`` rows of seg1.  ``target``: local
+        [B*(n0+n1), ld] buffer whose columns [rank*Hl*dh, (rank+1)*Hl*dh) receive this
+        rank's heads for the rows it owns (written by the peers' epilogues)."""
         Hl, dh = q.shape[1], q.shape[3]
-        S_loc = S_txt + S_img
+        S_loc = n0 + n1
         self.heap.barrier()  # every rank's q/k/v stores have landed
         col = self.rank * Hl * dh * target.element_size()
         peers = [p + col for p in self.heap.peer_ptrs(target)]
-        F.native().attention(q, k, v, float(scale), None, None, None, None, peers, S_txt * self.world, S_txt,
-                             S_img, [S_loc * ld, dh, ld])
+        F.native().attention(q, k, v, float(scale), None, None, kv_lo, kv_hi, peers, n0 * self.world, n0, n1,
+                             [S_loc * ld, dh, ld])
         self.heap.barrier()  # every output row has landed at its owner
 
     def close(self):
@@ -172,11 +174,12 @@ class CollectiveUlysses(_Base):
             for s in stages:
                 s.zero_()
 
-    def attention(self, q, k, v, scale, target, B, S_txt, S_img, ld):
+    def attention(self, q, k, v, scale, target, B, S_txt, S_img, ld, kv_lo=None, kv_hi=None):
+        # S_txt / S_img here are the per-rank row counts of seg0 / seg1
         Hl, S, dh = q.shape[1], q.shape[2], q.shape[3]
         self._exchange_qkv(S_txt, S_img)
         o = torch.empty(B, S, Hl * dh, dtype=q.dtype, device=q.device)
-        F.attention(q, k, v, scale, out=o.view(B, S, Hl, dh).permute(0, 2, 1, 3))
+        F.attention(q, k, v, scale, out=o.view(B, S, Hl, dh).permute(0, 2, 1, 3), kv_lo=kv_lo, kv_hi=kv_hi)
         send = [o[:, self._rows(S_txt, S_img, r)].contiguous() for r in range(self.world)]
         recv = [torch.empty_like(send[0]) for _ in range(self.world)]
         all_to_all(recv, send, self.group)
