@@ -371,6 +371,16 @@ void peer_put_f32(const at::Tensor& src, std::vector<int64_t> dst, int64_t dst_o
   DFL_CHECK_RC(dfl_peer_put_f32(&a, cur_stream()), "peer_put_f32");
 }
 
+void cfg_combine(const at::Tensor& mine, int64_t peer_ptr, at::Tensor out, double scale, bool mine_is_cond) {
+  check_bf16_cuda(mine, "mine");
+  TORCH_CHECK(mine.is_contiguous() && out.is_contiguous() && out.scalar_type() == at::kFloat &&
+                  out.numel() == mine.numel(), "mine (bf16) / out (f32) must be contiguous and equal in size");
+  const c10::cuda::CUDAGuard guard(mine.device());
+  DFL_CHECK_RC(dfl_cfg_combine(mine.data_ptr(), reinterpret_cast<const void*>(peer_ptr), out.data_ptr<float>(),
+                               mine.numel(), (float)scale, mine_is_cond ? 1 : 0, cur_stream()),
+               "cfg_combine");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -403,4 +413,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close);
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_put_f32", &peer_put_f32);
+  m.def("cfg_combine", &cfg_combine);
 }

@@ -67,7 +67,51 @@ __global__ void peer_put_f32_kernel(PeerPutArgs a) {
   }
 }
 
+// CFG-parallel exchange fused with the guidance combine: this rank holds one
+// branch's prediction, the partner's is read straight from its memory over
+// NVLink; out (f32) = u + s (c - u).
+__global__ void cfg_combine_kernel(const __nv_bfloat16* __restrict__ mine, const __nv_bfloat16* peer,
+                                   float* __restrict__ out, long long n, float s, int mine_is_cond) {
+  const long long n8 = n / 8;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const uint4 a = reinterpret_cast<const uint4*>(mine)[i];
+    const uint4 b = reinterpret_cast<const uint4*>(peer)[i];
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    float r[8];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float2 fa = unpack_bf16x2(av[h]), fb = unpack_bf16x2(bv[h]);
+      const float2 u = mine_is_cond ? fb : fa, c = mine_is_cond ? fa : fb;
+      r[2 * h] = u.x + s * (c.x - u.x);
+      r[2 * h + 1] = u.y + s * (c.y - u.y);
+    }
+    reinterpret_cast<float4*>(out)[2 * i] = make_float4(r[0], r[1], r[2], r[3]);
+    reinterpret_cast<float4*>(out)[2 * i + 1] = make_float4(r[4], r[5], r[6], r[7]);
+  }
+  for (long long i = n8 * 8 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float fa = __bfloat162float(mine[i]), fb = __bfloat162float(peer[i]);
+    const float u = mine_is_cond ? fb : fa, c = mine_is_cond ? fa : fb;
+    out[i] = u + s * (c - u);
+  }
+}
+
 }  // namespace
+
+extern "C" int dfl_cfg_combine(const void* mine, const void* peer, float* out, long long n, float scale,
+                               int mine_is_cond, cudaStream_t stream) {
+  if (n == 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(mine) | reinterpret_cast<uintptr_t>(peer) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return -2;
+  long long blocks = (n / 8 + 255) / 256;
+  if (blocks > 2048) blocks = 2048;
+  if (blocks < 1) blocks = 1;
+  cfg_combine_kernel<<<(int)blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(mine),
+                                                      reinterpret_cast<const __nv_bfloat16*>(peer), out, n, scale,
+                                                      mine_is_cond);
+  return (int)cudaGetLastError();
+}
 
 extern "C" int dfl_ipc_handle(const void* ptr, void* out64) {
   cudaIpcMemHandle_t h;

@@ -144,6 +144,10 @@ typedef struct PeerPutArgs {
 } PeerPutArgs;
 int dfl_peer_put_f32(const PeerPutArgs* a, cudaStream_t stream);
 
+// CFG-parallel: out (f32) = u + s (c - u), partner branch read over NVLink.
+int dfl_cfg_combine(const void* mine, const void* peer, float* out, long long n, float scale,
+                    int mine_is_cond, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

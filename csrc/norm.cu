@@ -193,10 +193,16 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
     float sq = 0.f, sk = 0.f;
     for (int h = warp; h < a.H; h += 4) {
       float xq[E], xk[E];
-      load_head<DH>(src + a.q_off + h * DH, lane, xq);
-      load_head<DH>(src + a.k_off + h * DH, lane, xk);
+      if (a.q_off >= 0) {
+        load_head<DH>(src + a.q_off + h * DH, lane, xq);
 #pragma unroll
-      for (int e = 0; e < E; ++e) sq += xq[e] * xq[e], sk += xk[e] * xk[e];
+        for (int e = 0; e < E; ++e) sq += xq[e] * xq[e];
+      }
+      if (a.k_off >= 0) {
+        load_head<DH>(src + a.k_off + h * DH, lane, xk);
+#pragma unroll
+        for (int e = 0; e < E; ++e) sk += xk[e] * xk[e];
+      }
     }
     sq = warp_sum(sq);
     sk = warp_sum(sk);
@@ -220,6 +226,7 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
     for (int which = 0; which < 2; ++which) {
       float x[E];
       const int off = which == 0 ? a.q_off : a.k_off;
+      if (off < 0) continue;  // stream not present (q-only / k,v-only passes)
       load_head<DH>(src + off + h * DH, lane, x);
       const __nv_bfloat16* wn = reinterpret_cast<const __nv_bfloat16*>(which == 0 ? a.wq : a.wk);
       if (a.norm_mode == 1) {
@@ -247,7 +254,7 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
       store_head<DH>(dst + dst_off, lane, x);
     }
     // v: plain copy into the destination layout
-    {
+    if (a.v_off >= 0) {
       float x[E];
       load_head<DH>(src + a.v_off + h * DH, lane, x);
       store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.v_dst[r]) + dst_off, lane, x);

@@ -135,10 +135,14 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
     position ``seq_off + s``.  ``heads_per_rank`` splits heads over the list.
     """
     qkv2 = _rows2d(qkv)
-    world = len(q_dst)
+    world = len(q_dst if q_dst is not None else (k_dst if k_dst is not None else v_dst))
     hpr = heads_per_rank or (H // world)
+    # a negative offset skips that stream (q-only / k,v-only passes); its destinations may be None
+    q_dst = q_dst if q_dst is not None else [None] * world
+    k_dst = k_dst if k_dst is not None else [None] * world
+    v_dst = v_dst if v_dst is not None else [None] * world
     if qkv2.is_cuda:
-        ptr = lambda ts: [t if isinstance(t, int) else t.data_ptr() for t in ts]  # noqa: E731
+        ptr = lambda ts: [0 if t is None else (t if isinstance(t, int) else t.data_ptr()) for t in ts]  # noqa: E731
         native().qkv_scatter(qkv2, q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos, sin,
                              rope_pos_off, rope_half, hpr, ptr(q_dst), ptr(k_dst), ptr(v_dst), S_dst,
                              seq_off, token_major)
@@ -147,35 +151,36 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
     B = rows // S_src
     ct = torch.float64 if qkv2.dtype == torch.float64 else torch.float32
     x = qkv2.to(ct).view(B, S_src, -1)
-    q = x[..., q_off:q_off + H * dh].reshape(B, S_src, H, dh)
-    k = x[..., k_off:k_off + H * dh].reshape(B, S_src, H, dh)
-    v = x[..., v_off:v_off + H * dh].reshape(B, S_src, H, dh)
-    if norm_mode == 1:
-        q = q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + eps)
-        k = k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + eps)
-        if wq is not None:
-            q = q * wq.to(ct)
-        if wk is not None:
-            k = k * wk.to(ct)
-    elif norm_mode == 2:
-        qf = q.reshape(B, S_src, H * dh)
-        kf = k.reshape(B, S_src, H * dh)
-        qf = qf * torch.rsqrt(qf.pow(2).mean(-1, keepdim=True) + eps)
-        kf = kf * torch.rsqrt(kf.pow(2).mean(-1, keepdim=True) + eps)
-        if wq is not None:
-            qf = qf * wq.to(ct)
-        if wk is not None:
-            kf = kf * wk.to(ct)
-        q, k = qf.view(B, S_src, H, dh), kf.view(B, S_src, H, dh)
-    q, k, v = (t.permute(0, 2, 1, 3) for t in (q, k, v))  # B, H, S, dh
+
+    def take(off):
+        return None if off < 0 else x[..., off:off + H * dh].reshape(B, S_src, H, dh)
+
+    q, k, v = take(q_off), take(k_off), take(v_off)
+
+    def norm(t, wn):
+        if t is None or norm_mode == 0:
+            return t
+        if norm_mode == 1:
+            t = t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps)
+            return t * wn.to(ct) if wn is not None else t
+        tf = t.reshape(B, S_src, H * dh)
+        tf = tf * torch.rsqrt(tf.pow(2).mean(-1, keepdim=True) + eps)
+        if wn is not None:
+            tf = tf * wn.to(ct)
+        return tf.view(B, S_src, H, dh)
+
+    q, k = norm(q, wq), norm(k, wk)
+    q, k, v = (None if t is None else t.permute(0, 2, 1, 3) for t in (q, k, v))  # B, H, S, dh
     if cos is not None:
         c = cos[rope_pos_off:rope_pos_off + S_src].to(ct)
         s_ = sin[rope_pos_off:rope_pos_off + S_src].to(ct)
-        q = _rope_cpu(q, c, s_, rope_half)
-        k = _rope_cpu(k, c, s_, rope_half)
+        q = None if q is None else _rope_cpu(q, c, s_, rope_half)
+        k = None if k is None else _rope_cpu(k, c, s_, rope_half)
     for r in range(world):
         hs = slice(r * hpr, (r + 1) * hpr)
         for src, dst in ((q, q_dst[r]), (k, k_dst[r]), (v, v_dst[r])):
+            if src is None:
+                continue
             part = src[:, hs]
             if token_major:
                 dst.view(B, S_dst, hpr, dh)[:, seq_off:seq_off + S_src] = part.permute(0, 2, 1, 3).to(dst.dtype)

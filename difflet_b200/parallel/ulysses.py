@@ -193,16 +193,35 @@ class CollectiveUlysses(_Base):
 
 
 def make_sequence_parallel(parallel, device, transport: str | None = None):
-    """Ulysses context over the cp axis of ``parallel`` (cp_mode='ulysses')."""
+    """Ulysses context over the cp axis of ``parallel`` (None when cp_degree == 1)."""
     from difflet_b200.parallel import groups
 
     if not dist.is_initialized():
         raise RuntimeError("sequence parallelism needs an initialised process group (run under torchrun)")
-    if parallel.tp_degree != 1 or parallel.cfg_parallel_enabled or parallel.dp_degree != 1:
-        raise NotImplementedError("this build's FLUX path composes Ulysses CP only (tp=1, no cfg/dp)")
-    groups.init_mesh(parallel.mesh_spec)
+    if parallel.tp_degree != 1 or parallel.dp_degree != 1:
+        raise NotImplementedError("sequence parallelism composes with cfg-parallel here (tp=1, dp=1)")
+    if groups.mesh() != parallel.mesh_spec:
+        groups.init_mesh(parallel.mesh_spec)
+    if parallel.cp_degree == 1:
+        return None
     group, ranks = groups.get_group("cp"), groups.get_group_ranks("cp")
     transport = transport or envs.DIFFLET_KERNEL_COMM
     if device.type == "cuda" and transport == "fused":
         return PeerUlysses(group, ranks, device)
     return CollectiveUlysses(group, ranks, device)
+
+
+def make_cfg_parallel(parallel, device, transport: str | None = None):
+    """CFG-parallel context over the cfg axis (None when cfg-parallel is off)."""
+    from difflet_b200.parallel import groups
+    from difflet_b200.parallel.cfg import CollectiveCfg, PeerCfg
+
+    if not parallel.cfg_parallel_enabled:
+        return None
+    if groups.mesh() != parallel.mesh_spec:
+        groups.init_mesh(parallel.mesh_spec)
+    group, ranks = groups.get_group("cfg"), groups.get_group_ranks("cfg")
+    transport = transport or envs.DIFFLET_KERNEL_COMM
+    if device.type == "cuda" and transport == "fused":
+        return PeerCfg(group, ranks, device)
+    return CollectiveCfg(group, ranks, device)
