@@ -1,0 +1,52 @@
+"""HunyuanVideo (registry ``hunyuan_video``) and HunyuanVideo 1.5 (``hunyuan_video_15``) engines.
+
+Reference: ``difflet/models/hunyuan_video/*`` and
+``difflet/backends/cuda/hunyuan_video{,_15}/*``.  HunyuanVideo is
+guidance-distilled (embedded guidance 6.0, flow shift 7.0); 1.5 runs true CFG
+(6.0) on token-refined Qwen2.5-VL text with 32-channel latents.
+"""
+
+from __future__ import annotations
+
+from difflet_b200.models.mmdit.entry import MMDiTEngine
+from difflet_b200.models.vae.hunyuan_vae import HunyuanVAEConfig, HunyuanVAEDecoder
+
+
+class HunyuanVideoEngine(MMDiTEngine):
+    preset = "hunyuan-video"
+    default_shape = {"height": 720, "width": 1280, "num_frames": 129}
+
+    def make_vae(self, dev):
+        if self.kw.get("random_init") or not self.model_path:
+            return HunyuanVAEDecoder.random_init(HunyuanVAEConfig(), device=dev, dtype=self.dtype, seed=5)
+        from difflet_b200.utils.checkpoint import load_component
+
+        return HunyuanVAEDecoder(HunyuanVAEConfig(), load_component(self.model_path, "vae", dtype=self.dtype, device=dev))
+
+    def app_kwargs(self):
+        return {"flow_shift": float(self.kw.get("flow_shift", 7.0)), "text_len": 256}
+
+
+class HunyuanVideo15Engine(HunyuanVideoEngine):
+    preset = "hunyuan-video-1.5"
+    default_shape = {"height": 480, "width": 848, "num_frames": 121}
+
+    def make_vae(self, dev):
+        cfg = HunyuanVAEConfig(latent_channels=32, block_out_channels=(128, 256, 512, 1024, 1024))
+        if self.kw.get("random_init") or not self.model_path:
+            return HunyuanVAEDecoder.random_init(cfg, device=dev, dtype=self.dtype, seed=6)
+        from difflet_b200.utils.checkpoint import load_component
+
+        return HunyuanVAEDecoder(cfg, load_component(self.model_path, "vae", dtype=self.dtype, device=dev))
+
+    def app_kwargs(self):
+        return {"flow_shift": float(self.kw.get("flow_shift", 5.0)), "text_len": 256, "true_cfg": True,
+                "cond_channels": self.cfg.in_channels - self.cfg.latent_channels}
+
+
+def create_application(**kw):
+    return HunyuanVideoEngine(**kw)
+
+
+def create_application_15(**kw):
+    return HunyuanVideo15Engine(**kw)

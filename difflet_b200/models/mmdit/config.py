@@ -83,6 +83,12 @@ PRESETS = {
     "tiny-hunyuan": MMDiTConfig(family="hunyuan_video", hidden=256, heads=2, head_dim=128, double_blocks=2,
                                 single_blocks=2, theta=256.0, order="img_txt", refiner_layers=2, text_dim=256,
                                 pooled_dim=256, guidance_embed=True, vae_scale_t=4),
+    # HunyuanVideo 1.5 (480p T2V): 54 dual-stream blocks, 16 heads, 1x1x1 patches of
+    # [32 latent | 32 condition | 1 mask] channels, token-refined Qwen2.5-VL text, true CFG
+    "hunyuan-video-1.5": MMDiTConfig(family="hunyuan_video", hidden=2048, heads=16, double_blocks=54,
+                                     single_blocks=0, theta=256.0, order="img_txt", refiner_layers=2,
+                                     text_dim=3584, pooled_dim=0, guidance_embed=False, in_channels=65,
+                                     out_channels=32, latent_channels=32, patch=1, vae_scale=16, vae_scale_t=4),
     # Qwen-Image 20B: 60 dual-stream blocks, Qwen2.5-VL text (3584), no pooled / guidance
     "qwen-image": MMDiTConfig(family="qwen_image", double_blocks=60, single_blocks=0, text_dim=3584, pooled_dim=0,
                               guidance_embed=False, txt_norm=True),
