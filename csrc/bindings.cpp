@@ -381,6 +381,28 @@ void cfg_combine(const at::Tensor& mine, int64_t peer_ptr, at::Tensor out, doubl
                "cfg_combine");
 }
 
+// TeaCache probe.  Scratch comes from torch's caching allocator, one buffer per
+// device, kept (and left ready) between calls.
+at::Tensor rel_l1(const at::Tensor& a, const at::Tensor& b) {
+  check_bf16_cuda(a, "a");
+  check_bf16_cuda(b, "b");
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && a.numel() == b.numel(), "a / b must match");
+  const c10::cuda::CUDAGuard guard(a.device());
+  static at::Tensor scratch[16];
+  int dev = c10::cuda::current_device();
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int blocks = dfl_rel_l1_blocks(a.numel(), sms);
+  const long long need = dfl_rel_l1_scratch_floats(blocks);
+  if (!scratch[dev].defined() || scratch[dev].numel() < need)
+    scratch[dev] = at::zeros({need}, a.options().dtype(at::kFloat));
+  at::Tensor out = at::empty({1}, a.options().dtype(at::kFloat));
+  DFL_CHECK_RC(dfl_rel_l1(a.data_ptr(), b.data_ptr(), a.numel(), scratch[dev].data_ptr<float>(), blocks,
+                          out.data_ptr<float>(), cur_stream()),
+               "rel_l1");
+  return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -414,4 +436,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_put_f32", &peer_put_f32);
   m.def("cfg_combine", &cfg_combine);
+  m.def("rel_l1", &rel_l1);
 }

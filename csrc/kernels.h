@@ -148,6 +148,14 @@ int dfl_peer_put_f32(const PeerPutArgs* a, cudaStream_t stream);
 int dfl_cfg_combine(const void* mine, const void* peer, float* out, long long n, float scale,
                     int mine_is_cond, cudaStream_t stream);
 
+// TeaCache probe: out = sum|a - b| / sum|b| (bf16 inputs, f32 scalar out).  `scratch`
+// holds dfl_rel_l1_scratch_floats(blocks) floats, zero on first use (the kernel
+// leaves its ticket at zero again for the next call).
+long long dfl_rel_l1_scratch_floats(int blocks);
+int dfl_rel_l1_blocks(long long n, int num_sms);
+int dfl_rel_l1(const void* a, const void* b, long long n, float* scratch, int blocks, float* out,
+               cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

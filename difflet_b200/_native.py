@@ -32,6 +32,7 @@ CUDA_SOURCES = [
     "comm.cu",
     "mx.cu",
     "conv.cu",
+    "probe.cu",
 ]
 CPP_SOURCES = ["bindings.cpp"]
 HEADERS = ["common.cuh", "kernels.h"]

@@ -1,0 +1,63 @@
+"""Data-parallel replicas for batch generation: a filesystem claim protocol.
+
+Reference: ``difflet/cli/dp/router.py:28-248`` and ``difflet/cli/dp/claims.py:19-76``.
+A JSONL file of requests is split across ``dp`` worker processes, each pinned to
+its own GPU subset (``CUDA_VISIBLE_DEVICES``).  A worker claims request ``i`` by
+creating ``<work>/<i>.claim`` with O_CREAT | O_EXCL; it writes ``<i>.done`` or
+``<i>.failed`` when finished, so a rerun resumes where the last one stopped and
+no request runs twice.  The dp axis carries no per-step collective.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+
+def try_claim(work: Path, i: int) -> bool:
+    if (work / f"{i}.done").exists():
+        return False
+    try:
+        fd = os.open(str(work / f"{i}.claim"), os.O_CREAT | os.O_EXCL | os.O_WRONLY, 0o644)
+    except FileExistsError:
+        return False
+    os.write(fd, str(os.getpid()).encode())
+    os.close(fd)
+    return True
+
+
+def mark(work: Path, i: int, ok: bool, info: dict | None = None) -> None:
+    (work / f"{i}.{'done' if ok else 'failed'}").write_text(json.dumps(info or {}))
+
+
+def load_requests(path: str) -> list[dict]:
+    return [json.loads(l) for l in Path(path).read_text().splitlines() if l.strip()]
+
+
+def worker_loop(requests: list[dict], work: Path, generate_one) -> int:
+    failures = 0
+    for i, req in enumerate(requests):
+        if not try_claim(work, i):
+            continue
+        try:
+            out = generate_one(req, i)
+            mark(work, i, True, {"output": out})
+        except Exception as exc:  # noqa: BLE001 - recorded, not fatal to the other requests
+            failures += 1
+            mark(work, i, False, {"error": repr(exc)})
+    return failures
+
+
+def run_router(argv_worker: list[str], dp: int, gpus_per_replica: int, work: str) -> int:
+    """Spawn ``dp`` worker processes of ``python -m difflet_b200 <argv_worker>`` on disjoint GPUs."""
+    Path(work).mkdir(parents=True, exist_ok=True)
+    procs = []
+    for r in range(dp):
+        env = dict(os.environ)
+        env["CUDA_VISIBLE_DEVICES"] = ",".join(str(r * gpus_per_replica + k) for k in range(gpus_per_replica))
+        env["DIFFLET_DP_RANK"] = str(r)
+        procs.append(subprocess.Popen([sys.executable, "-m", "difflet_b200"] + argv_worker, env=env))
+    return max(p.wait() for p in procs)

@@ -1,0 +1,292 @@
+"""``difflet`` command line: download -> compile -> generate (or ``run`` = all three), plan,
+serve, cache, clean, bench.
+
+Same commands and flags as the reference CLI (``difflet/cli/main.py:47-938,1300-1499``;
+flag table ``README.md:615-651``).  Multi-GPU runs re-exec under
+``torch.distributed.run`` (one rank per GPU); ``--dp N`` splits a ``--requests``
+JSONL batch over N replicas with the filesystem claim protocol.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import sys
+import time
+from pathlib import Path
+
+
+def _add_common(p: argparse.ArgumentParser) -> None:
+    p.add_argument("--model-id", required=True)
+    p.add_argument("--revision", default=None)
+    p.add_argument("--backend", default=None, choices=[None, "cuda", "cpu"])
+    p.add_argument("--tp-degree", type=int, default=1)
+    p.add_argument("--cp-degree", type=int, default=1)
+    p.add_argument("--cp-mode", default=None, choices=[None, "gather_kv", "ring", "ulysses"])
+    p.add_argument("--cfg-parallel", action="store_true")
+    p.add_argument("--sp", action="store_true")
+    p.add_argument("--dp", type=int, default=1)
+    p.add_argument("--dp-schedule", default="claim", choices=["claim", "static"])
+    p.add_argument("--mode", default=None, choices=[None, "latency", "throughput", "mixed"])
+    p.add_argument("--height", type=int, default=None)
+    p.add_argument("--width", type=int, default=None)
+    p.add_argument("--num-frames", type=int, default=None)
+    p.add_argument("--shapes", default=None)
+    p.add_argument("--cache-dir", default=None)
+    p.add_argument("--force", action="store_true")
+    p.add_argument("--random-weights", action="store_true", help="seeded random init (offline)")
+    p.add_argument("--preset", default=None, help="architecture preset override (e.g. tiny128)")
+    p.add_argument("--quant", default=None, choices=[None, "mxfp8"])
+    p.add_argument("--quant-compute", default="native", choices=["native", "dequant"])
+    p.add_argument("--teacache-cadence", type=int, default=None)
+    p.add_argument("--teacache-speedup", type=float, default=None)
+    p.add_argument("--teacache-calibration", default=None)
+    p.add_argument("--teacache-online-delta", type=float, default=None)
+    p.add_argument("--torch-compile", action="store_true", help="accepted for compatibility (no-op: native kernels)")
+    p.add_argument("--host-vae", action="store_true")
+    p.add_argument("--device-vae", action="store_true")
+
+
+def _add_gen(p: argparse.ArgumentParser) -> None:
+    p.add_argument("--prompt", default="A photo of a cat")
+    p.add_argument("--negative-prompt", default="")
+    p.add_argument("--steps", type=int, default=None)
+    p.add_argument("--guidance-scale", type=float, default=None)
+    p.add_argument("--guidance-scale-2", type=float, default=None)
+    p.add_argument("--true-cfg-scale", type=float, default=None)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--output", default="output")
+    p.add_argument("--requests", default=None, help="JSONL batch of requests")
+    p.add_argument("--work-dir", default=None)
+    p.add_argument("--keep-work-dir", action="store_true")
+
+
+def build_parser() -> argparse.ArgumentParser:
+    ap = argparse.ArgumentParser(prog="difflet", description="Blackwell-native diffusion inference")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    _add_common(sub.add_parser("download", help="download model weights from Hugging Face"))
+    _add_common(sub.add_parser("compile", help="build / verify the sm_100a kernels and write the cache manifest"))
+    g = sub.add_parser("generate", help="run inference")
+    _add_common(g)
+    _add_gen(g)
+    r = sub.add_parser("run", help="download + compile + generate")
+    _add_common(r)
+    _add_gen(r)
+    pl = sub.add_parser("plan", help="rank parallel configurations for a model on this machine")
+    pl.add_argument("--model-id", required=True)
+    pl.add_argument("--gpus", type=int, default=8)
+    pl.add_argument("--height", type=int, default=None)
+    pl.add_argument("--width", type=int, default=None)
+    pl.add_argument("--num-frames", type=int, default=None)
+    pl.add_argument("--top", type=int, default=5)
+    pl.add_argument("--json", action="store_true")
+    s = sub.add_parser("serve", help="OpenAI-compatible image / video server")
+    _add_common(s)
+    s.add_argument("--host", default="127.0.0.1")
+    s.add_argument("--port", type=int, default=8000)
+    s.add_argument("--api-key", default=None)
+    s.add_argument("--dp-degree", type=int, default=1)
+    c = sub.add_parser("cache", help="inspect the artefact cache")
+    c.add_argument("--cache-dir", default=None)
+    c.add_argument("--json", action="store_true")
+    cl = sub.add_parser("clean", help="remove cache entries")
+    cl.add_argument("--cache-dir", default=None)
+    cl.add_argument("--model", default=None)
+    cl.add_argument("--all", action="store_true")
+    b = sub.add_parser("bench", help="kernel microbenchmarks (or the headline bench with --headline)")
+    b.add_argument("--only", default="gemm,attn,ln")
+    b.add_argument("--headline", action="store_true")
+    return ap
+
+
+def parallel_from_args(a):
+    from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
+
+    cp_mode = a.cp_mode or ("ulysses" if a.cp_degree > 1 else "gather_kv")
+    return DiffletParallelConfig(tp_degree=a.tp_degree, cp_degree=a.cp_degree, cfg_parallel_enabled=a.cfg_parallel,
+                                 cp_mode=cp_mode, sp_enabled=a.sp, dp_degree=1)
+
+
+def _app_kwargs(a) -> dict:
+    kw = {}
+    if a.random_weights:
+        kw["random_init"] = True
+    if a.preset:
+        kw["preset"] = a.preset
+    if a.quant:
+        kw["quant"] = a.quant
+        kw["quant_compute"] = a.quant_compute
+    for k in ("teacache_cadence", "teacache_speedup", "teacache_calibration", "teacache_online_delta"):
+        v = getattr(a, k, None)
+        if v is not None:
+            kw[k] = v
+    return kw
+
+
+def _pipeline(a, load=True):
+    from difflet_b200.pipeline.bucketing import parse_shapes
+    from difflet_b200.pipeline.difflet_pipeline import DiffletPipeline
+
+    return DiffletPipeline.from_pretrained(
+        a.model_id, parallel=parallel_from_args(a), backend=a.backend, height=a.height, width=a.width,
+        num_frames=a.num_frames, shapes=parse_shapes(a.shapes) if a.shapes else None, revision=a.revision,
+        compile_cache_dir=a.cache_dir, force_compile=a.force, load=load, random_init=a.random_weights,
+        application_kwargs=_app_kwargs(a))
+
+
+def _gen_kwargs(a, req: dict | None = None) -> dict:
+    kw = {"prompt": a.prompt, "seed": a.seed}
+    if a.steps:
+        kw["num_inference_steps"] = a.steps
+    if a.guidance_scale is not None:
+        kw["guidance_scale"] = a.guidance_scale
+    if a.guidance_scale_2 is not None:
+        kw["guidance_scale_2"] = a.guidance_scale_2
+    if a.true_cfg_scale is not None:
+        kw["true_cfg_scale"] = a.true_cfg_scale
+    if a.negative_prompt:
+        kw["negative_prompt"] = a.negative_prompt
+    if a.height:
+        kw["height"] = a.height
+    if a.width:
+        kw["width"] = a.width
+    if a.num_frames:
+        kw["num_frames"] = a.num_frames
+    if req:
+        kw.update({k: v for k, v in req.items() if k != "output"})
+    return kw
+
+
+def save_result(out, path: str, entry) -> str:
+    from difflet_b200.utils.media import save_image, save_video
+
+    if out is None:
+        return ""
+    if out.dim() == 5:  # [B, F, H, W, 3]
+        return save_video(out[0], path if path.endswith(".avi") else path + ".avi")
+    return save_image(out[0], path if path.endswith(".png") else path + ".png")
+
+
+def _world_needed(a) -> int:
+    return parallel_from_args(a).world_size
+
+
+def cmd_generate(a) -> int:
+    world = _world_needed(a)
+    if world > 1 and not os.environ.get("DIFFLET_UNDER_TORCHRUN"):
+        from difflet_b200.cli.runner import run_torchrun
+
+        return run_torchrun(sys.argv[1:], world)
+    if a.dp > 1 and a.requests and not os.environ.get("DIFFLET_DP_RANK"):
+        from difflet_b200.cli.dp import run_router
+
+        work = a.work_dir or (a.output + ".work")
+        return run_router(sys.argv[1:], a.dp, world, work)
+    pipe = _pipeline(a)
+    entry = pipe.model_entry
+    outputs = []
+    if a.requests:
+        from difflet_b200.cli.dp import load_requests, worker_loop
+
+        work = Path(a.work_dir or (a.output + ".work"))
+        work.mkdir(parents=True, exist_ok=True)
+
+        def one(req, i):
+            out = pipe(**_gen_kwargs(a, req))
+            return save_result(out, req.get("output", f"{a.output}_{i}"), entry)
+
+        fails = worker_loop(load_requests(a.requests), work, one)
+        return 1 if fails else 0
+    t0 = time.time()
+    out = pipe(**_gen_kwargs(a))
+    path = save_result(out, a.output, entry)
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"output": path, "seconds": round(time.time() - t0, 3)}))
+    return 0
+
+
+def cmd_cache(a) -> int:
+    from difflet_b200 import envs
+
+    root = Path(a.cache_dir or envs.DIFFLET_COMPILE_CACHE)
+    rows = []
+    for m in sorted(root.glob("*/*/manifest.json")):
+        doc = json.loads(m.read_text())
+        rows.append({"model": m.parent.parent.name, "key": m.parent.name,
+                     "parallel": doc.get("inputs", {}).get("parallel"), "shapes": doc.get("inputs", {}).get("shapes"),
+                     "dtype": doc.get("inputs", {}).get("dtype")})
+    if a.json:
+        print(json.dumps(rows, indent=2))
+    else:
+        for r in rows:
+            print(f"{r['model']:20s} {r['key']}  {r['dtype']}  {r['parallel']}  {r['shapes']}")
+    return 0
+
+
+def cmd_clean(a) -> int:
+    from difflet_b200 import envs
+
+    root = Path(a.cache_dir or envs.DIFFLET_COMPILE_CACHE)
+    if a.all:
+        shutil.rmtree(root, ignore_errors=True)
+    elif a.model:
+        shutil.rmtree(root / a.model, ignore_errors=True)
+    return 0
+
+
+def cmd_plan(a) -> int:
+    from difflet_b200.planner import plan
+
+    res = plan(a.model_id, gpus=a.gpus, height=a.height, width=a.width, num_frames=a.num_frames)
+    res = res[: a.top]
+    if a.json:
+        print(json.dumps(res, indent=2))
+    else:
+        for r in res:
+            print(f"{r['est_step_ms']:9.1f} ms  world={r['world']}  {r['parallel']}")
+    return 0
+
+
+def cmd_serve(a) -> int:
+    from difflet_b200.serving.server import serve_main
+
+    return serve_main(a)
+
+
+def cmd_bench(a) -> int:
+    if a.headline:
+        import runpy
+
+        sys.argv = ["bench.py"]
+        runpy.run_path(str(Path(__file__).resolve().parents[2] / "bench.py"), run_name="__main__")
+        return 0
+    from difflet_b200.bench.kernels import main as kmain
+
+    kmain(["--only", a.only])
+    return 0
+
+
+def main(argv=None) -> int:
+    a = build_parser().parse_args(argv)
+    if a.cmd == "download":
+        from difflet_b200.pipeline.path_resolver import resolve_model_path
+        from difflet_b200.registry import resolve_model
+
+        e = resolve_model(a.model_id)
+        print(resolve_model_path(a.model_id, revision=a.revision, allow_patterns=e.download_patterns,
+                                 random_init=a.random_weights))
+        return 0
+    if a.cmd == "compile":
+        p = _pipeline(a, load=False)
+        print(json.dumps({"compiled_path": str(p.compiled_path)}))
+        return 0
+    if a.cmd in ("generate", "run"):
+        return cmd_generate(a)
+    return {"plan": cmd_plan, "serve": cmd_serve, "cache": cmd_cache, "clean": cmd_clean, "bench": cmd_bench}[a.cmd](a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

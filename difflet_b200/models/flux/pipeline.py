@@ -152,6 +152,10 @@ class FluxApplication:
         key = (B, txt_loc.shape[1], x16.shape[1], h_tok, w_tok)
         step = self._step_fn(key, x16, txt_loc, pooled, t_buf, gvec, mod_buf, (h_tok, w_tok))
         self.last_step_ms = []
+        tc = self.teacache
+        if tc is not None:
+            tc.cal.num_steps = num_inference_steps
+            tc.reset()
         for i in range(num_inference_steps):
             ev = None
             if time_steps and x16.is_cuda:
@@ -159,12 +163,13 @@ class FluxApplication:
                 ev[0].record()
             mod_buf.copy_(mod_all[i])
             t_buf.fill_(float(ts[i]))
-            if self.teacache is not None and self.teacache.should_skip(i, x16, mod_buf):
-                v = self.teacache.skip_noise_pred()
+            probe = self.dit.teacache_probe(x16, mod_buf) if (tc is not None and tc.needs_probe()) else None
+            if tc is not None and tc.should_skip(i, probe):
+                v = tc.skip_noise_pred()
             else:
                 v = step()
-                if self.teacache is not None:
-                    self.teacache.record_full_step(i, v)
+                if tc is not None:
+                    tc.record_full_step(i, v)
             F.euler_step(x32_loc, v, sched.dt(i), x16=x16)
             if ev is not None:
                 ev[1].record()

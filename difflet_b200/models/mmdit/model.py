@@ -222,6 +222,17 @@ class MMDiT:
                 return out
         return F.gemv(self.w["mod.w"], temb, self.w["mod.b"], silu_in=True)
 
+    def teacache_probe(self, x_tokens, mod) -> torch.Tensor:
+        """TeaCache signal source: block 0's modulated image input
+        ``LN(x_embed(x)) * (1 + scale) + shift`` (one GEMM + one fused LN)."""
+        cfg, w = self.cfg, self.w
+        B, S_img, _ = x_tokens.shape
+        D = cfg.hidden
+        h = F.linear(x_tokens.reshape(B * S_img, -1), w["x_embed.w"], w["x_embed.b"])
+        o = cfg.double_mod_offset(0, "img") if cfg.double_blocks else cfg.single_mod_offset(0)
+        return F.ln_modulate(h, shift=mod[:, o:o + D], scale=mod[:, o + D:o + 2 * D], eps=cfg.eps,
+                             rows_per_batch=S_img)
+
     def refine_text(self, txt, timestep, txt_valid=None):
         """HunyuanVideo token refiner: text self-attention blocks gated by (timestep,
         mean-pooled text).  txt [B, S, text_dim] -> [B, S, D] (replicated on every rank)."""

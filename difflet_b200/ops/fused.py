@@ -271,3 +271,12 @@ def timestep_embed(t, dim, *, max_period=10000.0, flip_sin_to_cos=True, downscal
     if flip_sin_to_cos:
         emb = torch.cat([emb[:, half:], emb[:, :half]], -1)
     return emb
+
+
+def rel_l1(a, b) -> torch.Tensor:
+    """sum|a - b| / sum|b| as a 1-element f32 tensor on the device (TeaCache probe)."""
+    if a.is_cuda:
+        return native().rel_l1(a.contiguous(), b.contiguous())
+    ct = torch.float64 if a.dtype == torch.float64 else torch.float32
+    den = b.to(ct).abs().sum()
+    return ((a.to(ct) - b.to(ct)).abs().sum() / den if den > 0 else den * 0).reshape(1)

@@ -220,3 +220,29 @@ def test_attention_bounds_large_logits_token_major(native):
 def test_error_word_clean(native):
     torch.cuda.synchronize()
     assert native.error_word(torch.cuda.current_device()).cpu().tolist() == [0, 0, 0, 0]
+
+
+def test_rel_l1_probe_twice(native):
+    torch.manual_seed(9)
+    for n in (1 << 20, 12345):
+        a = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+        ref = ((a.float() - b.float()).abs().sum() / b.float().abs().sum()).item()
+        for _ in range(2):  # second call reuses the scratch (ticket must be back at zero)
+            out = native.rel_l1(a, b)
+            torch.cuda.synchronize()
+            assert abs(out.item() - ref) < 1e-4 * abs(ref)
+
+
+def test_cfg_combine_local_pointer(native):
+    n = 4096 * 64 + 3
+    u = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    c = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(n, device="cuda")
+    native.cfg_combine(c, u.data_ptr(), out, 4.0, True)   # this rank holds cond
+    ref = u.float() + 4.0 * (c.float() - u.float())
+    torch.cuda.synchronize()
+    assert (out - ref).abs().max().item() < 1e-4
+    native.cfg_combine(u, c.data_ptr(), out, 4.0, False)  # this rank holds uncond
+    torch.cuda.synchronize()
+    assert (out - ref).abs().max().item() < 1e-4

@@ -1,0 +1,56 @@
+"""TeaCache controller modes and the FLUX pipeline integration (CPU)."""
+
+import torch
+
+from difflet_b200.models.flux.config import get_config
+from difflet_b200.models.flux.model import FluxTransformer
+from difflet_b200.models.flux.pipeline import FluxApplication
+from difflet_b200.pipeline.teacache import TeaCacheCalibration, TeaCacheController, build_controller
+from difflet_b200.pipeline.teacache_gate import decide_method, fit_coefficients
+
+
+def test_cadence_mode_and_residual_reuse():
+    c = TeaCacheController(TeaCacheCalibration(cadence=2, warmup_steps=1, cooldown_steps=1, num_steps=8))
+    preds = []
+    for i in range(8):
+        if c.should_skip(i, None):
+            v = c.skip_noise_pred()
+        else:
+            v = torch.full((4,), float(i))
+            c.record_full_step(i, v)
+        preds.append(v.clone())
+    assert c.skipped_steps > 0 and c.full_steps + c.skipped_steps == 8
+    # a skipped step extrapolates by the last residual
+    for i, v in enumerate(preds):
+        if float(v[0]) != float(i):
+            assert float(v[0]) == float(preds[i - 1][0]) + 1.0
+
+
+def test_adaptive_mode_skips_when_input_static():
+    cal = TeaCacheCalibration(coefficients=[1.0, 0.0], threshold=0.5, accumulate=True, warmup_steps=0,
+                              cooldown_steps=0, num_steps=10)
+    c = TeaCacheController(cal)
+    x = torch.ones(64)
+    skips = 0
+    for i in range(10):
+        if c.should_skip(i, x):
+            c.skip_noise_pred()
+            skips += 1
+        else:
+            c.record_full_step(i, torch.randn(8))
+    assert skips >= 5  # identical inputs -> zero signal -> skip after the cache fills
+
+
+def test_gate():
+    s = [0.1, 0.2, 0.3, 0.4, 0.5]
+    assert decide_method(s, [1, 2, 3, 4, 5]) == "adaptive"
+    assert len(fit_coefficients(s, [1, 2, 3, 4, 5], degree=2)) == 3
+
+
+def test_flux_pipeline_with_teacache_runs_fewer_steps():
+    cfg = get_config("tiny128")
+    dit = FluxTransformer.random_init(cfg, seed=1)
+    app = FluxApplication(dit, None, text_len=16)
+    app.teacache = build_controller({"teacache_cadence": 2})
+    out = app.generate(prompt="x", height=64, width=64, num_inference_steps=8, output_type="latent")
+    assert torch.isfinite(out).all() and app.teacache.skipped_steps >= 2
