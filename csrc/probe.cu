@@ -18,7 +18,7 @@ constexpr int kThreads = 256;
 __global__ void __launch_bounds__(kThreads) rel_l1_kernel(const __nv_bfloat16* __restrict__ a,
                                                           const __nv_bfloat16* __restrict__ b, long long n,
                                                           float* scratch, float* out) {
-  // scratch layout: [2 * gridDim.x] partial sums, then one uint32 ticket
+  // scratch layout: [0] uint32 ticket (fixed slot, whatever the grid), then 2 partials per block
   float num = 0.f, den = 0.f;
   const long long n8 = n / 8;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
@@ -48,10 +48,10 @@ __global__ void __launch_bounds__(kThreads) rel_l1_kernel(const __nv_bfloat16* _
   if (threadIdx.x == 0) {
     float tn = 0.f, td = 0.f;
     for (int w = 0; w < kThreads / 32; ++w) tn += s_num[w], td += s_den[w];
-    scratch[2 * blockIdx.x] = tn;
-    scratch[2 * blockIdx.x + 1] = td;
+    scratch[1 + 2 * blockIdx.x] = tn;
+    scratch[2 + 2 * blockIdx.x] = td;
     __threadfence();
-    unsigned int* ticket = reinterpret_cast<unsigned int*>(scratch + 2 * gridDim.x);
+    unsigned int* ticket = reinterpret_cast<unsigned int*>(scratch);
     s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
   }
   __syncthreads();
@@ -59,9 +59,12 @@ __global__ void __launch_bounds__(kThreads) rel_l1_kernel(const __nv_bfloat16* _
     __threadfence();
     float tn = 0.f, td = 0.f;
     const volatile float* vs = scratch;
-    for (unsigned int blk = 0; blk < gridDim.x; ++blk) tn += vs[2 * blk], td += vs[2 * blk + 1];
+    for (unsigned int blk = 0; blk < gridDim.x; ++blk) {
+      tn += vs[1 + 2 * blk];
+      td += vs[2 + 2 * blk];
+    }
     *out = td > 0.f ? tn / td : 0.f;
-    *reinterpret_cast<unsigned int*>(scratch + 2 * gridDim.x) = 0u;  // ready for the next call
+    *reinterpret_cast<unsigned int*>(scratch) = 0u;  // ready for the next call
   }
 }
 
