@@ -33,9 +33,10 @@ CUDA_SOURCES = [
     "mx.cu",
     "conv.cu",
     "probe.cu",
+    "probe_noalloc.cu",
 ]
 CPP_SOURCES = ["bindings.cpp"]
-HEADERS = ["common.cuh", "kernels.h"]
+HEADERS = ["common.cuh", "kernels.h", "probe_noalloc.h"]
 
 NVCC_FLAGS = [
     "-gencode",
