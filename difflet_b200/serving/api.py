@@ -1,0 +1,172 @@
+"""OpenAI-compatible HTTP API for image and video generation (FastAPI).
+
+Routes as in the reference (``difflet/serving/openai/api_server.py:96-515``):
+  GET  /health, /ready, /v1/models
+  POST /v1/chat/completions   image models: the last user message is the prompt;
+                              generation options in the body or ``extra_body``
+                              (size, height, width, num_inference_steps, seed,
+                              guidance_scale, negative_prompt, response_format);
+                              the answer carries the PNG as a data URL
+  POST /v1/images/generations image models: OpenAI Images API (b64_json)
+  POST /v1/videos             video models: create an asynchronous job
+  GET  /v1/videos/{id}        job status (queued / in_progress / completed / failed)
+  GET  /v1/videos/{id}/content  the encoded video
+An API key (``--api-key`` or ``DIFFLET_API_KEY``) is enforced as a Bearer token
+on every /v1 route.  A busy server answers 429.
+"""
+
+from __future__ import annotations
+
+import base64
+import time
+import uuid
+from typing import Any
+
+from fastapi import Body, FastAPI, HTTPException, Request
+from fastapi.responses import FileResponse, JSONResponse
+
+from difflet_b200.serving.engines import EngineError, QueueTimeout
+from difflet_b200.serving.video_jobs import VideoJobStore
+
+_GEN_KEYS = ("height", "width", "num_inference_steps", "seed", "guidance_scale", "guidance_scale_2",
+             "true_cfg_scale", "negative_prompt", "num_frames")
+
+
+def _parse_size(size: str | None):
+    if not size:
+        return {}
+    w, h = str(size).lower().split("x")
+    return {"width": int(w), "height": int(h)}
+
+
+def normalize_chat_request(payload: dict) -> dict:
+    if not isinstance(payload, dict):
+        raise HTTPException(400, "request body must be a JSON object")
+    msgs = payload.get("messages") or []
+    prompt = None
+    for m in reversed(msgs):
+        if m.get("role") == "user":
+            c = m.get("content")
+            if isinstance(c, list):
+                c = " ".join(p.get("text", "") for p in c if isinstance(p, dict) and p.get("type") == "text")
+            prompt = c
+            break
+    if not prompt:
+        raise HTTPException(400, "no user message with text content")
+    opts = dict(payload.get("extra_body") or {})
+    for k in _GEN_KEYS + ("size", "n"):
+        if k in payload:
+            opts.setdefault(k, payload[k])
+    req = {"prompt": prompt}
+    req.update(_parse_size(opts.pop("size", None)))
+    for k in _GEN_KEYS:
+        if k in opts and opts[k] is not None:
+            req[k] = opts[k]
+    return req
+
+
+def create_app(engine, model_id: str, *, output: str = "image", api_key: str | None = None,
+               request_timeout: float = 600.0, video_dir: str | None = None, encode_image=None,
+               encode_video=None) -> FastAPI:
+    from difflet_b200.utils.media import encode_mjpeg_avi, encode_png
+
+    encode_image = encode_image or encode_png
+    encode_video = encode_video or encode_mjpeg_avi
+    app = FastAPI(title="difflet_b200", version="0.1.0")
+    jobs = VideoJobStore(engine, video_dir, encode_video) if output == "video" else None
+
+    @app.middleware("http")
+    async def auth(request: Request, call_next):
+        if api_key and request.url.path.startswith("/v1/"):
+            got = request.headers.get("authorization", "")
+            if got != f"Bearer {api_key}":
+                return JSONResponse(status_code=401, content={"error": {"message": "invalid api key"}})
+        return await call_next(request)
+
+    @app.get("/health")
+    async def health():
+        if not engine.healthy:
+            return JSONResponse(status_code=503, content={"status": "unhealthy"})
+        return {"status": "ok"}
+
+    @app.get("/ready")
+    async def ready():
+        if not engine.ready:
+            return JSONResponse(status_code=503, content={"status": "not_ready", "model": model_id})
+        return {"status": "ready", "model": model_id}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": model_id, "object": "model", "owned_by": "difflet_b200",
+                                            "output": output}]}
+
+    def _run(req):
+        try:
+            return engine.generate(req, timeout=request_timeout)
+        except QueueTimeout:
+            raise HTTPException(429, "server busy, retry later")
+        except EngineError as exc:
+            raise HTTPException(500, str(exc)[-2000:])
+
+    if output == "image":
+        import asyncio
+
+        @app.post("/v1/chat/completions")
+        async def chat(payload: Any = Body(default=None)):
+            req = normalize_chat_request(payload)
+            t0 = time.perf_counter()
+            img = await asyncio.get_running_loop().run_in_executor(None, _run, req)
+            png = encode_image(img) if not isinstance(img, (bytes, bytearray)) else bytes(img)
+            url = "data:image/png;base64," + base64.b64encode(png).decode()
+            return {"id": "chatcmpl-" + uuid.uuid4().hex, "object": "chat.completion", "created": int(time.time()),
+                    "model": model_id,
+                    "choices": [{"index": 0, "finish_reason": "stop",
+                                 "message": {"role": "assistant", "content": [{"type": "image_url",
+                                                                               "image_url": {"url": url}}]}}],
+                    "usage": {"generation_seconds": round(time.perf_counter() - t0, 3)}}
+
+        @app.post("/v1/images/generations")
+        async def images(payload: Any = Body(default=None)):
+            if not isinstance(payload, dict) or not payload.get("prompt"):
+                raise HTTPException(400, "prompt is required")
+            req = {"prompt": payload["prompt"], **_parse_size(payload.get("size"))}
+            for k in _GEN_KEYS:
+                if k in payload:
+                    req[k] = payload[k]
+            img = await asyncio.get_running_loop().run_in_executor(None, _run, req)
+            png = encode_image(img) if not isinstance(img, (bytes, bytearray)) else bytes(img)
+            return {"created": int(time.time()), "data": [{"b64_json": base64.b64encode(png).decode()}]}
+
+    else:
+
+        @app.post("/v1/videos")
+        async def create_video(payload: Any = Body(default=None)):
+            if not isinstance(payload, dict) or not payload.get("prompt"):
+                raise HTTPException(400, "prompt is required")
+            req = {"prompt": payload["prompt"], **_parse_size(payload.get("size"))}
+            for k in _GEN_KEYS:
+                if k in payload:
+                    req[k] = payload[k]
+            if "seconds" in payload and "num_frames" not in req:
+                req["num_frames"] = int(float(payload["seconds"]) * 16) // 4 * 4 + 1
+            job = jobs.create(req)
+            return job.public()
+
+        @app.get("/v1/videos/{vid}")
+        async def get_video(vid: str):
+            job = jobs.get(vid)
+            if job is None:
+                raise HTTPException(404, "no such video")
+            return job.public()
+
+        @app.get("/v1/videos/{vid}/content")
+        async def video_content(vid: str):
+            job = jobs.get(vid)
+            if job is None:
+                raise HTTPException(404, "no such video")
+            if job.status != "completed":
+                raise HTTPException(409, f"video is {job.status}")
+            return FileResponse(job.path, media_type="video/x-msvideo")
+
+    app.state.jobs = jobs
+    return app

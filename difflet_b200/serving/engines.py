@@ -1,0 +1,244 @@
+"""Serving engines: in-process, resident worker process (heartbeat + recovery), replicas.
+
+Reference behaviour (``difflet/serving/engines/resident_worker.py:51-1404``,
+``difflet/serving/engines/replicated.py:20-82``):
+  * one request runs at a time per replica (a run lock); a request that cannot
+    get the lock within ``queue_timeout`` is refused (HTTP 429)
+  * the resident worker is a separate spawned process that loads the pipeline
+    once, runs a smoke request, then reports ready; it sends a heartbeat
+    (state, stage, request id) every ``heartbeat_s``
+  * recovery never fails open: on a request timeout, a lost heartbeat or a dead
+    worker the engine cancels, waits a grace period, terminates, restarts the
+    worker and fences (the in-flight request fails; later ones run on the new
+    worker)
+  * ``ReplicatedEngine`` spreads requests over N replicas (least loaded first)
+"""
+
+from __future__ import annotations
+
+import multiprocessing as mp
+import queue
+import threading
+import time
+import traceback
+import uuid
+from typing import Any, Callable
+
+
+class QueueTimeout(Exception):
+    """No replica became free within the queue timeout (HTTP 429)."""
+
+
+class EngineError(RuntimeError):
+    pass
+
+
+class InProcessEngine:
+    """Runs ``generate_fn(request) -> result`` in this process (tests, single-process serving)."""
+
+    def __init__(self, generate_fn: Callable[[dict], Any], queue_timeout: float = 30.0):
+        self.fn = generate_fn
+        self.queue_timeout = queue_timeout
+        self._lock = threading.Lock()
+        self.ready = True
+        self.healthy = True
+        self.inflight = 0
+        self.completed = 0
+
+    def generate(self, request: dict, timeout: float | None = None):
+        if not self._lock.acquire(timeout=self.queue_timeout):
+            raise QueueTimeout("server busy")
+        self.inflight += 1
+        try:
+            out = self.fn(request)
+            self.completed += 1
+            return out
+        finally:
+            self.inflight -= 1
+            self._lock.release()
+
+    def close(self):
+        pass
+
+
+def _worker_main(conn_req, conn_resp, hb, factory, factory_kwargs, heartbeat_s):
+    """Worker process: build the pipeline, smoke-test it, serve requests, beat."""
+    state = {"state": "loading", "stage": "", "request_id": None}
+    stop = threading.Event()
+
+    def beat():
+        while not stop.is_set():
+            try:
+                hb.put(dict(state, t=time.time()))
+            except Exception:
+                pass
+            stop.wait(heartbeat_s)
+
+    threading.Thread(target=beat, daemon=True).start()
+    try:
+        run = factory(**factory_kwargs)
+        state["state"] = "smoke"
+        run({"__smoke__": True})
+        state["state"] = "ready"
+        conn_resp.put(("ready", None, None))
+    except Exception:
+        conn_resp.put(("fatal", None, traceback.format_exc()))
+        stop.set()
+        return
+    while True:
+        msg = conn_req.get()
+        if msg is None:
+            break
+        rid, req = msg
+        state.update(state="running", request_id=rid, stage="generate")
+        try:
+            out = run(req)
+            conn_resp.put(("ok", rid, out))
+        except Exception:
+            conn_resp.put(("error", rid, traceback.format_exc()))
+        state.update(state="ready", request_id=None, stage="")
+    stop.set()
+
+
+class ResidentWorkerEngine:
+    """A pipeline resident in a spawned worker process, with heartbeat-based recovery.
+
+    ``factory(**factory_kwargs)`` runs in the worker and returns ``run(request) -> result``
+    (picklable result).  It must be importable by name (spawn)."""
+
+    def __init__(self, factory, factory_kwargs=None, *, queue_timeout=30.0, request_timeout=600.0,
+                 heartbeat_s=5.0, heartbeat_timeout=None, start_timeout=1800.0):
+        self.factory = factory
+        self.factory_kwargs = dict(factory_kwargs or {})
+        self.queue_timeout = queue_timeout
+        self.request_timeout = request_timeout
+        self.heartbeat_s = heartbeat_s
+        self.heartbeat_timeout = heartbeat_timeout or max(6 * heartbeat_s, 30.0)
+        self.start_timeout = start_timeout
+        self._ctx = mp.get_context("spawn")
+        self._lock = threading.Lock()
+        self.ready = False
+        self.healthy = True
+        self.inflight = 0
+        self.restarts = 0
+        self.last_heartbeat = None
+        self._start()
+
+    def _start(self):
+        self._req = self._ctx.Queue()
+        self._resp = self._ctx.Queue()
+        self._hb = self._ctx.Queue()
+        self.proc = self._ctx.Process(target=_worker_main, args=(self._req, self._resp, self._hb, self.factory,
+                                                                self.factory_kwargs, self.heartbeat_s),
+                                      daemon=True)
+        self.proc.start()
+        deadline = time.time() + self.start_timeout
+        while time.time() < deadline:
+            try:
+                kind, _, payload = self._resp.get(timeout=1.0)
+            except queue.Empty:
+                if not self.proc.is_alive():
+                    break
+                continue
+            if kind == "ready":
+                self.ready, self.healthy = True, True
+                return
+            if kind == "fatal":
+                self.healthy = False
+                raise EngineError(f"worker failed to start:\n{payload}")
+        self.healthy = False
+        raise EngineError("worker did not become ready")
+
+    def _drain_heartbeats(self):
+        while True:
+            try:
+                self.last_heartbeat = self._hb.get_nowait()
+            except queue.Empty:
+                return
+
+    def _recover(self, reason: str):
+        """Terminate -> restart -> fence.  The caller's request fails with ``reason``."""
+        self.ready = False
+        try:
+            self._req.put(None)
+            self.proc.join(timeout=5)
+        except Exception:
+            pass
+        if self.proc.is_alive():
+            self.proc.terminate()
+            self.proc.join(timeout=10)
+            if self.proc.is_alive():
+                self.proc.kill()
+        self.restarts += 1
+        self._start()
+        raise EngineError(f"request failed, worker restarted ({reason})")
+
+    def generate(self, request: dict, timeout: float | None = None):
+        if not self._lock.acquire(timeout=self.queue_timeout):
+            raise QueueTimeout("server busy")
+        self.inflight += 1
+        try:
+            rid = str(uuid.uuid4())
+            self._req.put((rid, request))
+            deadline = time.time() + (timeout or self.request_timeout)
+            last_beat = time.time()
+            while True:
+                try:
+                    kind, r, payload = self._resp.get(timeout=0.5)
+                except queue.Empty:
+                    self._drain_heartbeats()
+                    if self.last_heartbeat is not None:
+                        last_beat = max(last_beat, self.last_heartbeat.get("t", 0))
+                    now = time.time()
+                    if not self.proc.is_alive():
+                        self._recover("worker died")
+                    if now > deadline:
+                        self._recover("request timeout")
+                    if now - last_beat > self.heartbeat_timeout:
+                        self._recover("heartbeat lost")
+                    continue
+                if r != rid:
+                    continue  # a late answer for a request fenced off by a restart
+                if kind == "ok":
+                    return payload
+                raise EngineError(payload)
+        finally:
+            self.inflight -= 1
+            self._lock.release()
+
+    def close(self):
+        try:
+            self._req.put(None)
+            self.proc.join(timeout=5)
+        finally:
+            if self.proc.is_alive():
+                self.proc.terminate()
+
+
+class ReplicatedEngine:
+    """Least-loaded dispatch over N replicas (``serve --dp-degree N``)."""
+
+    def __init__(self, replicas: list):
+        self.replicas = replicas
+
+    @property
+    def ready(self):
+        return any(r.ready for r in self.replicas)
+
+    @property
+    def healthy(self):
+        return all(r.healthy for r in self.replicas)
+
+    def generate(self, request, timeout=None):
+        order = sorted(self.replicas, key=lambda r: r.inflight)
+        last = None
+        for r in order:
+            try:
+                return r.generate(request, timeout)
+            except QueueTimeout as exc:
+                last = exc
+        raise last or QueueTimeout("server busy")
+
+    def close(self):
+        for r in self.replicas:
+            r.close()
