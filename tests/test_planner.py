@@ -1,0 +1,23 @@
+"""Planner: legal candidates only, ranking, calibration."""
+
+from difflet_b200.planner import calibrate, enumerate_candidates, plan
+from difflet_b200.registry import resolve_model
+
+
+def test_flux_candidates_respect_capabilities():
+    e = resolve_model("black-forest-labs/FLUX.1-dev")
+    cands = enumerate_candidates(e, 8)
+    assert cands and all(not p.cfg_parallel_enabled for p in cands)  # distilled
+    assert all(24 % (p.tp_degree * (p.cp_degree if p.cp_mode == "ulysses" else 1)) == 0 for p in cands)
+    assert all(p.world_size == 8 for p in cands)
+
+
+def test_wan_plan_ranks_and_offers_cfg():
+    rows = plan("Wan-AI/Wan2.2-T2V-A14B-Diffusers", gpus=8)
+    assert rows and rows == sorted(rows, key=lambda r: (r["est_step_ms"], -r["dp"]))
+    assert any(r["parallel"].get("cfg_parallel_enabled") for r in rows)
+
+
+def test_calibrate_moves_scale():
+    s = calibrate([(1.0, 2.0)])
+    assert 0.05 <= s <= 1.0
