@@ -103,6 +103,7 @@ def main(argv=None):
     ap.add_argument("--e2e-images", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--cp-mode", default="ulysses", choices=["ulysses", "ring", "gather_kv"])
     args = ap.parse_args(argv)
     import faulthandler
 
@@ -121,7 +122,7 @@ def main(argv=None):
     from difflet_b200.pipeline.difflet_pipeline import DiffletPipeline
     from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
 
-    par = DiffletParallelConfig(cp_degree=world, cp_mode="ulysses") if world > 1 else DiffletParallelConfig()
+    par = DiffletParallelConfig(cp_degree=world, cp_mode=args.cp_mode) if world > 1 else DiffletParallelConfig()
     t_load = time.time()
     pipe = DiffletPipeline.from_pretrained(
         "black-forest-labs/FLUX.1-dev", parallel=par, height=args.height, width=args.width, random_init=True,
@@ -231,7 +232,7 @@ def main(argv=None):
             "data": "synthetic (random-init FLUX.1-dev weights, N(0,1) text states / pooled / latents)",
             "config": {"model": "FLUX.1-dev", "global_batch": B, "seq_len": S_img + S_txt,
                        "height": args.height, "width": args.width,
-                       "parallelism": f"ulysses{world}" if world > 1 else "single",
+                       "parallelism": f"{args.cp_mode}{world}" if world > 1 else "single",
                        "l2": "weights (24 GB) stream from HBM every step, larger than L2; no flush",
                        "cuda_graph": not args.no_graph, "load_s": round(load_s, 1)},
             "clocks": clocks,

@@ -97,6 +97,9 @@ struct AttnParams {
   __nv_bfloat16* o;
   __nv_bfloat16* o_peer[DFL_MAX_PEERS];
   int o_world, seg0_len, seg0_per, seg1_per;
+  float* acc_o;    // f32 [B, H, Sq, 128] running output (merge modes)
+  float* acc_lse;  // f32 [B, H, Sq] running log-sum-exp
+  int merge_mode;  // 0 none, 1 first partial, 2 merge, 3 merge + final bf16 store
 };
 
 // Output row address: local, or (Ulysses) the owning rank's buffer.
@@ -347,7 +350,80 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     }
     // ------------------------------------------------------------ epilogue
     const int qrow = q0 + g * kBM + row;
-    if (ok && n_tiles > 0 && mbar_wait(o_full, 0, err, kKidAttn, 122, abort_flag)) {
+    if (p.merge_mode != 0) {
+      // Partial over one key block, merged by log-sum-exp into a running fp32
+      // (acc_o, acc_lse): 1 = first partial (store), 2 = merge and store,
+      // 3 = merge and write the final bf16 row (no store to the accumulator).
+      const bool have = ok && n_tiles > 0 && mbar_wait(o_full, 0, err, kKidAttn, 123, abort_flag);
+      if (have) tc_fence_after();
+      const float lse_cur = (have && l > 0.f) ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+      const float inv = (have && l > 0.f) ? 1.f / l : 0.f;
+      const bool valid = qrow < p.Sq;
+      const long long arow = ((long long)b * p.H + h) * p.Sq + qrow;
+      float w_prev = 0.f, w_cur = 1.f, lse_new = lse_cur;
+      if (p.merge_mode >= 2 && valid) {
+        const float lse_prev = p.acc_lse[arow];
+        const float mx = fmaxf(lse_prev, lse_cur);
+        if (mx == -INFINITY) {
+          w_prev = 0.f, w_cur = 0.f, lse_new = -INFINITY;
+        } else {
+          w_prev = expf(lse_prev - mx);
+          w_cur = expf(lse_cur - mx);
+          const float s = w_prev + w_cur;
+          w_prev /= s;
+          w_cur /= s;
+          lse_new = mx + logf(s);
+        }
+      } else if (lse_cur == -INFINITY) {
+        w_cur = 0.f;
+      }
+      __nv_bfloat16* op = (valid && p.merge_mode == 3) ? out_row(p, b, h, qrow) : nullptr;
+      float* ao = valid ? p.acc_o + arow * kD : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o_raw[32];
+        if (have) {
+          tmem_ld_32x32b_x32(o_t + c * 32, o_raw);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o_raw[e] = 0u;
+        }
+        if (!valid) continue;
+        float o[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(o_raw[e]) * inv * w_cur;
+        if (p.merge_mode >= 2) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 a = reinterpret_cast<const float4*>(ao + c * 32)[q];
+            o[4 * q] += w_prev * a.x;
+            o[4 * q + 1] += w_prev * a.y;
+            o[4 * q + 2] += w_prev * a.z;
+            o[4 * q + 3] += w_prev * a.w;
+          }
+        }
+        if (op != nullptr) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(o[8 * q + 0], o[8 * q + 1]);
+            w.y = pack_bf16x2(o[8 * q + 2], o[8 * q + 3]);
+            w.z = pack_bf16x2(o[8 * q + 4], o[8 * q + 5]);
+            w.w = pack_bf16x2(o[8 * q + 6], o[8 * q + 7]);
+            reinterpret_cast<uint4*>(op + c * 32)[q] = w;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            reinterpret_cast<float4*>(ao + c * 32)[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        }
+      }
+      if (valid) {
+        if (p.merge_mode != 3) p.acc_lse[arow] = lse_new;
+        if (p.lse) p.lse[arow] = lse_new;
+      }
+    } else if (ok && n_tiles > 0 && mbar_wait(o_full, 0, err, kKidAttn, 122, abort_flag)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* op = qrow < p.Sq ? out_row(p, b, h, qrow) : nullptr;
@@ -445,6 +521,10 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   p.kv_hi = a->kv_hi;
   p.o = reinterpret_cast<__nv_bfloat16*>(a->o);
   p.o_world = a->o_world;
+  p.acc_o = a->acc_o;
+  p.acc_lse = a->acc_lse;
+  p.merge_mode = a->merge_mode;
+  if (a->merge_mode != 0 && (!a->acc_o || !a->acc_lse || (reinterpret_cast<uintptr_t>(a->acc_o) & 15))) return -9;
   p.seg0_len = a->seg0_len;
   p.seg0_per = a->seg0_per > 0 ? a->seg0_per : 1;
   p.seg1_per = a->seg1_per > 0 ? a->seg1_per : 1;

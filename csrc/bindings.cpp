@@ -149,7 +149,8 @@ void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_
                  const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t,
                  int64_t rope_pos_off, bool rope_half, int64_t heads_per_rank,
                  std::vector<int64_t> q_dst, std::vector<int64_t> k_dst, std::vector<int64_t> v_dst,
-                 int64_t S_dst, int64_t seq_off, bool out_token_major) {
+                 int64_t S_dst, int64_t seq_off, bool out_token_major, bool kv_replicate, int64_t q_S_dst,
+                 int64_t q_seq_off) {
   check_bf16_cuda(qkv, "qkv");
   check_rowmajor(qkv, "qkv");
   const c10::cuda::CUDAGuard guard(qkv.device());
@@ -188,6 +189,9 @@ void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_
   a.S_dst = (int)S_dst;
   a.seq_off = (int)seq_off;
   a.out_token_major = out_token_major ? 1 : 0;
+  a.kv_replicate = kv_replicate ? 1 : 0;
+  a.q_S_dst = (int)q_S_dst;
+  a.q_seq_off = (int)q_seq_off;
   DFL_CHECK_RC(dfl_qkv_scatter(&a, cur_stream()), "qkv_scatter");
 }
 
@@ -260,7 +264,8 @@ at::Tensor timestep_embed(const at::Tensor& t, int64_t dim, double max_period, b
 at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
                      c10::optional<at::Tensor> out, const c10::optional<at::Tensor>& lse,
                      const c10::optional<at::Tensor>& kv_lo, const c10::optional<at::Tensor>& kv_hi,
-                     std::vector<int64_t> o_peer, int64_t seg0_len, int64_t seg0_per, int64_t seg1_per, std::vector<int64_t> o_strides) {
+                     std::vector<int64_t> o_peer, int64_t seg0_len, int64_t seg0_per, int64_t seg1_per, std::vector<int64_t> o_strides,
+                     const c10::optional<at::Tensor>& acc_o, const c10::optional<at::Tensor>& acc_lse, int64_t merge_mode) {
   check_bf16_cuda(q, "q");
   check_bf16_cuda(k, "k");
   check_bf16_cuda(v, "v");
@@ -268,8 +273,9 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   TORCH_CHECK(q.stride(3) == 1 && k.stride(3) == 1 && v.stride(3) == 1, "unit inner stride required");
   const c10::cuda::CUDAGuard guard(q.device());
   const bool scatter = !o_peer.empty();
-  at::Tensor o = (out.has_value() && out->defined()) ? *out : (scatter ? at::empty({0}, q.options()) : at::empty_like(q));
-  TORCH_CHECK(scatter || (o.dim() == 4 && o.stride(3) == 1), "out must be [B, H, S, dh] with unit inner stride");
+  const bool no_out = scatter || merge_mode == 1 || merge_mode == 2;  // partials write only acc_o / acc_lse
+  at::Tensor o = (out.has_value() && out->defined()) ? *out : (no_out ? at::empty({0}, q.options()) : at::empty_like(q));
+  TORCH_CHECK(no_out || (o.dim() == 4 && o.stride(3) == 1), "out must be [B, H, S, dh] with unit inner stride");
   TORCH_CHECK(!scatter || o_strides.size() == 3, "o_strides (batch, head, seq) required with o_peer");
   AttnArgs a{};
   a.q = q.data_ptr();
@@ -282,6 +288,8 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   if (scatter) {
     a.o_bs = o_strides[0]; a.o_hs = o_strides[1]; a.o_ss = o_strides[2];
     a.o = reinterpret_cast<void*>(o_peer[0]);
+  } else if (o.dim() != 4) {
+    a.o_bs = a.o_hs = a.o_ss = 0;
   } else {
     a.o_bs = o.stride(0); a.o_hs = o.stride(1); a.o_ss = o.stride(2);
   }
@@ -304,6 +312,16 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   a.seg0_len = (int)seg0_len;
   a.seg0_per = (int)seg0_per;
   a.seg1_per = (int)seg1_per;
+  a.merge_mode = (int)merge_mode;
+  if (merge_mode != 0) {
+    TORCH_CHECK(acc_o.has_value() && acc_lse.has_value(), "merge needs acc_o and acc_lse");
+    TORCH_CHECK(acc_o->scalar_type() == at::kFloat && acc_o->is_contiguous() &&
+                    acc_o->numel() == (int64_t)a.B * a.H * a.Sq * 128, "acc_o must be f32 [B, H, Sq, 128]");
+    TORCH_CHECK(acc_lse->scalar_type() == at::kFloat && acc_lse->is_contiguous() &&
+                    acc_lse->numel() == (int64_t)a.B * a.H * a.Sq, "acc_lse must be f32 [B, H, Sq]");
+    a.acc_o = acc_o->data_ptr<float>();
+    a.acc_lse = acc_lse->data_ptr<float>();
+  }
   DFL_CHECK_RC(dfl_attention(&a, cur_stream()), "attention");
   return o;
 }
@@ -345,6 +363,12 @@ int64_t ipc_open(py::bytes handle, int64_t device) {
 }
 
 void ipc_close(int64_t ptr) { dfl_ipc_close(reinterpret_cast<void*>(ptr)); }
+
+void memcpy_async(int64_t dst, int64_t src, int64_t nbytes) {
+  DFL_CHECK_RC(dfl_memcpy_async(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), nbytes,
+                                cur_stream()),
+               "memcpy_async");
+}
 
 void peer_barrier(std::vector<int64_t> flags, const at::Tensor& counter, int64_t rank, int64_t timeout_cycles) {
   TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == at::kInt, "counter must be a CUDA int32 tensor");
@@ -426,13 +450,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out") = py::none(), py::arg("lse") = py::none(), py::arg("kv_lo") = py::none(),
         py::arg("kv_hi") = py::none(), py::arg("o_peer") = std::vector<int64_t>{},
         py::arg("seg0_len") = 0, py::arg("seg0_per") = 0, py::arg("seg1_per") = 0,
-        py::arg("o_strides") = std::vector<int64_t>{});
+        py::arg("o_strides") = std::vector<int64_t>{}, py::arg("acc_o") = py::none(),
+        py::arg("acc_lse") = py::none(), py::arg("merge_mode") = 0);
   m.def("error_word", &error_word);
   m.def("symm_alloc", &symm_alloc);
   m.def("from_ptr", &from_ptr);
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
+  m.def("memcpy_async", &memcpy_async);
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_put_f32", &peer_put_f32);
   m.def("cfg_combine", &cfg_combine);

@@ -130,6 +130,10 @@ extern "C" int dfl_ipc_open(const void* handle64, void** out) {
 
 extern "C" int dfl_ipc_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
 
+extern "C" int dfl_memcpy_async(void* dst, const void* src, long long nbytes, cudaStream_t stream) {
+  return (int)cudaMemcpyAsync(dst, src, (size_t)nbytes, cudaMemcpyDeviceToDevice, stream);
+}
+
 extern "C" int dfl_peer_barrier(const BarrierArgs* a, cudaStream_t stream) {
   if (a->world < 1 || a->world > DFL_MAX_PEERS || a->rank < 0 || a->rank >= a->world) return -2;
   peer_barrier_kernel<<<1, 32, 0, stream>>>(*a);

@@ -66,6 +66,11 @@ typedef struct QkvScatterArgs {
   void* q_dst[DFL_MAX_PEERS]; void* k_dst[DFL_MAX_PEERS]; void* v_dst[DFL_MAX_PEERS];
   int S_dst, seq_off;                // destination seq length / offset of row 0
   int out_token_major;               // 1: dst is [B, S_dst, H_local*dh] instead
+  // Gather-KV context parallelism: k / v of every head go to all `world`
+  // destinations (heads_per_rank == H), q only to q_dst[0] with its own
+  // sequence length / offset (the local query rows).
+  int kv_replicate;
+  int q_S_dst, q_seq_off;
 } QkvScatterArgs;
 int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream);
 
@@ -117,6 +122,12 @@ typedef struct AttnArgs {
   void* o_peer[DFL_MAX_PEERS];
   int o_world;
   int seg0_len, seg0_per, seg1_per;
+  // Log-sum-exp merge of key-block partials (ring / gather context parallelism):
+  // merge_mode 1 writes this partial to acc_o / acc_lse, 2 merges into them,
+  // 3 merges and writes the final bf16 output.  acc_o f32 [B, H, Sq, 128].
+  float* acc_o;
+  float* acc_lse;
+  int merge_mode;
 } AttnArgs;
 int dfl_attention(const AttnArgs* a, cudaStream_t stream);
 
@@ -143,6 +154,9 @@ typedef struct PeerPutArgs {
   int world;
 } PeerPutArgs;
 int dfl_peer_put_f32(const PeerPutArgs* a, cudaStream_t stream);
+
+// Copy-engine copy (peer -> local over NVLink; no SM work, no kernel).
+int dfl_memcpy_async(void* dst, const void* src, long long nbytes, cudaStream_t stream);
 
 // CFG-parallel: out (f32) = u + s (c - u), partner branch read over NVLink.
 int dfl_cfg_combine(const void* mine, const void* peer, float* out, long long n, float scale,

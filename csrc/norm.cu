@@ -215,12 +215,15 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
   }
 
   for (int h = warp; h < a.H; h += 4) {
-    const int r = h / H_local;
-    const int hl = h % H_local;
+    const int r = a.kv_replicate ? 0 : h / H_local;
+    const int hl = a.kv_replicate ? h : h % H_local;
     const long long dst_off =
         a.out_token_major
             ? ((long long)b * a.S_dst + dpos) * (long long)(H_local * DH) + (long long)hl * DH
             : (((long long)b * H_local + hl) * a.S_dst + dpos) * DH;
+    // replicate mode: q rows live in a local buffer of q_S_dst rows at q_seq_off
+    const long long q_off_rows =
+        a.kv_replicate ? (((long long)b * H_local + hl) * a.q_S_dst + a.q_seq_off + s) * DH : dst_off;
     // q and k
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
@@ -250,14 +253,23 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
         }
       }
       if (cos_row) rope_apply<DH>(x, lane, cos_row, sin_row, a.rope_half);
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(which == 0 ? a.q_dst[r] : a.k_dst[r]);
-      store_head<DH>(dst + dst_off, lane, x);
+      if (which == 0) {
+        store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.q_dst[r]) + q_off_rows, lane, x);
+      } else if (a.kv_replicate) {
+        for (int d = 0; d < a.world; ++d) store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.k_dst[d]) + dst_off, lane, x);
+      } else {
+        store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.k_dst[r]) + dst_off, lane, x);
+      }
     }
     // v: plain copy into the destination layout
     if (a.v_off >= 0) {
       float x[E];
       load_head<DH>(src + a.v_off + h * DH, lane, x);
-      store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.v_dst[r]) + dst_off, lane, x);
+      if (a.kv_replicate) {
+        for (int d = 0; d < a.world; ++d) store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.v_dst[d]) + dst_off, lane, x);
+      } else {
+        store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.v_dst[r]) + dst_off, lane, x);
+      }
     }
   }
 }
@@ -381,7 +393,8 @@ extern "C" int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream) {
 extern "C" int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream) {
   if (a->rows == 0) return 0;
   if (a->world < 1 || a->world > DFL_MAX_PEERS) return -2;
-  if (a->heads_per_rank * a->world != a->H) return -3;
+  if (a->kv_replicate ? (a->heads_per_rank != a->H || a->out_token_major) : a->heads_per_rank * a->world != a->H)
+    return -3;
   if (a->ld % 8) return -4;
   if (a->dh == 128)
     qkv_scatter_kernel<128><<<a->rows, 128, 0, stream>>>(*a);

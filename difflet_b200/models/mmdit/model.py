@@ -172,14 +172,14 @@ class MMDiT:
         ws["qkv_img"] = e(B * S_img, 3 * D)
         ws["qkv_txt"] = e(B * S_txt, 3 * D)
         ws["mlp"] = e(B * max(S_img, S_txt), F_)
-        Hl = H // world
         pe = (lambda *shape: par.empty(shape, dt)) if par is not None else e  # noqa: E731
         if par is not None:
             par.check_heads(H)
         ws["fused"] = pe(B * S_loc, 3 * D + F_) if cfg.single_blocks else None
-        ws["q"] = pe(B, Hl, S, dh)
-        ws["k"] = pe(B, Hl, S, dh)
-        ws["v"] = pe(B, Hl, S, dh)
+        if par is not None:  # the CP mode decides the q/k/v layout (heads x full sequence, or local rows)
+            ws["q"], ws["k"], ws["v"] = par.layout(B, H, dh, S_loc, S, dt)
+        else:
+            ws["q"], ws["k"], ws["v"] = e(B, H, S, dh), e(B, H, S, dh), e(B, H, S, dh)
         ws["attn"] = pe(B, S_loc, D)
         self._ws[key] = ws
         return ws
@@ -297,7 +297,8 @@ class MMDiT:
                 img_hw = (side, S_img_g // side)
             grid = (1, img_hw[0], img_hw[1])
         cos, sin = self.rope(S_txt_g, grid)
-        Hl = H // world
+        Hl = par.heads_local(H) if par is not None else H
+        S_loc = S_txt + S_img
         if mod is None:
             mod = self.modulation(self.temb(timestep, guidance, pooled))
         kv_lo = kv_hi = None
@@ -318,8 +319,11 @@ class MMDiT:
         norm = ws["norm"]
         q, k, v = ws["q"], ws["k"], ws["v"]
 
-        def dst(t):
-            return par.peer_views(t) if par is not None else [t]
+        def dst(q_, k_, v_, row, pos):
+            """qkv_scatter destinations for rows at local offset ``row`` / global position ``pos``."""
+            if par is not None:
+                return par.scatter_kwargs(q_, k_, v_, row, pos, S_loc, S, H)
+            return dict(q_dst=[q_], k_dst=[k_], v_dst=[v_], S_dst=S, seq_off=pos, heads_per_rank=H)
 
         def mslice(off):
             return mod[:, off:off + D]
@@ -333,9 +337,8 @@ class MMDiT:
                 F.ln_modulate(xs, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=nr, out=nb)
                 F.linear(nb, w[p + st + "_qkv.w"], w[p + st + "_qkv.b"], out=ws["qkv_" + st])
                 F.qkv_scatter(ws["qkv_" + st], q_off=0, k_off=D, v_off=2 * D, S_src=nr, H=H, dh=dh,
-                              q_dst=dst(q), k_dst=dst(k), v_dst=dst(v), S_dst=S, seq_off=pos, norm_mode=1,
-                              wq=w[p + st + "_qnorm"], wk=w[p + st + "_knorm"], eps=eps, cos=cos, sin=sin,
-                              rope_pos_off=pos, heads_per_rank=Hl)
+                              **dst(q, k, v, row_of[st], pos), norm_mode=1, wq=w[p + st + "_qnorm"],
+                              wk=w[p + st + "_knorm"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos)
             self._attention(ws, B, S_txt, S_img, D, Hl, dh, kv_lo=kv_lo, kv_hi=kv_hi)
             for st in ("img", "txt"):
                 xs, nr = xs_of[st], n_of[st]
@@ -350,7 +353,6 @@ class MMDiT:
                 F.linear(mb, w[p + st + "_down.w"], w[p + st + "_down.b"], out=xs, gate=mslice(o + 5 * D),
                          resid=xs, rows_per_batch=nr)
 
-        S_loc = S_txt + S_img
         if B > 1:  # dual -> single: the residual stream becomes [seg0 ; seg1] per batch
             for st in ("txt", "img"):
                 r0 = row_of[st]
@@ -374,9 +376,9 @@ class MMDiT:
                     for st in (s0, s1):
                         r0, nr, pos = row_of[st], n_of[st], pos_of[st]
                         F.qkv_scatter(rows[r0:r0 + nr], q_off=0, k_off=D + F_, v_off=2 * D + F_, S_src=nr, H=H,
-                                      dh=dh, q_dst=dst(q[b:b + 1]), k_dst=dst(k[b:b + 1]), v_dst=dst(v[b:b + 1]),
-                                      S_dst=S, seq_off=pos, norm_mode=1, wq=w[p + "qnorm"], wk=w[p + "knorm"],
-                                      eps=eps, cos=cos, sin=sin, rope_pos_off=pos, heads_per_rank=Hl)
+                                      dh=dh, **dst(q[b:b + 1], k[b:b + 1], v[b:b + 1], r0, pos), norm_mode=1,
+                                      wq=w[p + "qnorm"], wk=w[p + "knorm"], eps=eps, cos=cos, sin=sin,
+                                      rope_pos_off=pos)
             self._attention(ws, B, S_txt, S_img, D, Hl, dh, out_rows=fused, kv_lo=kv_lo, kv_hi=kv_hi)
             F.linear(fused[:, : D + F_], w[p + "proj.w"], w[p + "proj.b"], out=x2, gate=mslice(o + 2 * D),
                      resid=x2, rows_per_batch=S_loc)

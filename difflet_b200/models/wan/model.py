@@ -169,11 +169,13 @@ class WanTransformer:
         pe = (lambda *s: par.empty(s, dt)) if par is not None else e  # noqa: E731
         if par is not None:
             par.check_heads(H)
-        Hl = H // world
         ws = {"S": S, "x": e(B * S_loc, D), "norm": e(B * S_loc, D), "qkv": e(B * S_loc, 3 * D),
               "mlp": e(B * S_loc, cfg.ffn), "cq": e(B, H, S_loc, dh), "cqin": e(B * S_loc, D),
-              "cattn": e(B, S_loc, D),
-              "q": pe(B, Hl, S, dh), "k": pe(B, Hl, S, dh), "v": pe(B, Hl, S, dh), "attn": pe(B, S_loc, D)}
+              "cattn": e(B, S_loc, D), "attn": pe(B, S_loc, D)}
+        if par is not None:  # the CP mode decides the q/k/v layout
+            ws["q"], ws["k"], ws["v"] = par.layout(B, H, dh, S_loc, S, dt)
+        else:
+            ws["q"], ws["k"], ws["v"] = e(B, H, S, dh), e(B, H, S, dh), e(B, H, S, dh)
         self._ws[key] = ws
         return ws
 
@@ -221,7 +223,7 @@ class WanTransformer:
         D, H, dh = cfg.hidden, cfg.heads, cfg.head_dim
         world = par.world if par is not None else 1
         rank = par.rank if par is not None else 0
-        Hl = H // world
+        Hl = par.heads_local(H) if par is not None else H
         ws = self._workspace(B, S_loc)
         S = ws["S"]
         cos, sin = self.rope(grid)
@@ -234,17 +236,18 @@ class WanTransformer:
         pos = rank * S_loc
         ones = self._ones_gate(B)
 
-        def dst(t):
-            return par.peer_views(t) if par is not None else [t]
+        if par is not None:
+            tgt = par.scatter_kwargs(q, k, v, 0, pos, S_loc, S, H)
+        else:
+            tgt = dict(q_dst=[q], k_dst=[k], v_dst=[v], S_dst=S, seq_off=pos, heads_per_rank=H)
 
         for i in range(cfg.layers):
             p = f"blk.{i}."
             m = mods[i]  # [B, 6, D]: shift, scale, gate, c_shift, c_scale, c_gate
             F.ln_modulate(x, shift=m[:, 0], scale=m[:, 1], eps=eps, rows_per_batch=S_loc, out=norm)
             F.linear(norm, w[p + "qkv.w"], w[p + "qkv.b"], out=ws["qkv"])
-            F.qkv_scatter(ws["qkv"], q_off=0, k_off=D, v_off=2 * D, S_src=S_loc, H=H, dh=dh, q_dst=dst(q),
-                          k_dst=dst(k), v_dst=dst(v), S_dst=S, seq_off=pos, norm_mode=2, wq=w[p + "qn"],
-                          wk=w[p + "kn"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos, heads_per_rank=Hl)
+            F.qkv_scatter(ws["qkv"], q_off=0, k_off=D, v_off=2 * D, S_src=S_loc, H=H, dh=dh, **tgt, norm_mode=2,
+                          wq=w[p + "qn"], wk=w[p + "kn"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos)
             self._self_attention(ws, B, S_loc, Hl)
             F.linear(ws["attn"].view(B * S_loc, D), w[p + "o.w"], w[p + "o.b"], out=x, gate=m[:, 2], resid=x,
                      rows_per_batch=S_loc)

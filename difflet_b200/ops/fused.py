@@ -126,17 +126,21 @@ def _rope_cpu(x, cos, sin, half):
 
 def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, S_dst, seq_off=0,
                 norm_mode=1, wq=None, wk=None, eps=1e-6, cos=None, sin=None, rope_pos_off=0,
-                rope_half=False, heads_per_rank=None, token_major=False):
+                rope_half=False, heads_per_rank=None, token_major=False, kv_replicate=False, q_S_dst=0,
+                q_seq_off=0):
     """Normalise + rotate q/k of a token-major qkv buffer and scatter q/k/v by head.
 
     ``q_dst`` etc. are lists (one tensor per destination rank; a single-GPU call
     passes one).  Destination layout [B, H_local, S_dst, dh] (or [B, S_dst,
     H_local*dh] when ``token_major``); row ``s`` of the source lands at
     position ``seq_off + s``.  ``heads_per_rank`` splits heads over the list.
+    ``kv_replicate`` (gather-KV context parallelism): k and v of all heads go to
+    every destination, q only to ``q_dst[0]`` ([B, H, q_S_dst, dh], row
+    ``q_seq_off + s``).
     """
     qkv2 = _rows2d(qkv)
     world = len(q_dst if q_dst is not None else (k_dst if k_dst is not None else v_dst))
-    hpr = heads_per_rank or (H // world)
+    hpr = H if kv_replicate else (heads_per_rank or (H // world))
     # a negative offset skips that stream (q-only / k,v-only passes); its destinations may be None
     q_dst = q_dst if q_dst is not None else [None] * world
     k_dst = k_dst if k_dst is not None else [None] * world
@@ -145,7 +149,7 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
         ptr = lambda ts: [0 if t is None else (t if isinstance(t, int) else t.data_ptr()) for t in ts]  # noqa: E731
         native().qkv_scatter(qkv2, q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos, sin,
                              rope_pos_off, rope_half, hpr, ptr(q_dst), ptr(k_dst), ptr(v_dst), S_dst,
-                             seq_off, token_major)
+                             seq_off, token_major, kv_replicate, q_S_dst, q_seq_off)
         return
     rows = qkv2.shape[0]
     B = rows // S_src
@@ -176,6 +180,14 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
         s_ = sin[rope_pos_off:rope_pos_off + S_src].to(ct)
         q = None if q is None else _rope_cpu(q, c, s_, rope_half)
         k = None if k is None else _rope_cpu(k, c, s_, rope_half)
+    if kv_replicate:
+        if q is not None:
+            q_dst[0][:, :, q_seq_off:q_seq_off + S_src] = q.to(q_dst[0].dtype)
+        for r in range(world):
+            for src, dst in ((k, k_dst[r]), (v, v_dst[r])):
+                if src is not None:
+                    dst[:, :, seq_off:seq_off + S_src] = src.to(dst.dtype)
+        return
     for r in range(world):
         hs = slice(r * hpr, (r + 1) * hpr)
         for src, dst in ((q, q_dst[r]), (k, k_dst[r]), (v, v_dst[r])):
@@ -218,6 +230,51 @@ def attention(q, k, v, scale, *, out=None, lse=None, kv_lo=None, kv_hi=None):
         out.copy_(o)
         return out
     return o
+
+
+MERGE_FIRST, MERGE_MID, MERGE_LAST = 1, 2, 3
+
+
+def attention_partial(q, k, v, scale, acc_o, acc_lse, mode, *, out=None, lse=None, kv_lo=None, kv_hi=None):
+    """Attention over one key block, merged by log-sum-exp into a running result.
+
+    ``acc_o`` f32 [B, H, Sq, dh], ``acc_lse`` f32 [B, H, Sq].  ``mode`` 1 stores this
+    block's normalised output and LSE, 2 merges into them, 3 merges and writes the
+    final output to ``out`` (bf16, [B, H, Sq, dh] or any strided view).  Running the
+    blocks of a key sequence through modes 1, 2, ..., 3 equals attention over the
+    whole sequence (ring attention's online merge,
+    difflet/backends/neuron/ops_impl/attention.py:280-301)."""
+    if q.is_cuda and q.shape[-1] == 128:
+        if mode == MERGE_LAST and out is None:
+            out = torch.empty_like(q)
+        native().attention(q, k, v, float(scale), out if mode == MERGE_LAST else None, lse, kv_lo, kv_hi,
+                           acc_o=acc_o, acc_lse=acc_lse, merge_mode=int(mode))
+        return out if mode == MERGE_LAST else acc_o
+    ct = torch.float64 if q.dtype == torch.float64 else torch.float32
+    B, H, Sq, dh = q.shape
+    part_lse = torch.empty(B, H, Sq, dtype=ct, device=q.device)
+    o = attention(q.to(ct), k.to(ct), v.to(ct), scale, lse=part_lse, kv_lo=kv_lo, kv_hi=kv_hi).to(ct)
+    if mode == MERGE_FIRST:
+        new_o, new_lse = o, part_lse
+    else:
+        prev = acc_lse.to(ct)
+        mx = torch.maximum(prev, part_lse)
+        safe = torch.where(torch.isinf(mx), torch.zeros_like(mx), mx)
+        wp, wc = torch.exp(prev - safe), torch.exp(part_lse - safe)
+        s = wp + wc
+        new_lse = torch.where(s > 0, safe + torch.log(s), torch.full_like(s, float("-inf")))
+        s = torch.where(s > 0, s, torch.ones_like(s))
+        new_o = (wp / s)[..., None] * acc_o.to(ct) + (wc / s)[..., None] * o
+    if lse is not None:
+        lse.copy_(new_lse.to(lse.dtype))
+    if mode == MERGE_LAST:
+        if out is None:
+            return new_o.to(q.dtype)
+        out.copy_(new_o.to(out.dtype))
+        return out
+    acc_o.copy_(new_o.to(acc_o.dtype))
+    acc_lse.copy_(new_lse.to(acc_lse.dtype))
+    return acc_o
 
 
 def gemv(W, x, bias=None, *, silu_in=False, silu_out=False, out=None):

@@ -51,6 +51,12 @@ def all_to_all(recv: list, send: list, group) -> None:
 
 
 class _Base:
+    """Context-parallel state shared by every CP mode.  The model asks it for its
+    q/k/v buffers (``layout``), for the destinations of the fused q/k/v scatter
+    (``scatter_kwargs``) and runs ``attention``; the three modes differ only there."""
+
+    kind = "ulysses"
+
     def __init__(self, group, ranks, device):
         self.group = group
         self.ranks = list(ranks)
@@ -58,6 +64,22 @@ class _Base:
         self.rank = self.ranks.index(dist.get_rank())
         self.device = device
         self.decode_on_all_ranks = False
+
+    def heads_local(self, H: int) -> int:
+        return H // self.world
+
+    def layout(self, B, H, dh, S_loc, S, dtype):
+        """q, k, v buffers: this rank's heads over the full joint sequence."""
+        Hl = self.heads_local(H)
+        return tuple(self.empty((B, Hl, S, dh), dtype) for _ in range(3))
+
+    def scatter_kwargs(self, q, k, v, row, pos, S_loc, S, H):
+        """qkv_scatter destinations for rows at local offset ``row`` / global position ``pos``."""
+        return dict(q_dst=self.peer_views(q), k_dst=self.peer_views(k), v_dst=self.peer_views(v), S_dst=S,
+                    seq_off=pos, heads_per_rank=self.heads_local(H))
+
+    def close(self):
+        pass
 
     # token sharding of the model inputs / outputs
     def shard_tokens(self, x: torch.Tensor) -> torch.Tensor:
@@ -74,7 +96,9 @@ class _Base:
             raise ValueError(f"Ulysses needs heads % world == 0, got {H} heads on {self.world} ranks")
 
 
-class PeerUlysses(_Base):
+class PeerBase(_Base):
+    """Symmetric-heap transport shared by the fused (peer-memory) CP modes."""
+
     def __init__(self, group, ranks, device):
         super().__init__(group, ranks, device)
         from difflet_b200.parallel.symm import SymmetricHeap
@@ -112,6 +136,11 @@ class PeerUlysses(_Base):
     def before_attention(self):
         self.heap.barrier()
 
+    def close(self):
+        self.heap.close()
+
+
+class PeerUlysses(PeerBase):
     def attention(self, q, k, v, scale, target, B, n0, n1, ld, kv_lo=None, kv_hi=None):
         """q/k/v: this rank's heads over the full sequence ``[seg0 ; seg1]``; each rank
         owns ``n0`` rows of seg0 and ``n1`` rows of seg1.  ``target``: local
@@ -125,9 +154,6 @@ class PeerUlysses(_Base):
         F.native().attention(q, k, v, float(scale), None, None, kv_lo, kv_hi, peers, n0 * self.world, n0, n1,
                              [S_loc * ld, dh, ld])
         self.heap.barrier()  # every output row has landed at its owner
-
-    def close(self):
-        self.heap.close()
 
 
 class CollectiveUlysses(_Base):
@@ -193,7 +219,9 @@ class CollectiveUlysses(_Base):
 
 
 def make_sequence_parallel(parallel, device, transport: str | None = None):
-    """Ulysses context over the cp axis of ``parallel`` (None when cp_degree == 1)."""
+    """Context-parallel state over the cp axis of ``parallel`` (None when cp_degree == 1):
+    Ulysses, ring or gather-KV after ``parallel.cp_mode``, over peer memory
+    (``transport`` "fused", CUDA) or collectives ("nccl" / CPU gloo)."""
     from difflet_b200.parallel import groups
 
     if not dist.is_initialized():
@@ -206,9 +234,15 @@ def make_sequence_parallel(parallel, device, transport: str | None = None):
         return None
     group, ranks = groups.get_group("cp"), groups.get_group_ranks("cp")
     transport = transport or envs.DIFFLET_KERNEL_COMM
-    if device.type == "cuda" and transport == "fused":
-        return PeerUlysses(group, ranks, device)
-    return CollectiveUlysses(group, ranks, device)
+    fused = device.type == "cuda" and transport == "fused"
+    mode = getattr(parallel, "cp_mode", "ulysses")
+    if mode == "ring" or mode == "gather_kv":
+        from difflet_b200.parallel import ring
+
+        if mode == "ring":
+            return (ring.PeerRing if fused else ring.CollectiveRing)(group, ranks, device)
+        return (ring.PeerGatherKV if fused else ring.CollectiveGatherKV)(group, ranks, device)
+    return (PeerUlysses if fused else CollectiveUlysses)(group, ranks, device)
 
 
 def make_cfg_parallel(parallel, device, transport: str | None = None):

@@ -105,7 +105,7 @@ def test_qkv_scatter_norm_rope(native, dh):
     k = torch.zeros_like(q)
     v = torch.zeros_like(q)
     native.qkv_scatter(qkv, 0, D, 2 * D, S, H, dh, 1, wq, wk, 1e-6, cos, sin, off, False, H,
-                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S_dst, off, False)
+                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S_dst, off, False, False, 0, 0)
     torch.cuda.synchronize()
     x = qkv.float().view(B, S, 3, H, dh).permute(2, 0, 3, 1, 4)  # 3,B,H,S,dh
 
@@ -132,7 +132,7 @@ def test_qkv_scatter_across_heads_half_rope(native):
     k = torch.empty_like(q)
     v = torch.empty_like(q)
     native.qkv_scatter(qkv, 0, D, 2 * D, S, H, dh, 2, wq, wk, 1e-6, cos, sin, 0, True, H,
-                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S, 0, True)
+                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S, 0, True, False, 0, 0)
     torch.cuda.synchronize()
     x = qkv.float().view(S, 3, D)
     qn = x[:, 0] * torch.rsqrt(x[:, 0].pow(2).mean(-1, keepdim=True) + 1e-6) * wq.float()
@@ -141,6 +141,37 @@ def test_qkv_scatter_across_heads_half_rope(native):
     c, s_ = cos[:, None], sin[:, None]
     ref = torch.cat([x1 * c - x2 * s_, x2 * c + x1 * s_], -1).reshape(S, D)
     _close(q[0], ref)
+
+
+def test_qkv_scatter_kv_replicate(native):
+    """Gather-KV store pattern: k / v of all heads to every destination, q to a local buffer."""
+    from difflet_b200.ops import fused as F
+
+    torch.manual_seed(15)
+    B, S, H, dh = 2, 40, 4, 128
+    D = H * dh
+    S_loc, row, S_all, pos = 64, 24, 160, 100
+    qkv = torch.randn(B * S, 3 * D, device="cuda", dtype=torch.bfloat16)
+    wq = torch.randn(dh, device="cuda", dtype=torch.bfloat16)
+    wk = torch.randn(dh, device="cuda", dtype=torch.bfloat16)
+    ang = torch.rand(S_all, dh // 2, device="cuda") * 6
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    q = torch.zeros(B, H, S_loc, dh, device="cuda", dtype=torch.bfloat16)
+    ks = [torch.zeros(B, H, S_all, dh, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    vs = [torch.zeros_like(ks[0]) for _ in range(3)]
+    kw = dict(q_off=0, k_off=D, v_off=2 * D, S_src=S, H=H, dh=dh, norm_mode=1, wq=wq, wk=wk, eps=1e-6, cos=cos,
+              sin=sin, rope_pos_off=pos, S_dst=S_all, seq_off=pos, kv_replicate=True, q_S_dst=S_loc, q_seq_off=row)
+    F.qkv_scatter(qkv, q_dst=[q, None, None], k_dst=ks, v_dst=vs, **kw)
+    qc = torch.zeros(B, H, S_loc, dh, dtype=torch.float32)
+    kc = torch.zeros(B, H, S_all, dh, dtype=torch.float32)
+    vc = torch.zeros_like(kc)
+    kw.update(wq=wq.cpu().float(), wk=wk.cpu().float(), cos=cos.cpu(), sin=sin.cpu())
+    F.qkv_scatter(qkv.cpu().float(), q_dst=[qc], k_dst=[kc], v_dst=[vc], **kw)
+    torch.cuda.synchronize()
+    _close(q, qc.cuda())
+    for kd, vd in zip(ks, vs):
+        _close(kd, kc.cuda())
+        _close(vd, vc.cuda())
 
 
 def test_gemv_and_timestep(native):
@@ -197,6 +228,44 @@ def test_attention(native, B, H, Sq, Sk):
     ref, ref_lse = _attn_ref(q, k, v, scale)
     torch.cuda.synchronize()
     _close(o, ref)
+    assert (lse - ref_lse).abs().max().item() < 2e-2
+
+
+def test_attention_lse_merge_over_key_blocks(native):
+    """Ring emulated on one GPU: the keys in 3 blocks (one empty for a batch through its
+    window), partials merged by the kernel epilogue, equal full attention."""
+    from difflet_b200.ops import fused as F
+
+    torch.manual_seed(16)
+    B, H, Sq = 2, 3, 300
+    blocks = [256, 200, 130]
+    q = torch.randn(B, H, Sq, 128, device="cuda", dtype=torch.bfloat16) * 3
+    ks = [torch.randn(B, H, n, 128, device="cuda", dtype=torch.bfloat16) * 3 for n in blocks]
+    vs = [torch.randn(B, H, n, 128, device="cuda", dtype=torch.bfloat16) for n in blocks]
+    his = [torch.tensor([256, 256], device="cuda", dtype=torch.int32),
+           torch.tensor([0, 150], device="cuda", dtype=torch.int32),
+           torch.tensor([130, 7], device="cuda", dtype=torch.int32)]
+    scale = 1 / math.sqrt(128)
+    acc_o = torch.empty(B, H, Sq, 128, device="cuda")
+    acc_lse = torch.empty(B, H, Sq, device="cuda")
+    out = torch.empty(B, Sq, H * 128, device="cuda", dtype=torch.bfloat16)
+    o_view = out.view(B, Sq, H, 128).permute(0, 2, 1, 3)
+    lse = torch.empty(B, H, Sq, device="cuda")
+    for i, (k, v, hi) in enumerate(zip(ks, vs, his)):
+        mode = F.MERGE_FIRST if i == 0 else (F.MERGE_LAST if i == len(blocks) - 1 else F.MERGE_MID)
+        F.attention_partial(q, k, v, scale, acc_o, acc_lse, mode, out=o_view, lse=lse if i == 2 else None,
+                            kv_hi=hi)
+    # reference: concatenate the valid keys of each block
+    kk, vv, keep = torch.cat(ks, 2), torch.cat(vs, 2), []
+    for n, hi in zip(blocks, his):
+        keep.append(torch.arange(n, device="cuda")[None] < hi[:, None].long())
+    keep = torch.cat(keep, 1)  # [B, S_all]
+    s = torch.einsum("bhqd,bhkd->bhqk", q.float(), kk.float()) * scale
+    s = s.masked_fill(~keep[:, None, None, :], float("-inf"))
+    ref_lse = torch.logsumexp(s, -1)
+    ref = torch.einsum("bhqk,bhkd->bhqd", torch.softmax(s, -1), vv.float())
+    torch.cuda.synchronize()
+    _close(o_view, ref)
     assert (lse - ref_lse).abs().max().item() < 2e-2
 
 

@@ -1,4 +1,5 @@
-"""Ulysses sequence parallelism on CPU gloo ranks: every rank's shard equals the dense forward."""
+"""Context parallelism on CPU gloo ranks (Ulysses, ring, gather-KV): every rank's shard
+equals the dense forward (difflet tests/unit/backends/test_neuron_joint_attention_cp.py:54-72)."""
 
 import pytest
 import torch
@@ -8,12 +9,19 @@ from difflet_b200.parallel.testing import run_ranks
 pytestmark = pytest.mark.multirank
 
 
-def _sp_forward(rank, world, B):
+def _context(mode, world):
     import torch.distributed as dist
 
+    from difflet_b200.parallel import ring, ulysses
+
+    cls = {"ulysses": ulysses.CollectiveUlysses, "ring": ring.CollectiveRing,
+           "gather_kv": ring.CollectiveGatherKV}[mode]
+    return cls(dist.group.WORLD, list(range(world)), torch.device("cpu"))
+
+
+def _sp_forward(rank, world, B, mode):
     from difflet_b200.models.flux.config import get_config
     from difflet_b200.models.flux.model import FluxTransformer, pack_latents
-    from difflet_b200.parallel.ulysses import CollectiveUlysses
 
     cfg = get_config("tiny128", heads=4, hidden=512)
     m = FluxTransformer.random_init(cfg, dtype=torch.float64, seed=11)
@@ -24,7 +32,7 @@ def _sp_forward(rank, world, B):
     t = torch.full((B,), 0.4, dtype=torch.float64)
     gd = torch.full((B,), 3.5, dtype=torch.float64)
     dense = m(x, txt, pooled, t, gd, img_hw=(16, 16))
-    par = CollectiveUlysses(dist.group.WORLD, list(range(world)), torch.device("cpu"))
+    par = _context(mode, world)
     m2 = FluxTransformer(cfg, m.w)
     m2.par = par
     out = m2(par.shard_tokens(x), par.shard_tokens(txt), pooled, t, gd, img_hw=(16, 16))
@@ -32,7 +40,46 @@ def _sp_forward(rank, world, B):
     return (full - dense).abs().max().item()
 
 
+@pytest.mark.parametrize("mode", ["ulysses", "ring", "gather_kv"])
 @pytest.mark.parametrize("world,B", [(2, 1), (4, 1), (2, 2)])
-def test_ulysses_matches_dense(world, B):
-    errs = run_ranks(_sp_forward, world, B, timeout=240)
+def test_cp_matches_dense(world, B, mode):
+    errs = run_ranks(_sp_forward, world, B, mode, timeout=240)
     assert max(errs) < 1e-10, errs
+
+
+def _hv_forward(rank, world, mode):
+    from difflet_b200.models.mmdit import MMDiT, get_config, pack_latents
+
+    cfg = get_config("tiny-hunyuan")
+    m = MMDiT.random_init(cfg, dtype=torch.float64, seed=2)
+    g = torch.Generator().manual_seed(1)
+    B, T, Hh, Ww = 2, 2, 16, 16
+    x = pack_latents(torch.randn(B, 16, T, Hh, Ww, generator=g, dtype=torch.float64))
+    txt = torch.randn(B, 32, cfg.text_dim, generator=g, dtype=torch.float64)
+    pooled = torch.randn(B, cfg.pooled_dim, generator=g, dtype=torch.float64)
+    t = torch.tensor([0.3, 0.9], dtype=torch.float64)
+    gd = torch.tensor([6.0, 6.0], dtype=torch.float64)
+    valid = torch.tensor([11, 32])  # padded text: a window that ends inside one rank's text block
+    grid = (T, Hh // 2, Ww // 2)
+    dense = m(x, txt, pooled, t, gd, grid=grid, txt_valid=valid)
+    par = _context(mode, world)
+    m2 = MMDiT(cfg, m.w)
+    m2.par = par
+    out = m2(par.shard_tokens(x), txt, pooled, t, gd, grid=grid, txt_valid=valid)
+    return (par.gather_tokens(out) - dense).abs().max().item()
+
+
+@pytest.mark.parametrize("mode", ["ulysses", "ring", "gather_kv"])
+def test_hunyuan_padded_text_cp(mode):
+    errs = run_ranks(_hv_forward, 2, mode, timeout=240)
+    assert max(errs) < 1e-10, errs
+
+
+def test_block_windows():
+    from difflet_b200.parallel.ring import block_windows
+
+    # [img (2 x 4 rows) ; txt (2 x 3 rows)], prefix windows over the global order
+    hi = torch.tensor([8 + 4, 8 + 6, 8, 5])
+    w = block_windows(hi, 4, 3, 2)
+    # rank 0 block = img[0:4] + txt[0:3]; rank 1 block = img[4:8] + txt[3:6]
+    assert w.tolist() == [[4 + 3, 4 + 3, 4, 4], [4 + 1, 4 + 3, 4, 1]]

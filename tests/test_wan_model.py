@@ -40,9 +40,10 @@ def test_wan_fused_matches_oracle(B):
     assert (out - ref).abs().max().item() < 1e-11 * ref.abs().max().item()
 
 
-def _sp(rank, world):
+def _sp(rank, world, mode="ulysses"):
     import torch.distributed as dist
 
+    from difflet_b200.parallel.ring import CollectiveGatherKV, CollectiveRing
     from difflet_b200.parallel.ulysses import CollectiveUlysses
 
     cfg = get_wan_config("tiny-wan", heads=4, hidden=512)
@@ -52,7 +53,8 @@ def _sp(rank, world):
     t = torch.tensor([500.0], dtype=torch.float64)
     ctx = m.prepare_context(text)
     dense = m(x, t, ctx, grid=(3, 4, 6))
-    par = CollectiveUlysses(dist.group.WORLD, list(range(world)), torch.device("cpu"))
+    cls = {"ulysses": CollectiveUlysses, "ring": CollectiveRing, "gather_kv": CollectiveGatherKV}[mode]
+    par = cls(dist.group.WORLD, list(range(world)), torch.device("cpu"))
     m2 = WanTransformer(cfg, m.w)
     m2.par = par
     out = par.gather_tokens(m2(par.shard_tokens(x), t, ctx, grid=(3, 4, 6)))
@@ -60,7 +62,8 @@ def _sp(rank, world):
 
 
 @pytest.mark.multirank
-def test_wan_ulysses_matches_dense():
+@pytest.mark.parametrize("mode", ["ulysses", "ring", "gather_kv"])
+def test_wan_cp_matches_dense(mode):
     from difflet_b200.parallel.testing import run_ranks
 
-    assert max(run_ranks(_sp, 2, timeout=240)) < 1e-10
+    assert max(run_ranks(_sp, 2, mode, timeout=240)) < 1e-10
