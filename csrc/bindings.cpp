@@ -47,36 +47,39 @@ const void* opt_ptr(const c10::optional<at::Tensor>& t) {
 }
 
 // ---------------------------------------------------------------------------
-at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at::Tensor>& bias,
-                c10::optional<at::Tensor> out, int64_t epi, int64_t act_lo, int64_t act_hi,
-                const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
-                const c10::optional<at::Tensor>& resid, double alpha, bool out_f32) {
-  check_bf16_cuda(A, "A");
-  check_bf16_cuda(B, "B");
-  check_rowmajor(A, "A");
-  check_rowmajor(B, "B");
-  TORCH_CHECK(A.size(1) == B.size(1), "K mismatch: A ", A.sizes(), " B ", B.sizes());
-  const c10::cuda::CUDAGuard guard(A.device());
-  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+// Output + epilogue fields shared by the bf16 and MXFP8 GEMMs.  With out_peer
+// (tensor-parallel row scatter) rows go to peer buffers and no local D exists.
+static at::Tensor gemm_epilogue_args(GemmArgs& a, const at::Tensor& A, int64_t M, int64_t N,
+                                     const c10::optional<at::Tensor>& bias, c10::optional<at::Tensor> out,
+                                     int64_t epi, int64_t act_lo, int64_t act_hi,
+                                     const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
+                                     const c10::optional<at::Tensor>& resid, double alpha, bool out_f32,
+                                     const std::vector<int64_t>& out_peer, int64_t rows_per_rank,
+                                     int64_t peer_row_off, int64_t ldd_peer) {
   at::Tensor D;
-  if (out.has_value() && out->defined()) {
-    D = *out;
-    check_rowmajor(D, "out");
-    TORCH_CHECK(D.size(0) == M && D.size(1) == N, "out shape mismatch");
-    TORCH_CHECK(D.scalar_type() == (out_f32 ? at::kFloat : at::kBFloat16), "out dtype mismatch");
+  if (!out_peer.empty()) {
+    TORCH_CHECK(out_peer.size() <= DFL_MAX_PEERS, "at most 8 output peers");
+    TORCH_CHECK(rows_per_rank > 0 && ldd_peer > 0, "out_peer needs rows_per_rank and ldd");
+    a.out_world = (int)out_peer.size();
+    for (size_t r = 0; r < out_peer.size(); ++r) a.out_peer[r] = reinterpret_cast<void*>(out_peer[r]);
+    a.rows_per_rank = (int)rows_per_rank;
+    a.peer_row_off = peer_row_off;
+    a.ldd = ldd_peer;
+    D = at::empty({0}, A.options());
   } else {
-    D = at::empty({M, N}, A.options().dtype(out_f32 ? at::kFloat : at::kBFloat16));
+    if (out.has_value() && out->defined()) {
+      D = *out;
+      check_rowmajor(D, "out");
+      TORCH_CHECK(D.size(0) == M && D.size(1) == N, "out shape mismatch");
+      TORCH_CHECK(D.scalar_type() == (out_f32 ? at::kFloat : at::kBFloat16), "out dtype mismatch");
+    } else {
+      D = at::empty({M, N}, A.options().dtype(out_f32 ? at::kFloat : at::kBFloat16));
+    }
+    a.D = D.data_ptr();
+    a.ldd = D.stride(0);
   }
-  GemmArgs a{};
-  a.A = A.data_ptr();
-  a.B = B.data_ptr();
-  a.D = D.data_ptr();
-  a.lda = A.stride(0);
-  a.ldb = B.stride(0);
-  a.ldd = D.stride(0);
   a.M = (int)M;
   a.N = (int)N;
-  a.K = (int)K;
   a.out_f32 = out_f32 ? 1 : 0;
   if (bias.has_value() && bias->defined()) {
     check_bf16_cuda(*bias, "bias");
@@ -100,8 +103,79 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at
   }
   a.alpha = (float)alpha;
   a.err = err_ptr();
-  int rc = dfl_gemm_bf16(&a, cur_stream());
-  DFL_CHECK_RC(rc, "gemm");
+  return D;
+}
+
+at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at::Tensor>& bias,
+                c10::optional<at::Tensor> out, int64_t epi, int64_t act_lo, int64_t act_hi,
+                const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
+                const c10::optional<at::Tensor>& resid, double alpha, bool out_f32,
+                std::vector<int64_t> out_peer, int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer) {
+  check_bf16_cuda(A, "A");
+  check_bf16_cuda(B, "B");
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  TORCH_CHECK(A.size(1) == B.size(1), "K mismatch: A ", A.sizes(), " B ", B.sizes());
+  const c10::cuda::CUDAGuard guard(A.device());
+  GemmArgs a{};
+  at::Tensor D = gemm_epilogue_args(a, A, A.size(0), B.size(0), bias, out, epi, act_lo, act_hi, gate,
+                                    rows_per_batch, resid, alpha, out_f32, out_peer, rows_per_rank, peer_row_off,
+                                    ldd_peer);
+  a.A = A.data_ptr();
+  a.B = B.data_ptr();
+  a.lda = A.stride(0);
+  a.ldb = B.stride(0);
+  a.K = (int)A.size(1);
+  DFL_CHECK_RC(dfl_gemm_bf16(&a, cur_stream()), "gemm");
+  return D;
+}
+
+// ---------------------------------------------------------------- MXFP8
+std::vector<at::Tensor> mx_quantize(const at::Tensor& x, bool blocked) {
+  check_bf16_cuda(x, "x");
+  check_rowmajor(x, "x");
+  TORCH_CHECK(x.dim() == 2, "x must be [R, K]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t R = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % (blocked ? 128 : 32) == 0, "K must be a multiple of ", blocked ? 128 : 32);
+  at::Tensor q = at::empty({R, K}, x.options().dtype(at::kFloat8_e4m3fn));
+  // blocked scales: rows padded to 256 (the MXFP8 GEMM reads two 128-row atoms per 256-column B tile)
+  at::Tensor sf = blocked ? at::zeros({(R + 255) / 256 * 256 * (K / 32)}, x.options().dtype(at::kByte))
+                          : at::empty({R, K / 32}, x.options().dtype(at::kByte));
+  DFL_CHECK_RC(dfl_mx_quantize(x.data_ptr(), x.stride(0), (int)R, (int)K, q.data_ptr(), q.stride(0),
+                               sf.data_ptr(), blocked ? 1 : 0, cur_stream()),
+               "mx_quantize");
+  return {q, sf};
+}
+
+at::Tensor gemm_mx(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B, const at::Tensor& sfb,
+                   const c10::optional<at::Tensor>& bias, c10::optional<at::Tensor> out, int64_t epi,
+                   int64_t act_lo, int64_t act_hi, const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
+                   const c10::optional<at::Tensor>& resid, double alpha, bool out_f32, std::vector<int64_t> out_peer,
+                   int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kFloat8_e4m3fn &&
+                  B.scalar_type() == at::kFloat8_e4m3fn, "A and B must be CUDA float8_e4m3fn");
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  TORCH_CHECK(A.size(1) == B.size(1), "K mismatch");
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  TORCH_CHECK(sfa.scalar_type() == at::kByte && sfa.is_contiguous() && sfa.numel() >= (M + 127) / 128 * 128 * (K / 32),
+              "sfa must be the blocked uint8 scales of A");
+  TORCH_CHECK(sfb.scalar_type() == at::kByte && sfb.is_contiguous() &&
+                  sfb.numel() >= (N + 255) / 256 * 256 * (K / 32),
+              "sfb must be the blocked uint8 scales of B (rows padded to 256)");
+  const c10::cuda::CUDAGuard guard(A.device());
+  MxGemmArgs m{};
+  at::Tensor D = gemm_epilogue_args(m.g, A, M, N, bias, out, epi, act_lo, act_hi, gate, rows_per_batch, resid,
+                                    alpha, out_f32, out_peer, rows_per_rank, peer_row_off, ldd_peer);
+  m.g.A = A.data_ptr();
+  m.g.B = B.data_ptr();
+  m.g.lda = A.stride(0);
+  m.g.ldb = B.stride(0);
+  m.g.K = (int)K;
+  m.sfa = sfa.data_ptr();
+  m.sfb = sfb.data_ptr();
+  DFL_CHECK_RC(dfl_gemm_mx(&m, cur_stream()), "gemm_mx");
   return D;
 }
 
@@ -435,7 +509,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("alpha") = 1.0,
-        py::arg("out_f32") = false);
+        py::arg("out_f32") = false, py::arg("out_peer") = std::vector<int64_t>{}, py::arg("rows_per_rank") = 0,
+        py::arg("peer_row_off") = 0, py::arg("ldd") = 0);
+  m.def("mx_quantize", &mx_quantize, py::arg("x"), py::arg("blocked") = false);
+  m.def("gemm_mx", &gemm_mx, "block-scaled MXFP8 tcgen05 GEMM", py::arg("A"), py::arg("sfa"), py::arg("B"),
+        py::arg("sfb"), py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,
+        py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),
+        py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("alpha") = 1.0,
+        py::arg("out_f32") = false, py::arg("out_peer") = std::vector<int64_t>{}, py::arg("rows_per_rank") = 0,
+        py::arg("peer_row_off") = 0, py::arg("ldd") = 0);
   m.def("ln_modulate", &ln_modulate, py::arg("x"), py::arg("out") = py::none(),
         py::arg("w") = py::none(), py::arg("b") = py::none(), py::arg("shift") = py::none(),
         py::arg("scale") = py::none(), py::arg("rows_per_batch") = 0, py::arg("eps") = 1e-6,

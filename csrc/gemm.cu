@@ -20,6 +20,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "gemm_epilogue.cuh"
 #include "kernels.h"
 
 namespace {
@@ -29,20 +30,6 @@ using namespace dfl;
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;
-constexpr int kGroupM = 16;  // tile raster: 16 M-blocks per group for L2 reuse
-
-struct EpiParams {
-  void* D;
-  long long ldd;
-  const __nv_bfloat16* bias;
-  int act_lo, act_hi;
-  const float* gate;
-  long long gate_bstride;
-  int rows_per_batch;
-  const __nv_bfloat16* resid;
-  long long ldr;
-  float alpha;
-};
 
 template <int BN, int STAGES>
 struct Smem {
@@ -53,110 +40,6 @@ struct Smem {
   // full[S], empty[S], tmem_full[2], tmem_empty[2], then tmem addr + abort flag
   static constexpr int kTotal = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;  // + align slack
 };
-
-DFL_DEVICE void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
-  int group_tiles = kGroupM * num_n;
-  int g = t / group_tiles;
-  int first_m = g * kGroupM;
-  int gm = min(kGroupM, num_m - first_m);
-  int r = t - g * group_tiles;
-  mb = first_m + (r % gm);
-  nb = r / gm;
-}
-
-template <int EPI, bool OUT_F32>
-DFL_DEVICE void epilogue_chunk(const uint32_t (&r)[32], int row, int col0, int M, int N,
-                               const EpiParams& p) {
-  if (row >= M) return;
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-  const bool full = (col0 + 32 <= N);
-  if (p.bias != nullptr) {
-    if (full) {
-      const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 w = __ldg(b4 + q);
-        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float2 f = unpack_bf16x2(ws[h]);
-          v[q * 8 + 2 * h] += f.x;
-          v[q * 8 + 2 * h + 1] += f.y;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) v[j] += __bfloat162float(p.bias[col0 + j]);
-    }
-  }
-  if constexpr (EPI == kEpiGelu || EPI == kEpiSilu) {
-    if (col0 + 32 > p.act_lo && col0 < p.act_hi) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        int c = col0 + j;
-        if (c >= p.act_lo && c < p.act_hi) v[j] = (EPI == kEpiGelu) ? gelu_tanh(v[j]) : silu(v[j]);
-      }
-    }
-  }
-  if constexpr (EPI == kEpiGateResid) {
-    int b = row / p.rows_per_batch;
-    const float* g = p.gate + (long long)b * p.gate_bstride;
-    const __nv_bfloat16* rs = p.resid + (long long)row * p.ldr;
-    if (full) {
-      const float4* g4 = reinterpret_cast<const float4*>(g + col0);
-      const uint4* r4 = reinterpret_cast<const uint4*>(rs + col0);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float4 ga = __ldg(g4 + 2 * q);
-        float4 gb = __ldg(g4 + 2 * q + 1);
-        float gs[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-        uint4 rw = r4[q];
-        uint32_t rr[4] = {rw.x, rw.y, rw.z, rw.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float2 rf = unpack_bf16x2(rr[h]);
-          v[q * 8 + 2 * h] = rf.x + gs[2 * h] * v[q * 8 + 2 * h];
-          v[q * 8 + 2 * h + 1] = rf.y + gs[2 * h + 1] * v[q * 8 + 2 * h + 1];
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) v[j] = __bfloat162float(rs[col0 + j]) + g[col0 + j] * v[j];
-    }
-  }
-  if constexpr (OUT_F32) {
-    float* d = reinterpret_cast<float*>(p.D) + (long long)row * p.ldd + col0;
-    if (full) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        reinterpret_cast<float4*>(d)[q] =
-            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    } else {
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) d[j] = v[j];
-    }
-  } else {
-    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd + col0;
-    if (full) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 w;
-        w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
-        w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
-        w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
-        w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
-        reinterpret_cast<uint4*>(d)[q] = w;
-      }
-    } else {
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) d[j] = __float2bfloat16(v[j]);
-    }
-  }
-}
 
 template <int BN, int STAGES, int EPI, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -360,8 +243,9 @@ extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
   if ((reinterpret_cast<uintptr_t>(a->A) & 15) || (reinterpret_cast<uintptr_t>(a->B) & 15)) return -3;
   if ((a->lda * 2) % 16 || (a->ldb * 2) % 16) return -4;
   if (a->K % 8) return -5;
-  if (!a->out_f32 && ((a->ldd % 8) || (reinterpret_cast<uintptr_t>(a->D) & 15))) return -6;
-  if (a->out_f32 && ((a->ldd % 4) || (reinterpret_cast<uintptr_t>(a->D) & 15))) return -6;
+  const void* dchk = a->out_world > 0 ? a->out_peer[0] : a->D;
+  if (!a->out_f32 && ((a->ldd % 8) || (reinterpret_cast<uintptr_t>(dchk) & 15))) return -6;
+  if (a->out_f32 && ((a->ldd % 4) || (reinterpret_cast<uintptr_t>(dchk) & 15))) return -6;
   if (a->bias && (reinterpret_cast<uintptr_t>(a->bias) & 15)) return -7;
   if (a->epi == kEpiGateResid) {
     if (!a->gate || !a->resid || a->rows_per_batch <= 0) return -8;
@@ -389,6 +273,11 @@ extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
   ep.resid = reinterpret_cast<const __nv_bfloat16*>(a->resid);
   ep.ldr = a->ldr;
   ep.alpha = a->alpha;
+  ep.out_world = a->out_world;
+  ep.rows_per_rank = a->rows_per_rank > 0 ? a->rows_per_rank : a->M;
+  ep.peer_row_off = a->peer_row_off;
+  if (a->out_world < 0 || a->out_world > DFL_MAX_PEERS) return -9;
+  for (int r = 0; r < DFL_MAX_PEERS; ++r) ep.out_peer[r] = r < a->out_world ? a->out_peer[r] : nullptr;
   if (wide)
     return dispatch_epi<256, 4>(a->epi, a->out_f32, ta, tb, a->M, a->N, a->K, ep, a->err, stream, dev);
   return dispatch_epi<128, 6>(a->epi, a->out_f32, ta, tb, a->M, a->N, a->K, ep, a->err, stream, dev);

@@ -12,6 +12,8 @@ extern "C" {
 
 enum { kEpiNone = 0, kEpiGelu = 1, kEpiGateResid = 2, kEpiSilu = 3 };
 
+#define DFL_MAX_PEERS 8
+
 typedef struct GemmArgs {
   const void* A;   // bf16 [M, K], row stride lda (elements)
   const void* B;   // bf16 [N, K], row stride ldb
@@ -29,9 +31,36 @@ typedef struct GemmArgs {
   long long ldr;
   float alpha;         // scales the accumulator before bias
   int* err;
+  // Row scatter (out_world > 0): row r is stored to out_peer[r / rows_per_rank]
+  // at row peer_row_off + r % rows_per_rank with stride ldd (tensor-parallel
+  // partial sums sent to the rank that reduces them); D is unused then.
+  void* out_peer[DFL_MAX_PEERS];
+  int out_world;
+  int rows_per_rank;
+  long long peer_row_off;
 } GemmArgs;
 
 int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream);
+
+// MXFP8 GEMM on the block-scaled tensor cores (tcgen05 kind::mxf8f6f4):
+//   D = epi(A . B^T), A [M, K] / B [N, K] FP8 E4M3 (K-major, row strides in
+//   bytes g.lda / g.ldb), one E8M0 scale per 32 K values in the blocked layout
+//   written by dfl_mx_quantize (128-row x 128-K atoms of 512 bytes).  The
+//   epilogue fields of g are those of dfl_gemm_bf16; g.A / g.B are the FP8 data.
+typedef struct MxGemmArgs {
+  GemmArgs g;
+  const void* sfa;   // uint8 blocked scales of A (rows padded to 128)
+  const void* sfb;   // uint8 blocked scales of B
+} MxGemmArgs;
+int dfl_gemm_mx(const MxGemmArgs* a, cudaStream_t stream);
+
+// bf16 [R, K] -> FP8 E4M3 [R, K] (row stride ldq bytes) + E8M0 scales, one per
+// 32 K values (OCP MX: exponent = floor(log2(amax)) - 8, saturating convert).
+// blocked = 1: the tensor-core layout (atom (r/128, k/128) at byte
+// ((r/128) * (K/128) + k/128) * 512, inside it (r%32)*16 + ((r%128)/32)*4 +
+// (k/32)%4; rows padded to 128), blocked = 0: plain [R, K/32].
+int dfl_mx_quantize(const void* x, long long ldx, int R, int K, void* q, long long ldq, void* scales,
+                    int blocked, cudaStream_t stream);
 
 // y = (LN(x) [* w + b]) [* (1 + scale[b]) + shift[b]]      (fp32 statistics)
 typedef struct LnModArgs {
@@ -50,7 +79,6 @@ int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream);
 // q/k RMSNorm + RoPE + scatter to head-major [B, H_local, S_dst, dh] buffers.
 // Source rows are tokens; destination tables hold one pointer per rank so the
 // same pass performs the Ulysses sequence->head all-to-all over NVLink stores.
-#define DFL_MAX_PEERS 8
 typedef struct QkvScatterArgs {
   const void* qkv; long long ld;     // bf16 [rows, ld]
   int q_off, k_off, v_off;           // column offsets of the q / k / v blocks

@@ -36,7 +36,7 @@ CUDA_SOURCES = [
     "probe_noalloc.cu",
 ]
 CPP_SOURCES = ["bindings.cpp"]
-HEADERS = ["common.cuh", "kernels.h", "probe_noalloc.h"]
+HEADERS = ["common.cuh", "kernels.h", "probe_noalloc.h", "gemm_epilogue.cuh"]
 
 NVCC_FLAGS = [
     "-gencode",

@@ -4,7 +4,7 @@ Every number is a CUDA-event time on the launching stream after warm-up, with
 an L2 flush (a 256 MB write) before each timed launch, reported as the median
 of the timed launches.  Usage::
 
-    python -m difflet_b200.bench.kernels [--only gemm,attn,ln] [--cases flux_1gpu,...]
+    python -m difflet_b200.bench.kernels [--only gemm,attn,ln,mx] [--cases flux_1gpu,...]
                                          [--iters 20] [--no-ref]
 
 ``--no-ref`` skips the library comparison (used for ncu captures so the
@@ -74,6 +74,33 @@ def bench_gemm(nat, iters, flush, peaks, cases, ref):
     return rows
 
 
+def bench_mx(nat, iters, flush, peaks, cases, ref):
+    """MXFP8 block-scaled GEMM (operands pre-quantized, as weights are offline) and the
+    activation quantizer (bytes: bf16 in + fp8 out + scales)."""
+    rows = []
+    for name, M, N, K in _sel(GEMM_SHAPES, cases):
+        if K % 128:
+            continue
+        a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+        aq, asf = nat.mx_quantize(a, True)
+        bq, bsf = nat.mx_quantize(b, True)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        t = time_fn(lambda: nat.gemm_mx(aq, asf, bq, bsf, None, out=out), iters, flush=flush)
+        tq = time_fn(lambda: nat.mx_quantize(a, True), iters, flush=flush)
+        fl = 2.0 * M * N * K
+        r = {"kernel": "gemm_mx_tcgen05", "shape": name, "M": M, "N": N, "K": K, "ms": round(t, 4),
+             "tflops": round(fl / t / 1e9, 1),
+             "x_measured_bf16_peak": round(fl / t / 1e9 / peaks["bf16_tflops"], 3),
+             "quantize_ms": round(tq, 4), "quantize_gbs": round(M * K * 3.03125 / tq / 1e6, 1)}
+        if ref:
+            t_ref = time_fn(lambda: torch.matmul(a, b.t(), out=out), iters, flush=flush)
+            r.update({"cublas_bf16_ms": round(t_ref, 4), "cublas_bf16_tflops": round(fl / t_ref / 1e9, 1)})
+        rows.append(r)
+        del a, b, aq, bq, out
+    return rows
+
+
 def bench_attn(nat, iters, flush, peaks, cases, ref):
     rows = []
     for name, B, H, S in _sel(ATTN_CASES, cases):
@@ -133,6 +160,8 @@ def main(argv=None):
         rows += bench_attn(nat, args.iters, flush, peaks, cases, ref)
     if "ln" in only:
         rows += bench_ln(nat, args.iters, flush, peaks, cases, ref)
+    if "mx" in only:
+        rows += bench_mx(nat, args.iters, flush, peaks, cases, ref)
     _native.check_device_errors()
     for r in rows:
         print(json.dumps(r))

@@ -232,6 +232,73 @@ def attention(q, k, v, scale, *, out=None, lse=None, kv_lo=None, kv_hi=None):
     return o
 
 
+# --------------------------------------------------------------------------- MXFP8
+def block_scales(s_plain: torch.Tensor) -> torch.Tensor:
+    """Plain E8M0 scales [R, K/32] -> the tensor-core blocked layout (flat uint8): one
+    512-byte atom per (128 rows, 128 K), atoms K-fastest, inside an atom byte
+    (r%32)*16 + ((r%128)/32)*4 + (k/32)%4; rows padded to 256 with zeros."""
+    R, KB = s_plain.shape
+    if KB % 4:
+        raise ValueError("blocked MX scales need K to be a multiple of 128")
+    Rp = -(-R // 256) * 256
+    sp = torch.zeros(Rp, KB, dtype=torch.uint8, device=s_plain.device)
+    sp[:R] = s_plain
+    return sp.view(Rp // 128, 4, 32, KB // 4, 4).permute(0, 3, 2, 1, 4).contiguous().view(-1)
+
+
+def unblock_scales(s_blocked: torch.Tensor, R: int, K: int) -> torch.Tensor:
+    """Inverse of ``block_scales``: the plain [R, K/32] scales."""
+    KB = K // 32
+    Rp = s_blocked.numel() // KB
+    t = s_blocked.view(Rp // 128, KB // 4, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(Rp, KB)
+    return t[:R].contiguous()
+
+
+def mx_quantize(x: torch.Tensor, blocked: bool = True):
+    """bf16 [R, K] -> (FP8 E4M3 [R, K], E8M0 scales: blocked flat, or plain [R, K/32])."""
+    x2 = _rows2d(x)
+    if x2.is_cuda:
+        return native().mx_quantize(x2.contiguous(), blocked)
+    from difflet_b200.ops.mx import quantize_mx
+
+    q, s = quantize_mx(x2)
+    return q, (block_scales(s) if blocked else s)
+
+
+def linear_mx(aq, a_sf, bq, b_sf, bias=None, *, out=None, act=None, act_lo=0, act_hi=None, gate=None, resid=None,
+              rows_per_batch=0, alpha=1.0, out_f32=False, accumulate=False, out_dtype=None):
+    """``act(A B^T + b)`` (or ``resid + gate * (...)``) from MXFP8 operands with blocked
+    scales: A [M, K] activations, B [N, K] weights (``mx_quantize(..., blocked=True)``)."""
+    M, N = aq.shape[0], bq.shape[0]
+    if out_dtype is not None:
+        out_f32 = out_dtype == torch.float32
+    if aq.is_cuda:
+        act_hi = N if act_hi is None else act_hi
+        epi = EPI_GATE_RESID if gate is not None else _ACT[act]
+        if accumulate:
+            y = native().gemm_mx(aq, a_sf, bq, b_sf, bias, None, epi, act_lo, act_hi, gate, rows_per_batch, resid,
+                                 alpha, True)
+            out.add_(y.to(out.dtype))
+            return out
+        return native().gemm_mx(aq, a_sf, bq, b_sf, bias, out, epi, act_lo, act_hi, gate, rows_per_batch, resid,
+                                alpha, out_f32)
+    from difflet_b200.ops.mx import dequantize_mx
+
+    K = aq.shape[1]
+    a = dequantize_mx(aq, unblock_scales(a_sf, M, K), output_dtype=torch.float32)
+    b = dequantize_mx(bq, unblock_scales(b_sf, N, K), output_dtype=torch.float32)
+    y = linear(a, b, bias.float() if bias is not None else None, act=act, act_lo=act_lo, act_hi=act_hi,
+               gate=gate, resid=resid.float() if resid is not None else None, rows_per_batch=rows_per_batch,
+               alpha=alpha)
+    if accumulate:
+        out.add_(y.to(out.dtype))
+        return out
+    if out is not None:
+        out.copy_(y.to(out.dtype))
+        return out
+    return y.to(torch.float32 if out_f32 else torch.bfloat16)
+
+
 MERGE_FIRST, MERGE_MID, MERGE_LAST = 1, 2, 3
 
 

@@ -94,11 +94,15 @@ def matmul_mx(a_mx, a_scale, b_mx, b_scale, *, dtype: str = "float8_e4m3fn", out
     """``A @ B^T`` from MX operands (A ``[M, K]``, B ``[N, K]``); ``accumulate`` adds into ``out``."""
     _fmt(dtype)
     _check_group(group_size)
-    if a_mx.is_cuda and a_mx.dtype == torch.float8_e4m3fn and b_mx.dtype == torch.float8_e4m3fn:
+    if (a_mx.is_cuda and a_mx.dtype == torch.float8_e4m3fn and b_mx.dtype == torch.float8_e4m3fn
+            and a_mx.shape[-1] % 128 == 0):
         from difflet_b200.ops import fused as F
 
-        return F.linear_mx(a_mx, a_scale, b_mx, b_scale, bias=bias, out=out, accumulate=accumulate,
-                           out_dtype=out_dtype)
+        M, N = a_mx.shape[0], b_mx.shape[0]
+        if accumulate and out is None:
+            raise ValueError("accumulate=True needs out")
+        return F.linear_mx(a_mx, F.block_scales(a_scale), b_mx, F.block_scales(b_scale), bias=bias, out=out,
+                           accumulate=accumulate, out_dtype=out_dtype if out is None else out.dtype)
     a = dequantize_mx(a_mx, a_scale, dtype=dtype, output_dtype=torch.float32)
     b = dequantize_mx(b_mx, b_scale, dtype=dtype, output_dtype=torch.float32)
     y = a @ b.t()
