@@ -104,6 +104,8 @@ def main(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cp-mode", default="ulysses", choices=["ulysses", "ring", "gather_kv"])
+    ap.add_argument("--quant", default=None, choices=[None, "mxfp8"],
+                    help="MXFP8 block linears (default targets); the headline number is bf16")
     args = ap.parse_args(argv)
     import faulthandler
 
@@ -126,7 +128,8 @@ def main(argv=None):
     t_load = time.time()
     pipe = DiffletPipeline.from_pretrained(
         "black-forest-labs/FLUX.1-dev", parallel=par, height=args.height, width=args.width, random_init=True,
-        skip_warmup=True, application_kwargs={"cuda_graph": not args.no_graph})
+        skip_warmup=True, application_kwargs={"cuda_graph": not args.no_graph,
+                                              **({"quant": args.quant} if args.quant else {})})
     load_s = time.time() - t_load
     _log(f"pipeline loaded in {load_s:.1f}s")
     app = pipe.app.app
@@ -228,7 +231,7 @@ def main(argv=None):
             "higher_is_better": False,
             "scaling": "strong",
             "vs_baseline": round(ms / REF_PUBLISHED_STEP_MS, 4),
-            "dtype": "bf16",
+            "dtype": "bf16" if not args.quant else "bf16 + mxfp8 block linears",
             "data": "synthetic (random-init FLUX.1-dev weights, N(0,1) text states / pooled / latents)",
             "config": {"model": "FLUX.1-dev", "global_batch": B, "seq_len": S_img + S_txt,
                        "height": args.height, "width": args.width,

@@ -61,6 +61,9 @@ class FluxEngine:
             from difflet_b200.parallel.ulysses import make_sequence_parallel
 
             dit.par = make_sequence_parallel(self.parallel, dev)
+        from difflet_b200.quant.apply import quantize_engine_model
+
+        self.quant_report = quantize_engine_model(dit, "flux", self.kw)
         self.app = FluxApplication(dit, vae, use_cuda_graph=(self.backend == "cuda" and self.kw.get("cuda_graph", True)))
         if self.kw.get("teacache_speedup"):
             from difflet_b200.pipeline.teacache import build_controller

@@ -50,6 +50,9 @@ class MMDiTEngine:
 
             dit = MMDiT.from_diffusers_state_dict(self.cfg, load_component(self.model_path, "transformer"),
                                                   device=dev, dtype=self.dtype)
+        from difflet_b200.quant.apply import quantize_engine_model
+
+        self.quant_report = quantize_engine_model(dit, self.entry.name, self.kw)
         vae = self.make_vae(dev)
         cfg_par = None
         if self.parallel.world_size > 1:

@@ -55,6 +55,9 @@ class WanEngine:
 
             seq_par = make_sequence_parallel(self.parallel, dev)
             cfg_par = make_cfg_parallel(self.parallel, dev)
+        from difflet_b200.quant.apply import quantize_engine_model
+
+        self.quant_report = [quantize_engine_model(e, "wan", self.kw) for e in experts]
         self.app = WanApplication(experts, vae, flow_shift=float(self.kw.get("flow_shift", 12.0 if n == 2 else 5.0)),
                                   cfg_par=cfg_par, seq_par=seq_par)
 

@@ -49,15 +49,58 @@ def _rows2d(x: torch.Tensor) -> torch.Tensor:
     return x if x.dim() == 2 else x.reshape(-1, x.shape[-1])
 
 
+class MXWeight:
+    """A Linear weight held in MXFP8: FP8 E4M3 [N, K] + blocked E8M0 scales.  ``linear``
+    quantizes its input on the fly (``compute="mx"``, block-scaled tensor cores) or
+    dequantizes the weight to bf16 per call (``compute="dequant"``, memory only)."""
+
+    def __init__(self, q: torch.Tensor, sf_blocked: torch.Tensor, compute: str = "mx"):
+        self.q, self.sf, self.compute = q, sf_blocked, compute
+
+    @classmethod
+    def quantize(cls, w: torch.Tensor, compute: str = "mx") -> "MXWeight":
+        q, sf = mx_quantize(w.to(torch.bfloat16).contiguous(), blocked=True)
+        return cls(q, sf, compute)
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+    @property
+    def device(self):
+        return self.q.device
+
+    @property
+    def dtype(self):
+        return self.q.dtype
+
+    def dequantize(self, dtype=torch.bfloat16) -> torch.Tensor:
+        from difflet_b200.ops.mx import dequantize_mx
+
+        N, K = self.q.shape
+        return dequantize_mx(self.q, unblock_scales(self.sf, N, K), output_dtype=dtype)
+
+    def to(self, device=None, dtype=None):
+        if device is None:
+            return self
+        return MXWeight(self.q.to(device), self.sf.to(device), self.compute)
+
+
 # ---------------------------------------------------------------------------
 def linear(x, w, b=None, *, out=None, act=None, act_lo=0, act_hi=None, gate=None, resid=None,
            rows_per_batch=0, alpha=1.0, out_f32=False):
     """``act(alpha * x @ w.T + b)`` or ``resid + gate * (...)``.
 
-    x: [M, K]; w: [N, K]; b: [N]; gate: f32 [B, N] (rows_per_batch rows each);
-    resid: [M, N] (may be ``out``).  ``act`` applies to columns [act_lo, act_hi).
+    x: [M, K]; w: [N, K] (or an ``MXWeight``); b: [N]; gate: f32 [B, N] (rows_per_batch
+    rows each); resid: [M, N] (may be ``out``).  ``act`` applies to columns [act_lo, act_hi).
     """
     x2 = _rows2d(x)
+    if isinstance(w, MXWeight):
+        if w.compute == "mx":
+            xq, xs = mx_quantize(x2, blocked=True)
+            return linear_mx(xq, xs, w.q, w.sf, b, out=out, act=act, act_lo=act_lo, act_hi=act_hi, gate=gate,
+                             resid=resid, rows_per_batch=rows_per_batch, alpha=alpha, out_f32=out_f32)
+        w = w.dequantize(x2.dtype if not x2.is_cuda else torch.bfloat16)
     N = w.shape[0]
     act_hi = N if act_hi is None else act_hi
     if x2.is_cuda and envs.DIFFLET_KERNEL_GEMM != "cublas":

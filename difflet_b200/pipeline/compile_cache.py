@@ -107,6 +107,10 @@ class CacheSpec:
         }
         if self.candidate is not None and not self.candidate.is_trivial:
             d["candidate"] = self.candidate.to_cache_dict()
+        if (self.application_kwargs or {}).get("quant"):
+            from difflet_b200.quant.apply import spec_from_kwargs
+
+            d.update(spec_from_kwargs(self.model_name, self.application_kwargs).cache_fields())
         return d
 
     def manifest_metadata(self) -> dict[str, Any]:

@@ -43,7 +43,7 @@ def load_component(model_path: str, component: str, *, dtype=None, device="cpu",
                     t = h.get_slice(k)[a:b]
                 else:
                     t = h.get_tensor(k)
-                if dtype is not None and t.is_floating_point():
+                if dtype is not None and t.is_floating_point() and t.element_size() > 1:  # FP8 stays FP8
                     t = t.to(dtype)
                 out[k] = t.to(device)
     return out

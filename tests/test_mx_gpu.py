@@ -95,3 +95,28 @@ def test_matmul_mx_surface(native):
     ref = ops.matmul_mx(aq.cpu(), as_.cpu(), wq.cpu(), ws.cpu(), out_dtype=torch.float32)
     torch.cuda.synchronize()
     _close(y.cpu(), ref)
+
+
+def test_quantized_flux_model_matches_cpu_oracle(native):
+    """A tiny FLUX with the default MXFP8 targets on the GPU (block-scaled GEMMs, on-the-fly
+    activation quantization) against the same quantized model on the CPU oracle."""
+    from difflet_b200.models.flux.config import get_config
+    from difflet_b200.models.flux.model import FluxTransformer, pack_latents
+    from difflet_b200.quant import default_spec
+    from difflet_b200.quant.apply import apply_quant
+
+    cfg = get_config("tiny128", hidden=512, heads=4)
+    m_cpu = FluxTransformer.random_init(cfg, dtype=torch.float32, seed=3)
+    m_gpu = FluxTransformer(cfg, {k: v.to("cuda", torch.bfloat16) for k, v in m_cpu.w.items()})
+    spec = default_spec("flux")
+    r1, r2 = apply_quant(m_cpu, spec), apply_quant(m_gpu, spec)
+    assert r1["quantized"] == r2["quantized"] and r1["quantized"]
+    g = torch.Generator().manual_seed(0)
+    x = pack_latents(torch.randn(1, 16, 32, 32, generator=g))
+    txt = torch.randn(1, 64, cfg.text_dim, generator=g)
+    pooled = torch.randn(1, cfg.pooled_dim, generator=g)
+    t, gd = torch.tensor([0.4]), torch.tensor([3.5])
+    ref = m_cpu(x, txt, pooled, t, gd, img_hw=(16, 16))
+    out = m_gpu(x.cuda().bfloat16(), txt.cuda().bfloat16(), pooled.cuda(), t.cuda(), gd.cuda(), img_hw=(16, 16))
+    torch.cuda.synchronize()
+    assert ((out.float().cpu() - ref).norm() / ref.norm()).item() < 3e-2
