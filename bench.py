@@ -103,7 +103,8 @@ def main(argv=None):
     ap.add_argument("--e2e-images", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--cp-mode", default="ulysses", choices=["ulysses", "ring", "gather_kv"])
+    ap.add_argument("--cp-mode", default="ulysses", choices=["ulysses", "ring", "gather_kv", "tp"],
+                    help="how N>1 GPUs split the step: a context-parallel mode, or tensor parallelism")
     ap.add_argument("--quant", default=None, choices=[None, "mxfp8"],
                     help="MXFP8 block linears (default targets); the headline number is bf16")
     args = ap.parse_args(argv)
@@ -124,7 +125,12 @@ def main(argv=None):
     from difflet_b200.pipeline.difflet_pipeline import DiffletPipeline
     from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
 
-    par = DiffletParallelConfig(cp_degree=world, cp_mode=args.cp_mode) if world > 1 else DiffletParallelConfig()
+    if world == 1:
+        par = DiffletParallelConfig()
+    elif args.cp_mode == "tp":
+        par = DiffletParallelConfig(tp_degree=world)
+    else:
+        par = DiffletParallelConfig(cp_degree=world, cp_mode=args.cp_mode)
     t_load = time.time()
     pipe = DiffletPipeline.from_pretrained(
         "black-forest-labs/FLUX.1-dev", parallel=par, height=args.height, width=args.width, random_init=True,
@@ -139,10 +145,12 @@ def main(argv=None):
     B = 1
     h_tok, w_tok = args.height // 16, args.width // 16
     S_img, S_txt = h_tok * w_tok, 512
-    S_img_l, S_txt_l = S_img // world, S_txt // world
+    tp_mode = world > 1 and args.cp_mode == "tp"
+    shards = 1 if tp_mode else world  # TP replicates the tokens; CP shards them
+    S_img_l, S_txt_l = S_img // shards, S_txt // shards
 
     # ---------------- DiT step (device-timed) ----------------
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    g = torch.Generator(device=dev).manual_seed(1234 + (0 if tp_mode else rank))
     x32 = torch.randn(B, S_img_l, cfg.in_channels, device=dev, generator=g)
     x16 = x32.to(torch.bfloat16)
     txt = torch.randn(B, S_txt_l, cfg.text_dim, device=dev, generator=g).to(torch.bfloat16)

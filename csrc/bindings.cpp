@@ -438,6 +438,42 @@ int64_t ipc_open(py::bytes handle, int64_t device) {
 
 void ipc_close(int64_t ptr) { dfl_ipc_close(reinterpret_cast<void*>(ptr)); }
 
+void tp_reduce(const at::Tensor& slots, int64_t slot_rows, int64_t world, int64_t rows, int64_t N, int64_t row0,
+               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
+               const c10::optional<at::Tensor>& resid, std::vector<int64_t> out, int64_t ldo, int64_t out_row0) {
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kBFloat16, "slots must be CUDA bf16");
+  TORCH_CHECK(slots.numel() >= world * slot_rows * N, "slots too small");
+  TORCH_CHECK(!out.empty() && out.size() <= DFL_MAX_PEERS, "1..8 output pointers");
+  const c10::cuda::CUDAGuard guard(slots.device());
+  TpReduceArgs a{};
+  a.slots = slots.data_ptr();
+  a.slot_rows = slot_rows;
+  a.world = (int)world;
+  a.rows = (int)rows;
+  a.N = (int)N;
+  a.row0 = row0;
+  if (bias.has_value() && bias->defined()) {
+    check_bf16_cuda(*bias, "bias");
+    a.bias = bias->data_ptr();
+  }
+  if (gate.has_value() && gate->defined()) {
+    TORCH_CHECK(gate->scalar_type() == at::kFloat && gate->stride(1) == 1, "gate must be f32 [B, >=N]");
+    TORCH_CHECK(resid.has_value() && resid->defined(), "gate needs resid");
+    check_bf16_cuda(*resid, "resid");
+    check_rowmajor(*resid, "resid");
+    a.gate = gate->data_ptr<float>();
+    a.gate_bstride = gate->stride(0);
+    a.rows_per_batch = (int)rows_per_batch;
+    a.resid = resid->data_ptr();
+    a.ldr = resid->stride(0);
+  }
+  a.out_world = (int)out.size();
+  for (size_t d = 0; d < out.size(); ++d) a.out[d] = reinterpret_cast<void*>(out[d]);
+  a.ldo = ldo;
+  a.out_row0 = out_row0;
+  DFL_CHECK_RC(dfl_tp_reduce(&a, cur_stream()), "tp_reduce");
+}
+
 void memcpy_async(int64_t dst, int64_t src, int64_t nbytes) {
   DFL_CHECK_RC(dfl_memcpy_async(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), nbytes,
                                 cur_stream()),
@@ -541,6 +577,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("memcpy_async", &memcpy_async);
+  m.def("tp_reduce", &tp_reduce, py::arg("slots"), py::arg("slot_rows"), py::arg("world"), py::arg("rows"),
+        py::arg("N"), py::arg("row0"), py::arg("bias") = py::none(), py::arg("gate") = py::none(),
+        py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("out") = std::vector<int64_t>{},
+        py::arg("ldo") = 0, py::arg("out_row0") = 0);
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_put_f32", &peer_put_f32);
   m.def("cfg_combine", &cfg_combine);

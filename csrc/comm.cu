@@ -97,7 +97,76 @@ __global__ void cfg_combine_kernel(const __nv_bfloat16* __restrict__ mine, const
   }
 }
 
+// Sum of the world partials of this rank's rows (fp32, fixed source order:
+// deterministic), bias, gated residual, bf16 stores to every destination rank.
+__global__ void __launch_bounds__(256) tp_reduce_kernel(TpReduceArgs a) {
+  const int n8 = a.N / 8;
+  const long long total = (long long)a.rows * n8;
+  const __nv_bfloat16* slots = reinterpret_cast<const __nv_bfloat16*>(a.slots);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / n8);
+    const int c = (int)(i - (long long)r * n8) * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int src = 0; src < a.world; ++src) {
+      const uint4 w = *reinterpret_cast<const uint4*>(slots + ((long long)src * a.slot_rows + r) * a.N + c);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack_bf16x2(ws[h]);
+        v[2 * h] += f.x;
+        v[2 * h + 1] += f.y;
+      }
+    }
+    if (a.bias) {
+      const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.bias) + c);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack_bf16x2(ws[h]);
+        v[2 * h] += f.x;
+        v[2 * h + 1] += f.y;
+      }
+    }
+    const long long grow = a.row0 + r;
+    if (a.gate) {
+      const float* g = a.gate + (grow / a.rows_per_batch) * a.gate_bstride + c;
+      const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.resid) + grow * a.ldr + c);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack_bf16x2(ws[h]);
+        v[2 * h] = f.x + g[2 * h] * v[2 * h];
+        v[2 * h + 1] = f.y + g[2 * h + 1] * v[2 * h + 1];
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(v[0], v[1]);
+    o.y = pack_bf16x2(v[2], v[3]);
+    o.z = pack_bf16x2(v[4], v[5]);
+    o.w = pack_bf16x2(v[6], v[7]);
+    const long long orow = a.out_row0 + r;
+    for (int d = 0; d < a.out_world; ++d)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out[d]) + orow * a.ldo + c) = o;
+  }
+}
+
 }  // namespace
+
+extern "C" int dfl_tp_reduce(const TpReduceArgs* a, cudaStream_t stream) {
+  if (a->rows <= 0) return 0;
+  if (a->N % 8 || a->ldo % 8 || (a->gate && (a->ldr % 8 || a->gate_bstride % 4 || a->rows_per_batch <= 0)))
+    return -2;
+  if (a->out_world < 1 || a->out_world > DFL_MAX_PEERS || a->world < 1) return -3;
+  uintptr_t al = reinterpret_cast<uintptr_t>(a->slots) | reinterpret_cast<uintptr_t>(a->bias) |
+                 reinterpret_cast<uintptr_t>(a->resid) | reinterpret_cast<uintptr_t>(a->gate);
+  for (int d = 0; d < a->out_world; ++d) al |= reinterpret_cast<uintptr_t>(a->out[d]);
+  if (al & 15) return -4;
+  long long blocks = ((long long)a->rows * (a->N / 8) + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  tp_reduce_kernel<<<(int)blocks, 256, 0, stream>>>(*a);
+  return (int)cudaGetLastError();
+}
 
 extern "C" int dfl_cfg_combine(const void* mine, const void* peer, float* out, long long n, float scale,
                                int mine_is_cond, cudaStream_t stream) {

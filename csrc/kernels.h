@@ -183,6 +183,25 @@ typedef struct PeerPutArgs {
 } PeerPutArgs;
 int dfl_peer_put_f32(const PeerPutArgs* a, cudaStream_t stream);
 
+// Tensor-parallel reduction of row-parallel partials (the second half of the
+// fused GEMM -> reduce-scatter / all-reduce): this rank owns `rows` rows starting
+// at global row row0; slots holds every source rank's bf16 partial of them
+// ([world][slot_rows][N], written by the GEMM epilogue's row scatter).  y = sum +
+// bias, optionally resid + gate[b] * y, stored to out[0..out_world) at row row0 + r
+// (out_world = tp: all-reduce; 1: reduce-scatter for sequence parallelism).
+typedef struct TpReduceArgs {
+  const void* slots;
+  long long slot_rows;
+  int world, rows, N;
+  long long row0;
+  const void* bias;                     // bf16 [N] or NULL
+  const float* gate; long long gate_bstride; int rows_per_batch;  // gated residual or NULL
+  const void* resid; long long ldr;     // bf16, indexed by global row
+  void* out[DFL_MAX_PEERS]; long long ldo; int out_world;
+  long long out_row0;                   // row of out that receives global row row0
+} TpReduceArgs;
+int dfl_tp_reduce(const TpReduceArgs* a, cudaStream_t stream);
+
 // Copy-engine copy (peer -> local over NVLink; no SM work, no kernel).
 int dfl_memcpy_async(void* dst, const void* src, long long nbytes, cudaStream_t stream);
 

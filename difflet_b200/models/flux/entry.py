@@ -61,6 +61,11 @@ class FluxEngine:
             from difflet_b200.parallel.ulysses import make_sequence_parallel
 
             dit.par = make_sequence_parallel(self.parallel, dev)
+        if self.parallel.tp_degree > 1:  # this rank's heads / MLP columns, before any quantization
+            from difflet_b200.parallel.tp import make_tensor_parallel, shard_mmdit_weights
+
+            dit.tp = make_tensor_parallel(self.parallel, dev)
+            dit.w = shard_mmdit_weights(dit.cfg, dit.w, dit.tp.world, dit.tp.rank)
         from difflet_b200.quant.apply import quantize_engine_model
 
         self.quant_report = quantize_engine_model(dit, "flux", self.kw)

@@ -50,6 +50,11 @@ class MMDiTEngine:
 
             dit = MMDiT.from_diffusers_state_dict(self.cfg, load_component(self.model_path, "transformer"),
                                                   device=dev, dtype=self.dtype)
+        if self.parallel.tp_degree > 1:  # this rank's heads / MLP columns, before any quantization
+            from difflet_b200.parallel.tp import make_tensor_parallel, shard_mmdit_weights
+
+            dit.tp = make_tensor_parallel(self.parallel, dev)
+            dit.w = shard_mmdit_weights(dit.cfg, dit.w, dit.tp.world, dit.tp.rank)
         from difflet_b200.quant.apply import quantize_engine_model
 
         self.quant_report = quantize_engine_model(dit, self.entry.name, self.kw)

@@ -42,6 +42,7 @@ class MMDiT:
         self._ws = {}
         self._rope = {}
         self.par = None  # sequence-parallel context (None = single device)
+        self.tp = None   # tensor-parallel context: weights hold this rank's heads / MLP columns
 
     # ------------------------------------------------------------------ weights
     @property
@@ -147,6 +148,9 @@ class MMDiT:
         D, F_, H, dh = cfg.hidden, cfg.mlp_hidden, cfg.heads, cfg.head_dim
         dev, dt = self.device, self.dtype
         par = self.par
+        tp = self.tp
+        T = tp.world if tp is not None else 1
+        Dl, Fl = D // T, F_ // T  # this rank's attention / MLP columns
         world = par.world if par is not None else 1
         S_txt_g, S_img_g = S_txt * world, S_img * world
         S = S_txt_g + S_img_g
@@ -160,27 +164,30 @@ class MMDiT:
               "row": {s0: 0, s1: n[s0]},
               # global position of this rank's first row of each stream
               "pos": {s0: (par.rank if par else 0) * n[s0], s1: ng[s0] + (par.rank if par else 0) * n[s1]}}
-        ws["x"] = e(B, S_loc, D)  # residual stream [seg0_local ; seg1_local] per batch
+        # residual stream [seg0_local ; seg1_local] per batch (replicated in peer memory under TP)
+        ws["x"] = tp.empty((B, S_loc, D), dt) if tp is not None else e(B, S_loc, D)
         if B == 1:
             for st in ("txt", "img"):
                 r0 = ws["row"][st]
                 ws["x_" + st] = ws["x"][0, r0:r0 + n[st]]
         else:
-            ws["x_txt"] = e(B * S_txt, D)
-            ws["x_img"] = e(B * S_img, D)
+            xe = (lambda *shape: tp.empty(shape, dt)) if tp is not None else e  # noqa: E731
+            ws["x_txt"] = xe(B * S_txt, D)
+            ws["x_img"] = xe(B * S_img, D)
         ws["norm"] = e(B * S_loc, D)
-        ws["qkv_img"] = e(B * S_img, 3 * D)
-        ws["qkv_txt"] = e(B * S_txt, 3 * D)
-        ws["mlp"] = e(B * max(S_img, S_txt), F_)
+        ws["qkv_img"] = e(B * S_img, 3 * Dl)
+        ws["qkv_txt"] = e(B * S_txt, 3 * Dl)
+        ws["mlp"] = e(B * max(S_img, S_txt), Fl)
         pe = (lambda *shape: par.empty(shape, dt)) if par is not None else e  # noqa: E731
         if par is not None:
             par.check_heads(H)
-        ws["fused"] = pe(B * S_loc, 3 * D + F_) if cfg.single_blocks else None
+        ws["fused"] = pe(B * S_loc, 3 * Dl + Fl) if cfg.single_blocks else None
         if par is not None:  # the CP mode decides the q/k/v layout (heads x full sequence, or local rows)
             ws["q"], ws["k"], ws["v"] = par.layout(B, H, dh, S_loc, S, dt)
         else:
-            ws["q"], ws["k"], ws["v"] = e(B, H, S, dh), e(B, H, S, dh), e(B, H, S, dh)
-        ws["attn"] = pe(B, S_loc, D)
+            Ht = H // T
+            ws["q"], ws["k"], ws["v"] = e(B, Ht, S, dh), e(B, Ht, S, dh), e(B, Ht, S, dh)
+        ws["attn"] = pe(B, S_loc, Dl)
         self._ws[key] = ws
         return ws
 
@@ -215,7 +222,7 @@ class MMDiT:
 
     def modulation(self, temb: torch.Tensor) -> torch.Tensor:
         """All blocks' adaLN vectors in one GEMV: f32 [B, N_mod] = W_mod silu(temb) + b."""
-        par = self.par
+        par = self.par if self.par is not None else self.tp
         if par is not None and hasattr(par, "shard_gemv") and temb.is_cuda:
             out = par.shard_gemv(self.w["mod.w"], temb, self.w["mod.b"], silu_in=True)
             if out is not None:
@@ -297,8 +304,20 @@ class MMDiT:
                 img_hw = (side, S_img_g // side)
             grid = (1, img_hw[0], img_hw[1])
         cos, sin = self.rope(S_txt_g, grid)
-        Hl = par.heads_local(H) if par is not None else H
+        tp = self.tp
+        T = tp.world if tp is not None else 1
+        if tp is not None and par is not None:
+            raise NotImplementedError("tensor parallelism composes with cfg-parallel here, not with cp")
+        Ht, Dl, Fl = H // T, D // T, F_ // T  # heads / attention / MLP columns held by this rank
+        Hl = par.heads_local(H) if par is not None else Ht
         S_loc = S_txt + S_img
+
+        def row_linear(xin, wt, bias, out, gate, rpb):
+            """Row-parallel (under TP) output projection fused with out += gate * (.)"""
+            if tp is not None:
+                tp.row_linear(xin, wt, bias, out=out, gate=gate, resid=out, rows_per_batch=rpb)
+            else:
+                F.linear(xin, wt, bias, out=out, gate=gate, resid=out, rows_per_batch=rpb)
         if mod is None:
             mod = self.modulation(self.temb(timestep, guidance, pooled))
         kv_lo = kv_hi = None
@@ -323,7 +342,7 @@ class MMDiT:
             """qkv_scatter destinations for rows at local offset ``row`` / global position ``pos``."""
             if par is not None:
                 return par.scatter_kwargs(q_, k_, v_, row, pos, S_loc, S, H)
-            return dict(q_dst=[q_], k_dst=[k_], v_dst=[v_], S_dst=S, seq_off=pos, heads_per_rank=H)
+            return dict(q_dst=[q_], k_dst=[k_], v_dst=[v_], S_dst=S, seq_off=pos, heads_per_rank=Ht)
 
         def mslice(off):
             return mod[:, off:off + D]
@@ -336,7 +355,7 @@ class MMDiT:
                 nb = norm[: B * nr]
                 F.ln_modulate(xs, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=nr, out=nb)
                 F.linear(nb, w[p + st + "_qkv.w"], w[p + st + "_qkv.b"], out=ws["qkv_" + st])
-                F.qkv_scatter(ws["qkv_" + st], q_off=0, k_off=D, v_off=2 * D, S_src=nr, H=H, dh=dh,
+                F.qkv_scatter(ws["qkv_" + st], q_off=0, k_off=Dl, v_off=2 * Dl, S_src=nr, H=Ht, dh=dh,
                               **dst(q, k, v, row_of[st], pos), norm_mode=1, wq=w[p + st + "_qnorm"],
                               wk=w[p + st + "_knorm"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos)
             self._attention(ws, B, S_txt, S_img, D, Hl, dh, kv_lo=kv_lo, kv_hi=kv_hi)
@@ -345,13 +364,12 @@ class MMDiT:
                 o = cfg.double_mod_offset(i, st)
                 rows = slice(row_of[st], row_of[st] + nr)
                 self._rows_gemm(ws["attn"], rows, B, nr, w[p + st + "_out.w"], w[p + st + "_out.b"], xs,
-                                mslice(o + 2 * D))
+                                mslice(o + 2 * D), row_linear)
                 nb = norm[: B * nr]
                 F.ln_modulate(xs, shift=mslice(o + 3 * D), scale=mslice(o + 4 * D), eps=eps, rows_per_batch=nr, out=nb)
                 mb = ws["mlp"][: B * nr]
                 F.linear(nb, w[p + st + "_up.w"], w[p + st + "_up.b"], out=mb, act="gelu")
-                F.linear(mb, w[p + st + "_down.w"], w[p + st + "_down.b"], out=xs, gate=mslice(o + 5 * D),
-                         resid=xs, rows_per_batch=nr)
+                row_linear(mb, w[p + st + "_down.w"], w[p + st + "_down.b"], xs, mslice(o + 5 * D), nr)
 
         if B > 1:  # dual -> single: the residual stream becomes [seg0 ; seg1] per batch
             for st in ("txt", "img"):
@@ -364,12 +382,12 @@ class MMDiT:
             p = f"single.{j}."
             o = cfg.single_mod_offset(j)
             F.ln_modulate(x2, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=S_loc, out=norm)
-            F.linear(norm, w[p + "fused.w"], w[p + "fused.b"], out=fused, act="gelu", act_lo=D, act_hi=D + F_)
+            F.linear(norm, w[p + "fused.w"], w[p + "fused.b"], out=fused, act="gelu", act_lo=Dl, act_hi=Dl + Fl)
             if par is None:  # positions equal local rows: one pass over every row
-                F.qkv_scatter(fused, q_off=0, k_off=D + F_, v_off=2 * D + F_, S_src=S_loc, H=H, dh=dh,
+                F.qkv_scatter(fused, q_off=0, k_off=Dl + Fl, v_off=2 * Dl + Fl, S_src=S_loc, H=Ht, dh=dh,
                               q_dst=[q], k_dst=[k], v_dst=[v], S_dst=S, seq_off=0, norm_mode=1,
                               wq=w[p + "qnorm"], wk=w[p + "knorm"], eps=eps, cos=cos, sin=sin, rope_pos_off=0,
-                              heads_per_rank=Hl)
+                              heads_per_rank=Ht)
             else:
                 for b in range(B):
                     rows = fused[b * S_loc:(b + 1) * S_loc]
@@ -380,8 +398,7 @@ class MMDiT:
                                       wq=w[p + "qnorm"], wk=w[p + "knorm"], eps=eps, cos=cos, sin=sin,
                                       rope_pos_off=pos)
             self._attention(ws, B, S_txt, S_img, D, Hl, dh, out_rows=fused, kv_lo=kv_lo, kv_hi=kv_hi)
-            F.linear(fused[:, : D + F_], w[p + "proj.w"], w[p + "proj.b"], out=x2, gate=mslice(o + 2 * D),
-                     resid=x2, rows_per_batch=S_loc)
+            row_linear(fused[:, : Dl + Fl], w[p + "proj.w"], w[p + "proj.b"], x2, mslice(o + 2 * D), S_loc)
 
         # final adaLN-continuous (scale, shift) on the image rows + projection
         o = cfg.final_mod_offset()
@@ -418,15 +435,15 @@ class MMDiT:
         F.attention(q, k, v, scale, out=o, kv_lo=kv_lo, kv_hi=kv_hi)
 
     @staticmethod
-    def _rows_gemm(attn, rows, B, n_rows, wt, bias, xs, gate):
+    def _rows_gemm(attn, rows, B, n_rows, wt, bias, xs, gate, row_linear):
         """Output projection of one stream's rows of the attention output, fused with
-        ``x += gate * (o W^T + b)``."""
+        ``x += gate * (o W^T + b)`` (row-parallel under TP)."""
         if B == 1:
-            F.linear(attn[0, rows], wt, bias, out=xs, gate=gate, resid=xs, rows_per_batch=n_rows)
+            row_linear(attn[0, rows], wt, bias, xs, gate, n_rows)
             return
         for b in range(B):
             xb = xs[b * n_rows:(b + 1) * n_rows]
-            F.linear(attn[b, rows], wt, bias, out=xb, gate=gate[b:b + 1], resid=xb, rows_per_batch=n_rows)
+            row_linear(attn[b, rows], wt, bias, xb, gate[b:b + 1], n_rows)
 
 
 def pack_latents(lat: torch.Tensor, patch: int = 2) -> torch.Tensor:

@@ -1,0 +1,161 @@
+"""Tensor parallelism for the MMDiT families (Megatron column / row split).
+
+Column-parallel linears (q/k/v, MLP up, FLUX's single-block [q|mlp|k|v]) hold this
+rank's heads / MLP columns and need no communication; attention runs on the local
+heads over the whole sequence.  Row-parallel linears (attention output, MLP down,
+single-block ``proj_out`` over [attn|mlp]) produce partial sums that must be
+reduced; the B200 path fuses that reduction with the GEMM:
+
+``PeerTP.row_linear`` (peer memory)
+    1. the tcgen05 GEMM's epilogue stores each partial row straight into the
+       symmetric slot buffer of the rank that owns the row (row scatter over
+       NVLink, overlapped with the GEMM's remaining tiles);
+    2. device barrier;
+    3. ``tp_reduce`` on the owner sums the tp partials in a fixed order (fp32,
+       deterministic), adds the bias and the gated residual, and stores the
+       finished rows into every rank's residual stream (the all-gather half of
+       the all-reduce is its store pattern);
+    4. device barrier.
+``CollectiveTP.row_linear``: GEMM, ``all_reduce`` (NCCL / gloo), epilogue in
+torch -- the baseline and the CPU multi-rank oracle.
+
+Reference semantics: ColumnParallelLinear / RowParallelLinear and the TP
+collectives (difflet/backends/neuron/ops_impl/collectives.py:115-200), FLUX's
+merged single-block all-reduce (difflet/models/flux/modeling_flux.py:723-727),
+TP-aware q/k norms; the TPU collective-matmul design precedent
+(difflet/backends/tpu/ops_impl/collective_matmul.py:14-17).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from difflet_b200.ops import fused as F
+from difflet_b200.parallel.ulysses import PeerBase, _Base
+
+
+def _cols(t, lo, hi):
+    return t[:, lo:hi]
+
+
+def shard_mmdit_weights(cfg, w: dict, tp: int, rank: int) -> dict:
+    """This rank's slices of an MMDiT's fused weights (heads, MLP columns, K ranges)."""
+    if tp == 1:
+        return dict(w)
+    D, F_, H = cfg.hidden, cfg.mlp_hidden, cfg.heads
+    if H % tp or F_ % tp:
+        raise ValueError(f"tensor parallelism needs heads ({H}) and MLP width ({F_}) divisible by tp={tp}")
+    Dl, Fl = D // tp, F_ // tp
+    d0, d1, f0, f1 = rank * Dl, (rank + 1) * Dl, rank * Fl, (rank + 1) * Fl
+    out = {}
+    for k, t in w.items():
+        if k.startswith("ref."):
+            out[k] = t  # the token refiner runs replicated
+        elif k.endswith("_qkv.w") or k.endswith("_qkv.b"):
+            parts = t.split(D, 0)
+            out[k] = torch.cat([p[d0:d1] for p in parts], 0).contiguous()
+        elif k.endswith("_out.w"):
+            out[k] = t[:, d0:d1].contiguous()
+        elif k.endswith("_up.w") or k.endswith("_up.b"):
+            out[k] = t[f0:f1].contiguous()
+        elif k.endswith("_down.w"):
+            out[k] = t[:, f0:f1].contiguous()
+        elif k.endswith("fused.w") or k.endswith("fused.b"):
+            q, m, kk, v = t.split([D, F_, D, D], 0)
+            out[k] = torch.cat([q[d0:d1], m[f0:f1], kk[d0:d1], v[d0:d1]], 0).contiguous()
+        elif k.endswith("proj.w") and k.startswith("single."):
+            out[k] = torch.cat([t[:, d0:d1], t[:, D + f0:D + f1]], 1).contiguous()
+        else:
+            out[k] = t  # replicated: embedders, norms, modulation, final layer, refiner
+    return out
+
+
+class _TPBase(_Base):
+    kind = "tp"
+
+    def heads_local(self, H):
+        return H // self.world
+
+
+class PeerTP(_TPBase, PeerBase):
+    def __init__(self, group, ranks, device):
+        super().__init__(group, ranks, device)
+        self._slots = {}
+
+    def slots(self, rpr: int, N: int, dtype) -> torch.Tensor:
+        key = (N, dtype)
+        cur = self._slots.get(key)
+        if cur is None or cur.shape[0] < self.world * rpr:
+            cur = self.heap.empty((self.world * rpr, N), dtype)
+            self._slots[key] = cur
+        return cur
+
+    def row_linear(self, x, w, b=None, *, out, gate=None, resid=None, rows_per_batch=0):
+        """out[rows] = (resid + gate *) (sum over tp of x_r W_r^T + b); ``out`` / ``resid``
+        are replicated (symmetric-heap) row buffers of the same rows as ``x``."""
+        M, N = x.shape[0], w.shape[0]
+        W, r = self.world, self.rank
+        rpr = -(-M // W)
+        slots = self.slots(rpr, N, torch.bfloat16)
+        nat = F.native()
+        peers = self.heap.peer_ptrs(slots)
+        if isinstance(w, F.MXWeight):
+            xq, xs = F.mx_quantize(x, blocked=True)
+            nat.gemm_mx(xq, xs, w.q, w.sf, None, None, 0, out_peer=peers, rows_per_rank=rpr, peer_row_off=r * rpr,
+                        ldd=N)
+        else:
+            nat.gemm(x, w, None, None, 0, out_peer=peers, rows_per_rank=rpr, peer_row_off=r * rpr, ldd=N)
+        self.heap.barrier()  # every partial of this rank's rows has landed
+        rows = max(0, min(rpr, M - r * rpr))
+        nat.tp_reduce(slots, rpr, W, rows, N, r * rpr, b, gate, rows_per_batch if gate is not None else 0,
+                      resid if gate is not None else None, self.heap.peer_ptrs(out), out.stride(0), r * rpr)
+        self.heap.barrier()  # every finished row is in every rank's residual stream
+
+
+class CollectiveTP(_TPBase):
+    """Row-parallel reduction by ``all_reduce`` (NCCL on GPU, gloo on CPU)."""
+
+    def empty(self, shape, dtype):
+        return torch.zeros(shape, dtype=dtype, device=self.device)
+
+    def peer_views(self, t):
+        return [t]
+
+    def row_linear(self, x, w, b=None, *, out, gate=None, resid=None, rows_per_batch=0):
+        if isinstance(w, F.MXWeight):
+            w = w.dequantize()
+        ct = torch.float64 if x.dtype == torch.float64 else torch.float32
+        y = x.to(ct) @ w.to(ct).t()
+        dist.all_reduce(y, group=self.group)
+        if b is not None:
+            y = y + b.to(ct)
+        if gate is not None:
+            M = y.shape[0]
+            rpb = rows_per_batch if rows_per_batch > 0 else M
+            y = resid.to(ct) + gate[:, : y.shape[1]].to(ct).repeat_interleave(rpb, 0)[:M] * y
+        out.copy_(y.to(out.dtype))
+        return out
+
+
+def make_tensor_parallel(parallel, device, transport: str | None = None):
+    """TP context over the tp axis (None when tp_degree == 1)."""
+    from difflet_b200 import envs
+    from difflet_b200.parallel import groups
+
+    if parallel.tp_degree == 1:
+        return None
+    if not dist.is_initialized():
+        raise RuntimeError("tensor parallelism needs an initialised process group (run under torchrun)")
+    if groups.mesh() != parallel.mesh_spec:
+        groups.init_mesh(parallel.mesh_spec)
+    group, ranks = groups.get_group("tp"), groups.get_group_ranks("tp")
+    transport = transport or envs.DIFFLET_KERNEL_COMM
+    if device.type == "cuda" and transport == "fused":
+        return PeerTP(group, ranks, device)
+    return CollectiveTP(group, ranks, device)
+
+
+__all__ = ["CollectiveTP", "PeerTP", "make_tensor_parallel", "shard_mmdit_weights"]

@@ -224,14 +224,14 @@ def make_sequence_parallel(parallel, device, transport: str | None = None):
     (``transport`` "fused", CUDA) or collectives ("nccl" / CPU gloo)."""
     from difflet_b200.parallel import groups
 
+    if parallel.cp_degree == 1:
+        return None
     if not dist.is_initialized():
         raise RuntimeError("sequence parallelism needs an initialised process group (run under torchrun)")
     if parallel.tp_degree != 1 or parallel.dp_degree != 1:
-        raise NotImplementedError("sequence parallelism composes with cfg-parallel here (tp=1, dp=1)")
+        raise NotImplementedError("context parallelism composes with cfg-parallel here (tp=1, dp=1)")
     if groups.mesh() != parallel.mesh_spec:
         groups.init_mesh(parallel.mesh_spec)
-    if parallel.cp_degree == 1:
-        return None
     group, ranks = groups.get_group("cp"), groups.get_group_ranks("cp")
     transport = transport or envs.DIFFLET_KERNEL_COMM
     fused = device.type == "cuda" and transport == "fused"

@@ -83,3 +83,32 @@ def test_block_windows():
     w = block_windows(hi, 4, 3, 2)
     # rank 0 block = img[0:4] + txt[0:3]; rank 1 block = img[4:8] + txt[3:6]
     assert w.tolist() == [[4 + 3, 4 + 3, 4, 4], [4 + 1, 4 + 3, 4, 1]]
+
+
+def _tp_forward(rank, world, B, family):
+    import torch.distributed as dist
+
+    from difflet_b200.models.mmdit import MMDiT, get_config, pack_latents
+    from difflet_b200.parallel.tp import CollectiveTP, shard_mmdit_weights
+
+    name = {"flux": "tiny128", "qwen": "tiny-qwen"}[family]
+    cfg = get_config(name, heads=4, hidden=512) if family == "flux" else get_config(name)
+    m = MMDiT.random_init(cfg, dtype=torch.float64, seed=21)
+    g = torch.Generator().manual_seed(3)
+    x = pack_latents(torch.randn(B, 16, 16, 16, generator=g, dtype=torch.float64))
+    txt = torch.randn(B, 24, cfg.text_dim, generator=g, dtype=torch.float64)
+    pooled = torch.randn(B, cfg.pooled_dim, generator=g, dtype=torch.float64) if cfg.pooled_dim else None
+    t = torch.full((B,), 0.6, dtype=torch.float64)
+    gd = torch.full((B,), 3.5, dtype=torch.float64)
+    dense = m(x, txt, pooled, t, gd, grid=(1, 8, 8))
+    tp = CollectiveTP(dist.group.WORLD, list(range(world)), torch.device("cpu"))
+    m2 = MMDiT(cfg, shard_mmdit_weights(cfg, m.w, world, rank))
+    m2.tp = tp
+    out = m2(x, txt, pooled, t, gd, grid=(1, 8, 8))
+    return (out - dense).abs().max().item()
+
+
+@pytest.mark.parametrize("world,B,family", [(2, 1, "flux"), (4, 2, "flux"), (2, 2, "qwen")])
+def test_tensor_parallel_matches_dense(world, B, family):
+    errs = run_ranks(_tp_forward, world, B, family, timeout=240)
+    assert max(errs) < 1e-10, errs

@@ -48,6 +48,17 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             errs[name] = ((full - dense).norm() / dense.norm()).item()
             par.close()
+        from difflet_b200.parallel.tp import CollectiveTP, PeerTP, shard_mmdit_weights
+
+        for name, cls in (("peer_tp", PeerTP), ("nccl_tp", CollectiveTP)):
+            tp = cls(dist.group.WORLD, list(range(world)), torch.device("cuda", rank))
+            m2 = FluxTransformer(cfg, shard_mmdit_weights(cfg, m.w, world, rank))
+            m2.tp = tp
+            for _ in range(2):
+                out = m2(x, txt, pooled, t, gd, img_hw=(32, 32)).float()
+            torch.cuda.synchronize()
+            errs[name] = ((out - dense).norm() / dense.norm()).item()
+            tp.close()
         _native.check_device_errors()
         dist.barrier()
         dist.destroy_process_group()
