@@ -248,6 +248,10 @@ void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_
   if (cos_t.has_value() && cos_t->defined()) {
     TORCH_CHECK(cos_t->scalar_type() == at::kFloat && cos_t->is_contiguous(), "cos must be f32 contiguous");
     TORCH_CHECK(sin_t.has_value() && sin_t->scalar_type() == at::kFloat && sin_t->is_contiguous(), "sin must be f32 contiguous");
+    const int64_t half = dh / 2;
+    TORCH_CHECK(cos_t->size(-1) == half || cos_t->size(-1) == H * half,
+                "RoPE table rows must hold dh/2 (shared) or H*dh/2 (per head) values");
+    a.rope_heads = cos_t->size(-1) == half ? 0 : (int)H;
     a.cos_t = cos_t->data_ptr<float>();
     a.sin_t = sin_t->data_ptr<float>();
   }

@@ -99,6 +99,10 @@ typedef struct QkvScatterArgs {
   // sequence length / offset (the local query rows).
   int kv_replicate;
   int q_S_dst, q_seq_off;
+  // 0: one RoPE table row [dh/2] per position shared by all heads; n > 0: each
+  // row holds n heads' tables ([n * dh/2], head h uses slice h) -- rotary
+  // frequencies spread over the whole inner dimension.
+  int rope_heads;
 } QkvScatterArgs;
 int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream);
 

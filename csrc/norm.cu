@@ -183,8 +183,9 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
   const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + (long long)row * a.ld;
   const int H_local = a.heads_per_rank;
   const int dpos = a.seq_off + s;
-  const float* cos_row = a.cos_t ? a.cos_t + (long long)(a.rope_pos_off + s) * (DH / 2) : nullptr;
-  const float* sin_row = a.sin_t ? a.sin_t + (long long)(a.rope_pos_off + s) * (DH / 2) : nullptr;
+  const int rope_row = (a.rope_heads > 0 ? a.rope_heads : 1) * (DH / 2);
+  const float* cos_row = a.cos_t ? a.cos_t + (long long)(a.rope_pos_off + s) * rope_row : nullptr;
+  const float* sin_row = a.sin_t ? a.sin_t + (long long)(a.rope_pos_off + s) * rope_row : nullptr;
   __shared__ float red[2][4];
 
   // Across-heads RMS (mode 2): sum of squares over the whole q (and k) row.
@@ -252,7 +253,10 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
           for (int e = 0; e < E; ++e) x[e] *= __bfloat162float(wn[h * DH + lane * E + e]);
         }
       }
-      if (cos_row) rope_apply<DH>(x, lane, cos_row, sin_row, a.rope_half);
+      if (cos_row) {
+        const int ho = a.rope_heads > 0 ? h * (DH / 2) : 0;
+        rope_apply<DH>(x, lane, cos_row + ho, sin_row + ho, a.rope_half);
+      }
       if (which == 0) {
         store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.q_dst[r]) + q_off_rows, lane, x);
       } else if (a.kv_replicate) {

@@ -221,6 +221,9 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
     if cos is not None:
         c = cos[rope_pos_off:rope_pos_off + S_src].to(ct)
         s_ = sin[rope_pos_off:rope_pos_off + S_src].to(ct)
+        if c.shape[-1] == H * (dh // 2):  # per-head tables [S, H, dh/2] -> broadcast over [B, H, S, dh/2]
+            c = c.view(S_src, H, dh // 2).transpose(0, 1)
+            s_ = s_.view(S_src, H, dh // 2).transpose(0, 1)
         q = None if q is None else _rope_cpu(q, c, s_, rope_half)
         k = None if k is None else _rope_cpu(k, c, s_, rope_half)
     if kv_replicate:

@@ -55,6 +55,24 @@ def wan_fused_parts(cfg) -> dict[str, list[str]]:
     return parts
 
 
+def ltx2_fused_parts(cfg) -> dict[str, list[str]]:
+    parts = {}
+    for i in range(cfg.layers):
+        p, q = f"transformer_blocks.{i}.", f"blk.{i}."
+        for st, mod in (("v", "attn1"), ("a", "audio_attn1")):
+            parts[q + st + "_qkv.w"] = [p + mod + "." + n for n in ("to_q", "to_k", "to_v")]
+            parts[q + st + "_o.w"] = [p + mod + ".to_out.0"]
+        for pre, mod in (("v_c", "attn2"), ("a_c", "audio_attn2"), ("a2v_", "audio_to_video_attn"),
+                         ("v2a_", "video_to_audio_attn")):
+            parts[q + pre + "q.w"] = [p + mod + ".to_q"]
+            parts[q + pre + "kv.w"] = [p + mod + ".to_k", p + mod + ".to_v"]
+            parts[q + pre + "o.w"] = [p + mod + ".to_out.0"]
+        for st, ff in (("v", "ff"), ("a", "audio_ff")):
+            parts[q + st + "_up.w"] = [p + ff + ".net.0.proj"]
+            parts[q + st + "_down.w"] = [p + ff + ".net.2"]
+    return parts
+
+
 def apply_to_weights(w: dict, parts: dict[str, list[str]], spec: QuantSpec) -> dict[str, list[str]]:
     """Replace every fully targeted fused weight of ``w`` by an ``MXWeight`` (in place)."""
     done, partial = [], []
@@ -77,6 +95,8 @@ def apply_quant(model, spec: QuantSpec) -> dict[str, list[str]]:
     cfg = model.cfg
     if hasattr(cfg, "double_blocks"):
         parts = mmdit_fused_parts(cfg)
+    elif "blk.0.v_qkv.w" in model.w:
+        parts = ltx2_fused_parts(cfg)
     elif hasattr(cfg, "layers") and "blk.0.qkv.w" in model.w:
         parts = wan_fused_parts(cfg)
     else:
