@@ -55,8 +55,10 @@ static at::Tensor gemm_epilogue_args(GemmArgs& a, const at::Tensor& A, int64_t M
                                      const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
                                      const c10::optional<at::Tensor>& resid, double alpha, bool out_f32,
                                      const std::vector<int64_t>& out_peer, int64_t rows_per_rank,
-                                     int64_t peer_row_off, int64_t ldd_peer) {
+                                     int64_t peer_row_off, int64_t ldd_peer,
+                                     const c10::optional<at::Tensor>& gate_row_map) {
   at::Tensor D;
+  const int64_t N_out = epi == kEpiSwiGLU ? N / 2 : N;
   if (!out_peer.empty()) {
     TORCH_CHECK(out_peer.size() <= DFL_MAX_PEERS, "at most 8 output peers");
     TORCH_CHECK(rows_per_rank > 0 && ldd_peer > 0, "out_peer needs rows_per_rank and ldd");
@@ -70,10 +72,10 @@ static at::Tensor gemm_epilogue_args(GemmArgs& a, const at::Tensor& A, int64_t M
     if (out.has_value() && out->defined()) {
       D = *out;
       check_rowmajor(D, "out");
-      TORCH_CHECK(D.size(0) == M && D.size(1) == N, "out shape mismatch");
+      TORCH_CHECK(D.size(0) == M && D.size(1) == N_out, "out shape mismatch");
       TORCH_CHECK(D.scalar_type() == (out_f32 ? at::kFloat : at::kBFloat16), "out dtype mismatch");
     } else {
-      D = at::empty({M, N}, A.options().dtype(out_f32 ? at::kFloat : at::kBFloat16));
+      D = at::empty({M, N_out}, A.options().dtype(out_f32 ? at::kFloat : at::kBFloat16));
     }
     a.D = D.data_ptr();
     a.ldd = D.stride(0);
@@ -100,6 +102,11 @@ static at::Tensor gemm_epilogue_args(GemmArgs& a, const at::Tensor& A, int64_t M
     a.resid = resid->data_ptr();
     a.ldr = resid->stride(0);
     a.rows_per_batch = (int)(rows_per_batch > 0 ? rows_per_batch : M);
+    if (gate_row_map.has_value() && gate_row_map->defined()) {
+      TORCH_CHECK(gate_row_map->scalar_type() == at::kInt && gate_row_map->is_contiguous() &&
+                      gate_row_map->numel() == M, "gate_row_map must be int32 [M]");
+      a.gate_row_map = gate_row_map->data_ptr<int>();
+    }
   }
   a.alpha = (float)alpha;
   a.err = err_ptr();
@@ -110,7 +117,8 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at
                 c10::optional<at::Tensor> out, int64_t epi, int64_t act_lo, int64_t act_hi,
                 const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
                 const c10::optional<at::Tensor>& resid, double alpha, bool out_f32,
-                std::vector<int64_t> out_peer, int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer) {
+                std::vector<int64_t> out_peer, int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer,
+                const c10::optional<at::Tensor>& gate_row_map) {
   check_bf16_cuda(A, "A");
   check_bf16_cuda(B, "B");
   check_rowmajor(A, "A");
@@ -120,7 +128,7 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at
   GemmArgs a{};
   at::Tensor D = gemm_epilogue_args(a, A, A.size(0), B.size(0), bias, out, epi, act_lo, act_hi, gate,
                                     rows_per_batch, resid, alpha, out_f32, out_peer, rows_per_rank, peer_row_off,
-                                    ldd_peer);
+                                    ldd_peer, gate_row_map);
   a.A = A.data_ptr();
   a.B = B.data_ptr();
   a.lda = A.stride(0);
@@ -152,7 +160,8 @@ at::Tensor gemm_mx(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor&
                    const c10::optional<at::Tensor>& bias, c10::optional<at::Tensor> out, int64_t epi,
                    int64_t act_lo, int64_t act_hi, const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
                    const c10::optional<at::Tensor>& resid, double alpha, bool out_f32, std::vector<int64_t> out_peer,
-                   int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer) {
+                   int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer,
+                   const c10::optional<at::Tensor>& gate_row_map) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kFloat8_e4m3fn &&
                   B.scalar_type() == at::kFloat8_e4m3fn, "A and B must be CUDA float8_e4m3fn");
   check_rowmajor(A, "A");
@@ -166,8 +175,9 @@ at::Tensor gemm_mx(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor&
               "sfb must be the blocked uint8 scales of B (rows padded to 256)");
   const c10::cuda::CUDAGuard guard(A.device());
   MxGemmArgs m{};
+  TORCH_CHECK(epi != kEpiSwiGLU, "the MXFP8 GEMM has no SwiGLU epilogue");
   at::Tensor D = gemm_epilogue_args(m.g, A, M, N, bias, out, epi, act_lo, act_hi, gate, rows_per_batch, resid,
-                                    alpha, out_f32, out_peer, rows_per_rank, peer_row_off, ldd_peer);
+                                    alpha, out_f32, out_peer, rows_per_rank, peer_row_off, ldd_peer, gate_row_map);
   m.g.A = A.data_ptr();
   m.g.B = B.data_ptr();
   m.g.lda = A.stride(0);
@@ -182,7 +192,7 @@ at::Tensor gemm_mx(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor&
 at::Tensor ln_modulate(const at::Tensor& x, c10::optional<at::Tensor> out,
                        const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b,
                        const c10::optional<at::Tensor>& shift, const c10::optional<at::Tensor>& scale,
-                       int64_t rows_per_batch, double eps, bool rms) {
+                       int64_t rows_per_batch, double eps, bool rms, const c10::optional<at::Tensor>& row_map) {
   check_bf16_cuda(x, "x");
   check_rowmajor(x, "x");
   const c10::cuda::CUDAGuard guard(x.device());
@@ -213,6 +223,11 @@ at::Tensor ln_modulate(const at::Tensor& x, c10::optional<at::Tensor> out,
   a.D = (int)x.size(1);
   a.eps = (float)eps;
   a.rms = rms ? 1 : 0;
+  if (row_map.has_value() && row_map->defined()) {
+    TORCH_CHECK(row_map->scalar_type() == at::kInt && row_map->is_contiguous() && row_map->numel() == x.size(0),
+                "row_map must be int32 [M]");
+    a.row_map = row_map->data_ptr<int>();
+  }
   DFL_CHECK_RC(dfl_ln_modulate(&a, cur_stream()), "ln_modulate");
   return y;
 }
@@ -248,10 +263,11 @@ void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_
   if (cos_t.has_value() && cos_t->defined()) {
     TORCH_CHECK(cos_t->scalar_type() == at::kFloat && cos_t->is_contiguous(), "cos must be f32 contiguous");
     TORCH_CHECK(sin_t.has_value() && sin_t->scalar_type() == at::kFloat && sin_t->is_contiguous(), "sin must be f32 contiguous");
-    const int64_t half = dh / 2;
-    TORCH_CHECK(cos_t->size(-1) == half || cos_t->size(-1) == H * half,
-                "RoPE table rows must hold dh/2 (shared) or H*dh/2 (per head) values");
-    a.rope_heads = cos_t->size(-1) == half ? 0 : (int)H;
+    const int64_t half = dh / 2, width = cos_t->size(-1);
+    TORCH_CHECK(width == H * half || (width <= half && width > 0),
+                "RoPE table rows must hold dh/2 (shared), H*dh/2 (per head) or fewer (partial rotary) values");
+    a.rope_heads = (width == H * half && H > 1) ? (int)H : 0;
+    a.rope_dims = (a.rope_heads == 0 && width < half) ? (int)(2 * width) : 0;
     a.cos_t = cos_t->data_ptr<float>();
     a.sin_t = sin_t->data_ptr<float>();
   }
@@ -550,18 +566,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_f32") = false, py::arg("out_peer") = std::vector<int64_t>{}, py::arg("rows_per_rank") = 0,
-        py::arg("peer_row_off") = 0, py::arg("ldd") = 0);
+        py::arg("peer_row_off") = 0, py::arg("ldd") = 0, py::arg("gate_row_map") = py::none());
   m.def("mx_quantize", &mx_quantize, py::arg("x"), py::arg("blocked") = false);
   m.def("gemm_mx", &gemm_mx, "block-scaled MXFP8 tcgen05 GEMM", py::arg("A"), py::arg("sfa"), py::arg("B"),
         py::arg("sfb"), py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_f32") = false, py::arg("out_peer") = std::vector<int64_t>{}, py::arg("rows_per_rank") = 0,
-        py::arg("peer_row_off") = 0, py::arg("ldd") = 0);
+        py::arg("peer_row_off") = 0, py::arg("ldd") = 0, py::arg("gate_row_map") = py::none());
   m.def("ln_modulate", &ln_modulate, py::arg("x"), py::arg("out") = py::none(),
         py::arg("w") = py::none(), py::arg("b") = py::none(), py::arg("shift") = py::none(),
         py::arg("scale") = py::none(), py::arg("rows_per_batch") = 0, py::arg("eps") = 1e-6,
-        py::arg("rms") = false);
+        py::arg("rms") = false, py::arg("row_map") = py::none());
   m.def("qkv_scatter", &qkv_scatter);
   m.def("gemv", &gemv, py::arg("W"), py::arg("x"), py::arg("bias") = py::none(),
         py::arg("out") = py::none(), py::arg("silu_in") = false, py::arg("silu_out") = false);

@@ -178,14 +178,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mb * BM + sub * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
+      if constexpr (EPI == kEpiSwiGLU) {
+        // chunk pairs (h, g) of interleaved 32-column groups -> 32 output columns
+        EpiParams p2 = ep;
+        p2.bias = nullptr;
+        p2.alpha = 1.f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int col0 = nb * BN + c * 32;
-        if (col0 >= N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c * 32, r);
-        tmem_wait_ld();
-        epilogue_chunk<EPI, OUT_F32>(r, row, col0, M, N, ep);
+        for (int c = 0; c < BN / 32; c += 2) {
+          const int col0 = nb * BN + c * 32;
+          if (col0 >= N) break;  // warp-uniform
+          uint32_t rh[32], rg[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, rh);
+          tmem_ld_32x32b_x32(tbase + (c + 1) * 32, rg);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float h = __uint_as_float(rh[j]) * ep.alpha, g = __uint_as_float(rg[j]) * ep.alpha;
+            if (ep.bias) {
+              h += __bfloat162float(ep.bias[col0 + j]);
+              g += __bfloat162float(ep.bias[col0 + 32 + j]);
+            }
+            rh[j] = __float_as_uint(h * silu(g));
+          }
+          epilogue_chunk<kEpiNone, OUT_F32>(rh, row, col0 / 2, M, N / 2, p2);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col0 = nb * BN + c * 32;
+          if (col0 >= N) break;  // warp-uniform
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_wait_ld();
+          epilogue_chunk<EPI, OUT_F32>(r, row, col0, M, N, ep);
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -230,6 +256,8 @@ int dispatch_epi(int epi, bool out_f32, const CUtensorMap& ta, const CUtensorMap
       return launch_variant<BN, STAGES, kEpiSilu, false>(ta, tb, M, N, K, ep, err, s, dev);
     case kEpiGateResid:
       return launch_variant<BN, STAGES, kEpiGateResid, false>(ta, tb, M, N, K, ep, err, s, dev);
+    case kEpiSwiGLU:
+      return launch_variant<BN, STAGES, kEpiSwiGLU, false>(ta, tb, M, N, K, ep, err, s, dev);
     default:
       return -1;
   }
@@ -270,6 +298,8 @@ extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
   ep.gate = a->gate;
   ep.gate_bstride = a->gate_bstride;
   ep.rows_per_batch = a->rows_per_batch > 0 ? a->rows_per_batch : a->M;
+  ep.gate_row_map = a->gate_row_map;
+  if (a->epi == kEpiSwiGLU && (a->N % 64 || a->out_world > 0)) return -11;
   ep.resid = reinterpret_cast<const __nv_bfloat16*>(a->resid);
   ep.ldr = a->ldr;
   ep.alpha = a->alpha;

@@ -18,6 +18,7 @@ struct EpiParams {
   const float* gate;
   long long gate_bstride;
   int rows_per_batch;
+  const int* gate_row_map;
   const __nv_bfloat16* resid;
   long long ldr;
   float alpha;
@@ -77,7 +78,7 @@ DFL_DEVICE void epilogue_chunk(const uint32_t (&r)[32], int row, int col0, int M
     }
   }
   if constexpr (EPI == kEpiGateResid) {
-    int b = row / p.rows_per_batch;
+    int b = p.gate_row_map ? p.gate_row_map[row] : row / p.rows_per_batch;
     const float* g = p.gate + (long long)b * p.gate_bstride;
     const __nv_bfloat16* rs = p.resid + (long long)row * p.ldr;
     if (full) {

@@ -10,7 +10,9 @@
 extern "C" {
 #endif
 
-enum { kEpiNone = 0, kEpiGelu = 1, kEpiGateResid = 2, kEpiSilu = 3 };
+enum { kEpiNone = 0, kEpiGelu = 1, kEpiGateResid = 2, kEpiSilu = 3, kEpiSwiGLU = 4 };
+// kEpiSwiGLU: the weight rows are interleaved in 32-row groups [h_32 | g_32] and the
+// GEMM writes N/2 columns  out = (h + b_h) * silu(g + b_g).
 
 #define DFL_MAX_PEERS 8
 
@@ -27,6 +29,7 @@ typedef struct GemmArgs {
   const float* gate;   // f32 [batch, gate_bstride] for kEpiGateResid
   long long gate_bstride;
   int rows_per_batch;
+  const int* gate_row_map;  // optional: gate row of every output row (packed sequences)
   const void* resid;   // bf16 [M, ldr] (may alias D)
   long long ldr;
   float alpha;         // scales the accumulator before bias
@@ -73,6 +76,7 @@ typedef struct LnModArgs {
   int M, D;
   float eps;
   int rms;                           // 1: RMSNorm (no mean subtraction, no bias)
+  const int* row_map;                // optional: modulation row of every row (packed sequences)
 } LnModArgs;
 int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream);
 
@@ -103,6 +107,9 @@ typedef struct QkvScatterArgs {
   // row holds n heads' tables ([n * dh/2], head h uses slice h) -- rotary
   // frequencies spread over the whole inner dimension.
   int rope_heads;
+  // Rotary applied to the first rope_dims channels of each head (half-split pairs
+  // (i, i + rope_dims/2)), the rest passed through; 0 = all dh channels.
+  int rope_dims;
 } QkvScatterArgs;
 int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream);
 

@@ -377,6 +377,7 @@ extern "C" int dfl_gemm_mx(const MxGemmArgs* a, cudaStream_t stream) {
   ep.gate = g.gate;
   ep.gate_bstride = g.gate_bstride;
   ep.rows_per_batch = g.rows_per_batch > 0 ? g.rows_per_batch : g.M;
+  ep.gate_row_map = g.gate_row_map;
   ep.resid = reinterpret_cast<const __nv_bfloat16*>(g.resid);
   ep.ldr = g.ldr;
   ep.alpha = g.alpha;

@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(LnModArgs a) {
     }
   }
   const float rstd = rsqrtf(warp_sum(sq) / (float)a.D + a.eps);
-  const int b = row / a.rows_per_batch;
+  const int b = a.row_map ? a.row_map[row] : row / a.rows_per_batch;
   const float* sh = a.shift ? a.shift + (long long)b * a.mod_bstride : nullptr;
   const float* sc = a.scale ? a.scale + (long long)b * a.mod_bstride : nullptr;
   const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(a.w);
@@ -147,8 +147,25 @@ __device__ __forceinline__ void store_head(__nv_bfloat16* dst, int lane, const f
 
 template <int DH>
 __device__ __forceinline__ void rope_apply(float (&x)[DH / 32], int lane, const float* cos_row,
-                                           const float* sin_row, int half) {
+                                           const float* sin_row, int half, int rope_dims) {
   constexpr int E = DH / 32;
+  if (half && rope_dims > 0 && rope_dims < DH) {
+    // partial half-split rotary: channel i < R pairs with i +- R/2 (R/2 a multiple of E,
+    // so the partner sits at the same slot e of lane +- R/(2E)); channels >= R pass
+    const int R2 = rope_dims / 2;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int i = lane * E + e;
+      const int j = i < R2 ? i + R2 : (i < rope_dims ? i - R2 : i);
+      const float other = __shfl_sync(0xffffffffu, x[e], j / E);
+      if (i < rope_dims) {
+        const int fi = i < R2 ? i : i - R2;
+        const float c = cos_row[fi], s = sin_row[fi];
+        x[e] = (i < R2) ? (x[e] * c - other * s) : (x[e] * c + other * s);
+      }
+    }
+    return;
+  }
   if (!half) {
     // interleaved pairs (2i, 2i+1) live in one lane
 #pragma unroll
@@ -183,7 +200,7 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
   const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + (long long)row * a.ld;
   const int H_local = a.heads_per_rank;
   const int dpos = a.seq_off + s;
-  const int rope_row = (a.rope_heads > 0 ? a.rope_heads : 1) * (DH / 2);
+  const int rope_row = (a.rope_heads > 0 ? a.rope_heads : 1) * ((a.rope_dims > 0 ? a.rope_dims : DH) / 2);
   const float* cos_row = a.cos_t ? a.cos_t + (long long)(a.rope_pos_off + s) * rope_row : nullptr;
   const float* sin_row = a.sin_t ? a.sin_t + (long long)(a.rope_pos_off + s) * rope_row : nullptr;
   __shared__ float red[2][4];
@@ -255,7 +272,7 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
       }
       if (cos_row) {
         const int ho = a.rope_heads > 0 ? h * (DH / 2) : 0;
-        rope_apply<DH>(x, lane, cos_row + ho, sin_row + ho, a.rope_half);
+        rope_apply<DH>(x, lane, cos_row + ho, sin_row + ho, a.rope_half, a.rope_dims);
       }
       if (which == 0) {
         store_head<DH>(reinterpret_cast<__nv_bfloat16*>(a.q_dst[r]) + q_off_rows, lane, x);
@@ -400,6 +417,8 @@ extern "C" int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream) {
   if (a->kv_replicate ? (a->heads_per_rank != a->H || a->out_token_major) : a->heads_per_rank * a->world != a->H)
     return -3;
   if (a->ld % 8) return -4;
+  if (a->rope_dims && (a->rope_dims > a->dh || (a->rope_dims / 2) % (a->dh / 32) || !a->rope_half || a->rope_heads))
+    return -6;
   if (a->dh == 128)
     qkv_scatter_kernel<128><<<a->rows, 128, 0, stream>>>(*a);
   else if (a->dh == 64)

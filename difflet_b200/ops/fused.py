@@ -27,8 +27,19 @@ import torch.nn.functional as F
 
 from difflet_b200 import envs
 
-EPI_NONE, EPI_GELU, EPI_GATE_RESID, EPI_SILU = 0, 1, 2, 3
-_ACT = {None: EPI_NONE, "none": EPI_NONE, "gelu": EPI_GELU, "gelu_tanh": EPI_GELU, "silu": EPI_SILU}
+EPI_NONE, EPI_GELU, EPI_GATE_RESID, EPI_SILU, EPI_SWIGLU = 0, 1, 2, 3, 4
+_ACT = {None: EPI_NONE, "none": EPI_NONE, "gelu": EPI_GELU, "gelu_tanh": EPI_GELU, "silu": EPI_SILU,
+        "swiglu": EPI_SWIGLU}
+
+
+def swiglu_interleave(w_h: torch.Tensor, w_g: torch.Tensor) -> torch.Tensor:
+    """Rows of the value half ``w_h`` and the gate half ``w_g`` ([F, ...] each) interleaved in
+    32-row groups [h_32 | g_32 | h_32 | ...]: the layout the SwiGLU GEMM epilogue reads."""
+    F_ = w_h.shape[0]
+    if F_ % 32:
+        raise ValueError("SwiGLU width must be a multiple of 32")
+    rest = w_h.shape[1:]
+    return torch.stack([w_h.reshape(F_ // 32, 32, *rest), w_g.reshape(F_ // 32, 32, *rest)], 1).reshape(2 * F_, *rest)
 
 _nat = None
 # Host-side count of native kernel launches (each fused-op call is one launch).
@@ -88,7 +99,7 @@ class MXWeight:
 
 # ---------------------------------------------------------------------------
 def linear(x, w, b=None, *, out=None, act=None, act_lo=0, act_hi=None, gate=None, resid=None,
-           rows_per_batch=0, alpha=1.0, out_f32=False):
+           rows_per_batch=0, alpha=1.0, out_f32=False, gate_row_map=None):
     """``act(alpha * x @ w.T + b)`` or ``resid + gate * (...)``.
 
     x: [M, K]; w: [N, K] (or an ``MXWeight``); b: [N]; gate: f32 [B, N] (rows_per_batch
@@ -105,7 +116,8 @@ def linear(x, w, b=None, *, out=None, act=None, act_lo=0, act_hi=None, gate=None
     act_hi = N if act_hi is None else act_hi
     if x2.is_cuda and envs.DIFFLET_KERNEL_GEMM != "cublas":
         epi = EPI_GATE_RESID if gate is not None else _ACT[act]
-        return native().gemm(x2, w, b, out, epi, act_lo, act_hi, gate, rows_per_batch, resid, alpha, out_f32)
+        return native().gemm(x2, w, b, out, epi, act_lo, act_hi, gate, rows_per_batch, resid, alpha, out_f32,
+                             gate_row_map=gate_row_map)
     # reference path: the CPU oracle (any dtype), or the cuBLAS A/B baseline on CUDA
     if x2.is_cuda:
         y = torch.matmul(x2, w.t()).float()
@@ -118,10 +130,16 @@ def linear(x, w, b=None, *, out=None, act=None, act_lo=0, act_hi=None, gate=None
         y[:, act_lo:act_hi] = F.gelu(y[:, act_lo:act_hi], approximate="tanh")
     elif act == "silu":
         y[:, act_lo:act_hi] = F.silu(y[:, act_lo:act_hi])
+    elif act == "swiglu":
+        yy = y.view(y.shape[0], N // 64, 2, 32)
+        y = (yy[:, :, 0] * F.silu(yy[:, :, 1])).reshape(y.shape[0], N // 2)
     if gate is not None:
         M = y.shape[0]
-        rpb = rows_per_batch if rows_per_batch > 0 else M
-        g = gate[:, :N].to(y.dtype).repeat_interleave(rpb, 0)[:M]
+        if gate_row_map is not None:
+            g = gate[:, :N].to(y.dtype)[gate_row_map.long().to(gate.device)]
+        else:
+            rpb = rows_per_batch if rows_per_batch > 0 else M
+            g = gate[:, :N].to(y.dtype).repeat_interleave(rpb, 0)[:M]
         y = resid.to(y.dtype) + g * y
     dt = torch.float32 if out_f32 else (x2.dtype if not x2.is_cuda else torch.bfloat16)
     if out is not None:
@@ -131,10 +149,11 @@ def linear(x, w, b=None, *, out=None, act=None, act_lo=0, act_hi=None, gate=None
 
 
 def ln_modulate(x, *, shift=None, scale=None, w=None, b=None, eps=1e-6, rms=False, rows_per_batch=0,
-                out=None):
+                out=None, row_map=None):
+    """``row_map`` (int32 [M]): the shift / scale row of every row (packed sequences)."""
     x2 = _rows2d(x)
     if x2.is_cuda:
-        return native().ln_modulate(x2, out, w, b, shift, scale, rows_per_batch, eps, rms)
+        return native().ln_modulate(x2, out, w, b, shift, scale, rows_per_batch, eps, rms, row_map)
     xf = x2.to(torch.float64 if x2.dtype == torch.float64 else torch.float32)
     if rms:
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
@@ -146,10 +165,15 @@ def ln_modulate(x, *, shift=None, scale=None, w=None, b=None, eps=1e-6, rms=Fals
         y = y + b.to(y.dtype)
     M = y.shape[0]
     rpb = rows_per_batch if rows_per_batch > 0 else M
+
+    def rows(t):
+        t = t.to(y.dtype)
+        return t[row_map.long().to(t.device)] if row_map is not None else t.repeat_interleave(rpb, 0)[:M]
+
     if scale is not None:
-        y = y * (1 + scale.to(y.dtype).repeat_interleave(rpb, 0)[:M])
+        y = y * (1 + rows(scale))
     if shift is not None:
-        y = y + shift.to(y.dtype).repeat_interleave(rpb, 0)[:M]
+        y = y + rows(shift)
     y = y.to(x2.dtype)
     if out is not None:
         out.copy_(y)
@@ -221,11 +245,17 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
     if cos is not None:
         c = cos[rope_pos_off:rope_pos_off + S_src].to(ct)
         s_ = sin[rope_pos_off:rope_pos_off + S_src].to(ct)
-        if c.shape[-1] == H * (dh // 2):  # per-head tables [S, H, dh/2] -> broadcast over [B, H, S, dh/2]
+        if c.shape[-1] == H * (dh // 2) and H > 1:  # per-head tables [S, H, dh/2] -> over [B, H, S, dh/2]
             c = c.view(S_src, H, dh // 2).transpose(0, 1)
             s_ = s_.view(S_src, H, dh // 2).transpose(0, 1)
-        q = None if q is None else _rope_cpu(q, c, s_, rope_half)
-        k = None if k is None else _rope_cpu(k, c, s_, rope_half)
+        R = 2 * c.shape[-1]
+        if R < dh:  # partial rotary: the first R channels rotate, the rest pass through
+            rot = lambda t: None if t is None else torch.cat([_rope_cpu(t[..., :R], c, s_, rope_half),  # noqa: E731
+                                                              t[..., R:]], -1)
+            q, k = rot(q), rot(k)
+        else:
+            q = None if q is None else _rope_cpu(q, c, s_, rope_half)
+            k = None if k is None else _rope_cpu(k, c, s_, rope_half)
     if kv_replicate:
         if q is not None:
             q_dst[0][:, :, q_seq_off:q_seq_off + S_src] = q.to(q_dst[0].dtype)
