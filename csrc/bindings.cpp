@@ -192,13 +192,18 @@ at::Tensor gemm_mx(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor&
 at::Tensor ln_modulate(const at::Tensor& x, c10::optional<at::Tensor> out,
                        const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b,
                        const c10::optional<at::Tensor>& shift, const c10::optional<at::Tensor>& scale,
-                       int64_t rows_per_batch, double eps, bool rms, const c10::optional<at::Tensor>& row_map) {
+                       int64_t rows_per_batch, double eps, bool rms, const c10::optional<at::Tensor>& row_map,
+                       std::vector<int64_t> y_peer, int64_t row0, int64_t rows) {
   check_bf16_cuda(x, "x");
   check_rowmajor(x, "x");
   const c10::cuda::CUDAGuard guard(x.device());
   at::Tensor y = (out.has_value() && out->defined()) ? *out : at::empty_like(x);
   check_rowmajor(y, "out");
   LnModArgs a{};
+  TORCH_CHECK(y_peer.size() <= DFL_MAX_PEERS, "at most 8 output peers");
+  a.y_world = (int)y_peer.size();
+  for (size_t d = 0; d < y_peer.size(); ++d) a.y_peer[d] = reinterpret_cast<void*>(y_peer[d]);
+  a.row0 = row0;
   a.x = x.data_ptr();
   a.ldx = x.stride(0);
   a.y = y.data_ptr();
@@ -219,7 +224,8 @@ at::Tensor ln_modulate(const at::Tensor& x, c10::optional<at::Tensor> out,
   }
   a.mod_bstride = bstride;
   a.rows_per_batch = (int)(rows_per_batch > 0 ? rows_per_batch : x.size(0));
-  a.M = (int)x.size(0);
+  a.M = (int)(rows >= 0 ? rows : x.size(0));
+  TORCH_CHECK(row0 >= 0 && row0 + a.M <= x.size(0), "row range out of bounds");
   a.D = (int)x.size(1);
   a.eps = (float)eps;
   a.rms = rms ? 1 : 0;
@@ -460,7 +466,8 @@ void ipc_close(int64_t ptr) { dfl_ipc_close(reinterpret_cast<void*>(ptr)); }
 
 void tp_reduce(const at::Tensor& slots, int64_t slot_rows, int64_t world, int64_t rows, int64_t N, int64_t row0,
                const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
-               const c10::optional<at::Tensor>& resid, std::vector<int64_t> out, int64_t ldo, int64_t out_row0) {
+               const c10::optional<at::Tensor>& resid, std::vector<int64_t> out, int64_t ldo, int64_t out_row0,
+               int64_t resid_row0) {
   TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kBFloat16, "slots must be CUDA bf16");
   TORCH_CHECK(slots.numel() >= world * slot_rows * N, "slots too small");
   TORCH_CHECK(!out.empty() && out.size() <= DFL_MAX_PEERS, "1..8 output pointers");
@@ -486,6 +493,7 @@ void tp_reduce(const at::Tensor& slots, int64_t slot_rows, int64_t world, int64_
     a.rows_per_batch = (int)rows_per_batch;
     a.resid = resid->data_ptr();
     a.ldr = resid->stride(0);
+    a.resid_row0 = resid_row0;
   }
   a.out_world = (int)out.size();
   for (size_t d = 0; d < out.size(); ++d) a.out[d] = reinterpret_cast<void*>(out[d]);
@@ -577,7 +585,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ln_modulate", &ln_modulate, py::arg("x"), py::arg("out") = py::none(),
         py::arg("w") = py::none(), py::arg("b") = py::none(), py::arg("shift") = py::none(),
         py::arg("scale") = py::none(), py::arg("rows_per_batch") = 0, py::arg("eps") = 1e-6,
-        py::arg("rms") = false, py::arg("row_map") = py::none());
+        py::arg("rms") = false, py::arg("row_map") = py::none(), py::arg("y_peer") = std::vector<int64_t>{},
+        py::arg("row0") = 0, py::arg("rows") = -1);
   m.def("qkv_scatter", &qkv_scatter);
   m.def("gemv", &gemv, py::arg("W"), py::arg("x"), py::arg("bias") = py::none(),
         py::arg("out") = py::none(), py::arg("silu_in") = false, py::arg("silu_out") = false);
@@ -600,7 +609,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce", &tp_reduce, py::arg("slots"), py::arg("slot_rows"), py::arg("world"), py::arg("rows"),
         py::arg("N"), py::arg("row0"), py::arg("bias") = py::none(), py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("out") = std::vector<int64_t>{},
-        py::arg("ldo") = 0, py::arg("out_row0") = 0);
+        py::arg("ldo") = 0, py::arg("out_row0") = 0, py::arg("resid_row0") = 0);
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_put_f32", &peer_put_f32);
   m.def("cfg_combine", &cfg_combine);

@@ -131,7 +131,8 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(TpReduceArgs a) {
     const long long grow = a.row0 + r;
     if (a.gate) {
       const float* g = a.gate + (grow / a.rows_per_batch) * a.gate_bstride + c;
-      const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.resid) + grow * a.ldr + c);
+      const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.resid) +
+                                                      (grow - a.resid_row0) * a.ldr + c);
       const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int h = 0; h < 4; ++h) {

@@ -77,6 +77,11 @@ typedef struct LnModArgs {
   float eps;
   int rms;                           // 1: RMSNorm (no mean subtraction, no bias)
   const int* row_map;                // optional: modulation row of every row (packed sequences)
+  // Sequence-parallel all-gather fused into the norm: process rows [row0, row0 + M) only
+  // and store each output row into y_peer[0..y_world) (every rank's full buffer) instead of y.
+  long long row0;
+  void* y_peer[DFL_MAX_PEERS];
+  int y_world;
 } LnModArgs;
 int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream);
 
@@ -210,6 +215,7 @@ typedef struct TpReduceArgs {
   const void* resid; long long ldr;     // bf16, indexed by global row
   void* out[DFL_MAX_PEERS]; long long ldo; int out_world;
   long long out_row0;                   // row of out that receives global row row0
+  long long resid_row0;                 // global row held by resid's row 0
 } TpReduceArgs;
 int dfl_tp_reduce(const TpReduceArgs* a, cudaStream_t stream);
 

@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(LnModArgs a) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (warp >= a.M) return;
-  const int row = warp;
+  const int row = (int)(a.row0 + warp);
   const int nvec = a.D / 8;  // 16-byte vectors per row
   const uint4* x4 = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) +
                                                    (long long)row * a.ldx);
@@ -109,7 +109,12 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(LnModArgs a) {
       out.y = pack_bf16x2(o[2], o[3]);
       out.z = pack_bf16x2(o[4], o[5]);
       out.w = pack_bf16x2(o[6], o[7]);
-      y4[vi] = out;
+      if (a.y_world > 0) {  // sequence-parallel all-gather: this row into every rank's buffer
+        for (int d = 0; d < a.y_world; ++d)
+          reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y_peer[d]) + (long long)row * a.ldy)[vi] = out;
+      } else {
+        y4[vi] = out;
+      }
     }
   }
 }
@@ -395,6 +400,7 @@ extern "C" int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream) {
   if ((a->ldx % 8) || (a->ldy % 8)) return -3;
   if ((a->shift || a->scale) && (a->mod_bstride % 4)) return -4;
   if (a->M == 0) return 0;
+  if (a->y_world < 0 || a->y_world > DFL_MAX_PEERS) return -5;
   LnModArgs c = *a;
   if (c.rows_per_batch <= 0) c.rows_per_batch = c.M;
   int threads = 256;

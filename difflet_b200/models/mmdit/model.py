@@ -174,7 +174,8 @@ class MMDiT:
             xe = (lambda *shape: tp.empty(shape, dt)) if tp is not None else e  # noqa: E731
             ws["x_txt"] = xe(B * S_txt, D)
             ws["x_img"] = xe(B * S_img, D)
-        ws["norm"] = e(B * S_loc, D)
+        sp = tp is not None and tp.sp
+        ws["norm"] = tp.empty((B * S_loc, D), dt) if sp else e(B * S_loc, D)  # all-gathered under SP
         ws["qkv_img"] = e(B * S_img, 3 * Dl)
         ws["qkv_txt"] = e(B * S_txt, 3 * Dl)
         ws["mlp"] = e(B * max(S_img, S_txt), Fl)
@@ -312,6 +313,16 @@ class MMDiT:
         Hl = par.heads_local(H) if par is not None else Ht
         S_loc = S_txt + S_img
 
+        sp = tp is not None and tp.sp
+        if sp and B != 1:
+            raise NotImplementedError("sequence parallelism runs batch 1 here (use cfg-parallel for CFG)")
+
+        def ln(xin, out, **kw):
+            """Norm + modulation; under SP this rank's rows, all-gathered into every rank's ``out``."""
+            if sp:
+                return tp.ln_gather(xin, out, **kw)
+            return F.ln_modulate(xin, out=out, **kw)
+
         def row_linear(xin, wt, bias, out, gate, rpb):
             """Row-parallel (under TP) output projection fused with out += gate * (.)"""
             if tp is not None:
@@ -353,7 +364,7 @@ class MMDiT:
                 xs, nr, pos = xs_of[st], n_of[st], pos_of[st]
                 o = cfg.double_mod_offset(i, st)
                 nb = norm[: B * nr]
-                F.ln_modulate(xs, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=nr, out=nb)
+                ln(xs, nb, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=nr)
                 F.linear(nb, w[p + st + "_qkv.w"], w[p + st + "_qkv.b"], out=ws["qkv_" + st])
                 F.qkv_scatter(ws["qkv_" + st], q_off=0, k_off=Dl, v_off=2 * Dl, S_src=nr, H=Ht, dh=dh,
                               **dst(q, k, v, row_of[st], pos), norm_mode=1, wq=w[p + st + "_qnorm"],
@@ -366,11 +377,14 @@ class MMDiT:
                 self._rows_gemm(ws["attn"], rows, B, nr, w[p + st + "_out.w"], w[p + st + "_out.b"], xs,
                                 mslice(o + 2 * D), row_linear)
                 nb = norm[: B * nr]
-                F.ln_modulate(xs, shift=mslice(o + 3 * D), scale=mslice(o + 4 * D), eps=eps, rows_per_batch=nr, out=nb)
+                ln(xs, nb, shift=mslice(o + 3 * D), scale=mslice(o + 4 * D), eps=eps, rows_per_batch=nr)
                 mb = ws["mlp"][: B * nr]
                 F.linear(nb, w[p + st + "_up.w"], w[p + st + "_up.b"], out=mb, act="gelu")
                 row_linear(mb, w[p + st + "_down.w"], w[p + st + "_down.b"], xs, mslice(o + 5 * D), nr)
 
+        if sp:  # dual -> single: the rows each rank owns change; replicate the residual stream once
+            for st in ("txt", "img"):
+                tp.sync_rows(xs_of[st])
         if B > 1:  # dual -> single: the residual stream becomes [seg0 ; seg1] per batch
             for st in ("txt", "img"):
                 r0 = row_of[st]
@@ -381,7 +395,7 @@ class MMDiT:
         for j in range(cfg.single_blocks):
             p = f"single.{j}."
             o = cfg.single_mod_offset(j)
-            F.ln_modulate(x2, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=S_loc, out=norm)
+            ln(x2, norm, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=S_loc)
             F.linear(norm, w[p + "fused.w"], w[p + "fused.b"], out=fused, act="gelu", act_lo=Dl, act_hi=Dl + Fl)
             if par is None:  # positions equal local rows: one pass over every row
                 F.qkv_scatter(fused, q_off=0, k_off=Dl + Fl, v_off=2 * Dl + Fl, S_src=S_loc, H=Ht, dh=dh,
@@ -400,6 +414,8 @@ class MMDiT:
             self._attention(ws, B, S_txt, S_img, D, Hl, dh, out_rows=fused, kv_lo=kv_lo, kv_hi=kv_hi)
             row_linear(fused[:, : Dl + Fl], w[p + "proj.w"], w[p + "proj.b"], x2, mslice(o + 2 * D), S_loc)
 
+        if sp:  # the final layer reads every image row
+            tp.sync_rows(x2)
         # final adaLN-continuous (scale, shift) on the image rows + projection
         o = cfg.final_mod_offset()
         out = torch.empty(B * S_img, cfg.out_channels, device=x_tokens.device, dtype=x_tokens.dtype)

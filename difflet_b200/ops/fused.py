@@ -149,11 +149,14 @@ def linear(x, w, b=None, *, out=None, act=None, act_lo=0, act_hi=None, gate=None
 
 
 def ln_modulate(x, *, shift=None, scale=None, w=None, b=None, eps=1e-6, rms=False, rows_per_batch=0,
-                out=None, row_map=None):
-    """``row_map`` (int32 [M]): the shift / scale row of every row (packed sequences)."""
+                out=None, row_map=None, y_peer=None, row0=0, rows=None):
+    """``row_map`` (int32 [M]): the shift / scale row of every row (packed sequences).
+    ``y_peer`` (device pointers of every rank's ``out``), ``row0`` / ``rows``: normalise only
+    rows [row0, row0 + rows) and store them into every rank's buffer (sequence parallelism)."""
     x2 = _rows2d(x)
     if x2.is_cuda:
-        return native().ln_modulate(x2, out, w, b, shift, scale, rows_per_batch, eps, rms, row_map)
+        return native().ln_modulate(x2, out, w, b, shift, scale, rows_per_batch, eps, rms, row_map,
+                                    list(y_peer or []), int(row0), -1 if rows is None else int(rows))
     xf = x2.to(torch.float64 if x2.dtype == torch.float64 else torch.float32)
     if rms:
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)

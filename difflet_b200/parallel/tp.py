@@ -75,9 +75,15 @@ def shard_mmdit_weights(cfg, w: dict, tp: int, rank: int) -> dict:
 
 class _TPBase(_Base):
     kind = "tp"
+    sp = False  # Megatron sequence parallelism: residual rows sharded, AG in the norm, RS in the reducer
 
     def heads_local(self, H):
         return H // self.world
+
+    def row_range(self, M: int):
+        rpr = -(-M // self.world)
+        r0 = self.rank * rpr
+        return r0, max(0, min(rpr, M - r0))
 
 
 class PeerTP(_TPBase, PeerBase):
@@ -110,9 +116,30 @@ class PeerTP(_TPBase, PeerBase):
             nat.gemm(x, w, None, None, 0, out_peer=peers, rows_per_rank=rpr, peer_row_off=r * rpr, ldd=N)
         self.heap.barrier()  # every partial of this rank's rows has landed
         rows = max(0, min(rpr, M - r * rpr))
+        # all-reduce: the finished rows go to every rank; sequence parallel: only to this rank (reduce-scatter)
+        dst = [out.data_ptr()] if self.sp else self.heap.peer_ptrs(out)
         nat.tp_reduce(slots, rpr, W, rows, N, r * rpr, b, gate, rows_per_batch if gate is not None else 0,
-                      resid if gate is not None else None, self.heap.peer_ptrs(out), out.stride(0), r * rpr)
-        self.heap.barrier()  # every finished row is in every rank's residual stream
+                      resid if gate is not None else None, dst, out.stride(0), r * rpr)
+        self.heap.barrier()  # the slots are free again (and, all-reduce, every row is everywhere)
+
+    def ln_gather(self, x, out, **kw):
+        """Sequence-parallel norm: this rank normalises its own rows of ``x`` and stores them
+        into every rank's ``out`` (the all-gather is the kernel's store pattern)."""
+        r0, n = self.row_range(x.shape[0])
+        F.ln_modulate(x, out=out, y_peer=self.heap.peer_ptrs(out), row0=r0, rows=n, **kw)
+        self.heap.barrier()
+        return out
+
+    def sync_rows(self, x):
+        """Copy this rank's own rows of ``x`` (a symmetric buffer) into every rank's copy."""
+        r0, n = self.row_range(x.shape[0])
+        if n:
+            src = x[r0:r0 + n]
+            nb = n * x.stride(0) * x.element_size()
+            for r, p in enumerate(self.heap.peer_ptrs(src)):
+                if r != self.rank:
+                    F.native().memcpy_async(p, src.data_ptr(), nb)
+        self.heap.barrier()
 
 
 class CollectiveTP(_TPBase):
@@ -123,6 +150,26 @@ class CollectiveTP(_TPBase):
 
     def peer_views(self, t):
         return [t]
+
+    def ln_gather(self, x, out, **kw):
+        r0, n = self.row_range(x.shape[0])
+        y = F.ln_modulate(x, **kw)
+        parts = [torch.empty_like(y) for _ in range(self.world)]
+        dist.all_gather(parts, y.contiguous(), group=self.group)
+        for r in range(self.world):  # rank r's rows come from its copy (the rows it owns)
+            rr0 = r * -(-x.shape[0] // self.world)
+            rn = max(0, min(-(-x.shape[0] // self.world), x.shape[0] - rr0))
+            out[rr0:rr0 + rn] = parts[r][rr0:rr0 + rn]
+        return out
+
+    def sync_rows(self, x):
+        r0, n = self.row_range(x.shape[0])
+        parts = [torch.empty_like(x) for _ in range(self.world)]
+        dist.all_gather(parts, x.contiguous(), group=self.group)
+        M = x.shape[0]
+        rpr = -(-M // self.world)
+        for r in range(self.world):
+            x[r * rpr:min(M, (r + 1) * rpr)] = parts[r][r * rpr:min(M, (r + 1) * rpr)]
 
     def row_linear(self, x, w, b=None, *, out, gate=None, resid=None, rows_per_batch=0):
         if isinstance(w, F.MXWeight):
@@ -141,6 +188,13 @@ class CollectiveTP(_TPBase):
 
 
 def make_tensor_parallel(parallel, device, transport: str | None = None):
+    ctx = _make_tp(parallel, device, transport)
+    if ctx is not None:
+        ctx.sp = bool(getattr(parallel, "sp_enabled", False))
+    return ctx
+
+
+def _make_tp(parallel, device, transport):
     """TP context over the tp axis (None when tp_degree == 1)."""
     from difflet_b200 import envs
     from difflet_b200.parallel import groups

@@ -85,7 +85,7 @@ def test_block_windows():
     assert w.tolist() == [[4 + 3, 4 + 3, 4, 4], [4 + 1, 4 + 3, 4, 1]]
 
 
-def _tp_forward(rank, world, B, family):
+def _tp_forward(rank, world, B, family, sp=False):
     import torch.distributed as dist
 
     from difflet_b200.models.mmdit import MMDiT, get_config, pack_latents
@@ -103,12 +103,14 @@ def _tp_forward(rank, world, B, family):
     dense = m(x, txt, pooled, t, gd, grid=(1, 8, 8))
     tp = CollectiveTP(dist.group.WORLD, list(range(world)), torch.device("cpu"))
     m2 = MMDiT(cfg, shard_mmdit_weights(cfg, m.w, world, rank))
+    tp.sp = sp
     m2.tp = tp
     out = m2(x, txt, pooled, t, gd, grid=(1, 8, 8))
     return (out - dense).abs().max().item()
 
 
-@pytest.mark.parametrize("world,B,family", [(2, 1, "flux"), (4, 2, "flux"), (2, 2, "qwen")])
-def test_tensor_parallel_matches_dense(world, B, family):
-    errs = run_ranks(_tp_forward, world, B, family, timeout=240)
+@pytest.mark.parametrize("world,B,family,sp", [(2, 1, "flux", False), (4, 2, "flux", False), (2, 2, "qwen", False),
+                                               (2, 1, "flux", True), (2, 1, "qwen", True)])
+def test_tensor_parallel_matches_dense(world, B, family, sp):
+    errs = run_ranks(_tp_forward, world, B, family, sp, timeout=240)
     assert max(errs) < 1e-10, errs

@@ -50,8 +50,10 @@ def _worker(rank, world, port, q):
             par.close()
         from difflet_b200.parallel.tp import CollectiveTP, PeerTP, shard_mmdit_weights
 
-        for name, cls in (("peer_tp", PeerTP), ("nccl_tp", CollectiveTP)):
+        for name, cls, sp in (("peer_tp", PeerTP, False), ("nccl_tp", CollectiveTP, False),
+                              ("peer_tp_sp", PeerTP, True)):
             tp = cls(dist.group.WORLD, list(range(world)), torch.device("cuda", rank))
+            tp.sp = sp
             m2 = FluxTransformer(cfg, shard_mmdit_weights(cfg, m.w, world, rank))
             m2.tp = tp
             for _ in range(2):
