@@ -105,6 +105,7 @@ def main(argv=None):
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cp-mode", default="ulysses", choices=["ulysses", "ring", "gather_kv", "tp"],
                     help="how N>1 GPUs split the step: a context-parallel mode, or tensor parallelism")
+    ap.add_argument("--sp", action="store_true", help="with --cp-mode tp: Megatron sequence parallelism")
     ap.add_argument("--quant", default=None, choices=[None, "mxfp8"],
                     help="MXFP8 block linears (default targets); the headline number is bf16")
     args = ap.parse_args(argv)
@@ -128,7 +129,7 @@ def main(argv=None):
     if world == 1:
         par = DiffletParallelConfig()
     elif args.cp_mode == "tp":
-        par = DiffletParallelConfig(tp_degree=world)
+        par = DiffletParallelConfig(tp_degree=world, sp_enabled=args.sp)
     else:
         par = DiffletParallelConfig(cp_degree=world, cp_mode=args.cp_mode)
     t_load = time.time()
@@ -243,7 +244,7 @@ def main(argv=None):
             "data": "synthetic (random-init FLUX.1-dev weights, N(0,1) text states / pooled / latents)",
             "config": {"model": "FLUX.1-dev", "global_batch": B, "seq_len": S_img + S_txt,
                        "height": args.height, "width": args.width,
-                       "parallelism": f"{args.cp_mode}{world}" if world > 1 else "single",
+                       "parallelism": (f"{args.cp_mode}{world}" + ("+sp" if args.sp else "")) if world > 1 else "single",
                        "l2": "weights (24 GB) stream from HBM every step, larger than L2; no flush",
                        "cuda_graph": not args.no_graph, "load_s": round(load_s, 1)},
             "clocks": clocks,

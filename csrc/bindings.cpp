@@ -502,6 +502,42 @@ void tp_reduce(const at::Tensor& slots, int64_t slot_rows, int64_t world, int64_
   DFL_CHECK_RC(dfl_tp_reduce(&a, cur_stream()), "tp_reduce");
 }
 
+at::Tensor conv3d(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t kt,
+                  int64_t kh, int64_t kw, bool causal, const c10::optional<at::Tensor>& resid, bool silu,
+                  c10::optional<at::Tensor> out) {
+  check_bf16_cuda(x, "x");
+  check_bf16_cuda(w, "w");
+  TORCH_CHECK(x.dim() == 5 && x.is_contiguous(), "x must be contiguous [N, T, H, W, Ci]");
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.size(1) == kt * kh * kw * x.size(4), "w must be [Co, taps*Ci]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t Co = w.size(0);
+  at::Tensor y = (out.has_value() && out->defined()) ? *out
+                                                     : at::empty({x.size(0), x.size(1), x.size(2), x.size(3), Co}, x.options());
+  TORCH_CHECK(y.is_contiguous() && y.numel() == x.numel() / x.size(4) * Co, "out must be contiguous [N, T, H, W, Co]");
+  ConvArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.y = y.data_ptr();
+  at::Tensor ones;
+  if (bias.has_value() && bias->defined()) {
+    check_bf16_cuda(*bias, "bias");
+    a.bias = bias->data_ptr();
+  }
+  if (resid.has_value() && resid->defined()) {
+    check_bf16_cuda(*resid, "resid");
+    TORCH_CHECK(resid->is_contiguous() && resid->numel() == y.numel(), "resid must match out");
+    a.resid = resid->data_ptr();
+    ones = at::ones({Co}, x.options().dtype(at::kFloat));
+    a.ones = ones.data_ptr<float>();
+  }
+  a.N = (int)x.size(0), a.T = (int)x.size(1), a.H = (int)x.size(2), a.W = (int)x.size(3), a.Ci = (int)x.size(4);
+  a.Co = (int)Co;
+  a.kt = (int)kt, a.kh = (int)kh, a.kw = (int)kw, a.causal = causal ? 1 : 0, a.silu = silu ? 1 : 0;
+  a.err = err_ptr();
+  DFL_CHECK_RC(dfl_conv3d(&a, cur_stream()), "conv3d");
+  return y;
+}
+
 void memcpy_async(int64_t dst, int64_t src, int64_t nbytes) {
   DFL_CHECK_RC(dfl_memcpy_async(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), nbytes,
                                 cur_stream()),
@@ -606,6 +642,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("memcpy_async", &memcpy_async);
+  m.def("conv3d", &conv3d, "implicit-GEMM tcgen05 convolution (channels-last)", py::arg("x"), py::arg("w"),
+        py::arg("bias") = py::none(), py::arg("kt") = 3, py::arg("kh") = 3, py::arg("kw") = 3,
+        py::arg("causal") = true, py::arg("resid") = py::none(), py::arg("silu") = false, py::arg("out") = py::none());
   m.def("tp_reduce", &tp_reduce, py::arg("slots"), py::arg("slot_rows"), py::arg("world"), py::arg("rows"),
         py::arg("N"), py::arg("row0"), py::arg("bias") = py::none(), py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("out") = std::vector<int64_t>{},

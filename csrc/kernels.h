@@ -219,6 +219,20 @@ typedef struct TpReduceArgs {
 } TpReduceArgs;
 int dfl_tp_reduce(const TpReduceArgs* a, cudaStream_t stream);
 
+// Implicit-GEMM convolution, stride 1, kernel 1 or 3 per axis, channels-last bf16:
+// x [N, T, H, W, Ci], w [Co, kt*kh*kw, Ci] (tap-major: t, h, w), y [N, T, H, W, Co].
+// Spatial zero padding k/2; temporal causal (kt - 1 frames in front) or symmetric.
+// Ci a multiple of 32, Co a multiple of 32.  Optional bias, residual (y = resid + conv,
+// `ones` = f32 [Co] of ones), SiLU.
+typedef struct ConvArgs {
+  const void* x; const void* w; void* y;
+  const void* bias; const void* resid; const float* ones;
+  int N, T, H, W, Ci, Co;
+  int kt, kh, kw, causal, silu;
+  int* err;
+} ConvArgs;
+int dfl_conv3d(const ConvArgs* a, cudaStream_t stream);
+
 // Copy-engine copy (peer -> local over NVLink; no SM work, no kernel).
 int dfl_memcpy_async(void* dst, const void* src, long long nbytes, cudaStream_t stream);
 

@@ -101,6 +101,43 @@ def bench_mx(nat, iters, flush, peaks, cases, ref):
     return rows
 
 
+CONV_CASES = [("kl_512_128", 1, 1, 128, 128, 512, 512, (1, 3, 3)), ("kl_256_512", 1, 1, 512, 512, 256, 256, (1, 3, 3)),
+              ("kl_128_1024", 1, 1, 1024, 1024, 128, 128, (1, 3, 3)),
+              ("wan_384_180x320", 1, 4, 180, 320, 384, 384, (3, 3, 3)), ("wan_96_720x1280", 1, 2, 720, 1280, 96, 96, (3, 3, 3))]
+
+
+def bench_conv(nat, iters, flush, peaks, cases, ref):
+    """Implicit-GEMM conv vs cuDNN (channels-last bf16) on VAE decoder layers."""
+    from difflet_b200.ops import fused as F
+
+    rows = []
+    for name, N, T, H, W, Ci, Co, k in _sel(CONV_CASES, cases):
+        x = torch.randn(N, T, H, W, Ci, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(Co, Ci, *k, device="cuda", dtype=torch.bfloat16) * 0.02
+        w2 = F.conv_weight(w)
+        b = torch.zeros(Co, device="cuda", dtype=torch.bfloat16)
+        out = torch.empty(N, T, H, W, Co, device="cuda", dtype=torch.bfloat16)
+        t = time_fn(lambda: nat.conv3d(x, w2, b, k[0], k[1], k[2], True, None, False, out), iters, flush=flush)
+        fl = 2.0 * N * T * H * W * Ci * Co * k[0] * k[1] * k[2]
+        r = {"kernel": "conv_tcgen05", "shape": name, "ms": round(t, 4), "tflops": round(fl / t / 1e9, 1),
+             "frac_of_measured_peak": round(fl / t / 1e9 / peaks["bf16_tflops"], 3)}
+        if ref:
+            if k[0] == 1:
+                xc = x[:, 0].permute(0, 3, 1, 2)  # NCHW view of channels-last data
+                wc = w[:, :, 0].contiguous(memory_format=torch.channels_last)
+                fn = lambda: torch.nn.functional.conv2d(xc, wc, b, padding=1)  # noqa: E731
+            else:
+                xc = torch.nn.functional.pad(x.permute(0, 4, 1, 2, 3), (1, 1, 1, 1, 2, 0))
+                xc = xc.contiguous(memory_format=torch.channels_last_3d)
+                wc = w.contiguous(memory_format=torch.channels_last_3d)
+                fn = lambda: torch.nn.functional.conv3d(xc, wc, b)  # noqa: E731
+            tr = time_fn(fn, iters, flush=flush)
+            r.update({"cudnn_ms": round(tr, 4), "cudnn_tflops": round(fl / tr / 1e9, 1)})
+        rows.append(r)
+        del x, out
+    return rows
+
+
 def bench_attn(nat, iters, flush, peaks, cases, ref):
     rows = []
     for name, B, H, S in _sel(ATTN_CASES, cases):
@@ -162,6 +199,8 @@ def main(argv=None):
         rows += bench_ln(nat, args.iters, flush, peaks, cases, ref)
     if "mx" in only:
         rows += bench_mx(nat, args.iters, flush, peaks, cases, ref)
+    if "conv" in only:
+        rows += bench_conv(nat, args.iters, flush, peaks, cases, ref)
     _native.check_device_errors()
     for r in rows:
         print(json.dumps(r))

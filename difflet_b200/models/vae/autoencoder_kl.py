@@ -94,15 +94,34 @@ class KLDecoder:
         x = F.group_norm(x, self.cfg.norm_groups, self.w[name + ".weight"], self.w[name + ".bias"], eps=1e-6)
         return F.silu(x) if silu else x
 
-    def _conv(self, x, name, pad=1):
-        return F.conv2d(x, self.w[name + ".weight"], self.w[name + ".bias"], padding=pad)
+    def _native_ok(self, x, name):
+        w = self.w[name + ".weight"]
+        return (x.is_cuda and x.dtype == torch.bfloat16 and x.shape[1] % 32 == 0 and w.shape[0] % 32 == 0
+                and w.shape[-1] in (1, 3))
+
+    def _conv(self, x, name, pad=1, resid=None):
+        """Conv2d (+ residual).  bf16 CUDA tensors with 32-multiple channel counts run the
+        tcgen05 implicit-GEMM kernel on channels-last data; the rest goes to cuDNN."""
+        if self._native_ok(x, name):
+            from difflet_b200.ops import fused as FO
+
+            key = name + ".cl"
+            if key not in self.w:
+                self.w[key] = FO.conv_weight(self.w[name + ".weight"])
+            k = self.w[name + ".weight"].shape[-1]
+            xc = x.permute(0, 2, 3, 1).contiguous()[:, None]  # [N, 1, H, W, C]
+            rc = None if resid is None else resid.permute(0, 2, 3, 1).contiguous()[:, None]
+            y = FO.conv_cl(xc, self.w[key], self.w[name + ".bias"], kt=1, kh=k, kw=k, resid=rc)
+            return y[:, 0].permute(0, 3, 1, 2)  # NCHW view of channels-last data
+        y = F.conv2d(x, self.w[name + ".weight"], self.w[name + ".bias"], padding=pad)
+        return y if resid is None else resid + y
 
     def _resnet(self, x, name):
         h = self._conv(self._gn(x, name + ".norm1", True), name + ".conv1")
-        h = self._conv(self._gn(h, name + ".norm2", True), name + ".conv2")
         if name + ".conv_shortcut.weight" in self.w:
             x = self._conv(x, name + ".conv_shortcut", pad=0)
-        return x + h
+        # the residual add is fused into the second convolution's epilogue
+        return self._conv(self._gn(h, name + ".norm2", True), name + ".conv2", resid=x)
 
     def _attn(self, x, name):
         B, C, H, W = x.shape

@@ -311,6 +311,40 @@ def attention(q, k, v, scale, *, out=None, lse=None, kv_lo=None, kv_hi=None):
     return o
 
 
+# --------------------------------------------------------------------------- convolution
+def conv_weight(w: torch.Tensor) -> torch.Tensor:
+    """torch conv weight [Co, Ci, (kt,) kh, kw] -> the kernel's [Co, taps * Ci] (tap-major t, h, w)."""
+    if w.dim() == 4:
+        w = w[:, :, None]
+    Co, Ci = w.shape[:2]
+    return w.permute(0, 2, 3, 4, 1).reshape(Co, -1, Ci).reshape(Co, -1).contiguous()
+
+
+def conv_cl(x, w2, b=None, *, kt=3, kh=3, kw=3, causal=True, resid=None, silu=False, out=None):
+    """Stride-1 convolution on channels-last x [N, T, H, W, Ci] with ``conv_weight`` weights;
+    zero spatial padding k/2, temporal causal (kt - 1 in front) or symmetric padding;
+    optional bias, SiLU, residual add (y = resid + conv).  CUDA -> tcgen05 implicit GEMM."""
+    if x.is_cuda:
+        return native().conv3d(x, w2, b, kt, kh, kw, causal, resid, silu, out)
+    N, T, H, W, Ci = x.shape
+    Co = w2.shape[0]
+    ct = torch.float64 if x.dtype == torch.float64 else torch.float32
+    w5 = w2.to(ct).view(Co, kt, kh, kw, Ci).permute(0, 4, 1, 2, 3)
+    xc = x.to(ct).permute(0, 4, 1, 2, 3)
+    pt0, pt1 = (kt - 1, 0) if causal else (kt // 2, kt // 2)
+    xc = F.pad(xc, (kw // 2, kw // 2, kh // 2, kh // 2, pt0, pt1))
+    y = F.conv3d(xc, w5, None if b is None else b.to(ct))
+    if silu:
+        y = F.silu(y)
+    y = y.permute(0, 2, 3, 4, 1)
+    if resid is not None:
+        y = y + resid.to(ct)
+    if out is not None:
+        out.copy_(y.to(out.dtype))
+        return out
+    return y.to(x.dtype)
+
+
 # --------------------------------------------------------------------------- MXFP8
 def block_scales(s_plain: torch.Tensor) -> torch.Tensor:
     """Plain E8M0 scales [R, K/32] -> the tensor-core blocked layout (flat uint8): one

@@ -315,3 +315,27 @@ def test_cfg_combine_local_pointer(native):
     native.cfg_combine(u, c.data_ptr(), out, 4.0, False)  # this rank holds uncond
     torch.cuda.synchronize()
     assert (out - ref).abs().max().item() < 1e-4
+
+
+@pytest.mark.parametrize("N,T,H,W,Ci,Co,k,causal", [
+    (1, 1, 40, 72, 128, 128, (1, 3, 3), True),     # 2-D (KL decoder), partial 128-wide row tiles
+    (1, 5, 12, 150, 96, 96, (3, 3, 3), True),      # causal 3-D, 32-channel steps (Wan widths)
+    (2, 3, 8, 20, 64, 256, (3, 3, 3), False),      # symmetric temporal padding, BN 256
+    (1, 4, 6, 130, 192, 64, (1, 1, 1), True),      # 1x1x1 shortcut
+    (1, 3, 10, 70, 96, 192, (3, 3, 3), True),      # BN 192
+    (1, 2, 9, 33, 384, 96, (3, 3, 3), True),       # BN 96 (one N tile), 64-channel steps
+])
+def test_conv_cl_matches_torch(native, N, T, H, W, Ci, Co, k, causal):
+    from difflet_b200.ops import fused as F
+
+    torch.manual_seed(11)
+    x = torch.randn(N, T, H, W, Ci, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(Co, Ci, *k, device="cuda") / (Ci * k[0] * k[1] * k[2]) ** 0.5).bfloat16()
+    b = torch.randn(Co, device="cuda", dtype=torch.bfloat16)
+    resid = torch.randn(N, T, H, W, Co, device="cuda", dtype=torch.bfloat16)
+    w2 = F.conv_weight(w)
+    y = F.conv_cl(x, w2, b, kt=k[0], kh=k[1], kw=k[2], causal=causal, resid=resid)
+    ref = F.conv_cl(x.cpu().float(), w2.cpu().float(), b.cpu().float(), kt=k[0], kh=k[1], kw=k[2], causal=causal,
+                    resid=resid.cpu().float())
+    torch.cuda.synchronize()
+    _close(y.cpu(), ref)

@@ -137,3 +137,19 @@ def test_swiglu_rowmap_partial_rope_kernels(native):
     F.qkv_scatter(qkv.cpu().float(), q_dst=[qc], k_dst=[kc], v_dst=[vc], cos=cos.cpu(), sin=sin.cpu(), **kw)
     torch.cuda.synchronize()
     assert _rel(q, qc) < 1e-2 and _rel(k, kc) < 1e-2
+
+
+def test_kl_decoder_native_conv_vs_cpu(native):
+    """FLUX's KL decoder with its convolutions on the tcgen05 implicit-GEMM kernel."""
+    from difflet_b200.models.vae.autoencoder_kl import KLDecoder, KLDecoderConfig
+
+    cfg = KLDecoderConfig(block_out_channels=(64, 128, 128, 128))
+    cpu = KLDecoder.random_init(cfg, seed=4)
+    gpu = KLDecoder(cfg, {k: v.to("cuda", torch.bfloat16) for k, v in cpu.w.items()})
+    z = torch.randn(1, 16, 16, 24, generator=torch.Generator().manual_seed(5))
+    ref = cpu.decode(z)
+    out = gpu.decode(z.cuda())
+    torch.cuda.synchronize()
+    assert "decoder.conv_in.cl" not in gpu.w  # 16 input channels: cuDNN
+    assert "decoder.mid_block.resnets.0.conv1.cl" in gpu.w  # 128 channels: native
+    assert _rel(out, ref) < 3e-2
