@@ -118,7 +118,7 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at
                 const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
                 const c10::optional<at::Tensor>& resid, double alpha, bool out_f32,
                 std::vector<int64_t> out_peer, int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer,
-                const c10::optional<at::Tensor>& gate_row_map) {
+                const c10::optional<at::Tensor>& gate_row_map, int64_t cta_mode) {
   check_bf16_cuda(A, "A");
   check_bf16_cuda(B, "B");
   check_rowmajor(A, "A");
@@ -134,6 +134,7 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at
   a.lda = A.stride(0);
   a.ldb = B.stride(0);
   a.K = (int)A.size(1);
+  a.cta_mode = (int)cta_mode;
   DFL_CHECK_RC(dfl_gemm_bf16(&a, cur_stream()), "gemm");
   return D;
 }
@@ -605,12 +606,14 @@ at::Tensor rel_l1(const at::Tensor& a, const at::Tensor& b) {
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "difflet_b200 native sm_100a kernels";
+  m.def("gemm_set_pair_auto", [](bool on) { dfl_gemm_set_pair_auto(on ? 1 : 0); });
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("B"),
         py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_f32") = false, py::arg("out_peer") = std::vector<int64_t>{}, py::arg("rows_per_rank") = 0,
-        py::arg("peer_row_off") = 0, py::arg("ldd") = 0, py::arg("gate_row_map") = py::none());
+        py::arg("peer_row_off") = 0, py::arg("ldd") = 0, py::arg("gate_row_map") = py::none(),
+        py::arg("cta_mode") = 0);
   m.def("mx_quantize", &mx_quantize, py::arg("x"), py::arg("blocked") = false);
   m.def("gemm_mx", &gemm_mx, "block-scaled MXFP8 tcgen05 GEMM", py::arg("A"), py::arg("sfa"), py::arg("B"),
         py::arg("sfb"), py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,

@@ -265,6 +265,14 @@ int dispatch_epi(int epi, bool out_f32, const CUtensorMap& ta, const CUtensorMap
 
 }  // namespace
 
+extern "C" int dfl_gemm_pair_launch(const void* ta, const void* tb, int M, int N, int K, const void* ep, int epi,
+                                    int out_f32, int* err, cudaStream_t stream, int dev);
+
+// Automatic choice of the CTA-pair kernel for wide GEMMs with M >= 1024 (on by default;
+// dfl_gemm_set_pair_auto(0) restores the one-CTA kernel everywhere).
+static int g_pair_auto = 1;
+extern "C" void dfl_gemm_set_pair_auto(int on) { g_pair_auto = on; }
+
 extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
   // Host-side argument checks (TMA: 16-byte aligned bases and row strides).
   if (a->M <= 0 || a->N <= 0 || a->K <= 0) return -2;
@@ -308,6 +316,15 @@ extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
   ep.peer_row_off = a->peer_row_off;
   if (a->out_world < 0 || a->out_world > DFL_MAX_PEERS) return -9;
   for (int r = 0; r < DFL_MAX_PEERS; ++r) ep.out_peer[r] = r < a->out_world ? a->out_peer[r] : nullptr;
+  const bool pair = a->cta_mode == 2 || (a->cta_mode == 0 && g_pair_auto && wide && a->M >= 1024);
+  if (pair && a->epi != kEpiSwiGLU) {
+    CUtensorMap ta2, tb2;  // 2-CTA tiles: 128 A rows and 128 B rows per CTA
+    rc = dfl_host::make_tmap_2d_bf16(&ta2, a->A, a->K, a->M, a->lda, BK, BM, true);
+    if (rc) return 1000 + rc;
+    rc = dfl_host::make_tmap_2d_bf16(&tb2, a->B, a->K, a->N, a->ldb, BK, 128, true);
+    if (rc) return 2000 + rc;
+    return dfl_gemm_pair_launch(&ta2, &tb2, a->M, a->N, a->K, &ep, a->epi, a->out_f32, a->err, stream, dev);
+  }
   if (wide)
     return dispatch_epi<256, 4>(a->epi, a->out_f32, ta, tb, a->M, a->N, a->K, ep, a->err, stream, dev);
   return dispatch_epi<128, 6>(a->epi, a->out_f32, ta, tb, a->M, a->N, a->K, ep, a->err, stream, dev);

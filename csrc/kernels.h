@@ -41,9 +41,12 @@ typedef struct GemmArgs {
   int out_world;
   int rows_per_rank;
   long long peer_row_off;
+  // 0: automatic choice, 1: one CTA per 128 x BN tile, 2: CTA pairs (cta_group::2, 256 x 256 tiles)
+  int cta_mode;
 } GemmArgs;
 
 int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream);
+void dfl_gemm_set_pair_auto(int on);
 
 // MXFP8 GEMM on the block-scaled tensor cores (tcgen05 kind::mxf8f6f4):
 //   D = epi(A . B^T), A [M, K] / B [N, K] FP8 E4M3 (K-major, row strides in

@@ -27,6 +27,7 @@ EXT_NAME = "_difflet_C"
 
 CUDA_SOURCES = [
     "gemm.cu",
+    "gemm2.cu",
     "norm.cu",
     "attention.cu",
     "comm.cu",

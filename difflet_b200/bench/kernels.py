@@ -61,11 +61,13 @@ def bench_gemm(nat, iters, flush, peaks, cases, ref):
         a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
         b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
         out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        t_ours = time_fn(lambda: nat.gemm(a, b, None, out=out), iters, flush=flush)
+        t_ours = time_fn(lambda: nat.gemm(a, b, None, out=out, cta_mode=1), iters, flush=flush)
+        t_pair = time_fn(lambda: nat.gemm(a, b, None, out=out, cta_mode=2), iters, flush=flush)
         fl = 2.0 * M * N * K
         r = {"kernel": "gemm_tcgen05", "shape": name, "M": M, "N": N, "K": K, "ms": round(t_ours, 4),
              "tflops": round(fl / t_ours / 1e9, 1),
-             "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3)}
+             "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3),
+             "pair_ms": round(t_pair, 4), "pair_tflops": round(fl / t_pair / 1e9, 1)}
         if ref:
             t_ref = time_fn(lambda: torch.matmul(a, b.t(), out=out), iters, flush=flush)
             r.update({"cublas_ms": round(t_ref, 4), "cublas_tflops": round(fl / t_ref / 1e9, 1)})

@@ -52,6 +52,7 @@ def native():
         from difflet_b200 import _native
 
         _nat = _native.require()
+        _nat.gemm_set_pair_auto(envs.DIFFLET_GEMM_PAIR != "0")
     LAUNCHES[0] += 1
     return _nat
 

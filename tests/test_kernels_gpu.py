@@ -339,3 +339,29 @@ def test_conv_cl_matches_torch(native, N, T, H, W, Ci, Co, k, causal):
                     resid=resid.cpu().float())
     torch.cuda.synchronize()
     _close(y.cpu(), ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (1000, 1280, 512), (4608, 3072, 3072), (300, 2304, 128)])
+def test_gemm_cta_pair(native, M, N, K):
+    """The 2-CTA (cta_group::2) GEMM: plain, GELU window and gated residual epilogues."""
+    torch.manual_seed(M + K)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    b = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    bias = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    ref = a.float() @ b.float().t() + bias.float()
+    out = native.gemm(a, b, bias, cta_mode=2)
+    torch.cuda.synchronize()
+    _close(out, ref)
+    g = native.gemm(a, b, bias, epi=1, act_lo=128, act_hi=N, cta_mode=2)
+    ref_g = ref.clone()
+    ref_g[:, 128:] = torch.nn.functional.gelu(ref_g[:, 128:], approximate="tanh")
+    gate = torch.randn(2, N, device="cuda")
+    resid = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    r = resid.clone()
+    native.gemm(a, b, bias, out=r, epi=2, gate=gate, rows_per_batch=(M + 1) // 2, resid=r, cta_mode=2)
+    rows = torch.arange(M, device="cuda") // ((M + 1) // 2)
+    ref_r = resid.float() + gate[rows] * ref
+    torch.cuda.synchronize()
+    _close(g, ref_g)
+    _close(r, ref_r)
+    assert native.error_word(0)[0].item() == 0
