@@ -56,10 +56,19 @@ static at::Tensor gemm_epilogue_args(GemmArgs& a, const at::Tensor& A, int64_t M
                                      const c10::optional<at::Tensor>& resid, double alpha, bool out_f32,
                                      const std::vector<int64_t>& out_peer, int64_t rows_per_rank,
                                      int64_t peer_row_off, int64_t ldd_peer,
-                                     const c10::optional<at::Tensor>& gate_row_map) {
+                                     const c10::optional<at::Tensor>& gate_row_map, const std::string& qkv_plan) {
   at::Tensor D;
   const int64_t N_out = epi == kEpiSwiGLU ? N / 2 : N;
-  if (!out_peer.empty()) {
+  if (epi == kEpiQkv) {
+    TORCH_CHECK(qkv_plan.size() == sizeof(QkvScatterArgs), "epi=qkv needs a qkv_plan (from qkv_plan())");
+    a.qkv = reinterpret_cast<const QkvScatterArgs*>(qkv_plan.data());
+    TORCH_CHECK(!out_f32 && out_peer.empty(), "the qkv epilogue stores bf16 locally");
+  }
+  if (epi == kEpiQkv && !(out.has_value() && out->defined())) {
+    D = at::empty({0}, A.options());  // every column goes to the head scatter (checked natively)
+    a.D = nullptr;
+    a.ldd = 0;
+  } else if (!out_peer.empty()) {
     TORCH_CHECK(out_peer.size() <= DFL_MAX_PEERS, "at most 8 output peers");
     TORCH_CHECK(rows_per_rank > 0 && ldd_peer > 0, "out_peer needs rows_per_rank and ldd");
     a.out_world = (int)out_peer.size();
@@ -118,7 +127,7 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at
                 const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
                 const c10::optional<at::Tensor>& resid, double alpha, bool out_f32,
                 std::vector<int64_t> out_peer, int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer,
-                const c10::optional<at::Tensor>& gate_row_map, int64_t cta_mode) {
+                const c10::optional<at::Tensor>& gate_row_map, int64_t cta_mode, const std::string& qkv_plan) {
   check_bf16_cuda(A, "A");
   check_bf16_cuda(B, "B");
   check_rowmajor(A, "A");
@@ -128,7 +137,7 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, const c10::optional<at
   GemmArgs a{};
   at::Tensor D = gemm_epilogue_args(a, A, A.size(0), B.size(0), bias, out, epi, act_lo, act_hi, gate,
                                     rows_per_batch, resid, alpha, out_f32, out_peer, rows_per_rank, peer_row_off,
-                                    ldd_peer, gate_row_map);
+                                    ldd_peer, gate_row_map, qkv_plan);
   a.A = A.data_ptr();
   a.B = B.data_ptr();
   a.lda = A.stride(0);
@@ -162,7 +171,7 @@ at::Tensor gemm_mx(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor&
                    int64_t act_lo, int64_t act_hi, const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
                    const c10::optional<at::Tensor>& resid, double alpha, bool out_f32, std::vector<int64_t> out_peer,
                    int64_t rows_per_rank, int64_t peer_row_off, int64_t ldd_peer,
-                   const c10::optional<at::Tensor>& gate_row_map) {
+                   const c10::optional<at::Tensor>& gate_row_map, const std::string& qkv_plan) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kFloat8_e4m3fn &&
                   B.scalar_type() == at::kFloat8_e4m3fn, "A and B must be CUDA float8_e4m3fn");
   check_rowmajor(A, "A");
@@ -178,7 +187,8 @@ at::Tensor gemm_mx(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor&
   MxGemmArgs m{};
   TORCH_CHECK(epi != kEpiSwiGLU, "the MXFP8 GEMM has no SwiGLU epilogue");
   at::Tensor D = gemm_epilogue_args(m.g, A, M, N, bias, out, epi, act_lo, act_hi, gate, rows_per_batch, resid,
-                                    alpha, out_f32, out_peer, rows_per_rank, peer_row_off, ldd_peer, gate_row_map);
+                                    alpha, out_f32, out_peer, rows_per_rank, peer_row_off, ldd_peer, gate_row_map,
+                                    qkv_plan);
   m.g.A = A.data_ptr();
   m.g.B = B.data_ptr();
   m.g.lda = A.stride(0);
@@ -239,27 +249,23 @@ at::Tensor ln_modulate(const at::Tensor& x, c10::optional<at::Tensor> out,
   return y;
 }
 
-void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_off, int64_t S_src,
-                 int64_t H, int64_t dh, int64_t norm_mode, const c10::optional<at::Tensor>& wq,
-                 const c10::optional<at::Tensor>& wk, double eps,
-                 const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t,
-                 int64_t rope_pos_off, bool rope_half, int64_t heads_per_rank,
-                 std::vector<int64_t> q_dst, std::vector<int64_t> k_dst, std::vector<int64_t> v_dst,
-                 int64_t S_dst, int64_t seq_off, bool out_token_major, bool kv_replicate, int64_t q_S_dst,
-                 int64_t q_seq_off) {
-  check_bf16_cuda(qkv, "qkv");
-  check_rowmajor(qkv, "qkv");
-  const c10::cuda::CUDAGuard guard(qkv.device());
+// Head-scatter description shared by the standalone qkv_scatter kernel and the GEMM
+// qkv epilogue (source fields qkv / ld / rows are filled by the caller).
+QkvScatterArgs make_qkv_args(int64_t q_off, int64_t k_off, int64_t v_off, int64_t S_src, int64_t H, int64_t dh,
+                             int64_t norm_mode, const c10::optional<at::Tensor>& wq,
+                             const c10::optional<at::Tensor>& wk, double eps, const c10::optional<at::Tensor>& cos_t,
+                             const c10::optional<at::Tensor>& sin_t, int64_t rope_pos_off, bool rope_half,
+                             int64_t heads_per_rank, const std::vector<int64_t>& q_dst,
+                             const std::vector<int64_t>& k_dst, const std::vector<int64_t>& v_dst, int64_t S_dst,
+                             int64_t seq_off, bool out_token_major, bool kv_replicate, int64_t q_S_dst,
+                             int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off) {
   const int world = (int)q_dst.size();
   TORCH_CHECK(world >= 1 && world <= DFL_MAX_PEERS, "1..8 destinations");
   TORCH_CHECK(k_dst.size() == q_dst.size() && v_dst.size() == q_dst.size(), "dst tables differ");
   QkvScatterArgs a{};
-  a.qkv = qkv.data_ptr();
-  a.ld = qkv.stride(0);
   a.q_off = (int)q_off;
   a.k_off = (int)k_off;
   a.v_off = (int)v_off;
-  a.rows = (int)qkv.size(0);
   a.S_src = (int)S_src;
   a.H = (int)H;
   a.dh = (int)dh;
@@ -293,7 +299,45 @@ void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_
   a.kv_replicate = kv_replicate ? 1 : 0;
   a.q_S_dst = (int)q_S_dst;
   a.q_seq_off = (int)q_seq_off;
+  a.seg_rows = (int)seg_rows;
+  a.seg1_seq_off = (int)seg1_seq_off;
+  a.seg1_rope_off = (int)seg1_rope_off;
+  return a;
+}
+
+void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_off, int64_t S_src,
+                 int64_t H, int64_t dh, int64_t norm_mode, const c10::optional<at::Tensor>& wq,
+                 const c10::optional<at::Tensor>& wk, double eps,
+                 const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t,
+                 int64_t rope_pos_off, bool rope_half, int64_t heads_per_rank,
+                 std::vector<int64_t> q_dst, std::vector<int64_t> k_dst, std::vector<int64_t> v_dst,
+                 int64_t S_dst, int64_t seq_off, bool out_token_major, bool kv_replicate, int64_t q_S_dst,
+                 int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off) {
+  check_bf16_cuda(qkv, "qkv");
+  check_rowmajor(qkv, "qkv");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  QkvScatterArgs a = make_qkv_args(q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos_t, sin_t,
+                                   rope_pos_off, rope_half, heads_per_rank, q_dst, k_dst, v_dst, S_dst, seq_off,
+                                   out_token_major, kv_replicate, q_S_dst, q_seq_off, seg_rows, seg1_seq_off,
+                                   seg1_rope_off);
+  a.qkv = qkv.data_ptr();
+  a.ld = qkv.stride(0);
+  a.rows = (int)qkv.size(0);
   DFL_CHECK_RC(dfl_qkv_scatter(&a, cur_stream()), "qkv_scatter");
+}
+
+// The same description packed for the GEMM's qkv epilogue (epi = 5, argument qkv_plan).
+py::bytes qkv_plan(int64_t q_off, int64_t k_off, int64_t v_off, int64_t S_src, int64_t H, int64_t dh,
+                   int64_t norm_mode, const c10::optional<at::Tensor>& wq, const c10::optional<at::Tensor>& wk,
+                   double eps, const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t,
+                   int64_t rope_pos_off, bool rope_half, int64_t heads_per_rank, std::vector<int64_t> q_dst,
+                   std::vector<int64_t> k_dst, std::vector<int64_t> v_dst, int64_t S_dst, int64_t seq_off,
+                   bool out_token_major, bool kv_replicate, int64_t q_S_dst, int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off) {
+  QkvScatterArgs a = make_qkv_args(q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos_t, sin_t,
+                                   rope_pos_off, rope_half, heads_per_rank, q_dst, k_dst, v_dst, S_dst, seq_off,
+                                   out_token_major, kv_replicate, q_S_dst, q_seq_off, seg_rows, seg1_seq_off,
+                                   seg1_rope_off);
+  return py::bytes(reinterpret_cast<const char*>(&a), sizeof(a));
 }
 
 at::Tensor gemv(const at::Tensor& W, const at::Tensor& x, const c10::optional<at::Tensor>& bias,
@@ -613,20 +657,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_f32") = false, py::arg("out_peer") = std::vector<int64_t>{}, py::arg("rows_per_rank") = 0,
         py::arg("peer_row_off") = 0, py::arg("ldd") = 0, py::arg("gate_row_map") = py::none(),
-        py::arg("cta_mode") = 0);
+        py::arg("cta_mode") = 0, py::arg("qkv_plan") = py::bytes());
   m.def("mx_quantize", &mx_quantize, py::arg("x"), py::arg("blocked") = false);
   m.def("gemm_mx", &gemm_mx, "block-scaled MXFP8 tcgen05 GEMM", py::arg("A"), py::arg("sfa"), py::arg("B"),
         py::arg("sfb"), py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_f32") = false, py::arg("out_peer") = std::vector<int64_t>{}, py::arg("rows_per_rank") = 0,
-        py::arg("peer_row_off") = 0, py::arg("ldd") = 0, py::arg("gate_row_map") = py::none());
+        py::arg("peer_row_off") = 0, py::arg("ldd") = 0, py::arg("gate_row_map") = py::none(),
+        py::arg("qkv_plan") = py::bytes());
   m.def("ln_modulate", &ln_modulate, py::arg("x"), py::arg("out") = py::none(),
         py::arg("w") = py::none(), py::arg("b") = py::none(), py::arg("shift") = py::none(),
         py::arg("scale") = py::none(), py::arg("rows_per_batch") = 0, py::arg("eps") = 1e-6,
         py::arg("rms") = false, py::arg("row_map") = py::none(), py::arg("y_peer") = std::vector<int64_t>{},
         py::arg("row0") = 0, py::arg("rows") = -1);
   m.def("qkv_scatter", &qkv_scatter);
+  m.def("qkv_plan", &qkv_plan);
   m.def("gemv", &gemv, py::arg("W"), py::arg("x"), py::arg("bias") = py::none(),
         py::arg("out") = py::none(), py::arg("silu_in") = false, py::arg("silu_out") = false);
   m.def("euler_step", &euler_step, py::arg("x32"), py::arg("x16"), py::arg("v"),

@@ -178,43 +178,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mb * BM + sub * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
-      if constexpr (EPI == kEpiSwiGLU) {
-        // chunk pairs (h, g) of interleaved 32-column groups -> 32 output columns
-        EpiParams p2 = ep;
-        p2.bias = nullptr;
-        p2.alpha = 1.f;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
-          const int col0 = nb * BN + c * 32;
-          if (col0 >= N) break;  // warp-uniform
-          uint32_t rh[32], rg[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, rh);
-          tmem_ld_32x32b_x32(tbase + (c + 1) * 32, rg);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float h = __uint_as_float(rh[j]) * ep.alpha, g = __uint_as_float(rg[j]) * ep.alpha;
-            if (ep.bias) {
-              h += __bfloat162float(ep.bias[col0 + j]);
-              g += __bfloat162float(ep.bias[col0 + 32 + j]);
-            }
-            rh[j] = __float_as_uint(h * silu(g));
-          }
-          epilogue_chunk<kEpiNone, OUT_F32>(rh, row, col0 / 2, M, N / 2, p2);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int col0 = nb * BN + c * 32;
-          if (col0 >= N) break;  // warp-uniform
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, r);
-          tmem_wait_ld();
-          epilogue_chunk<EPI, OUT_F32>(r, row, col0, M, N, ep);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
+      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, M, N, ep, [&]() {
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[acc]);
+      });
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -258,6 +225,8 @@ int dispatch_epi(int epi, bool out_f32, const CUtensorMap& ta, const CUtensorMap
       return launch_variant<BN, STAGES, kEpiGateResid, false>(ta, tb, M, N, K, ep, err, s, dev);
     case kEpiSwiGLU:
       return launch_variant<BN, STAGES, kEpiSwiGLU, false>(ta, tb, M, N, K, ep, err, s, dev);
+    case kEpiQkv:
+      return launch_variant<BN, STAGES, kEpiQkv, false>(ta, tb, M, N, K, ep, err, s, dev);
     default:
       return -1;
   }
@@ -280,6 +249,7 @@ extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
   if ((a->lda * 2) % 16 || (a->ldb * 2) % 16) return -4;
   if (a->K % 8) return -5;
   const void* dchk = a->out_world > 0 ? a->out_peer[0] : a->D;
+  if (a->epi == kEpiQkv && a->D == nullptr) dchk = nullptr;  // every column goes to the head scatter
   if (!a->out_f32 && ((a->ldd % 8) || (reinterpret_cast<uintptr_t>(dchk) & 15))) return -6;
   if (a->out_f32 && ((a->ldd % 4) || (reinterpret_cast<uintptr_t>(dchk) & 15))) return -6;
   if (a->bias && (reinterpret_cast<uintptr_t>(a->bias) & 15)) return -7;
@@ -298,26 +268,10 @@ extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
   rc = dfl_host::make_tmap_2d_bf16(&tb, a->B, a->K, a->N, a->ldb, BK, wide ? 256 : 128, true);
   if (rc) return 2000 + rc;
   EpiParams ep;
-  ep.D = a->D;
-  ep.ldd = a->ldd;
-  ep.bias = reinterpret_cast<const __nv_bfloat16*>(a->bias);
-  ep.act_lo = a->act_lo;
-  ep.act_hi = a->act_hi;
-  ep.gate = a->gate;
-  ep.gate_bstride = a->gate_bstride;
-  ep.rows_per_batch = a->rows_per_batch > 0 ? a->rows_per_batch : a->M;
-  ep.gate_row_map = a->gate_row_map;
-  if (a->epi == kEpiSwiGLU && (a->N % 64 || a->out_world > 0)) return -11;
-  ep.resid = reinterpret_cast<const __nv_bfloat16*>(a->resid);
-  ep.ldr = a->ldr;
-  ep.alpha = a->alpha;
-  ep.out_world = a->out_world;
-  ep.rows_per_rank = a->rows_per_rank > 0 ? a->rows_per_rank : a->M;
-  ep.peer_row_off = a->peer_row_off;
-  if (a->out_world < 0 || a->out_world > DFL_MAX_PEERS) return -9;
-  for (int r = 0; r < DFL_MAX_PEERS; ++r) ep.out_peer[r] = r < a->out_world ? a->out_peer[r] : nullptr;
+  rc = dfl_host::fill_epi_params(*a, ep);
+  if (rc) return rc;
   const bool pair = a->cta_mode == 2 || (a->cta_mode == 0 && g_pair_auto && wide && a->M >= 1024);
-  if (pair && a->epi != kEpiSwiGLU) {
+  if (pair) {
     CUtensorMap ta2, tb2;  // 2-CTA tiles: 128 A rows and 128 B rows per CTA
     rc = dfl_host::make_tmap_2d_bf16(&ta2, a->A, a->K, a->M, a->lda, BK, BM, true);
     if (rc) return 1000 + rc;

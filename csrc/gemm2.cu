@@ -204,20 +204,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mb * 2 * BM + (int)rank * BM + sub * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int col0 = nb * BN + c * 32;
-        if (col0 >= N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c * 32, r);
-        tmem_wait_ld();
-        epilogue_chunk<EPI, OUT_F32>(r, row, col0, M, N, ep);
-      }
-      tc_fence_before();
-      if (rank == 0)
-        mbar_arrive(&tempty_bar[acc]);
-      else
-        mbar_arrive_cta0(&tempty_bar[acc]);
+      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, M, N, ep, [&]() {
+        tc_fence_before();
+        if (rank == 0)
+          mbar_arrive(&tempty_bar[acc]);
+        else
+          mbar_arrive_cta0(&tempty_bar[acc]);
+      });
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -277,6 +270,10 @@ extern "C" int dfl_gemm_pair_launch(const void* ta, const void* tb, int M, int N
       return launch_pair<kEpiSilu, false>(a, b, M, N, K, ep, err, stream, dev);
     case kEpiGateResid:
       return launch_pair<kEpiGateResid, false>(a, b, M, N, K, ep, err, stream, dev);
+    case kEpiSwiGLU:
+      return launch_pair<kEpiSwiGLU, false>(a, b, M, N, K, ep, err, stream, dev);
+    case kEpiQkv:
+      return launch_pair<kEpiQkv, false>(a, b, M, N, K, ep, err, stream, dev);
     default:
       return -1;
   }

@@ -1,8 +1,12 @@
 // Shared GEMM epilogue for the tcgen05 GEMMs (bf16 and MXFP8): tile raster,
-// bias, GELU-tanh / SiLU on a column window, residual + gate * y, bf16 / f32
-// stores, and an optional row scatter into peer ranks' buffers (tensor-parallel
-// partial sums land directly at the rank that owns each row).
+// bias, GELU-tanh / SiLU on a column window, residual + gate * y, SwiGLU, bf16 /
+// f32 stores, an optional row scatter into peer ranks' buffers (tensor-parallel
+// partial sums land directly at the rank that owns each row), and the q/k/v head
+// scatter (per-head RMSNorm + RoPE + store into head-major buffers, one per rank:
+// the Ulysses sequence->head all-to-all fused into the projection that feeds it).
 #pragma once
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -28,6 +32,8 @@ struct EpiParams {
   int out_world;
   int rows_per_rank;
   long long peer_row_off;
+  // kEpiQkv: head scatter of the q / k / v column blocks (source rows = GEMM rows)
+  QkvScatterArgs qs;
 };
 
 DFL_DEVICE void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
@@ -40,15 +46,16 @@ DFL_DEVICE void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   nb = r / gm;
 }
 
-template <int EPI, bool OUT_F32>
+// LIN = false: r already holds the finished linear output (alpha and bias applied).
+template <int EPI, bool OUT_F32, bool LIN = true>
 DFL_DEVICE void epilogue_chunk(const uint32_t (&r)[32], int row, int col0, int M, int N,
                                const EpiParams& p) {
   if (row >= M) return;
   float v[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+  for (int j = 0; j < 32; ++j) v[j] = LIN ? __uint_as_float(r[j]) * p.alpha : __uint_as_float(r[j]);
   const bool full = (col0 + 32 <= N);
-  if (p.bias != nullptr) {
+  if (LIN && p.bias != nullptr) {
     if (full) {
       const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
@@ -141,4 +148,333 @@ DFL_DEVICE void epilogue_chunk(const uint32_t (&r)[32], int row, int col0, int M
   }
 }
 
+// ---------------------------------------------------------------------------
+// q/k/v head scatter.  One thread owns one row of the 128-row tile; a head is
+// dh / 32 TMEM chunks of that row.  The linear output is rounded to bf16 first
+// (the value the unfused path stores and re-reads), then per-head RMS, the norm
+// weight, RoPE (interleaved pairs (2i, 2i+1), or half-split pairs (i, i + dh/2) =
+// chunks c and c + dh/64), and a bf16 store to every destination of the head.
+DFL_DEVICE void qkv_linear_chunk(const uint32_t (&r)[32], float (&x)[32], const __nv_bfloat16* bias, float alpha) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(r[j]) * alpha;
+  if (bias != nullptr) {
+    const uint4* b4 = reinterpret_cast<const uint4*>(bias);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w = __ldg(b4 + q);
+      uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float2 f = unpack_bf16x2(ws[h]);
+        x[q * 8 + 2 * h] += f.x;
+        x[q * 8 + 2 * h + 1] += f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(__float2bfloat16(x[j]));
+}
+
+DFL_DEVICE void qkv_scale_chunk(float (&x)[32], float rr, const __nv_bfloat16* w) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] *= rr;
+  if (w != nullptr) {
+    const uint4* w4 = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u = __ldg(w4 + q);
+      uint32_t us[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float2 f = unpack_bf16x2(us[h]);
+        x[q * 8 + 2 * h] *= f.x;
+        x[q * 8 + 2 * h + 1] *= f.y;
+      }
+    }
+  }
+}
+
+DFL_DEVICE void store_bf16x32(__nv_bfloat16* d, const float (&x)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16x2(x[8 * q + 0], x[8 * q + 1]);
+    w.y = pack_bf16x2(x[8 * q + 2], x[8 * q + 3]);
+    w.z = pack_bf16x2(x[8 * q + 4], x[8 * q + 5]);
+    w.w = pack_bf16x2(x[8 * q + 6], x[8 * q + 7]);
+    reinterpret_cast<uint4*>(d)[q] = w;
+  }
+}
+
+DFL_DEVICE void load_f32x16(const float* p, float (&x)[16]) {
+  const float4* p4 = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float4 f = __ldg(p4 + q);
+    x[4 * q] = f.x, x[4 * q + 1] = f.y, x[4 * q + 2] = f.z, x[4 * q + 3] = f.w;
+  }
+}
+
+// Which block (0 q, 1 k, 2 v) and head the column col0 starts, or false for other columns.
+DFL_DEVICE bool qkv_locate(const QkvScatterArgs& a, int col0, int& which, int& h) {
+  const int offs[3] = {a.q_off, a.k_off, a.v_off};
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    if (offs[i] >= 0 && col0 >= offs[i] && col0 < offs[i] + a.H * a.dh) {
+      which = i;
+      h = (col0 - offs[i]) / a.dh;
+      return true;
+    }
+  }
+  return false;
+}
+
+template <int DH, class Rel>
+DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int which, int h, const EpiParams& ep,
+                                  bool last, Rel& release) {
+  constexpr int NC = DH / 32;
+  const QkvScatterArgs& a = ep.qs;
+  const bool valid = row < M;
+  const int b = valid ? row / a.S_src : 0;
+  const int s = valid ? row - b * a.S_src : 0;
+  const __nv_bfloat16* bias = ep.bias ? ep.bias + hcol : nullptr;
+  const bool norm = which < 2 && a.norm_mode == 1;
+  float rr = 1.f;
+  if (norm) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < NC; ++c) {
+      uint32_t r[32];
+      float x[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, r);
+      tmem_wait_ld();
+      qkv_linear_chunk(r, x, bias ? bias + c * 32 : nullptr, ep.alpha);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss += x[j] * x[j];
+    }
+    rr = rsqrtf(ss / (float)DH + a.eps);
+  }
+  const __nv_bfloat16* wn =
+      norm ? reinterpret_cast<const __nv_bfloat16*>(which == 0 ? a.wq : a.wk) : nullptr;
+  // destinations (same addressing as dfl_qkv_scatter)
+  const int Hl = a.heads_per_rank;
+  const bool seg1 = a.seg_rows > 0 && s >= a.seg_rows;
+  const int dpos = seg1 ? a.seg1_seq_off + (s - a.seg_rows) : a.seq_off + s;
+  const int rpos = seg1 ? a.seg1_rope_off + (s - a.seg_rows) : a.rope_pos_off + s;
+  const int owner = a.kv_replicate ? 0 : h / Hl;
+  const int hl = a.kv_replicate ? h : h % Hl;
+  const long long dst_off = a.out_token_major
+                                ? ((long long)b * a.S_dst + dpos) * (long long)(Hl * DH) + (long long)hl * DH
+                                : (((long long)b * Hl + hl) * a.S_dst + dpos) * DH;
+  const long long q_off_rows =
+      a.kv_replicate ? (((long long)b * Hl + hl) * a.q_S_dst + a.q_seq_off + s) * DH : dst_off;
+  const int ndst = (which > 0 && a.kv_replicate) ? a.world : 1;
+  auto dst = [&](int d) -> __nv_bfloat16* {
+    if (which == 0) return reinterpret_cast<__nv_bfloat16*>(a.q_dst[owner]) + q_off_rows;
+    void* base = which == 1 ? (a.kv_replicate ? a.k_dst[d] : a.k_dst[owner])
+                            : (a.kv_replicate ? a.v_dst[d] : a.v_dst[owner]);
+    return reinterpret_cast<__nv_bfloat16*>(base) + dst_off;
+  };
+  const float* cs = nullptr;
+  const float* sn = nullptr;
+  if (which < 2 && a.cos_t != nullptr && valid) {
+    const long long rope_row = (long long)(a.rope_heads > 0 ? a.rope_heads : 1) * (DH / 2);
+    const long long o = (long long)rpos * rope_row + (a.rope_heads > 0 ? h * (DH / 2) : 0);
+    cs = a.cos_t + o;
+    sn = a.sin_t + o;
+  }
+  const bool rope = which < 2 && a.cos_t != nullptr;  // warp-uniform (cs may be null on invalid rows)
+  if (!(rope && a.rope_half)) {
+#pragma unroll 1
+    for (int c = 0; c < NC; ++c) {
+      uint32_t r[32];
+      float x[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, r);
+      tmem_wait_ld();
+      if (last && c == NC - 1) release();
+      qkv_linear_chunk(r, x, bias ? bias + c * 32 : nullptr, ep.alpha);
+      if (norm) qkv_scale_chunk(x, rr, wn ? wn + c * 32 : nullptr);
+      if (cs != nullptr) {  // pairs (2p, 2p+1) of this chunk use frequencies c*16 + p
+        float cv[16], sv[16];
+        load_f32x16(cs + c * 16, cv);
+        load_f32x16(sn + c * 16, sv);
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+          const float x0 = x[2 * p], x1 = x[2 * p + 1];
+          x[2 * p] = x0 * cv[p] - x1 * sv[p];
+          x[2 * p + 1] = x1 * cv[p] + x0 * sv[p];
+        }
+      }
+      if (valid)
+        for (int d = 0; d < ndst; ++d) store_bf16x32(dst(d) + c * 32, x);
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < NC / 2; ++c) {
+      uint32_t r1[32], r2[32];
+      float x1[32], x2[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, r1);
+      tmem_ld_32x32b_x32(taddr + (c + NC / 2) * 32, r2);
+      tmem_wait_ld();
+      if (last && c == NC / 2 - 1) release();
+      qkv_linear_chunk(r1, x1, bias ? bias + c * 32 : nullptr, ep.alpha);
+      qkv_linear_chunk(r2, x2, bias ? bias + (c + NC / 2) * 32 : nullptr, ep.alpha);
+      if (norm) {
+        qkv_scale_chunk(x1, rr, wn ? wn + c * 32 : nullptr);
+        qkv_scale_chunk(x2, rr, wn ? wn + (c + NC / 2) * 32 : nullptr);
+      }
+      if (cs != nullptr) {  // column i (< dh/2) pairs with i + dh/2, frequency i
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float cv[16], sv[16];
+          load_f32x16(cs + c * 32 + hh * 16, cv);
+          load_f32x16(sn + c * 32 + hh * 16, sv);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float a1 = x1[hh * 16 + j], a2 = x2[hh * 16 + j];
+            x1[hh * 16 + j] = a1 * cv[j] - a2 * sv[j];
+            x2[hh * 16 + j] = a2 * cv[j] + a1 * sv[j];
+          }
+        }
+      }
+      if (valid) {
+        for (int d = 0; d < ndst; ++d) {
+          __nv_bfloat16* p = dst(d);
+          store_bf16x32(p + c * 32, x1);
+          store_bf16x32(p + (c + NC / 2) * 32, x2);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One accumulator tile row (BN columns starting at col_base) of one thread:
+// TMEM -> registers -> epilogue.  `release()` runs once, right after the tile's
+// last TMEM load has completed (the accumulator may then be overwritten).
+template <int EPI, bool OUT_F32, int BN, class Rel>
+DFL_DEVICE void epilogue_tile(uint32_t tbase, int row, int col_base, int M, int N, const EpiParams& ep,
+                              Rel&& release) {
+  const int ncols = min(BN, N - col_base);
+  const int nch = (ncols + 31) / 32;  // warp-uniform
+  if constexpr (EPI == kEpiSwiGLU) {
+    // chunk pairs (h, g) of interleaved 32-column groups -> 32 output columns
+#pragma unroll 1
+    for (int c = 0; c < nch; c += 2) {
+      const int col0 = col_base + c * 32;
+      uint32_t rh[32], rg[32];
+      tmem_ld_32x32b_x32(tbase + c * 32, rh);
+      tmem_ld_32x32b_x32(tbase + (c + 1) * 32, rg);
+      tmem_wait_ld();
+      if (c + 2 >= nch) release();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float hv = __uint_as_float(rh[j]) * ep.alpha, gv = __uint_as_float(rg[j]) * ep.alpha;
+        if (ep.bias) {
+          hv += __bfloat162float(ep.bias[col0 + j]);
+          gv += __bfloat162float(ep.bias[col0 + 32 + j]);
+        }
+        rh[j] = __float_as_uint(hv * silu(gv));
+      }
+      epilogue_chunk<kEpiNone, OUT_F32, false>(rh, row, col0 / 2, M, N / 2, ep);
+    }
+  } else if constexpr (EPI == kEpiQkv) {
+#pragma unroll 1
+    for (int c = 0; c < nch;) {
+      const int col0 = col_base + c * 32;
+      int which = 0, h = 0;
+      if (qkv_locate(ep.qs, col0, which, h)) {
+        const int hc = ep.qs.dh / 32;
+        const bool last = c + hc >= nch;
+        if (hc == 4)
+          qkv_head_epilogue<128>(tbase + c * 32, row, M, col0, which, h, ep, last, release);
+        else
+          qkv_head_epilogue<64>(tbase + c * 32, row, M, col0, which, h, ep, last, release);
+        c += hc;
+      } else {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, r);
+        tmem_wait_ld();
+        if (c + 1 >= nch) release();
+        epilogue_chunk<kEpiGelu, false>(r, row, col0, M, N, ep);
+        ++c;
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < nch; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tbase + c * 32, r);
+      tmem_wait_ld();
+      if (c + 1 >= nch) release();
+      epilogue_chunk<EPI, OUT_F32>(r, row, col_base + c * 32, M, N, ep);
+    }
+  }
+}
+
 }  // namespace dfl
+
+// ---------------------------------------------------------------------------
+// Host: GemmArgs -> EpiParams with the argument checks shared by every GEMM.
+namespace dfl_host {
+
+inline bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }
+
+// kEpiQkv plan checks: the fused head scatter covers per-head RMS (or none), full-width
+// RoPE, dh 64 / 128, head blocks aligned to dh inside [0, N), bf16 output, no row scatter.
+inline int check_qkv_plan(const GemmArgs& a) {
+  const QkvScatterArgs* q = a.qkv;
+  if (q == nullptr || a.out_f32 || a.out_world > 0) return -20;
+  if (q->dh != 64 && q->dh != 128) return -21;
+  if (q->norm_mode != 0 && q->norm_mode != 1) return -22;
+  if (q->rope_dims != 0 && q->rope_dims != q->dh) return -23;
+  if ((q->cos_t == nullptr) != (q->sin_t == nullptr)) return -23;
+  if (q->cos_t && (misaligned16(q->cos_t) || misaligned16(q->sin_t))) return -23;
+  if (q->S_src <= 0 || q->H <= 0 || q->heads_per_rank <= 0 || q->world < 1 || q->world > DFL_MAX_PEERS) return -24;
+  if (q->norm_mode == 1 && ((q->wq && misaligned16(q->wq)) || (q->wk && misaligned16(q->wk)))) return -25;
+  const int offs[3] = {q->q_off, q->k_off, q->v_off};
+  void* const* dsts[3] = {q->q_dst, q->k_dst, q->v_dst};
+  long long covered = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (offs[i] < 0) continue;
+    if (offs[i] % q->dh || (long long)offs[i] + (long long)q->H * q->dh > a.N) return -26;
+    covered += (long long)q->H * q->dh;
+    // destinations written: q_dst[0] / all ranks (gather-KV replication), else one per head owner
+    const int nd = q->kv_replicate ? (i == 0 ? 1 : q->world) : (q->H + q->heads_per_rank - 1) / q->heads_per_rank;
+    if (nd > q->world) return -24;
+    for (int d = 0; d < nd; ++d)
+      if (dsts[i][d] == nullptr || misaligned16(dsts[i][d])) return -27;
+  }
+  if (a.D == nullptr && covered != a.N) return -28;  // columns outside q / k / v need D
+  return 0;
+}
+
+inline int fill_epi_params(const GemmArgs& a, dfl::EpiParams& ep) {
+  std::memset(&ep, 0, sizeof(ep));
+  ep.D = a.D;
+  ep.ldd = a.ldd;
+  ep.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  ep.act_lo = a.act_lo;
+  ep.act_hi = a.act_hi;
+  ep.gate = a.gate;
+  ep.gate_bstride = a.gate_bstride;
+  ep.rows_per_batch = a.rows_per_batch > 0 ? a.rows_per_batch : a.M;
+  ep.gate_row_map = a.gate_row_map;
+  ep.resid = reinterpret_cast<const __nv_bfloat16*>(a.resid);
+  ep.ldr = a.ldr;
+  ep.alpha = a.alpha;
+  if (a.out_world < 0 || a.out_world > DFL_MAX_PEERS) return -9;
+  ep.out_world = a.out_world;
+  ep.rows_per_rank = a.rows_per_rank > 0 ? a.rows_per_rank : a.M;
+  ep.peer_row_off = a.peer_row_off;
+  for (int r = 0; r < DFL_MAX_PEERS; ++r) ep.out_peer[r] = r < a.out_world ? a.out_peer[r] : nullptr;
+  if (a.epi == kEpiSwiGLU && (a.N % 64 || a.out_world > 0)) return -11;
+  if (a.epi == kEpiQkv) {
+    const int rc = check_qkv_plan(a);
+    if (rc) return rc;
+    ep.qs = *a.qkv;
+  }
+  return 0;
+}
+
+}  // namespace dfl_host

@@ -10,9 +10,14 @@
 extern "C" {
 #endif
 
-enum { kEpiNone = 0, kEpiGelu = 1, kEpiGateResid = 2, kEpiSilu = 3, kEpiSwiGLU = 4 };
+enum { kEpiNone = 0, kEpiGelu = 1, kEpiGateResid = 2, kEpiSilu = 3, kEpiSwiGLU = 4, kEpiQkv = 5 };
 // kEpiSwiGLU: the weight rows are interleaved in 32-row groups [h_32 | g_32] and the
 // GEMM writes N/2 columns  out = (h + b_h) * silu(g + b_g).
+// kEpiQkv: the q / k / v column blocks named by GemmArgs.qkv are normalised, rotated and
+// scattered by head exactly as dfl_qkv_scatter would do on the stored rows (no round trip
+// through D); every other column takes the GELU window epilogue into D.
+
+struct QkvScatterArgs;
 
 #define DFL_MAX_PEERS 8
 
@@ -43,6 +48,10 @@ typedef struct GemmArgs {
   long long peer_row_off;
   // 0: automatic choice, 1: one CTA per 128 x BN tile, 2: CTA pairs (cta_group::2, 256 x 256 tiles)
   int cta_mode;
+  // kEpiQkv: the head scatter applied in the epilogue (its qkv / ld / rows fields are unused;
+  // the source rows are the GEMM rows).  Per-head RMS (norm_mode 0 / 1), full-width RoPE,
+  // dh 64 or 128, column offsets multiples of dh.
+  const struct QkvScatterArgs* qkv;
 } GemmArgs;
 
 int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream);
@@ -118,6 +127,10 @@ typedef struct QkvScatterArgs {
   // Rotary applied to the first rope_dims channels of each head (half-split pairs
   // (i, i + rope_dims/2)), the rest passed through; 0 = all dh channels.
   int rope_dims;
+  // Two-segment rows (a rank's [text ; image] slice of a joint sequence): source rows
+  // s >= seg_rows of each batch land at seg1_seq_off + (s - seg_rows) and use RoPE
+  // table row seg1_rope_off + (s - seg_rows).  0 = one segment.
+  int seg_rows, seg1_seq_off, seg1_rope_off;
 } QkvScatterArgs;
 int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream);
 

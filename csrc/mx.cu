@@ -277,19 +277,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mb * BM + sub * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16);
-      // Chunk by chunk; TMEM is released once the last chunk is in registers.
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c * 32, r);
-        tmem_wait_ld();
-        if (c == BN / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive(tempty_bar);
-        }
-        const int col0 = nb * BN + c * 32;
-        if (col0 < N) epilogue_chunk<EPI, OUT_F32>(r, row, col0, M, N, ep);
-      }
+      // TMEM is released once the tile's last chunk is in registers.
+      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, M, N, ep, [&]() {
+        tc_fence_before();
+        mbar_arrive(tempty_bar);
+      });
       acc_phase ^= 1u;
     }
   }
@@ -356,6 +348,7 @@ extern "C" int dfl_gemm_mx(const MxGemmArgs* a, cudaStream_t stream) {
   if (g.lda % 16 || g.ldb % 16) return -4;
   if ((reinterpret_cast<uintptr_t>(a->sfa) | reinterpret_cast<uintptr_t>(a->sfb)) & 15) return -10;
   const void* dchk = g.out_world > 0 ? g.out_peer[0] : g.D;
+  if (g.epi == kEpiQkv && g.D == nullptr) dchk = nullptr;  // every column goes to the head scatter
   if (!g.out_f32 && ((g.ldd % 8) || (reinterpret_cast<uintptr_t>(dchk) & 15))) return -6;
   if (g.out_f32 && ((g.ldd % 4) || (reinterpret_cast<uintptr_t>(dchk) & 15))) return -6;
   if (g.bias && (reinterpret_cast<uintptr_t>(g.bias) & 15)) return -7;
@@ -369,22 +362,8 @@ extern "C" int dfl_gemm_mx(const MxGemmArgs* a, cudaStream_t stream) {
   rc = make_tmap_2d_u8(&tb, g.B, g.K, g.N, g.ldb, BK, BN);
   if (rc) return 2000 + rc;
   EpiParams ep;
-  ep.D = g.D;
-  ep.ldd = g.ldd;
-  ep.bias = reinterpret_cast<const __nv_bfloat16*>(g.bias);
-  ep.act_lo = g.act_lo;
-  ep.act_hi = g.act_hi;
-  ep.gate = g.gate;
-  ep.gate_bstride = g.gate_bstride;
-  ep.rows_per_batch = g.rows_per_batch > 0 ? g.rows_per_batch : g.M;
-  ep.gate_row_map = g.gate_row_map;
-  ep.resid = reinterpret_cast<const __nv_bfloat16*>(g.resid);
-  ep.ldr = g.ldr;
-  ep.alpha = g.alpha;
-  ep.out_world = g.out_world;
-  ep.rows_per_rank = g.rows_per_rank > 0 ? g.rows_per_rank : g.M;
-  ep.peer_row_off = g.peer_row_off;
-  for (int r = 0; r < DFL_MAX_PEERS; ++r) ep.out_peer[r] = r < g.out_world ? g.out_peer[r] : nullptr;
+  rc = dfl_host::fill_epi_params(g, ep);
+  if (rc) return rc;
   switch (g.epi) {
     case kEpiNone:
       return g.out_f32 ? launch_mx<kEpiNone, true>(ta, tb, a, ep, stream, dev)
@@ -395,6 +374,8 @@ extern "C" int dfl_gemm_mx(const MxGemmArgs* a, cudaStream_t stream) {
       return launch_mx<kEpiSilu, false>(ta, tb, a, ep, stream, dev);
     case kEpiGateResid:
       return launch_mx<kEpiGateResid, false>(ta, tb, a, ep, stream, dev);
+    case kEpiQkv:
+      return launch_mx<kEpiQkv, false>(ta, tb, a, ep, stream, dev);
     default:
       return -1;
   }

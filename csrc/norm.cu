@@ -204,10 +204,12 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
   const int s = row % a.S_src;
   const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + (long long)row * a.ld;
   const int H_local = a.heads_per_rank;
-  const int dpos = a.seq_off + s;
+  const bool seg1 = a.seg_rows > 0 && s >= a.seg_rows;
+  const int dpos = seg1 ? a.seg1_seq_off + (s - a.seg_rows) : a.seq_off + s;
+  const int rpos = seg1 ? a.seg1_rope_off + (s - a.seg_rows) : a.rope_pos_off + s;
   const int rope_row = (a.rope_heads > 0 ? a.rope_heads : 1) * ((a.rope_dims > 0 ? a.rope_dims : DH) / 2);
-  const float* cos_row = a.cos_t ? a.cos_t + (long long)(a.rope_pos_off + s) * rope_row : nullptr;
-  const float* sin_row = a.sin_t ? a.sin_t + (long long)(a.rope_pos_off + s) * rope_row : nullptr;
+  const float* cos_row = a.cos_t ? a.cos_t + (long long)rpos * rope_row : nullptr;
+  const float* sin_row = a.sin_t ? a.sin_t + (long long)rpos * rope_row : nullptr;
   __shared__ float red[2][4];
 
   // Across-heads RMS (mode 2): sum of squares over the whole q (and k) row.

@@ -66,6 +66,8 @@ environment_variables: dict[str, Callable[[], Any]] = {
     "DIFFLET_KERNEL_GEMM": lambda: _str(os.environ.get("DIFFLET_KERNEL_GEMM"), "native"),
     # 1: wide GEMMs with M >= 1024 run on CTA pairs (cta_group::2, 256 x 256 tiles); 0: one CTA per tile
     "DIFFLET_GEMM_PAIR": lambda: _str(os.environ.get("DIFFLET_GEMM_PAIR"), "1"),
+    # 1: q/k RMSNorm + RoPE + head scatter run in the qkv projection's GEMM epilogue; 0: separate kernel
+    "DIFFLET_FUSE_QKV": lambda: _str(os.environ.get("DIFFLET_FUSE_QKV"), "1"),
     # serving
     "DIFFLET_API_KEY": lambda: _str(os.environ.get("DIFFLET_API_KEY"), None),
     "DIFFLET_SERVE_QUEUE_TIMEOUT_S": lambda: _float(os.environ.get("DIFFLET_SERVE_QUEUE_TIMEOUT_S"), 30.0),

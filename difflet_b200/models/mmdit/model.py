@@ -365,10 +365,12 @@ class MMDiT:
                 o = cfg.double_mod_offset(i, st)
                 nb = norm[: B * nr]
                 ln(xs, nb, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=nr)
-                F.linear(nb, w[p + st + "_qkv.w"], w[p + st + "_qkv.b"], out=ws["qkv_" + st])
-                F.qkv_scatter(ws["qkv_" + st], q_off=0, k_off=Dl, v_off=2 * Dl, S_src=nr, H=Ht, dh=dh,
-                              **dst(q, k, v, row_of[st], pos), norm_mode=1, wq=w[p + st + "_qnorm"],
-                              wk=w[p + st + "_knorm"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos)
+                # qkv projection with q/k RMSNorm + RoPE + head scatter (the Ulysses all-to-all under
+                # CP) in its epilogue
+                F.linear_qkv(nb, w[p + st + "_qkv.w"], w[p + st + "_qkv.b"], out=ws["qkv_" + st],
+                             scatter=dict(q_off=0, k_off=Dl, v_off=2 * Dl, S_src=nr, H=Ht, dh=dh,
+                                          **dst(q, k, v, row_of[st], pos), norm_mode=1, wq=w[p + st + "_qnorm"],
+                                          wk=w[p + st + "_knorm"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos))
             self._attention(ws, B, S_txt, S_img, D, Hl, dh, kv_lo=kv_lo, kv_hi=kv_hi)
             for st in ("img", "txt"):
                 xs, nr = xs_of[st], n_of[st]
@@ -396,21 +398,18 @@ class MMDiT:
             p = f"single.{j}."
             o = cfg.single_mod_offset(j)
             ln(x2, norm, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=S_loc)
-            F.linear(norm, w[p + "fused.w"], w[p + "fused.b"], out=fused, act="gelu", act_lo=Dl, act_hi=Dl + Fl)
-            if par is None:  # positions equal local rows: one pass over every row
-                F.qkv_scatter(fused, q_off=0, k_off=Dl + Fl, v_off=2 * Dl + Fl, S_src=S_loc, H=Ht, dh=dh,
-                              q_dst=[q], k_dst=[k], v_dst=[v], S_dst=S, seq_off=0, norm_mode=1,
-                              wq=w[p + "qnorm"], wk=w[p + "knorm"], eps=eps, cos=cos, sin=sin, rope_pos_off=0,
-                              heads_per_rank=Ht)
-            else:
-                for b in range(B):
-                    rows = fused[b * S_loc:(b + 1) * S_loc]
-                    for st in (s0, s1):
-                        r0, nr, pos = row_of[st], n_of[st], pos_of[st]
-                        F.qkv_scatter(rows[r0:r0 + nr], q_off=0, k_off=D + F_, v_off=2 * D + F_, S_src=nr, H=H,
-                                      dh=dh, **dst(q[b:b + 1], k[b:b + 1], v[b:b + 1], r0, pos), norm_mode=1,
-                                      wq=w[p + "qnorm"], wk=w[p + "knorm"], eps=eps, cos=cos, sin=sin,
-                                      rope_pos_off=pos)
+            # [q | mlp | k | v] projection: GELU on the MLP columns (kept in `fused` next to the
+            # attention output slot), q/k/v normalised, rotated and scattered by head in the epilogue
+            if par is None:  # positions equal local rows
+                place = dict(q_dst=[q], k_dst=[k], v_dst=[v], S_dst=S, seq_off=0, rope_pos_off=0, heads_per_rank=Ht)
+            else:  # this rank's [seg0 ; seg1] rows: each segment placed as the CP mode lays it out
+                place = dst(q, k, v, row_of[s0], pos_of[s0])
+                place.update(rope_pos_off=pos_of[s0], seg_rows=n_of[s0],
+                             seg1_seq_off=dst(q, k, v, row_of[s1], pos_of[s1])["seq_off"], seg1_rope_off=pos_of[s1])
+            F.linear_qkv(norm, w[p + "fused.w"], w[p + "fused.b"], out=fused, act="gelu", act_lo=Dl, act_hi=Dl + Fl,
+                         scatter=dict(q_off=0, k_off=Dl + Fl, v_off=2 * Dl + Fl, S_src=S_loc, H=Ht, dh=dh,
+                                      norm_mode=1, wq=w[p + "qnorm"], wk=w[p + "knorm"], eps=eps, cos=cos, sin=sin,
+                                      **place))
             self._attention(ws, B, S_txt, S_img, D, Hl, dh, out_rows=fused, kv_lo=kv_lo, kv_hi=kv_hi)
             row_linear(fused[:, : Dl + Fl], w[p + "proj.w"], w[p + "proj.b"], x2, mslice(o + 2 * D), S_loc)
 

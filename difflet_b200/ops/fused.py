@@ -12,6 +12,8 @@ Ops:
   ln_modulate   LayerNorm / RMSNorm (+affine) (* (1 + scale) + shift)
   qkv_scatter   per-head / across-heads q,k RMSNorm + RoPE + scatter to
                 head-major (or token-major) destinations, one per rank
+  linear_qkv    linear whose q/k/v column blocks go through qkv_scatter inside the
+                GEMM epilogue (no round trip of the qkv rows through HBM)
   attention     softmax(scale q k^T) v with key window and LSE
   gemv          modulation linears (M <= 8), f32 in/out, optional SiLU
   euler_step    x += dt * (u + s (c - u)) on f32 latents (+ bf16 mirror)
@@ -27,7 +29,7 @@ import torch.nn.functional as F
 
 from difflet_b200 import envs
 
-EPI_NONE, EPI_GELU, EPI_GATE_RESID, EPI_SILU, EPI_SWIGLU = 0, 1, 2, 3, 4
+EPI_NONE, EPI_GELU, EPI_GATE_RESID, EPI_SILU, EPI_SWIGLU, EPI_QKV = 0, 1, 2, 3, 4, 5
 _ACT = {None: EPI_NONE, "none": EPI_NONE, "gelu": EPI_GELU, "gelu_tanh": EPI_GELU, "silu": EPI_SILU,
         "swiglu": EPI_SWIGLU}
 
@@ -46,15 +48,20 @@ _nat = None
 LAUNCHES = [0]
 
 
-def native():
+def _lib():
+    """The native module, without counting a launch (host-only helpers)."""
     global _nat
     if _nat is None:
         from difflet_b200 import _native
 
         _nat = _native.require()
         _nat.gemm_set_pair_auto(envs.DIFFLET_GEMM_PAIR != "0")
-    LAUNCHES[0] += 1
     return _nat
+
+
+def native():
+    LAUNCHES[0] += 1
+    return _lib()
 
 
 def _rows2d(x: torch.Tensor) -> torch.Tensor:
@@ -198,7 +205,7 @@ def _rope_cpu(x, cos, sin, half):
 def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, S_dst, seq_off=0,
                 norm_mode=1, wq=None, wk=None, eps=1e-6, cos=None, sin=None, rope_pos_off=0,
                 rope_half=False, heads_per_rank=None, token_major=False, kv_replicate=False, q_S_dst=0,
-                q_seq_off=0):
+                q_seq_off=0, seg_rows=0, seg1_seq_off=0, seg1_rope_off=0):
     """Normalise + rotate q/k of a token-major qkv buffer and scatter q/k/v by head.
 
     ``q_dst`` etc. are lists (one tensor per destination rank; a single-GPU call
@@ -207,7 +214,9 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
     position ``seq_off + s``.  ``heads_per_rank`` splits heads over the list.
     ``kv_replicate`` (gather-KV context parallelism): k and v of all heads go to
     every destination, q only to ``q_dst[0]`` ([B, H, q_S_dst, dh], row
-    ``q_seq_off + s``).
+    ``q_seq_off + s``).  ``seg_rows`` > 0: rows ``s >= seg_rows`` of each batch form a
+    second segment placed at ``seg1_seq_off + (s - seg_rows)`` with RoPE row
+    ``seg1_rope_off + (s - seg_rows)`` (a rank's [text ; image] slice of a joint sequence).
     """
     qkv2 = _rows2d(qkv)
     world = len(q_dst if q_dst is not None else (k_dst if k_dst is not None else v_dst))
@@ -217,10 +226,23 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
     k_dst = k_dst if k_dst is not None else [None] * world
     v_dst = v_dst if v_dst is not None else [None] * world
     if qkv2.is_cuda:
-        ptr = lambda ts: [0 if t is None else (t if isinstance(t, int) else t.data_ptr()) for t in ts]  # noqa: E731
-        native().qkv_scatter(qkv2, q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos, sin,
-                             rope_pos_off, rope_half, hpr, ptr(q_dst), ptr(k_dst), ptr(v_dst), S_dst,
-                             seq_off, token_major, kv_replicate, q_S_dst, q_seq_off)
+        native().qkv_scatter(qkv2, *_scatter_args(q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, S_dst,
+                                                  seq_off, norm_mode, wq, wk, eps, cos, sin, rope_pos_off, rope_half,
+                                                  hpr, token_major, kv_replicate, q_S_dst, q_seq_off, seg_rows,
+                                                  seg1_seq_off, seg1_rope_off))
+        return
+    if 0 < seg_rows < S_src:  # oracle: one call per segment
+        Bn = qkv2.shape[0] // S_src
+        x3 = qkv2.view(Bn, S_src, -1)
+        common = dict(q_off=q_off, k_off=k_off, v_off=v_off, H=H, dh=dh, q_dst=q_dst, k_dst=k_dst, v_dst=v_dst,
+                      S_dst=S_dst, norm_mode=norm_mode, wq=wq, wk=wk, eps=eps, cos=cos, sin=sin, rope_half=rope_half,
+                      heads_per_rank=heads_per_rank, token_major=token_major, kv_replicate=kv_replicate,
+                      q_S_dst=q_S_dst)
+        n1 = S_src - seg_rows
+        qkv_scatter(x3[:, :seg_rows].reshape(Bn * seg_rows, -1), S_src=seg_rows, seq_off=seq_off,
+                    rope_pos_off=rope_pos_off, q_seq_off=q_seq_off, **common)
+        qkv_scatter(x3[:, seg_rows:].reshape(Bn * n1, -1), S_src=n1, seq_off=seg1_seq_off,
+                    rope_pos_off=seg1_rope_off, q_seq_off=q_seq_off + seg_rows, **common)
         return
     rows = qkv2.shape[0]
     B = rows // S_src
@@ -278,6 +300,67 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
                 dst.view(B, S_dst, hpr, dh)[:, seq_off:seq_off + S_src] = part.permute(0, 2, 1, 3).to(dst.dtype)
             else:
                 dst[:, :, seq_off:seq_off + S_src] = part.to(dst.dtype)
+
+
+def _scatter_args(q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, S_dst, seq_off, norm_mode, wq, wk, eps,
+                  cos, sin, rope_pos_off, rope_half, hpr, token_major, kv_replicate, q_S_dst, q_seq_off, seg_rows=0,
+                  seg1_seq_off=0, seg1_rope_off=0):
+    """Positional arguments of the native head scatter (after the source rows)."""
+    ptr = lambda ts: [0 if t is None else (t if isinstance(t, int) else t.data_ptr()) for t in ts]  # noqa: E731
+    return (q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos, sin, rope_pos_off, rope_half, hpr,
+            ptr(q_dst), ptr(k_dst), ptr(v_dst), S_dst, seq_off, token_major, kv_replicate, q_S_dst, q_seq_off,
+            seg_rows, seg1_seq_off, seg1_rope_off)
+
+
+def _qkv_epilogue_ok(sc: dict, act) -> bool:
+    """The GEMM epilogue covers per-head RMS (or none), full-width RoPE, dh 64 / 128 and
+    head blocks aligned to dh; anything else runs the standalone scatter kernel."""
+    if envs.DIFFLET_FUSE_QKV == "0" or envs.DIFFLET_KERNEL_GEMM == "cublas" or act not in (None, "none", "gelu"):
+        return False
+    dh, H = sc["dh"], sc["H"]
+    if dh not in (64, 128) or sc.get("norm_mode", 1) not in (0, 1):
+        return False
+    if any(o >= 0 and o % dh for o in (sc["q_off"], sc["k_off"], sc["v_off"])):
+        return False
+    cos = sc.get("cos")
+    return cos is None or cos.shape[-1] in (dh // 2, H * dh // 2)
+
+
+def linear_qkv(x, w, b=None, *, scatter: dict, out=None, act=None, act_lo=0, act_hi=None):
+    """``linear`` whose q / k / v column blocks are consumed by ``qkv_scatter(**scatter)``.
+
+    On the GPU the head scatter (per-head q/k RMSNorm, RoPE, store by head into every
+    destination rank's buffer) runs in the GEMM epilogue straight from the tensor-memory
+    accumulator; the other columns get ``act`` on [act_lo, act_hi) and land in the same
+    columns of ``out`` (which may be None when q, k and v cover every column).  The
+    qkv columns of ``out`` are left unwritten on that path.  Otherwise (CPU oracle,
+    unsupported scatter options) the full projection is stored and scattered.
+    """
+    x2 = _rows2d(x)
+    N = w.shape[0]
+    act_hi = N if act_hi is None else act_hi
+    if x2.is_cuda and _qkv_epilogue_ok(scatter, act) and not (isinstance(w, MXWeight) and w.compute != "mx"):
+        sc = dict(scatter)
+        world = len(next(d for d in (sc.get("q_dst"), sc.get("k_dst"), sc.get("v_dst")) if d is not None))
+        kv_rep = sc.get("kv_replicate", False)
+        hpr = sc["H"] if kv_rep else (sc.get("heads_per_rank") or sc["H"] // world)
+        dst = [sc.get(k) if sc.get(k) is not None else [None] * world for k in ("q_dst", "k_dst", "v_dst")]
+        plan = _lib().qkv_plan(*_scatter_args(
+            sc["q_off"], sc["k_off"], sc["v_off"], sc["S_src"], sc["H"], sc["dh"], dst[0], dst[1], dst[2],
+            sc["S_dst"], sc.get("seq_off", 0), sc.get("norm_mode", 1), sc.get("wq"), sc.get("wk"),
+            sc.get("eps", 1e-6), sc.get("cos"), sc.get("sin"), sc.get("rope_pos_off", 0), sc.get("rope_half", False),
+            hpr, sc.get("token_major", False), kv_rep, sc.get("q_S_dst", 0), sc.get("q_seq_off", 0),
+            sc.get("seg_rows", 0), sc.get("seg1_seq_off", 0), sc.get("seg1_rope_off", 0)))
+        lo, hi = (act_lo, act_hi) if act == "gelu" else (0, 0)  # non-qkv columns: GELU window or identity
+        if isinstance(w, MXWeight):
+            xq, xs = mx_quantize(x2, blocked=True)
+            native().gemm_mx(xq, xs, w.q, w.sf, b, out, EPI_QKV, lo, hi, None, 0, None, 1.0, False, qkv_plan=plan)
+        else:
+            native().gemm(x2, w, b, out, EPI_QKV, lo, hi, None, 0, None, 1.0, False, qkv_plan=plan)
+        return out
+    y = linear(x2, w, b, out=out, act=act, act_lo=act_lo, act_hi=act_hi)
+    qkv_scatter(y, **scatter)
+    return out if out is not None else y
 
 
 def attention(q, k, v, scale, *, out=None, lse=None, kv_lo=None, kv_hi=None):

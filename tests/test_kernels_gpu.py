@@ -105,7 +105,7 @@ def test_qkv_scatter_norm_rope(native, dh):
     k = torch.zeros_like(q)
     v = torch.zeros_like(q)
     native.qkv_scatter(qkv, 0, D, 2 * D, S, H, dh, 1, wq, wk, 1e-6, cos, sin, off, False, H,
-                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S_dst, off, False, False, 0, 0)
+                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S_dst, off, False, False, 0, 0, 0, 0, 0)
     torch.cuda.synchronize()
     x = qkv.float().view(B, S, 3, H, dh).permute(2, 0, 3, 1, 4)  # 3,B,H,S,dh
 
@@ -132,7 +132,7 @@ def test_qkv_scatter_across_heads_half_rope(native):
     k = torch.empty_like(q)
     v = torch.empty_like(q)
     native.qkv_scatter(qkv, 0, D, 2 * D, S, H, dh, 2, wq, wk, 1e-6, cos, sin, 0, True, H,
-                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S, 0, True, False, 0, 0)
+                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S, 0, True, False, 0, 0, 0, 0, 0)
     torch.cuda.synchronize()
     x = qkv.float().view(S, 3, D)
     qn = x[:, 0] * torch.rsqrt(x[:, 0].pow(2).mean(-1, keepdim=True) + 1e-6) * wq.float()
