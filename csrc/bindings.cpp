@@ -7,6 +7,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <string>
 #include <vector>
 
 #include "kernels.h"
@@ -164,6 +165,46 @@ std::vector<at::Tensor> mx_quantize(const at::Tensor& x, bool blocked) {
                                sf.data_ptr(), blocked ? 1 : 0, cur_stream()),
                "mx_quantize");
   return {q, sf};
+}
+
+// Grouped GEMM: problem i is gemm(A[i], B[i], bias[i], out[i], epi, ...); one launch.
+std::vector<at::Tensor> gemm_group(std::vector<at::Tensor> A, std::vector<at::Tensor> B,
+                                   std::vector<c10::optional<at::Tensor>> bias,
+                                   std::vector<c10::optional<at::Tensor>> out, int64_t epi, std::vector<int64_t> act_lo,
+                                   std::vector<int64_t> act_hi, std::vector<c10::optional<at::Tensor>> gate,
+                                   std::vector<int64_t> rows_per_batch, std::vector<c10::optional<at::Tensor>> resid,
+                                   std::vector<std::string> qkv_plan, int64_t cta_mode) {
+  const size_t n = A.size();
+  TORCH_CHECK(n >= 1 && n <= 2 && B.size() == n && bias.size() == n && out.size() == n && act_lo.size() == n &&
+                  act_hi.size() == n && gate.size() == n && rows_per_batch.size() == n && resid.size() == n &&
+                  qkv_plan.size() == n,
+              "gemm_group: 1 or 2 problems, one entry per problem in every list");
+  const c10::cuda::CUDAGuard guard(A[0].device());
+  std::vector<GemmArgs> args(n);
+  std::vector<at::Tensor> outs;
+  for (size_t i = 0; i < n; ++i) {
+    check_bf16_cuda(A[i], "A");
+    check_bf16_cuda(B[i], "B");
+    check_rowmajor(A[i], "A");
+    check_rowmajor(B[i], "B");
+    TORCH_CHECK(A[i].size(1) == B[i].size(1), "K mismatch in problem ", i);
+    TORCH_CHECK(A[i].device() == A[0].device(), "all problems on one device");
+    GemmArgs& a = args[i];
+    a = GemmArgs{};
+    outs.push_back(gemm_epilogue_args(a, A[i], A[i].size(0), B[i].size(0), bias[i], out[i], epi, act_lo[i],
+                                      act_hi[i], gate[i], rows_per_batch[i], resid[i], 1.0, false, {}, 0, 0, 0,
+                                      c10::nullopt, qkv_plan[i]));
+    a.A = A[i].data_ptr();
+    a.B = B[i].data_ptr();
+    a.lda = A[i].stride(0);
+    a.ldb = B[i].stride(0);
+    a.K = (int)A[i].size(1);
+    a.cta_mode = (int)cta_mode;
+  }
+  std::vector<const GemmArgs*> ptrs;
+  for (auto& a : args) ptrs.push_back(&a);
+  DFL_CHECK_RC(dfl_gemm_bf16_group(ptrs.data(), (int)n, cur_stream()), "gemm_group");
+  return outs;
 }
 
 at::Tensor gemm_mx(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B, const at::Tensor& sfb,
@@ -658,6 +699,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_f32") = false, py::arg("out_peer") = std::vector<int64_t>{}, py::arg("rows_per_rank") = 0,
         py::arg("peer_row_off") = 0, py::arg("ldd") = 0, py::arg("gate_row_map") = py::none(),
         py::arg("cta_mode") = 0, py::arg("qkv_plan") = py::bytes());
+  m.def("gemm_group", &gemm_group, "grouped tcgen05 GEMMs (one launch)", py::arg("A"), py::arg("B"),
+        py::arg("bias"), py::arg("out"), py::arg("epi"), py::arg("act_lo"), py::arg("act_hi"), py::arg("gate"),
+        py::arg("rows_per_batch"), py::arg("resid"), py::arg("qkv_plan"), py::arg("cta_mode") = 0);
   m.def("mx_quantize", &mx_quantize, py::arg("x"), py::arg("blocked") = false);
   m.def("gemm_mx", &gemm_mx, "block-scaled MXFP8 tcgen05 GEMM", py::arg("A"), py::arg("sfa"), py::arg("B"),
         py::arg("sfb"), py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,

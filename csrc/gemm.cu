@@ -16,6 +16,7 @@
 // residual of the FLUX blocks (difflet/models/flux/modeling_flux.py:712,
 // 721-729, 844-867).
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -43,9 +44,7 @@ struct Smem {
 
 template <int BN, int STAGES, int EPI, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                        const __grid_constant__ CUtensorMap tmap_b, int M, int N, int K,
-                        EpiParams ep, int* err) {
+    gemm_tcgen05_kernel(const __grid_constant__ GemmGroup grp, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzle atoms
@@ -60,10 +59,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int num_m = (M + BM - 1) / BM;
-  const int num_n = (N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
-  const int num_k = (K + BK - 1) / BK;
+  const int num_tiles = grp.total_tiles;
   constexpr uint32_t kTmemCols = 2 * BN;
 
   if (threadIdx.x == 0) {
@@ -78,8 +74,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_shared();
-    prefetch_tmap(&tmap_a);
-    prefetch_tmap(&tmap_b);
+    for (int i = 0; i < grp.count; ++i) {
+      prefetch_tmap(&grp.p[i].ta);
+      prefetch_tmap(&grp.p[i].tb);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -99,8 +97,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        int lt, mb, nb;
+        const GemmProblem& P = group_tile(grp, t, lt);
+        tile_coords(lt, P.num_m, P.num_n, mb, nb);
+        const int num_k = (P.K + BK - 1) / BK;
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kKidGemm, 10 + stage, abort_flag)) {
             ok = false;
@@ -109,8 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-          tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, mb * BM);
-          tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, nb * BN);
+          tma_load_2d(sa, &P.ta, &full_bar[stage], kb * BK, mb * BM);
+          tma_load_2d(sb, &P.tb, &full_bar[stage], kb * BK, nb * BN);
           issued[stage] = true;
           issued_parity[stage] = phase;
           if (++stage == STAGES) {
@@ -140,6 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        int lt;
+        const int num_k = (group_tile(grp, t, lt).K + BK - 1) / BK;
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, err, kKidGemm, 30 + stage, abort_flag)) {
             ok = false;
@@ -172,13 +174,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      int lt, mb, nb;
+      const GemmProblem& P = group_tile(grp, t, lt);
+      tile_coords(lt, P.num_m, P.num_n, mb, nb);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err, kKidGemm, 40 + acc, abort_flag)) break;
       tc_fence_after();
       const int row = mb * BM + sub * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
-      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, M, N, ep, [&]() {
+      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, P.M, P.N, P.ep, [&]() {
         tc_fence_before();
         mbar_arrive(&tempty_bar[acc]);
       });
@@ -194,8 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, int STAGES, int EPI, bool OUT_F32>
-int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
-                   const EpiParams& ep, int* err, cudaStream_t stream, int device) {
+int launch_variant(const GemmGroup& g, int* err, cudaStream_t stream, int device) {
   using S = Smem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI, OUT_F32>;
   static bool attr_set[16] = {false};
@@ -204,52 +206,40 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
     if (e != cudaSuccess) return (int)e;
     attr_set[device & 15] = true;
   }
-  int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  int grid = tiles < dfl_host::num_sms(device) ? tiles : dfl_host::num_sms(device);
-  kern<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, M, N, K, ep, err);
+  const int sms = dfl_host::num_sms(device);
+  const int grid = g.total_tiles < sms ? g.total_tiles : sms;
+  kern<<<grid, kThreads, S::kTotal, stream>>>(g, err);
   return (int)cudaGetLastError();
 }
 
 template <int BN, int STAGES>
-int dispatch_epi(int epi, bool out_f32, const CUtensorMap& ta, const CUtensorMap& tb, int M,
-                 int N, int K, const EpiParams& ep, int* err, cudaStream_t s, int dev) {
+int dispatch_epi(int epi, bool out_f32, const GemmGroup& g, int* err, cudaStream_t s, int dev) {
   switch (epi) {
     case kEpiNone:
-      return out_f32 ? launch_variant<BN, STAGES, kEpiNone, true>(ta, tb, M, N, K, ep, err, s, dev)
-                     : launch_variant<BN, STAGES, kEpiNone, false>(ta, tb, M, N, K, ep, err, s, dev);
+      return out_f32 ? launch_variant<BN, STAGES, kEpiNone, true>(g, err, s, dev)
+                     : launch_variant<BN, STAGES, kEpiNone, false>(g, err, s, dev);
     case kEpiGelu:
-      return launch_variant<BN, STAGES, kEpiGelu, false>(ta, tb, M, N, K, ep, err, s, dev);
+      return launch_variant<BN, STAGES, kEpiGelu, false>(g, err, s, dev);
     case kEpiSilu:
-      return launch_variant<BN, STAGES, kEpiSilu, false>(ta, tb, M, N, K, ep, err, s, dev);
+      return launch_variant<BN, STAGES, kEpiSilu, false>(g, err, s, dev);
     case kEpiGateResid:
-      return launch_variant<BN, STAGES, kEpiGateResid, false>(ta, tb, M, N, K, ep, err, s, dev);
+      return launch_variant<BN, STAGES, kEpiGateResid, false>(g, err, s, dev);
     case kEpiSwiGLU:
-      return launch_variant<BN, STAGES, kEpiSwiGLU, false>(ta, tb, M, N, K, ep, err, s, dev);
+      return launch_variant<BN, STAGES, kEpiSwiGLU, false>(g, err, s, dev);
     case kEpiQkv:
-      return launch_variant<BN, STAGES, kEpiQkv, false>(ta, tb, M, N, K, ep, err, s, dev);
+      return launch_variant<BN, STAGES, kEpiQkv, false>(g, err, s, dev);
     default:
       return -1;
   }
 }
 
-}  // namespace
-
-extern "C" int dfl_gemm_pair_launch(const void* ta, const void* tb, int M, int N, int K, const void* ep, int epi,
-                                    int out_f32, int* err, cudaStream_t stream, int dev);
-
-// Automatic choice of the CTA-pair kernel for wide GEMMs with M >= 1024 (on by default;
-// dfl_gemm_set_pair_auto(0) restores the one-CTA kernel everywhere).
-static int g_pair_auto = 1;
-extern "C" void dfl_gemm_set_pair_auto(int on) { g_pair_auto = on; }
-
-extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
-  // Host-side argument checks (TMA: 16-byte aligned bases and row strides).
+// Host-side argument checks (TMA: 16-byte aligned bases and row strides).
+int check_args(const GemmArgs* a) {
   if (a->M <= 0 || a->N <= 0 || a->K <= 0) return -2;
   if ((reinterpret_cast<uintptr_t>(a->A) & 15) || (reinterpret_cast<uintptr_t>(a->B) & 15)) return -3;
   if ((a->lda * 2) % 16 || (a->ldb * 2) % 16) return -4;
   if (a->K % 8) return -5;
   const void* dchk = a->out_world > 0 ? a->out_peer[0] : a->D;
-  if (a->epi == kEpiQkv && a->D == nullptr) dchk = nullptr;  // every column goes to the head scatter
   if (!a->out_f32 && ((a->ldd % 8) || (reinterpret_cast<uintptr_t>(dchk) & 15))) return -6;
   if (a->out_f32 && ((a->ldd % 4) || (reinterpret_cast<uintptr_t>(dchk) & 15))) return -6;
   if (a->bias && (reinterpret_cast<uintptr_t>(a->bias) & 15)) return -7;
@@ -259,30 +249,62 @@ extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) {
         (a->ldr % 8) || (a->gate_bstride % 4))
       return -8;
   }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int dfl_gemm_pair_launch(const void* group, int epi, int out_f32, int* err, cudaStream_t stream, int dev);
+
+// Automatic choice of the CTA-pair kernel for wide GEMMs with M >= 1024 (on by default;
+// dfl_gemm_set_pair_auto(0) restores the one-CTA kernel everywhere).
+static int g_pair_auto = 1;
+extern "C" void dfl_gemm_set_pair_auto(int on) { g_pair_auto = on; }
+
+// One launch for `count` GEMMs that share the epilogue kind and output type.  The tile
+// shape (CTA pairs with 256 x 256 tiles, or one CTA with 128 x 256 / 128 x 128 tiles)
+// follows the first problem; the others are tiled the same way.
+extern "C" int dfl_gemm_bf16_group(const GemmArgs* const* args, int count, cudaStream_t stream) {
+  if (count < 1 || count > kMaxGroup) return -12;
+  const GemmArgs* a0 = args[0];
+  for (int i = 0; i < count; ++i) {
+    const int rc = check_args(args[i]);
+    if (rc) return rc;
+    if (args[i]->epi != a0->epi || args[i]->out_f32 != a0->out_f32 || args[i]->err != a0->err) return -12;
+  }
   int dev = 0;
   cudaGetDevice(&dev);
-  const bool wide = a->N >= 1024;
-  CUtensorMap ta, tb;
-  int rc = dfl_host::make_tmap_2d_bf16(&ta, a->A, a->K, a->M, a->lda, BK, BM, true);
-  if (rc) return 1000 + rc;
-  rc = dfl_host::make_tmap_2d_bf16(&tb, a->B, a->K, a->N, a->ldb, BK, wide ? 256 : 128, true);
-  if (rc) return 2000 + rc;
-  EpiParams ep;
-  rc = dfl_host::fill_epi_params(*a, ep);
-  if (rc) return rc;
-  const bool pair = a->cta_mode == 2 || (a->cta_mode == 0 && g_pair_auto && wide && a->M >= 1024);
-  if (pair) {
-    CUtensorMap ta2, tb2;  // 2-CTA tiles: 128 A rows and 128 B rows per CTA
-    rc = dfl_host::make_tmap_2d_bf16(&ta2, a->A, a->K, a->M, a->lda, BK, BM, true);
+  bool wide = true;
+  for (int i = 0; i < count; ++i) wide = wide && args[i]->N >= 1024;
+  const bool pair = a0->cta_mode == 2 || (a0->cta_mode == 0 && g_pair_auto && wide && a0->M >= 1024);
+  const int bm = pair ? 2 * BM : BM;
+  const int bn = (pair || wide) ? 256 : 128;
+  GemmGroup g;
+  std::memset(&g, 0, sizeof(g));
+  g.count = count;
+  for (int i = 0; i < count; ++i) {
+    const GemmArgs* a = args[i];
+    GemmProblem& P = g.p[i];
+    int rc = dfl_host::make_tmap_2d_bf16(&P.ta, a->A, a->K, a->M, a->lda, BK, BM, true);
     if (rc) return 1000 + rc;
-    rc = dfl_host::make_tmap_2d_bf16(&tb2, a->B, a->K, a->N, a->ldb, BK, 128, true);
+    rc = dfl_host::make_tmap_2d_bf16(&P.tb, a->B, a->K, a->N, a->ldb, BK, pair ? 128 : bn, true);
     if (rc) return 2000 + rc;
-    return dfl_gemm_pair_launch(&ta2, &tb2, a->M, a->N, a->K, &ep, a->epi, a->out_f32, a->err, stream, dev);
+    rc = dfl_host::fill_epi_params(*a, P.ep);
+    if (rc) return rc;
+    P.M = a->M;
+    P.N = a->N;
+    P.K = a->K;
+    P.num_m = (a->M + bm - 1) / bm;
+    P.num_n = (a->N + bn - 1) / bn;
+    P.tiles = P.num_m * P.num_n;
+    g.total_tiles += P.tiles;
   }
-  if (wide)
-    return dispatch_epi<256, 4>(a->epi, a->out_f32, ta, tb, a->M, a->N, a->K, ep, a->err, stream, dev);
-  return dispatch_epi<128, 6>(a->epi, a->out_f32, ta, tb, a->M, a->N, a->K, ep, a->err, stream, dev);
+  if (pair) return dfl_gemm_pair_launch(&g, a0->epi, a0->out_f32, a0->err, stream, dev);
+  if (wide) return dispatch_epi<256, 4>(a0->epi, a0->out_f32, g, a0->err, stream, dev);
+  return dispatch_epi<128, 6>(a0->epi, a0->out_f32, g, a0->err, stream, dev);
 }
+
+extern "C" int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream) { return dfl_gemm_bf16_group(&a, 1, stream); }
 
 // ---------------------------------------------------------------------------
 // Host helpers shared by every TMA user in this library.

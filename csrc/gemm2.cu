@@ -78,8 +78,7 @@ DFL_DEVICE void mbar_arrive_cta0(uint64_t* bar) {
 
 template <int EPI, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M,
-                     int N, int K, EpiParams ep, int* err) {
+    gemm_pair_kernel(const __grid_constant__ GemmGroup grp, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kBarOff);
@@ -92,10 +91,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_rank();
   const int pair = blockIdx.x / 2, num_pairs = gridDim.x / 2;
-  const int num_m = (M + 2 * BM - 1) / (2 * BM);
-  const int num_n = (N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
-  const int num_k = (K + BK - 1) / BK;
+  const int num_tiles = grp.total_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -109,8 +105,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_mbar_init_cluster();
     fence_proxy_async_shared();
-    prefetch_tmap(&tmap_a);
-    prefetch_tmap(&tmap_b);
+    for (int i = 0; i < grp.count; ++i) {
+      prefetch_tmap(&grp.p[i].ta);
+      prefetch_tmap(&grp.p[i].tb);
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -132,8 +130,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
       bool ok = true;
       for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-        int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        int lt, mb, nb;
+        const GemmProblem& P = group_tile(grp, t, lt);
+        tile_coords(lt, P.num_m, P.num_n, mb, nb);
+        const int num_k = (P.K + BK - 1) / BK;
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kKidGemm, 310 + stage, abort_flag)) {
             ok = false;
@@ -141,8 +141,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * kStageBytes;
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * kStageBytes);
-          tma_load_2d_pair(sa, &tmap_a, &full_bar[stage], kb * BK, mb * 2 * BM + (int)rank * BM);
-          tma_load_2d_pair(sa + kABytes, &tmap_b, &full_bar[stage], kb * BK, nb * BN + (int)rank * (BN / 2));
+          tma_load_2d_pair(sa, &P.ta, &full_bar[stage], kb * BK, mb * 2 * BM + (int)rank * BM);
+          tma_load_2d_pair(sa + kABytes, &P.tb, &full_bar[stage], kb * BK, nb * BN + (int)rank * (BN / 2));
           issued[stage] = true;
           issued_parity[stage] = phase;
           if (++stage == STAGES) {
@@ -169,6 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        int lt;
+        const int num_k = (group_tile(grp, t, lt).K + BK - 1) / BK;
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, err, kKidGemm, 330 + stage, abort_flag)) {
             ok = false;
@@ -198,13 +200,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = pair; t < num_tiles; t += num_pairs) {
-      int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      int lt, mb, nb;
+      const GemmProblem& P = group_tile(grp, t, lt);
+      tile_coords(lt, P.num_m, P.num_n, mb, nb);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err, kKidGemm, 340 + acc, abort_flag)) break;
       tc_fence_after();
       const int row = mb * 2 * BM + (int)rank * BM + sub * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
-      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, M, N, ep, [&]() {
+      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, P.M, P.N, P.ep, [&]() {
         tc_fence_before();
         if (rank == 0)
           mbar_arrive(&tempty_bar[acc]);
@@ -224,8 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int EPI, bool OUT_F32>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiParams& ep, int* err,
-                cudaStream_t stream, int dev) {
+int launch_pair(const GemmGroup& g, int* err, cudaStream_t stream, int dev) {
   auto kern = gemm_pair_kernel<EPI, OUT_F32>;
   static bool attr[16] = {false};
   if (!attr[dev & 15]) {
@@ -233,9 +235,8 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
     if (e != cudaSuccess) return (int)e;
     attr[dev & 15] = true;
   }
-  const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
   const int pairs_max = dfl_host::num_sms(dev) / 2;
-  const int pairs = tiles < pairs_max ? tiles : pairs_max;
+  const int pairs = g.total_tiles < pairs_max ? g.total_tiles : pairs_max;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -248,32 +249,29 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ep, err);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, g, err);
   return (int)e;
 }
 
 }  // namespace
 
-// Same contract as dfl_gemm_bf16 (the epilogue parameters are prepared there).
-extern "C" int dfl_gemm_pair_launch(const void* ta, const void* tb, int M, int N, int K, const void* ep_ptr, int epi,
-                                    int out_f32, int* err, cudaStream_t stream, int dev) {
-  const CUtensorMap& a = *reinterpret_cast<const CUtensorMap*>(ta);
-  const CUtensorMap& b = *reinterpret_cast<const CUtensorMap*>(tb);
-  const EpiParams& ep = *reinterpret_cast<const EpiParams*>(ep_ptr);
+// Grouped launch prepared by dfl_gemm_bf16_group (tiles of 256 rows, B boxes of 128 rows).
+extern "C" int dfl_gemm_pair_launch(const void* group, int epi, int out_f32, int* err, cudaStream_t stream, int dev) {
+  const GemmGroup& g = *reinterpret_cast<const GemmGroup*>(group);
   switch (epi) {
     case kEpiNone:
-      return out_f32 ? launch_pair<kEpiNone, true>(a, b, M, N, K, ep, err, stream, dev)
-                     : launch_pair<kEpiNone, false>(a, b, M, N, K, ep, err, stream, dev);
+      return out_f32 ? launch_pair<kEpiNone, true>(g, err, stream, dev)
+                     : launch_pair<kEpiNone, false>(g, err, stream, dev);
     case kEpiGelu:
-      return launch_pair<kEpiGelu, false>(a, b, M, N, K, ep, err, stream, dev);
+      return launch_pair<kEpiGelu, false>(g, err, stream, dev);
     case kEpiSilu:
-      return launch_pair<kEpiSilu, false>(a, b, M, N, K, ep, err, stream, dev);
+      return launch_pair<kEpiSilu, false>(g, err, stream, dev);
     case kEpiGateResid:
-      return launch_pair<kEpiGateResid, false>(a, b, M, N, K, ep, err, stream, dev);
+      return launch_pair<kEpiGateResid, false>(g, err, stream, dev);
     case kEpiSwiGLU:
-      return launch_pair<kEpiSwiGLU, false>(a, b, M, N, K, ep, err, stream, dev);
+      return launch_pair<kEpiSwiGLU, false>(g, err, stream, dev);
     case kEpiQkv:
-      return launch_pair<kEpiQkv, false>(a, b, M, N, K, ep, err, stream, dev);
+      return launch_pair<kEpiQkv, false>(g, err, stream, dev);
     default:
       return -1;
   }

@@ -36,6 +36,35 @@ struct EpiParams {
   QkvScatterArgs qs;
 };
 
+// Grouped launch: up to kMaxGroup independent GEMMs (same epilogue kind) share one
+// persistent grid; their tiles are numbered one problem after the other, so the
+// tiles of a small problem (the 512-row text stream of a dual block) fill the
+// last wave of a large one instead of running as a mostly idle launch of its own.
+constexpr int kMaxGroup = 2;
+
+struct alignas(64) GemmProblem {
+  CUtensorMap ta, tb;
+  EpiParams ep;
+  int M, N, K;
+  int num_m, num_n, tiles;
+};
+
+struct alignas(64) GemmGroup {
+  GemmProblem p[kMaxGroup];
+  int count, total_tiles;
+};
+
+// Problem owning grouped tile t, and the tile's index inside it.
+DFL_DEVICE const GemmProblem& group_tile(const GemmGroup& g, int t, int& local) {
+  int i = 0;
+  while (i + 1 < g.count && t >= g.p[i].tiles) {
+    t -= g.p[i].tiles;
+    ++i;
+  }
+  local = t;
+  return g.p[i];
+}
+
 DFL_DEVICE void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   int group_tiles = kGroupM * num_n;
   int g = t / group_tiles;

@@ -55,6 +55,9 @@ typedef struct GemmArgs {
 } GemmArgs;
 
 int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream);
+// Up to 2 GEMMs with the same epilogue kind and output type in one persistent launch
+// (their tiles share the grid; the tile shape follows args[0]).
+int dfl_gemm_bf16_group(const GemmArgs* const* args, int count, cudaStream_t stream);
 void dfl_gemm_set_pair_auto(int on);
 
 // MXFP8 GEMM on the block-scaled tensor cores (tcgen05 kind::mxf8f6f4):

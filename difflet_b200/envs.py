@@ -68,6 +68,8 @@ environment_variables: dict[str, Callable[[], Any]] = {
     "DIFFLET_GEMM_PAIR": lambda: _str(os.environ.get("DIFFLET_GEMM_PAIR"), "1"),
     # 1: q/k RMSNorm + RoPE + head scatter run in the qkv projection's GEMM epilogue; 0: separate kernel
     "DIFFLET_FUSE_QKV": lambda: _str(os.environ.get("DIFFLET_FUSE_QKV"), "1"),
+    # 1: the text- and image-stream GEMMs of a dual block share one grouped launch; 0: two launches
+    "DIFFLET_GEMM_GROUP": lambda: _str(os.environ.get("DIFFLET_GEMM_GROUP"), "1"),
     # serving
     "DIFFLET_API_KEY": lambda: _str(os.environ.get("DIFFLET_API_KEY"), None),
     "DIFFLET_SERVE_QUEUE_TIMEOUT_S": lambda: _float(os.environ.get("DIFFLET_SERVE_QUEUE_TIMEOUT_S"), 30.0),

@@ -178,7 +178,7 @@ class MMDiT:
         ws["norm"] = tp.empty((B * S_loc, D), dt) if sp else e(B * S_loc, D)  # all-gathered under SP
         ws["qkv_img"] = e(B * S_img, 3 * Dl)
         ws["qkv_txt"] = e(B * S_txt, 3 * Dl)
-        ws["mlp"] = e(B * max(S_img, S_txt), Fl)
+        ws["mlp"] = e(B * S_loc, Fl)  # [img rows ; txt rows]: both streams' MLPs live at once
         pe = (lambda *shape: par.empty(shape, dt)) if par is not None else e  # noqa: E731
         if par is not None:
             par.check_heads(H)
@@ -358,31 +358,49 @@ class MMDiT:
         def mslice(off):
             return mod[:, off:off + D]
 
+        # per-stream slices of the norm / MLP buffers, so both streams' GEMMs can share one launch
+        off_of = {"img": 0, "txt": n_of["img"]}
+        ns = {st: norm[B * off_of[st]:B * (off_of[st] + n_of[st])] for st in ("img", "txt")}
+        ms = {st: ws["mlp"][B * off_of[st]:B * (off_of[st] + n_of[st])] for st in ("img", "txt")}
+        group_rows = tp is None and B == 1  # row GEMMs straight into the residual stream (no TP reducer)
         for i in range(cfg.double_blocks):
             p = f"double.{i}."
+            mo = {st: cfg.double_mod_offset(i, st) for st in ("img", "txt")}
+            calls = []
             for st in ("img", "txt"):
                 xs, nr, pos = xs_of[st], n_of[st], pos_of[st]
-                o = cfg.double_mod_offset(i, st)
-                nb = norm[: B * nr]
-                ln(xs, nb, shift=mslice(o), scale=mslice(o + D), eps=eps, rows_per_batch=nr)
+                ln(xs, ns[st], shift=mslice(mo[st]), scale=mslice(mo[st] + D), eps=eps, rows_per_batch=nr)
                 # qkv projection with q/k RMSNorm + RoPE + head scatter (the Ulysses all-to-all under
                 # CP) in its epilogue
-                F.linear_qkv(nb, w[p + st + "_qkv.w"], w[p + st + "_qkv.b"], out=ws["qkv_" + st],
-                             scatter=dict(q_off=0, k_off=Dl, v_off=2 * Dl, S_src=nr, H=Ht, dh=dh,
-                                          **dst(q, k, v, row_of[st], pos), norm_mode=1, wq=w[p + st + "_qnorm"],
-                                          wk=w[p + st + "_knorm"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos))
+                calls.append(dict(x=ns[st], w=w[p + st + "_qkv.w"], b=w[p + st + "_qkv.b"], out=ws["qkv_" + st],
+                                  scatter=dict(q_off=0, k_off=Dl, v_off=2 * Dl, S_src=nr, H=Ht, dh=dh,
+                                               **dst(q, k, v, row_of[st], pos), norm_mode=1,
+                                               wq=w[p + st + "_qnorm"], wk=w[p + st + "_knorm"], eps=eps, cos=cos,
+                                               sin=sin, rope_pos_off=pos)))
+            F.linear_group(calls)
             self._attention(ws, B, S_txt, S_img, D, Hl, dh, kv_lo=kv_lo, kv_hi=kv_hi)
+            if group_rows:
+                F.linear_group([dict(x=ws["attn"][0, row_of[st]:row_of[st] + n_of[st]], w=w[p + st + "_out.w"],
+                                     b=w[p + st + "_out.b"], out=xs_of[st], gate=mslice(mo[st] + 2 * D),
+                                     resid=xs_of[st], rows_per_batch=n_of[st]) for st in ("img", "txt")])
+            else:
+                for st in ("img", "txt"):
+                    rows = slice(row_of[st], row_of[st] + n_of[st])
+                    self._rows_gemm(ws["attn"], rows, B, n_of[st], w[p + st + "_out.w"], w[p + st + "_out.b"],
+                                    xs_of[st], mslice(mo[st] + 2 * D), row_linear)
             for st in ("img", "txt"):
-                xs, nr = xs_of[st], n_of[st]
-                o = cfg.double_mod_offset(i, st)
-                rows = slice(row_of[st], row_of[st] + nr)
-                self._rows_gemm(ws["attn"], rows, B, nr, w[p + st + "_out.w"], w[p + st + "_out.b"], xs,
-                                mslice(o + 2 * D), row_linear)
-                nb = norm[: B * nr]
-                ln(xs, nb, shift=mslice(o + 3 * D), scale=mslice(o + 4 * D), eps=eps, rows_per_batch=nr)
-                mb = ws["mlp"][: B * nr]
-                F.linear(nb, w[p + st + "_up.w"], w[p + st + "_up.b"], out=mb, act="gelu")
-                row_linear(mb, w[p + st + "_down.w"], w[p + st + "_down.b"], xs, mslice(o + 5 * D), nr)
+                ln(xs_of[st], ns[st], shift=mslice(mo[st] + 3 * D), scale=mslice(mo[st] + 4 * D), eps=eps,
+                   rows_per_batch=n_of[st])
+            F.linear_group([dict(x=ns[st], w=w[p + st + "_up.w"], b=w[p + st + "_up.b"], out=ms[st], act="gelu")
+                            for st in ("img", "txt")])
+            if group_rows:
+                F.linear_group([dict(x=ms[st], w=w[p + st + "_down.w"], b=w[p + st + "_down.b"], out=xs_of[st],
+                                     gate=mslice(mo[st] + 5 * D), resid=xs_of[st], rows_per_batch=n_of[st])
+                                for st in ("img", "txt")])
+            else:
+                for st in ("img", "txt"):
+                    row_linear(ms[st], w[p + st + "_down.w"], w[p + st + "_down.b"], xs_of[st],
+                               mslice(mo[st] + 5 * D), n_of[st])
 
         if sp:  # dual -> single: the rows each rank owns change; replicate the residual stream once
             for st in ("txt", "img"):

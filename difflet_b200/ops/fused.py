@@ -14,6 +14,7 @@ Ops:
                 head-major (or token-major) destinations, one per rank
   linear_qkv    linear whose q/k/v column blocks go through qkv_scatter inside the
                 GEMM epilogue (no round trip of the qkv rows through HBM)
+  linear_group  two linear / linear_qkv calls with one epilogue kind as one launch
   attention     softmax(scale q k^T) v with key window and LSE
   gemv          modulation linears (M <= 8), f32 in/out, optional SiLU
   euler_step    x += dt * (u + s (c - u)) on f32 latents (+ bf16 mirror)
@@ -326,6 +327,20 @@ def _qkv_epilogue_ok(sc: dict, act) -> bool:
     return cos is None or cos.shape[-1] in (dh // 2, H * dh // 2)
 
 
+def _qkv_plan(sc: dict) -> bytes:
+    """The packed head-scatter description the GEMM's qkv epilogue reads."""
+    world = len(next(d for d in (sc.get("q_dst"), sc.get("k_dst"), sc.get("v_dst")) if d is not None))
+    kv_rep = sc.get("kv_replicate", False)
+    hpr = sc["H"] if kv_rep else (sc.get("heads_per_rank") or sc["H"] // world)
+    dst = [sc.get(k) if sc.get(k) is not None else [None] * world for k in ("q_dst", "k_dst", "v_dst")]
+    return _lib().qkv_plan(*_scatter_args(
+        sc["q_off"], sc["k_off"], sc["v_off"], sc["S_src"], sc["H"], sc["dh"], dst[0], dst[1], dst[2], sc["S_dst"],
+        sc.get("seq_off", 0), sc.get("norm_mode", 1), sc.get("wq"), sc.get("wk"), sc.get("eps", 1e-6), sc.get("cos"),
+        sc.get("sin"), sc.get("rope_pos_off", 0), sc.get("rope_half", False), hpr, sc.get("token_major", False),
+        kv_rep, sc.get("q_S_dst", 0), sc.get("q_seq_off", 0), sc.get("seg_rows", 0), sc.get("seg1_seq_off", 0),
+        sc.get("seg1_rope_off", 0)))
+
+
 def linear_qkv(x, w, b=None, *, scatter: dict, out=None, act=None, act_lo=0, act_hi=None):
     """``linear`` whose q / k / v column blocks are consumed by ``qkv_scatter(**scatter)``.
 
@@ -340,17 +355,7 @@ def linear_qkv(x, w, b=None, *, scatter: dict, out=None, act=None, act_lo=0, act
     N = w.shape[0]
     act_hi = N if act_hi is None else act_hi
     if x2.is_cuda and _qkv_epilogue_ok(scatter, act) and not (isinstance(w, MXWeight) and w.compute != "mx"):
-        sc = dict(scatter)
-        world = len(next(d for d in (sc.get("q_dst"), sc.get("k_dst"), sc.get("v_dst")) if d is not None))
-        kv_rep = sc.get("kv_replicate", False)
-        hpr = sc["H"] if kv_rep else (sc.get("heads_per_rank") or sc["H"] // world)
-        dst = [sc.get(k) if sc.get(k) is not None else [None] * world for k in ("q_dst", "k_dst", "v_dst")]
-        plan = _lib().qkv_plan(*_scatter_args(
-            sc["q_off"], sc["k_off"], sc["v_off"], sc["S_src"], sc["H"], sc["dh"], dst[0], dst[1], dst[2],
-            sc["S_dst"], sc.get("seq_off", 0), sc.get("norm_mode", 1), sc.get("wq"), sc.get("wk"),
-            sc.get("eps", 1e-6), sc.get("cos"), sc.get("sin"), sc.get("rope_pos_off", 0), sc.get("rope_half", False),
-            hpr, sc.get("token_major", False), kv_rep, sc.get("q_S_dst", 0), sc.get("q_seq_off", 0),
-            sc.get("seg_rows", 0), sc.get("seg1_seq_off", 0), sc.get("seg1_rope_off", 0)))
+        plan = _qkv_plan(scatter)
         lo, hi = (act_lo, act_hi) if act == "gelu" else (0, 0)  # non-qkv columns: GELU window or identity
         if isinstance(w, MXWeight):
             xq, xs = mx_quantize(x2, blocked=True)
@@ -361,6 +366,59 @@ def linear_qkv(x, w, b=None, *, scatter: dict, out=None, act=None, act_lo=0, act
     y = linear(x2, w, b, out=out, act=act, act_lo=act_lo, act_hi=act_hi)
     qkv_scatter(y, **scatter)
     return out if out is not None else y
+
+
+def _group_epi(c: dict):
+    """Epilogue kind of one grouped call, or None when it cannot join a grouped launch."""
+    x, w = c["x"], c["w"]
+    if not x.is_cuda or isinstance(w, MXWeight):
+        return None
+    if c.get("scatter") is not None:
+        return EPI_QKV if _qkv_epilogue_ok(c["scatter"], c.get("act")) else None
+    if c.get("gate") is not None:
+        return EPI_GATE_RESID
+    act = c.get("act")
+    return None if act == "swiglu" else _ACT[act]
+
+
+def linear_group(calls: list) -> list:
+    """Two ``linear`` (or ``linear_qkv``, with a ``scatter`` entry) calls as ONE persistent
+    GEMM launch whose grid covers both problems' tiles, e.g. the text- and image-stream
+    projections of a dual block (the 512-row text GEMM alone fills a third of the SMs).
+
+    Each call is a dict of ``linear`` keyword arguments plus ``x`` and ``w``; calls that do not
+    share an epilogue kind (or use MXFP8 weights) run one after the other.  Returns the outputs.
+    """
+    epis = [_group_epi(c) for c in calls]
+    if (len(calls) != 2 or None in epis or epis[0] != epis[1] or envs.DIFFLET_GEMM_GROUP == "0"
+            or envs.DIFFLET_KERNEL_GEMM == "cublas"):
+        outs = []
+        for c in calls:
+            kw = {k: v for k, v in c.items() if k not in ("x", "w", "b")}
+            fn = linear_qkv if kw.get("scatter") is not None else linear
+            if kw.get("scatter") is None:
+                kw.pop("scatter", None)
+            outs.append(fn(c["x"], c["w"], c.get("b"), **kw))
+        return outs
+    epi = epis[0]
+    A, Bw, bias, out, lo, hi, gate, rpb, resid, plans = ([] for _ in range(10))
+    for c in calls:
+        N = c["w"].shape[0]
+        A.append(_rows2d(c["x"]))
+        Bw.append(c["w"])
+        bias.append(c.get("b"))
+        out.append(c.get("out"))
+        act_lo, act_hi = c.get("act_lo", 0), c.get("act_hi")
+        act_hi = N if act_hi is None else act_hi
+        if epi == EPI_QKV:
+            act_lo, act_hi = (act_lo, act_hi) if c.get("act") == "gelu" else (0, 0)
+        lo.append(act_lo)
+        hi.append(act_hi)
+        gate.append(c.get("gate"))
+        rpb.append(c.get("rows_per_batch", 0))
+        resid.append(c.get("resid"))
+        plans.append(_qkv_plan(c["scatter"]) if epi == EPI_QKV else b"")
+    return native().gemm_group(A, Bw, bias, out, epi, lo, hi, gate, rpb, resid, plans)
 
 
 def attention(q, k, v, scale, *, out=None, lse=None, kv_lo=None, kv_hi=None):

@@ -169,3 +169,65 @@ def test_qkv_epilogue_mxfp8(native, monkeypatch):
     ref, _ = _run(monkeypatch, False, x, w, b, scatter)
     for a, r in zip(fused, ref):
         _close(a, r, 1e-2)
+
+
+@pytest.mark.parametrize("epi", ["gate", "gelu", "qkv"])
+def test_grouped_gemm_matches_separate(native, monkeypatch, epi):
+    """Two problems (4096-row image stream + 512-row text stream shapes, scaled down) in one
+    grouped launch equal two separate launches."""
+    torch.manual_seed(16)
+    H, dh = 4, 128
+    D = H * dh
+    shapes = [(1100, 256), (300, 256)]  # (rows, K): pair tiles for the first, shared by the second
+
+    def problem(M, K):
+        N = 3 * D if epi == "qkv" else (1536 if epi == "gelu" else D)
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.06
+        b = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+        return x, w, b
+
+    probs = [problem(M, K) for M, K in shapes]
+    gates = [torch.randn(1, D, device="cuda") for _ in probs]
+    resid0 = [torch.randn(M, D, device="cuda", dtype=torch.bfloat16) for M, _ in shapes]
+    wq = torch.randn(dh, device="cuda", dtype=torch.bfloat16)
+    wk = torch.randn(dh, device="cuda", dtype=torch.bfloat16)
+    cos, sin = _tables(2000, dh // 2)
+
+    def calls():
+        out, dsts = [], []
+        for (x, w, b), (M, _), g, r0 in zip(probs, shapes, gates, resid0):
+            c = dict(x=x, w=w, b=b)
+            if epi == "gate":
+                o = r0.clone()
+                c.update(out=o, gate=g, resid=o, rows_per_batch=M)
+            elif epi == "gelu":
+                o = torch.zeros(M, w.shape[0], device="cuda", dtype=torch.bfloat16)
+                c.update(out=o, act="gelu")
+            else:
+                o = torch.zeros(M, w.shape[0], device="cuda", dtype=torch.bfloat16)
+                qd, kd, vd = (torch.zeros(1, H, M, dh, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+                dsts += [qd, kd, vd]
+                c.update(out=o, scatter=dict(q_off=0, k_off=D, v_off=2 * D, S_src=M, H=H, dh=dh, q_dst=[qd],
+                                             k_dst=[kd], v_dst=[vd], S_dst=M, norm_mode=1, wq=wq, wk=wk, eps=1e-6,
+                                             cos=cos, sin=sin))
+            out.append(o)
+            out_calls.append(c)
+        return out, dsts
+
+    monkeypatch.setenv("DIFFLET_GEMM_GROUP", "1")
+    out_calls = []
+    got, got_d = calls()
+    before = F.LAUNCHES[0]
+    F.linear_group(out_calls)
+    assert F.LAUNCHES[0] - before == 1
+    torch.cuda.synchronize()
+    monkeypatch.setenv("DIFFLET_GEMM_GROUP", "0")
+    out_calls = []
+    ref, ref_d = calls()
+    F.linear_group(out_calls)
+    torch.cuda.synchronize()
+    for a, r in zip(got + got_d, ref + ref_d):
+        if epi == "qkv" and a.dim() == 2:
+            continue  # the qkv columns of `out` are not written by the fused path
+        _close(a, r, 1e-2)  # the small problem runs on the large one's tile shape when grouped
