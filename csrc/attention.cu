@@ -1,17 +1,19 @@
 // Flash attention forward for sm_100a (head_dim 128, bf16 in/out, fp32 softmax).
 //
 // One CTA per (256-query block, head, batch), two 128-row Q tiles in ping-pong:
-//   warp 0      TMA producer: Q0/Q1 once, then K_j / V_j tiles (2-stage ring,
+//   warp 8      TMA producer: Q0/Q1 once, then K_j / V_j tiles (2-stage ring,
 //               shared by both Q tiles)
-//   warp 1      MMA issuer, in the order  PV0(j-1), QK0(j), PV1(j-1), QK1(j):
+//   warp 9      MMA issuer, in the order  PV0(j-1), QK0(j), PV1(j-1), QK1(j):
 //               S_g = Q_g K_j^T into TMEM; P_g (bf16) is written back over S_g
 //               by the softmax warps and consumed as the A operand straight
 //               from TMEM (tcgen05.mma ... [a_tmem]); O_g += P_g V (V read from
 //               smem as an MN-major operand).  tcgen05 operations of one thread
 //               complete in order, so when S_g(j) is ready the previous PV_g
 //               has finished: no extra barrier guards P reuse or O rescaling.
-//   warps 2..5  softmax for Q tile 0; warps 6..9 for Q tile 1: one query row per
-//               thread, running max in log2 units, exp2 on the SFU, P packed to
+//   warps 0..3  softmax for Q tile 0; warps 4..7 for Q tile 1 (216 registers each
+//               after the setmaxnreg split): one query row per thread, running
+//               max in log2 units, exp2 on the SFU and (a fixed share) on the FMA
+//               pipe by a cubic, P packed to
 //               bf16x2 and stored to TMEM; O_g is rescaled in TMEM only when the
 //               max grew by more than 2^8 (a stale max keeps P <= 256, exact
 //               after the final 1/l); epilogue normalises and stores rows.
@@ -39,14 +41,17 @@ constexpr int kChunk = 16384;
 // QT = Q tiles per CTA: 2 (ping-pong, default) or 1 (small grids: twice the CTAs)
 template <int QT>
 struct AttnSmem {
-  static constexpr int kThreads = 64 + 128 * QT;
+  // warpgroups 0..QT-1: softmax of Q tile g; last warpgroup: TMA warp, MMA warp, 2 idle warps
+  static constexpr int kThreads = 128 * QT + 128;
+  static constexpr int kProducerWarp = 4 * QT;
+  static constexpr int kMmaWarp = 4 * QT + 1;
   static constexpr uint32_t kTmemCols = QT == 2 ? 512 : 256;
   static constexpr int kQ = 0;                              // QT tiles
   static constexpr int kK = kQ + QT * kTileBytes;           // kNS tiles
   static constexpr int kV = kK + kNS * kTileBytes;          // kNS tiles
   static constexpr int kBar = kV + kNS * kTileBytes;
-  // q_full, k_full[NS], v_full[NS], k_empty[NS], v_empty[NS], s_full[2], p_full[2], o_full
-  static constexpr int kNumBars = 1 + 4 * kNS + 2 + 2 + 1;
+  // q_full, k_full[NS], v_full[NS], k_empty[NS], v_empty[NS], s_full[2], p_full[2][2], o_full
+  static constexpr int kNumBars = 1 + 4 * kNS + 2 + 4 + 1;
   static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -61,6 +66,61 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ void regs_dec_64() { asm volatile("setmaxnreg.dec.sync.aligned.u32 64;"); }
+__device__ __forceinline__ void regs_inc_216() { asm volatile("setmaxnreg.inc.sync.aligned.u32 216;"); }
+
+// Packed f32x2 arithmetic (two lanes of a 64-bit register pair per instruction).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two values on the FMA pipe, so part of the softmax exponentials leave the
+// SFU (whose 16 results / clock / SM match the tensor core's pace at head dim 128).
+// Range reduction x = j + f, j = round(x) (the 1.5 * 2^23 addition trick), f in
+// [-0.5, 0.5]; 2^f by a cubic fitted here for minimum relative error on that interval
+// (Lawson's iteratively reweighted least squares on 4000 Chebyshev nodes; max relative
+// error 7.5e-5, below the bf16 rounding of P); 2^j added to the exponent bits.
+// x is clamped at -125 (masked keys give 2^-125 instead of 0: negligible next to l >= 1).
+__device__ __forceinline__ void poly_exp2_x2(uint64_t x2, float& e0, float& e1) {
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x0 = fmaxf(x0, -125.f);
+  x1 = fmaxf(x1, -125.f);
+  const uint64_t xc = f2_pack(x0, x1);
+  const uint64_t magic = f2_pack(12582912.f, 12582912.f);
+  const uint64_t t = f2_add(xc, magic);                                 // j in the low mantissa bits
+  const uint64_t j = f2_add(t, f2_pack(-12582912.f, -12582912.f));      // round(x)
+  const uint64_t f = f2_fma(j, f2_pack(-1.f, -1.f), xc);                // x - round(x)
+  uint64_t pl = f2_fma(f2_pack(0.055171665f, 0.055171665f), f, f2_pack(0.24261113f, 0.24261113f));
+  pl = f2_fma(pl, f, f2_pack(0.69326097f, 0.69326097f));
+  pl = f2_fma(pl, f, f2_pack(0.99992806f, 0.99992806f));
+  float p0, p1, t0, t1;
+  f2_unpack(pl, p0, p1);
+  f2_unpack(t, t0, t1);
+  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 // D[tmem] (+)= A[tmem] * B[smem]  (A: M x K, one row per lane, 2 bf16 per column)
@@ -127,7 +187,8 @@ __device__ __forceinline__ void tma_load_4d(uint8_t* dst, const CUtensorMap* map
       : "memory");
 }
 
-template <int QT>
+// POLY: of every 8 exponential pairs of a row, POLY are evaluated on the FMA pipe.
+template <int QT, int POLY>
 __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, AttnParams p, int* err) {
@@ -142,7 +203,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
   uint64_t* v_empty = k_empty + kNS;
   uint64_t* s_full = v_empty + kNS;
   uint64_t* p_full = s_full + 2;
-  uint64_t* o_full = p_full + 2;
+  uint64_t* o_full = p_full + 4;  // p_full[2 g + h]: keys [64 h, 64 h + 64) of P_g stored
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AttnSmem<QT>::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -157,7 +218,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < AttnSmem<QT>::kNumBars; ++i) {
       uint64_t* bar = &bars[i];
-      const bool softmax_arrivals = (bar == p_full) || (bar == p_full + 1);
+      const bool softmax_arrivals = bar >= p_full && bar < p_full + 4;
       mbar_init(bar, softmax_arrivals ? 128 : 1);
     }
     *abort_flag = 0;
@@ -167,7 +228,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     prefetch_tmap(&tk);
     prefetch_tmap(&tv);
   }
-  if (warp == 1) {
+  if (warp == AttnSmem<QT>::kMmaWarp) {
     tmem_alloc(tmem_slot, AttnSmem<QT>::kTmemCols);
     tmem_relinquish();
   }
@@ -176,7 +237,12 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  // Register split for QT = 2 (launch: 384 threads x 168): the TMA / MMA warpgroup gives
+  // registers back (64 each), the two softmax warpgroups take them (216 each):
+  // 128 * 64 + 256 * 216 = 63488 <= 384 * 168.  Every warp of a warpgroup executes its setmaxnreg,
+  // inside its role's branch so that the compiler applies the new limit to that code.
+  if (warp == AttnSmem<QT>::kProducerWarp) {
+    if constexpr (QT == 2) regs_dec_64();
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
       mbar_arrive_expect_tx(q_full, QT * kTileBytes);
@@ -214,7 +280,8 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == AttnSmem<QT>::kMmaWarp) {
+    if constexpr (QT == 2) regs_dec_64();
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16_f32(kBM, kBN, 0, 0);
@@ -232,14 +299,19 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         umma_commit(&s_full[g]);
       };
       auto issue_pv = [&](int g, int jj) -> bool {
-        if (!mbar_wait(&p_full[g], jj & 1, err, kKidAttn, 111 + g, abort_flag)) return false;
-        tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + AttnSmem<QT>::kV + (jj % kNS) * kTileBytes);
+        // P_g arrives in two halves: the first 64 keys' MMAs run while the softmax
+        // finishes the second half
+        for (int hf = 0; hf < 2; ++hf) {
+          if (!mbar_wait(&p_full[2 * g + hf], jj & 1, err, kKidAttn, 130 + 2 * g + hf, abort_flag)) return false;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, kChunk, 1024);
-          umma_f16_ts(tmem + tmem_o_col<QT>(g), tmem + tmem_s_col(g) + kk * 8, bd, idesc_pv,
-                      (jj > 0 || kk > 0) ? 1u : 0u);
+          for (int kq = 0; kq < kBN / 32; ++kq) {
+            const int kk = hf * (kBN / 32) + kq;
+            uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, kChunk, 1024);
+            umma_f16_ts(tmem + tmem_o_col<QT>(g), tmem + tmem_s_col(g) + kk * 8, bd, idesc_pv,
+                        (jj > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         return true;
       };
@@ -270,9 +342,12 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         }
       }
     }
+  } else if (warp >= AttnSmem<QT>::kProducerWarp) {
+    if constexpr (QT == 2) regs_dec_64();  // the two idle warps of the last warpgroup
   } else {
+    if constexpr (QT == 2) regs_inc_216();
     // ------------------------------------------------------------ softmax groups
-    const int g = (warp - 2) / 4;           // Q tile of this warpgroup
+    const int g = warp / 4;                 // Q tile of this warpgroup
     const int sub = warp & 3;               // TMEM lane quarter of this warp
     const int row = sub * 32 + lane;        // row within the Q tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
@@ -297,15 +372,17 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
           if (key < lo || key >= hi) s[c] = -INFINITY;
         }
       }
-      // row max over raw scores: 8 independent chains (short dependency depth)
+      // row max over raw scores: 8 independent chains of 3-input max (short dependency depth)
       float mxa[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) mxa[t] = s[t];
 #pragma unroll
-      for (int c = 8; c < 128; c += 8) {
+      for (int c = 8; c < 120; c += 16) {
 #pragma unroll
-        for (int t = 0; t < 8; ++t) mxa[t] = fmaxf(mxa[t], s[c + t]);
+        for (int t = 0; t < 8; ++t) mxa[t] = max3(mxa[t], s[c + t], s[c + 8 + t]);
       }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mxa[t] = fmaxf(mxa[t], s[120 + t]);
       const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
                              fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
       const float m_new = fmaxf(m, mx * p.scale_log2);  // scale > 0: max commutes with it
@@ -328,25 +405,42 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         }
         l *= f;
       }
-      // p = 2^(s * scale_log2 - m): one FFMA + one SFU op per element; 4 sum chains
+      // p = 2^(s * scale_log2 - m): packed FFMA per pair, then the SFU (or, for POLY of
+      // every 8 pairs, the FMA-pipe polynomial); packed sums in 2 chains
       const float sc = p.scale_log2, neg_m = -m_use;
-      float rsa[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(neg_m, neg_m);
+      uint64_t rs2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
+      for (int qtr = 0; qtr < 4; ++qtr) {  // 32 scores -> 16 packed P words per TMEM store
+        uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float e0 = fast_exp2(fmaf(s[half * 64 + 2 * c], sc, neg_m));
-          const float e1 = fast_exp2(fmaf(s[half * 64 + 2 * c + 1], sc, neg_m));
-          rsa[c & 3] += e0 + e1;
+        for (int c = 0; c < 16; ++c) {
+          const uint64_t x2 = f2_fma(f2_pack(s[qtr * 32 + 2 * c], s[qtr * 32 + 2 * c + 1]), sc2, nm2);
+          float e0, e1;
+          if ((c & 7) >= 8 - POLY) {
+            poly_exp2_x2(x2, e0, e1);
+          } else {
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            e0 = fast_exp2(x0);
+            e1 = fast_exp2(x1);
+          }
+          rs2[c & 1] = f2_add(rs2[c & 1], f2_pack(e0, e1));
           pk[c] = pack_bf16x2(e0, e1);
         }
-        tmem_st_32x32b_x32(s_t + half * 32, pk);
+        tmem_st_32x32b_x16(s_t + qtr * 16, pk);
+        if (qtr & 1) {  // keys [0, 64) / [64, 128) of P are in TMEM
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&p_full[2 * g + (qtr >> 1)]);
+        }
       }
-      l += (rsa[0] + rsa[1]) + (rsa[2] + rsa[3]);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[g]);
+      {
+        float a0, a1, b0, b1;
+        f2_unpack(rs2[0], a0, a1);
+        f2_unpack(rs2[1], b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      }
     }
     // ------------------------------------------------------------ epilogue
     const int qrow = q0 + g * kBM + row;
@@ -457,7 +551,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, AttnSmem<QT>::kTmemCols);
+  if (warp == AttnSmem<QT>::kMmaWarp) tmem_dealloc(tmem, AttnSmem<QT>::kTmemCols);
 }
 
 int make_tmap_4d(CUtensorMap* map, const void* base, long long S, int H, int B, long long ss,
@@ -473,24 +567,46 @@ int make_tmap_4d(CUtensorMap* map, const void* base, long long S, int H, int B, 
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-template <int QT>
-int launch_attn(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
-                const CUtensorMap& tv, cudaStream_t stream) {
+template <int QT, int POLY>
+int launch_attn_poly(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
+                     const CUtensorMap& tv, cudaStream_t stream) {
   static bool attr[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 15]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<QT, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnSmem<QT>::kTotal);
     if (e != cudaSuccess) return (int)e;
+    if (QT == 2) {  // the setmaxnreg split must fit in the registers the CTA is launched with
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, attn_fwd_kernel<QT, POLY>);
+      if (e != cudaSuccess) return (int)e;
+      if (fa.numRegs * AttnSmem<QT>::kThreads < 128 * 64 + 256 * 216) return -11;
+    }
     attr[dev & 15] = true;
   }
   dim3 grid((a->Sq + QT * kBM - 1) / (QT * kBM), a->H, a->B);
-  attn_fwd_kernel<QT><<<grid, AttnSmem<QT>::kThreads, AttnSmem<QT>::kTotal, stream>>>(tq, tk, tv, p, a->err);
+  attn_fwd_kernel<QT, POLY><<<grid, AttnSmem<QT>::kThreads, AttnSmem<QT>::kTotal, stream>>>(tq, tk, tv, p, a->err);
   return (int)cudaGetLastError();
 }
 
+int g_attn_poly = 0;  // exponential pairs (of 8) on the FMA pipe (0 measured fastest at head dim 128)
+
+template <int QT>
+int launch_attn(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
+                const CUtensorMap& tv, cudaStream_t stream) {
+  switch (g_attn_poly) {
+    case 0: return launch_attn_poly<QT, 0>(a, p, tq, tk, tv, stream);
+    case 1: return launch_attn_poly<QT, 1>(a, p, tq, tk, tv, stream);
+    case 3: return launch_attn_poly<QT, 3>(a, p, tq, tk, tv, stream);
+    default: return launch_attn_poly<QT, 2>(a, p, tq, tk, tv, stream);
+  }
+}
+
 }  // namespace
+
+// Fraction (n / 8) of the softmax exponentials evaluated by the FMA-pipe polynomial.
+extern "C" void dfl_attention_set_poly(int n) { g_attn_poly = n < 0 ? 0 : (n > 3 ? 3 : n); }
 
 extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   if (a->dh != kD) return -2;

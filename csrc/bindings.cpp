@@ -692,6 +692,7 @@ at::Tensor rel_l1(const at::Tensor& a, const at::Tensor& b) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "difflet_b200 native sm_100a kernels";
   m.def("gemm_set_pair_auto", [](bool on) { dfl_gemm_set_pair_auto(on ? 1 : 0); });
+  m.def("attention_set_poly", [](int64_t n) { dfl_attention_set_poly((int)n); });
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("B"),
         py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),

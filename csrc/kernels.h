@@ -193,6 +193,8 @@ typedef struct AttnArgs {
   int merge_mode;
 } AttnArgs;
 int dfl_attention(const AttnArgs* a, cudaStream_t stream);
+// n of every 8 softmax exponential pairs on the FMA pipe (0..3; default 0).
+void dfl_attention_set_poly(int n);
 
 // ---------------------------------------------------------------------------
 // Peer-memory communication runtime (comm.cu)

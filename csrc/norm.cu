@@ -27,6 +27,61 @@ using namespace dfl;
 // ---------------------------------------------------------------------------
 constexpr int kMaxVec = 24;  // 24 x 8 bf16 per lane -> D <= 6144
 
+__device__ __forceinline__ void unpack_bf16x8(const uint4& w, float (&f)[8]) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const float2 t = unpack_bf16x2(ws[h]);
+    f[2 * h] = t.x;
+    f[2 * h + 1] = t.y;
+  }
+}
+
+// One 8-value output vector: (x - mean) * rstd [* w + b] [* (1 + scale) + shift], stored
+// locally or (sequence-parallel all-gather) into every rank's buffer.
+__device__ __forceinline__ void ln_store_vec(const LnModArgs& a, int row, int vi, const uint4& raw, float mean,
+                                             float rstd, const float* sh, const float* sc, const __nv_bfloat16* w,
+                                             const __nv_bfloat16* bb, uint4* y4) {
+  const int c0 = vi * 8;
+  float o[8];
+  unpack_bf16x8(raw, o);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = (o[j] - mean) * rstd;
+  if (w) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] *= __bfloat162float(w[c0 + j]);
+  }
+  if (bb) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] += __bfloat162float(bb[c0 + j]);
+  }
+  if (sc) {
+    float4 s0 = *reinterpret_cast<const float4*>(sc + c0);
+    float4 s1 = *reinterpret_cast<const float4*>(sc + c0 + 4);
+    float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] *= (1.f + s[j]);
+  }
+  if (sh) {
+    float4 s0 = *reinterpret_cast<const float4*>(sh + c0);
+    float4 s1 = *reinterpret_cast<const float4*>(sh + c0 + 4);
+    float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] += s[j];
+  }
+  uint4 out;
+  out.x = pack_bf16x2(o[0], o[1]);
+  out.y = pack_bf16x2(o[2], o[3]);
+  out.z = pack_bf16x2(o[4], o[5]);
+  out.w = pack_bf16x2(o[6], o[7]);
+  if (a.y_world > 0) {  // sequence-parallel all-gather: this row into every rank's buffer
+    for (int d = 0; d < a.y_world; ++d)
+      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y_peer[d]) + (long long)row * a.ldy)[vi] = out;
+  } else {
+    y4[vi] = out;
+  }
+}
+
 template <int kMaxVec>
 __global__ void __launch_bounds__(256) ln_modulate_kernel(LnModArgs a) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
@@ -36,22 +91,21 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(LnModArgs a) {
   const int nvec = a.D / 8;  // 16-byte vectors per row
   const uint4* x4 = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) +
                                                    (long long)row * a.ldx);
-  float xs[kMaxVec][8];
+  // the row stays in registers as packed bf16 (4 registers per 8 values): low register
+  // count, so more rows per SM are in flight
+  uint4 raw[kMaxVec];
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < kMaxVec; ++i) {
     int vi = lane + 32 * i;
-    if (vi < nvec) {
-      uint4 w = x4[vi];
-      uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    raw[i] = vi < nvec ? x4[vi] : make_uint4(0u, 0u, 0u, 0u);
+  }
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        float2 f = unpack_bf16x2(ws[h]);
-        xs[i][2 * h] = f.x;
-        xs[i][2 * h + 1] = f.y;
-        sum += f.x + f.y;
-      }
-    }
+  for (int i = 0; i < kMaxVec; ++i) {
+    float f[8];
+    unpack_bf16x8(raw[i], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += f[j];
   }
   float mean = 0.f;
   if (!a.rms) mean = warp_sum(sum) / (float)a.D;
@@ -60,9 +114,11 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(LnModArgs a) {
   for (int i = 0; i < kMaxVec; ++i) {
     int vi = lane + 32 * i;
     if (vi < nvec) {
+      float f[8];
+      unpack_bf16x8(raw[i], f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float d = xs[i][j] - mean;
+        float d = f[j] - mean;
         sq += d * d;
       }
     }
@@ -77,45 +133,65 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(LnModArgs a) {
 #pragma unroll
   for (int i = 0; i < kMaxVec; ++i) {
     int vi = lane + 32 * i;
-    if (vi < nvec) {
-      int c0 = vi * 8;
-      float o[8];
+    if (vi < nvec) ln_store_vec(a, row, vi, raw[i], mean, rstd, sh, sc, w, bb, y4);
+  }
+}
+
+// Block-per-row variant for wide rows (D >= 1024): 128 threads share a row, each holding
+// VPT 16-byte vectors, so registers stay low and many rows per SM are in flight.
+template <int VPT>
+__global__ void __launch_bounds__(128) ln_modulate_row_kernel(LnModArgs a) {
+  __shared__ float red[2][4];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int row = (int)(a.row0 + blockIdx.x);
+  const int nvec = a.D / 8;
+  const uint4* x4 = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) +
+                                                   (long long)row * a.ldx);
+  uint4 raw[VPT];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = (xs[i][j] - mean) * rstd;
-      if (w) {
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = t + 128 * i;
+    raw[i] = vi < nvec ? x4[vi] : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float sum = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] *= __bfloat162float(w[c0 + j]);
-      }
-      if (bb) {
+  for (int i = 0; i < VPT; ++i) {
+    float f[8];
+    unpack_bf16x8(raw[i], f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] += __bfloat162float(bb[c0 + j]);
-      }
-      if (sc) {
-        float4 s0 = *reinterpret_cast<const float4*>(sc + c0);
-        float4 s1 = *reinterpret_cast<const float4*>(sc + c0 + 4);
-        float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    for (int j = 0; j < 8; ++j) sum += f[j];
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[0][warp] = sum;
+  __syncthreads();
+  const float mean = a.rms ? 0.f : (red[0][0] + red[0][1] + red[0][2] + red[0][3]) / (float)a.D;
+  float sq = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] *= (1.f + s[j]);
-      }
-      if (sh) {
-        float4 s0 = *reinterpret_cast<const float4*>(sh + c0);
-        float4 s1 = *reinterpret_cast<const float4*>(sh + c0 + 4);
-        float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  for (int i = 0; i < VPT; ++i) {
+    if (t + 128 * i < nvec) {
+      float f[8];
+      unpack_bf16x8(raw[i], f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] += s[j];
-      }
-      uint4 out;
-      out.x = pack_bf16x2(o[0], o[1]);
-      out.y = pack_bf16x2(o[2], o[3]);
-      out.z = pack_bf16x2(o[4], o[5]);
-      out.w = pack_bf16x2(o[6], o[7]);
-      if (a.y_world > 0) {  // sequence-parallel all-gather: this row into every rank's buffer
-        for (int d = 0; d < a.y_world; ++d)
-          reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y_peer[d]) + (long long)row * a.ldy)[vi] = out;
-      } else {
-        y4[vi] = out;
+      for (int j = 0; j < 8; ++j) {
+        const float d = f[j] - mean;
+        sq += d * d;
       }
     }
+  }
+  sq = warp_sum(sq);
+  if (lane == 0) red[1][warp] = sq;
+  __syncthreads();
+  const float rstd = rsqrtf((red[1][0] + red[1][1] + red[1][2] + red[1][3]) / (float)a.D + a.eps);
+  const int b = a.row_map ? a.row_map[row] : row / a.rows_per_batch;
+  const float* sh = a.shift ? a.shift + (long long)b * a.mod_bstride : nullptr;
+  const float* sc = a.scale ? a.scale + (long long)b * a.mod_bstride : nullptr;
+  const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(a.w);
+  const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(a.b);
+  uint4* y4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + (long long)row * a.ldy);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = t + 128 * i;
+    if (vi < nvec) ln_store_vec(a, row, vi, raw[i], mean, rstd, sh, sc, w, bb, y4);
   }
 }
 
@@ -305,6 +381,32 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
 // ---------------------------------------------------------------------------
 // GEMV: one warp per output row, x staged in shared memory (f32).
 // ---------------------------------------------------------------------------
+// Streaming 16-byte weight load (read once: no L1 allocation).
+__device__ __forceinline__ uint4 ld_stream16(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void gemv_accum(const uint4& w, const float* xs, int v, int K, int batch,
+                                           float (&acc)[8]) {
+  float wf[8];
+  unpack_bf16x8(w, wf);
+#pragma unroll
+  for (int bi = 0; bi < 8; ++bi) {
+    if (bi < batch) {
+      const float4* xr = reinterpret_cast<const float4*>(xs + bi * K + v * 8);
+      float4 x0 = xr[0], x1 = xr[1];
+      acc[bi] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w + wf[4] * x1.x + wf[5] * x1.y +
+                 wf[6] * x1.z + wf[7] * x1.w;
+    }
+  }
+}
+
+constexpr int kGemvU = 6;  // 16-byte weight loads in flight per lane (memory-level parallelism)
+
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   extern __shared__ float xs[];  // [batch, K]
   for (int i = threadIdx.x; i < a.batch * a.K; i += blockDim.x) {
@@ -314,31 +416,21 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   __syncthreads();
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
+  const int nv = a.K / 8;
   const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   for (int n = blockIdx.x * warps + threadIdx.x / 32; n < a.N; n += gridDim.x * warps) {
     const uint4* w4 = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.W) +
                                                      (long long)n * a.ldw);
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int v = lane; v < a.K / 8; v += 32) {
-      uint4 w = __ldg(w4 + v);
-      uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-      float wf[8];
+    int v = lane;
+    for (; v + 32 * (kGemvU - 1) < nv; v += 32 * kGemvU) {
+      uint4 w[kGemvU];
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        float2 f = unpack_bf16x2(ws[h]);
-        wf[2 * h] = f.x;
-        wf[2 * h + 1] = f.y;
-      }
+      for (int u = 0; u < kGemvU; ++u) w[u] = ld_stream16(w4 + v + 32 * u);
 #pragma unroll
-      for (int bi = 0; bi < 8; ++bi) {
-        if (bi < a.batch) {
-          const float4* xr = reinterpret_cast<const float4*>(xs + bi * a.K + v * 8);
-          float4 x0 = xr[0], x1 = xr[1];
-          acc[bi] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
-                     wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
-        }
-      }
+      for (int u = 0; u < kGemvU; ++u) gemv_accum(w[u], xs, v + 32 * u, a.K, a.batch, acc);
     }
+    for (; v < nv; v += 32) gemv_accum(ld_stream16(w4 + v), xs, v, a.K, a.batch, acc);
 #pragma unroll
     for (int bi = 0; bi < 8; ++bi) {
       if (bi >= a.batch) break;
@@ -405,6 +497,19 @@ extern "C" int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream) {
   if (a->y_world < 0 || a->y_world > DFL_MAX_PEERS) return -5;
   LnModArgs c = *a;
   if (c.rows_per_batch <= 0) c.rows_per_batch = c.M;
+  const int nvec = c.D / 8;
+  if (nvec >= 128) {  // wide rows: one 128-thread block per row
+    const int vpt = (nvec + 127) / 128;
+    switch (vpt) {
+      case 1: ln_modulate_row_kernel<1><<<c.M, 128, 0, stream>>>(c); break;
+      case 2: ln_modulate_row_kernel<2><<<c.M, 128, 0, stream>>>(c); break;
+      case 3: ln_modulate_row_kernel<3><<<c.M, 128, 0, stream>>>(c); break;
+      case 4: ln_modulate_row_kernel<4><<<c.M, 128, 0, stream>>>(c); break;
+      case 5: ln_modulate_row_kernel<5><<<c.M, 128, 0, stream>>>(c); break;
+      default: ln_modulate_row_kernel<6><<<c.M, 128, 0, stream>>>(c); break;
+    }
+    return (int)cudaGetLastError();
+  }
   int threads = 256;
   int blocks = (int)((c.M * 32LL + threads - 1) / threads);
   int nv = (c.D / 8 + 31) / 32;

@@ -4,7 +4,7 @@ Every number is a CUDA-event time on the launching stream after warm-up, with
 an L2 flush (a 256 MB write) before each timed launch, reported as the median
 of the timed launches.  Usage::
 
-    python -m difflet_b200.bench.kernels [--only gemm,attn,ln,mx] [--cases flux_1gpu,...]
+    python -m difflet_b200.bench.kernels [--only gemm,attn,ln,mx,gemv] [--cases flux_1gpu,...]
                                          [--iters 20] [--no-ref]
 
 ``--no-ref`` skips the library comparison (used for ncu captures so the
@@ -34,13 +34,17 @@ LN_CASES = [("flux_ln", 4608, 3072), ("wan_ln_sp4", 18900, 5120)]
 
 
 def time_fn(fn, iters=20, warmup=3, flush=None):
+    """Median CUDA-event time of fn().  ``flush`` (a buffer larger than L2) is READ before
+    each call: the L2 then holds clean lines, so the timed kernel does not pay for writing
+    back a flush's dirty lines (which a write-based flush would charge to it)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     times = []
+    sink = None if flush is None else torch.empty((), device=flush.device, dtype=flush.dtype)
     for _ in range(iters):
         if flush is not None:
-            flush.zero_()
+            torch.sum(flush, out=sink)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
@@ -176,6 +180,23 @@ def bench_ln(nat, iters, flush, peaks, cases, ref):
     return rows
 
 
+GEMV_CASES = [("flux_double_mod", 1, 2 * 6 * 3072, 3072), ("flux_all_mod", 1, 19 * 12 * 3072, 3072)]
+
+
+def bench_gemv(nat, iters, flush, peaks, cases, ref):
+    """adaLN modulation GEMVs (batch 1): weight bytes streamed once per call."""
+    rows = []
+    for name, B, N, K in _sel(GEMV_CASES, cases):
+        W = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(B, K, device="cuda")
+        y = torch.empty(B, N, device="cuda")
+        t = time_fn(lambda: nat.gemv(W, x, None, y, True, False), iters, flush=flush)
+        byts = N * K * 2
+        rows.append({"kernel": "gemv", "shape": name, "ms": round(t, 4), "gbs": round(byts / t / 1e6, 1),
+                     "frac_of_measured_hbm": round(byts / t / 1e6 / peaks["hbm_gbs"], 3)})
+    return rows
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,ln")
@@ -184,9 +205,10 @@ def main(argv=None):
     ap.add_argument("--no-ref", action="store_true")
     args = ap.parse_args(argv)
     from difflet_b200 import _native
+    from difflet_b200.ops.fused import _lib
     from difflet_b200.utils.peaks import load_peaks
 
-    nat = _native.require()
+    nat = _lib()  # the native module with the DIFFLET_* kernel switches applied
     peaks = load_peaks()
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
     only = set(args.only.split(","))
@@ -199,6 +221,8 @@ def main(argv=None):
         rows += bench_attn(nat, args.iters, flush, peaks, cases, ref)
     if "ln" in only:
         rows += bench_ln(nat, args.iters, flush, peaks, cases, ref)
+    if "gemv" in only:
+        rows += bench_gemv(nat, args.iters, flush, peaks, cases, ref)
     if "mx" in only:
         rows += bench_mx(nat, args.iters, flush, peaks, cases, ref)
     if "conv" in only:

@@ -70,6 +70,8 @@ environment_variables: dict[str, Callable[[], Any]] = {
     "DIFFLET_FUSE_QKV": lambda: _str(os.environ.get("DIFFLET_FUSE_QKV"), "1"),
     # 1: the text- and image-stream GEMMs of a dual block share one grouped launch; 0: two launches
     "DIFFLET_GEMM_GROUP": lambda: _str(os.environ.get("DIFFLET_GEMM_GROUP"), "1"),
+    # softmax exponential pairs (of every 8) evaluated by the FMA-pipe polynomial in attention (0..3)
+    "DIFFLET_ATTN_POLY": lambda: _int(os.environ.get("DIFFLET_ATTN_POLY"), 0),
     # serving
     "DIFFLET_API_KEY": lambda: _str(os.environ.get("DIFFLET_API_KEY"), None),
     "DIFFLET_SERVE_QUEUE_TIMEOUT_S": lambda: _float(os.environ.get("DIFFLET_SERVE_QUEUE_TIMEOUT_S"), 30.0),

@@ -57,6 +57,7 @@ def _lib():
 
         _nat = _native.require()
         _nat.gemm_set_pair_auto(envs.DIFFLET_GEMM_PAIR != "0")
+        _nat.attention_set_poly(envs.DIFFLET_ATTN_POLY)
     return _nat
 
 
