@@ -173,7 +173,24 @@ def _world_needed(a) -> int:
     return parallel_from_args(a).world_size
 
 
+def _check_spec(a) -> None:
+    """Refuse options the model does not take before any process or weight is started."""
+    from difflet_b200.models.spec import check_cli_args, check_generate_kwargs, spec_for_model_id
+
+    spec = spec_for_model_id(a.model_id)
+    if spec is not None:
+        check_cli_args(spec, a)
+        check_generate_kwargs(spec, {k: v for k, v in _gen_kwargs(a).items() if k != "prompt"})
+
+
 def cmd_generate(a) -> int:
+    from difflet_b200.models.spec import SpecRefusal
+
+    try:
+        _check_spec(a)
+    except SpecRefusal as e:
+        print(f"difflet: {e}", file=sys.stderr)
+        return 2
     world = _world_needed(a)
     if world > 1 and not os.environ.get("DIFFLET_UNDER_TORCHRUN"):
         from difflet_b200.cli.runner import run_torchrun

@@ -181,5 +181,5 @@ def _ensure_builtins():
     register_model(ModelEntry(
         name="minimax_h3", application_factory="difflet_b200.models.minimax_h3.entry:create_application",
         hf_paths=("MiniMaxAI/MiniMax-H3", "minimax-h3"), detector=lambda m: "minimax" in m.lower(),
-        default_parallel=P(), default_shape={"height": 480, "width": 832, "num_frames": 49},
+        default_parallel=P(), default_shape={"height": 480, "width": 832, "num_frames": 124},
         capabilities=ModelCapabilities(num_attention_heads=24, is_distilled=False), output="video"))

@@ -100,7 +100,24 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
         return {"object": "list", "data": [{"id": model_id, "object": "model", "owned_by": "difflet_b200",
                                             "output": output}]}
 
+    from difflet_b200.models.spec import SpecRefusal, check_generate_kwargs, spec_for_model_id
+
+    spec = spec_for_model_id(model_id)
+
+    def _validate(req):
+        """Options the model does not take answer 400 before the request is queued."""
+        if spec is None:
+            return
+        try:
+            check_generate_kwargs(spec, req)
+        except SpecRefusal as exc:
+            raise HTTPException(400, str(exc))
+        for field, why in spec.refused_video_fields:
+            if req.get(field) is not None:
+                raise HTTPException(400, f"{field}: {why}")
+
     def _run(req):
+        _validate(req)
         try:
             return engine.generate(req, timeout=request_timeout)
         except QueueTimeout:
@@ -149,6 +166,7 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
                     req[k] = payload[k]
             if "seconds" in payload and "num_frames" not in req:
                 req["num_frames"] = int(float(payload["seconds"]) * 16) // 4 * 4 + 1
+            _validate(req)
             job = jobs.create(req)
             return job.public()
 
