@@ -299,7 +299,7 @@ QkvScatterArgs make_qkv_args(int64_t q_off, int64_t k_off, int64_t v_off, int64_
                              int64_t heads_per_rank, const std::vector<int64_t>& q_dst,
                              const std::vector<int64_t>& k_dst, const std::vector<int64_t>& v_dst, int64_t S_dst,
                              int64_t seq_off, bool out_token_major, bool kv_replicate, int64_t q_S_dst,
-                             int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off) {
+                             int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off, const c10::optional<at::Tensor>& row_sumsq, int64_t norm_total) {
   const int world = (int)q_dst.size();
   TORCH_CHECK(world >= 1 && world <= DFL_MAX_PEERS, "1..8 destinations");
   TORCH_CHECK(k_dst.size() == q_dst.size() && v_dst.size() == q_dst.size(), "dst tables differ");
@@ -343,6 +343,12 @@ QkvScatterArgs make_qkv_args(int64_t q_off, int64_t k_off, int64_t v_off, int64_
   a.seg_rows = (int)seg_rows;
   a.seg1_seq_off = (int)seg1_seq_off;
   a.seg1_rope_off = (int)seg1_rope_off;
+  if (norm_mode == 3) {
+    TORCH_CHECK(row_sumsq.has_value() && row_sumsq->defined() && row_sumsq->scalar_type() == at::kFloat &&
+                    row_sumsq->is_contiguous(), "norm_mode 3 needs row_sumsq (f32 [rows, 2], contiguous)");
+    a.row_sumsq = row_sumsq->data_ptr<float>();
+    a.norm_total = (int)norm_total;
+  }
   return a;
 }
 
@@ -353,18 +359,29 @@ void qkv_scatter(const at::Tensor& qkv, int64_t q_off, int64_t k_off, int64_t v_
                  int64_t rope_pos_off, bool rope_half, int64_t heads_per_rank,
                  std::vector<int64_t> q_dst, std::vector<int64_t> k_dst, std::vector<int64_t> v_dst,
                  int64_t S_dst, int64_t seq_off, bool out_token_major, bool kv_replicate, int64_t q_S_dst,
-                 int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off) {
+                 int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off, const c10::optional<at::Tensor>& row_sumsq, int64_t norm_total) {
   check_bf16_cuda(qkv, "qkv");
   check_rowmajor(qkv, "qkv");
   const c10::cuda::CUDAGuard guard(qkv.device());
   QkvScatterArgs a = make_qkv_args(q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos_t, sin_t,
                                    rope_pos_off, rope_half, heads_per_rank, q_dst, k_dst, v_dst, S_dst, seq_off,
                                    out_token_major, kv_replicate, q_S_dst, q_seq_off, seg_rows, seg1_seq_off,
-                                   seg1_rope_off);
+                                   seg1_rope_off, row_sumsq, norm_total);
   a.qkv = qkv.data_ptr();
   a.ld = qkv.stride(0);
   a.rows = (int)qkv.size(0);
   DFL_CHECK_RC(dfl_qkv_scatter(&a, cur_stream()), "qkv_scatter");
+}
+
+at::Tensor row_sumsq(const at::Tensor& x, int64_t off0, int64_t off1, int64_t width) {
+  check_bf16_cuda(x, "x");
+  check_rowmajor(x, "x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = at::empty({x.size(0), 2}, x.options().dtype(at::kFloat));
+  DFL_CHECK_RC(dfl_row_sumsq(x.data_ptr(), x.stride(0), (int)x.size(0), (int)off0, (int)off1, (int)width,
+                             out.data_ptr<float>(), cur_stream()),
+               "row_sumsq");
+  return out;
 }
 
 // The same description packed for the GEMM's qkv epilogue (epi = 5, argument qkv_plan).
@@ -373,11 +390,11 @@ py::bytes qkv_plan(int64_t q_off, int64_t k_off, int64_t v_off, int64_t S_src, i
                    double eps, const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t,
                    int64_t rope_pos_off, bool rope_half, int64_t heads_per_rank, std::vector<int64_t> q_dst,
                    std::vector<int64_t> k_dst, std::vector<int64_t> v_dst, int64_t S_dst, int64_t seq_off,
-                   bool out_token_major, bool kv_replicate, int64_t q_S_dst, int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off) {
+                   bool out_token_major, bool kv_replicate, int64_t q_S_dst, int64_t q_seq_off, int64_t seg_rows, int64_t seg1_seq_off, int64_t seg1_rope_off, const c10::optional<at::Tensor>& row_sumsq, int64_t norm_total) {
   QkvScatterArgs a = make_qkv_args(q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos_t, sin_t,
                                    rope_pos_off, rope_half, heads_per_rank, q_dst, k_dst, v_dst, S_dst, seq_off,
                                    out_token_major, kv_replicate, q_S_dst, q_seq_off, seg_rows, seg1_seq_off,
-                                   seg1_rope_off);
+                                   seg1_rope_off, row_sumsq, norm_total);
   return py::bytes(reinterpret_cast<const char*>(&a), sizeof(a));
 }
 
@@ -718,6 +735,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("row0") = 0, py::arg("rows") = -1);
   m.def("qkv_scatter", &qkv_scatter);
   m.def("qkv_plan", &qkv_plan);
+  m.def("row_sumsq", &row_sumsq);
   m.def("gemv", &gemv, py::arg("W"), py::arg("x"), py::arg("bias") = py::none(),
         py::arg("out") = py::none(), py::arg("silu_in") = false, py::arg("silu_out") = false);
   m.def("euler_step", &euler_step, py::arg("x32"), py::arg("x16"), py::arg("v"),

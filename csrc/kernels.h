@@ -134,8 +134,18 @@ typedef struct QkvScatterArgs {
   // s >= seg_rows of each batch land at seg1_seq_off + (s - seg_rows) and use RoPE
   // table row seg1_rope_off + (s - seg_rows).  0 = one segment.
   int seg_rows, seg1_seq_off, seg1_rope_off;
+  // norm_mode 3 (across-heads RMS under tensor parallelism): the row's sum of squares
+  // over ALL heads, already reduced across ranks: row_sumsq[2 r] (q), [2 r + 1] (k);
+  // rstd = rsqrt(sum / norm_total + eps), the weights wq / wk hold this rank's heads.
+  const float* row_sumsq;
+  int norm_total;
 } QkvScatterArgs;
 int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream);
+
+// Per-row partial sums of squares of two column blocks (q and k of a tensor-parallel
+// shard): out[2 r + i] = sum_c x[r, off_i + c]^2 over c < width (0 when off_i < 0).
+int dfl_row_sumsq(const void* x, long long ld, int rows, int off0, int off1, int width, float* out,
+                  cudaStream_t stream);
 
 // y[b, n] = act_in(x[b, :]) . W[n, :] + bias[n]   (bf16 W, f32 x / y; batch <= 8)
 typedef struct GemvArgs {

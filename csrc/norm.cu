@@ -313,6 +313,9 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
     float tk = red[1][0] + red[1][1] + red[1][2] + red[1][3];
     rq = rsqrtf(tq / (float)(a.H * DH) + a.eps);
     rk = rsqrtf(tk / (float)(a.H * DH) + a.eps);
+  } else if (a.norm_mode == 3) {  // sums over all heads, reduced across tensor-parallel ranks
+    rq = rsqrtf(a.row_sumsq[2 * row] / (float)a.norm_total + a.eps);
+    rk = rsqrtf(a.row_sumsq[2 * row + 1] / (float)a.norm_total + a.eps);
   }
 
   for (int h = warp; h < a.H; h += 4) {
@@ -344,7 +347,7 @@ __global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
 #pragma unroll
           for (int e = 0; e < E; ++e) x[e] *= __bfloat162float(wn[lane * E + e]);
         }
-      } else if (a.norm_mode == 2) {
+      } else if (a.norm_mode >= 2) {
         float rr = which == 0 ? rq : rk;
 #pragma unroll
         for (int e = 0; e < E; ++e) x[e] *= rr;
@@ -524,12 +527,48 @@ extern "C" int dfl_ln_modulate(const LnModArgs* a, cudaStream_t stream) {
   return (int)cudaGetLastError();
 }
 
+// One warp per row: sums of squares of two column blocks (16-byte loads).
+__global__ void __launch_bounds__(256) row_sumsq_kernel(const __nv_bfloat16* x, long long ld, int rows, int off0,
+                                                        int off1, int width, float* out) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int off = i == 0 ? off0 : off1;
+    float ss = 0.f;
+    if (off >= 0) {
+      const uint4* p = reinterpret_cast<const uint4*>(x + (long long)row * ld + off);
+      for (int v = lane; v < width / 8; v += 32) {
+        float f[8];
+        unpack_bf16x8(p[v], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) out[2 * row + i] = ss;
+  }
+}
+
+extern "C" int dfl_row_sumsq(const void* x, long long ld, int rows, int off0, int off1, int width, float* out,
+                             cudaStream_t stream) {
+  if (rows == 0) return 0;
+  if (width % 8 || ld % 8 || (off0 > 0 && off0 % 8) || (off1 > 0 && off1 % 8)) return -2;
+  if (reinterpret_cast<uintptr_t>(x) & 15) return -3;
+  const int blocks = (rows * 32 + 255) / 256;
+  row_sumsq_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), ld, rows, off0, off1,
+                                                width, out);
+  return (int)cudaGetLastError();
+}
+
 extern "C" int dfl_qkv_scatter(const QkvScatterArgs* a, cudaStream_t stream) {
   if (a->rows == 0) return 0;
   if (a->world < 1 || a->world > DFL_MAX_PEERS) return -2;
   if (a->kv_replicate ? (a->heads_per_rank != a->H || a->out_token_major) : a->heads_per_rank * a->world != a->H)
     return -3;
   if (a->ld % 8) return -4;
+  if (a->norm_mode == 3 && (!a->row_sumsq || a->norm_total <= 0)) return -7;
   if (a->rope_dims && (a->rope_dims > a->dh || (a->rope_dims / 2) % (a->dh / 32) || !a->rope_half || a->rope_heads))
     return -6;
   if (a->dh == 128)

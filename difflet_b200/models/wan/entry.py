@@ -55,6 +55,13 @@ class WanEngine:
 
             seq_par = make_sequence_parallel(self.parallel, dev)
             cfg_par = make_cfg_parallel(self.parallel, dev)
+        if self.parallel.tp_degree > 1:  # heads / FFN columns over the tp axis (across-heads q/k RMS all-reduced)
+            from difflet_b200.parallel.tp import make_tensor_parallel, shard_wan_weights
+
+            tp = make_tensor_parallel(self.parallel, dev)
+            for e in experts:
+                e.tp = tp
+                e.w = shard_wan_weights(e.cfg, e.w, tp.world, tp.rank)
         from difflet_b200.quant.apply import quantize_engine_model
 
         self.quant_report = [quantize_engine_model(e, "wan", self.kw) for e in experts]

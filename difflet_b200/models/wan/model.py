@@ -76,6 +76,7 @@ class WanTransformer:
         self.cfg = cfg
         self.w = weights
         self.par = None
+        self.tp = None  # tensor-parallel context (heads / FFN columns sharded; see parallel/tp.py)
         self._ws = {}
         self._rope = {}
         self._ones = {}
@@ -150,6 +151,24 @@ class WanTransformer:
                 self._rope[grid] = rope_tables(ids, self.cfg.axes_dim, self.cfg.theta, device=self.device)
         return self._rope[grid]
 
+    def _qk_norm(self, buf, q_off: int, k_off: int) -> dict:
+        """Across-heads q/k RMS arguments of ``qkv_scatter``.  Under TP each rank holds D/T of
+        the row: the per-row sums of squares over its heads are summed over the tp ranks first
+        (a [rows, 2] f32 all-reduce), then every rank normalises with the full-row RMS."""
+        if self.tp is None:
+            return {"norm_mode": 2}
+        width = self.cfg.hidden // self.tp.world
+        rs = F.row_sumsq(buf, q_off, k_off, width)
+        self.tp.allreduce_rows(rs)
+        return {"norm_mode": 3, "row_sumsq": rs, "norm_total": self.cfg.hidden}
+
+    def _row_linear(self, xin, wt, bias, out, gate, rpb):
+        """Output projections fused with ``out += gate * (.)`` (row-parallel under TP)."""
+        if self.tp is not None:
+            self.tp.row_linear(xin, wt, bias, out=out, gate=gate, resid=out, rows_per_batch=rpb)
+        else:
+            F.linear(xin, wt, bias, out=out, gate=gate, resid=out, rows_per_batch=rpb)
+
     def _ones_gate(self, B):
         if B not in self._ones:
             dt = torch.float64 if self.dtype == torch.float64 else torch.float32
@@ -160,8 +179,10 @@ class WanTransformer:
         key = (B, S_loc)
         if key in self._ws:
             return self._ws[key]
-        cfg, par = self.cfg, self.par
+        cfg, par, tp = self.cfg, self.par, self.tp
         D, H, dh = cfg.hidden, cfg.heads, cfg.head_dim
+        T = tp.world if tp is not None else 1
+        Dl, Ht = D // T, H // T  # this rank's attention columns / heads
         world = par.world if par is not None else 1
         S = S_loc * world
         dev, dt = self.device, self.dtype
@@ -169,13 +190,15 @@ class WanTransformer:
         pe = (lambda *s: par.empty(s, dt)) if par is not None else e  # noqa: E731
         if par is not None:
             par.check_heads(H)
-        ws = {"S": S, "x": e(B * S_loc, D), "norm": e(B * S_loc, D), "qkv": e(B * S_loc, 3 * D),
-              "mlp": e(B * S_loc, cfg.ffn), "cq": e(B, H, S_loc, dh), "cqin": e(B * S_loc, D),
-              "cattn": e(B, S_loc, D), "attn": pe(B, S_loc, D)}
+        # the residual stream is written by every rank's TP reducer: symmetric memory under TP
+        x = tp.empty((B * S_loc, D), dt) if tp is not None else e(B * S_loc, D)
+        ws = {"S": S, "x": x, "norm": e(B * S_loc, D), "qkv": e(B * S_loc, 3 * Dl),
+              "mlp": e(B * S_loc, cfg.ffn // T), "cq": e(B, Ht, S_loc, dh), "cqin": e(B * S_loc, Dl),
+              "cattn": e(B, S_loc, Dl), "attn": pe(B, S_loc, Dl)}
         if par is not None:  # the CP mode decides the q/k/v layout
             ws["q"], ws["k"], ws["v"] = par.layout(B, H, dh, S_loc, S, dt)
         else:
-            ws["q"], ws["k"], ws["v"] = e(B, H, S, dh), e(B, H, S, dh), e(B, H, S, dh)
+            ws["q"], ws["k"], ws["v"] = e(B, Ht, S, dh), e(B, Ht, S, dh), e(B, Ht, S, dh)
         self._ws[key] = ws
         return ws
 
@@ -185,7 +208,8 @@ class WanTransformer:
         prompt.  text [B, L, text_dim] -> list of (k, v) [B, H, L, dh]."""
         cfg, w = self.cfg, self.w
         B, L, _ = text.shape
-        D, H, dh = cfg.hidden, cfg.heads, cfg.head_dim
+        T = self.tp.world if self.tp is not None else 1
+        D, H, dh = cfg.hidden // T, cfg.heads // T, cfg.head_dim  # this rank's columns / heads
         if text_valid is not None:  # zero the padding rows (reference pad-zeroing)
             mask = torch.arange(L, device=text.device)[None, :] < text_valid.to(text.device)[:, None]
             text = text * mask[..., None].to(text.dtype)
@@ -199,7 +223,7 @@ class WanTransformer:
             k = torch.empty(B, H, L, dh, device=ctx.device, dtype=ctx.dtype)
             v = torch.empty_like(k)
             F.qkv_scatter(kv, q_off=-1, k_off=0, v_off=D, S_src=L, H=H, dh=dh, q_dst=None, k_dst=[k], v_dst=[v],
-                          S_dst=L, norm_mode=2, wk=w[p + "ckn"], eps=cfg.eps, heads_per_rank=H)
+                          S_dst=L, wk=w[p + "ckn"], eps=cfg.eps, heads_per_rank=H, **self._qk_norm(kv, -1, 0))
             kvs.append((k, v))
         return kvs
 
@@ -218,9 +242,12 @@ class WanTransformer:
     def forward(self, x_tokens, timestep, context, *, grid, mods=None, temb=None):
         """x_tokens [B, S(local), C*pt*ph*pw]; timestep [B] in [0, 1000]; context = the
         cached per-block (k, v) from ``prepare_context``; grid = (t, h, w) token grid."""
-        cfg, w, par = self.cfg, self.w, self.par
+        cfg, w, par, tp = self.cfg, self.w, self.par, self.tp
+        if tp is not None and par is not None:
+            raise NotImplementedError("Wan tensor parallelism composes with cfg-parallel here, not with cp")
         B, S_loc, _ = x_tokens.shape
-        D, H, dh = cfg.hidden, cfg.heads, cfg.head_dim
+        T = tp.world if tp is not None else 1
+        D, H, dh = cfg.hidden // T, cfg.heads // T, cfg.head_dim  # this rank's columns / heads
         world = par.world if par is not None else 1
         rank = par.rank if par is not None else 0
         Hl = par.heads_local(H) if par is not None else H
@@ -246,25 +273,24 @@ class WanTransformer:
             m = mods[i]  # [B, 6, D]: shift, scale, gate, c_shift, c_scale, c_gate
             F.ln_modulate(x, shift=m[:, 0], scale=m[:, 1], eps=eps, rows_per_batch=S_loc, out=norm)
             F.linear(norm, w[p + "qkv.w"], w[p + "qkv.b"], out=ws["qkv"])
-            F.qkv_scatter(ws["qkv"], q_off=0, k_off=D, v_off=2 * D, S_src=S_loc, H=H, dh=dh, **tgt, norm_mode=2,
-                          wq=w[p + "qn"], wk=w[p + "kn"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos)
+            F.qkv_scatter(ws["qkv"], q_off=0, k_off=D, v_off=2 * D, S_src=S_loc, H=H, dh=dh, **tgt,
+                          wq=w[p + "qn"], wk=w[p + "kn"], eps=eps, cos=cos, sin=sin, rope_pos_off=pos,
+                          **self._qk_norm(ws["qkv"], 0, D))
             self._self_attention(ws, B, S_loc, Hl)
-            F.linear(ws["attn"].view(B * S_loc, D), w[p + "o.w"], w[p + "o.b"], out=x, gate=m[:, 2], resid=x,
-                     rows_per_batch=S_loc)
+            self._row_linear(ws["attn"].view(B * S_loc, D), w[p + "o.w"], w[p + "o.b"], x, m[:, 2], S_loc)
             # cross-attention (local queries, all heads, cached text K/V)
             F.ln_modulate(x, w=w[p + "n2.w"], b=w[p + "n2.b"], eps=eps, out=norm)
             F.linear(norm, w[p + "cq.w"], w[p + "cq.b"], out=ws["cqin"])
             F.qkv_scatter(ws["cqin"], q_off=0, k_off=-1, v_off=-1, S_src=S_loc, H=H, dh=dh, q_dst=[ws["cq"]],
-                          k_dst=None, v_dst=None, S_dst=S_loc, norm_mode=2, wq=w[p + "cqn"], eps=eps,
-                          heads_per_rank=H)
+                          k_dst=None, v_dst=None, S_dst=S_loc, wq=w[p + "cqn"], eps=eps, heads_per_rank=H,
+                          **self._qk_norm(ws["cqin"], 0, -1))
             ck, cv = context[i]
             F.attention(ws["cq"], ck, cv, 1.0 / math.sqrt(dh), out=ws["cattn"].view(B, S_loc, H, dh).permute(0, 2, 1, 3))
-            F.linear(ws["cattn"].view(B * S_loc, D), w[p + "co.w"], w[p + "co.b"], out=x, gate=ones, resid=x,
-                     rows_per_batch=S_loc)
+            self._row_linear(ws["cattn"].view(B * S_loc, D), w[p + "co.w"], w[p + "co.b"], x, ones, S_loc)
             # feed-forward
             F.ln_modulate(x, shift=m[:, 3], scale=m[:, 4], eps=eps, rows_per_batch=S_loc, out=norm)
             F.linear(norm, w[p + "up.w"], w[p + "up.b"], out=ws["mlp"], act="gelu")
-            F.linear(ws["mlp"], w[p + "down.w"], w[p + "down.b"], out=x, gate=m[:, 5], resid=x, rows_per_batch=S_loc)
+            self._row_linear(ws["mlp"], w[p + "down.w"], w[p + "down.b"], x, m[:, 5], S_loc)
         if temb is None:
             temb, _ = self.time_embed(timestep)
         fm = (w["out.sst"][None] + temb[:, None].to(w["out.sst"].dtype)).contiguous()  # [B, 2, D]: shift, scale

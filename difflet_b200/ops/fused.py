@@ -15,6 +15,7 @@ Ops:
   linear_qkv    linear whose q/k/v column blocks go through qkv_scatter inside the
                 GEMM epilogue (no round trip of the qkv rows through HBM)
   linear_group  two linear / linear_qkv calls with one epilogue kind as one launch
+  row_sumsq     per-row sums of squares of q / k column blocks (TP across-heads RMS)
   attention     softmax(scale q k^T) v with key window and LSE
   gemv          modulation linears (M <= 8), f32 in/out, optional SiLU
   euler_step    x += dt * (u + s (c - u)) on f32 latents (+ bf16 mirror)
@@ -207,7 +208,7 @@ def _rope_cpu(x, cos, sin, half):
 def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, S_dst, seq_off=0,
                 norm_mode=1, wq=None, wk=None, eps=1e-6, cos=None, sin=None, rope_pos_off=0,
                 rope_half=False, heads_per_rank=None, token_major=False, kv_replicate=False, q_S_dst=0,
-                q_seq_off=0, seg_rows=0, seg1_seq_off=0, seg1_rope_off=0):
+                q_seq_off=0, seg_rows=0, seg1_seq_off=0, seg1_rope_off=0, row_sumsq=None, norm_total=0):
     """Normalise + rotate q/k of a token-major qkv buffer and scatter q/k/v by head.
 
     ``q_dst`` etc. are lists (one tensor per destination rank; a single-GPU call
@@ -219,6 +220,9 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
     ``q_seq_off + s``).  ``seg_rows`` > 0: rows ``s >= seg_rows`` of each batch form a
     second segment placed at ``seg1_seq_off + (s - seg_rows)`` with RoPE row
     ``seg1_rope_off + (s - seg_rows)`` (a rank's [text ; image] slice of a joint sequence).
+    ``norm_mode`` 3: across-heads RMS whose per-row sums of squares over all heads
+    (``row_sumsq`` f32 [rows, 2]: q, k; already reduced over tensor-parallel ranks) are
+    given; ``norm_total`` = number of values they sum (all heads x dh).
     """
     qkv2 = _rows2d(qkv)
     world = len(q_dst if q_dst is not None else (k_dst if k_dst is not None else v_dst))
@@ -231,7 +235,7 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
         native().qkv_scatter(qkv2, *_scatter_args(q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, S_dst,
                                                   seq_off, norm_mode, wq, wk, eps, cos, sin, rope_pos_off, rope_half,
                                                   hpr, token_major, kv_replicate, q_S_dst, q_seq_off, seg_rows,
-                                                  seg1_seq_off, seg1_rope_off))
+                                                  seg1_seq_off, seg1_rope_off, row_sumsq, norm_total))
         return
     if 0 < seg_rows < S_src:  # oracle: one call per segment
         Bn = qkv2.shape[0] // S_src
@@ -241,10 +245,13 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
                       heads_per_rank=heads_per_rank, token_major=token_major, kv_replicate=kv_replicate,
                       q_S_dst=q_S_dst)
         n1 = S_src - seg_rows
+        rs3 = None if row_sumsq is None else row_sumsq.view(Bn, S_src, 2)
         qkv_scatter(x3[:, :seg_rows].reshape(Bn * seg_rows, -1), S_src=seg_rows, seq_off=seq_off,
-                    rope_pos_off=rope_pos_off, q_seq_off=q_seq_off, **common)
+                    rope_pos_off=rope_pos_off, q_seq_off=q_seq_off, norm_total=norm_total,
+                    row_sumsq=None if rs3 is None else rs3[:, :seg_rows].reshape(-1, 2), **common)
         qkv_scatter(x3[:, seg_rows:].reshape(Bn * n1, -1), S_src=n1, seq_off=seg1_seq_off,
-                    rope_pos_off=seg1_rope_off, q_seq_off=q_seq_off + seg_rows, **common)
+                    rope_pos_off=seg1_rope_off, q_seq_off=q_seq_off + seg_rows, norm_total=norm_total,
+                    row_sumsq=None if rs3 is None else rs3[:, seg_rows:].reshape(-1, 2), **common)
         return
     rows = qkv2.shape[0]
     B = rows // S_src
@@ -256,9 +263,13 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
 
     q, k, v = take(q_off), take(k_off), take(v_off)
 
-    def norm(t, wn):
+    def norm(t, wn, which=0):
         if t is None or norm_mode == 0:
             return t
+        if norm_mode == 3:
+            ss = row_sumsq[:, which].to(ct).view(B, S_src, 1, 1)
+            t = t * torch.rsqrt(ss / norm_total + eps)
+            return t * wn.to(ct).view(H, dh) if wn is not None else t
         if norm_mode == 1:
             t = t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps)
             return t * wn.to(ct) if wn is not None else t
@@ -268,7 +279,7 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
             tf = tf * wn.to(ct)
         return tf.view(B, S_src, H, dh)
 
-    q, k = norm(q, wq), norm(k, wk)
+    q, k = norm(q, wq, 0), norm(k, wk, 1)
     q, k, v = (None if t is None else t.permute(0, 2, 1, 3) for t in (q, k, v))  # B, H, S, dh
     if cos is not None:
         c = cos[rope_pos_off:rope_pos_off + S_src].to(ct)
@@ -306,12 +317,23 @@ def qkv_scatter(qkv, *, q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, 
 
 def _scatter_args(q_off, k_off, v_off, S_src, H, dh, q_dst, k_dst, v_dst, S_dst, seq_off, norm_mode, wq, wk, eps,
                   cos, sin, rope_pos_off, rope_half, hpr, token_major, kv_replicate, q_S_dst, q_seq_off, seg_rows=0,
-                  seg1_seq_off=0, seg1_rope_off=0):
+                  seg1_seq_off=0, seg1_rope_off=0, row_sumsq=None, norm_total=0):
     """Positional arguments of the native head scatter (after the source rows)."""
     ptr = lambda ts: [0 if t is None else (t if isinstance(t, int) else t.data_ptr()) for t in ts]  # noqa: E731
     return (q_off, k_off, v_off, S_src, H, dh, norm_mode, wq, wk, eps, cos, sin, rope_pos_off, rope_half, hpr,
             ptr(q_dst), ptr(k_dst), ptr(v_dst), S_dst, seq_off, token_major, kv_replicate, q_S_dst, q_seq_off,
-            seg_rows, seg1_seq_off, seg1_rope_off)
+            seg_rows, seg1_seq_off, seg1_rope_off, row_sumsq, norm_total)
+
+
+def row_sumsq(x, off0: int, off1: int, width: int) -> torch.Tensor:
+    """f32 [rows, 2]: per-row sums of squares of columns [off_i, off_i + width) (0 for off_i < 0)."""
+    x2 = _rows2d(x)
+    if x2.is_cuda:
+        return native().row_sumsq(x2, off0, off1, width)
+    ct = torch.float64 if x2.dtype == torch.float64 else torch.float32
+    cols = [x2[:, o:o + width].to(ct).pow(2).sum(1) if o >= 0 else torch.zeros(x2.shape[0], dtype=ct)
+            for o in (off0, off1)]
+    return torch.stack(cols, 1)
 
 
 def _qkv_epilogue_ok(sc: dict, act) -> bool:

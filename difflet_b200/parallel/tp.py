@@ -1,4 +1,4 @@
-"""Tensor parallelism for the MMDiT families (Megatron column / row split).
+"""Tensor parallelism for the MMDiT families and Wan (Megatron column / row split).
 
 Column-parallel linears (q/k/v, MLP up, FLUX's single-block [q|mlp|k|v]) hold this
 rank's heads / MLP columns and need no communication; attention runs on the local
@@ -73,6 +73,39 @@ def shard_mmdit_weights(cfg, w: dict, tp: int, rank: int) -> dict:
     return out
 
 
+def shard_wan_weights(cfg, w: dict, tp: int, rank: int) -> dict:
+    """This rank's slices of a Wan transformer's weights: q/k/v, cross-attention q and k/v,
+    the MLP up projection and the across-heads q/k norm weights by heads / columns
+    (column-parallel); the attention / cross-attention outputs and MLP down by K
+    (row-parallel, bias added once by the reducer); everything else replicated."""
+    if tp == 1:
+        return dict(w)
+    D, Fh, H = cfg.hidden, cfg.ffn, cfg.heads
+    if H % tp or Fh % tp:
+        raise ValueError(f"tensor parallelism needs heads ({H}) and FFN width ({Fh}) divisible by tp={tp}")
+    Dl, Fl = D // tp, Fh // tp
+    d0, d1, f0, f1 = rank * Dl, (rank + 1) * Dl, rank * Fl, (rank + 1) * Fl
+    out = {}
+    for k, t in w.items():
+        name = k.rsplit(".", 2)[-2:] if k.startswith("blk.") else None
+        leaf = ".".join(name) if name else k
+        if not k.startswith("blk."):
+            out[k] = t
+        elif leaf in ("qkv.w", "qkv.b", "ckv.w", "ckv.b"):
+            out[k] = torch.cat([p[d0:d1] for p in t.split(D, 0)], 0).contiguous()
+        elif leaf in ("cq.w", "cq.b") or k.endswith((".qn", ".kn", ".cqn", ".ckn")):
+            out[k] = t[d0:d1].contiguous()
+        elif leaf in ("up.w", "up.b"):
+            out[k] = t[f0:f1].contiguous()
+        elif leaf in ("o.w", "co.w"):
+            out[k] = t[:, d0:d1].contiguous()
+        elif leaf == "down.w":
+            out[k] = t[:, f0:f1].contiguous()
+        else:
+            out[k] = t  # output biases (added once by the reducer), norm affine
+    return out
+
+
 class _TPBase(_Base):
     kind = "tp"
     sp = False  # Megatron sequence parallelism: residual rows sharded, AG in the norm, RS in the reducer
@@ -121,6 +154,24 @@ class PeerTP(_TPBase, PeerBase):
         nat.tp_reduce(slots, rpr, W, rows, N, r * rpr, b, gate, rows_per_batch if gate is not None else 0,
                       resid if gate is not None else None, dst, out.stride(0), r * rpr)
         self.heap.barrier()  # the slots are free again (and, all-reduce, every row is everywhere)
+
+    def allreduce_rows(self, t: torch.Tensor) -> torch.Tensor:
+        """In-place sum over the tp ranks of a small f32 tensor (per-row partial statistics):
+        each rank stores its copy into slot ``rank`` of every rank's symmetric buffer, one
+        device barrier, then every rank adds the slots in rank order (identical results).
+        Two alternating buffers make one barrier per call enough."""
+        n = t.numel()
+        key = ("ar", n)
+        bufs = self._slots.get(key)
+        if bufs is None:
+            bufs = self._slots[key] = [self.heap.empty((self.world, n), torch.float32) for _ in range(2)]
+            self._ar_turn = 0
+        buf = bufs[self._ar_turn]
+        self._ar_turn ^= 1
+        F.native().peer_put_f32(t.reshape(-1), self.heap.peer_ptrs(buf), self.rank * n)
+        self.heap.barrier()
+        torch.sum(buf, 0, out=t.view(-1))
+        return t
 
     def ln_gather(self, x, out, **kw):
         """Sequence-parallel norm: this rank normalises its own rows of ``x`` and stores them
@@ -171,6 +222,10 @@ class CollectiveTP(_TPBase):
         for r in range(self.world):
             x[r * rpr:min(M, (r + 1) * rpr)] = parts[r][r * rpr:min(M, (r + 1) * rpr)]
 
+    def allreduce_rows(self, t: torch.Tensor) -> torch.Tensor:
+        dist.all_reduce(t, group=self.group)
+        return t
+
     def row_linear(self, x, w, b=None, *, out, gate=None, resid=None, rows_per_batch=0):
         if isinstance(w, F.MXWeight):
             w = w.dequantize()
@@ -212,4 +267,4 @@ def _make_tp(parallel, device, transport):
     return CollectiveTP(group, ranks, device)
 
 
-__all__ = ["CollectiveTP", "PeerTP", "make_tensor_parallel", "shard_mmdit_weights"]
+__all__ = ["CollectiveTP", "PeerTP", "make_tensor_parallel", "shard_mmdit_weights", "shard_wan_weights"]

@@ -105,7 +105,7 @@ def test_qkv_scatter_norm_rope(native, dh):
     k = torch.zeros_like(q)
     v = torch.zeros_like(q)
     native.qkv_scatter(qkv, 0, D, 2 * D, S, H, dh, 1, wq, wk, 1e-6, cos, sin, off, False, H,
-                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S_dst, off, False, False, 0, 0, 0, 0, 0)
+                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S_dst, off, False, False, 0, 0, 0, 0, 0, None, 0)
     torch.cuda.synchronize()
     x = qkv.float().view(B, S, 3, H, dh).permute(2, 0, 3, 1, 4)  # 3,B,H,S,dh
 
@@ -132,7 +132,7 @@ def test_qkv_scatter_across_heads_half_rope(native):
     k = torch.empty_like(q)
     v = torch.empty_like(q)
     native.qkv_scatter(qkv, 0, D, 2 * D, S, H, dh, 2, wq, wk, 1e-6, cos, sin, 0, True, H,
-                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S, 0, True, False, 0, 0, 0, 0, 0)
+                       [q.data_ptr()], [k.data_ptr()], [v.data_ptr()], S, 0, True, False, 0, 0, 0, 0, 0, None, 0)
     torch.cuda.synchronize()
     x = qkv.float().view(S, 3, D)
     qn = x[:, 0] * torch.rsqrt(x[:, 0].pow(2).mean(-1, keepdim=True) + 1e-6) * wq.float()
@@ -365,3 +365,32 @@ def test_gemm_cta_pair(native, M, N, K):
     _close(g, ref_g)
     _close(r, ref_r)
     assert native.error_word(0)[0].item() == 0
+
+
+def test_row_sumsq_and_external_rms_norm(native):
+    """Across-heads q/k RMS from supplied per-row sums (the tensor-parallel path): the
+    sums kernel and qkv_scatter norm_mode 3 against the fp32 oracle."""
+    from difflet_b200.ops import fused as F
+
+    torch.manual_seed(31)
+    S, H, dh = 70, 4, 128
+    D = H * dh
+    qkv = torch.randn(S, 3 * D, device="cuda", dtype=torch.bfloat16)
+    rs = F.row_sumsq(qkv, 0, D, D)
+    ref = torch.stack([qkv[:, :D].float().pow(2).sum(1), qkv[:, D:2 * D].float().pow(2).sum(1)], 1)
+    _close(rs, ref, 1e-4)
+    rs_total = rs * 2.0  # as if the other half of the heads lived on another rank with equal sums
+    wq = torch.randn(D, device="cuda", dtype=torch.bfloat16)
+    wk = torch.randn(D, device="cuda", dtype=torch.bfloat16)
+    q = torch.empty(1, H, S, dh, device="cuda", dtype=torch.bfloat16)
+    k, v = torch.empty_like(q), torch.empty_like(q)
+    kw = dict(q_off=0, k_off=D, v_off=2 * D, S_src=S, H=H, dh=dh, S_dst=S, norm_mode=3, eps=1e-6,
+              norm_total=2 * D, heads_per_rank=H)
+    F.qkv_scatter(qkv, q_dst=[q], k_dst=[k], v_dst=[v], wq=wq, wk=wk, row_sumsq=rs_total, **kw)
+    qc, kc, vc = (torch.zeros(1, H, S, dh) for _ in range(3))
+    F.qkv_scatter(qkv.cpu().float(), q_dst=[qc], k_dst=[kc], v_dst=[vc], wq=wq.cpu().float(), wk=wk.cpu().float(),
+                  row_sumsq=rs_total.cpu(), **kw)
+    torch.cuda.synchronize()
+    _close(q, qc.cuda())
+    _close(k, kc.cuda())
+    _close(v, vc.cuda())

@@ -67,3 +67,30 @@ def test_wan_cp_matches_dense(mode):
     from difflet_b200.parallel.testing import run_ranks
 
     assert max(run_ranks(_sp, 2, mode, timeout=240)) < 1e-10
+
+
+def _tp(rank, world):
+    import torch.distributed as dist
+
+    from difflet_b200.parallel.tp import CollectiveTP, shard_wan_weights
+
+    cfg = get_wan_config("tiny-wan", heads=4, hidden=512, ffn=1024)
+    m = WanTransformer.random_init(cfg, dtype=torch.float64, seed=6)
+    lat, text = _inputs(cfg)
+    x = patchify(lat)
+    t = torch.tensor([500.0], dtype=torch.float64)
+    dense = m(x, t, m.prepare_context(text), grid=(3, 4, 6))
+    m2 = WanTransformer(cfg, shard_wan_weights(cfg, m.w, world, rank))
+    m2.tp = CollectiveTP(dist.group.WORLD, list(range(world)), torch.device("cpu"))
+    out = m2(x, t, m2.prepare_context(text), grid=(3, 4, 6))
+    return (out - dense).abs().max().item()
+
+
+@pytest.mark.multirank
+@pytest.mark.parametrize("world", [2, 4])
+def test_wan_tensor_parallel_matches_dense(world):
+    """Heads / FFN columns over tp ranks; the across-heads q/k RMS (self- and cross-attention,
+    and the cached text keys) uses per-row sums of squares all-reduced over the ranks."""
+    from difflet_b200.parallel.testing import run_ranks
+
+    assert max(run_ranks(_tp, world, timeout=240)) < 1e-10
