@@ -61,6 +61,26 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             errs[name] = ((out - dense).norm() / dense.norm()).item()
             tp.close()
+        # Wan under TP: across-heads q/k RMS from all-reduced per-row sums (peer memory and NCCL)
+        from difflet_b200.models.wan.model import WanTransformer, get_wan_config, patchify
+        from difflet_b200.parallel.tp import shard_wan_weights
+
+        wcfg = get_wan_config("tiny-wan", heads=4, hidden=512, ffn=1024)
+        wm = WanTransformer.random_init(wcfg, device="cuda", dtype=torch.bfloat16, seed=12)
+        lat = torch.randn(1, 16, 3, 16, 24, generator=g).cuda().bfloat16()
+        text = torch.randn(1, wcfg.text_len, wcfg.text_dim, generator=g).cuda().bfloat16()
+        tw = torch.tensor([500.0], device="cuda")
+        wx = patchify(lat)
+        wdense = wm(wx, tw, wm.prepare_context(text), grid=(3, 8, 12)).float()
+        for name, cls in (("wan_peer_tp", PeerTP), ("wan_nccl_tp", CollectiveTP)):
+            tp = cls(dist.group.WORLD, list(range(world)), torch.device("cuda", rank))
+            w2 = WanTransformer(wcfg, shard_wan_weights(wcfg, wm.w, world, rank))
+            w2.tp = tp
+            for _ in range(2):
+                out = w2(wx, tw, w2.prepare_context(text), grid=(3, 8, 12)).float()
+            torch.cuda.synchronize()
+            errs[name] = ((out - wdense).norm() / wdense.norm()).item()
+            tp.close()
         _native.check_device_errors()
         dist.barrier()
         dist.destroy_process_group()
