@@ -34,7 +34,9 @@ using namespace dfl;
 constexpr int kBM = 128;   // queries per Q tile
 constexpr int kBN = 128;   // keys per tile
 constexpr int kD = 128;    // head dim
-constexpr int kNS = 2;     // K/V ring depth
+// K and V tiles share one FIFO ring of shared-memory slots, loaded in the order
+// K0, V0, K1, V1, ... and freed in the same order (K_j after QK_1(j), V_j after PV_1(j)),
+// so a slot is refilled as soon as the tile loaded kRing loads earlier is consumed.
 constexpr int kTileBytes = 128 * kD * 2;  // 32 KB (two 16 KB swizzle chunks)
 constexpr int kChunk = 16384;
 
@@ -47,11 +49,11 @@ struct AttnSmem {
   static constexpr int kMmaWarp = 4 * QT + 1;
   static constexpr uint32_t kTmemCols = QT == 2 ? 512 : 256;
   static constexpr int kQ = 0;                              // QT tiles
-  static constexpr int kK = kQ + QT * kTileBytes;           // kNS tiles
-  static constexpr int kV = kK + kNS * kTileBytes;          // kNS tiles
-  static constexpr int kBar = kV + kNS * kTileBytes;
-  // q_full, k_full[NS], v_full[NS], k_empty[NS], v_empty[NS], s_full[2], p_full[2][2], o_full
-  static constexpr int kNumBars = 1 + 4 * kNS + 2 + 4 + 1;
+  static constexpr int kRing = QT == 2 ? 5 : 6;             // K/V slots (224 KB of smem with Q)
+  static constexpr int kKV = kQ + QT * kTileBytes;
+  static constexpr int kBar = kKV + kRing * kTileBytes;
+  // q_full, kv_full[R], kv_empty[R], s_full[2], p_full[2][2], o_full
+  static constexpr int kNumBars = 1 + 2 * kRing + 2 + 4 + 1;
   static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -160,7 +162,17 @@ struct AttnParams {
   float* acc_o;    // f32 [B, H, Sq, 128] running output (merge modes)
   float* acc_lse;  // f32 [B, H, Sq] running log-sum-exp
   int merge_mode;  // 0 none, 1 first partial, 2 merge, 3 merge + final bf16 store
+  long long* trace;
 };
+
+// Diagnostics (builds with -DDFL_ATTN_TRACE only): SM clock at event ev of key tile j
+// (lane 0 of each warp of CTA (0, 0, 0)); compiled out otherwise.
+__device__ __forceinline__ void attn_trace(const AttnParams& p, int warp, int lane, int j, int ev) {
+#ifdef DFL_ATTN_TRACE
+  if (p.trace != nullptr && lane == 0 && j < 64 && (blockIdx.x | blockIdx.y | blockIdx.z) == 0)
+    p.trace[((long long)warp * 64 + j) * 8 + ev] = clock64();
+#endif
+}
 
 // Output row address: local, or (Ulysses) the owning rank's buffer.
 __device__ __forceinline__ __nv_bfloat16* out_row(const AttnParams& p, int b, int h, int s) {
@@ -197,11 +209,10 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnSmem<QT>::kBar);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + kNS;
-  uint64_t* k_empty = v_full + kNS;
-  uint64_t* v_empty = k_empty + kNS;
-  uint64_t* s_full = v_empty + kNS;
+  constexpr int R = AttnSmem<QT>::kRing;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + R;
+  uint64_t* s_full = kv_empty + R;
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 4;  // p_full[2 g + h]: keys [64 h, 64 h + 64) of P_g stored
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AttnSmem<QT>::kNumBars);
@@ -250,34 +261,33 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         for (int c = 0; c < 2; ++c)
           tma_load_4d(smem + AttnSmem<QT>::kQ + g * kTileBytes + c * kChunk, &tq, q_full, c * 64,
                       q0 + g * kBM, h, b);
-      bool issued_k[kNS] = {false, false}, issued_v[kNS] = {false, false};
-      uint32_t par_k[kNS] = {0, 0}, par_v[kNS] = {0, 0};
+      // load L = 2 j + which (which 0: K_j, 1: V_j) goes to slot L % R, use (L / R)
+      bool issued[R];
+      uint32_t par_i[R];
+      for (int i = 0; i < R; ++i) issued[i] = false, par_i[i] = 0;
       bool ok = true;
       for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j % kNS;
-        const uint32_t par = (j / kNS) & 1;
         const int k0 = (t_first + j) * kBN;
         for (int which = 0; which < 2; ++which) {
-          uint64_t* empty = which == 0 ? &k_empty[st] : &v_empty[st];
-          uint64_t* full = which == 0 ? &k_full[st] : &v_full[st];
-          if (!mbar_wait(empty, par ^ 1u, err, kKidAttn, 100 + which, abort_flag)) {
+          const int L = 2 * j + which, slot = L % R;
+          const uint32_t par = (L / R) & 1;
+          if (!mbar_wait(&kv_empty[slot], par ^ 1u, err, kKidAttn, 100 + which, abort_flag)) {
             ok = false;
             break;
           }
-          uint8_t* dst = smem + (which == 0 ? AttnSmem<QT>::kK : AttnSmem<QT>::kV) + st * kTileBytes;
+          uint8_t* dst = smem + AttnSmem<QT>::kKV + slot * kTileBytes;
           const CUtensorMap* map = which == 0 ? &tk : &tv;
-          mbar_arrive_expect_tx(full, kTileBytes);
-          for (int c = 0; c < 2; ++c) tma_load_4d(dst + c * kChunk, map, full, c * 64, k0, h, b);
-          if (which == 0) issued_k[st] = true, par_k[st] = par;
-          else issued_v[st] = true, par_v[st] = par;
+          attn_trace(p, warp, lane, j, which);
+          mbar_arrive_expect_tx(&kv_full[slot], kTileBytes);
+          for (int c = 0; c < 2; ++c) tma_load_4d(dst + c * kChunk, map, &kv_full[slot], c * 64, k0, h, b);
+          issued[slot] = true;
+          par_i[slot] = par;
         }
       }
       if (!ok) {  // our own bulk copies must land before the CTA exits
         mbar_wait(q_full, 0, nullptr, 0, 0, nullptr, 200000000LL);
-        for (int s = 0; s < kNS; ++s) {
-          if (issued_k[s]) mbar_wait(&k_full[s], par_k[s], nullptr, 0, 0, nullptr, 200000000LL);
-          if (issued_v[s]) mbar_wait(&v_full[s], par_v[s], nullptr, 0, 0, nullptr, 200000000LL);
-        }
+        for (int i = 0; i < R; ++i)
+          if (issued[i]) mbar_wait(&kv_full[i], par_i[i], nullptr, 0, 0, nullptr, 200000000LL);
       }
     }
   } else if (warp == AttnSmem<QT>::kMmaWarp) {
@@ -287,19 +297,27 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
       constexpr uint32_t idesc_qk = make_idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_bf16_f32(kBM, kD, 0, 1);
       bool ok = mbar_wait(q_full, 0, err, kKidAttn, 110, abort_flag);
-      auto issue_qk = [&](int g, int st) {
-        const uint32_t q_addr = smem_u32(smem + AttnSmem<QT>::kQ + g * kTileBytes);
-        const uint32_t k_addr = smem_u32(smem + AttnSmem<QT>::kK + st * kTileBytes);
+      // Descriptors: the high word (strides, swizzle, version) is a compile-time constant and
+      // the low field is the start address in 16-byte units (every smem address here is below
+      // 2^18 bytes), so a tile / k-step is a 32-bit add on the address field.
+      constexpr uint64_t kHiK = make_sdesc_sw128(0, 16, 1024);      // K-major Q / K tiles
+      constexpr uint64_t kHiV = make_sdesc_sw128(0, kChunk, 1024);  // MN-major V tiles
+      const uint32_t q_lo = smem_u32(smem + AttnSmem<QT>::kQ) >> 4;
+      const uint32_t kv_lo = smem_u32(smem + AttnSmem<QT>::kKV) >> 4;
+      auto slot_lo = [&](int L) { return kv_lo + (uint32_t)(L % R) * (kTileBytes >> 4); };
+      auto issue_qk = [&](int g, int jj) {
+        const uint32_t qa = q_lo + (uint32_t)g * (kTileBytes >> 4), ka = slot_lo(2 * jj);
+        const uint32_t d_tmem = tmem + tmem_s_col(g);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
-          uint64_t ad = make_sdesc_sw128(q_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
-          uint64_t bd = make_sdesc_sw128(k_addr + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
-          umma_f16_ss(tmem + tmem_s_col(g), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          const uint32_t o = (uint32_t)((((kk >> 2) * kChunk) + (kk & 3) * 32) >> 4);
+          umma_f16_ss(d_tmem, kHiK | (qa + o), kHiK | (ka + o), idesc_qk, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[g]);
       };
       auto issue_pv = [&](int g, int jj) -> bool {
-        const uint32_t v_addr = smem_u32(smem + AttnSmem<QT>::kV + (jj % kNS) * kTileBytes);
+        const uint32_t va = slot_lo(2 * jj + 1);
+        const uint32_t o_tmem = tmem + tmem_o_col<QT>(g), p_tmem = tmem + tmem_s_col(g);
         // P_g arrives in two halves: the first 64 keys' MMAs run while the softmax
         // finishes the second half
         for (int hf = 0; hf < 2; ++hf) {
@@ -308,36 +326,40 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
 #pragma unroll
           for (int kq = 0; kq < kBN / 32; ++kq) {
             const int kk = hf * (kBN / 32) + kq;
-            uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, kChunk, 1024);
-            umma_f16_ts(tmem + tmem_o_col<QT>(g), tmem + tmem_s_col(g) + kk * 8, bd, idesc_pv,
+            umma_f16_ts(o_tmem, p_tmem + kk * 8, kHiV | (va + (uint32_t)((kk * 2048) >> 4)), idesc_pv,
                         (jj > 0 || kk > 0) ? 1u : 0u);
           }
         }
         return true;
       };
+      auto wait_load = [&](int L, int detail) {
+        return mbar_wait(&kv_full[L % R], (L / R) & 1, err, kKidAttn, detail, abort_flag);
+      };
       for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j % kNS;
-        if (!mbar_wait(&k_full[st], (j / kNS) & 1, err, kKidAttn, 113, abort_flag)) { ok = false; break; }
-        const int pst = (j + kNS - 1) % kNS;
+        attn_trace(p, warp, lane, j, 5);
+        if (!wait_load(2 * j, 113)) { ok = false; break; }
+        attn_trace(p, warp, lane, j, 0);
         if (j > 0) {
-          if (!mbar_wait(&v_full[pst], ((j - 1) / kNS) & 1, err, kKidAttn, 114, abort_flag)) { ok = false; break; }
+          if (!wait_load(2 * j - 1, 114)) { ok = false; break; }
           if (!issue_pv(0, j - 1)) { ok = false; break; }
         }
+        attn_trace(p, warp, lane, j, 1);
         tc_fence_after();
-        issue_qk(0, st);
+        issue_qk(0, j);
+        attn_trace(p, warp, lane, j, 2);
         if (j > 0) {
           if (QT == 2 && !issue_pv(1, j - 1)) { ok = false; break; }
-          umma_commit(&v_empty[pst]);
+          umma_commit(&kv_empty[(2 * j - 1) % R]);  // V_{j-1} consumed
         }
-        if (QT == 2) issue_qk(1, st);
-        umma_commit(&k_empty[st]);
+        attn_trace(p, warp, lane, j, 3);
+        if (QT == 2) issue_qk(1, j);
+        umma_commit(&kv_empty[(2 * j) % R]);  // K_j consumed
+        attn_trace(p, warp, lane, j, 4);
       }
       if (ok) {
         const int jl = n_tiles - 1;
-        const int pst = jl % kNS;
-        if (mbar_wait(&v_full[pst], (jl / kNS) & 1, err, kKidAttn, 115, abort_flag) && issue_pv(0, jl) &&
-            (QT == 1 || issue_pv(1, jl))) {
-          umma_commit(&v_empty[pst]);
+        if (wait_load(2 * jl + 1, 115) && issue_pv(0, jl) && (QT == 1 || issue_pv(1, jl))) {
+          umma_commit(&kv_empty[(2 * jl + 1) % R]);
           umma_commit(o_full);
         }
       }
@@ -358,12 +380,14 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait(&s_full[g], j & 1, err, kKidAttn, 120 + g, abort_flag)) { ok = false; break; }
+      attn_trace(p, warp, lane, j, 0);
       tc_fence_after();
       float s[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         tmem_ld_32x32b_x32(s_t + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
+      attn_trace(p, warp, lane, j, 1);
       const int k0 = (t_first + j) * kBN;
       if ((k0 < lo) || (k0 + kBN > hi)) {  // edge tile: mask keys outside [lo, hi)
 #pragma unroll
@@ -405,6 +429,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         }
         l *= f;
       }
+      attn_trace(p, warp, lane, j, 2);
       // p = 2^(s * scale_log2 - m): packed FFMA per pair, then the SFU (or, for POLY of
       // every 8 pairs, the FMA-pipe polynomial); packed sums in 2 chains
       const float sc = p.scale_log2, neg_m = -m_use;
@@ -433,6 +458,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(&p_full[2 * g + (qtr >> 1)]);
+          attn_trace(p, warp, lane, j, 3 + (qtr >> 1));
         }
       }
       {
@@ -640,6 +666,7 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   p.acc_o = a->acc_o;
   p.acc_lse = a->acc_lse;
   p.merge_mode = a->merge_mode;
+  p.trace = a->trace;
   if (a->merge_mode != 0 && (!a->acc_o || !a->acc_lse || (reinterpret_cast<uintptr_t>(a->acc_o) & 15))) return -9;
   p.seg0_len = a->seg0_len;
   p.seg0_per = a->seg0_per > 0 ? a->seg0_per : 1;

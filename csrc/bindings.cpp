@@ -468,7 +468,8 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
                      c10::optional<at::Tensor> out, const c10::optional<at::Tensor>& lse,
                      const c10::optional<at::Tensor>& kv_lo, const c10::optional<at::Tensor>& kv_hi,
                      std::vector<int64_t> o_peer, int64_t seg0_len, int64_t seg0_per, int64_t seg1_per, std::vector<int64_t> o_strides,
-                     const c10::optional<at::Tensor>& acc_o, const c10::optional<at::Tensor>& acc_lse, int64_t merge_mode) {
+                     const c10::optional<at::Tensor>& acc_o, const c10::optional<at::Tensor>& acc_lse, int64_t merge_mode,
+                     const c10::optional<at::Tensor>& trace) {
   check_bf16_cuda(q, "q");
   check_bf16_cuda(k, "k");
   check_bf16_cuda(v, "v");
@@ -502,6 +503,11 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   a.Sk = (int)k.size(2);
   a.dh = (int)q.size(3);
   a.scale = (float)scale;
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_contiguous() && trace->numel() >= 16 * 64 * 8,
+                "trace must be int64 with at least 16 * 64 * 8 entries");
+    a.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   if (lse.has_value() && lse->defined()) {
     TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->is_contiguous(), "lse must be f32 [B, H, Sq]");
     a.lse = lse->data_ptr<float>();
@@ -746,7 +752,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("kv_hi") = py::none(), py::arg("o_peer") = std::vector<int64_t>{},
         py::arg("seg0_len") = 0, py::arg("seg0_per") = 0, py::arg("seg1_per") = 0,
         py::arg("o_strides") = std::vector<int64_t>{}, py::arg("acc_o") = py::none(),
-        py::arg("acc_lse") = py::none(), py::arg("merge_mode") = 0);
+        py::arg("acc_lse") = py::none(), py::arg("merge_mode") = 0, py::arg("trace") = py::none());
   m.def("error_word", &error_word);
   m.def("symm_alloc", &symm_alloc);
   m.def("from_ptr", &from_ptr);

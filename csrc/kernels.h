@@ -201,6 +201,9 @@ typedef struct AttnArgs {
   float* acc_o;
   float* acc_lse;
   int merge_mode;
+  // Optional diagnostics: clock64() at fixed points of every warp of CTA (0, 0, 0),
+  // trace[(warp * 64 + j) * 8 + event] for key tiles j < 64 (NULL = off).
+  long long* trace;
 } AttnArgs;
 int dfl_attention(const AttnArgs* a, cudaStream_t stream);
 // n of every 8 softmax exponential pairs on the FMA pipe (0..3; default 0).

@@ -44,7 +44,7 @@ def time_fn(fn, iters=20, warmup=3, flush=None):
     sink = None if flush is None else torch.empty((), device=flush.device, dtype=flush.dtype)
     for _ in range(iters):
         if flush is not None:
-            torch.sum(flush, out=sink)
+            torch.sum(flush, dim=0, out=sink)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
