@@ -92,6 +92,37 @@ def run_reference(args, world, rank):
     raise RuntimeError("unreachable: reference CUDA path imported but no runner is defined")
 
 
+def _profile_step(path: str, rank: int, world: int, fwd) -> None:
+    """One eager forward on every rank under torch.profiler (same collectives everywhere);
+    rank 0 writes kernel name, launches and total device microseconds."""
+    import csv
+    from collections import defaultdict
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    _barrier(world)
+    torch.cuda.synchronize()
+    # every rank runs under the profiler, so no rank's device waits time out on a slower peer
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fwd()
+        torch.cuda.synchronize()
+    _barrier(world)
+    if rank != 0:
+        return
+    tot, cnt = defaultdict(float), defaultdict(int)
+    for ev in prof.events():
+        if ev.device_type.name == "CUDA":
+            tot[ev.name] += ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
+            cnt[ev.name] += 1
+    with open(path, "w", newline="") as f:
+        w = csv.writer(f)
+        w.writerow(["kernel", "launches", "device_us"])
+        for name, us in sorted(tot.items(), key=lambda kv: -kv[1]):
+            w.writerow([name[:160], cnt[name], round(us, 1)])
+    _log(f"profiled one eager step of rank 0 into {path}")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -103,6 +134,10 @@ def main(argv=None):
     ap.add_argument("--e2e-images", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--profile-step", default=None,
+                    help="after timing, profile one eager DiT step (torch.profiler, rank 0) and write the "
+                         "per-kernel device time to this CSV (analysis only: numbers under a profiler are "
+                         "never the bench value)")
     ap.add_argument("--cp-mode", default="ulysses", choices=["ulysses", "ring", "gather_kv", "tp"],
                     help="how N>1 GPUs split the step: a context-parallel mode, or tensor parallelism")
     ap.add_argument("--sp", action="store_true", help="with --cp-mode tp: Megatron sequence parallelism")
@@ -191,6 +226,8 @@ def main(argv=None):
     ms = _max_over_ranks(ms, world)
     _log(f"timed {args.steps} steps: {ms:.3f} ms/step")
     clocks = sampler.summary() if rank == 0 else {}
+    if args.profile_step:
+        _profile_step(args.profile_step, rank, world, lambda: dit(x16, txt, pooled, t_buf, gvec, img_hw=(h_tok, w_tok)))
     from difflet_b200 import _native
 
     _native.check_device_errors()

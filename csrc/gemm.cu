@@ -39,7 +39,10 @@ struct Smem {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
   // full[S], empty[S], tmem_full[2], tmem_empty[2], then tmem addr + abort flag
-  static constexpr int kTotal = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;  // + align slack
+  // q/k/v head-scatter staging (kEpiQkv) after the barriers, then the 1024-byte align slack
+  static constexpr int kStageOff = (kBarOffset + (2 * STAGES + 4) * 8 + 16 + 15) / 16 * 16;
+  static constexpr int kTotal = kStageOff + kHeadStageBytes + 1024;
+  static_assert(kTotal <= 232448, "shared memory budget");
 };
 
 template <int BN, int STAGES, int EPI, bool OUT_F32>
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, P.M, P.N, P.ep, [&]() {
         tc_fence_before();
         mbar_arrive(&tempty_bar[acc]);
-      });
+      }, EPI == kEpiQkv ? smem + S::kStageOff + sub * kHeadStageWarp : nullptr);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }

@@ -27,7 +27,9 @@ constexpr int kABytes = BM * BK * 2;        // 16 KB
 constexpr int kBBytes = (BN / 2) * BK * 2;  // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kBarOff = STAGES * kStageBytes;
-constexpr int kSmemTotal = kBarOff + (2 * STAGES + 4) * 8 + 16 + 1024;
+constexpr int kStageOff = (kBarOff + (2 * STAGES + 4) * 8 + 16 + 15) / 16 * 16;  // head-scatter staging
+constexpr int kSmemTotal = kStageOff + kHeadStageBytes + 1024;
+static_assert(kSmemTotal <= 232448, "shared memory budget");
 constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // shared::cluster address of CTA 0's copy
 
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&tempty_bar[acc]);
         else
           mbar_arrive_cta0(&tempty_bar[acc]);
-      });
+      }, EPI == kEpiQkv ? smem + kStageOff + sub * kHeadStageWarp : nullptr);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }

@@ -258,9 +258,37 @@ DFL_DEVICE bool qkv_locate(const QkvScatterArgs& a, int col0, int& which, int& h
   return false;
 }
 
+// Per-warp staging for the head scatter: 32 rows of one head, 256 B per row, 16-byte pieces
+// stored at piece ^ (row % pieces_per_row) (an XOR swizzle: the 32 rows' stores of one piece
+// spread over the banks, and every access stays 16-byte aligned).  A head of 32 consecutive
+// rows is then written as whole rows by the warp together (512 contiguous bytes per store
+// instruction) instead of 32 scattered 16-byte pieces: full-sized NVLink packets for peer
+// destinations, full L2 lines locally.
+constexpr int kHeadStageRow = 256;
+constexpr int kHeadStageWarp = 32 * kHeadStageRow;
+constexpr int kHeadStageBytes = 4 * kHeadStageWarp;  // the four epilogue warps
+static_assert(kHeadStageRow % 16 == 0 && kHeadStageWarp % 16 == 0, "16-byte aligned staging rows");
+
+// The epilogue thread of a row is lane (row % 32) of its warp (tiles start at multiples of 32 rows).
+DFL_DEVICE int lane_of_row(int row) { return row & 31; }
+
+// 32 values = 4 pieces starting at piece p0 of staging row `lane` (swizzle mask `swz`).
+DFL_DEVICE void stage_bf16x32(uint8_t* stage, int lane, int p0, int swz, const float (&x)[32]) {
+  uint8_t* row = stage + lane * kHeadStageRow;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16x2(x[8 * q + 0], x[8 * q + 1]);
+    w.y = pack_bf16x2(x[8 * q + 2], x[8 * q + 3]);
+    w.z = pack_bf16x2(x[8 * q + 4], x[8 * q + 5]);
+    w.w = pack_bf16x2(x[8 * q + 6], x[8 * q + 7]);
+    *reinterpret_cast<uint4*>(row + 16 * ((p0 + q) ^ swz)) = w;
+  }
+}
+
 template <int DH, class Rel>
 DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int which, int h, const EpiParams& ep,
-                                  bool last, Rel& release) {
+                                  bool last, Rel& release, uint8_t* stage) {
   constexpr int NC = DH / 32;
   const QkvScatterArgs& a = ep.qs;
   const bool valid = row < M;
@@ -334,7 +362,9 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
           x[2 * p + 1] = x1 * cv[p] + x0 * sv[p];
         }
       }
-      if (valid)
+      if (stage != nullptr)
+        stage_bf16x32(stage, lane_of_row(row), 4 * c, lane_of_row(row) & (DH / 8 - 1), x);
+      else if (valid)
         for (int d = 0; d < ndst; ++d) store_bf16x32(dst(d) + c * 32, x);
     }
   } else {
@@ -366,7 +396,10 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
           }
         }
       }
-      if (valid) {
+      if (stage != nullptr) {
+        stage_bf16x32(stage, lane_of_row(row), 4 * c, lane_of_row(row) & (DH / 8 - 1), x1);
+        stage_bf16x32(stage, lane_of_row(row), 4 * (c + NC / 2), lane_of_row(row) & (DH / 8 - 1), x2);
+      } else if (valid) {
         for (int d = 0; d < ndst; ++d) {
           __nv_bfloat16* p = dst(d);
           store_bf16x32(p + c * 32, x1);
@@ -374,6 +407,25 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
         }
       }
     }
+  }
+  if (stage != nullptr) {
+    // the warp writes its 32 rows of this head: row r's destination comes from lane r
+    constexpr int kPieces = DH / 8;  // 16-byte pieces per row
+    constexpr int kRowsPerStep = 32 / kPieces;
+    const int piece = lane_of_row(row) % kPieces;
+    __syncwarp();
+    for (int d = 0; d < ndst; ++d) {
+      const unsigned long long mine = valid ? reinterpret_cast<unsigned long long>(dst(d)) : 0ull;
+#pragma unroll 4
+      for (int it = 0; it < 32 / kRowsPerStep; ++it) {
+        const int r = it * kRowsPerStep + lane_of_row(row) / kPieces;
+        const unsigned long long pr = __shfl_sync(0xffffffffu, mine, r);
+        if (pr != 0ull)
+          reinterpret_cast<uint4*>(pr)[piece] =
+              *reinterpret_cast<const uint4*>(stage + r * kHeadStageRow + 16 * (piece ^ (r & (kPieces - 1))));
+      }
+    }
+    __syncwarp();
   }
 }
 
@@ -383,7 +435,7 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
 // last TMEM load has completed (the accumulator may then be overwritten).
 template <int EPI, bool OUT_F32, int BN, class Rel>
 DFL_DEVICE void epilogue_tile(uint32_t tbase, int row, int col_base, int M, int N, const EpiParams& ep,
-                              Rel&& release) {
+                              Rel&& release, uint8_t* stage = nullptr) {
   const int ncols = min(BN, N - col_base);
   const int nch = (ncols + 31) / 32;  // warp-uniform
   if constexpr (EPI == kEpiSwiGLU) {
@@ -416,9 +468,9 @@ DFL_DEVICE void epilogue_tile(uint32_t tbase, int row, int col_base, int M, int 
         const int hc = ep.qs.dh / 32;
         const bool last = c + hc >= nch;
         if (hc == 4)
-          qkv_head_epilogue<128>(tbase + c * 32, row, M, col0, which, h, ep, last, release);
+          qkv_head_epilogue<128>(tbase + c * 32, row, M, col0, which, h, ep, last, release, stage);
         else
-          qkv_head_epilogue<64>(tbase + c * 32, row, M, col0, which, h, ep, last, release);
+          qkv_head_epilogue<64>(tbase + c * 32, row, M, col0, which, h, ep, last, release, stage);
         c += hc;
       } else {
         uint32_t r[32];
