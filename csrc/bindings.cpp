@@ -716,6 +716,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "difflet_b200 native sm_100a kernels";
   m.def("gemm_set_pair_auto", [](bool on) { dfl_gemm_set_pair_auto(on ? 1 : 0); });
   m.def("attention_set_poly", [](int64_t n) { dfl_attention_set_poly((int)n); });
+  m.def("gemm_set_split_workspace", [](const at::Tensor& ws, const at::Tensor& sem) {
+    TORCH_CHECK(ws.is_cuda() && sem.is_cuda() && ws.device() == sem.device(), "workspace tensors on one device");
+    TORCH_CHECK(ws.scalar_type() == at::kFloat && sem.scalar_type() == at::kInt && ws.is_contiguous() &&
+                    sem.is_contiguous(), "ws f32, sem int32, contiguous");
+    dfl_gemm_set_split_workspace((int)ws.device().index(), ws.data_ptr(), ws.numel() * 4, sem.data_ptr(),
+                                 (int)sem.numel());
+  });
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("B"),
         py::arg("bias") = py::none(), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("act_lo") = 0, py::arg("act_hi") = -1, py::arg("gate") = py::none(),

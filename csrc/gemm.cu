@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* split_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // split-K wait outcome
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -100,11 +101,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        int lt, mb, nb;
+        int lt, mb, nb, kb0, kb1;
         const GemmProblem& P = group_tile(grp, t, lt);
-        tile_coords(lt, P.num_m, P.num_n, mb, nb);
-        const int num_k = (P.K + BK - 1) / BK;
-        for (int kb = 0; kb < num_k; ++kb) {
+        tile_coords(lt / P.splits, P.num_m, P.num_n, mb, nb);
+        split_k_range(P, lt % P.splits, BK, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kKidGemm, 10 + stage, abort_flag)) {
             ok = false;
             break;
@@ -143,9 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        int lt;
-        const int num_k = (group_tile(grp, t, lt).K + BK - 1) / BK;
-        for (int kb = 0; kb < num_k; ++kb) {
+        int lt, kb0, kb1;
+        const GemmProblem& P = group_tile(grp, t, lt);
+        split_k_range(P, lt % P.splits, BK, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, err, kKidGemm, 30 + stage, abort_flag)) {
             ok = false;
             break;
@@ -157,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < BK / 16; ++k) {
             uint64_t ad = make_sdesc_sw128(a_addr + k * 32, 16, 1024);
             uint64_t bd = make_sdesc_sw128(b_addr + k * 32, 16, 1024);
-            umma_f16_ss(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -179,15 +181,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int lt, mb, nb;
       const GemmProblem& P = group_tile(grp, t, lt);
-      tile_coords(lt, P.num_m, P.num_n, mb, nb);
+      const int tile = lt / P.splits;
+      tile_coords(tile, P.num_m, P.num_n, mb, nb);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err, kKidGemm, 40 + acc, abort_flag)) break;
       tc_fence_after();
       const int row = mb * BM + sub * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
-      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, P.M, P.N, P.ep, [&]() {
+      auto release = [&]() {
         tc_fence_before();
         mbar_arrive(&tempty_bar[acc]);
-      }, EPI == kEpiQkv ? smem + S::kStageOff + sub * kHeadStageWarp : nullptr);
+      };
+      if constexpr (EPI != kEpiSwiGLU && EPI != kEpiQkv) {
+        if (P.splits > 1) {
+          epilogue_tile_split<EPI, OUT_F32, BN>(tbase, sub * 32 + lane, row, nb * BN, P, tile, lt % P.splits,
+                                                release, err, abort_flag, split_ok);
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1u;
+          continue;
+        }
+      }
+      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, P.M, P.N, P.ep, release,
+                                      EPI == kEpiQkv ? smem + S::kStageOff + sub * kHeadStageWarp : nullptr);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -264,6 +278,42 @@ extern "C" int dfl_gemm_pair_launch(const void* group, int epi, int out_f32, int
 static int g_pair_auto = 1;
 extern "C" void dfl_gemm_set_pair_auto(int on) { g_pair_auto = on; }
 
+// Split-K workspace of each device (set by the host runtime; none = no split-K).
+static float* g_split_ws[16];
+static long long g_split_ws_floats[16];
+static int* g_split_sem[16];
+static int g_split_sem_count[16];
+extern "C" void dfl_gemm_set_split_workspace(int device, void* ws, long long ws_bytes, void* sem, int sem_count) {
+  const int d = device & 15;
+  g_split_ws[d] = reinterpret_cast<float*>(ws);
+  g_split_ws_floats[d] = ws_bytes / 4;
+  g_split_sem[d] = reinterpret_cast<int*>(sem);
+  g_split_sem_count[d] = sem_count;
+}
+
+// Small-M launches whose tiles fill under 60 % of the SMs split K in two (problems with at
+// least 8 K blocks): twice the items, one f32 round trip of each tile through L2.
+static void plan_split_k(GemmGroup& g, int epi, int bn, int sms, int dev) {
+  const int d = dev & 15;
+  if (!g_split_ws[d] || epi == kEpiSwiGLU || epi == kEpiQkv || g.total_tiles * 10 > sms * 6) return;
+  long long ws_off = 0;
+  int sem_off = 0;
+  for (int i = 0; i < g.count; ++i) {
+    GemmProblem& P = g.p[i];
+    const int base_tiles = P.num_m * P.num_n;
+    if ((P.K + BK - 1) / BK < 8) continue;
+    const long long need = (long long)base_tiles * BM * bn;
+    if (ws_off + need > g_split_ws_floats[d] || sem_off + base_tiles > g_split_sem_count[d]) continue;
+    P.splits = 2;
+    P.ws = g_split_ws[d] + ws_off;
+    P.sem = g_split_sem[d] + sem_off;
+    ws_off += need;
+    sem_off += base_tiles;
+    g.total_tiles += base_tiles;  // one more item per tile
+    P.tiles = base_tiles * 2;
+  }
+}
+
 // One launch for `count` GEMMs that share the epilogue kind and output type.  The tile
 // shape (CTA pairs with 256 x 256 tiles, or one CTA with 128 x 256 / 128 x 128 tiles)
 // follows the first problem; the others are tiled the same way.
@@ -300,9 +350,11 @@ extern "C" int dfl_gemm_bf16_group(const GemmArgs* const* args, int count, cudaS
     P.num_m = (a->M + bm - 1) / bm;
     P.num_n = (a->N + bn - 1) / bn;
     P.tiles = P.num_m * P.num_n;
+    P.splits = 1;
     g.total_tiles += P.tiles;
   }
   if (pair) return dfl_gemm_pair_launch(&g, a0->epi, a0->out_f32, a0->err, stream, dev);
+  plan_split_k(g, a0->epi, bn, dfl_host::num_sms(dev), dev);
   if (wide) return dispatch_epi<256, 4>(a0->epi, a0->out_f32, g, a0->err, stream, dev);
   return dispatch_epi<128, 6>(a0->epi, a0->out_f32, g, a0->err, stream, dev);
 }

@@ -46,7 +46,16 @@ struct alignas(64) GemmProblem {
   CUtensorMap ta, tb;
   EpiParams ep;
   int M, N, K;
-  int num_m, num_n, tiles;
+  int num_m, num_n, tiles;  // tiles counts split items (num_m * num_n * splits)
+  // Serial split-K (small-M GEMMs that leave SMs idle): the K range of an output tile is
+  // cut into `splits` items, adjacent in the tile order so they run concurrently on
+  // different SMs.  Item s > 0 waits for sem[tile] == s, adds the f32 partial in ws,
+  // and either stores the sum back (sem = s + 1) or, the last item, runs the real
+  // epilogue (sem back to 0).  Items of one tile complete in order: the lowest unfinished
+  // item never waits, so the persistent grid (every CTA resident) always progresses.
+  int splits;
+  float* ws;  // f32 [num_m * num_n][128][BN] partial tiles
+  int* sem;   // [num_m * num_n] split counters, 0 between launches
 };
 
 struct alignas(64) GemmGroup {
@@ -63,6 +72,14 @@ DFL_DEVICE const GemmProblem& group_tile(const GemmGroup& g, int t, int& local) 
   }
   local = t;
   return g.p[i];
+}
+
+// K blocks [kb0, kb1) of split item `split` (every item gets at least one block).
+DFL_DEVICE void split_k_range(const GemmProblem& P, int split, int BK, int& kb0, int& kb1) {
+  const int num_k = (P.K + BK - 1) / BK;
+  const int per = (num_k + P.splits - 1) / P.splits;
+  kb0 = split * per;
+  kb1 = min(num_k, kb0 + per);
 }
 
 DFL_DEVICE void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
@@ -491,6 +508,77 @@ DFL_DEVICE void epilogue_tile(uint32_t tbase, int row, int col_base, int M, int 
       epilogue_chunk<EPI, OUT_F32>(r, row, col_base + c * 32, M, N, ep);
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// Split-K item epilogue (the four epilogue warps, 128 threads, named barrier 1).
+DFL_DEVICE void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+DFL_DEVICE int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int EPI, bool OUT_F32, int BN, class Rel>
+DFL_DEVICE void epilogue_tile_split(uint32_t tbase, int trow, int row, int col_base, const GemmProblem& P, int tile,
+                                    int split, Rel&& release, int* err, volatile int* abort_flag,
+                                    volatile int* split_ok) {
+  const bool first_thread = trow == 0;
+  const bool last = split == P.splits - 1;
+  int* sem = P.sem + tile;
+  if (split > 0) {  // the previous item's partial must be in ws
+    if (first_thread) {
+      int ok = 1;
+      const long long t0 = clock64();
+      while (ld_acquire_gpu(sem) != split) {
+        if (*abort_flag || clock64() - t0 > kLocalWaitCycles) {
+          record_error(err, kErrMbarTimeout, kKidGemm, 60, split);
+          *abort_flag = 1;
+          ok = 0;
+          break;
+        }
+      }
+      *split_ok = ok;
+    }
+    epi_bar();
+    if (!*split_ok) {  // one shared decision: the TMEM loads below are warp-collective
+      release();
+      return;
+    }
+  }
+  float* wrow = P.ws + ((size_t)tile * 128 + trow) * BN;  // this thread's row of the partial tile
+  const int ncols = min(BN, P.N - col_base);
+  const int nch = (ncols + 31) / 32;
+#pragma unroll 1
+  for (int c = 0; c < nch; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tbase + c * 32, r);
+    tmem_wait_ld();
+    if (c + 1 >= nch) release();
+    float4* w4 = reinterpret_cast<float4*>(wrow + c * 32);
+    if (split > 0) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 a = w4[q];
+        r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + a.x);
+        r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + a.y);
+        r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + a.z);
+        r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + a.w);
+      }
+    }
+    if (!last) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        w4[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                            __uint_as_float(r[4 * q + 3]));
+    } else {
+      epilogue_chunk<EPI, OUT_F32>(r, row, col_base + c * 32, P.M, P.N, P.ep);
+    }
+  }
+  __threadfence();
+  epi_bar();  // every thread's partial (or final rows) is written
+  if (first_thread) atomicExch(sem, last ? 0 : split + 1);
 }
 
 }  // namespace dfl

@@ -68,6 +68,8 @@ environment_variables: dict[str, Callable[[], Any]] = {
     "DIFFLET_GEMM_PAIR": lambda: _str(os.environ.get("DIFFLET_GEMM_PAIR"), "1"),
     # 1: q/k RMSNorm + RoPE + head scatter run in the qkv projection's GEMM epilogue; 0: separate kernel
     "DIFFLET_FUSE_QKV": lambda: _str(os.environ.get("DIFFLET_FUSE_QKV"), "1"),
+    # 1: small-M GEMMs that leave SMs idle split K in two across SMs (serial fixup); 0: never
+    "DIFFLET_GEMM_SPLITK": lambda: _str(os.environ.get("DIFFLET_GEMM_SPLITK"), "1"),
     # 1: the text- and image-stream GEMMs of a dual block share one grouped launch; 0: two launches
     "DIFFLET_GEMM_GROUP": lambda: _str(os.environ.get("DIFFLET_GEMM_GROUP"), "1"),
     # softmax exponential pairs (of every 8) evaluated by the FMA-pipe polynomial in attention (0..3)

@@ -59,7 +59,25 @@ def _lib():
         _nat = _native.require()
         _nat.gemm_set_pair_auto(envs.DIFFLET_GEMM_PAIR != "0")
         _nat.attention_set_poly(envs.DIFFLET_ATTN_POLY)
+    _split_workspace(_nat)
     return _nat
+
+
+_SPLIT_WS = {}
+
+
+def _split_workspace(nat) -> None:
+    """Split-K workspace of the current device (64 MB f32 partial tiles + zeroed counters),
+    registered once per device; small-M GEMMs split K across SMs with it."""
+    if envs.DIFFLET_GEMM_SPLITK == "0" or not torch.cuda.is_available():
+        return
+    dev = torch.cuda.current_device()
+    if dev in _SPLIT_WS:
+        return
+    ws = torch.empty(16 << 20, device=f"cuda:{dev}", dtype=torch.float32)
+    sem = torch.zeros(1 << 14, device=f"cuda:{dev}", dtype=torch.int32)
+    _SPLIT_WS[dev] = (ws, sem)
+    nat.gemm_set_split_workspace(ws, sem)
 
 
 def native():

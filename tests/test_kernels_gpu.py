@@ -394,3 +394,33 @@ def test_row_sumsq_and_external_rms_norm(native):
     _close(q, qc.cuda())
     _close(k, kc.cuda())
     _close(v, vc.cuda())
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 3072, 4096), (576, 3072, 15360), (64, 1536, 2048)])
+def test_gemm_split_k_small_m(native, monkeypatch, M, N, K):
+    """Small-M GEMMs split K across SMs (serial f32 fixup): plain + bias and the gated residual
+    epilogue against the fp32 reference, repeated calls (the counters return to 0), and a
+    grouped launch of two split problems."""
+    from difflet_b200.ops import fused as F
+
+    torch.manual_seed(41)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.03
+    bias = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    ref = a.float() @ b.float().t() + bias.float()
+    for _ in range(3):
+        _close(F.linear(a, b, bias), ref)
+    gate = torch.randn(1, N, device="cuda")
+    resid = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    out = resid.clone()
+    F.linear(a, b, bias, out=out, gate=gate, resid=out, rows_per_batch=M)
+    _close(out, resid.float() + gate * ref)
+    a2 = torch.randn(M // 2 + 8, K, device="cuda", dtype=torch.bfloat16)
+    o1, o2 = F.linear_group([dict(x=a, w=b, b=bias), dict(x=a2, w=b, b=bias)])
+    _close(o1, ref)
+    _close(o2, a2.float() @ b.float().t() + bias.float())
+    monkeypatch.setenv("DIFFLET_GEMM_SPLITK", "0")  # registered already: the switch only affects new devices
+    torch.cuda.synchronize()
+    from difflet_b200 import _native
+
+    _native.check_device_errors()
