@@ -25,6 +25,8 @@
 // the CUDA SDPA path difflet/backends/cuda/ops_impl/attention.py:41-86 (scale
 // given explicitly, bounded key windows as in
 // difflet/backends/neuron/ops_impl/attention.py:212-249, LSE as in :280-301).
+#include <cmath>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -163,6 +165,9 @@ struct AttnParams {
   float* acc_lse;  // f32 [B, H, Sq] running log-sum-exp
   int merge_mode;  // 0 none, 1 first partial, 2 merge, 3 merge + final bf16 store
   long long* trace;
+  int kv_splits;    // > 1: CTA x = query block * kv_splits + chunk, partials to split_o / split_lse
+  float* split_o;
+  float* split_lse;
 };
 
 // Diagnostics (builds with -DDFL_ATTN_TRACE only): SM clock at event ev of key tile j
@@ -220,11 +225,21 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * (QT * kBM);
+  const int splits = p.kv_splits > 1 ? p.kv_splits : 1;
+  const int chunk = blockIdx.x % splits;
+  const int q0 = (blockIdx.x / splits) * (QT * kBM);
   const int lo = p.kv_lo ? max(0, p.kv_lo[b]) : 0;
   const int hi = p.kv_hi ? min(p.Sk, p.kv_hi[b]) : p.Sk;
-  const int t_first = lo / kBN;
-  const int n_tiles = hi > lo ? (hi + kBN - 1) / kBN - t_first : 0;
+  const int tiles_all = hi > lo ? (hi + kBN - 1) / kBN - lo / kBN : 0;
+  const int per_chunk = (tiles_all + splits - 1) / splits;
+  const int t_first = lo / kBN + chunk * per_chunk;
+  const int n_tiles = max(0, min(per_chunk, tiles_all - chunk * per_chunk));
+  // split-KV: this CTA's partial goes to its chunk's slot (the merge-mode-1 epilogue)
+  const int merge_mode = splits > 1 ? 1 : p.merge_mode;
+  const long long split_rows = (long long)p.B * p.H * p.Sq;
+  float* const acc_o = splits > 1 ? p.split_o + (long long)chunk * split_rows * kD : p.acc_o;
+  float* const acc_lse = splits > 1 ? p.split_lse + (long long)chunk * split_rows : p.acc_lse;
+  float* const lse_out = splits > 1 ? nullptr : p.lse;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < AttnSmem<QT>::kNumBars; ++i) {
@@ -470,7 +485,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     }
     // ------------------------------------------------------------ epilogue
     const int qrow = q0 + g * kBM + row;
-    if (p.merge_mode != 0) {
+    if (merge_mode != 0) {
       // Partial over one key block, merged by log-sum-exp into a running fp32
       // (acc_o, acc_lse): 1 = first partial (store), 2 = merge and store,
       // 3 = merge and write the final bf16 row (no store to the accumulator).
@@ -481,8 +496,8 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
       const bool valid = qrow < p.Sq;
       const long long arow = ((long long)b * p.H + h) * p.Sq + qrow;
       float w_prev = 0.f, w_cur = 1.f, lse_new = lse_cur;
-      if (p.merge_mode >= 2 && valid) {
-        const float lse_prev = p.acc_lse[arow];
+      if (merge_mode >= 2 && valid) {
+        const float lse_prev = acc_lse[arow];
         const float mx = fmaxf(lse_prev, lse_cur);
         if (mx == -INFINITY) {
           w_prev = 0.f, w_cur = 0.f, lse_new = -INFINITY;
@@ -497,8 +512,8 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
       } else if (lse_cur == -INFINITY) {
         w_cur = 0.f;
       }
-      __nv_bfloat16* op = (valid && p.merge_mode == 3) ? out_row(p, b, h, qrow) : nullptr;
-      float* ao = valid ? p.acc_o + arow * kD : nullptr;
+      __nv_bfloat16* op = (valid && merge_mode == 3) ? out_row(p, b, h, qrow) : nullptr;
+      float* ao = valid ? acc_o + arow * kD : nullptr;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o_raw[32];
@@ -513,7 +528,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         float o[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(o_raw[e]) * inv * w_cur;
-        if (p.merge_mode >= 2) {
+        if (merge_mode >= 2) {
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const float4 a = reinterpret_cast<const float4*>(ao + c * 32)[q];
@@ -540,8 +555,8 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         }
       }
       if (valid) {
-        if (p.merge_mode != 3) p.acc_lse[arow] = lse_new;
-        if (p.lse) p.lse[arow] = lse_new;
+        if (merge_mode != 3) acc_lse[arow] = lse_new;
+        if (lse_out) lse_out[arow] = lse_new;
       }
     } else if (ok && n_tiles > 0 && mbar_wait(o_full, 0, err, kKidAttn, 122, abort_flag)) {
       tc_fence_after();
@@ -564,13 +579,13 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
           }
         }
       }
-      if (p.lse && qrow < p.Sq)
-        p.lse[((long long)b * p.H + h) * p.Sq + qrow] =
+      if (lse_out && qrow < p.Sq)
+        lse_out[((long long)b * p.H + h) * p.Sq + qrow] =
             l > 0.f ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
     } else if (n_tiles == 0 && qrow < p.Sq) {
       __nv_bfloat16* op = out_row(p, b, h, qrow);
       for (int d = 0; d < kD; ++d) op[d] = __float2bfloat16(0.f);
-      if (p.lse) p.lse[((long long)b * p.H + h) * p.Sq + qrow] = -INFINITY;
+      if (lse_out) lse_out[((long long)b * p.H + h) * p.Sq + qrow] = -INFINITY;
     }
   }
 
@@ -578,6 +593,35 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == AttnSmem<QT>::kMmaWarp) tmem_dealloc(tmem, AttnSmem<QT>::kTmemCols);
+}
+
+// Split-KV combine: one warp per query row merges the kv_splits normalised partials by
+// log-sum-exp and writes the bf16 row (Ulysses scatter included) and, if asked, the LSE.
+__global__ void __launch_bounds__(256) attn_combine_kernel(AttnParams p) {
+  const long long rows = (long long)p.B * p.H * p.Sq;
+  const long long r = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (r >= rows) return;
+  const int S = p.kv_splits;
+  float m = -INFINITY;
+  for (int c = 0; c < S; ++c) m = fmaxf(m, p.split_lse[c * rows + r]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float wsum = 0.f;
+  if (m != -INFINITY) {
+    for (int c = 0; c < S; ++c) {
+      const float w = expf(p.split_lse[c * rows + r] - m);
+      const float4 o = reinterpret_cast<const float4*>(p.split_o + (c * rows + r) * kD)[lane];
+      wsum += w;
+      acc.x += w * o.x, acc.y += w * o.y, acc.z += w * o.z, acc.w += w * o.w;
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  const int s = (int)(r % p.Sq), h = (int)((r / p.Sq) % p.H), b = (int)(r / ((long long)p.Sq * p.H));
+  uint2 pk;
+  pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+  pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  reinterpret_cast<uint2*>(out_row(p, b, h, s))[lane] = pk;
+  if (p.lse && lane == 0) p.lse[r] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
 }
 
 int make_tmap_4d(CUtensorMap* map, const void* base, long long S, int H, int B, long long ss,
@@ -611,8 +655,13 @@ int launch_attn_poly(const AttnArgs* a, const AttnParams& p, const CUtensorMap& 
     }
     attr[dev & 15] = true;
   }
-  dim3 grid((a->Sq + QT * kBM - 1) / (QT * kBM), a->H, a->B);
+  const int splits = p.kv_splits > 1 ? p.kv_splits : 1;
+  dim3 grid((a->Sq + QT * kBM - 1) / (QT * kBM) * splits, a->H, a->B);
   attn_fwd_kernel<QT, POLY><<<grid, AttnSmem<QT>::kThreads, AttnSmem<QT>::kTotal, stream>>>(tq, tk, tv, p, a->err);
+  if (splits > 1) {
+    const long long rows = (long long)a->B * a->H * a->Sq;
+    attn_combine_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(p);
+  }
   return (int)cudaGetLastError();
 }
 
@@ -633,6 +682,30 @@ int launch_attn(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, c
 
 // Fraction (n / 8) of the softmax exponentials evaluated by the FMA-pipe polynomial.
 extern "C" void dfl_attention_set_poly(int n) { g_attn_poly = n < 0 ? 0 : (n > 3 ? 3 : n); }
+
+// Key-range splits: modelled time = waves of CTAs x (one full-range CTA time / s) + the
+// split overhead (partial f32 rows written and read back by the combine, CTA start-up),
+// fitted on B200: 8 us + 0.4 ns per query row and split; s > 1 only with >= 4 key tiles per
+// chunk and a predicted gain of 10 %.  (Measured at 4608 keys: 3 heads 68.6 -> 60.2 us with
+// two chunks; 6 and 12 heads are fastest unsplit.)
+extern "C" int dfl_attention_plan_splits(const AttnArgs* a) {
+  if (a->merge_mode != 0 || a->dh != kD || a->Sk <= 0) return 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const double sms = dfl_host::num_sms(dev);
+  const double units = (double)((a->Sq + 2 * kBM - 1) / (2 * kBM)) * a->H * a->B;
+  const int kv_tiles = (a->Sk + kBN - 1) / kBN;
+  const double t_cta_us = 0.0172 * a->Sk;  // one 256-query CTA over every key (measured: 79 us at 4608)
+  const double rows = (double)a->B * a->H * a->Sq;
+  int best = 1;
+  double best_t = std::ceil(units / sms) * t_cta_us;
+  for (int s = 2; s <= 8; ++s) {
+    if (kv_tiles / s < 4) break;
+    const double t = std::ceil(units * s / sms) * t_cta_us / s + 8.0 + 4.0e-4 * rows * s;
+    if (t < best_t * 0.9) best = s, best_t = t;
+  }
+  return best;
+}
 
 extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   if (a->dh != kD) return -2;
@@ -679,6 +752,14 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
     if (a->seg1_per * a->o_world != a->Sq - a->seg0_len) return -7;
     for (int r = 0; r < a->o_world; ++r)
       if (!a->o_peer[r] || (reinterpret_cast<uintptr_t>(a->o_peer[r]) & 15)) return -8;
+  }
+  p.kv_splits = a->kv_splits > 1 ? a->kv_splits : 1;
+  p.split_o = a->split_o;
+  p.split_lse = a->split_lse;
+  if (p.kv_splits > 1) {
+    if (a->merge_mode != 0 || !a->split_o || !a->split_lse || (reinterpret_cast<uintptr_t>(a->split_o) & 15))
+      return -10;
+    return launch_attn<2>(a, p, tq, tk, tv, stream);  // 256-row query blocks, split key ranges
   }
   // Two ping-pong Q tiles per CTA unless that leaves more than half the SMs idle:
   // then one Q tile per CTA doubles the CTA count while still fitting one wave.

@@ -7,6 +7,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -469,7 +470,7 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
                      const c10::optional<at::Tensor>& kv_lo, const c10::optional<at::Tensor>& kv_hi,
                      std::vector<int64_t> o_peer, int64_t seg0_len, int64_t seg0_per, int64_t seg1_per, std::vector<int64_t> o_strides,
                      const c10::optional<at::Tensor>& acc_o, const c10::optional<at::Tensor>& acc_lse, int64_t merge_mode,
-                     const c10::optional<at::Tensor>& trace) {
+                     const c10::optional<at::Tensor>& trace, int64_t kv_split) {
   check_bf16_cuda(q, "q");
   check_bf16_cuda(k, "k");
   check_bf16_cuda(v, "v");
@@ -530,6 +531,17 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
                     acc_lse->numel() == (int64_t)a.B * a.H * a.Sq, "acc_lse must be f32 [B, H, Sq]");
     a.acc_o = acc_o->data_ptr<float>();
     a.acc_lse = acc_lse->data_ptr<float>();
+  }
+  // split-KV partial buffers (stream-ordered allocations, released after the launch)
+  at::Tensor split_o, split_lse;
+  const int splits = kv_split < 0 ? dfl_attention_plan_splits(&a) : (int)std::max<int64_t>(kv_split, 1);
+  if (splits > 1 && merge_mode == 0) {
+    const int64_t rows = (int64_t)a.B * a.H * a.Sq;
+    split_o = at::empty({splits, rows, 128}, q.options().dtype(at::kFloat));
+    split_lse = at::empty({splits, rows}, q.options().dtype(at::kFloat));
+    a.kv_splits = splits;
+    a.split_o = split_o.data_ptr<float>();
+    a.split_lse = split_lse.data_ptr<float>();
   }
   DFL_CHECK_RC(dfl_attention(&a, cur_stream()), "attention");
   return o;
@@ -759,7 +771,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("kv_hi") = py::none(), py::arg("o_peer") = std::vector<int64_t>{},
         py::arg("seg0_len") = 0, py::arg("seg0_per") = 0, py::arg("seg1_per") = 0,
         py::arg("o_strides") = std::vector<int64_t>{}, py::arg("acc_o") = py::none(),
-        py::arg("acc_lse") = py::none(), py::arg("merge_mode") = 0, py::arg("trace") = py::none());
+        py::arg("acc_lse") = py::none(), py::arg("merge_mode") = 0, py::arg("trace") = py::none(),
+        py::arg("kv_split") = -1);
   m.def("error_word", &error_word);
   m.def("symm_alloc", &symm_alloc);
   m.def("from_ptr", &from_ptr);

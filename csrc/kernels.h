@@ -207,8 +207,17 @@ typedef struct AttnArgs {
   // Optional diagnostics: clock64() at fixed points of every warp of CTA (0, 0, 0),
   // trace[(warp * 64 + j) * 8 + event] for key tiles j < 64 (NULL = off).
   long long* trace;
+  // Split-KV (launches whose query blocks leave SMs idle): kv_splits CTAs share a query
+  // block, each over a contiguous key range, writing its normalised partial and LSE to
+  // split_o f32 [kv_splits][B*H*Sq][128] / split_lse [kv_splits][B*H*Sq]; a combine pass
+  // merges them by log-sum-exp into the output.  Ask dfl_attention_plan_splits first.
+  int kv_splits;
+  float* split_o;
+  float* split_lse;
 } AttnArgs;
 int dfl_attention(const AttnArgs* a, cudaStream_t stream);
+// Key-range split count that minimises the modelled time of this launch (1 = none).
+int dfl_attention_plan_splits(const AttnArgs* a);
 // n of every 8 softmax exponential pairs on the FMA pipe (0..3; default 0).
 void dfl_attention_set_poly(int n);
 

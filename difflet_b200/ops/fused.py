@@ -462,10 +462,16 @@ def linear_group(calls: list) -> list:
     return native().gemm_group(A, Bw, bias, out, epi, lo, hi, gate, rpb, resid, plans)
 
 
+def kv_split_mode() -> int:
+    """Key-range split of the native attention: -1 lets the kernel's model choose (launches
+    whose query blocks leave SMs idle run as several key chunks + a log-sum-exp combine)."""
+    return -1 if envs.DIFFLET_ATTN_SPLIT != "0" else 1
+
+
 def attention(q, k, v, scale, *, out=None, lse=None, kv_lo=None, kv_hi=None):
     """softmax(scale * q k^T) v over [B, H, S, dh]; key window [kv_lo[b], kv_hi[b])."""
     if q.is_cuda and envs.DIFFLET_KERNEL_ATTN != "sdpa" and q.shape[-1] == 128:
-        return native().attention(q, k, v, float(scale), out, lse, kv_lo, kv_hi)
+        return native().attention(q, k, v, float(scale), out, lse, kv_lo, kv_hi, kv_split=kv_split_mode())
     ct = torch.float64 if q.dtype == torch.float64 else torch.float32
     if q.is_cuda and lse is None and kv_lo is None:
         o = F.scaled_dot_product_attention(q, k, v, scale=float(scale))

@@ -152,7 +152,7 @@ class PeerUlysses(PeerBase):
         col = self.rank * Hl * dh * target.element_size()
         peers = [p + col for p in self.heap.peer_ptrs(target)]
         F.native().attention(q, k, v, float(scale), None, None, kv_lo, kv_hi, peers, n0 * self.world, n0, n1,
-                             [S_loc * ld, dh, ld])
+                             [S_loc * ld, dh, ld], kv_split=F.kv_split_mode())
         self.heap.barrier()  # every output row has landed at its owner
 
 
