@@ -63,7 +63,7 @@ class LTX2Application:
                  num_inference_steps=40, guidance_scale=4.0, audio_guidance_scale=None, stg_scale=0.0,
                  audio_stg_scale=None, spatio_temporal_guidance_blocks=None, modality_scale=1.0,
                  audio_modality_scale=None, guidance_rescale=0.0, seed=0, output_type="np", latents=None,
-                 audio_latents=None, return_latents=False):
+                 audio_latents=None, return_latents=False, callback=None):
         dit, cfg = self.dit, self.cfg
         dev, dt = dit.device, dit.dtype
         ags = guidance_scale if audio_guidance_scale is None else audio_guidance_scale
@@ -109,6 +109,8 @@ class LTX2Application:
                 # x0-space CFG equals u + s (c - u) on the velocities: one fused exchange per stream
                 xv = xv + (s_next - s) * cfg_par.combine(pv.contiguous(), guidance_scale)
                 xa = xa + (s_next - s) * cfg_par.combine(pa.contiguous(), ags)
+                if callback is not None:
+                    callback(i, xv)
                 continue
             pv, pa = pv.float(), pa.float()
             x0v = xv - s * pv
@@ -143,6 +145,8 @@ class LTX2Application:
             vel_a = (xa - ga) / s
             xv = xv + (s_next - s) * vel_v
             xa = xa + (s_next - s) * vel_a
+            if callback is not None:  # per-step observer (video latents)
+                callback(i, xv)
         lat_v = unpack_video(xv, grid)
         lat_a = unpack_audio(xa, cfg.audio_channels)
         if return_latents or self.decoders is None:

@@ -33,7 +33,7 @@ class MiniMaxH3Application:
     @torch.no_grad()
     def generate(self, prompt: str, *, height=480, width=832, num_frames=124, num_inference_steps=30, seed=0,
                  keyframes=None, keyframe_anchors=(), output_type="np", return_latents=False,
-                 check_duration=True):
+                 check_duration=True, callback=None):
         """``keyframes``: condition latents [1, C, 1, H/16, W/16] per anchor ("first" / "last")."""
         dit, cfg = self.dit, self.cfg
         dev, dt = dit.device, dit.dtype
@@ -73,6 +73,8 @@ class MiniMaxH3Application:
             pv, pa = dit(packed.to(dt), arows.to(dt), text_d, ts, tidx, lay)
             vrows = vsched.step(pv[:, lay.num_condition_rows:], i, vrows)
             arows = asched.step(pa, i, arows)
+            if callback is not None:  # per-step observer (video latent rows)
+                callback(i, vrows)
         lat_v = L.unpatchify(vrows, cfg.in_channels, lay.num_latent_frames, lh, lw)
         lat_a = arows.reshape(L.AUDIO_CHANNELS, lay.num_audio_latents, cfg.audio_in_channels).permute(0, 2, 1)
         if return_latents or self.decoders is None:

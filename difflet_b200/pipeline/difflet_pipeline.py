@@ -117,4 +117,18 @@ class DiffletPipeline:
         self.app.load(self.compiled_path, skip_warmup=skip_warmup)
 
     def __call__(self, *args: Any, **kwargs: Any) -> Any:
-        return self.app(*args, **kwargs)
+        from difflet_b200.utils import telemetry
+
+        self._requests = getattr(self, "_requests", 0) + 1
+        req = f"r{self._requests:05d}"
+        rec = telemetry.StepRecorder.maybe(req)
+        if rec is not None:  # chain the per-step observer in front of a user callback
+            user = kwargs.get("callback")
+            kwargs["callback"] = (lambda i, x: (rec.callback(i, x), user(i, x))) if user else rec.callback
+            rec.start()
+        with telemetry.span("request", request=req, model=self.model_entry.name), \
+                telemetry.nvtx_range(f"difflet.request.{req}"):
+            out = self.app(*args, **kwargs)
+        if rec is not None:
+            rec.finish()
+        return out
