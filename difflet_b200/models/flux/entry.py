@@ -47,6 +47,9 @@ class FluxEngine:
 
     def load(self, compiled_path=None, skip_warmup=False):
         dev = self._device()
+        from difflet_b200.utils.hbm import preload_check
+
+        preload_check(FluxTransformer.weight_shapes(self.cfg), self.dtype, dev, what="FLUX DiT")
         if self.kw.get("random_init") or not self.model_path:
             dit = FluxTransformer.random_init(self.cfg, device=dev, dtype=self.dtype, seed=int(self.kw.get("seed", 0)))
             vae = KLDecoder.random_init(KLDecoderConfig(), device=dev, dtype=self.dtype, seed=1)

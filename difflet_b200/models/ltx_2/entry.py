@@ -38,6 +38,9 @@ class LTX2Engine:
     def load(self, compiled_path=None, skip_warmup=False):
         dev = torch.device("cuda", torch.cuda.current_device()) if self.backend == "cuda" else torch.device("cpu")
         dcfg = TINY_DECODER if self.cfg.in_channels != 128 else LTX2DecoderConfig()
+        from difflet_b200.utils.hbm import preload_check
+
+        preload_check(LTX2Transformer.weight_shapes(self.cfg), self.dtype, dev, what="LTX-2 DiT")
         if self.kw.get("random_init") or not self.model_path:
             dit = LTX2Transformer.random_init(self.cfg, device=dev, dtype=self.dtype, seed=int(self.kw.get("seed", 0)))
         else:

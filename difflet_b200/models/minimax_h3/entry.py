@@ -38,6 +38,9 @@ class MiniMaxH3Engine:
         dev = torch.device("cuda", torch.cuda.current_device()) if self.backend == "cuda" else torch.device("cpu")
         if self.parallel.world_size > 1:
             raise NotImplementedError("MiniMax-H3 runs on one GPU here")
+        from difflet_b200.utils.hbm import preload_check
+
+        preload_check(MiniMaxH3Transformer.weight_shapes(self.cfg), self.dtype, dev, what="MiniMax-H3 DiT")
         if self.kw.get("random_init") or not self.model_path:
             dit = MiniMaxH3Transformer.random_init(self.cfg, device=dev, dtype=self.dtype,
                                                    seed=int(self.kw.get("seed", 0)))

@@ -43,6 +43,9 @@ class MMDiTEngine:
 
     def load(self, compiled_path=None, skip_warmup=False):
         dev = torch.device("cuda", torch.cuda.current_device()) if self.backend == "cuda" else torch.device("cpu")
+        from difflet_b200.utils.hbm import preload_check
+
+        preload_check(MMDiT.weight_shapes(self.cfg), self.dtype, dev, what=f"{self.entry.name} DiT")
         if self.kw.get("random_init") or not self.model_path:
             dit = MMDiT.random_init(self.cfg, device=dev, dtype=self.dtype, seed=int(self.kw.get("seed", 0)))
         else:

@@ -39,6 +39,9 @@ class WanEngine:
     def load(self, compiled_path=None, skip_warmup=False):
         dev = torch.device("cuda", torch.cuda.current_device()) if self.backend == "cuda" else torch.device("cpu")
         n = 2 if self.two_experts else 1
+        from difflet_b200.utils.hbm import preload_check
+
+        preload_check(WanTransformer.weight_shapes(self.wcfg), self.dtype, dev, what="Wan experts", copies=n)
         if self.kw.get("random_init") or not self.model_path:
             experts = [WanTransformer.random_init(self.wcfg, device=dev, dtype=self.dtype, seed=10 + i) for i in range(n)]
             vae = WanVAEDecoder.random_init(WanVAEConfig(), device=dev, dtype=self.dtype, seed=3)
