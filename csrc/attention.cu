@@ -180,7 +180,7 @@ __device__ __forceinline__ void attn_trace(const AttnParams& p, int warp, int la
 }
 
 // Output row address: local, or (Ulysses) the owning rank's buffer.
-__device__ __forceinline__ __nv_bfloat16* out_row(const AttnParams& p, int b, int h, int s) {
+__device__ __forceinline__ __nv_bfloat16* out_row(const AttnParams& p, int b, int h, int s, int* err = nullptr) {
   if (p.o_world <= 1)
     return p.o + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)s * p.o_ss;
   int owner, lrow;
@@ -192,6 +192,7 @@ __device__ __forceinline__ __nv_bfloat16* out_row(const AttnParams& p, int b, in
     owner = s2 / p.seg1_per;
     lrow = p.seg0_per + (s2 - owner * p.seg1_per);
   }
+  if (!DFL_GUARD(owner < p.o_world, err, kKidAttn, 80, s)) return nullptr;
   return p.o_peer[owner] + (long long)b * p.o_bs + (long long)h * p.o_hs + (long long)lrow * p.o_ss;
 }
 
@@ -512,7 +513,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
       } else if (lse_cur == -INFINITY) {
         w_cur = 0.f;
       }
-      __nv_bfloat16* op = (valid && merge_mode == 3) ? out_row(p, b, h, qrow) : nullptr;
+      __nv_bfloat16* op = (valid && merge_mode == 3) ? out_row(p, b, h, qrow, err) : nullptr;
       float* ao = valid ? acc_o + arow * kD : nullptr;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -561,7 +562,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     } else if (ok && n_tiles > 0 && mbar_wait(o_full, 0, err, kKidAttn, 122, abort_flag)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* op = qrow < p.Sq ? out_row(p, b, h, qrow) : nullptr;
+      __nv_bfloat16* op = qrow < p.Sq ? out_row(p, b, h, qrow, err) : nullptr;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o_raw[32];
@@ -583,8 +584,9 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         lse_out[((long long)b * p.H + h) * p.Sq + qrow] =
             l > 0.f ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
     } else if (n_tiles == 0 && qrow < p.Sq) {
-      __nv_bfloat16* op = out_row(p, b, h, qrow);
-      for (int d = 0; d < kD; ++d) op[d] = __float2bfloat16(0.f);
+      __nv_bfloat16* op = out_row(p, b, h, qrow, err);
+      if (op != nullptr)
+        for (int d = 0; d < kD; ++d) op[d] = __float2bfloat16(0.f);
       if (lse_out) lse_out[((long long)b * p.H + h) * p.Sq + qrow] = -INFINITY;
     }
   }
@@ -620,7 +622,8 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnParams p) {
   uint2 pk;
   pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
   pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-  reinterpret_cast<uint2*>(out_row(p, b, h, s))[lane] = pk;
+  __nv_bfloat16* op = out_row(p, b, h, s);
+  if (op != nullptr) reinterpret_cast<uint2*>(op)[lane] = pk;
   if (p.lse && lane == 0) p.lse[r] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
 }
 

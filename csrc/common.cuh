@@ -51,6 +51,17 @@ DFL_DEVICE void record_error(int* err, int code, int kid, int d0, int d1) {
 // ~4 s at 1.9 GHz.  A healthy wait is microseconds; running out means a bug.
 constexpr long long kLocalWaitCycles = 8000000000LL;
 
+// Debug builds (-DDFL_BOUNDS_CHECK, DIFFLET_BOUNDS_CHECK=1): index guards on values the host
+// cannot check without a device read (per-row maps, peer owners).  A failed guard records
+// kErrBounds with the kernel id and the offending index and the access is skipped; release
+// builds compile the guard to `true`.
+#ifdef DFL_BOUNDS_CHECK
+#define DFL_GUARD(cond, err, kid, d0, d1) \
+  ((cond) ? true : (::dfl::record_error((err), ::dfl::kErrBounds, (kid), (int)(d0), (int)(d1)), false))
+#else
+#define DFL_GUARD(cond, err, kid, d0, d1) true
+#endif
+
 // ---------------------------------------------------------------------------
 // Shared-memory address helpers
 // ---------------------------------------------------------------------------

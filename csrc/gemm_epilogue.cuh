@@ -34,6 +34,7 @@ struct EpiParams {
   long long peer_row_off;
   // kEpiQkv: head scatter of the q / k / v column blocks (source rows = GEMM rows)
   QkvScatterArgs qs;
+  int* err;  // device error word (bounds-check builds record guard failures here)
 };
 
 // Grouped launch: up to kMaxGroup independent GEMMs (same epilogue kind) share one
@@ -132,6 +133,7 @@ DFL_DEVICE void epilogue_chunk(const uint32_t (&r)[32], int row, int col0, int M
   }
   if constexpr (EPI == kEpiGateResid) {
     int b = p.gate_row_map ? p.gate_row_map[row] : row / p.rows_per_batch;
+    if (!DFL_GUARD(b >= 0, p.err, kKidGemm, 71, row)) return;
     const float* g = p.gate + (long long)b * p.gate_bstride;
     const __nv_bfloat16* rs = p.resid + (long long)row * p.ldr;
     if (full) {
@@ -161,6 +163,7 @@ DFL_DEVICE void epilogue_chunk(const uint32_t (&r)[32], int row, int col0, int M
   long long drow = row;
   if (p.out_world > 0) {
     const int owner = row / p.rows_per_rank;
+    if (!DFL_GUARD(owner < p.out_world, p.err, kKidGemm, 70, row)) return;
     dbase = p.out_peer[owner];
     drow = p.peer_row_off + (row - owner * p.rows_per_rank);
   }
@@ -308,9 +311,9 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
                                   bool last, Rel& release, uint8_t* stage) {
   constexpr int NC = DH / 32;
   const QkvScatterArgs& a = ep.qs;
-  const bool valid = row < M;
-  const int b = valid ? row / a.S_src : 0;
-  const int s = valid ? row - b * a.S_src : 0;
+  const bool row_ok = row < M;
+  const int b = row_ok ? row / a.S_src : 0;
+  const int s = row_ok ? row - b * a.S_src : 0;
   const __nv_bfloat16* bias = ep.bias ? ep.bias + hcol : nullptr;
   const bool norm = which < 2 && a.norm_mode == 1;
   float rr = 1.f;
@@ -337,6 +340,7 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
   const int rpos = seg1 ? a.seg1_rope_off + (s - a.seg_rows) : a.rope_pos_off + s;
   const int owner = a.kv_replicate ? 0 : h / Hl;
   const int hl = a.kv_replicate ? h : h % Hl;
+  const bool valid = row_ok && DFL_GUARD(owner < a.world, ep.err, kKidGemm, 72, h);
   const long long dst_off = a.out_token_major
                                 ? ((long long)b * a.S_dst + dpos) * (long long)(Hl * DH) + (long long)hl * DH
                                 : (((long long)b * Hl + hl) * a.S_dst + dpos) * DH;
@@ -632,6 +636,7 @@ inline int fill_epi_params(const GemmArgs& a, dfl::EpiParams& ep) {
   ep.resid = reinterpret_cast<const __nv_bfloat16*>(a.resid);
   ep.ldr = a.ldr;
   ep.alpha = a.alpha;
+  ep.err = a.err;
   if (a.out_world < 0 || a.out_world > DFL_MAX_PEERS) return -9;
   ep.out_world = a.out_world;
   ep.rows_per_rank = a.rows_per_rank > 0 ? a.rows_per_rank : a.M;

@@ -52,6 +52,21 @@ NVCC_FLAGS = [
 ]
 CXX_FLAGS = ["-O3", "-std=c++17"]
 
+
+def _bounds_check() -> bool:
+    from difflet_b200 import envs
+
+    return bool(envs.DIFFLET_BOUNDS_CHECK)
+
+
+def _ext_name() -> str:
+    """The release module, or the debug build with device index guards (DIFFLET_BOUNDS_CHECK=1)."""
+    return EXT_NAME + ("_bounds" if _bounds_check() else "")
+
+
+def _nvcc_flags() -> list:
+    return NVCC_FLAGS + (["-DDFL_BOUNDS_CHECK"] if _bounds_check() else [])
+
 _lock = threading.Lock()
 _module = None
 _load_error: Exception | None = None
@@ -71,20 +86,20 @@ def source_hash() -> str:
     for p in sorted(_sources() + [CSRC / n for n in HEADERS if (CSRC / n).exists()]):
         h.update(p.name.encode())
         h.update(p.read_bytes())
-    h.update(" ".join(NVCC_FLAGS + CXX_FLAGS).encode())
+    h.update(" ".join(_nvcc_flags() + CXX_FLAGS).encode())
     return h.hexdigest()[:24]
 
 
 def _so_path() -> Path | None:
     for suffix in importlib.machinery.EXTENSION_SUFFIXES + [".so"]:
-        p = BUILD_DIR / f"{EXT_NAME}{suffix}"
+        p = BUILD_DIR / f"{_ext_name()}{suffix}"
         if p.exists():
             return p
     return None
 
 
 def _stamp() -> Path:
-    return BUILD_DIR / f"{EXT_NAME}.hash"
+    return BUILD_DIR / f"{_ext_name()}.hash"
 
 
 def build(verbose: bool = False, force: bool = False):
@@ -100,10 +115,10 @@ def build(verbose: bool = False, force: bool = False):
     # torch's own arch list must not add other targets: the -gencode above is the only one.
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
     mod = cpp_extension.load(
-        name=EXT_NAME,
+        name=_ext_name(),
         sources=[str(p) for p in _sources()],
         extra_cflags=CXX_FLAGS,
-        extra_cuda_cflags=NVCC_FLAGS,
+        extra_cuda_cflags=_nvcc_flags(),
         extra_include_paths=[str(CSRC)],
         build_directory=str(BUILD_DIR),
         verbose=verbose,
@@ -128,10 +143,10 @@ def load():
                 return build()
             import torch  # noqa: F401  (libtorch symbols must be loaded first)
 
-            spec = importlib.util.spec_from_file_location(EXT_NAME, str(so))
+            spec = importlib.util.spec_from_file_location(_ext_name(), str(so))
             mod = importlib.util.module_from_spec(spec)
             spec.loader.exec_module(mod)
-            sys.modules[EXT_NAME] = mod
+            sys.modules[_ext_name()] = mod
             _module = mod
             return mod
         except Exception as exc:  # pragma: no cover - surfaced by require()

@@ -58,10 +58,30 @@ class SymmetricHeap:
         self._nbytes[t.data_ptr()] = nbytes
         return t, ptrs
 
+    CANARY_BYTES = 256
+    CANARY_BYTE = 0xA5
+
     def empty(self, shape, dtype) -> torch.Tensor:
+        """A symmetric buffer.  With DIFFLET_BOUNDS_CHECK=1 it is followed by a 256-byte canary
+        region that ``check_canaries`` verifies (a peer store past the end shows up there)."""
         n = int(math.prod(shape)) * torch.empty((), dtype=dtype).element_size()
-        raw, _ = self._alloc_raw(n)
+        guard = self.CANARY_BYTES if envs.DIFFLET_BOUNDS_CHECK else 0
+        raw, _ = self._alloc_raw(n + guard)
+        if guard:
+            if not hasattr(self, "_canaries"):
+                self._canaries = []
+            c = raw[n:n + guard]
+            c.fill_(self.CANARY_BYTE)
+            self._canaries.append(c)
         return raw[:n].view(dtype).view(shape)
+
+    def check_canaries(self) -> None:
+        """Raise when any canary region after a symmetric buffer was overwritten."""
+        for i, c in enumerate(getattr(self, "_canaries", [])):
+            if not bool((c == self.CANARY_BYTE).all()):
+                from difflet_b200.utils.errors import DeviceError
+
+                raise DeviceError(code=3, kernel=0, detail=(i, int((c != self.CANARY_BYTE).sum())))
 
     def peer_ptrs(self, t: torch.Tensor) -> list[int]:
         """Peer pointers of the same element as ``t`` (which may be a view) on every rank."""
