@@ -50,28 +50,50 @@ class FluxEngine:
         from difflet_b200.utils.hbm import preload_check
 
         preload_check(FluxTransformer.weight_shapes(self.cfg), self.dtype, dev, what="FLUX DiT")
+        from difflet_b200.quant.apply import quantize_engine_model
+
+        tp = None
+        if self.parallel.tp_degree > 1:  # this rank's heads / MLP columns, before any quantization
+            from difflet_b200.parallel.tp import make_tensor_parallel
+
+            tp = make_tensor_parallel(self.parallel, dev)
+
+        def device_weights(dit):
+            """Checkpoint layout -> this rank's sharded (and quantized) engine weights."""
+            if tp is not None:
+                from difflet_b200.parallel.tp import shard_mmdit_weights
+
+                dit.w = shard_mmdit_weights(dit.cfg, dit.w, tp.world, tp.rank)
+            self.quant_report = quantize_engine_model(dit, "flux", self.kw)
+            return dit.w
+
         if self.kw.get("random_init") or not self.model_path:
             dit = FluxTransformer.random_init(self.cfg, device=dev, dtype=self.dtype, seed=int(self.kw.get("seed", 0)))
+            device_weights(dit)
             vae = KLDecoder.random_init(KLDecoderConfig(), device=dev, dtype=self.dtype, seed=1)
         else:
+            from difflet_b200.utils import weight_store
             from difflet_b200.utils.checkpoint import load_component
 
-            sd = load_component(self.model_path, "transformer", dtype=self.dtype)
-            dit = FluxTransformer.from_diffusers_state_dict(self.cfg, sd, device=dev, dtype=self.dtype)
+            def build():
+                sd = load_component(self.model_path, "transformer", dtype=self.dtype)
+                return device_weights(FluxTransformer.from_diffusers_state_dict(self.cfg, sd, device=dev,
+                                                                                dtype=self.dtype))
+
+            layout = {"cfg": repr(self.cfg), "quant": self.kw.get("quant"), "compute": self.kw.get("quant_compute")}
+            w, self.weight_store = weight_store.load_or_build(
+                "flux", self.model_path, self.dtype, tp.world if tp else 1, tp.rank if tp else 0, layout, dev, build,
+                compute="mx" if self.kw.get("quant_compute", "native") == "native" else "dequant")
+            if self.weight_store == "hit":
+                self.quant_report = {"weight_store": "hit"}
+            dit = FluxTransformer(self.cfg, w)
             vsd = load_component(self.model_path, "vae", dtype=self.dtype, device=dev)
             vae = KLDecoder(KLDecoderConfig(), vsd)
+        dit.tp = tp
         if self.parallel.world_size > 1:
             from difflet_b200.parallel.ulysses import make_sequence_parallel
 
             dit.par = make_sequence_parallel(self.parallel, dev)
-        if self.parallel.tp_degree > 1:  # this rank's heads / MLP columns, before any quantization
-            from difflet_b200.parallel.tp import make_tensor_parallel, shard_mmdit_weights
-
-            dit.tp = make_tensor_parallel(self.parallel, dev)
-            dit.w = shard_mmdit_weights(dit.cfg, dit.w, dit.tp.world, dit.tp.rank)
-        from difflet_b200.quant.apply import quantize_engine_model
-
-        self.quant_report = quantize_engine_model(dit, "flux", self.kw)
         self.app = FluxApplication(dit, vae, use_cuda_graph=(self.backend == "cuda" and self.kw.get("cuda_graph", True)))
         if self.kw.get("teacache_speedup"):
             from difflet_b200.pipeline.teacache import build_controller
