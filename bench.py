@@ -288,6 +288,13 @@ def main(argv=None):
             "gpu_launches": int(launches_per_step * args.steps),
             "e2e": e2e,
         }
+        try:  # traceability extras: peak device memory, source revision, versions, GPU
+            from difflet_b200.bench import provenance
+
+            out["memory"] = provenance.memory()
+            out["provenance"] = provenance.collect()
+        except Exception as exc:  # noqa: BLE001 - never lose the result line over metadata
+            out["provenance"] = {"error": repr(exc)}
         print(json.dumps(out), flush=True)
     # release CUDA graphs (and any NCCL work they hold) before tearing anything down
     app._graphs.clear()
