@@ -21,16 +21,33 @@ using namespace dfl;
 constexpr int BM = 128;      // rows per CTA (256 per pair)
 constexpr int BN = 256;      // columns per pair tile; each CTA loads BN / 2 rows of B
 constexpr int BK = 64;
-constexpr int STAGES = 6;
-constexpr int kThreads = 192;
 constexpr int kABytes = BM * BK * 2;        // 16 KB
 constexpr int kBBytes = (BN / 2) * BK * 2;  // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kBarOff = STAGES * kStageBytes;
-constexpr int kStageOff = (kBarOff + (2 * STAGES + 4) * 8 + 16 + 15) / 16 * 16;  // head-scatter staging
-constexpr int kSmemTotal = kStageOff + kHeadStageBytes + 1024;
-static_assert(kSmemTotal <= 232448, "shared memory budget");
+
+// Launch shape for EW epilogue warps (4: one per TMEM lane quarter, each owning all BN columns
+// of its 32 rows; 8: two per lane quarter, each owning BN / 2 columns, so two epilogue warps
+// share every SM sub-partition and hide each other's TMEM / L2 latency).  The q/k/v head
+// scatter stages 8 KB per epilogue warp, which with 8 warps costs one operand stage.
+template <int EPI, int EW>
+struct PairCfg {
+  // EW == 8: warpgroup 0 = TMA warp, MMA warp and two idle warps, warpgroups 1-2 = epilogue,
+  // with a register split (128 x 64 + 256 x 216 = 63488 <= 384 x 168 at launch).
+  static constexpr int kThreads = EW == 8 ? 384 : 192;
+  static constexpr int kFirstEpiWarp = EW == 8 ? 4 : 2;
+  static constexpr int kCols = BN * 4 / EW;  // accumulator columns per epilogue warp
+  static constexpr int STAGES = (EPI == kEpiQkv && EW == 8) ? 5 : 6;
+  static constexpr int kBarOff = STAGES * kStageBytes;
+  static constexpr int kStageOff = (kBarOff + (2 * STAGES + 4) * 8 + 16 + 15) / 16 * 16;  // head-scatter staging
+  static constexpr int kSmemTotal = kStageOff + (EPI == kEpiQkv ? EW * kHeadStageWarp : 0) + 1024;
+  static_assert(kSmemTotal <= 232448, "shared memory budget");
+  static_assert(EW == 4 || EW == 8, "epilogue warps");
+};
 constexpr uint32_t kTmemCols = 2 * BN;
+constexpr int kRegsLow = 64, kRegsHigh = 216;  // EW == 8 register split
+
+DFL_DEVICE void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 64;"); }
+DFL_DEVICE void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 216;"); }
 constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // shared::cluster address of CTA 0's copy
 
 DFL_DEVICE uint32_t cluster_rank() {
@@ -78,9 +95,12 @@ DFL_DEVICE void mbar_arrive_cta0(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
 
-template <int EPI, bool OUT_F32>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int EPI, bool OUT_F32, int EW>
+__global__ void __launch_bounds__(PairCfg<EPI, EW>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ GemmGroup grp, int* err) {
+  using C = PairCfg<EPI, EW>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int kBarOff = C::kBarOff;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kBarOff);
@@ -102,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 2 * 128);  // both CTAs' epilogue threads (CTA 0's copy is the one used)
+      mbar_init(&tempty_bar[a], 2 * 32 * EW);  // both CTAs' epilogue threads (CTA 0's copy is the one used)
     }
     *abort_flag = 0;
     fence_mbar_init_cluster();
@@ -124,6 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
+    if constexpr (EW == 8) regs_dec();
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -159,6 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
+    if constexpr (EW == 8) regs_dec();
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = make_idesc_bf16_f32(2 * BM, BN);
       int stage = 0, acc = 0;
@@ -197,8 +219,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (acc == 0) acc_phase ^= 1u;
       }
     }
+  } else if (warp < C::kFirstEpiWarp) {
+    if constexpr (EW == 8) regs_dec();  // the idle warps of warpgroup 0
   } else {
-    const int sub = warp & 3;
+    if constexpr (EW == 8) regs_inc();
+    const int ew = warp - C::kFirstEpiWarp;  // epilogue warp 0 .. EW-1
+    const int sub = warp & 3;  // the TMEM lane quarter this warp may access
+    const int slice = ew >> 2;  // which kCols columns of the tile (EW == 8: two slices)
+    uint8_t* stage = EPI == kEpiQkv ? smem + C::kStageOff + ew * kHeadStageWarp : nullptr;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = pair; t < num_tiles; t += num_pairs) {
@@ -208,14 +236,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err, kKidGemm, 340 + acc, abort_flag)) break;
       tc_fence_after();
       const int row = mb * 2 * BM + (int)rank * BM + sub * 32 + lane;
-      const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
-      epilogue_tile<EPI, OUT_F32, BN>(tbase, row, nb * BN, P.M, P.N, P.ep, [&]() {
+      const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN + slice * C::kCols;
+      epilogue_tile<EPI, OUT_F32, C::kCols>(tbase, row, nb * BN + slice * C::kCols, P.M, P.N, P.ep, [&]() {
         tc_fence_before();
         if (rank == 0)
           mbar_arrive(&tempty_bar[acc]);
         else
           mbar_arrive_cta0(&tempty_bar[acc]);
-      }, EPI == kEpiQkv ? smem + kStageOff + sub * kHeadStageWarp : nullptr);
+      }, stage);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -228,21 +256,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
 }
 
-template <int EPI, bool OUT_F32>
-int launch_pair(const GemmGroup& g, int* err, cudaStream_t stream, int dev) {
-  auto kern = gemm_pair_kernel<EPI, OUT_F32>;
+// Epilogue warps per pair CTA: 0 = 8 for the q/k/v head scatter (the heaviest epilogue), 4 for
+// the rest; 4 or 8 = that count for every epilogue.
+int g_epi_warps = 0;
+
+template <int EPI, bool OUT_F32, int EW>
+int launch_pair_ew(const GemmGroup& g, int* err, cudaStream_t stream, int dev) {
+  using C = PairCfg<EPI, EW>;
+  auto kern = gemm_pair_kernel<EPI, OUT_F32, EW>;
   static bool attr[16] = {false};
   if (!attr[dev & 15]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemTotal);
     if (e != cudaSuccess) return (int)e;
+    if (EW == 8) {  // the setmaxnreg split must fit in the registers the CTA is launched with
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, kern);
+      if (e != cudaSuccess) return (int)e;
+      if (fa.numRegs * C::kThreads < 128 * kRegsLow + 256 * kRegsHigh) return -11;
+    }
     attr[dev & 15] = true;
   }
   const int pairs_max = dfl_host::num_sms(dev) / 2;
   const int pairs = g.total_tiles < pairs_max ? g.total_tiles : pairs_max;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemTotal;
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemTotal;
   cfg.stream = stream;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -255,7 +294,16 @@ int launch_pair(const GemmGroup& g, int* err, cudaStream_t stream, int dev) {
   return (int)e;
 }
 
+template <int EPI, bool OUT_F32>
+int launch_pair(const GemmGroup& g, int* err, cudaStream_t stream, int dev) {
+  const int ew = g_epi_warps ? g_epi_warps : (EPI == kEpiQkv ? 8 : 4);
+  return ew == 8 ? launch_pair_ew<EPI, OUT_F32, 8>(g, err, stream, dev)
+                 : launch_pair_ew<EPI, OUT_F32, 4>(g, err, stream, dev);
+}
+
 }  // namespace
+
+extern "C" void dfl_gemm_set_epi_warps(int n) { g_epi_warps = (n == 4 || n == 8) ? n : 0; }
 
 // Grouped launch prepared by dfl_gemm_bf16_group (tiles of 256 rows, B boxes of 128 rows).
 extern "C" int dfl_gemm_pair_launch(const void* group, int epi, int out_f32, int* err, cudaStream_t stream, int dev) {

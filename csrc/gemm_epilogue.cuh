@@ -459,6 +459,10 @@ DFL_DEVICE void epilogue_tile(uint32_t tbase, int row, int col_base, int M, int 
                               Rel&& release, uint8_t* stage = nullptr) {
   const int ncols = min(BN, N - col_base);
   const int nch = (ncols + 31) / 32;  // warp-uniform
+  if (nch <= 0) {  // a column slice past N (pair kernel with two slices per tile)
+    release();
+    return;
+  }
   if constexpr (EPI == kEpiSwiGLU) {
     // chunk pairs (h, g) of interleaved 32-column groups -> 32 output columns
 #pragma unroll 1

@@ -58,6 +58,7 @@ int dfl_gemm_bf16(const GemmArgs* a, cudaStream_t stream);
 // Split-K workspace of `device` (f32 partial tiles + int counters that must start at 0 and
 // are left at 0 by every launch); GEMMs that use it must not run concurrently on the device.
 void dfl_gemm_set_split_workspace(int device, void* ws, long long ws_bytes, void* sem, int sem_count);
+void dfl_gemm_set_epi_warps(int n);  // pair-kernel epilogue warps: 0 auto (8 for the q/k/v scatter), 4 or 8
 // Up to 2 GEMMs with the same epilogue kind and output type in one persistent launch
 // (their tiles share the grid; the tile shape follows args[0]).
 int dfl_gemm_bf16_group(const GemmArgs* const* args, int count, cudaStream_t stream);

@@ -4,7 +4,7 @@ Every number is a CUDA-event time on the launching stream after warm-up, with
 an L2 flush (a 256 MB write) before each timed launch, reported as the median
 of the timed launches.  Usage::
 
-    python -m difflet_b200.bench.kernels [--only gemm,attn,ln,mx,gemv] [--cases flux_1gpu,...]
+    python -m difflet_b200.bench.kernels [--only gemm,attn,ln,mx,gemv,qkv] [--cases flux_1gpu,...]
                                          [--iters 20] [--no-ref]
 
 ``--no-ref`` skips the library comparison (used for ncu captures so the
@@ -77,6 +77,49 @@ def bench_gemm(nat, iters, flush, peaks, cases, ref):
             r.update({"cublas_ms": round(t_ref, 4), "cublas_tflops": round(fl / t_ref / 1e9, 1)})
         rows.append(r)
         del a, b, out
+    return rows
+
+
+QKV_CASES = [("flux_single_qkv_epilogue", 4608, 24, 128, 12288, 3072), ("flux_double_qkv_epilogue", 4096, 24, 128, 0, 3072)]
+
+
+def bench_qkv(nat, iters, flush, peaks, cases, ref):
+    """The projection feeding attention with the q/k RMSNorm + RoPE + head scatter in its
+    epilogue (FLUX single block: [q | mlp | k | v] with GELU on the MLP columns)."""
+    from difflet_b200.ops import fused as F
+
+    rows = []
+    for name, M, H, dh, Fm, K in _sel(QKV_CASES, cases):
+        D = H * dh
+        N = 3 * D + Fm
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+        b = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        q, k, v = (torch.empty(1, H, M, dh, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+        wq = torch.ones(dh, device="cuda", dtype=torch.bfloat16)
+        ang = torch.rand(M, dh // 2, device="cuda")
+        cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+        sc = dict(q_off=0, k_off=D + Fm, v_off=2 * D + Fm, S_src=M, H=H, dh=dh, q_dst=[q], k_dst=[k], v_dst=[v],
+                  S_dst=M, norm_mode=1, wq=wq, wk=wq, eps=1e-6, cos=cos, sin=sin)
+        kw = dict(act="gelu", act_lo=D, act_hi=D + Fm) if Fm else {}
+        t = time_fn(lambda: F.linear_qkv(x, w, b, scatter=sc, out=out, **kw), iters, flush=flush)
+        fl = 2.0 * M * N * K
+        r = {"kernel": "gemm_qkv_epilogue", "shape": name, "M": M, "N": N, "K": K, "ms": round(t, 4),
+             "tflops": round(fl / t / 1e9, 1), "frac_of_measured_peak": round(fl / t / 1e9 / peaks["bf16_tflops"], 3)}
+        if ref:  # the epilogue's parts: plain GEMM, GELU window only, then the scatter without norm / RoPE
+            t_plain = time_fn(lambda: nat.gemm(x, w, b, out=out), iters, flush=flush)
+            r["plain_gemm_ms"] = round(t_plain, 4)
+            if Fm:
+                t_gelu = time_fn(lambda: F.linear(x, w, b, out=out, act="gelu", act_lo=D, act_hi=D + Fm), iters,
+                                 flush=flush)
+                r["gelu_window_ms"] = round(t_gelu, 4)
+            for tag, upd in (("no_rope", dict(cos=None, sin=None)), ("no_norm_no_rope", dict(cos=None, sin=None,
+                                                                                            norm_mode=0))):
+                sc2 = dict(sc, **upd)
+                r[f"qkv_{tag}_ms"] = round(time_fn(lambda: F.linear_qkv(x, w, b, scatter=sc2, out=out, **kw), iters,
+                                                   flush=flush), 4)
+        rows.append(r)
     return rows
 
 
@@ -221,6 +264,8 @@ def main(argv=None):
         rows += bench_attn(nat, args.iters, flush, peaks, cases, ref)
     if "ln" in only:
         rows += bench_ln(nat, args.iters, flush, peaks, cases, ref)
+    if "qkv" in only:
+        rows += bench_qkv(nat, args.iters, flush, peaks, cases, ref)
     if "gemv" in only:
         rows += bench_gemv(nat, args.iters, flush, peaks, cases, ref)
     if "mx" in only:

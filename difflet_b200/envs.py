@@ -72,6 +72,8 @@ environment_variables: dict[str, Callable[[], Any]] = {
     "DIFFLET_GEMM_SPLITK": lambda: _str(os.environ.get("DIFFLET_GEMM_SPLITK"), "1"),
     # 1: the text- and image-stream GEMMs of a dual block share one grouped launch; 0: two launches
     "DIFFLET_GEMM_GROUP": lambda: _str(os.environ.get("DIFFLET_GEMM_GROUP"), "1"),
+    # epilogue warps of the 2-SM GEMM: 0 = 8 for the q/k/v head-scatter epilogue and 4 otherwise; 4 or 8 = always
+    "DIFFLET_GEMM_EPI_WARPS": lambda: _int(os.environ.get("DIFFLET_GEMM_EPI_WARPS"), 0),
     # "auto": attention launches whose query blocks leave SMs idle split the key range; "0": never
     "DIFFLET_ATTN_SPLIT": lambda: _str(os.environ.get("DIFFLET_ATTN_SPLIT"), "auto"),
     # softmax exponential pairs (of every 8) evaluated by the FMA-pipe polynomial in attention (0..3)
