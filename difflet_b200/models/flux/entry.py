@@ -94,7 +94,14 @@ class FluxEngine:
             from difflet_b200.parallel.ulysses import make_sequence_parallel
 
             dit.par = make_sequence_parallel(self.parallel, dev)
-        self.app = FluxApplication(dit, vae, use_cuda_graph=(self.backend == "cuda" and self.kw.get("cuda_graph", True)))
+        text_encoder = None
+        if self.model_path and not self.kw.get("random_init") and self.kw.get("load_text_encoder", True):
+            from difflet_b200.models.text_encoders import load_text_encoder
+
+            text_encoder = load_text_encoder("flux", self.model_path, dev, self.dtype,
+                                             max_sequence_length=256 if "schnell" in str(self.model_path).lower() else 512)
+        self.app = FluxApplication(dit, vae, text_encoder=text_encoder,
+                                   use_cuda_graph=(self.backend == "cuda" and self.kw.get("cuda_graph", True)))
         if self.kw.get("teacache_speedup"):
             from difflet_b200.pipeline.teacache import build_controller
 

@@ -15,6 +15,7 @@ from difflet_b200.models.vae.hunyuan_vae import HunyuanVAEConfig, HunyuanVAEDeco
 class HunyuanVideoEngine(MMDiTEngine):
     preset = "hunyuan-video"
     default_shape = {"height": 720, "width": 1280, "num_frames": 129}
+    text_family = "hunyuan_video"
 
     def make_vae(self, dev):
         if self.kw.get("random_init") or not self.model_path:
@@ -30,6 +31,7 @@ class HunyuanVideoEngine(MMDiTEngine):
 class HunyuanVideo15Engine(HunyuanVideoEngine):
     preset = "hunyuan-video-1.5"
     default_shape = {"height": 480, "width": 848, "num_frames": 121}
+    text_family = None  # Qwen2.5-VL + glyph byT5 encoders: synthetic embeddings of the DiT's text width
 
     def make_vae(self, dev):
         cfg = HunyuanVAEConfig(latent_channels=32, block_out_channels=(128, 256, 512, 1024, 1024))

@@ -18,6 +18,7 @@ from difflet_b200.models.mmdit.pipeline import MMDiTApplication
 class MMDiTEngine:
     preset = "hunyuan-video"
     default_shape = {"height": 720, "width": 1280, "num_frames": 129}
+    text_family = None  # prompt-encoder recipe of models/text_encoders.py (None: synthetic embeddings)
 
     def __init__(self, *, entry, model_path, parallel, dtype, shape, backend, application_kwargs):
         self.entry, self.model_path, self.parallel, self.dtype = entry, model_path, parallel, dtype
@@ -68,7 +69,15 @@ class MMDiTEngine:
 
             dit.par = make_sequence_parallel(self.parallel, dev)
             cfg_par = make_cfg_parallel(self.parallel, dev)
-        self.app = MMDiTApplication(dit, vae, cfg_par=cfg_par, **self.app_kwargs())
+        kwargs = self.app_kwargs()
+        if (self.text_family and self.model_path and not self.kw.get("random_init")
+                and self.kw.get("load_text_encoder", True) and "text_encoder" not in kwargs):
+            from difflet_b200.models.text_encoders import load_text_encoder
+
+            te = load_text_encoder(self.text_family, self.model_path, dev, self.dtype, max_len=kwargs.get("text_len"))
+            if te is not None:
+                kwargs["text_encoder"] = te
+        self.app = MMDiTApplication(dit, vae, cfg_par=cfg_par, **kwargs)
 
     def generate(self, **kw):
         for k, v in self.default_shape.items():

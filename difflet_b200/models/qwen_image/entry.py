@@ -15,6 +15,7 @@ from difflet_b200.models.vae.wan_vae import WanVAEConfig, WanVAEDecoder
 class QwenImageEngine(MMDiTEngine):
     preset = "qwen-image"
     default_shape = {"height": 1328, "width": 1328}
+    text_family = "qwen_image"
 
     def make_vae(self, dev):
         if self.kw.get("random_init") or not self.model_path:

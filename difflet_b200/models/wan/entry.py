@@ -68,8 +68,13 @@ class WanEngine:
         from difflet_b200.quant.apply import quantize_engine_model
 
         self.quant_report = [quantize_engine_model(e, "wan", self.kw) for e in experts]
+        text_encoder = None
+        if self.model_path and not self.kw.get("random_init") and self.kw.get("load_text_encoder", True):
+            from difflet_b200.models.text_encoders import load_text_encoder
+
+            text_encoder = load_text_encoder("wan", self.model_path, dev, self.dtype, text_len=experts[0].cfg.text_len)
         self.app = WanApplication(experts, vae, flow_shift=float(self.kw.get("flow_shift", 12.0 if n == 2 else 5.0)),
-                                  cfg_par=cfg_par, seq_par=seq_par)
+                                  text_encoder=text_encoder, cfg_par=cfg_par, seq_par=seq_par)
 
     def generate(self, **kw):
         kw.setdefault("height", self.shape.get("height") or 720)
