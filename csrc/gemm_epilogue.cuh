@@ -306,6 +306,36 @@ DFL_DEVICE void stage_bf16x32(uint8_t* stage, int lane, int p0, int swz, const f
   }
 }
 
+// RoPE of one 32-column chunk c of interleaved pairs (2p, 2p+1): frequencies c*16 + p.
+DFL_DEVICE void rope_interleaved_chunk(float (&x)[32], const float* cs, const float* sn, int c) {
+  float cv[16], sv[16];
+  load_f32x16(cs + c * 16, cv);
+  load_f32x16(sn + c * 16, sv);
+#pragma unroll
+  for (int p = 0; p < 16; ++p) {
+    const float x0 = x[2 * p], x1 = x[2 * p + 1];
+    x[2 * p] = x0 * cv[p] - x1 * sv[p];
+    x[2 * p + 1] = x1 * cv[p] + x0 * sv[p];
+  }
+}
+
+// RoPE of half-split pairs: column i of chunk c (first half) with the same column of chunk
+// c + dh/64 (second half), frequency c*32 + i.
+DFL_DEVICE void rope_half_chunks(float (&x1)[32], float (&x2)[32], const float* cs, const float* sn, int c) {
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    float cv[16], sv[16];
+    load_f32x16(cs + c * 32 + hh * 16, cv);
+    load_f32x16(sn + c * 32 + hh * 16, sv);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float a1 = x1[hh * 16 + j], a2 = x2[hh * 16 + j];
+      x1[hh * 16 + j] = a1 * cv[j] - a2 * sv[j];
+      x2[hh * 16 + j] = a2 * cv[j] + a1 * sv[j];
+    }
+  }
+}
+
 template <int DH, class Rel>
 DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int which, int h, const EpiParams& ep,
                                   bool last, Rel& release, uint8_t* stage) {
@@ -316,21 +346,6 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
   const int s = row_ok ? row - b * a.S_src : 0;
   const __nv_bfloat16* bias = ep.bias ? ep.bias + hcol : nullptr;
   const bool norm = which < 2 && a.norm_mode == 1;
-  float rr = 1.f;
-  if (norm) {
-    float ss = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < NC; ++c) {
-      uint32_t r[32];
-      float x[32];
-      tmem_ld_32x32b_x32(taddr + c * 32, r);
-      tmem_wait_ld();
-      qkv_linear_chunk(r, x, bias ? bias + c * 32 : nullptr, ep.alpha);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) ss += x[j] * x[j];
-    }
-    rr = rsqrtf(ss / (float)DH + a.eps);
-  }
   const __nv_bfloat16* wn =
       norm ? reinterpret_cast<const __nv_bfloat16*>(which == 0 ? a.wq : a.wk) : nullptr;
   // destinations (same addressing as dfl_qkv_scatter)
@@ -361,8 +376,66 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
     cs = a.cos_t + o;
     sn = a.sin_t + o;
   }
-  const bool rope = which < 2 && a.cos_t != nullptr;  // warp-uniform (cs may be null on invalid rows)
-  if (!(rope && a.rope_half)) {
+  const bool half = which < 2 && a.cos_t != nullptr && a.rope_half;  // warp-uniform (cs may be null)
+  // chunk c's 32 finished values -> staging row or every destination
+  auto emit = [&](int c, const float (&x)[32]) {
+    if (stage != nullptr)
+      stage_bf16x32(stage, lane_of_row(row), 4 * c, lane_of_row(row) & (DH / 8 - 1), x);
+    else if (valid)
+      for (int d = 0; d < ndst; ++d) store_bf16x32(dst(d) + c * 32, x);
+  };
+  if (norm) {
+    // One pass over tensor memory: the head's bf16 values (bias, alpha and the bf16 rounding
+    // of the unfused projection applied) stay in registers, packed two per word, while the
+    // sum of squares accumulates; the accumulator is released after the last load.
+    uint32_t hp[DH / 2];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      uint32_t r[32];
+      float x[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, r);
+      tmem_wait_ld();
+      if (last && c == NC - 1) release();
+      qkv_linear_chunk(r, x, bias ? bias + c * 32 : nullptr, ep.alpha);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        ss += x[2 * j] * x[2 * j] + x[2 * j + 1] * x[2 * j + 1];
+        hp[c * 16 + j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);  // exact: x is bf16-rounded
+      }
+    }
+    const float rr = rsqrtf(ss / (float)DH + a.eps);
+    auto unpack = [&](int c, float (&x)[32]) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float2 f = unpack_bf16x2(hp[c * 16 + j]);
+        x[2 * j] = f.x;
+        x[2 * j + 1] = f.y;
+      }
+    };
+    if (!half) {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        float x[32];
+        unpack(c, x);
+        qkv_scale_chunk(x, rr, wn ? wn + c * 32 : nullptr);
+        if (cs != nullptr) rope_interleaved_chunk(x, cs, sn, c);
+        emit(c, x);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < NC / 2; ++c) {
+        float x1[32], x2[32];
+        unpack(c, x1);
+        unpack(c + NC / 2, x2);
+        qkv_scale_chunk(x1, rr, wn ? wn + c * 32 : nullptr);
+        qkv_scale_chunk(x2, rr, wn ? wn + (c + NC / 2) * 32 : nullptr);
+        if (cs != nullptr) rope_half_chunks(x1, x2, cs, sn, c);
+        emit(c, x1);
+        emit(c + NC / 2, x2);
+      }
+    }
+  } else if (!half) {
 #pragma unroll 1
     for (int c = 0; c < NC; ++c) {
       uint32_t r[32];
@@ -371,22 +444,8 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
       tmem_wait_ld();
       if (last && c == NC - 1) release();
       qkv_linear_chunk(r, x, bias ? bias + c * 32 : nullptr, ep.alpha);
-      if (norm) qkv_scale_chunk(x, rr, wn ? wn + c * 32 : nullptr);
-      if (cs != nullptr) {  // pairs (2p, 2p+1) of this chunk use frequencies c*16 + p
-        float cv[16], sv[16];
-        load_f32x16(cs + c * 16, cv);
-        load_f32x16(sn + c * 16, sv);
-#pragma unroll
-        for (int p = 0; p < 16; ++p) {
-          const float x0 = x[2 * p], x1 = x[2 * p + 1];
-          x[2 * p] = x0 * cv[p] - x1 * sv[p];
-          x[2 * p + 1] = x1 * cv[p] + x0 * sv[p];
-        }
-      }
-      if (stage != nullptr)
-        stage_bf16x32(stage, lane_of_row(row), 4 * c, lane_of_row(row) & (DH / 8 - 1), x);
-      else if (valid)
-        for (int d = 0; d < ndst; ++d) store_bf16x32(dst(d) + c * 32, x);
+      if (cs != nullptr) rope_interleaved_chunk(x, cs, sn, c);
+      emit(c, x);
     }
   } else {
 #pragma unroll 1
@@ -399,34 +458,9 @@ DFL_DEVICE void qkv_head_epilogue(uint32_t taddr, int row, int M, int hcol, int 
       if (last && c == NC / 2 - 1) release();
       qkv_linear_chunk(r1, x1, bias ? bias + c * 32 : nullptr, ep.alpha);
       qkv_linear_chunk(r2, x2, bias ? bias + (c + NC / 2) * 32 : nullptr, ep.alpha);
-      if (norm) {
-        qkv_scale_chunk(x1, rr, wn ? wn + c * 32 : nullptr);
-        qkv_scale_chunk(x2, rr, wn ? wn + (c + NC / 2) * 32 : nullptr);
-      }
-      if (cs != nullptr) {  // column i (< dh/2) pairs with i + dh/2, frequency i
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float cv[16], sv[16];
-          load_f32x16(cs + c * 32 + hh * 16, cv);
-          load_f32x16(sn + c * 32 + hh * 16, sv);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float a1 = x1[hh * 16 + j], a2 = x2[hh * 16 + j];
-            x1[hh * 16 + j] = a1 * cv[j] - a2 * sv[j];
-            x2[hh * 16 + j] = a2 * cv[j] + a1 * sv[j];
-          }
-        }
-      }
-      if (stage != nullptr) {
-        stage_bf16x32(stage, lane_of_row(row), 4 * c, lane_of_row(row) & (DH / 8 - 1), x1);
-        stage_bf16x32(stage, lane_of_row(row), 4 * (c + NC / 2), lane_of_row(row) & (DH / 8 - 1), x2);
-      } else if (valid) {
-        for (int d = 0; d < ndst; ++d) {
-          __nv_bfloat16* p = dst(d);
-          store_bf16x32(p + c * 32, x1);
-          store_bf16x32(p + (c + NC / 2) * 32, x2);
-        }
-      }
+      if (cs != nullptr) rope_half_chunks(x1, x2, cs, sn, c);
+      emit(c, x1);
+      emit(c + NC / 2, x2);
     }
   }
   if (stage != nullptr) {
