@@ -54,8 +54,8 @@ struct AttnSmem {
   static constexpr int kRing = QT == 2 ? 5 : 6;             // K/V slots (224 KB of smem with Q)
   static constexpr int kKV = kQ + QT * kTileBytes;
   static constexpr int kBar = kKV + kRing * kTileBytes;
-  // q_full, kv_full[R], kv_empty[R], s_full[2], p_full[2][2], o_full
-  static constexpr int kNumBars = 1 + 2 * kRing + 2 + 4 + 1;
+  // q_full, kv_full[R], kv_empty[R], s_full[2], p_full[2][2], o_full, pv_half[2]
+  static constexpr int kNumBars = 1 + 2 * kRing + 2 + 4 + 1 + 2;
   static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -168,6 +168,7 @@ struct AttnParams {
   int kv_splits;    // > 1: CTA x = query block * kv_splits + chunk, partials to split_o / split_lse
   float* split_o;
   float* split_lse;
+  int spec;  // 1: speculative running max (exponentials before the max is known)
 };
 
 // Diagnostics (builds with -DDFL_ATTN_TRACE only): SM clock at event ev of key tile j
@@ -221,6 +222,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
   uint64_t* s_full = kv_empty + R;
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 4;  // p_full[2 g + h]: keys [64 h, 64 h + 64) of P_g stored
+  uint64_t* pv_half = o_full + 1;  // pv_half[g]: the first half of PV_g (one phase per key tile) completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AttnSmem<QT>::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -345,6 +347,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
             umma_f16_ts(o_tmem, p_tmem + kk * 8, kHiV | (va + (uint32_t)((kk * 2048) >> 4)), idesc_pv,
                         (jj > 0 || kk > 0) ? 1u : 0u);
           }
+          if (hf == 0) umma_commit(&pv_half[g]);
         }
         return true;
       };
@@ -412,47 +415,13 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
           if (key < lo || key >= hi) s[c] = -INFINITY;
         }
       }
-      // row max over raw scores: 8 independent chains of 3-input max (short dependency depth)
-      float mxa[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mxa[t] = s[t];
-#pragma unroll
-      for (int c = 8; c < 120; c += 16) {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) mxa[t] = max3(mxa[t], s[c + t], s[c + 8 + t]);
-      }
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mxa[t] = fmaxf(mxa[t], s[120 + t]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-      const float m_new = fmaxf(m, mx * p.scale_log2);  // scale > 0: max commutes with it
-      // the rescale decision is warp-uniform: tcgen05.ld / st are warp-collective
-      const bool need = (j > 0) && __any_sync(0xffffffffu, m_new > m + 8.0f);
-      const float m_old = m;
-      if (j == 0 || need) m = m_new;
-      const float m_use = (m == -INFINITY) ? 0.f : m;
-      if (need) {
-        // O_g is stable: PV_g(j-1) completed before S_g(j) (in-order tcgen05)
-        const float f = (m_old == -INFINITY) ? 0.f : fast_exp2(m_old - m);
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
-          uint32_t o_raw[16];
-          tmem_ld_32x32b_x16(o_t + c * 16, o_raw);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * f);
-          tmem_st_32x32b_x16(o_t + c * 16, o_raw);
-        }
-        l *= f;
-      }
-      attn_trace(p, warp, lane, j, 2);
-      // p = 2^(s * scale_log2 - m): packed FFMA per pair, then the SFU (or, for POLY of
-      // every 8 pairs, the FMA-pipe polynomial); packed sums in 2 chains
-      const float sc = p.scale_log2, neg_m = -m_use;
-      const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(neg_m, neg_m);
-      uint64_t rs2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
-#pragma unroll
-      for (int qtr = 0; qtr < 4; ++qtr) {  // 32 scores -> 16 packed P words per TMEM store
+      const float sc = p.scale_log2;
+      const uint64_t sc2 = f2_pack(sc, sc);
+      // P of keys [32 qtr, 32 qtr + 32) = 2^(s * scale_log2 - m_use): packed FFMA per pair, then the
+      // SFU (or, for POLY of every 8 pairs, the FMA-pipe polynomial), bf16x2 into TMEM over S;
+      // row sums into rs (2 packed chains)
+      auto exp_quarter = [&](int qtr, float m_use, uint64_t (&rs)[2]) {
+        const uint64_t nm2 = f2_pack(-m_use, -m_use);
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
@@ -466,22 +435,109 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
             e0 = fast_exp2(x0);
             e1 = fast_exp2(x1);
           }
-          rs2[c & 1] = f2_add(rs2[c & 1], f2_pack(e0, e1));
+          rs[c & 1] = f2_add(rs[c & 1], f2_pack(e0, e1));
           pk[c] = pack_bf16x2(e0, e1);
         }
         tmem_st_32x32b_x16(s_t + qtr * 16, pk);
-        if (qtr & 1) {  // keys [0, 64) / [64, 128) of P are in TMEM
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(&p_full[2 * g + (qtr >> 1)]);
-          attn_trace(p, warp, lane, j, 3 + (qtr >> 1));
+      };
+      auto signal_half = [&](int hf) {  // keys [64 hf, 64 hf + 64) of P are in TMEM
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[2 * g + hf]);
+        attn_trace(p, warp, lane, j, 3 + hf);
+      };
+      auto add_sums = [&](const uint64_t (&rs)[2]) {
+        float a0, a1, b0, b1;
+        f2_unpack(rs[0], a0, a1);
+        f2_unpack(rs[1], b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      };
+      // raw-score max over keys [k0, k0 + 64): 8 chains of 3-input max (short dependency depth)
+      auto half_max = [&](int k0) {
+        float mxa[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) mxa[t] = fmaxf(s[k0 + t], s[k0 + 8 + t]);
+#pragma unroll
+        for (int c = k0 + 16; c < k0 + 64; c += 16) {
+#pragma unroll
+          for (int t = 0; t < 8; ++t) mxa[t] = max3(mxa[t], s[c + t], s[c + 8 + t]);
+        }
+        return fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                     fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+      };
+      // O_g *= f (TMEM round trip); O_g is stable whenever this runs (see callers)
+      auto rescale_o = [&](float f) {
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t o_raw[16];
+          tmem_ld_32x32b_x16(o_t + c * 16, o_raw);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * f);
+          tmem_st_32x32b_x16(o_t + c * 16, o_raw);
+        }
+      };
+      // Speculative tile (a running max exists in every row of the warp): the exponentials of
+      // each half use the current max while the half's own max is computed alongside them (off
+      // the critical path).  Half 0 keeps the lazy-rescale rule (accept growth <= 2^8, else the
+      // exact tile below recomputes everything from the scores still in registers).  Half 1 is
+      // committed after half 0 went to the tensor core: growth up to 2^64 is accepted (P <= 2^64
+      // is exact in bf16 / f32, and the next tile rescales), beyond that the warp waits for the
+      // first half of PV_g(j), rescales O_g and l to the new max and recomputes half 1.
+      bool done = false;
+      if (p.spec && j > 0 && __all_sync(0xffffffffu, m != -INFINITY)) {
+        uint64_t rs0[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+        exp_quarter(0, m, rs0);
+        exp_quarter(1, m, rs0);
+        const float mh0 = half_max(0);
+        attn_trace(p, warp, lane, j, 2);
+        if (!__any_sync(0xffffffffu, mh0 * sc > m + 8.0f)) {
+          signal_half(0);
+          add_sums(rs0);
+          uint64_t rs1[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+          exp_quarter(2, m, rs1);
+          exp_quarter(3, m, rs1);
+          const float mh1 = half_max(64);
+          if (__any_sync(0xffffffffu, mh1 * sc > m + 64.0f)) {
+            const float m2 = fmaxf(m, mh1 * sc);
+            const float f = fast_exp2(m - m2);
+            if (!mbar_wait(&pv_half[g], j & 1, err, kKidAttn, 124 + g, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            rescale_o(f);
+            l *= f;
+            m = m2;
+            rs1[0] = rs1[1] = f2_pack(0.f, 0.f);
+            exp_quarter(2, m, rs1);
+            exp_quarter(3, m, rs1);
+          }
+          signal_half(1);
+          add_sums(rs1);
+          done = true;
         }
       }
-      {
-        float a0, a1, b0, b1;
-        f2_unpack(rs2[0], a0, a1);
-        f2_unpack(rs2[1], b0, b1);
-        l += (a0 + a1) + (b0 + b1);
+      if (!done) {
+        const float mx = fmaxf(half_max(0), half_max(64));
+        const float m_new = fmaxf(m, mx * sc);  // scale > 0: max commutes with it
+        // the rescale decision is warp-uniform: tcgen05.ld / st are warp-collective
+        const bool need = (j > 0) && __any_sync(0xffffffffu, m_new > m + 8.0f);
+        const float m_old = m;
+        if (j == 0 || need) m = m_new;
+        const float m_use = (m == -INFINITY) ? 0.f : m;
+        // O_g is stable: PV_g(j-1) completed before S_g(j) (in-order tcgen05)
+        if (need) {
+          const float f = (m_old == -INFINITY) ? 0.f : fast_exp2(m_old - m);
+          rescale_o(f);
+          l *= f;
+        }
+        attn_trace(p, warp, lane, j, 2);
+        uint64_t rs[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+        exp_quarter(0, m_use, rs);
+        exp_quarter(1, m_use, rs);
+        signal_half(0);
+        exp_quarter(2, m_use, rs);
+        exp_quarter(3, m_use, rs);
+        signal_half(1);
+        add_sums(rs);
       }
     }
     // ------------------------------------------------------------ epilogue
@@ -668,6 +724,7 @@ int launch_attn_poly(const AttnArgs* a, const AttnParams& p, const CUtensorMap& 
   return (int)cudaGetLastError();
 }
 
+int g_attn_spec = 0;  // speculative running max in the softmax warps (measured 2.6 % slower at head dim 128)
 int g_attn_poly = 0;  // exponential pairs (of 8) on the FMA pipe (0 measured fastest at head dim 128)
 
 template <int QT>
@@ -685,6 +742,7 @@ int launch_attn(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, c
 
 // Fraction (n / 8) of the softmax exponentials evaluated by the FMA-pipe polynomial.
 extern "C" void dfl_attention_set_poly(int n) { g_attn_poly = n < 0 ? 0 : (n > 3 ? 3 : n); }
+extern "C" void dfl_attention_set_spec(int on) { g_attn_spec = on ? 1 : 0; }
 
 // Key-range splits: modelled time = waves of CTAs x (one full-range CTA time / s) + the
 // split overhead (partial f32 rows written and read back by the combine, CTA start-up),
@@ -758,6 +816,7 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   }
   p.kv_splits = a->kv_splits > 1 ? a->kv_splits : 1;
   p.split_o = a->split_o;
+  p.spec = g_attn_spec;
   p.split_lse = a->split_lse;
   if (p.kv_splits > 1) {
     if (a->merge_mode != 0 || !a->split_o || !a->split_lse || (reinterpret_cast<uintptr_t>(a->split_o) & 15))

@@ -728,6 +728,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "difflet_b200 native sm_100a kernels";
   m.def("gemm_set_pair_auto", [](bool on) { dfl_gemm_set_pair_auto(on ? 1 : 0); });
   m.def("attention_set_poly", [](int64_t n) { dfl_attention_set_poly((int)n); });
+  m.def("attention_set_spec", [](int64_t on) { dfl_attention_set_spec((int)on); });
   m.def("gemm_set_epi_warps", [](int64_t n) { dfl_gemm_set_epi_warps((int)n); });
   m.def("gemm_set_split_workspace", [](const at::Tensor& ws, const at::Tensor& sem) {
     TORCH_CHECK(ws.is_cuda() && sem.is_cuda() && ws.device() == sem.device(), "workspace tensors on one device");

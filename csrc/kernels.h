@@ -221,6 +221,7 @@ int dfl_attention(const AttnArgs* a, cudaStream_t stream);
 int dfl_attention_plan_splits(const AttnArgs* a);
 // n of every 8 softmax exponential pairs on the FMA pipe (0..3; default 0).
 void dfl_attention_set_poly(int n);
+void dfl_attention_set_spec(int on);  // speculative running max (default 0)
 
 // ---------------------------------------------------------------------------
 // Peer-memory communication runtime (comm.cu)

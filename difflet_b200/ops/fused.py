@@ -59,6 +59,7 @@ def _lib():
         _nat = _native.require()
         _nat.gemm_set_pair_auto(envs.DIFFLET_GEMM_PAIR != "0")
         _nat.attention_set_poly(envs.DIFFLET_ATTN_POLY)
+        _nat.attention_set_spec(envs.DIFFLET_ATTN_SPEC)
         _nat.gemm_set_epi_warps(envs.DIFFLET_GEMM_EPI_WARPS)
     _split_workspace(_nat)
     return _nat

@@ -286,6 +286,41 @@ def test_attention_bounds_large_logits_token_major(native):
     _close(o_view, ref)
 
 
+def test_attention_running_max_jumps(native):
+    """Scores that jump after the first key tile take every running-max path of the softmax:
+    growth beyond 2^64 inside the second half of a tile (rescale after the first half of PV),
+    growth accepted on the stale max (second half, then rescaled by the next tile), growth in
+    the first half (exact tile), and large random logits; half of the query rows see no jump."""
+    torch.manual_seed(21)
+    B, H, Sq, Sk = 1, 4, 256, 512
+    q = torch.randn(B, H, Sq, 128, device="cuda") * 0.05
+    k = torch.randn(B, H, Sk, 128, device="cuda") * 0.05
+    v = torch.randn(B, H, Sk, 128, device="cuda")
+    q[..., 0] = (torch.arange(Sq, device="cuda") % 2).float()  # odd rows see the jump
+    k[..., 0] = 0.0
+    k[0, 0, 228, 0] = 60.0  # tile 1, second half: 2^86 above the running max
+    k[0, 1, 218, 0] = 20.0  # tile 1, second half: 2^29, accepted on the stale max
+    k[0, 2, 266, 0] = 60.0  # tile 2, first half
+    k[0, 3] = torch.randn(Sk, 128, device="cuda") * 2.0
+    q[0, 3] = torch.randn(Sq, 128, device="cuda") * 2.0
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    scale = 1.0
+    ref, ref_lse = _attn_ref(q, k, v, scale)
+    try:
+        for spec in (0, 1):  # exact running max, then the speculative one
+            native.attention_set_spec(spec)
+            lse = torch.empty(B, H, Sq, device="cuda")
+            o = native.attention(q, k, v, scale, lse=lse)
+            torch.cuda.synchronize()
+            _close(o, ref)
+            assert (lse - ref_lse).abs().max().item() < 5e-2
+    finally:
+        from difflet_b200 import envs
+
+        native.attention_set_spec(envs.DIFFLET_ATTN_SPEC)
+    assert native.error_word(torch.cuda.current_device()).cpu().tolist() == [0, 0, 0, 0]
+
+
 def test_error_word_clean(native):
     torch.cuda.synchronize()
     assert native.error_word(torch.cuda.current_device()).cpu().tolist() == [0, 0, 0, 0]
