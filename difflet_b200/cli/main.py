@@ -98,6 +98,10 @@ def build_parser() -> argparse.ArgumentParser:
     b = sub.add_parser("bench", help="kernel microbenchmarks (or the headline bench with --headline)")
     b.add_argument("--only", default="gemm,attn,ln")
     b.add_argument("--headline", action="store_true")
+    b.add_argument("--suite", default=None, help="run a bench suite (name under bench/suites or a YAML path)")
+    b.add_argument("--out", default="bench_results", help="suite results directory (JSONL per suite)")
+    b.add_argument("--dry-run", action="store_true", help="print the suite's launches without running them")
+    b.add_argument("--no-idle-check", action="store_true", help="skip the GPU idle check before each launch")
     return ap
 
 
@@ -274,6 +278,23 @@ def cmd_serve(a) -> int:
 
 
 def cmd_bench(a) -> int:
+    if a.suite:
+        from difflet_b200.bench import suite as S
+
+        su = S.load_suite(a.suite)
+        launches = S.plan(su)
+        idle = None
+        if not (a.dry_run or a.no_idle_check):
+            from difflet_b200.bench.host import check_idle
+
+            idle = check_idle
+        recs = S.run(su, launches, a.out, idle=idle, dry_run=a.dry_run)
+        if a.dry_run:
+            for r in recs:
+                print(json.dumps({"run": r["run"], "launch": r["launch"], "argv": r["argv"]}))
+            return 0
+        print(json.dumps(S.summarize(su, recs), indent=1))
+        return 1 if any(r.get("error") for r in recs) else 0
     if a.headline:
         import runpy
 
