@@ -88,6 +88,10 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--port", type=int, default=8000)
     s.add_argument("--api-key", default=None)
     s.add_argument("--dp-degree", type=int, default=1)
+    s.add_argument("--max-queued-requests", type=int, default=8, help="waiting requests per replica before HTTP 429")
+    s.add_argument("--queue-timeout", type=float, default=None, help="seconds a request may wait for its replica")
+    s.add_argument("--request-timeout", type=float, default=600.0, help="seconds before a request is cancelled")
+    s.add_argument("--heartbeat-interval", type=float, default=None, help="worker heartbeat period (s)")
     c = sub.add_parser("cache", help="inspect the artefact cache")
     c.add_argument("--cache-dir", default=None)
     c.add_argument("--json", action="store_true")

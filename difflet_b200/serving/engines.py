@@ -33,21 +33,47 @@ class EngineError(RuntimeError):
     pass
 
 
+class _Admission:
+    """One running request per replica; at most ``max_queued`` more wait for it (beyond that a
+    request is refused at once), each for at most ``queue_timeout`` seconds."""
+
+    def __init__(self, queue_timeout: float, max_queued: int | None):
+        self.queue_timeout = queue_timeout
+        self.max_queued = max_queued
+        self._lock = threading.Lock()
+        self._guard = threading.Lock()
+        self.waiting = 0
+
+    def acquire(self):
+        with self._guard:
+            if self.max_queued is not None and self.waiting >= self.max_queued and self._lock.locked():
+                raise QueueTimeout("server busy: queue full")
+            self.waiting += 1
+        try:
+            if not self._lock.acquire(timeout=self.queue_timeout):
+                raise QueueTimeout("server busy")
+        finally:
+            with self._guard:
+                self.waiting -= 1
+
+    def release(self):
+        self._lock.release()
+
+
 class InProcessEngine:
     """Runs ``generate_fn(request) -> result`` in this process (tests, single-process serving)."""
 
-    def __init__(self, generate_fn: Callable[[dict], Any], queue_timeout: float = 30.0):
+    def __init__(self, generate_fn: Callable[[dict], Any], queue_timeout: float = 30.0, max_queued: int | None = None):
         self.fn = generate_fn
         self.queue_timeout = queue_timeout
-        self._lock = threading.Lock()
+        self._adm = _Admission(queue_timeout, max_queued)
         self.ready = True
         self.healthy = True
         self.inflight = 0
         self.completed = 0
 
     def generate(self, request: dict, timeout: float | None = None):
-        if not self._lock.acquire(timeout=self.queue_timeout):
-            raise QueueTimeout("server busy")
+        self._adm.acquire()
         self.inflight += 1
         try:
             out = self.fn(request)
@@ -55,7 +81,7 @@ class InProcessEngine:
             return out
         finally:
             self.inflight -= 1
-            self._lock.release()
+            self._adm.release()
 
     def close(self):
         pass
@@ -107,16 +133,16 @@ class ResidentWorkerEngine:
     (picklable result).  It must be importable by name (spawn)."""
 
     def __init__(self, factory, factory_kwargs=None, *, queue_timeout=30.0, request_timeout=600.0,
-                 heartbeat_s=5.0, heartbeat_timeout=None, start_timeout=1800.0):
+                 heartbeat_s=5.0, heartbeat_timeout=None, start_timeout=1800.0, max_queued=None):
         self.factory = factory
         self.factory_kwargs = dict(factory_kwargs or {})
         self.queue_timeout = queue_timeout
+        self._adm = _Admission(queue_timeout, max_queued)
         self.request_timeout = request_timeout
         self.heartbeat_s = heartbeat_s
         self.heartbeat_timeout = heartbeat_timeout or max(6 * heartbeat_s, 30.0)
         self.start_timeout = start_timeout
         self._ctx = mp.get_context("spawn")
-        self._lock = threading.Lock()
         self.ready = False
         self.healthy = True
         self.inflight = 0
@@ -174,8 +200,7 @@ class ResidentWorkerEngine:
         raise EngineError(f"request failed, worker restarted ({reason})")
 
     def generate(self, request: dict, timeout: float | None = None):
-        if not self._lock.acquire(timeout=self.queue_timeout):
-            raise QueueTimeout("server busy")
+        self._adm.acquire()
         self.inflight += 1
         try:
             rid = str(uuid.uuid4())
@@ -204,7 +229,7 @@ class ResidentWorkerEngine:
                 raise EngineError(payload)
         finally:
             self.inflight -= 1
-            self._lock.release()
+            self._adm.release()
 
     def close(self):
         try:

@@ -9,7 +9,6 @@ images / frames (moved to the host) for the API layer to encode.
 from __future__ import annotations
 
 import logging
-import os
 
 
 def pipeline_runner(model_id: str, pipeline_kwargs: dict):
@@ -48,11 +47,14 @@ def serve_main(a) -> int:
     kw = {"parallel": parallel_from_args(a), "backend": a.backend, "height": a.height, "width": a.width,
           "num_frames": a.num_frames, "compile_cache_dir": a.cache_dir, "random_init": a.random_weights,
           "application_kwargs": _app_kwargs(a)}
-    api_key = a.api_key or os.environ.get("DIFFLET_API_KEY")
-    replicas = [ResidentWorkerEngine(pipeline_runner, {"model_id": a.model_id, "pipeline_kwargs": kw})
-                for _ in range(max(1, a.dp_degree))]
+    from difflet_b200.serving.options import ServeOptions
+
+    opts = ServeOptions.from_args(a)
+    replicas = [ResidentWorkerEngine(pipeline_runner, {"model_id": a.model_id, "pipeline_kwargs": kw},
+                                     **opts.engine_kwargs())
+                for _ in range(opts.replicas)]
     engine = replicas[0] if len(replicas) == 1 else ReplicatedEngine(replicas)
-    app = create_app(engine, a.model_id, output=entry.output, api_key=api_key)
-    uvicorn.run(app, host=a.host, port=a.port, log_level="info")
+    app = create_app(engine, a.model_id, output=entry.output, api_key=opts.api_key)
+    uvicorn.run(app, host=opts.host, port=opts.port, log_level="info")
     engine.close()
     return 0

@@ -102,3 +102,35 @@ def test_resident_worker_recovers_from_crash_and_timeout():
         assert eng.restarts == 2 and eng.generate({"prompt": "e"}) == {"echo": "e"}
     finally:
         eng.close()
+
+
+def test_queue_full_refused_at_once_and_options():
+    """One request runs, ``max_queued`` wait; the next is refused without waiting."""
+    from difflet_b200.serving.engines import QueueTimeout
+    from difflet_b200.serving.options import ServeOptions
+
+    gate = threading.Event()
+    eng = InProcessEngine(lambda req: (gate.wait(5), req)[1], queue_timeout=5.0, max_queued=1)
+    running = threading.Thread(target=lambda: eng.generate({"i": 0}))
+    running.start()
+    time.sleep(0.1)
+    waiting = threading.Thread(target=lambda: eng.generate({"i": 1}))
+    waiting.start()
+    time.sleep(0.1)
+    t0 = time.time()
+    try:
+        eng.generate({"i": 2})
+        refused = False
+    except QueueTimeout as exc:
+        refused = "queue full" in str(exc)
+    assert refused and time.time() - t0 < 1.0
+    gate.set()
+    running.join()
+    waiting.join()
+    assert eng.completed == 2
+
+    o = ServeOptions(model_id="flux", api_key="secret", max_queued_requests=3)
+    assert "secret" not in repr(o) and o.engine_kwargs()["max_queued"] == 3
+    for bad in ({"port": 0}, {"replicas": 0}, {"queue_timeout": 0}, {"heartbeat_interval": 0.0}):
+        with pytest.raises(ValueError):
+            ServeOptions(model_id="flux", **bad)
