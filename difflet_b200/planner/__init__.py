@@ -28,7 +28,9 @@ _EFF_SCALE = [0.85]      # calibrated fraction of the measured GEMM peak
 
 
 def model_shape(entry, height=None, width=None, num_frames=None) -> dict:
-    """Per-step workload: tokens, hidden, layers, heads, params (rough, from the presets)."""
+    """Per-step workload: tokens, hidden, layers, heads, and ``params`` = the weights of the linears
+    every token passes through (MMDiT dual blocks count one stream; the per-step modulation
+    GEMVs are not token work)."""
     s = entry.resolve_shape(height=height, width=width, num_frames=num_frames)
     h, w, f = s.get("height") or 1024, s.get("width") or 1024, s.get("num_frames")
     if entry.name == "wan":
@@ -40,7 +42,8 @@ def model_shape(entry, height=None, width=None, num_frames=None) -> dict:
         return dict(tokens=t * (h // 16) * (w // 16), text=256, hidden=3072, layers=60, heads=24, params=13e9, mlp=4)
     if entry.name == "qwen_image":
         return dict(tokens=(h // 16) * (w // 16), text=256, hidden=3072, layers=60, heads=24, params=20e9, mlp=4)
-    return dict(tokens=(h // 16) * (w // 16), text=512, hidden=3072, layers=57, heads=24, params=12e9, mlp=4)
+    # FLUX.1: 19 dual blocks (one stream per token: 113 M) + 38 single blocks (113 M)
+    return dict(tokens=(h // 16) * (w // 16), text=512, hidden=3072, layers=57, heads=24, params=6.45e9, mlp=4)
 
 
 def enumerate_candidates(entry, gpus: int, exact: bool = True) -> list[DiffletParallelConfig]:
@@ -69,15 +72,32 @@ def _eff(rows: int) -> float:
     return _EFF_SCALE[0] * min(1.0, rows / 2048.0) ** 0.35
 
 
+ATTN_EFF = 0.80  # flash attention's measured fraction of the sustained GEMM peak (FLUX 24 x 4608)
+KERNEL_TAIL_S = 3e-6  # fill / drain of one launch inside the CUDA graph
+KERNELS_PER_LAYER = 8
+N_SMS = 148
+
+
+def _attn_occupancy(heads_per_rank: int, seq: int) -> float:
+    """Fraction of the SMs the attention grid keeps busy (256-query CTAs; grids under half the
+    SMs split the key range in two)."""
+    ctas = max(1, heads_per_rank) * math.ceil(seq / 256)
+    if ctas * 2 <= N_SMS:
+        ctas *= 2
+    return ctas / (math.ceil(ctas / N_SMS) * N_SMS)
+
+
 def estimate_step_s(entry, p: DiffletParallelConfig, shape: dict, peak_flops: float) -> float:
     S = shape["tokens"] + shape["text"]
     D, L = shape["hidden"], shape["layers"]
     cfg_mult = 1 if (entry.capabilities and entry.capabilities.is_distilled) else 2
-    flops = 2.0 * shape["params"] * S + 4.0 * L * S * S * D
-    flops *= cfg_mult
+    gemm_flops = 2.0 * shape["params"] * S * cfg_mult
+    attn_flops = 4.0 * L * S * S * D * cfg_mult
     world_model = p.tp_degree * p.cp_degree * (2 if p.cfg_parallel_enabled else 1)
-    rows = S // (p.cp_degree * (1 if p.tp_degree == 1 else 1))
-    t_comp = flops / (world_model * peak_flops * _eff(rows))
+    rows = S // p.cp_degree
+    heads_rank = max(1, shape["heads"] // (p.tp_degree * p.cp_degree))
+    t_comp = gemm_flops / (world_model * peak_flops * _eff(rows)) + attn_flops / (
+        world_model * peak_flops * ATTN_EFF * _attn_occupancy(heads_rank, S))
     act = S * D * 2 / max(1, p.cp_degree)  # bytes of one activation shard
     comm = 0.0
     syncs = 0
@@ -99,7 +119,7 @@ def estimate_step_s(entry, p: DiffletParallelConfig, shape: dict, peak_flops: fl
         comm += shape["tokens"] * 64 * 2
         syncs += 2
     t_comm = comm / LINK_BW / max(1.0, 0.5 * (1 + (p.cp_degree > 1)))  # partial overlap with compute
-    return (t_comp + t_comm + syncs * SYNC_S) * cfg_mult / cfg_mult
+    return t_comp + t_comm + syncs * SYNC_S + L * KERNELS_PER_LAYER * KERNEL_TAIL_S
 
 
 def plan(model_id: str, *, gpus: int = 8, height=None, width=None, num_frames=None, exact: bool = True) -> list[dict]:

@@ -21,3 +21,18 @@ def test_wan_plan_ranks_and_offers_cfg():
 def test_calibrate_moves_scale():
     s = calibrate([(1.0, 2.0)])
     assert 0.05 <= s <= 1.0
+
+
+def test_flux_estimates_track_measured_steps():
+    """The cost model against FLUX.1-dev 1024² DiT steps measured on B200 with this engine
+    (Ulysses): 65.3 / 37.7 / 22.8 / 17.4 ms at 1 / 2 / 4 / 8 GPUs."""
+    from difflet_b200 import planner as P
+    from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
+    from difflet_b200.registry import resolve_model
+
+    e = resolve_model("black-forest-labs/FLUX.1-dev")
+    shape = P.model_shape(e)
+    for n, measured_ms in ((1, 65.3), (2, 37.7), (4, 22.8), (8, 17.4)):
+        p = DiffletParallelConfig(cp_degree=n, cp_mode="ulysses") if n > 1 else DiffletParallelConfig()
+        est_ms = P.estimate_step_s(e, p, shape, 1397.4e12) * 1e3
+        assert abs(est_ms - measured_ms) / measured_ms < 0.2, (n, est_ms, measured_ms)
