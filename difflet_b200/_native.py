@@ -59,13 +59,24 @@ def _bounds_check() -> bool:
     return bool(envs.DIFFLET_BOUNDS_CHECK)
 
 
+def _attn_trace() -> bool:
+    import os
+
+    return os.environ.get("DIFFLET_ATTN_TRACE", "0") not in ("", "0")
+
+
 def _ext_name() -> str:
-    """The release module, or the debug build with device index guards (DIFFLET_BOUNDS_CHECK=1)."""
-    return EXT_NAME + ("_bounds" if _bounds_check() else "")
+    """The release module, the debug build with device index guards (DIFFLET_BOUNDS_CHECK=1), or
+    the attention-trace diagnostic build (DIFFLET_ATTN_TRACE=1: per-tile clock64 events)."""
+    if _bounds_check():
+        return EXT_NAME + "_bounds"
+    return EXT_NAME + ("_trace" if _attn_trace() else "")
 
 
 def _nvcc_flags() -> list:
-    return NVCC_FLAGS + (["-DDFL_BOUNDS_CHECK"] if _bounds_check() else [])
+    if _bounds_check():
+        return NVCC_FLAGS + ["-DDFL_BOUNDS_CHECK"]
+    return NVCC_FLAGS + (["-DDFL_ATTN_TRACE"] if _attn_trace() else [])
 
 _lock = threading.Lock()
 _module = None
