@@ -1,4 +1,5 @@
 """Headline benchmark: FLUX.1-dev 1024x1024 DiT denoise step (and e2e s/image) on N B200s.
+``--model wan``: Wan2.2-T2V-A14B 1280x720x81 DiT step / decode / e2e s/video.
 
 Contract (one rank per GPU; the driver launches N > 1 under torch.distributed.run):
   python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
@@ -123,6 +124,157 @@ def _profile_step(path: str, rank: int, world: int, fwd) -> None:
     _log(f"profiled one eager step of rank 0 into {path}")
 
 
+def wan_layout(world: int, spec: str | None):
+    """DiffletParallelConfig of a Wan layout: cfg2 / ulysses<N> / tp<N> factors joined by 'x'."""
+    from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
+
+    if spec is None:
+        spec = {1: "single", 2: "cfg2", 4: "cfg2xulysses2", 8: "cfg2xulysses4"}.get(world, f"cfg2xulysses{world // 2}")
+    if spec == "single":
+        return DiffletParallelConfig(), spec
+    cfg, cp, tp, mode = False, 1, 1, "gather_kv"
+    for part in spec.split("x"):
+        if part == "cfg2":
+            cfg = True
+        elif part.startswith("tp"):
+            tp = int(part[2:])
+        else:
+            for m in ("ulysses", "ring", "gather_kv"):
+                if part.startswith(m):
+                    mode, cp = m, int(part[len(m):])
+    par = DiffletParallelConfig(tp_degree=tp, cp_degree=cp, cfg_parallel_enabled=cfg, cp_mode=mode)
+    if par.world_size != world:
+        raise SystemExit(f"layout {spec} needs {par.world_size} ranks, launched with {world}")
+    return par, spec
+
+
+def run_wan(args, world, rank):
+    """Wan2.2-T2V-A14B (two 14B experts) at 1280x720x81 frames: 40 UniPC steps, true CFG 5.0.
+
+    * ``value``: one denoise step (high-noise expert, both CFG branches, the fused CFG + UniPC
+      kernel), device-timed over K steps after W warm-up steps, max over ranks.  The 28 GB expert
+      and the ~20 GB of per-step activations stream through HBM every step (far above L2).
+    * ``decode`` (``--decode``): one causal VAE decode of the 21x90x160 latents to 81 frames.
+    * ``e2e`` (``--e2e``): a whole video through the public API -- host->device copies of the
+      text states and noise from pinned memory, 40 steps, decode, uint8 frames back to the host."""
+    import torch
+
+    from difflet_b200 import _native
+    from difflet_b200.bench.clocks import ClockSampler
+    from difflet_b200.pipeline.difflet_pipeline import DiffletPipeline
+
+    par, layout = wan_layout(world, args.layout)
+    H, W, Fr = args.height if args.height != 1024 else 720, args.width if args.width != 1024 else 1280, args.frames
+    t_load = time.time()
+    pipe = DiffletPipeline.from_pretrained("Wan-AI/Wan2.2-T2V-A14B-Diffusers", parallel=par, height=H, width=W,
+                                           num_frames=Fr, random_init=True, skip_warmup=True)
+    load_s = time.time() - t_load
+    _log(f"Wan pipeline loaded in {load_s:.1f}s ({layout})")
+    app = pipe.app.app
+    cfg = app.cfg
+    steps_total = 40
+    gen = torch.Generator().manual_seed(11)
+    T = (Fr - 1) // cfg.vae_scale_t + 1
+    emb = torch.randn(1, cfg.text_len, cfg.text_dim, generator=gen).to(torch.bfloat16).pin_memory()
+    neg = torch.randn(1, cfg.text_len, cfg.text_dim, generator=gen).to(torch.bfloat16).pin_memory()
+    noise = torch.randn(1, cfg.in_channels, T, H // cfg.vae_scale, W // cfg.vae_scale, generator=gen).pin_memory()
+    if args.warmup + args.steps > 26:
+        raise SystemExit("warm-up + timed steps must stay on the high-noise expert (<= 26 of 40 steps)")
+    run = app.prepare(prompt_embeds=emb, negative_prompt_embeds=neg, height=H, width=W, num_frames=Fr,
+                      num_inference_steps=steps_total, guidance_scale=5.0, latents=noise)
+    S_tok = run.grid[0] * run.grid[1] * run.grid[2]
+    _log(f"{S_tok} tokens per branch; warming up {args.warmup} steps")
+    for i in range(args.warmup):
+        run.step(i)
+    torch.cuda.synchronize()
+    n0 = _launch_count()
+    run.step(args.warmup)
+    launches_per_step = _launch_count() - n0
+    _barrier(world)
+    sampler = ClockSampler(_gpu_ids(world) if rank == 0 else [])
+    with sampler:
+        _barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(args.steps):
+            run.step(args.warmup + 1 + i)
+        end.record()
+        _barrier(world)
+    ms = _max_over_ranks(start.elapsed_time(end) / args.steps, world)
+    clocks = sampler.summary() if rank == 0 else {}
+    _log(f"timed {args.steps} steps: {ms:.1f} ms/step")
+    _native.check_device_errors()
+
+    decode = None
+    if args.decode:
+        lat = run.latents()
+        _barrier(world)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        video = app.decode(lat)
+        t1.record()
+        torch.cuda.synchronize()
+        dec_ms = _max_over_ranks(t0.elapsed_time(t1), world)
+        decode = {"ms": round(dec_ms, 1), "frames": Fr,
+                  "shape": None if video is None else list(video.shape)}
+        _log(f"decode: {dec_ms:.1f} ms")
+        del video
+    del run
+    e2e = None
+    if args.e2e:
+        h2d = sum(t.numel() * t.element_size() for t in (emb, neg, noise))
+        d2h = 0
+
+        def one_video():
+            nonlocal d2h
+            vid = pipe(prompt_embeds=emb, negative_prompt_embeds=neg, latents=noise, num_inference_steps=steps_total,
+                       guidance_scale=5.0, height=H, width=W, num_frames=Fr)
+            if vid is not None:
+                host = vid.to("cpu")
+                d2h = host.numel() * host.element_size()
+
+        _barrier(world)
+        t0 = time.perf_counter()
+        one_video()
+        _barrier(world)
+        e2e_s = _max_over_ranks(time.perf_counter() - t0, world)
+        e2e = {"value": round(e2e_s, 3), "unit": "s/video", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "steps_per_video": steps_total,
+               "note": "first call of the process (includes per-prompt context setup; no separate warm-up video)"}
+        _native.check_device_errors()
+    if rank == 0:
+        out = {
+            "metric": "Wan2.2-T2V-A14B 1280x720x81 DiT denoise step latency (both CFG branches, max over ranks)",
+            "value": round(ms, 2), "unit": "ms/step", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 2), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (random-init Wan2.2-A14B experts, N(0,1) umT5-shaped text / noise)",
+            "config": {"model": "Wan2.2-T2V-A14B", "global_batch": 1, "seq_len": S_tok, "height": H, "width": W,
+                       "frames": Fr, "guidance": 5.0, "parallelism": layout, "load_s": round(load_s, 1),
+                       "l2": "28 GB expert + activations stream from HBM every step; no flush"},
+            "clocks": clocks, "gpu_launches": int(launches_per_step * args.steps), "decode": decode, "e2e": e2e,
+        }
+        print(json.dumps(out), flush=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def _launch_count() -> int:
+    from difflet_b200.ops import fused as F
+
+    return F.LAUNCHES[0]
+
+
+def _gpu_ids(world: int) -> list:
+    ids = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()]
+    return ids[:world] if ids else list(range(world))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -143,6 +295,15 @@ def main(argv=None):
     ap.add_argument("--sp", action="store_true", help="with --cp-mode tp: Megatron sequence parallelism")
     ap.add_argument("--quant", default=None, choices=[None, "mxfp8"],
                     help="MXFP8 block linears (default targets); the headline number is bf16")
+    ap.add_argument("--model", default="flux", choices=["flux", "wan"],
+                    help="flux: the headline FLUX.1-dev config; wan: Wan2.2-T2V-A14B 720p x 81 frames")
+    ap.add_argument("--layout", default=None,
+                    help="wan: parallel layout (default by N: 1 batched CFG, 2 cfg2, 4 cfg2xulysses2, "
+                         "8 cfg2xulysses4; also e.g. ulysses8, cfg2xtp2xulysses2)")
+    ap.add_argument("--frames", type=int, default=81)
+    ap.add_argument("--decode", action="store_true", help="wan: also time one VAE decode of the final latents")
+    ap.add_argument("--e2e", action="store_true",
+                    help="wan: time the full 40-step generate + decode through the public API (minutes at N=1)")
     args = ap.parse_args(argv)
     import faulthandler
 
@@ -153,6 +314,8 @@ def main(argv=None):
     world, rank, local = _dist_setup()
     if args.impl == "reference":
         return run_reference(args, world, rank)
+    if args.model == "wan":
+        return run_wan(args, world, rank)
 
     import torch
 

@@ -12,9 +12,8 @@
 //               has finished: no extra barrier guards P reuse or O rescaling.
 //   warps 0..3  softmax for Q tile 0; warps 4..7 for Q tile 1 (216 registers each
 //               after the setmaxnreg split): one query row per thread, running
-//               max in log2 units, exp2 on the SFU and (a fixed share) on the FMA
-//               pipe by a cubic, P packed to
-//               bf16x2 and stored to TMEM; O_g is rescaled in TMEM only when the
+//               max in log2 units, exp2 on the SFU, P packed to bf16x2 and
+//               stored to TMEM; O_g is rescaled in TMEM only when the
 //               max grew by more than 2^8 (a stale max keeps P <= 256, exact
 //               after the final 1/l); epilogue normalises and stores rows.
 // Optional per-batch key window [kv_lo, kv_hi), natural-log LSE output (ring /
@@ -54,8 +53,8 @@ struct AttnSmem {
   static constexpr int kRing = QT == 2 ? 5 : 6;             // K/V slots (224 KB of smem with Q)
   static constexpr int kKV = kQ + QT * kTileBytes;
   static constexpr int kBar = kKV + kRing * kTileBytes;
-  // q_full, kv_full[R], kv_empty[R], s_full[2], p_full[2][2], o_full, pv_half[2]
-  static constexpr int kNumBars = 1 + 2 * kRing + 2 + 4 + 1 + 2;
+  // q_full, kv_full[R], kv_empty[R], s_full[2], p_full[2][2], o_full
+  static constexpr int kNumBars = 1 + 2 * kRing + 2 + 4 + 1;
   static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -100,33 +99,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for two values on the FMA pipe, so part of the softmax exponentials leave the
-// SFU (whose 16 results / clock / SM match the tensor core's pace at head dim 128).
-// Range reduction x = j + f, j = round(x) (the 1.5 * 2^23 addition trick), f in
-// [-0.5, 0.5]; 2^f by a cubic fitted here for minimum relative error on that interval
-// (Lawson's iteratively reweighted least squares on 4000 Chebyshev nodes; max relative
-// error 7.5e-5, below the bf16 rounding of P); 2^j added to the exponent bits.
-// x is clamped at -125 (masked keys give 2^-125 instead of 0: negligible next to l >= 1).
-__device__ __forceinline__ void poly_exp2_x2(uint64_t x2, float& e0, float& e1) {
-  float x0, x1;
-  f2_unpack(x2, x0, x1);
-  x0 = fmaxf(x0, -125.f);
-  x1 = fmaxf(x1, -125.f);
-  const uint64_t xc = f2_pack(x0, x1);
-  const uint64_t magic = f2_pack(12582912.f, 12582912.f);
-  const uint64_t t = f2_add(xc, magic);                                 // j in the low mantissa bits
-  const uint64_t j = f2_add(t, f2_pack(-12582912.f, -12582912.f));      // round(x)
-  const uint64_t f = f2_fma(j, f2_pack(-1.f, -1.f), xc);                // x - round(x)
-  uint64_t pl = f2_fma(f2_pack(0.055171665f, 0.055171665f), f, f2_pack(0.24261113f, 0.24261113f));
-  pl = f2_fma(pl, f, f2_pack(0.69326097f, 0.69326097f));
-  pl = f2_fma(pl, f, f2_pack(0.99992806f, 0.99992806f));
-  float p0, p1, t0, t1;
-  f2_unpack(pl, p0, p1);
-  f2_unpack(t, t0, t1);
-  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
-  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
-}
-
 // D[tmem] (+)= A[tmem] * B[smem]  (A: M x K, one row per lane, 2 bf16 per column)
 __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
@@ -164,21 +136,10 @@ struct AttnParams {
   float* acc_o;    // f32 [B, H, Sq, 128] running output (merge modes)
   float* acc_lse;  // f32 [B, H, Sq] running log-sum-exp
   int merge_mode;  // 0 none, 1 first partial, 2 merge, 3 merge + final bf16 store
-  long long* trace;
   int kv_splits;    // > 1: CTA x = query block * kv_splits + chunk, partials to split_o / split_lse
   float* split_o;
   float* split_lse;
-  int spec;  // 1: speculative running max (exponentials before the max is known)
 };
-
-// Diagnostics (builds with -DDFL_ATTN_TRACE only): SM clock at event ev of key tile j
-// (lane 0 of each warp of CTA (0, 0, 0)); compiled out otherwise.
-__device__ __forceinline__ void attn_trace(const AttnParams& p, int warp, int lane, int j, int ev) {
-#ifdef DFL_ATTN_TRACE
-  if (p.trace != nullptr && lane == 0 && j < 64 && (blockIdx.x | blockIdx.y | blockIdx.z) == 0)
-    p.trace[((long long)warp * 64 + j) * 8 + ev] = clock64();
-#endif
-}
 
 // Output row address: local, or (Ulysses) the owning rank's buffer.
 __device__ __forceinline__ __nv_bfloat16* out_row(const AttnParams& p, int b, int h, int s, int* err = nullptr) {
@@ -206,8 +167,7 @@ __device__ __forceinline__ void tma_load_4d(uint8_t* dst, const CUtensorMap* map
       : "memory");
 }
 
-// POLY: of every 8 exponential pairs of a row, POLY are evaluated on the FMA pipe.
-template <int QT, int POLY>
+template <int QT>
 __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, AttnParams p, int* err) {
@@ -222,7 +182,6 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
   uint64_t* s_full = kv_empty + R;
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 4;  // p_full[2 g + h]: keys [64 h, 64 h + 64) of P_g stored
-  uint64_t* pv_half = o_full + 1;  // pv_half[g]: the first half of PV_g (one phase per key tile) completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AttnSmem<QT>::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -295,7 +254,6 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
           }
           uint8_t* dst = smem + AttnSmem<QT>::kKV + slot * kTileBytes;
           const CUtensorMap* map = which == 0 ? &tk : &tv;
-          attn_trace(p, warp, lane, j, which);
           mbar_arrive_expect_tx(&kv_full[slot], kTileBytes);
           for (int c = 0; c < 2; ++c) tma_load_4d(dst + c * kChunk, map, &kv_full[slot], c * 64, k0, h, b);
           issued[slot] = true;
@@ -347,7 +305,6 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
             umma_f16_ts(o_tmem, p_tmem + kk * 8, kHiV | (va + (uint32_t)((kk * 2048) >> 4)), idesc_pv,
                         (jj > 0 || kk > 0) ? 1u : 0u);
           }
-          if (hf == 0) umma_commit(&pv_half[g]);
         }
         return true;
       };
@@ -355,25 +312,19 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         return mbar_wait(&kv_full[L % R], (L / R) & 1, err, kKidAttn, detail, abort_flag);
       };
       for (int j = 0; j < n_tiles && ok; ++j) {
-        attn_trace(p, warp, lane, j, 5);
         if (!wait_load(2 * j, 113)) { ok = false; break; }
-        attn_trace(p, warp, lane, j, 0);
         if (j > 0) {
           if (!wait_load(2 * j - 1, 114)) { ok = false; break; }
           if (!issue_pv(0, j - 1)) { ok = false; break; }
         }
-        attn_trace(p, warp, lane, j, 1);
         tc_fence_after();
         issue_qk(0, j);
-        attn_trace(p, warp, lane, j, 2);
         if (j > 0) {
           if (QT == 2 && !issue_pv(1, j - 1)) { ok = false; break; }
           umma_commit(&kv_empty[(2 * j - 1) % R]);  // V_{j-1} consumed
         }
-        attn_trace(p, warp, lane, j, 3);
         if (QT == 2) issue_qk(1, j);
         umma_commit(&kv_empty[(2 * j) % R]);  // K_j consumed
-        attn_trace(p, warp, lane, j, 4);
       }
       if (ok) {
         const int jl = n_tiles - 1;
@@ -399,14 +350,12 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait(&s_full[g], j & 1, err, kKidAttn, 120 + g, abort_flag)) { ok = false; break; }
-      attn_trace(p, warp, lane, j, 0);
       tc_fence_after();
       float s[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         tmem_ld_32x32b_x32(s_t + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
-      attn_trace(p, warp, lane, j, 1);
       const int k0 = (t_first + j) * kBN;
       if ((k0 < lo) || (k0 + kBN > hi)) {  // edge tile: mask keys outside [lo, hi)
 #pragma unroll
@@ -418,23 +367,16 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
       const float sc = p.scale_log2;
       const uint64_t sc2 = f2_pack(sc, sc);
       // P of keys [32 qtr, 32 qtr + 32) = 2^(s * scale_log2 - m_use): packed FFMA per pair, then the
-      // SFU (or, for POLY of every 8 pairs, the FMA-pipe polynomial), bf16x2 into TMEM over S;
-      // row sums into rs (2 packed chains)
+      // SFU, bf16x2 into TMEM over S; row sums into rs (2 packed chains)
       auto exp_quarter = [&](int qtr, float m_use, uint64_t (&rs)[2]) {
         const uint64_t nm2 = f2_pack(-m_use, -m_use);
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const uint64_t x2 = f2_fma(f2_pack(s[qtr * 32 + 2 * c], s[qtr * 32 + 2 * c + 1]), sc2, nm2);
-          float e0, e1;
-          if ((c & 7) >= 8 - POLY) {
-            poly_exp2_x2(x2, e0, e1);
-          } else {
-            float x0, x1;
-            f2_unpack(x2, x0, x1);
-            e0 = fast_exp2(x0);
-            e1 = fast_exp2(x1);
-          }
+          float x0, x1;
+          f2_unpack(x2, x0, x1);
+          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
           rs[c & 1] = f2_add(rs[c & 1], f2_pack(e0, e1));
           pk[c] = pack_bf16x2(e0, e1);
         }
@@ -444,7 +386,6 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[2 * g + hf]);
-        attn_trace(p, warp, lane, j, 3 + hf);
       };
       auto add_sums = [&](const uint64_t (&rs)[2]) {
         float a0, a1, b0, b1;
@@ -477,45 +418,7 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
           tmem_st_32x32b_x16(o_t + c * 16, o_raw);
         }
       };
-      // Speculative tile (a running max exists in every row of the warp): the exponentials of
-      // each half use the current max while the half's own max is computed alongside them (off
-      // the critical path).  Half 0 keeps the lazy-rescale rule (accept growth <= 2^8, else the
-      // exact tile below recomputes everything from the scores still in registers).  Half 1 is
-      // committed after half 0 went to the tensor core: growth up to 2^64 is accepted (P <= 2^64
-      // is exact in bf16 / f32, and the next tile rescales), beyond that the warp waits for the
-      // first half of PV_g(j), rescales O_g and l to the new max and recomputes half 1.
-      bool done = false;
-      if (p.spec && j > 0 && __all_sync(0xffffffffu, m != -INFINITY)) {
-        uint64_t rs0[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
-        exp_quarter(0, m, rs0);
-        exp_quarter(1, m, rs0);
-        const float mh0 = half_max(0);
-        attn_trace(p, warp, lane, j, 2);
-        if (!__any_sync(0xffffffffu, mh0 * sc > m + 8.0f)) {
-          signal_half(0);
-          add_sums(rs0);
-          uint64_t rs1[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
-          exp_quarter(2, m, rs1);
-          exp_quarter(3, m, rs1);
-          const float mh1 = half_max(64);
-          if (__any_sync(0xffffffffu, mh1 * sc > m + 64.0f)) {
-            const float m2 = fmaxf(m, mh1 * sc);
-            const float f = fast_exp2(m - m2);
-            if (!mbar_wait(&pv_half[g], j & 1, err, kKidAttn, 124 + g, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            rescale_o(f);
-            l *= f;
-            m = m2;
-            rs1[0] = rs1[1] = f2_pack(0.f, 0.f);
-            exp_quarter(2, m, rs1);
-            exp_quarter(3, m, rs1);
-          }
-          signal_half(1);
-          add_sums(rs1);
-          done = true;
-        }
-      }
-      if (!done) {
+      {
         const float mx = fmaxf(half_max(0), half_max(64));
         const float m_new = fmaxf(m, mx * sc);  // scale > 0: max commutes with it
         // the rescale decision is warp-uniform: tcgen05.ld / st are warp-collective
@@ -529,7 +432,6 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
           rescale_o(f);
           l *= f;
         }
-        attn_trace(p, warp, lane, j, 2);
         uint64_t rs[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
         exp_quarter(0, m_use, rs);
         exp_quarter(1, m_use, rs);
@@ -696,19 +598,19 @@ int make_tmap_4d(CUtensorMap* map, const void* base, long long S, int H, int B, 
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-template <int QT, int POLY>
-int launch_attn_poly(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
-                     const CUtensorMap& tv, cudaStream_t stream) {
+template <int QT>
+int launch_attn(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
+                const CUtensorMap& tv, cudaStream_t stream) {
   static bool attr[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 15]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<QT, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnSmem<QT>::kTotal);
     if (e != cudaSuccess) return (int)e;
     if (QT == 2) {  // the setmaxnreg split must fit in the registers the CTA is launched with
       cudaFuncAttributes fa;
-      e = cudaFuncGetAttributes(&fa, attn_fwd_kernel<QT, POLY>);
+      e = cudaFuncGetAttributes(&fa, attn_fwd_kernel<QT>);
       if (e != cudaSuccess) return (int)e;
       if (fa.numRegs * AttnSmem<QT>::kThreads < 128 * 64 + 256 * 216) return -11;
     }
@@ -716,7 +618,7 @@ int launch_attn_poly(const AttnArgs* a, const AttnParams& p, const CUtensorMap& 
   }
   const int splits = p.kv_splits > 1 ? p.kv_splits : 1;
   dim3 grid((a->Sq + QT * kBM - 1) / (QT * kBM) * splits, a->H, a->B);
-  attn_fwd_kernel<QT, POLY><<<grid, AttnSmem<QT>::kThreads, AttnSmem<QT>::kTotal, stream>>>(tq, tk, tv, p, a->err);
+  attn_fwd_kernel<QT><<<grid, AttnSmem<QT>::kThreads, AttnSmem<QT>::kTotal, stream>>>(tq, tk, tv, p, a->err);
   if (splits > 1) {
     const long long rows = (long long)a->B * a->H * a->Sq;
     attn_combine_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(p);
@@ -724,25 +626,7 @@ int launch_attn_poly(const AttnArgs* a, const AttnParams& p, const CUtensorMap& 
   return (int)cudaGetLastError();
 }
 
-int g_attn_spec = 0;  // speculative running max in the softmax warps (measured 2.6 % slower at head dim 128)
-int g_attn_poly = 0;  // exponential pairs (of 8) on the FMA pipe (0 measured fastest at head dim 128)
-
-template <int QT>
-int launch_attn(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
-                const CUtensorMap& tv, cudaStream_t stream) {
-  switch (g_attn_poly) {
-    case 0: return launch_attn_poly<QT, 0>(a, p, tq, tk, tv, stream);
-    case 1: return launch_attn_poly<QT, 1>(a, p, tq, tk, tv, stream);
-    case 3: return launch_attn_poly<QT, 3>(a, p, tq, tk, tv, stream);
-    default: return launch_attn_poly<QT, 2>(a, p, tq, tk, tv, stream);
-  }
-}
-
 }  // namespace
-
-// Fraction (n / 8) of the softmax exponentials evaluated by the FMA-pipe polynomial.
-extern "C" void dfl_attention_set_poly(int n) { g_attn_poly = n < 0 ? 0 : (n > 3 ? 3 : n); }
-extern "C" void dfl_attention_set_spec(int on) { g_attn_spec = on ? 1 : 0; }
 
 // Key-range splits: modelled time = waves of CTAs x (one full-range CTA time / s) + the
 // split overhead (partial f32 rows written and read back by the combine, CTA start-up),
@@ -800,7 +684,6 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   p.acc_o = a->acc_o;
   p.acc_lse = a->acc_lse;
   p.merge_mode = a->merge_mode;
-  p.trace = a->trace;
   if (a->merge_mode != 0 && (!a->acc_o || !a->acc_lse || (reinterpret_cast<uintptr_t>(a->acc_o) & 15))) return -9;
   p.seg0_len = a->seg0_len;
   p.seg0_per = a->seg0_per > 0 ? a->seg0_per : 1;
@@ -816,7 +699,6 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   }
   p.kv_splits = a->kv_splits > 1 ? a->kv_splits : 1;
   p.split_o = a->split_o;
-  p.spec = g_attn_spec;
   p.split_lse = a->split_lse;
   if (p.kv_splits > 1) {
     if (a->merge_mode != 0 || !a->split_o || !a->split_lse || (reinterpret_cast<uintptr_t>(a->split_o) & 15))

@@ -452,6 +452,46 @@ void euler_step(at::Tensor x32, const c10::optional<at::Tensor>& x16, const at::
   DFL_CHECK_RC(dfl_euler_step(&a, cur_stream()), "euler_step");
 }
 
+// Guidance + sampler update (see kernels.h GuidedStepArgs).  b_ptr: the other branch's prediction
+// (0 = none) as a raw device pointer, so it may be a peer rank's buffer; coeffs = (k_v, e[5], g[6]).
+void guided_step(const at::Tensor& a, int64_t b_ptr, double scale, at::Tensor x, const c10::optional<at::Tensor>& x16,
+                 const c10::optional<at::Tensor>& last, const c10::optional<at::Tensor>& m1,
+                 const c10::optional<at::Tensor>& m2, const c10::optional<at::Tensor>& m_out,
+                 std::vector<double> coeffs, bool store_last, bool swap_ab) {
+  check_bf16_cuda(a, "a");
+  TORCH_CHECK(a.is_contiguous(), "a must be contiguous");
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous() && x.numel() == a.numel(), "x must be f32 like a");
+  TORCH_CHECK(coeffs.size() == 12, "coeffs: k_v, e[5] (x, last, m1, m2, m), g[6] (x, last, m1, m2, m, v)");
+  auto f32 = [&](const c10::optional<at::Tensor>& t, const char* name) -> float* {
+    if (!(t.has_value() && t->defined())) return nullptr;
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == x.numel(), name,
+                " must be f32 contiguous like x");
+    return t->data_ptr<float>();
+  };
+  const c10::cuda::CUDAGuard guard(x.device());
+  GuidedStepArgs g{};
+  g.a = a.data_ptr();
+  g.b = reinterpret_cast<const void*>(b_ptr);
+  g.scale = (float)scale;
+  g.x = x.data_ptr<float>();
+  if (x16.has_value() && x16->defined()) {
+    check_bf16_cuda(*x16, "x16");
+    TORCH_CHECK(x16->is_contiguous() && x16->numel() == x.numel(), "x16 must match x");
+    g.x16 = x16->data_ptr();
+  }
+  g.last = f32(last, "last");
+  g.m1 = f32(m1, "m1");
+  g.m2 = f32(m2, "m2");
+  g.m_out = f32(m_out, "m_out");
+  g.n = x.numel();
+  g.k_v = (float)coeffs[0];
+  for (int t = 0; t < 5; ++t) g.e[t] = (float)coeffs[1 + t];
+  for (int t = 0; t < 6; ++t) g.g[t] = (float)coeffs[6 + t];
+  g.store_last = store_last ? 1 : 0;
+  g.swap_ab = swap_ab ? 1 : 0;
+  DFL_CHECK_RC(dfl_guided_step(&g, cur_stream()), "guided_step");
+}
+
 at::Tensor timestep_embed(const at::Tensor& t, int64_t dim, double max_period, bool flip_sin_to_cos,
                           double downscale_freq_shift, double scale) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.dim() == 1 && t.is_contiguous(), "t must be f32 [B]");
@@ -470,7 +510,7 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
                      const c10::optional<at::Tensor>& kv_lo, const c10::optional<at::Tensor>& kv_hi,
                      std::vector<int64_t> o_peer, int64_t seg0_len, int64_t seg0_per, int64_t seg1_per, std::vector<int64_t> o_strides,
                      const c10::optional<at::Tensor>& acc_o, const c10::optional<at::Tensor>& acc_lse, int64_t merge_mode,
-                     const c10::optional<at::Tensor>& trace, int64_t kv_split) {
+                     int64_t kv_split) {
   check_bf16_cuda(q, "q");
   check_bf16_cuda(k, "k");
   check_bf16_cuda(v, "v");
@@ -504,11 +544,6 @@ at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   a.Sk = (int)k.size(2);
   a.dh = (int)q.size(3);
   a.scale = (float)scale;
-  if (trace.has_value() && trace->defined()) {
-    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_contiguous() && trace->numel() >= 16 * 64 * 8,
-                "trace must be int64 with at least 16 * 64 * 8 entries");
-    a.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
-  }
   if (lse.has_value() && lse->defined()) {
     TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->is_contiguous(), "lse must be f32 [B, H, Sq]");
     a.lse = lse->data_ptr<float>();
@@ -727,8 +762,6 @@ at::Tensor rel_l1(const at::Tensor& a, const at::Tensor& b) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "difflet_b200 native sm_100a kernels";
   m.def("gemm_set_pair_auto", [](bool on) { dfl_gemm_set_pair_auto(on ? 1 : 0); });
-  m.def("attention_set_poly", [](int64_t n) { dfl_attention_set_poly((int)n); });
-  m.def("attention_set_spec", [](int64_t on) { dfl_attention_set_spec((int)on); });
   m.def("gemm_set_epi_warps", [](int64_t n) { dfl_gemm_set_epi_warps((int)n); });
   m.def("gemm_set_split_workspace", [](const at::Tensor& ws, const at::Tensor& sem) {
     TORCH_CHECK(ws.is_cuda() && sem.is_cuda() && ws.device() == sem.device(), "workspace tensors on one device");
@@ -773,8 +806,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("kv_hi") = py::none(), py::arg("o_peer") = std::vector<int64_t>{},
         py::arg("seg0_len") = 0, py::arg("seg0_per") = 0, py::arg("seg1_per") = 0,
         py::arg("o_strides") = std::vector<int64_t>{}, py::arg("acc_o") = py::none(),
-        py::arg("acc_lse") = py::none(), py::arg("merge_mode") = 0, py::arg("trace") = py::none(),
-        py::arg("kv_split") = -1);
+        py::arg("acc_lse") = py::none(), py::arg("merge_mode") = 0, py::arg("kv_split") = -1);
   m.def("error_word", &error_word);
   m.def("symm_alloc", &symm_alloc);
   m.def("from_ptr", &from_ptr);
@@ -792,5 +824,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_put_f32", &peer_put_f32);
   m.def("cfg_combine", &cfg_combine);
+  m.def("guided_step", &guided_step, py::arg("a"), py::arg("b_ptr"), py::arg("scale"), py::arg("x"),
+        py::arg("x16") = py::none(), py::arg("last") = py::none(), py::arg("m1") = py::none(),
+        py::arg("m2") = py::none(), py::arg("m_out") = py::none(), py::arg("coeffs"), py::arg("store_last"),
+        py::arg("swap_ab") = false);
   m.def("rel_l1", &rel_l1);
 }

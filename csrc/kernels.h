@@ -174,6 +174,32 @@ typedef struct SchedArgs {
 } SchedArgs;
 int dfl_euler_step(const SchedArgs* a, cudaStream_t stream);
 
+// Guidance combine fused with a sampler update (sched.cu), u = (x, last, m1, m2, m):
+//   v = a + scale (b - a) (b NULL: v = a; swap_ab: v = b + scale (a - b)); m = x + k_v v;
+//   xc = e . u; xn = g[0..4] . u + g[5] v;
+//   x <- xn, x16 <- bf16(xn) (x16 != NULL), last <- xc (store_last), m_out <- m (m_out != NULL).
+// a / b bf16 (either may be a peer rank's buffer), x / last / m1 / m2 / m_out f32, all n elements,
+// 16-byte aligned; NULL last / m1 / m2 read as zero.  m_out may alias m2 (each element is read
+// before it is written).
+typedef struct GuidedStepArgs {
+  const void* a;
+  const void* b;
+  float scale;
+  float* x;
+  void* x16;
+  float* last;
+  const float* m1;
+  const float* m2;
+  float* m_out;
+  long long n;
+  float k_v;
+  float e[5];
+  float g[6];
+  int store_last;
+  int swap_ab;
+} GuidedStepArgs;
+int dfl_guided_step(const GuidedStepArgs* a, cudaStream_t stream);
+
 // Sinusoidal timestep features: out[b, :] = [cos(t f) | sin(t f)] (flip) or [sin | cos].
 int dfl_timestep_embed(const float* t, int batch, int dim, float max_period, int flip_sin_to_cos,
                        float downscale_freq_shift, float scale, float* out, cudaStream_t stream);
@@ -205,9 +231,6 @@ typedef struct AttnArgs {
   float* acc_o;
   float* acc_lse;
   int merge_mode;
-  // Optional diagnostics: clock64() at fixed points of every warp of CTA (0, 0, 0),
-  // trace[(warp * 64 + j) * 8 + event] for key tiles j < 64 (NULL = off).
-  long long* trace;
   // Split-KV (launches whose query blocks leave SMs idle): kv_splits CTAs share a query
   // block, each over a contiguous key range, writing its normalised partial and LSE to
   // split_o f32 [kv_splits][B*H*Sq][128] / split_lse [kv_splits][B*H*Sq]; a combine pass
@@ -219,9 +242,6 @@ typedef struct AttnArgs {
 int dfl_attention(const AttnArgs* a, cudaStream_t stream);
 // Key-range split count that minimises the modelled time of this launch (1 = none).
 int dfl_attention_plan_splits(const AttnArgs* a);
-// n of every 8 softmax exponential pairs on the FMA pipe (0..3; default 0).
-void dfl_attention_set_poly(int n);
-void dfl_attention_set_spec(int on);  // speculative running max (default 0)
 
 // ---------------------------------------------------------------------------
 // Peer-memory communication runtime (comm.cu)

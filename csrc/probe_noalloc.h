@@ -23,7 +23,18 @@
 //     the library holds that array until the process exits.
 //   * The first call on a device resolves the array's device address with
 //     cudaGetSymbolAddress while that device is current; make that first call
-//     before any stream capture on the device.
+//     before any stream capture on the device.  With lazy module loading (the
+//     CUDA default) that first call is also when the driver loads this
+//     library's device code on the device and reserves memory for it and for
+//     the static array (with CUDA_MODULE_LOADING=EAGER, when the library is
+//     loaded).  "Allocates nothing" therefore holds from the second call on:
+//     a caller that forbids allocation after start-up makes one call per
+//     device during its start-up.
+//   * The resolved address is cached per device index for the life of the
+//     process, which assumes one primary context per device.  After
+//     cudaDeviceReset (or anything else that destroys and re-creates the
+//     context) the cached address is stale: such a caller must not use this
+//     entry point again in the same process.
 //   * All calls share the one array and it keeps whatever the last call left
 //     there.  The entry point clears the part that must start at zero (the
 //     completion ticket) on `stream` before each launch.  Calls that overlap

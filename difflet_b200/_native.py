@@ -35,6 +35,7 @@ CUDA_SOURCES = [
     "conv.cu",
     "probe.cu",
     "probe_noalloc.cu",
+    "sched.cu",
 ]
 CPP_SOURCES = ["bindings.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "probe_noalloc.h", "gemm_epilogue.cuh"]
@@ -59,24 +60,13 @@ def _bounds_check() -> bool:
     return bool(envs.DIFFLET_BOUNDS_CHECK)
 
 
-def _attn_trace() -> bool:
-    import os
-
-    return os.environ.get("DIFFLET_ATTN_TRACE", "0") not in ("", "0")
-
-
-def _ext_name() -> str:
-    """The release module, the debug build with device index guards (DIFFLET_BOUNDS_CHECK=1), or
-    the attention-trace diagnostic build (DIFFLET_ATTN_TRACE=1: per-tile clock64 events)."""
-    if _bounds_check():
-        return EXT_NAME + "_bounds"
-    return EXT_NAME + ("_trace" if _attn_trace() else "")
+def _ext_name(bounds: bool | None = None) -> str:
+    """The release module, or the debug build with device index guards (DIFFLET_BOUNDS_CHECK=1)."""
+    return EXT_NAME + ("_bounds" if (_bounds_check() if bounds is None else bounds) else "")
 
 
-def _nvcc_flags() -> list:
-    if _bounds_check():
-        return NVCC_FLAGS + ["-DDFL_BOUNDS_CHECK"]
-    return NVCC_FLAGS + (["-DDFL_ATTN_TRACE"] if _attn_trace() else [])
+def _nvcc_flags(bounds: bool | None = None) -> list:
+    return NVCC_FLAGS + (["-DDFL_BOUNDS_CHECK"] if (_bounds_check() if bounds is None else bounds) else [])
 
 _lock = threading.Lock()
 _module = None
@@ -92,32 +82,39 @@ def _sources() -> list[Path]:
     return out
 
 
-def source_hash() -> str:
+def source_hash(bounds: bool | None = None) -> str:
     h = hashlib.sha256()
     for p in sorted(_sources() + [CSRC / n for n in HEADERS if (CSRC / n).exists()]):
         h.update(p.name.encode())
         h.update(p.read_bytes())
-    h.update(" ".join(_nvcc_flags() + CXX_FLAGS).encode())
+    h.update(" ".join(_nvcc_flags(bounds) + CXX_FLAGS).encode())
     return h.hexdigest()[:24]
 
 
-def _so_path() -> Path | None:
+def _so_path(bounds: bool | None = None) -> Path | None:
     for suffix in importlib.machinery.EXTENSION_SUFFIXES + [".so"]:
-        p = BUILD_DIR / f"{_ext_name()}{suffix}"
+        p = BUILD_DIR / f"{_ext_name(bounds)}{suffix}"
         if p.exists():
             return p
     return None
 
 
-def _stamp() -> Path:
-    return BUILD_DIR / f"{_ext_name()}.hash"
+def _stamp(bounds: bool | None = None) -> Path:
+    return BUILD_DIR / f"{_ext_name(bounds)}.hash"
+
+
+def _build_dir(bounds: bool) -> Path:
+    # each variant keeps its own object files (the flags differ); every .so lands in _build/
+    return BUILD_DIR if not bounds else BUILD_DIR / "bounds"
 
 
 def build(verbose: bool = False, force: bool = False):
-    """Compile every CUDA source for sm_100a and return the loaded module."""
+    """Compile every CUDA source for sm_100a (the variant the environment selects: release, or
+    the bounds-check build under DIFFLET_BOUNDS_CHECK=1) and return the loaded module."""
     global _module
     from torch.utils import cpp_extension
 
+    variant = _bounds_check()
     BUILD_DIR.mkdir(parents=True, exist_ok=True)
     want = source_hash()
     if not force and _so_path() is not None and _stamp().exists() and _stamp().read_text() == want:
@@ -125,19 +122,36 @@ def build(verbose: bool = False, force: bool = False):
     os.environ.setdefault("MAX_JOBS", str(min(8, os.cpu_count() or 4)))
     # torch's own arch list must not add other targets: the -gencode above is the only one.
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    bdir = _build_dir(variant)
+    bdir.mkdir(parents=True, exist_ok=True)
     mod = cpp_extension.load(
         name=_ext_name(),
         sources=[str(p) for p in _sources()],
         extra_cflags=CXX_FLAGS,
         extra_cuda_cflags=_nvcc_flags(),
         extra_include_paths=[str(CSRC)],
-        build_directory=str(BUILD_DIR),
+        build_directory=str(bdir),
         verbose=verbose,
         with_cuda=True,
     )
+    if bdir != BUILD_DIR:  # the loader looks for every variant's .so in _build/
+        import shutil
+
+        for f in bdir.glob(f"{_ext_name()}*.so"):
+            shutil.copy2(f, BUILD_DIR / f.name)
     _stamp().write_text(want)
     _module = mod
     return mod
+
+
+def build_bounds_variant(verbose: bool = False) -> None:
+    """Build the bounds-check variant (``_difflet_C_bounds``) in a child process, so this process
+    keeps the release module it may already have loaded."""
+    import subprocess
+
+    env = dict(os.environ, DIFFLET_BOUNDS_CHECK="1")
+    code = f"from difflet_b200 import _native; _native.build(verbose={bool(verbose)})"
+    subprocess.run([sys.executable, "-c", code], env=env, cwd=str(_REPO), check=True)
 
 
 def load():

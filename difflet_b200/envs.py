@@ -76,10 +76,6 @@ environment_variables: dict[str, Callable[[], Any]] = {
     "DIFFLET_GEMM_EPI_WARPS": lambda: _int(os.environ.get("DIFFLET_GEMM_EPI_WARPS"), 0),
     # "auto": attention launches whose query blocks leave SMs idle split the key range; "0": never
     "DIFFLET_ATTN_SPLIT": lambda: _str(os.environ.get("DIFFLET_ATTN_SPLIT"), "auto"),
-    # 1: attention softmax computes a tile's exponentials on the running max while that tile's max is found
-    "DIFFLET_ATTN_SPEC": lambda: _int(os.environ.get("DIFFLET_ATTN_SPEC"), 0),
-    # softmax exponential pairs (of every 8) evaluated by the FMA-pipe polynomial in attention (0..3)
-    "DIFFLET_ATTN_POLY": lambda: _int(os.environ.get("DIFFLET_ATTN_POLY"), 0),
     # serving
     "DIFFLET_API_KEY": lambda: _str(os.environ.get("DIFFLET_API_KEY"), None),
     "DIFFLET_SERVE_QUEUE_TIMEOUT_S": lambda: _float(os.environ.get("DIFFLET_SERVE_QUEUE_TIMEOUT_S"), 30.0),

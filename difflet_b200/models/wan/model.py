@@ -239,9 +239,11 @@ class WanTransformer:
         return temb, mods
 
     # ------------------------------------------------------------------ forward
-    def forward(self, x_tokens, timestep, context, *, grid, mods=None, temb=None):
+    def forward(self, x_tokens, timestep, context, *, grid, mods=None, temb=None, out=None):
         """x_tokens [B, S(local), C*pt*ph*pw]; timestep [B] in [0, 1000]; context = the
-        cached per-block (k, v) from ``prepare_context``; grid = (t, h, w) token grid."""
+        cached per-block (k, v) from ``prepare_context``; grid = (t, h, w) token grid.
+        ``out`` (optional, [B, S(local), out_dim] bf16): where the final projection stores the
+        prediction (a CFG-parallel exchange buffer)."""
         cfg, w, par, tp = self.cfg, self.w, self.par, self.tp
         if tp is not None and par is not None:
             raise NotImplementedError("Wan tensor parallelism composes with cfg-parallel here, not with cp")
@@ -295,7 +297,7 @@ class WanTransformer:
             temb, _ = self.time_embed(timestep)
         fm = (w["out.sst"][None] + temb[:, None].to(w["out.sst"].dtype)).contiguous()  # [B, 2, D]: shift, scale
         F.ln_modulate(x, shift=fm[:, 0], scale=fm[:, 1], eps=eps, rows_per_batch=S_loc, out=norm)
-        out = F.linear(norm, w["final.w"], w["final.b"])
+        out = F.linear(norm, w["final.w"], w["final.b"], out=None if out is None else out.view(B * S_loc, -1))
         return out.view(B, S_loc, -1)
 
     __call__ = forward

@@ -58,8 +58,6 @@ def _lib():
 
         _nat = _native.require()
         _nat.gemm_set_pair_auto(envs.DIFFLET_GEMM_PAIR != "0")
-        _nat.attention_set_poly(envs.DIFFLET_ATTN_POLY)
-        _nat.attention_set_spec(envs.DIFFLET_ATTN_SPEC)
         _nat.gemm_set_epi_warps(envs.DIFFLET_GEMM_EPI_WARPS)
     _split_workspace(_nat)
     return _nat
@@ -683,6 +681,40 @@ def euler_step(x32, v, dt, *, x16=None, cond=None, guidance=1.0):
     if x16 is not None:
         x16.copy_(x32.to(x16.dtype))
     return x32
+
+
+def guided_step(a, b=None, *, scale=1.0, x, x16=None, last=None, m1=None, m2=None, m_out=None, k_v=0.0,
+                e=(1.0, 0.0, 0.0, 0.0, 0.0), g=(1.0, 0.0, 0.0, 0.0, 0.0, 0.0), store_last=False, b_ptr=None,
+                swap=False):
+    """Guidance combine + sampler update in one pass (``csrc/sched.cu``): v = a + scale (b - a)
+    (v = a without b; ``swap``: b is the uncond branch, v = b + scale (a - b)), m = x + k_v v, xc = e . (x, last, m1, m2, m), xn = g . (x, last, m1, m2, m, v);
+    x <- xn (f32, in place), x16 <- bf16(xn), last <- xc (``store_last``), m_out <- m.
+    On CUDA, ``b_ptr`` (a raw device pointer, e.g. the CFG partner's buffer) replaces ``b``."""
+    coeffs = [float(k_v)] + [float(c) for c in e] + [float(c) for c in g]
+    if x.is_cuda:
+        ptr = int(b_ptr) if b_ptr is not None else (b.data_ptr() if b is not None else 0)
+        native().guided_step(a, ptr, float(scale), x, x16, last, m1, m2, m_out, coeffs, bool(store_last),
+                             bool(swap))
+        return x
+    ct = x.dtype
+    if b is None:
+        v = a.to(ct)
+    else:
+        u_, c_ = (b, a) if swap else (a, b)
+        v = u_.to(ct) + scale * (c_.to(ct) - u_.to(ct))
+    m = x + coeffs[0] * v
+    z = torch.zeros_like(x)
+    u = [x, last if last is not None else z, m1 if m1 is not None else z, m2 if m2 is not None else z, m]
+    xc = sum(c * t for c, t in zip(coeffs[1:6], u))
+    xn = sum(c * t for c, t in zip(coeffs[6:11], u)) + coeffs[11] * v
+    if store_last:
+        last.copy_(xc)
+    if m_out is not None:
+        m_out.copy_(m)
+    x.copy_(xn)
+    if x16 is not None:
+        x16.copy_(xn.to(x16.dtype))
+    return x
 
 
 def timestep_embed(t, dim, *, max_period=10000.0, flip_sin_to_cos=True, downscale_freq_shift=0.0,

@@ -34,54 +34,71 @@ class MeshSpec:
     tp: int = 1
 
     def __post_init__(self) -> None:
-        for axis in AXES:
-            v = getattr(self, axis)
-            if not isinstance(v, int) or isinstance(v, bool) or v < 1:
-                raise ValueError(f"{axis} must be an int >= 1, got {v!r}")
+        bad = [(a, getattr(self, a)) for a in AXES
+               if isinstance(getattr(self, a), bool) or not isinstance(getattr(self, a), int) or getattr(self, a) < 1]
+        if bad:
+            axis, v = bad[0]
+            raise ValueError(f"mesh axis {axis} needs a positive integer degree (got {v!r})")
+
+    # Mixed-radix view: digits in AXES order (dp most significant, tp least).
+    def _sizes(self) -> tuple[int, ...]:
+        return tuple(getattr(self, a) for a in AXES)
+
+    def _check_axis(self, axis: str) -> int:
+        try:
+            return AXES.index(axis)
+        except ValueError:
+            raise ValueError(f"{axis!r} is not a mesh axis (axes: {', '.join(AXES)})") from None
 
     @property
     def world_size(self) -> int:
-        return self.dp * self.cfg * self.cp * self.tp
+        n = 1
+        for size in self._sizes():
+            n *= size
+        return n
 
     def axis_size(self, axis: str) -> int:
-        if axis not in AXES:
-            raise ValueError(f"unknown axis {axis!r}; expected one of {AXES}")
-        return getattr(self, axis)
+        return self._sizes()[self._check_axis(axis)]
 
     def axis_stride(self, axis: str) -> int:
-        self.axis_size(axis)
-        return {"tp": 1, "cp": self.tp, "cfg": self.tp * self.cp, "dp": self.tp * self.cp * self.cfg}[axis]
+        """Rank distance between neighbours along ``axis``: the product of the faster axes."""
+        stride = 1
+        for size in self._sizes()[self._check_axis(axis) + 1:]:
+            stride *= size
+        return stride
 
     def coords_of(self, rank: int) -> MeshCoords:
-        if not 0 <= rank < self.world_size:
-            raise ValueError(f"rank {rank} out of range [0, {self.world_size})")
-        return MeshCoords(
-            dp=rank // (self.tp * self.cp * self.cfg),
-            cfg=(rank // (self.tp * self.cp)) % self.cfg,
-            cp=(rank // self.tp) % self.cp,
-            tp=rank % self.tp,
-        )
+        if rank < 0 or rank >= self.world_size:
+            raise ValueError(f"rank {rank} is outside a mesh of {self.world_size} ranks")
+        digits = []
+        rest = rank
+        for size in reversed(self._sizes()):  # least significant digit (tp) first
+            rest, d = divmod(rest, size)
+            digits.append(d)
+        return MeshCoords(*reversed(digits))
 
     def rank_of(self, *, dp: int = 0, cfg: int = 0, cp: int = 0, tp: int = 0) -> int:
-        for axis, c in (("dp", dp), ("cfg", cfg), ("cp", cp), ("tp", tp)):
-            if not 0 <= c < self.axis_size(axis):
-                raise ValueError(f"{axis} coordinate {c} out of range [0, {self.axis_size(axis)})")
-        return tp + self.tp * (cp + self.cp * (cfg + self.cfg * dp))
+        coords = (dp, cfg, cp, tp)
+        rank = 0
+        for axis, c, size in zip(AXES, coords, self._sizes()):
+            if c < 0 or c >= size:
+                raise ValueError(f"coordinate {c} does not exist on mesh axis {axis} of degree {size}")
+            rank = rank * size + c
+        return rank
 
     def axis_rank(self, rank: int, axis: str) -> int:
-        self.axis_size(axis)
-        return getattr(self.coords_of(rank), axis)
+        return self.coords_of(rank)[self._check_axis(axis)]
 
     def axis_groups(self, axis: str) -> list[list[int]]:
-        size, stride = self.axis_size(axis), self.axis_stride(axis)
-        return [
-            [base + i * stride for i in range(size)]
-            for base in range(self.world_size)
-            if (base // stride) % size == 0
-        ]
+        """Every group of ranks that share all coordinates except ``axis``, each in axis order."""
+        i = self._check_axis(axis)
+        groups: dict[tuple, list[int]] = {}
+        for r in range(self.world_size):
+            c = self.coords_of(r)
+            groups.setdefault(c[:i] + c[i + 1:], []).append(r)
+        return list(groups.values())
 
     def group_of(self, rank: int, axis: str) -> list[int]:
-        for g in self.axis_groups(axis):
-            if rank in g:
-                return g
-        raise ValueError(rank)
+        c = self.coords_of(rank)
+        i = self._check_axis(axis)
+        return [self.rank_of(**dict(zip(AXES, c[:i] + (j,) + c[i + 1:]))) for j in range(self.axis_size(axis))]

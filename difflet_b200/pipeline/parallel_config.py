@@ -27,15 +27,15 @@ class DiffletParallelConfig:
     dp_degree: int = 1
 
     def __post_init__(self) -> None:
-        for name in ("tp_degree", "cp_degree", "dp_degree"):
-            if getattr(self, name) < 1:
-                raise ValueError(f"{name} must be >= 1")
+        low = [n for n in ("tp_degree", "cp_degree", "dp_degree") if getattr(self, n) < 1]
+        if low:
+            raise ValueError(f"{low[0]} is {getattr(self, low[0])}; every parallel degree is at least 1")
         if self.cp_mode not in CP_MODES:
-            raise ValueError(f"cp_mode must be one of {set(CP_MODES)}, got {self.cp_mode!r}")
+            raise ValueError(f"unknown cp_mode {self.cp_mode!r} (known: {', '.join(sorted(CP_MODES))})")
         if self.cp_mode != "gather_kv" and self.cp_degree <= 1:
-            raise ValueError(f"cp_mode={self.cp_mode!r} requires cp_degree > 1")
+            raise ValueError(f"cp_mode {self.cp_mode!r} only applies with a context-parallel degree above 1")
         if self.sp_enabled and self.cp_degree > 1:
-            raise ValueError("sp_enabled and cp_degree > 1 are mutually exclusive")
+            raise ValueError("Megatron sequence parallelism (sp) and context parallelism (cp > 1) cannot be combined")
         if self.sp_enabled and self.tp_degree <= 1:
             raise ValueError("sp_enabled shards over the tensor-parallel group: needs tp_degree > 1")
 
@@ -83,14 +83,12 @@ class CandidateConfig:
 
     def __post_init__(self) -> None:
         if self.max_candidates < 1:
-            raise ValueError("max_candidates must be >= 1")
+            raise ValueError(f"max_candidates is {self.max_candidates}; at least one candidate is needed")
         if self.active_candidates is None:
             object.__setattr__(self, "active_candidates", self.max_candidates)
         if not 1 <= self.active_candidates <= self.max_candidates:
-            raise ValueError(
-                f"active_candidates must satisfy 1 <= active <= max_candidates ({self.max_candidates}), "
-                f"got {self.active_candidates}"
-            )
+            raise ValueError(f"{self.active_candidates} active candidates do not fit the range 1.."
+                             f"{self.max_candidates} set by max_candidates")
 
     @property
     def is_trivial(self) -> bool:

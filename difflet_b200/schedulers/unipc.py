@@ -82,9 +82,36 @@ class UniPCScheduler:
     def step(self, model_output: torch.Tensor, sample: torch.Tensor) -> torch.Tensor:
         """model_output: predicted velocity (any float dtype); sample: fp32 latents.
         Returns the next fp32 sample."""
+        m_t = self._x0(model_output, sample, float(self.sigmas[self.step_index]))
+        return self._advance(m_t, sample)
+
+    def fused_coeffs(self):
+        """This step's update as weights over the sampler state u = (x, last, m1, m2, m) (x the
+        current sample, last the previous corrected sample, m1 / m2 the previous two data
+        predictions, m = x - sigma v this step's), for the fused guidance + sampler kernel.
+
+        The corrector and predictor are linear in u, so the weights are what ``_advance`` returns
+        when it runs on the basis vectors of u instead of tensors: the same code, the same
+        bookkeeping (order warm-up, lower-order final steps).  Returns (k_v, e, g): m = x + k_v v,
+        corrected sample xc = e . u, next sample xn = g . u (+ g[5] v, zero here)."""
+        bx, blast, bm1, bm2, bm = np.eye(5)
         i = self.step_index
-        sig = self.sigmas
-        m_t = self._x0(model_output, sample, float(sig[i]))
+        have = [o is not None for o in self.model_outputs]
+        # where step() would hold tensors, hold the matching basis vectors (history newest last)
+        basis_hist = [bm2, bm1][-len(have):] if len(have) <= 2 else [None] * (len(have) - 2) + [bm2, bm1]
+        self.model_outputs = [b if h else None for b, h in zip(basis_hist, have)]
+        had_last = self.last_sample is not None
+        self.last_sample = blast if had_last else None
+        xn = self._advance(bm, bx)
+        xc = self.last_sample
+        # back to presence markers: the tensors themselves live in the caller's device buffers
+        self.model_outputs = [True if o is not None else None for o in self.model_outputs]
+        self.last_sample = True
+        return -float(self.sigmas[i]), [float(c) for c in xc], [float(c) for c in xn] + [0.0]
+
+    def _advance(self, m_t, sample):
+        """Corrector on ``sample`` with the new data prediction ``m_t``, history shift, predictor."""
+        i = self.step_index
         use_corr = i > 0 and (i - 1) not in self.disable_corrector and self.last_sample is not None
         if use_corr:
             sample = self._corrector(m_t, sample)

@@ -27,86 +27,101 @@ TIMING_ENV = "DIFFLET_BENCH_TIMING_DIR"
 STEP_TIMES_ENV = "DIFFLET_STEP_TIMES_FILE"
 DUMP_ENV = "DIFFLET_DUMP_LATENTS_DIR"
 
-_handle = None
-_handle_pid = None
-_failed = False
 _step_index = 0
 
 
 def enabled() -> bool:
-    return bool(os.environ.get(TIMING_ENV))
+    """True when a timing directory is configured (read on every call: tests flip it)."""
+    return os.environ.get(TIMING_ENV, "") != ""
 
 
-def _rank_world() -> tuple[int, int]:
-    dist = sys.modules.get("torch.distributed")
+def _identity() -> tuple[int, int]:
+    """(rank, world) of this process.  An initialised process group is authoritative; it is
+    only consulted when ``torch.distributed`` was imported already (importing torch here would
+    cost seconds inside whatever the caller is timing).  Otherwise torchrun's environment."""
+    env_rank, env_world = os.environ.get("RANK", "0"), os.environ.get("WORLD_SIZE", "1")
+    mod = sys.modules.get("torch.distributed")
+    if mod is not None:
+        try:
+            if mod.is_initialized():
+                return mod.get_rank(), mod.get_world_size()
+        except (RuntimeError, ValueError, AttributeError):
+            pass  # group being torn down: fall back to the environment
     try:
-        if dist is not None and dist.is_available() and dist.is_initialized():
-            return dist.get_rank(), dist.get_world_size()
-    except Exception:  # noqa: BLE001 - a half-initialised process group
-        pass
-    try:
-        return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+        return int(env_rank), int(env_world)
     except ValueError:
         return 0, 1
 
 
-def _jsonable(v: Any) -> Any:
-    if v is None or isinstance(v, (bool, int, float, str)):
-        return v
+def _plain(v: Any) -> Any:
+    """JSON-safe copy of ``v``: containers recursed, unknown objects as their ``str``."""
     if isinstance(v, dict):
-        return {str(k): _jsonable(x) for k, x in v.items()}
+        return {str(k): _plain(x) for k, x in v.items()}
     if isinstance(v, (list, tuple, set)):
-        return [_jsonable(x) for x in v]
-    return str(v)
+        return [_plain(x) for x in v]
+    return v if v is None or isinstance(v, (bool, int, float, str)) else str(v)
 
 
-def _write(kind: str, fields: dict) -> None:
-    rank, world = _rank_world()
-    rec = {"event": kind, "t_ns": time.monotonic_ns(), "pid": os.getpid(), "rank": rank, "world": world}
-    rec.update(_jsonable(fields))
-    _handle.write(json.dumps(rec, ensure_ascii=False) + "\n")
+class _Sink:
+    """One append-only JSONL file per process.  It is opened lazily and re-opened in a forked
+    child (the pid is part of the name); the first record of a file describes the process.
+    The first failure switches the sink off for the rest of the process."""
+
+    def __init__(self) -> None:
+        self.fh = None
+        self.pid = -1
+        self.dead = False
+
+    def _filename(self) -> str:
+        launched = "LOCAL_RANK" in os.environ
+        tag = ("rank" + os.environ.get("RANK", "0")) if launched else "proc"
+        return os.path.join(os.environ[TIMING_ENV], f"{tag}-{os.getpid()}.jsonl")
+
+    def _record(self, kind: str, fields: dict) -> str:
+        rank, world = _identity()
+        body = {"event": kind, "t_ns": time.monotonic_ns(), "pid": os.getpid(), "rank": rank, "world": world}
+        body.update(_plain(fields))
+        return json.dumps(body, ensure_ascii=False)
+
+    def write(self, kind: str, fields: dict) -> None:
+        if self.dead:
+            return
+        try:
+            if self.fh is None or self.pid != os.getpid():
+                os.makedirs(os.environ[TIMING_ENV], exist_ok=True)
+                self.fh = open(self._filename(), "a", encoding="utf-8", buffering=1)
+                self.pid = os.getpid()
+                role = "rank" if "LOCAL_RANK" in os.environ else "proc"
+                self.fh.write(self._record("process", {"argv": list(sys.argv), "role": role}) + "\n")
+            self.fh.write(self._record(kind, fields) + "\n")
+        except OSError as exc:
+            self.dead = True
+            print(f"[telemetry] timing events disabled after an error: {exc!r}", file=sys.stderr, flush=True)
 
 
-def _open():
-    global _handle, _handle_pid
-    pid = os.getpid()
-    if _handle is not None and _handle_pid == pid:
-        return
-    d = os.environ[TIMING_ENV]
-    os.makedirs(d, exist_ok=True)
-    role = "rank" if "LOCAL_RANK" in os.environ else "proc"
-    name = f"{role}{os.environ.get('RANK', '0') if role == 'rank' else ''}-{pid}.jsonl"
-    _handle = open(os.path.join(d, name), "a", encoding="utf-8", buffering=1)
-    _handle_pid = pid
-    _write("process", {"argv": list(sys.argv), "role": role})
+_SINK = _Sink()
 
 
 def event(kind: str, /, **fields: Any) -> None:
     """Append one event (no-op unless ``DIFFLET_BENCH_TIMING_DIR`` is set)."""
-    global _failed
-    if _failed or not enabled():
-        return
-    try:
-        _open()
-        _write(kind, fields)
-    except Exception as exc:  # noqa: BLE001 - telemetry never fails a run
-        _failed = True
-        print(f"[telemetry] timing events disabled after an error: {exc!r}", file=sys.stderr, flush=True)
+    if enabled():
+        _SINK.write(kind, fields)
 
 
-@contextlib.contextmanager
-def span(name: str, **fields: Any) -> Iterator[None]:
-    """``span`` begin / end events around a block (the end is written on error too)."""
-    if not enabled():
-        yield
-        return
-    event("span", name=name, phase="begin", **fields)
-    ok = False
-    try:
-        yield
-        ok = True
-    finally:
-        event("span", name=name, phase="end", ok=ok, **fields)
+class span(contextlib.AbstractContextManager):  # noqa: N801 - used like a function
+    """``span`` begin / end events around a block; the end event carries ``ok`` (False when
+    the block raised) and is written on error too."""
+
+    def __init__(self, name: str, **fields: Any) -> None:
+        self.name, self.fields = name, fields
+
+    def __enter__(self):
+        event("span", name=self.name, phase="begin", **self.fields)
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        event("span", name=self.name, phase="end", ok=exc_type is None, **self.fields)
+        return False
 
 
 @contextlib.contextmanager

@@ -8,6 +8,12 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+# bf16 outputs of fp32-accumulated contractions: half a bf16 ulp is 2^-9 of the value, so a max-abs
+# error of 5e-3 x max|ref| leaves 2.5x headroom over rounding; attention (P rounded to bf16 before PV)
+# and the fused norm kernels keep the wider default.
+GEMM_TOL = 5e-3
+
+
 def _close(out, ref, tol=2e-2):
     out = out.float()
     ref = ref.float()
@@ -25,7 +31,7 @@ def test_gemm_plain_bias(native, M, N, K):
     out = native.gemm(a, b, bias)
     ref = a.float() @ b.float().t() + bias.float()
     torch.cuda.synchronize()
-    _close(out, ref)
+    _close(out, ref, tol=GEMM_TOL)
     out32 = native.gemm(a, b, None, out_f32=True)
     _close(out32, a.float() @ b.float().t(), tol=1e-3)
 
@@ -42,7 +48,7 @@ def test_gemm_gelu_window_and_strided_out(native):
     ref = a.float() @ b.float().t() + bias.float()
     ref[:, 512:1024] = torch.nn.functional.gelu(ref[:, 512:1024], approximate="tanh")
     torch.cuda.synchronize()
-    _close(view, ref)
+    _close(view, ref, tol=GEMM_TOL)
     assert big[:, :128].abs().max().item() == 0 and big[:, 128 + N :].abs().max().item() == 0
 
 
@@ -58,7 +64,7 @@ def test_gemm_gate_residual(native):
     ref = resid.float() + gate.repeat_interleave(S, 0) * (a.float() @ w.float().t() + bias.float())
     native.gemm(a, w, bias, out=resid, epi=2, gate=gate, rows_per_batch=S, resid=resid)
     torch.cuda.synchronize()
-    _close(resid, ref)
+    _close(resid, ref, tol=GEMM_TOL)
 
 
 @pytest.mark.parametrize("D", [256, 3072, 5120])
@@ -306,18 +312,11 @@ def test_attention_running_max_jumps(native):
     q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
     scale = 1.0
     ref, ref_lse = _attn_ref(q, k, v, scale)
-    try:
-        for spec in (0, 1):  # exact running max, then the speculative one
-            native.attention_set_spec(spec)
-            lse = torch.empty(B, H, Sq, device="cuda")
-            o = native.attention(q, k, v, scale, lse=lse)
-            torch.cuda.synchronize()
-            _close(o, ref)
-            assert (lse - ref_lse).abs().max().item() < 5e-2
-    finally:
-        from difflet_b200 import envs
-
-        native.attention_set_spec(envs.DIFFLET_ATTN_SPEC)
+    lse = torch.empty(B, H, Sq, device="cuda")
+    o = native.attention(q, k, v, scale, lse=lse)
+    torch.cuda.synchronize()
+    _close(o, ref)
+    assert (lse - ref_lse).abs().max().item() < 5e-2
     assert native.error_word(torch.cuda.current_device()).cpu().tolist() == [0, 0, 0, 0]
 
 
@@ -373,7 +372,7 @@ def test_conv_cl_matches_torch(native, N, T, H, W, Ci, Co, k, causal):
     ref = F.conv_cl(x.cpu().float(), w2.cpu().float(), b.cpu().float(), kt=k[0], kh=k[1], kw=k[2], causal=causal,
                     resid=resid.cpu().float())
     torch.cuda.synchronize()
-    _close(y.cpu(), ref)
+    _close(y.cpu(), ref, tol=GEMM_TOL)
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 256, 64), (1000, 1280, 512), (4608, 3072, 3072), (300, 2304, 128)])
@@ -386,7 +385,7 @@ def test_gemm_cta_pair(native, M, N, K):
     ref = a.float() @ b.float().t() + bias.float()
     out = native.gemm(a, b, bias, cta_mode=2)
     torch.cuda.synchronize()
-    _close(out, ref)
+    _close(out, ref, tol=GEMM_TOL)
     g = native.gemm(a, b, bias, epi=1, act_lo=128, act_hi=N, cta_mode=2)
     ref_g = ref.clone()
     ref_g[:, 128:] = torch.nn.functional.gelu(ref_g[:, 128:], approximate="tanh")
@@ -397,8 +396,8 @@ def test_gemm_cta_pair(native, M, N, K):
     rows = torch.arange(M, device="cuda") // ((M + 1) // 2)
     ref_r = resid.float() + gate[rows] * ref
     torch.cuda.synchronize()
-    _close(g, ref_g)
-    _close(r, ref_r)
+    _close(g, ref_g, tol=GEMM_TOL)
+    _close(r, ref_r, tol=GEMM_TOL)
     assert native.error_word(0)[0].item() == 0
 
 
@@ -444,16 +443,16 @@ def test_gemm_split_k_small_m(native, monkeypatch, M, N, K):
     bias = torch.randn(N, device="cuda", dtype=torch.bfloat16)
     ref = a.float() @ b.float().t() + bias.float()
     for _ in range(3):
-        _close(F.linear(a, b, bias), ref)
+        _close(F.linear(a, b, bias), ref, tol=GEMM_TOL)
     gate = torch.randn(1, N, device="cuda")
     resid = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
     out = resid.clone()
     F.linear(a, b, bias, out=out, gate=gate, resid=out, rows_per_batch=M)
-    _close(out, resid.float() + gate * ref)
+    _close(out, resid.float() + gate * ref, tol=GEMM_TOL)
     a2 = torch.randn(M // 2 + 8, K, device="cuda", dtype=torch.bfloat16)
     o1, o2 = F.linear_group([dict(x=a, w=b, b=bias), dict(x=a2, w=b, b=bias)])
-    _close(o1, ref)
-    _close(o2, a2.float() @ b.float().t() + bias.float())
+    _close(o1, ref, tol=GEMM_TOL)
+    _close(o2, a2.float() @ b.float().t() + bias.float(), tol=GEMM_TOL)
     monkeypatch.setenv("DIFFLET_GEMM_SPLITK", "0")  # registered already: the switch only affects new devices
     torch.cuda.synchronize()
     from difflet_b200 import _native
@@ -479,3 +478,48 @@ def test_attention_split_kv(native, split):
     torch.cuda.synchronize()
     _close(o, ref)
     assert (lse - ref_lse).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("n,swap", [(1 << 20, False), (12345, True), (7, False)])
+def test_guided_step_unipc_matches_oracle(native, n, swap):
+    """The fused CFG combine + UniPC step (csrc/sched.cu) over several steps against the same
+    update run by the CPU oracle in fp32; ``swap`` feeds the cond branch as ``a``."""
+    from difflet_b200.schedulers.guided import GuidedSampler
+    from difflet_b200.schedulers.unipc import UniPCScheduler
+
+    torch.manual_seed(n)
+    x0 = torch.randn(n)
+    gpu = GuidedSampler(UniPCScheduler(shift=5.0).set_timesteps(6), x0.cuda().clone(),
+                        torch.empty(n, device="cuda", dtype=torch.bfloat16))
+    cpu = GuidedSampler(UniPCScheduler(shift=5.0).set_timesteps(6), x0.clone())
+    for _ in range(6):
+        u = torch.randn(n).bfloat16()
+        c = torch.randn(n).bfloat16()
+        if swap:
+            gpu.step(c.cuda(), u.cuda(), 5.0, swap=True)
+        else:
+            gpu.step(u.cuda(), c.cuda(), 5.0)
+        cpu.step(u, c, 5.0)
+    torch.cuda.synchronize()
+    ref = cpu.x
+    assert (gpu.x.cpu() - ref).abs().max().item() <= 1e-4 * ref.abs().max().item()
+    assert torch.equal(gpu.x16.cpu(), gpu.x.cpu().bfloat16())
+    assert native.error_word(torch.cuda.current_device()).cpu().tolist() == [0, 0, 0, 0]
+
+
+def test_guided_step_euler(native):
+    from difflet_b200.schedulers import FlowMatchEulerScheduler
+    from difflet_b200.schedulers.guided import GuidedSampler
+
+    n = 4096 + 3
+    sched = FlowMatchEulerScheduler(use_dynamic_shifting=False, shift=3.0).set_timesteps(4)
+    x = torch.randn(n, device="cuda")
+    ref = x.clone()
+    s = GuidedSampler(sched, x)
+    for i in range(4):
+        u = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+        c = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+        s.step(u, c, 4.0)
+        ref = ref + sched.dt(i) * (u.float() + 4.0 * (c.float() - u.float()))
+    torch.cuda.synchronize()
+    assert (x - ref).abs().max().item() <= 1e-5 * ref.abs().max().item()

@@ -40,9 +40,8 @@ def test_event_writer_never_fails(tmp_path, monkeypatch):
     blocker = tmp_path / "file"
     blocker.write_text("x")
     monkeypatch.setenv("DIFFLET_BENCH_TIMING_DIR", str(blocker / "sub"))  # cannot be created
-    monkeypatch.setattr(telemetry, "_failed", False)
-    monkeypatch.setattr(telemetry, "_handle", None)
+    monkeypatch.setattr(telemetry, "_SINK", telemetry._Sink())
     telemetry.event("args", a=1)  # swallowed, then disabled
-    assert telemetry._failed
+    assert telemetry._SINK.dead
     with telemetry.span("x"):
         pass
