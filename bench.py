@@ -124,6 +124,13 @@ def _profile_step(path: str, rank: int, world: int, fwd) -> None:
     _log(f"profiled one eager step of rank 0 into {path}")
 
 
+def _flux_layout_name(par, args) -> str:
+    if par.cp_degree == 1:
+        return f"tp{par.tp_degree}" + ("+sp" if args.sp else "")
+    name = f"{par.cp_mode}{par.cp_degree}"
+    return name if par.tp_degree == 1 else f"tp{par.tp_degree}x{name}"
+
+
 def wan_layout(world: int, spec: str | None):
     """DiffletParallelConfig of a Wan layout: cfg2 / ulysses<N> / tp<N> factors joined by 'x'."""
     from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
@@ -293,6 +300,9 @@ def main(argv=None):
     ap.add_argument("--cp-mode", default="ulysses", choices=["ulysses", "ring", "gather_kv", "tp"],
                     help="how N>1 GPUs split the step: a context-parallel mode, or tensor parallelism")
     ap.add_argument("--sp", action="store_true", help="with --cp-mode tp: Megatron sequence parallelism")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="with a context-parallel --cp-mode: tensor-parallel degree inside each cp group "
+                         "(heads / MLP columns over tp, the sequence over the remaining N / tp ranks)")
     ap.add_argument("--quant", default=None, choices=[None, "mxfp8"],
                     help="MXFP8 block linears (default targets); the headline number is bf16")
     ap.add_argument("--model", default="flux", choices=["flux", "wan"],
@@ -328,6 +338,10 @@ def main(argv=None):
         par = DiffletParallelConfig()
     elif args.cp_mode == "tp":
         par = DiffletParallelConfig(tp_degree=world, sp_enabled=args.sp)
+    elif args.tp > 1 and args.tp < world:
+        if world % args.tp:
+            raise SystemExit(f"--tp {args.tp} does not divide {world} GPUs")
+        par = DiffletParallelConfig(tp_degree=args.tp, cp_degree=world // args.tp, cp_mode=args.cp_mode)
     else:
         par = DiffletParallelConfig(cp_degree=world, cp_mode=args.cp_mode)
     t_load = time.time()
@@ -344,12 +358,12 @@ def main(argv=None):
     B = 1
     h_tok, w_tok = args.height // 16, args.width // 16
     S_img, S_txt = h_tok * w_tok, 512
-    tp_mode = world > 1 and args.cp_mode == "tp"
-    shards = 1 if tp_mode else world  # TP replicates the tokens; CP shards them
+    shards = par.cp_degree  # TP replicates the tokens; CP shards them
+    cp_rank = (rank // par.tp_degree) % par.cp_degree
     S_img_l, S_txt_l = S_img // shards, S_txt // shards
 
     # ---------------- DiT step (device-timed) ----------------
-    g = torch.Generator(device=dev).manual_seed(1234 + (0 if tp_mode else rank))
+    g = torch.Generator(device=dev).manual_seed(1234 + cp_rank)
     x32 = torch.randn(B, S_img_l, cfg.in_channels, device=dev, generator=g)
     x16 = x32.to(torch.bfloat16)
     txt = torch.randn(B, S_txt_l, cfg.text_dim, device=dev, generator=g).to(torch.bfloat16)
@@ -444,7 +458,7 @@ def main(argv=None):
             "data": "synthetic (random-init FLUX.1-dev weights, N(0,1) text states / pooled / latents)",
             "config": {"model": "FLUX.1-dev", "global_batch": B, "seq_len": S_img + S_txt,
                        "height": args.height, "width": args.width,
-                       "parallelism": (f"{args.cp_mode}{world}" + ("+sp" if args.sp else "")) if world > 1 else "single",
+                       "parallelism": _flux_layout_name(par, args) if world > 1 else "single",
                        "l2": "weights (24 GB) stream from HBM every step, larger than L2; no flush",
                        "cuda_graph": not args.no_graph, "load_s": round(load_s, 1)},
             "clocks": clocks,

@@ -660,16 +660,18 @@ void tp_reduce(const at::Tensor& slots, int64_t slot_rows, int64_t world, int64_
 
 at::Tensor conv3d(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t kt,
                   int64_t kh, int64_t kw, bool causal, const c10::optional<at::Tensor>& resid, bool silu,
-                  c10::optional<at::Tensor> out) {
+                  c10::optional<at::Tensor> out, bool valid_t, bool valid_h) {
   check_bf16_cuda(x, "x");
   check_bf16_cuda(w, "w");
   TORCH_CHECK(x.dim() == 5 && x.is_contiguous(), "x must be contiguous [N, T, H, W, Ci]");
   TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.size(1) == kt * kh * kw * x.size(4), "w must be [Co, taps*Ci]");
   const c10::cuda::CUDAGuard guard(x.device());
   const int64_t Co = w.size(0);
-  at::Tensor y = (out.has_value() && out->defined()) ? *out
-                                                     : at::empty({x.size(0), x.size(1), x.size(2), x.size(3), Co}, x.options());
-  TORCH_CHECK(y.is_contiguous() && y.numel() == x.numel() / x.size(4) * Co, "out must be contiguous [N, T, H, W, Co]");
+  const int64_t To = valid_t ? x.size(1) - kt + 1 : x.size(1), Ho = valid_h ? x.size(2) - kh + 1 : x.size(2);
+  TORCH_CHECK(To > 0 && Ho > 0, "valid convolution of fewer frames / rows than its kernel");
+  at::Tensor y = (out.has_value() && out->defined()) ? *out : at::empty({x.size(0), To, Ho, x.size(3), Co}, x.options());
+  TORCH_CHECK(y.is_contiguous() && y.numel() == x.size(0) * To * Ho * x.size(3) * Co,
+              "out must be contiguous [N, T_out, H_out, W, Co]");
   ConvArgs a{};
   a.x = x.data_ptr();
   a.w = w.data_ptr();
@@ -689,9 +691,48 @@ at::Tensor conv3d(const at::Tensor& x, const at::Tensor& w, const c10::optional<
   a.N = (int)x.size(0), a.T = (int)x.size(1), a.H = (int)x.size(2), a.W = (int)x.size(3), a.Ci = (int)x.size(4);
   a.Co = (int)Co;
   a.kt = (int)kt, a.kh = (int)kh, a.kw = (int)kw, a.causal = causal ? 1 : 0, a.silu = silu ? 1 : 0;
+  a.valid_t = valid_t ? 1 : 0, a.valid_h = valid_h ? 1 : 0;
   a.err = err_ptr();
   DFL_CHECK_RC(dfl_conv3d(&a, cur_stream()), "conv3d");
   return y;
+}
+
+// VAE slab helpers: x [F, Hl, W, C]; y [F, Ho + 2 halo, Wo, C]; up / down = peer pointers (0: none).
+static VaeRowArgs vae_args(const at::Tensor& x, const at::Tensor& y, int64_t Ho, int64_t Wo, bool halo, int64_t up,
+                           int64_t up_rows, int64_t down, int64_t down_rows) {
+  check_bf16_cuda(x, "x");
+  check_bf16_cuda(y, "y");
+  TORCH_CHECK(x.dim() == 4 && x.is_contiguous() && y.dim() == 4 && y.is_contiguous(), "x / y: contiguous [F, H, W, C]");
+  TORCH_CHECK(y.size(0) == x.size(0) && y.size(3) == x.size(3) && y.size(1) == Ho + (halo ? 2 : 0) && y.size(2) == Wo,
+              "y must be [F, Ho + 2 halo, Wo, C]");
+  VaeRowArgs a{};
+  a.x = x.data_ptr();
+  a.y = y.data_ptr();
+  a.F = (int)x.size(0), a.Ho = (int)Ho, a.Wo = (int)Wo, a.C = (int)x.size(3);
+  a.halo = halo ? 1 : 0;
+  a.up = reinterpret_cast<void*>(up);
+  a.up_rows = (int)up_rows;
+  a.down = reinterpret_cast<void*>(down);
+  a.down_rows = (int)down_rows;
+  return a;
+}
+
+void vae_chan_norm(const at::Tensor& x, const at::Tensor& gamma, at::Tensor y, bool silu, bool halo, int64_t up,
+                   int64_t up_rows, int64_t down, int64_t down_rows) {
+  check_bf16_cuda(gamma, "gamma");
+  TORCH_CHECK(gamma.is_contiguous() && gamma.numel() == x.size(3), "gamma must be [C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  VaeRowArgs a = vae_args(x, y, x.size(1), x.size(2), halo, up, up_rows, down, down_rows);
+  a.gamma = gamma.data_ptr();
+  a.silu = silu ? 1 : 0;
+  DFL_CHECK_RC(dfl_vae_chan_norm(&a, cur_stream()), "vae_chan_norm");
+}
+
+void vae_upsample2x(const at::Tensor& x, at::Tensor y, bool halo, int64_t up, int64_t up_rows, int64_t down,
+                    int64_t down_rows) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  VaeRowArgs a = vae_args(x, y, 2 * x.size(1), 2 * x.size(2), halo, up, up_rows, down, down_rows);
+  DFL_CHECK_RC(dfl_vae_upsample2x(&a, cur_stream()), "vae_upsample2x");
 }
 
 void memcpy_async(int64_t dst, int64_t src, int64_t nbytes) {
@@ -816,7 +857,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("memcpy_async", &memcpy_async);
   m.def("conv3d", &conv3d, "implicit-GEMM tcgen05 convolution (channels-last)", py::arg("x"), py::arg("w"),
         py::arg("bias") = py::none(), py::arg("kt") = 3, py::arg("kh") = 3, py::arg("kw") = 3,
-        py::arg("causal") = true, py::arg("resid") = py::none(), py::arg("silu") = false, py::arg("out") = py::none());
+        py::arg("causal") = true, py::arg("resid") = py::none(), py::arg("silu") = false, py::arg("out") = py::none(),
+        py::arg("valid_t") = false, py::arg("valid_h") = false);
   m.def("tp_reduce", &tp_reduce, py::arg("slots"), py::arg("slot_rows"), py::arg("world"), py::arg("rows"),
         py::arg("N"), py::arg("row0"), py::arg("bias") = py::none(), py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("out") = std::vector<int64_t>{},
@@ -824,6 +866,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_put_f32", &peer_put_f32);
   m.def("cfg_combine", &cfg_combine);
+  m.def("vae_chan_norm", &vae_chan_norm, py::arg("x"), py::arg("gamma"), py::arg("y"), py::arg("silu"),
+        py::arg("halo") = false, py::arg("up") = 0, py::arg("up_rows") = 0, py::arg("down") = 0,
+        py::arg("down_rows") = 0);
+  m.def("vae_upsample2x", &vae_upsample2x, py::arg("x"), py::arg("y"), py::arg("halo") = false, py::arg("up") = 0,
+        py::arg("up_rows") = 0, py::arg("down") = 0, py::arg("down_rows") = 0);
   m.def("guided_step", &guided_step, py::arg("a"), py::arg("b_ptr"), py::arg("scale"), py::arg("x"),
         py::arg("x16") = py::none(), py::arg("last") = py::none(), py::arg("m1") = py::none(),
         py::arg("m2") = py::none(), py::arg("m_out") = py::none(), py::arg("coeffs"), py::arg("store_last"),

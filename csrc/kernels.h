@@ -295,11 +295,32 @@ int dfl_tp_reduce(const TpReduceArgs* a, cudaStream_t stream);
 typedef struct ConvArgs {
   const void* x; const void* w; void* y;
   const void* bias; const void* resid; const float* ones;
-  int N, T, H, W, Ci, Co;
+  int N, T, H, W, Ci, Co;  // input extents (x is [N, T, H, W, Ci])
   int kt, kh, kw, causal, silu;
+  // valid_t: no temporal padding (the input already starts with the causal context, e.g. a
+  // streaming cache), T_out = T - kt + 1; valid_h: no padding along H (the input carries halo
+  // rows from the neighbouring spatial slabs), H_out = H - kh + 1.  Otherwise T / H are kept.
+  int valid_t, valid_h;
   int* err;
 } ConvArgs;
 int dfl_conv3d(const ConvArgs* a, cudaStream_t stream);
+
+// Channels-last VAE helpers (vae.cu) on spatial slabs.  x [F, Hl, W, C]; y [F, Ho + 2 halo, Wo, C]
+// (this rank's Ho rows after `halo` rows of context); with halo the first / last output rows are
+// also stored into the slab above (`up`: a peer's y with up_rows own rows) / below (`down`).
+typedef struct VaeRowArgs {
+  const void* x; void* y;
+  const void* gamma;          // chan_norm: [C] bf16
+  int F, Ho, Wo, C;           // frames, output rows / width of this rank's slab, channels (% 8)
+  int halo;
+  void* up; int up_rows;
+  void* down; int down_rows;
+  int silu;
+} VaeRowArgs;
+// y = silu?(x / max(||x||_C, 1e-12) * sqrt(C) * gamma), Ho = Hl, Wo = W
+int dfl_vae_chan_norm(const VaeRowArgs* a, cudaStream_t stream);
+// nearest 2x upsample: Ho = 2 Hl, Wo = 2 W
+int dfl_vae_upsample2x(const VaeRowArgs* a, cudaStream_t stream);
 
 // Copy-engine copy (peer -> local over NVLink; no SM work, no kernel).
 int dfl_memcpy_async(void* dst, const void* src, long long nbytes, cudaStream_t stream);

@@ -36,6 +36,7 @@ CUDA_SOURCES = [
     "probe.cu",
     "probe_noalloc.cu",
     "sched.cu",
+    "vae.cu",
 ]
 CPP_SOURCES = ["bindings.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "probe_noalloc.h", "gemm_epilogue.cuh"]
@@ -199,14 +200,29 @@ def require():
 
 
 def check_device_errors(device=None) -> None:
-    """Raise if any kernel recorded an error in the per-device error word."""
+    """Raise if any kernel recorded an error in the per-device error word.
+
+    A communication timeout (a peer flag that never arrived) raises ``CommTimeoutError`` and stays
+    recorded: every later peer barrier on the device returns at once instead of waiting again, so
+    the ranks that are still alive fail fast until ``clear_device_errors`` (after the process group
+    was rebuilt).  Other errors are cleared once reported."""
     import torch
 
     mod = require()
     dev = torch.cuda.current_device() if device is None else int(device)
     word = mod.error_word(dev).cpu().tolist()
     if word[0] != 0:
-        mod.error_word(dev).zero_()
-        from difflet_b200.utils.errors import DeviceError
+        from difflet_b200.utils.errors import CommTimeoutError, DeviceError
 
+        if word[0] == 2:
+            raise CommTimeoutError(code=word[0], kernel=word[1], detail=(word[2], word[3]))
+        mod.error_word(dev).zero_()
         raise DeviceError(code=word[0], kernel=word[1], detail=(word[2], word[3]))
+
+
+def clear_device_errors(device=None) -> None:
+    """Forget a recorded device error (after recovery), re-arming the bounded waits."""
+    import torch
+
+    dev = torch.cuda.current_device() if device is None else int(device)
+    require().error_word(dev).zero_()

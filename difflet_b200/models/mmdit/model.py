@@ -180,11 +180,11 @@ class MMDiT:
         ws["qkv_txt"] = e(B * S_txt, 3 * Dl)
         ws["mlp"] = e(B * S_loc, Fl)  # [img rows ; txt rows]: both streams' MLPs live at once
         pe = (lambda *shape: par.empty(shape, dt)) if par is not None else e  # noqa: E731
-        if par is not None:
-            par.check_heads(H)
+        if par is not None:  # context parallelism splits this rank's tensor-parallel heads
+            par.check_heads(H // T)
         ws["fused"] = pe(B * S_loc, 3 * Dl + Fl) if cfg.single_blocks else None
         if par is not None:  # the CP mode decides the q/k/v layout (heads x full sequence, or local rows)
-            ws["q"], ws["k"], ws["v"] = par.layout(B, H, dh, S_loc, S, dt)
+            ws["q"], ws["k"], ws["v"] = par.layout(B, H // T, dh, S_loc, S, dt)
         else:
             Ht = H // T
             ws["q"], ws["k"], ws["v"] = e(B, Ht, S, dh), e(B, Ht, S, dh), e(B, Ht, S, dh)
@@ -307,10 +307,11 @@ class MMDiT:
         cos, sin = self.rope(S_txt_g, grid)
         tp = self.tp
         T = tp.world if tp is not None else 1
-        if tp is not None and par is not None:
-            raise NotImplementedError("tensor parallelism composes with cfg-parallel here, not with cp")
-        Ht, Dl, Fl = H // T, D // T, F_ // T  # heads / attention / MLP columns held by this rank
-        Hl = par.heads_local(H) if par is not None else Ht
+        # heads / attention / MLP columns held by this rank (tensor parallelism); context
+        # parallelism then splits the rank's Ht heads (Ulysses) or its rows (ring / gather-KV)
+        # over the cp group: the q/k/v scatter and the attention epilogue address cp peers only
+        Ht, Dl, Fl = H // T, D // T, F_ // T
+        Hl = par.heads_local(Ht) if par is not None else Ht
         S_loc = S_txt + S_img
 
         sp = tp is not None and tp.sp
@@ -352,7 +353,7 @@ class MMDiT:
         def dst(q_, k_, v_, row, pos):
             """qkv_scatter destinations for rows at local offset ``row`` / global position ``pos``."""
             if par is not None:
-                return par.scatter_kwargs(q_, k_, v_, row, pos, S_loc, S, H)
+                return par.scatter_kwargs(q_, k_, v_, row, pos, S_loc, S, Ht)
             return dict(q_dst=[q_], k_dst=[k_], v_dst=[v_], S_dst=S, seq_off=pos, heads_per_rank=Ht)
 
         def mslice(off):
@@ -454,7 +455,7 @@ class MMDiT:
         q, k, v = ws["q"], ws["k"], ws["v"]
         scale = 1.0 / math.sqrt(dh)
         if par is not None:
-            target = ws["attn"].view(B * (S_txt + S_img), D) if out_rows is None else out_rows
+            target = ws["attn"].view(B * (S_txt + S_img), -1) if out_rows is None else out_rows
             n0 = ws["n"][self.cfg.streams[0]]
             n1 = ws["n"][self.cfg.streams[1]]
             par.attention(q, k, v, scale, target, B, n0, n1, target.shape[1], kv_lo=kv_lo, kv_hi=kv_hi)

@@ -188,15 +188,15 @@ class WanTransformer:
         dev, dt = self.device, self.dtype
         e = lambda *s: torch.empty(s, device=dev, dtype=dt)  # noqa: E731
         pe = (lambda *s: par.empty(s, dt)) if par is not None else e  # noqa: E731
-        if par is not None:
-            par.check_heads(H)
+        if par is not None:  # context parallelism splits this rank's tensor-parallel heads
+            par.check_heads(Ht)
         # the residual stream is written by every rank's TP reducer: symmetric memory under TP
         x = tp.empty((B * S_loc, D), dt) if tp is not None else e(B * S_loc, D)
         ws = {"S": S, "x": x, "norm": e(B * S_loc, D), "qkv": e(B * S_loc, 3 * Dl),
               "mlp": e(B * S_loc, cfg.ffn // T), "cq": e(B, Ht, S_loc, dh), "cqin": e(B * S_loc, Dl),
               "cattn": e(B, S_loc, Dl), "attn": pe(B, S_loc, Dl)}
         if par is not None:  # the CP mode decides the q/k/v layout
-            ws["q"], ws["k"], ws["v"] = par.layout(B, H, dh, S_loc, S, dt)
+            ws["q"], ws["k"], ws["v"] = par.layout(B, Ht, dh, S_loc, S, dt)
         else:
             ws["q"], ws["k"], ws["v"] = e(B, Ht, S, dh), e(B, Ht, S, dh), e(B, Ht, S, dh)
         self._ws[key] = ws
@@ -245,8 +245,6 @@ class WanTransformer:
         ``out`` (optional, [B, S(local), out_dim] bf16): where the final projection stores the
         prediction (a CFG-parallel exchange buffer)."""
         cfg, w, par, tp = self.cfg, self.w, self.par, self.tp
-        if tp is not None and par is not None:
-            raise NotImplementedError("Wan tensor parallelism composes with cfg-parallel here, not with cp")
         B, S_loc, _ = x_tokens.shape
         T = tp.world if tp is not None else 1
         D, H, dh = cfg.hidden // T, cfg.heads // T, cfg.head_dim  # this rank's columns / heads

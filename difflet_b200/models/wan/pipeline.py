@@ -193,14 +193,20 @@ class WanApplication:
         return ((video.float() * 0.5 + 0.5).clamp(0, 1) * 255).round().to(torch.uint8).permute(0, 2, 3, 4, 1)
 
     def decode(self, lat):
-        """Causal VAE decode; with a multi-GPU decoder every rank decodes its share and rank 0
-        returns the video (others None)."""
+        """Causal VAE decode.  Under a multi-GPU world every rank decodes a slab of rows (halo rows
+        exchanged over NVLink by the producer kernels) and rank 0 returns the video [B, 3, F, H, W]
+        in [-1, 1] (the other ranks None)."""
         import torch.distributed as dist
 
-        if getattr(self.vae, "distributed", False):
+        if dist.is_initialized() and dist.get_world_size() > 1 and hasattr(self.vae, "set_slabs"):
+            rows = lat.shape[3]
+            if self.vae.slabs is None or self.vae.slabs.rows != rows or self.vae.slabs.world == 1:
+                from difflet_b200.parallel.slabs import make_slabs
+
+                self.vae.set_slabs(make_slabs(rows, lat.device))
             return self.vae.decode(lat)
         if dist.is_initialized() and dist.get_rank() != 0:
             return None
-        return self.vae.decode(lat)  # [B, 3, F, H, W] in [-1, 1]
+        return self.vae.decode(lat)
 
     __call__ = generate

@@ -509,19 +509,23 @@ def conv_weight(w: torch.Tensor) -> torch.Tensor:
     return w.permute(0, 2, 3, 4, 1).reshape(Co, -1, Ci).reshape(Co, -1).contiguous()
 
 
-def conv_cl(x, w2, b=None, *, kt=3, kh=3, kw=3, causal=True, resid=None, silu=False, out=None):
+def conv_cl(x, w2, b=None, *, kt=3, kh=3, kw=3, causal=True, resid=None, silu=False, out=None, valid_t=False,
+            valid_h=False):
     """Stride-1 convolution on channels-last x [N, T, H, W, Ci] with ``conv_weight`` weights;
     zero spatial padding k/2, temporal causal (kt - 1 in front) or symmetric padding;
-    optional bias, SiLU, residual add (y = resid + conv).  CUDA -> tcgen05 implicit GEMM."""
+    ``valid_t``: no temporal padding (x starts with its causal context: T_out = T - kt + 1);
+    ``valid_h``: no padding along H (x carries halo rows: H_out = H - kh + 1).
+    Optional bias, SiLU, residual add (y = resid + conv).  CUDA -> tcgen05 implicit GEMM."""
     if x.is_cuda:
-        return native().conv3d(x, w2, b, kt, kh, kw, causal, resid, silu, out)
+        return native().conv3d(x, w2, b, kt, kh, kw, causal, resid, silu, out, valid_t, valid_h)
     N, T, H, W, Ci = x.shape
     Co = w2.shape[0]
     ct = torch.float64 if x.dtype == torch.float64 else torch.float32
     w5 = w2.to(ct).view(Co, kt, kh, kw, Ci).permute(0, 4, 1, 2, 3)
     xc = x.to(ct).permute(0, 4, 1, 2, 3)
-    pt0, pt1 = (kt - 1, 0) if causal else (kt // 2, kt // 2)
-    xc = F.pad(xc, (kw // 2, kw // 2, kh // 2, kh // 2, pt0, pt1))
+    pt0, pt1 = (0, 0) if valid_t else ((kt - 1, 0) if causal else (kt // 2, kt // 2))
+    ph = 0 if valid_h else kh // 2
+    xc = F.pad(xc, (kw // 2, kw // 2, ph, ph, pt0, pt1))
     y = F.conv3d(xc, w5, None if b is None else b.to(ct))
     if silu:
         y = F.silu(y)
@@ -532,6 +536,35 @@ def conv_cl(x, w2, b=None, *, kt=3, kh=3, kw=3, causal=True, resid=None, silu=Fa
         out.copy_(y.to(out.dtype))
         return out
     return y.to(x.dtype)
+
+
+def vae_chan_norm(x, gamma, y, *, silu=True, halo=0, up=0, up_rows=0, down=0, down_rows=0):
+    """Channels-last RMS over the channels of each pixel (``x / max(|x|, 1e-12) * sqrt(C) * gamma``,
+    optional SiLU) of x [F, Hl, W, C] into y [F, Hl + 2 halo, W, C] at row offset ``halo``; on CUDA
+    the first / last rows also go to the slabs above / below (``up`` / ``down``: peer pointers of
+    their y, 0 = none) -- the halo exchange of a spatially split decode."""
+    if x.is_cuda:
+        native().vae_chan_norm(x, gamma, y, bool(silu), bool(halo), int(up), int(up_rows), int(down),
+                               int(down_rows))
+        return y
+    ct = torch.float64 if x.dtype == torch.float64 else torch.float32
+    xf = x.to(ct)
+    v = xf / xf.norm(dim=-1, keepdim=True).clamp_min(1e-12) * (x.shape[-1] ** 0.5) * gamma.to(ct)
+    if silu:
+        v = F.silu(v)
+    y[:, halo:halo + x.shape[1]] = v.to(y.dtype)
+    return y
+
+
+def vae_upsample2x(x, y, *, halo=0, up=0, up_rows=0, down=0, down_rows=0):
+    """Nearest 2x (H, W) upsample of channels-last x [F, Hl, W, C] into y [F, 2 Hl + 2 halo, 2 W, C]
+    (halo rows to the neighbouring slabs as in ``vae_chan_norm``)."""
+    if x.is_cuda:
+        native().vae_upsample2x(x, y, bool(halo), int(up), int(up_rows), int(down), int(down_rows))
+        return y
+    v = x.repeat_interleave(2, dim=1).repeat_interleave(2, dim=2)
+    y[:, halo:halo + v.shape[1]] = v.to(y.dtype)
+    return y
 
 
 # --------------------------------------------------------------------------- MXFP8

@@ -228,8 +228,9 @@ def make_sequence_parallel(parallel, device, transport: str | None = None):
         return None
     if not dist.is_initialized():
         raise RuntimeError("sequence parallelism needs an initialised process group (run under torchrun)")
-    if parallel.tp_degree != 1 or parallel.dp_degree != 1:
-        raise NotImplementedError("context parallelism composes with cfg-parallel here (tp=1, dp=1)")
+    if parallel.dp_degree != 1:
+        raise NotImplementedError("data-parallel replicas are separate processes groups (cli/dp.py); "
+                                  "build one model replica per dp coordinate")
     if groups.mesh() != parallel.mesh_spec:
         groups.init_mesh(parallel.mesh_spec)
     group, ranks = groups.get_group("cp"), groups.get_group_ranks("cp")

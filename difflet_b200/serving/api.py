@@ -25,7 +25,7 @@ from typing import Any
 from fastapi import Body, FastAPI, HTTPException, Request
 from fastapi.responses import FileResponse, JSONResponse
 
-from difflet_b200.serving.engines import EngineError, QueueTimeout
+from difflet_b200.serving.engines import EngineError, QueueTimeout, RequestCancelled
 from difflet_b200.serving.video_jobs import VideoJobStore
 
 _GEN_KEYS = ("height", "width", "num_inference_steps", "seed", "guidance_scale", "guidance_scale_2",
@@ -67,13 +67,13 @@ def normalize_chat_request(payload: dict) -> dict:
 
 def create_app(engine, model_id: str, *, output: str = "image", api_key: str | None = None,
                request_timeout: float = 600.0, video_dir: str | None = None, encode_image=None,
-               encode_video=None) -> FastAPI:
+               encode_video=None, artifact_store=None) -> FastAPI:
     from difflet_b200.utils.media import encode_mjpeg_avi, encode_png
 
     encode_image = encode_image or encode_png
     encode_video = encode_video or encode_mjpeg_avi
     app = FastAPI(title="difflet_b200", version="0.1.0")
-    jobs = VideoJobStore(engine, video_dir, encode_video) if output == "video" else None
+    jobs = VideoJobStore(engine, video_dir, encode_video, artifact_store=artifact_store) if output == "video" else None
 
     @app.middleware("http")
     async def auth(request: Request, call_next):
@@ -116,23 +116,38 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
             if req.get(field) is not None:
                 raise HTTPException(400, f"{field}: {why}")
 
-    def _run(req):
+    def _run(req, request_id=None):
         _validate(req)
         try:
+            if request_id is not None and hasattr(engine, "cancel"):
+                return engine.generate(req, timeout=request_timeout, request_id=request_id)
             return engine.generate(req, timeout=request_timeout)
         except QueueTimeout:
             raise HTTPException(429, "server busy, retry later")
+        except RequestCancelled as exc:
+            raise HTTPException(499, str(exc))
         except EngineError as exc:
             raise HTTPException(500, str(exc)[-2000:])
+
+    @app.post("/v1/requests/{rid}/cancel")
+    async def cancel_request(rid: str):
+        """Cancel a running request started with an ``X-Request-Id`` header (or a video job id)."""
+        if jobs is not None and jobs.get(rid) is not None:
+            return jobs.cancel(rid).public()
+        ok = bool(hasattr(engine, "cancel") and engine.cancel(rid))
+        if not ok:
+            raise HTTPException(404, "no running request with that id")
+        return {"id": rid, "status": "cancelling"}
 
     if output == "image":
         import asyncio
 
         @app.post("/v1/chat/completions")
-        async def chat(payload: Any = Body(default=None)):
+        async def chat(request: Request, payload: Any = Body(default=None)):
             req = normalize_chat_request(payload)
             t0 = time.perf_counter()
-            img = await asyncio.get_running_loop().run_in_executor(None, _run, req)
+            rid = request.headers.get("x-request-id")
+            img = await asyncio.get_running_loop().run_in_executor(None, _run, req, rid)
             png = encode_image(img) if not isinstance(img, (bytes, bytearray)) else bytes(img)
             url = "data:image/png;base64," + base64.b64encode(png).decode()
             return {"id": "chatcmpl-" + uuid.uuid4().hex, "object": "chat.completion", "created": int(time.time()),
@@ -143,14 +158,14 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
                     "usage": {"generation_seconds": round(time.perf_counter() - t0, 3)}}
 
         @app.post("/v1/images/generations")
-        async def images(payload: Any = Body(default=None)):
+        async def images(request: Request, payload: Any = Body(default=None)):
             if not isinstance(payload, dict) or not payload.get("prompt"):
                 raise HTTPException(400, "prompt is required")
             req = {"prompt": payload["prompt"], **_parse_size(payload.get("size"))}
             for k in _GEN_KEYS:
                 if k in payload:
                     req[k] = payload[k]
-            img = await asyncio.get_running_loop().run_in_executor(None, _run, req)
+            img = await asyncio.get_running_loop().run_in_executor(None, _run, req, request.headers.get("x-request-id"))
             png = encode_image(img) if not isinstance(img, (bytes, bytearray)) else bytes(img)
             return {"created": int(time.time()), "data": [{"b64_json": base64.b64encode(png).decode()}]}
 
@@ -177,6 +192,12 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
                 raise HTTPException(404, "no such video")
             return job.public()
 
+        @app.get("/v1/videos")
+        async def list_videos(after: str | None = None, limit: int = 20):
+            page = jobs.repo.list(after=after, limit=max(1, min(100, limit)))
+            return {"object": "list", "data": [j.public() for j in page],
+                    "has_more": len(jobs.repo.list(after=page[-1].id, limit=1)) > 0 if page else False}
+
         @app.get("/v1/videos/{vid}/content")
         async def video_content(vid: str):
             job = jobs.get(vid)
@@ -184,7 +205,32 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
                 raise HTTPException(404, "no such video")
             if job.status != "completed":
                 raise HTTPException(409, f"video is {job.status}")
+            if job.url and not job.url.startswith("file://"):
+                from fastapi.responses import RedirectResponse
+
+                return RedirectResponse(job.url, status_code=307)
             return FileResponse(job.path, media_type="video/x-msvideo")
+
+        @app.post("/v1/videos/{vid}/cancel")
+        async def cancel_video(vid: str):
+            if jobs.get(vid) is None:
+                raise HTTPException(404, "no such video")
+            return jobs.cancel(vid).public()
+
+        @app.delete("/v1/videos/{vid}")
+        async def delete_video(vid: str):
+            """Delete a finished job's record (a queued or running one is cancelled first)."""
+            from difflet_b200.serving.video_jobs import TERMINAL
+
+            job = jobs.get(vid)
+            if job is None:
+                raise HTTPException(404, "no such video")
+            if job.status not in TERMINAL:
+                job = jobs.cancel(vid)
+                if job.status not in TERMINAL:
+                    return {"id": vid, "object": "video.deleted", "deleted": False, "status": job.status}
+            jobs.repo.delete(vid)
+            return {"id": vid, "object": "video.deleted", "deleted": True}
 
     app.state.jobs = jobs
     return app

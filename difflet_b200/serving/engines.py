@@ -11,7 +11,13 @@ Reference behaviour (``difflet/serving/engines/resident_worker.py:51-1404``,
     worker the engine cancels, waits a grace period, terminates, restarts the
     worker and fences (the in-flight request fails; later ones run on the new
     worker)
-  * ``ReplicatedEngine`` spreads requests over N replicas (least loaded first)
+  * ``ReplicatedEngine`` spreads requests over N replicas (least loaded first); each replica
+    is pinned to its own GPUs (``CUDA_VISIBLE_DEVICES``), and a replica whose parallel world is
+    larger than one GPU runs as a group of rank processes (rank 0 answers, the others follow
+    every request; ``parallel/groups.py`` rendezvous on 127.0.0.1)
+  * a running request can be cancelled: the worker checks a shared flag between denoise
+    steps (rank 0 decides, every rank of a group learns the decision through a broadcast at
+    the same step) and the request ends with ``RequestCancelled``
 """
 
 from __future__ import annotations
@@ -31,6 +37,10 @@ class QueueTimeout(Exception):
 
 class EngineError(RuntimeError):
     pass
+
+
+class RequestCancelled(EngineError):
+    """The request was cancelled while it ran."""
 
 
 class _Admission:
@@ -87,10 +97,70 @@ class InProcessEngine:
         pass
 
 
-def _worker_main(conn_req, conn_resp, hb, factory, factory_kwargs, heartbeat_s):
-    """Worker process: build the pipeline, smoke-test it, serve requests, beat."""
+def _apply_env(env: dict | None) -> None:
+    """Process environment of a worker (GPU pinning, rendezvous), before CUDA is initialised."""
+    import os
+
+    if env:
+        os.environ.update({k: str(v) for k, v in env.items()})
+
+
+def _call_run(run, req, should_cancel):
+    import inspect
+
+    try:
+        takes = "should_cancel" in inspect.signature(run).parameters
+    except (TypeError, ValueError):
+        takes = False
+    return run(req, should_cancel=should_cancel) if takes else run(req)
+
+
+def _follower_main(rank, world, port, env, factory, factory_kwargs, feed, cancel_flag):
+    """Rank > 0 of a multi-GPU replica: same pipeline, runs every request rank 0 forwards."""
+    _apply_env(dict(env or {}, RANK=rank, LOCAL_RANK=rank, WORLD_SIZE=world, MASTER_ADDR="127.0.0.1",
+                    MASTER_PORT=port))
+    from difflet_b200.parallel.groups import init_distributed
+
+    init_distributed()
+    run = factory(**factory_kwargs)
+    decide = _group_cancel(cancel_flag)
+    run({"__smoke__": True})
+    while True:
+        req = feed.get()
+        if req is None:
+            break
+        try:
+            _call_run(run, req, decide)
+        except Exception:  # noqa: BLE001 - rank 0 reports the request's outcome
+            pass
+
+
+def _group_cancel(cancel_flag):
+    """should_cancel() for every rank of a group: rank 0 reads the shared flag, a broadcast makes
+    the decision the same on every rank at the same step (no rank leaves a collective early)."""
+    import torch.distributed as dist
+
+    def decide() -> bool:
+        import torch
+
+        if not dist.is_initialized() or dist.get_world_size() == 1:
+            return bool(cancel_flag.value)
+        dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
+        t = torch.tensor([int(cancel_flag.value) if dist.get_rank() == 0 else 0], device=dev)
+        dist.broadcast(t, 0)
+        return bool(t.item())
+
+    return decide
+
+
+def _worker_main(conn_req, conn_resp, hb, factory, factory_kwargs, heartbeat_s, env=None, world=1,
+                 cancel_flag=None):
+    """Worker process (rank 0 of its replica): build the pipeline, smoke-test it, serve requests,
+    beat.  With world > 1 it first starts the replica's other ranks and rendezvouses with them."""
+    _apply_env(env)
     state = {"state": "loading", "stage": "", "request_id": None}
     stop = threading.Event()
+    followers, feeds = [], []
 
     def beat():
         while not stop.is_set():
@@ -102,7 +172,25 @@ def _worker_main(conn_req, conn_resp, hb, factory, factory_kwargs, heartbeat_s):
 
     threading.Thread(target=beat, daemon=True).start()
     try:
+        if world > 1:
+            from difflet_b200.parallel.testing import free_port
+
+            port = free_port()
+            ctx = mp.get_context("spawn")
+            for r in range(1, world):
+                q = ctx.Queue()
+                p = ctx.Process(target=_follower_main, args=(r, world, port, env, factory, factory_kwargs, q,
+                                                             cancel_flag), daemon=True)
+                p.start()
+                followers.append(p)
+                feeds.append(q)
+            _apply_env({"RANK": 0, "LOCAL_RANK": 0, "WORLD_SIZE": world, "MASTER_ADDR": "127.0.0.1",
+                        "MASTER_PORT": port})
+            from difflet_b200.parallel.groups import init_distributed
+
+            init_distributed()
         run = factory(**factory_kwargs)
+        decide = _group_cancel(cancel_flag) if cancel_flag is not None else (lambda: False)
         state["state"] = "smoke"
         run({"__smoke__": True})
         state["state"] = "ready"
@@ -117,12 +205,21 @@ def _worker_main(conn_req, conn_resp, hb, factory, factory_kwargs, heartbeat_s):
             break
         rid, req = msg
         state.update(state="running", request_id=rid, stage="generate")
+        if cancel_flag is not None:
+            cancel_flag.value = 0
+        for q in feeds:
+            q.put(req)
         try:
-            out = run(req)
+            out = _call_run(run, req, decide)
             conn_resp.put(("ok", rid, out))
-        except Exception:
-            conn_resp.put(("error", rid, traceback.format_exc()))
+        except Exception as exc:  # noqa: BLE001
+            kind = "cancelled" if type(exc).__name__ == "RequestCancelled" else "error"
+            conn_resp.put((kind, rid, traceback.format_exc()))
         state.update(state="ready", request_id=None, stage="")
+    for q in feeds:
+        q.put(None)
+    for p in followers:
+        p.join(timeout=30)
     stop.set()
 
 
@@ -133,9 +230,16 @@ class ResidentWorkerEngine:
     (picklable result).  It must be importable by name (spawn)."""
 
     def __init__(self, factory, factory_kwargs=None, *, queue_timeout=30.0, request_timeout=600.0,
-                 heartbeat_s=5.0, heartbeat_timeout=None, start_timeout=1800.0, max_queued=None):
+                 heartbeat_s=5.0, heartbeat_timeout=None, start_timeout=1800.0, max_queued=None,
+                 devices: list | None = None, world: int = 1, env: dict | None = None):
         self.factory = factory
         self.factory_kwargs = dict(factory_kwargs or {})
+        self.devices = list(devices) if devices is not None else None
+        self.world = int(world)
+        self.env = dict(env or {})
+        if self.devices is not None:  # this replica's GPUs only (replica i of dp: its own slice)
+            self.env["CUDA_VISIBLE_DEVICES"] = ",".join(str(d) for d in self.devices)
+        self._current = None
         self.queue_timeout = queue_timeout
         self._adm = _Admission(queue_timeout, max_queued)
         self.request_timeout = request_timeout
@@ -143,6 +247,7 @@ class ResidentWorkerEngine:
         self.heartbeat_timeout = heartbeat_timeout or max(6 * heartbeat_s, 30.0)
         self.start_timeout = start_timeout
         self._ctx = mp.get_context("spawn")
+        self._cancel = self._ctx.Value("b", 0)
         self.ready = False
         self.healthy = True
         self.inflight = 0
@@ -155,8 +260,9 @@ class ResidentWorkerEngine:
         self._resp = self._ctx.Queue()
         self._hb = self._ctx.Queue()
         self.proc = self._ctx.Process(target=_worker_main, args=(self._req, self._resp, self._hb, self.factory,
-                                                                self.factory_kwargs, self.heartbeat_s),
-                                      daemon=True)
+                                                                self.factory_kwargs, self.heartbeat_s, self.env,
+                                                                self.world, self._cancel),
+                                      daemon=False)
         self.proc.start()
         deadline = time.time() + self.start_timeout
         while time.time() < deadline:
@@ -199,11 +305,19 @@ class ResidentWorkerEngine:
         self._start()
         raise EngineError(f"request failed, worker restarted ({reason})")
 
-    def generate(self, request: dict, timeout: float | None = None):
+    def cancel(self, request_id: str) -> bool:
+        """Ask the worker to stop the running request ``request_id`` at its next denoise step."""
+        if self._current != request_id:
+            return False
+        self._cancel.value = 1
+        return True
+
+    def generate(self, request: dict, timeout: float | None = None, request_id: str | None = None):
         self._adm.acquire()
         self.inflight += 1
         try:
-            rid = str(uuid.uuid4())
+            rid = request_id or str(uuid.uuid4())
+            self._current = rid
             self._req.put((rid, request))
             deadline = time.time() + (timeout or self.request_timeout)
             last_beat = time.time()
@@ -226,8 +340,11 @@ class ResidentWorkerEngine:
                     continue  # a late answer for a request fenced off by a restart
                 if kind == "ok":
                     return payload
+                if kind == "cancelled":
+                    raise RequestCancelled(f"request {rid} cancelled")
                 raise EngineError(payload)
         finally:
+            self._current = None
             self.inflight -= 1
             self._adm.release()
 
@@ -254,15 +371,20 @@ class ReplicatedEngine:
     def healthy(self):
         return all(r.healthy for r in self.replicas)
 
-    def generate(self, request, timeout=None):
+    def generate(self, request, timeout=None, request_id=None):
         order = sorted(self.replicas, key=lambda r: r.inflight)
         last = None
         for r in order:
             try:
+                if request_id is not None and hasattr(r, "cancel"):
+                    return r.generate(request, timeout, request_id=request_id)
                 return r.generate(request, timeout)
             except QueueTimeout as exc:
                 last = exc
         raise last or QueueTimeout("server busy")
+
+    def cancel(self, request_id: str) -> bool:
+        return any(r.cancel(request_id) for r in self.replicas if hasattr(r, "cancel"))
 
     def close(self):
         for r in self.replicas:

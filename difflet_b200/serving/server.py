@@ -12,13 +12,17 @@ import logging
 
 
 def pipeline_runner(model_id: str, pipeline_kwargs: dict):
-    """Runs inside the worker process: load once, return run(request)."""
+    """Runs inside every rank process of a replica: load once, return run(request, should_cancel).
+
+    ``should_cancel()`` is polled between denoise steps (every rank of a multi-GPU replica polls
+    at the same step and gets the same answer); a cancelled request raises RequestCancelled."""
     from difflet_b200.pipeline.difflet_pipeline import DiffletPipeline
+    from difflet_b200.serving.engines import RequestCancelled
 
     pipe = DiffletPipeline.from_pretrained(model_id, **pipeline_kwargs)
     video = pipe.model_entry.output == "video"
 
-    def run(req: dict):
+    def run(req: dict, should_cancel=None):
         if req.get("__smoke__"):
             kw = {"prompt": "smoke", "num_inference_steps": 2}
             if video:
@@ -26,12 +30,37 @@ def pipeline_runner(model_id: str, pipeline_kwargs: dict):
             kw["height"], kw["width"] = 256, 256
             pipe(**kw)
             return None
+        req = dict(req)
+        if should_cancel is not None:
+            user_cb = req.pop("callback", None)
+
+            def callback(i, latents):
+                if should_cancel():
+                    raise RequestCancelled(f"cancelled at step {i}")
+                if user_cb is not None:
+                    user_cb(i, latents)
+
+            req["callback"] = callback
         out = pipe(**req)
         if out is None:
             return None
         return out[0].cpu()
 
     return run
+
+
+def replica_devices(replicas: int, model_world: int, visible: list | None = None) -> list[list[int]]:
+    """GPU indices of each replica: consecutive slices of ``model_world`` GPUs (replica i of a
+    dp group never shares a GPU with another replica)."""
+    import torch
+
+    gpus = visible if visible is not None else list(range(torch.cuda.device_count()))
+    need = replicas * model_world
+    if gpus and len(gpus) < need:
+        raise ValueError(f"{replicas} replicas x {model_world} GPUs each need {need} GPUs, {len(gpus)} visible")
+    if not gpus:
+        return [[] for _ in range(replicas)]
+    return [gpus[i * model_world:(i + 1) * model_world] for i in range(replicas)]
 
 
 def serve_main(a) -> int:
@@ -50,11 +79,20 @@ def serve_main(a) -> int:
     from difflet_b200.serving.options import ServeOptions
 
     opts = ServeOptions.from_args(a)
+    world = kw["parallel"].model_world_size
+    import os
+
+    visible = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()] or None
+    devices = replica_devices(opts.replicas, world, visible) if a.backend != "cpu" else [None] * opts.replicas
     replicas = [ResidentWorkerEngine(pipeline_runner, {"model_id": a.model_id, "pipeline_kwargs": kw},
-                                     **opts.engine_kwargs())
-                for _ in range(opts.replicas)]
+                                     devices=dev or None, world=world, **opts.engine_kwargs())
+                for dev in devices]
     engine = replicas[0] if len(replicas) == 1 else ReplicatedEngine(replicas)
-    app = create_app(engine, a.model_id, output=entry.output, api_key=opts.api_key)
+    from difflet_b200.serving.artifacts import make_artifact_store
+
+    store = make_artifact_store() if entry.output == "video" and any(k.startswith("DIFFLET_S3_") for k in os.environ) \
+        else None
+    app = create_app(engine, a.model_id, output=entry.output, api_key=opts.api_key, artifact_store=store)
     uvicorn.run(app, host=opts.host, port=opts.port, log_level="info")
     engine.close()
     return 0

@@ -523,3 +523,78 @@ def test_guided_step_euler(native):
         ref = ref + sched.dt(i) * (u.float() + 4.0 * (c.float() - u.float()))
     torch.cuda.synchronize()
     assert (x - ref).abs().max().item() <= 1e-5 * ref.abs().max().item()
+
+
+def test_peer_barrier_timeout_fails_fast(native):
+    """A barrier slot that nothing ever sets: the bounded wait runs out, the kernel records a
+    communication timeout and returns (the context stays usable), the host raises
+    CommTimeoutError, and the next barrier returns at once instead of waiting again."""
+    import time
+
+    from difflet_b200 import _native
+    from difflet_b200.utils.errors import CommTimeoutError
+
+    torch.cuda.synchronize()
+    _native.clear_device_errors()
+    world = 2
+    mine = torch.zeros(world, device="cuda", dtype=torch.int32)    # this rank's slots
+    ghost = torch.zeros(world, device="cuda", dtype=torch.int32)   # a "peer" that never arrives
+    counter = torch.zeros(1, device="cuda", dtype=torch.int32)
+    flags = [mine.data_ptr(), ghost.data_ptr()]
+    native.peer_barrier(flags, counter, 0, 20_000_000)  # ~10 ms at 2 GHz
+    torch.cuda.synchronize()
+    with pytest.raises(CommTimeoutError):
+        _native.check_device_errors()
+    t0 = time.perf_counter()
+    native.peer_barrier(flags, counter, 0, 4_000_000_000)  # would wait ~2 s if it waited at all
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 0.5
+    with pytest.raises(CommTimeoutError):  # still recorded: later collectives keep failing fast
+        _native.check_device_errors()
+    _native.clear_device_errors()
+    _native.check_device_errors()
+    x = torch.randn(256, 256, device="cuda", dtype=torch.bfloat16)
+    assert torch.isfinite(native.gemm(x, x, None).float()).all()  # the context is still usable
+
+
+def test_vae_chan_norm_and_upsample_with_halo_stores(native):
+    """Channel RMS + SiLU and the nearest upsampler write their rows at the halo offset and their
+    boundary rows into the neighbouring slabs' halo rows (here local tensors stand in for the
+    peers' buffers, with different row counts, as the last slab of an uneven split has)."""
+    from difflet_b200.ops import fused as F
+
+    torch.manual_seed(5)
+    Fr, rows, W, C = 3, 5, 24, 96
+    x = torch.randn(Fr, rows, W, C, device="cuda", dtype=torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(C, device="cuda")).bfloat16()
+    y = torch.zeros(Fr, rows + 2, W, C, device="cuda", dtype=torch.bfloat16)
+    up = torch.zeros(Fr, 7 + 2, W, C, device="cuda", dtype=torch.bfloat16)
+    down = torch.zeros(Fr, 4 + 2, W, C, device="cuda", dtype=torch.bfloat16)
+    F.vae_chan_norm(x, gamma, y, silu=True, halo=1, up=up.data_ptr(), up_rows=7, down=down.data_ptr(), down_rows=4)
+    xf = x.float()
+    ref = torch.nn.functional.silu(xf / xf.norm(dim=-1, keepdim=True) * C ** 0.5 * gamma.float())
+    torch.cuda.synchronize()
+    _close(y[:, 1:rows + 1], ref)
+    assert torch.equal(up[:, 8], y[:, 1]) and torch.equal(down[:, 0], y[:, rows])
+    assert y[:, 0].abs().sum() == 0 and y[:, rows + 1].abs().sum() == 0  # own halo rows untouched
+    assert up[:, :8].abs().sum() == 0 and down[:, 1:].abs().sum() == 0
+    u = torch.zeros(Fr, 2 * rows + 2, 2 * W, C, device="cuda", dtype=torch.bfloat16)
+    up2 = torch.zeros(Fr, 6 + 2, 2 * W, C, device="cuda", dtype=torch.bfloat16)
+    F.vae_upsample2x(x, u, halo=1, up=up2.data_ptr(), up_rows=6)
+    ref_u = x.repeat_interleave(2, 1).repeat_interleave(2, 2)
+    torch.cuda.synchronize()
+    assert torch.equal(u[:, 1:2 * rows + 1], ref_u) and torch.equal(up2[:, 7], ref_u[:, 0])
+
+
+def test_wan_vae_native_decoder_matches_reference(native):
+    """The channels-last Wan VAE decoder on the native kernels (bf16) against the NCTHW
+    PyTorch decoder in fp32 on the CPU, three latent frames (first-chunk and cached paths)."""
+    from difflet_b200.models.vae.wan_vae import WanVAEConfig, WanVAEDecoder, WanVAEReference
+
+    cfg = WanVAEConfig(base_dim=32)
+    dec = WanVAEDecoder.random_init(cfg, device="cuda", dtype=torch.bfloat16, seed=4)
+    z = torch.randn(1, 16, 3, 6, 20, generator=torch.Generator().manual_seed(1))
+    out = dec.decode(z.cuda().bfloat16()).float().cpu()
+    ref = WanVAEReference(cfg, {k: v.float().cpu() for k, v in dec.w.items()}).decode(z)
+    assert out.shape == ref.shape == (1, 3, 9, 48, 160)
+    assert ((out - ref).norm() / ref.norm()).item() < 3e-2

@@ -114,3 +114,47 @@ def _tp_forward(rank, world, B, family, sp=False):
 def test_tensor_parallel_matches_dense(world, B, family, sp):
     errs = run_ranks(_tp_forward, world, B, family, sp, timeout=240)
     assert max(errs) < 1e-10, errs
+
+
+def _cp_tp_forward(rank, world, tp_deg, mode, family):
+    """Context parallelism inside tensor parallelism: the mesh's tp axis shards heads / MLP
+    columns, its cp axis shards the sequence (Ulysses splits each rank's tp heads further)."""
+    from difflet_b200.models.mmdit import MMDiT, get_config, pack_latents
+    from difflet_b200.parallel import groups
+    from difflet_b200.parallel.tp import make_tensor_parallel, shard_mmdit_weights
+    from difflet_b200.parallel.ulysses import make_sequence_parallel
+    from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
+
+    par_cfg = DiffletParallelConfig(tp_degree=tp_deg, cp_degree=world // tp_deg, cp_mode=mode)
+    groups.init_mesh(par_cfg.mesh_spec)
+    dev = torch.device("cpu")
+    name = {"flux": "tiny128", "hunyuan": "tiny-hunyuan"}[family]
+    cfg = get_config(name, heads=8, hidden=1024) if family == "flux" else get_config(name, heads=4, hidden=512)
+    m = MMDiT.random_init(cfg, dtype=torch.float64, seed=31)
+    g = torch.Generator().manual_seed(4)
+    B = 1
+    if family == "flux":
+        x = pack_latents(torch.randn(B, 16, 16, 16, generator=g, dtype=torch.float64))
+        grid, valid = (1, 8, 8), None
+    else:
+        x = pack_latents(torch.randn(B, 16, 2, 16, 16, generator=g, dtype=torch.float64))
+        grid, valid = (2, 8, 8), torch.tensor([21])
+    txt = torch.randn(B, 32, cfg.text_dim, generator=g, dtype=torch.float64)
+    pooled = torch.randn(B, cfg.pooled_dim, generator=g, dtype=torch.float64) if cfg.pooled_dim else None
+    t = torch.full((B,), 0.6, dtype=torch.float64)
+    gd = torch.full((B,), 3.5, dtype=torch.float64)
+    dense = m(x, txt, pooled, t, gd, grid=grid, txt_valid=valid)
+    tp = make_tensor_parallel(par_cfg, dev, transport="nccl")
+    sp = make_sequence_parallel(par_cfg, dev, transport="nccl")
+    m2 = MMDiT(cfg, shard_mmdit_weights(cfg, m.w, tp.world, tp.rank))
+    m2.tp, m2.par = tp, sp
+    txt_in = txt if cfg.refiner_layers else sp.shard_tokens(txt)
+    out = m2(sp.shard_tokens(x), txt_in, pooled, t, gd, grid=grid, txt_valid=valid)
+    return (sp.gather_tokens(out) - dense).abs().max().item()
+
+
+@pytest.mark.parametrize("tp_deg,mode,family", [(2, "ulysses", "flux"), (2, "ring", "flux"), (2, "gather_kv", "flux"),
+                                                (2, "ulysses", "hunyuan")])
+def test_context_parallel_inside_tensor_parallel(tp_deg, mode, family):
+    errs = run_ranks(_cp_tp_forward, 4, tp_deg, mode, family, timeout=300)
+    assert max(errs) < 1e-10, errs

@@ -94,3 +94,36 @@ def test_wan_tensor_parallel_matches_dense(world):
     from difflet_b200.parallel.testing import run_ranks
 
     assert max(run_ranks(_tp, world, timeout=240)) < 1e-10
+
+
+def _cp_tp(rank, world, mode):
+    from difflet_b200.parallel import groups
+    from difflet_b200.parallel.tp import make_tensor_parallel, shard_wan_weights
+    from difflet_b200.parallel.ulysses import make_sequence_parallel
+    from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
+
+    par_cfg = DiffletParallelConfig(tp_degree=2, cp_degree=world // 2, cp_mode=mode)
+    groups.init_mesh(par_cfg.mesh_spec)
+    dev = torch.device("cpu")
+    cfg = get_wan_config("tiny-wan", heads=8, hidden=1024, ffn=1024)
+    m = WanTransformer.random_init(cfg, dtype=torch.float64, seed=8)
+    lat, text = _inputs(cfg)
+    x = patchify(lat)
+    t = torch.tensor([500.0], dtype=torch.float64)
+    dense = m(x, t, m.prepare_context(text), grid=(3, 4, 6))
+    tp = make_tensor_parallel(par_cfg, dev, transport="nccl")
+    sp = make_sequence_parallel(par_cfg, dev, transport="nccl")
+    m2 = WanTransformer(cfg, shard_wan_weights(cfg, m.w, tp.world, tp.rank))
+    m2.tp, m2.par = tp, sp
+    out = sp.gather_tokens(m2(sp.shard_tokens(x), t, m2.prepare_context(text), grid=(3, 4, 6)))
+    return (out - dense).abs().max().item()
+
+
+@pytest.mark.multirank
+@pytest.mark.parametrize("mode", ["ulysses", "ring"])
+def test_wan_context_parallel_inside_tensor_parallel(mode):
+    """tp2 x cp2 over gloo ranks: heads / FFN columns over tp (across-heads q/k RMS summed over
+    tp), the sequence over cp (Ulysses splits each tp rank's heads again)."""
+    from difflet_b200.parallel.testing import run_ranks
+
+    assert max(run_ranks(_cp_tp, 4, mode, timeout=300)) < 1e-10
