@@ -37,9 +37,14 @@ def load_requests(path: str) -> list[dict]:
     return [json.loads(l) for l in Path(path).read_text().splitlines() if l.strip()]
 
 
-def worker_loop(requests: list[dict], work: Path, generate_one) -> int:
+def worker_loop(requests: list[dict], work: Path, generate_one, replica: tuple | None = None) -> int:
+    """Run the requests this worker gets: by claim (first free worker takes the next request), or
+    with ``replica`` = (r, dp) statically every dp-th request starting at r (still claimed, so
+    a rerun skips what is done)."""
     failures = 0
     for i, req in enumerate(requests):
+        if replica is not None and i % replica[1] != replica[0]:
+            continue
         if not try_claim(work, i):
             continue
         try:
@@ -51,8 +56,9 @@ def worker_loop(requests: list[dict], work: Path, generate_one) -> int:
     return failures
 
 
-def run_router(argv_worker: list[str], dp: int, gpus_per_replica: int, work: str) -> int:
-    """Spawn ``dp`` worker processes of ``python -m difflet_b200 <argv_worker>`` on disjoint GPUs."""
+def run_router(argv_worker: list[str], dp: int, gpus_per_replica: int, work: str, schedule: str = "claim") -> int:
+    """Spawn ``dp`` worker processes of ``python -m difflet_b200 <argv_worker>`` on disjoint GPUs
+    (``schedule``: claim or static, see ``worker_loop``)."""
     Path(work).mkdir(parents=True, exist_ok=True)
     procs = []
     for r in range(dp):

@@ -22,14 +22,17 @@ def _add_common(p: argparse.ArgumentParser) -> None:
     p.add_argument("--model-id", required=True)
     p.add_argument("--revision", default=None)
     p.add_argument("--backend", default=None, choices=[None, "cuda", "cpu"])
-    p.add_argument("--tp-degree", type=int, default=1)
-    p.add_argument("--cp-degree", type=int, default=1)
+    p.add_argument("--tp-degree", type=int, default=None)
+    p.add_argument("--cp-degree", type=int, default=None)
     p.add_argument("--cp-mode", default=None, choices=[None, "gather_kv", "ring", "ulysses"])
     p.add_argument("--cfg-parallel", action="store_true")
     p.add_argument("--sp", action="store_true")
-    p.add_argument("--dp", type=int, default=1)
-    p.add_argument("--dp-schedule", default="claim", choices=["claim", "static"])
-    p.add_argument("--mode", default=None, choices=[None, "latency", "throughput", "mixed"])
+    p.add_argument("--dp", type=int, default=None)
+    p.add_argument("--dp-schedule", default="claim", choices=["claim", "static"],
+                   help="--dp batches: replicas claim requests as they free up (claim), or replica r takes "
+                        "requests r, r + dp, ... (static)")
+    p.add_argument("--mode", default=None, choices=[None, "latency", "throughput", "mixed"],
+                   help="parallel layout preset for this node's GPUs (explicit parallel flags win)")
     p.add_argument("--height", type=int, default=None)
     p.add_argument("--width", type=int, default=None)
     p.add_argument("--num-frames", type=int, default=None)
@@ -45,8 +48,8 @@ def _add_common(p: argparse.ArgumentParser) -> None:
     p.add_argument("--teacache-calibration", default=None)
     p.add_argument("--teacache-online-delta", type=float, default=None)
     p.add_argument("--torch-compile", action="store_true", help="accepted for compatibility (no-op: native kernels)")
-    p.add_argument("--host-vae", action="store_true")
-    p.add_argument("--device-vae", action="store_true")
+    p.add_argument("--host-vae", action="store_true", help="decode on the host CPU in fp32 (frees device memory)")
+    p.add_argument("--device-vae", action="store_true", help="decode on the GPU (the default)")
 
 
 def _add_gen(p: argparse.ArgumentParser) -> None:
@@ -60,7 +63,8 @@ def _add_gen(p: argparse.ArgumentParser) -> None:
     p.add_argument("--output", default="output")
     p.add_argument("--requests", default=None, help="JSONL batch of requests")
     p.add_argument("--work-dir", default=None)
-    p.add_argument("--keep-work-dir", action="store_true")
+    p.add_argument("--keep-work-dir", action="store_true",
+                   help="keep a --dp batch's claim / result directory after a successful run")
 
 
 def build_parser() -> argparse.ArgumentParser:
@@ -76,7 +80,7 @@ def build_parser() -> argparse.ArgumentParser:
     _add_gen(r)
     pl = sub.add_parser("plan", help="rank parallel configurations for a model on this machine")
     pl.add_argument("--model-id", required=True)
-    pl.add_argument("--gpus", type=int, default=8)
+    pl.add_argument("--gpus", type=int, default=None, help="GPU count (default: detected through NVML, else 8)")
     pl.add_argument("--height", type=int, default=None)
     pl.add_argument("--width", type=int, default=None)
     pl.add_argument("--num-frames", type=int, default=None)
@@ -87,11 +91,18 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--host", default="127.0.0.1")
     s.add_argument("--port", type=int, default=8000)
     s.add_argument("--api-key", default=None)
-    s.add_argument("--dp-degree", type=int, default=1)
+    s.add_argument("--dp-degree", type=int, default=None)
     s.add_argument("--max-queued-requests", type=int, default=8, help="waiting requests per replica before HTTP 429")
     s.add_argument("--queue-timeout", type=float, default=None, help="seconds a request may wait for its replica")
     s.add_argument("--request-timeout", type=float, default=600.0, help="seconds before a request is cancelled")
     s.add_argument("--heartbeat-interval", type=float, default=None, help="worker heartbeat period (s)")
+    q = sub.add_parser("quant", help="write the MXFP8 checkpoint of a model (or print its plan)")
+    q.add_argument("--model-id", required=True)
+    q.add_argument("--revision", default=None)
+    q.add_argument("--cache-dir", default=None)
+    q.add_argument("--out", default=None, help="output directory (default: under the cache dir)")
+    q.add_argument("--random-weights", action="store_true", help="plan only, from the architecture's shapes")
+    q.add_argument("--json", action="store_true")
     c = sub.add_parser("cache", help="inspect the artefact cache")
     c.add_argument("--cache-dir", default=None)
     c.add_argument("--json", action="store_true")
@@ -112,8 +123,9 @@ def build_parser() -> argparse.ArgumentParser:
 def parallel_from_args(a):
     from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
 
-    cp_mode = a.cp_mode or ("ulysses" if a.cp_degree > 1 else "gather_kv")
-    return DiffletParallelConfig(tp_degree=a.tp_degree, cp_degree=a.cp_degree, cfg_parallel_enabled=a.cfg_parallel,
+    tp, cp = a.tp_degree or 1, a.cp_degree or 1
+    cp_mode = a.cp_mode or ("ulysses" if cp > 1 else "gather_kv")
+    return DiffletParallelConfig(tp_degree=tp, cp_degree=cp, cfg_parallel_enabled=a.cfg_parallel,
                                  cp_mode=cp_mode, sp_enabled=a.sp, dp_degree=1)
 
 
@@ -126,6 +138,8 @@ def _app_kwargs(a) -> dict:
     if a.quant:
         kw["quant"] = a.quant
         kw["quant_compute"] = a.quant_compute
+    if getattr(a, "host_vae", False):
+        kw["host_vae"] = True
     for k in ("teacache_cadence", "teacache_speedup", "teacache_calibration", "teacache_online_delta"):
         v = getattr(a, k, None)
         if v is not None:
@@ -200,15 +214,21 @@ def cmd_generate(a) -> int:
         print(f"difflet: {e}", file=sys.stderr)
         return 2
     world = _world_needed(a)
-    if world > 1 and not os.environ.get("DIFFLET_UNDER_TORCHRUN"):
-        from difflet_b200.cli.runner import run_torchrun
-
-        return run_torchrun(sys.argv[1:], world)
     if a.dp > 1 and a.requests and not os.environ.get("DIFFLET_DP_RANK"):
         from difflet_b200.cli.dp import run_router
 
         work = a.work_dir or (a.output + ".work")
-        return run_router(sys.argv[1:], a.dp, world, work)
+        rc = run_router(sys.argv[1:], a.dp, world, work, schedule=a.dp_schedule)
+        if rc == 0 and not a.keep_work_dir:
+            shutil.rmtree(work, ignore_errors=True)
+        return rc
+    if world > 1 and not os.environ.get("DIFFLET_UNDER_TORCHRUN"):
+        from difflet_b200.cli.runner import run_torchrun
+
+        return run_torchrun(sys.argv[1:], world)
+    from difflet_b200.cli.prewarm import prewarm_cuda
+
+    prewarm_cuda()  # the CUDA context comes up while the weights load
     pipe = _pipeline(a)
     entry = pipe.model_entry
     outputs = []
@@ -222,7 +242,9 @@ def cmd_generate(a) -> int:
             out = pipe(**_gen_kwargs(a, req))
             return save_result(out, req.get("output", f"{a.output}_{i}"), entry)
 
-        fails = worker_loop(load_requests(a.requests), work, one)
+        dp_rank = int(os.environ.get("DIFFLET_DP_RANK", "0"))
+        fails = worker_loop(load_requests(a.requests), work, one,
+                            replica=(dp_rank, a.dp) if a.dp_schedule == "static" else None)
         return 1 if fails else 0
     t0 = time.time()
     out = pipe(**_gen_kwargs(a))
@@ -265,6 +287,11 @@ def cmd_clean(a) -> int:
 def cmd_plan(a) -> int:
     from difflet_b200.planner import plan
 
+    if a.gpus is None:
+        from difflet_b200.planner.hardware import detect
+
+        hw = detect()
+        a.gpus = hw.gpus or 8
     res = plan(a.model_id, gpus=a.gpus, height=a.height, width=a.width, num_frames=a.num_frames)
     res = res[: a.top]
     if a.json:
@@ -273,6 +300,58 @@ def cmd_plan(a) -> int:
         for r in res:
             print(f"{r['est_step_ms']:9.1f} ms  world={r['world']}  {r['parallel']}")
     return 0
+
+
+def cmd_quant(a) -> int:
+    """MXFP8 checkpoint of a model: which linears are quantized (the model's default targets, or
+    DIFFLET_QUANT_TARGETS), written once under the cache dir (or --out) and reused by
+    ``--quant mxfp8`` loads."""
+    from difflet_b200 import envs
+    from difflet_b200.quant import checkpoint as QC
+    from difflet_b200.quant.targets import default_spec
+    from difflet_b200.registry import resolve_model
+
+    entry = resolve_model(a.model_id)
+    spec = default_spec(entry.name)
+    if a.random_weights:
+        info = _quant_plan_from_shapes(entry)
+        print(json.dumps(info, indent=1) if a.json else
+              f"{entry.name}: {len(info['targets'])} of {info['linears']} linears in MXFP8, "
+              f"{len(info['mxfp8_fused_weights'])} fused engine weights")
+        return 0
+    from difflet_b200.pipeline.path_resolver import resolve_model_path
+
+    model_dir = resolve_model_path(a.model_id, revision=a.revision, allow_patterns=entry.download_patterns)
+    src = Path(model_dir) / "transformer" if (Path(model_dir) / "transformer").is_dir() else Path(model_dir)
+    out = QC.write_quantized_dir(src, a.out, spec) if a.out else \
+        QC.ensure_quantized_dir(a.cache_dir or envs.DIFFLET_COMPILE_CACHE, src, spec)
+    man = QC.read_manifest(out)
+    print(json.dumps({"quantized": str(out), "counts": man["counts"], "digest": man["digest"]}))
+    return 0
+
+
+def _quant_plan_from_shapes(entry) -> dict:
+    """Which diffusers linears of the architecture the model's MXFP8 spec quantizes, and which
+    fused engine weights that makes MXFP8 (all their parts targeted) -- no weights needed."""
+    from difflet_b200.quant import apply as QA
+    from difflet_b200.quant.targets import default_spec
+
+    spec = default_spec(entry.name)
+    if entry.name == "wan":
+        from difflet_b200.models.wan.model import get_wan_config
+
+        parts = QA.wan_fused_parts(get_wan_config("wan2.2-t2v-a14b"))
+    else:
+        from difflet_b200.models.mmdit import get_config
+
+        preset = {"flux": "flux-dev", "hunyuan_video": "hunyuan-video", "qwen_image": "qwen-image"}.get(entry.name)
+        if preset is None:
+            raise SystemExit(f"difflet quant: no architecture plan for {entry.name!r}; give a checkpoint instead")
+        parts = QA.mmdit_fused_parts(get_config(preset))
+    linears = sorted({n for names in parts.values() for n in names})
+    targets = [n for n in linears if spec.matches(n)]
+    fused = [k for k, names in parts.items() if all(spec.matches(n) for n in names)]
+    return {"model": entry.name, "linears": len(linears), "targets": targets, "mxfp8_fused_weights": fused}
 
 
 def cmd_serve(a) -> int:
@@ -313,6 +392,13 @@ def cmd_bench(a) -> int:
 
 def main(argv=None) -> int:
     a = build_parser().parse_args(argv)
+    if hasattr(a, "tp_degree"):
+        if getattr(a, "host_vae", False) and getattr(a, "device_vae", False):
+            print("difflet: --host-vae and --device-vae exclude each other", file=sys.stderr)
+            return 2
+        from difflet_b200.cli.modes import apply_mode
+
+        apply_mode(a)
     if a.cmd == "download":
         from difflet_b200.pipeline.path_resolver import resolve_model_path
         from difflet_b200.registry import resolve_model
@@ -327,7 +413,8 @@ def main(argv=None) -> int:
         return 0
     if a.cmd in ("generate", "run"):
         return cmd_generate(a)
-    return {"plan": cmd_plan, "serve": cmd_serve, "cache": cmd_cache, "clean": cmd_clean, "bench": cmd_bench}[a.cmd](a)
+    return {"plan": cmd_plan, "serve": cmd_serve, "cache": cmd_cache, "clean": cmd_clean, "bench": cmd_bench,
+            "quant": cmd_quant}[a.cmd](a)
 
 
 if __name__ == "__main__":

@@ -89,6 +89,10 @@ class FluxEngine:
             dit = FluxTransformer(self.cfg, w)
             vsd = load_component(self.model_path, "vae", dtype=self.dtype, device=dev)
             vae = KLDecoder(KLDecoderConfig(), vsd)
+        if self.kw.get("host_vae"):  # decode on the host CPU in fp32 (frees the decoder's device memory)
+            from difflet_b200.utils.host_vae import move_to_host
+
+            move_to_host(vae)
         dit.tp = tp
         if self.parallel.world_size > 1:
             from difflet_b200.parallel.ulysses import make_sequence_parallel

@@ -187,7 +187,9 @@ class FluxApplication:
             raise RuntimeError("no VAE loaded; use output_type='latent'")
         if par is not None and par.rank != 0 and not par.decode_on_all_ranks:
             return None
-        img = self.vae.decode(lat)
+        from difflet_b200.utils.host_vae import for_vae
+
+        img = self.vae.decode(for_vae(self.vae, lat))
         if output_type == "float":
             return img
         from difflet_b200.models.vae.autoencoder_kl import to_uint8

@@ -52,6 +52,10 @@ class WanEngine:
             experts = [WanTransformer.from_diffusers_state_dict(self.wcfg, load_component(self.model_path, c),
                                                                device=dev, dtype=self.dtype) for c in comps]
             vae = WanVAEDecoder(WanVAEConfig(), load_component(self.model_path, "vae", dtype=self.dtype, device=dev))
+        if self.kw.get("host_vae"):  # decode on the host CPU in fp32 (frees the decoder's device memory)
+            from difflet_b200.utils.host_vae import move_to_host
+
+            move_to_host(vae)
         seq_par = cfg_par = None
         if self.parallel.world_size > 1:
             from difflet_b200.parallel.ulysses import make_cfg_parallel, make_sequence_parallel

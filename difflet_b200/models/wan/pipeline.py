@@ -198,6 +198,12 @@ class WanApplication:
         in [-1, 1] (the other ranks None)."""
         import torch.distributed as dist
 
+        from difflet_b200.utils.host_vae import for_vae, vae_device
+
+        if vae_device(self.vae) is not None and vae_device(self.vae).type == "cpu" and lat.is_cuda:  # --host-vae
+            if dist.is_initialized() and dist.get_rank() != 0:
+                return None
+            return self.vae.decode(for_vae(self.vae, lat))
         if dist.is_initialized() and dist.get_world_size() > 1 and hasattr(self.vae, "set_slabs"):
             rows = lat.shape[3]
             if self.vae.slabs is None or self.vae.slabs.rows != rows or self.vae.slabs.world == 1:

@@ -174,3 +174,22 @@ def build_controller(kw: dict, family: str = "flux", num_steps: int = 28) -> Tea
     if kw.get("teacache_online_delta"):
         cal.online_delta_alpha = float(kw["teacache_online_delta"])
     return TeaCacheController(cal)
+
+
+def build_probe_free_controller(*, cadence: int | None = None, online_delta_alpha: float | None = None,
+                                num_steps: int = 0) -> TeaCacheController:
+    """A controller for the modes that need no probe and no calibration file: a fixed cadence
+    (skip decisions by step index) or online-delta (from the noise-prediction trajectory the
+    pipeline already has).  Exactly one of the two.  ``num_steps`` may stay 0: the pipelines set
+    it to the request's step count before denoising, so the cooldown protects the real tail.
+    Reference behaviour: difflet/pipeline/teacache.py:365-405."""
+    cadence = int(cadence or 0)
+    alpha = float(online_delta_alpha or 0.0)
+    if cadence <= 0 and alpha <= 0.0:
+        raise ValueError(f"a probe-free TeaCache needs cadence > 0 or online_delta_alpha > 0 "
+                         f"(got {cadence}, {alpha})")
+    if cadence > 0 and alpha > 0.0:
+        raise ValueError("cadence and online_delta_alpha exclude each other")
+    cal = TeaCacheCalibration(accumulate=False, num_steps=num_steps, cadence=cadence, online_delta_alpha=alpha,
+                              coefficients=[0.0], threshold=0.0)
+    return TeaCacheController(cal)

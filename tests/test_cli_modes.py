@@ -1,0 +1,79 @@
+"""CLI presets and flags: --mode layouts per model class and GPU count, explicit flags winning,
+--host-vae decode on the host, --dp-schedule static assignment, difflet quant plans."""
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+from difflet_b200.cli.main import build_parser
+from difflet_b200.cli.modes import apply_mode, preset
+
+
+def test_presets_by_model_class():
+    flux, wan = "black-forest-labs/FLUX.1-dev", "Wan-AI/Wan2.2-T2V-A14B-Diffusers"
+    assert preset(flux, "latency", 8) == preset(flux, "latency", 8).__class__(1, False, 8, "ulysses")
+    p = preset(wan, "latency", 8)
+    assert (p.dp, p.cfg_parallel, p.cp_degree) == (1, True, 4)  # 40 heads: cp 4
+    p = preset(wan, "mixed", 8)
+    assert (p.dp, p.cfg_parallel, p.cp_degree) == (2, True, 2)
+    p = preset(flux, "throughput", 8)
+    assert (p.dp, p.cfg_parallel, p.cp_degree) == (8, False, 1)
+    p = preset(flux, "latency", 5)  # 24 heads: the largest cp dividing both
+    assert p.cp_degree == 1 or 24 % p.cp_degree == 0
+
+
+def test_explicit_flags_win_over_the_mode():
+    a = build_parser().parse_args(["generate", "--model-id", "Wan-AI/Wan2.2-T2V-A14B-Diffusers", "--mode", "latency",
+                                   "--cp-degree", "2"])
+    apply_mode(a, gpus=8)
+    assert a.cp_degree == 2 and a.cfg_parallel and a.dp == 1 and a.tp_degree == 1
+    b = build_parser().parse_args(["generate", "--model-id", "black-forest-labs/FLUX.1-dev"])
+    apply_mode(b, gpus=8)
+    assert (b.dp, b.cp_degree, b.tp_degree) == (1, 1, 1)
+
+
+def test_host_vae_decodes_on_cpu(tmp_path, monkeypatch):
+    from difflet_b200.models.vae.autoencoder_kl import KLDecoder, KLDecoderConfig
+    from difflet_b200.utils.host_vae import for_vae, move_to_host, vae_device
+
+    vae = KLDecoder.random_init(KLDecoderConfig(block_out_channels=(32, 32, 32, 32)), dtype=torch.bfloat16)
+    move_to_host(vae)
+    assert vae_device(vae).type == "cpu" and next(iter(vae.w.values())).dtype == torch.float32
+    z = for_vae(vae, torch.randn(1, 16, 4, 4, dtype=torch.bfloat16))
+    assert z.dtype == torch.float32 and vae.decode(z).shape == (1, 3, 32, 32)
+
+
+def test_dp_static_schedule(tmp_path):
+    from difflet_b200.cli.dp import worker_loop
+
+    reqs = [{"i": i} for i in range(7)]
+    got = {0: [], 1: []}
+    for r in (0, 1):
+        worker_loop(reqs, tmp_path, lambda req, i, r=r: got[r].append(i) or "ok", replica=(r, 2))
+    assert got == {0: [0, 2, 4, 6], 1: [1, 3, 5]}
+    assert sorted(p.name for p in Path(tmp_path).glob("*.done")) == sorted(f"{i}.done" for i in range(7))
+
+
+def test_quant_plan_command():
+    r = subprocess.run([sys.executable, "-m", "difflet_b200", "quant", "--model-id", "black-forest-labs/FLUX.1-dev",
+                        "--random-weights", "--json"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    info = json.loads(r.stdout)
+    assert info["model"] == "flux" and info["targets"] and info["mxfp8_fused_weights"]
+    assert all("norm" not in t for t in info["targets"])
+
+
+def test_host_and_device_vae_exclusive():
+    from difflet_b200.cli.main import main
+
+    assert main(["generate", "--model-id", "black-forest-labs/FLUX.1-dev", "--host-vae", "--device-vae"]) == 2
+
+
+@pytest.mark.parametrize("flag", ["--keep-work-dir"])
+def test_work_dir_flag_parses(flag):
+    a = build_parser().parse_args(["generate", "--model-id", "x", flag])
+    assert a.keep_work_dir

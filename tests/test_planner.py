@@ -40,3 +40,51 @@ def test_flux_estimates_track_measured_steps(monkeypatch):
         p = DiffletParallelConfig(cp_degree=n, cp_mode="ulysses") if n > 1 else DiffletParallelConfig()
         est_ms = P.estimate_step_s(e, p, shape, 1397.4e12) * 1e3
         assert abs(est_ms - measured_ms) / measured_ms < 0.2, (n, est_ms, measured_ms)
+
+
+class _FakeNVML:
+    """A stand-in for pynvml: 8 GPUs of 183,359 MiB with 18 active NVLinks each."""
+
+    NVML_NVLINK_MAX_LINKS = 18
+
+    def __init__(self, n=8, links=18):
+        self.n, self.links, self.calls = n, links, []
+
+    def nvmlInit(self):
+        self.calls.append("init")
+
+    def nvmlShutdown(self):
+        self.calls.append("shutdown")
+
+    def nvmlDeviceGetCount(self):
+        return self.n
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return i
+
+    def nvmlDeviceGetName(self, h):
+        return b"NVIDIA B200"
+
+    def nvmlDeviceGetMemoryInfo(self, h):
+        class M:
+            total = 183359 * 2**20
+        return M()
+
+    def nvmlDeviceGetNvLinkState(self, h, link):
+        return 1 if link < self.links else 0
+
+
+def test_hardware_detection_reads_nvml_only():
+    from difflet_b200.planner.hardware import detect
+
+    fake = _FakeNVML()
+    hw = detect(fake)
+    assert (hw.gpus, hw.sku, hw.nvlink, hw.nvlink_links, hw.source) == (8, "NVIDIA B200", True, 18, "nvml")
+    assert abs(hw.hbm_gb - 179.1) < 0.2
+    assert fake.calls == ["init", "shutdown"]  # queries only: no setter exists on the fake
+
+    class Broken:
+        def nvmlInit(self):
+            raise OSError("no driver")
+
+    assert detect(Broken()).source == "none"

@@ -54,3 +54,39 @@ def test_flux_pipeline_with_teacache_runs_fewer_steps():
     app.teacache = build_controller({"teacache_cadence": 2})
     out = app.generate(prompt="x", height=64, width=64, num_inference_steps=8, output_type="latent")
     assert torch.isfinite(out).all() and app.teacache.skipped_steps >= 2
+
+
+def test_run_gate_picks_a_method_and_calibrates():
+    """run_gate on a synthetic trajectory: a probe proportional to the output change -> adaptive
+    with a fitted polynomial; no probe and smooth changes -> online-delta."""
+    import torch
+
+    from difflet_b200.pipeline.teacache_gate import run_gate
+
+    g = torch.Generator().manual_seed(0)
+    scales = [1.0 + 0.5 * i + 0.05 * float(torch.rand(1, generator=g)) for i in range(12)]
+
+    def step(i, lat):
+        return lat * scales[i], lat * (scales[i] ** 0.5)
+
+    cal, summ = run_gate(family="flux", num_steps=12, init_latent=lambda: torch.ones(64),
+                         step_fn=step, advance_fn=lambda lat, out, i: lat)
+    assert summ["method"] == "adaptive" and summ["n_pairs"] == 11
+    assert cal.accumulate and len(cal.coefficients) >= 2
+    cal2, summ2 = run_gate(family="flux", num_steps=12, init_latent=lambda: torch.ones(64),
+                           step_fn=lambda i, lat: (lat * (1 + 0.1 * i), None), advance_fn=lambda lat, out, i: lat)
+    assert summ2["probe_pearson"] is None and summ2["method"] in ("online_delta", "cadence")
+    assert (cal2.online_delta_alpha > 0) != (cal2.cadence > 0)
+
+
+def test_probe_free_controller():
+    import pytest
+
+    from difflet_b200.pipeline.teacache import build_probe_free_controller
+
+    c = build_probe_free_controller(cadence=2)
+    assert c.cal.cadence == 2 and not c.needs_probe()
+    with pytest.raises(ValueError):
+        build_probe_free_controller()
+    with pytest.raises(ValueError):
+        build_probe_free_controller(cadence=2, online_delta_alpha=0.3)
