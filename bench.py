@@ -271,6 +271,117 @@ def run_wan(args, world, rank):
     return 0
 
 
+def run_mmdit(args, world, rank):
+    """BASELINE config 4 (HunyuanVideo 13B, 720x1280x129, 118,800 image tokens, embedded guidance,
+    ring-attention CP over N) or config 5 (Qwen-Image 20B, 1328^2 = 6,889 tokens, MXFP8 block
+    linears, true CFG 4.0 batched on one GPU / CFG-parallel pairs, TP over the rest).
+
+    ``value``: one DiT denoise step (every CFG branch, guidance combine, Euler update), device-timed
+    over K steps after W warm-up steps, max over ranks.  Weights (26 / 40 GB) and activations
+    stream through HBM every step (far above L2).  ``--layout`` overrides the default by N."""
+    import torch
+
+    from difflet_b200 import _native
+    from difflet_b200.bench.clocks import ClockSampler
+    from difflet_b200.models.mmdit.model import pack_latents
+    from difflet_b200.ops import fused as F
+    from difflet_b200.pipeline.difflet_pipeline import DiffletPipeline
+
+    hv = args.model == "hunyuan"
+    default = ({1: "single"}.get(world, f"ring{world}") if hv else {1: "single"}.get(world, f"tp{world}"))
+    par, layout = wan_layout(world, args.layout or default)
+    if hv:
+        Fr = 129 if args.frames == 81 else args.frames  # config 4: 129 frames (the Wan default is 81)
+        model_id, H, W, steps_total, text_len = "hunyuanvideo-community/HunyuanVideo", 720, 1280, 50, 256
+        kw = {}
+    else:
+        model_id, H, W, Fr, steps_total, text_len = "Qwen/Qwen-Image", 1328, 1328, None, 50, 256
+        kw = {"quant": "mxfp8"} if args.quant != "none" else {}
+    t_load = time.time()
+    pipe = DiffletPipeline.from_pretrained(model_id, parallel=par, height=H, width=W, num_frames=Fr, random_init=True,
+                                           skip_warmup=True, application_kwargs=kw)
+    load_s = time.time() - t_load
+    app = pipe.app.app
+    cfg, dit, dev, dt = app.cfg, app.dit, app.device, app.dit.dtype
+    gen = torch.Generator().manual_seed(21)
+    lh, lw = H // cfg.vae_scale, W // cfg.vae_scale
+    T = (Fr - 1) // cfg.vae_scale_t + 1 if hv else 1
+    grid = (T // cfg.patch_t, lh // cfg.patch, lw // cfg.patch)
+    S_img = grid[0] * grid[1] * grid[2]
+    lat = torch.randn(1, cfg.latent_channels, *((T, lh, lw) if hv else (lh, lw)), generator=gen)
+    x32 = pack_latents(lat.to(dev), cfg.patch).contiguous()
+    true_cfg = not hv
+    cfg_par = app.cfg_par if true_cfg else None
+    nb = 2 if (true_cfg and cfg_par is None) else 1
+    txt = torch.randn(nb, text_len, cfg.text_dim, generator=gen).to(dev, dt)
+    pool = torch.randn(nb, cfg.pooled_dim, generator=gen).to(dev) if cfg.pooled_dim else None
+    tv = torch.full((nb,), text_len, dtype=torch.int32, device=dev) if hv else None
+    par_seq = dit.par
+    if par_seq is not None:
+        x32 = par_seq.shard_tokens(x32).contiguous()
+        if not cfg.refiner_layers:
+            txt = par_seq.shard_tokens(txt).contiguous()
+    x16 = torch.empty((nb,) + tuple(x32.shape[1:]), device=dev, dtype=dt)
+    tvec = torch.full((nb,), 0.8, device=dev)
+    gvec = torch.full((nb,), 6.0, device=dev)
+    scale, dt_step = 4.0, -1.0 / steps_total
+
+    def one_step():
+        x16[:1].copy_(x32)
+        if nb == 2:
+            x16[1:].copy_(x16[:1])
+        v = dit(x16, txt, pool, tvec, gvec, grid=grid, txt_valid=tv)
+        if cfg_par is not None:
+            v32 = cfg_par.combine(v, scale)
+        elif nb == 2:
+            u, c = v[:1].float(), v[1:].float()
+            v32 = u + scale * (c - u)
+            v32 = v32 * (c.norm(dim=-1, keepdim=True) / v32.norm(dim=-1, keepdim=True).clamp_min(1e-12))
+        else:
+            v32 = v.float()
+        x32.add_(v32, alpha=dt_step)
+
+    _log(f"{model_id}: {S_img} image tokens, layout {layout}, loaded in {load_s:.1f}s; warming up")
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    n0 = _launch_count()
+    one_step()
+    launches = _launch_count() - n0
+    _barrier(world)
+    sampler = ClockSampler(_gpu_ids(world) if rank == 0 else [])
+    with sampler:
+        _barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            one_step()
+        b.record()
+        _barrier(world)
+    ms = _max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    _native.check_device_errors()
+    del F
+    if rank == 0:
+        name = "HunyuanVideo 720x1280x129" if hv else "Qwen-Image 1328x1328 " + ("MXFP8" if kw else "bf16")
+        print(json.dumps({
+            "metric": f"{name} DiT denoise step latency (max over ranks)", "value": round(ms, 2), "unit": "ms/step",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" + (" + mxfp8 block linears" if kw else ""),
+            "data": "synthetic (random-init weights of the named architecture, N(0,1) text states / latents)",
+            "config": {"model": model_id, "global_batch": 1, "seq_len": S_img + text_len, "height": H, "width": W,
+                       "frames": Fr, "true_cfg": true_cfg, "parallelism": layout, "load_s": round(load_s, 1),
+                       "l2": "weights + activations stream from HBM every step; no flush"},
+            "clocks": sampler.summary(), "gpu_launches": int(launches * args.steps), "e2e": None}), flush=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def _launch_count() -> int:
     from difflet_b200.ops import fused as F
 
@@ -303,10 +414,11 @@ def main(argv=None):
     ap.add_argument("--tp", type=int, default=1,
                     help="with a context-parallel --cp-mode: tensor-parallel degree inside each cp group "
                          "(heads / MLP columns over tp, the sequence over the remaining N / tp ranks)")
-    ap.add_argument("--quant", default=None, choices=[None, "mxfp8"],
+    ap.add_argument("--quant", default=None, choices=[None, "mxfp8", "none"],
                     help="MXFP8 block linears (default targets); the headline number is bf16")
-    ap.add_argument("--model", default="flux", choices=["flux", "wan"],
-                    help="flux: the headline FLUX.1-dev config; wan: Wan2.2-T2V-A14B 720p x 81 frames")
+    ap.add_argument("--model", default="flux", choices=["flux", "wan", "hunyuan", "qwen"],
+                    help="flux: the headline FLUX.1-dev config; wan: Wan2.2-T2V-A14B 720p x 81 frames; "
+                         "hunyuan: HunyuanVideo 720p x 129 frames (ring CP); qwen: Qwen-Image 1328^2 MXFP8 true CFG (TP)")
     ap.add_argument("--layout", default=None,
                     help="wan: parallel layout (default by N: 1 batched CFG, 2 cfg2, 4 cfg2xulysses2, "
                          "8 cfg2xulysses4; also e.g. ulysses8, cfg2xtp2xulysses2)")
@@ -326,6 +438,8 @@ def main(argv=None):
         return run_reference(args, world, rank)
     if args.model == "wan":
         return run_wan(args, world, rank)
+    if args.model in ("hunyuan", "qwen"):
+        return run_mmdit(args, world, rank)
 
     import torch
 

@@ -29,7 +29,8 @@ GEMM_SHAPES = [
     ("wan_ffn_up_sp4", 18900, 13824, 5120),
     ("square_8192", 8192, 8192, 8192),
 ]
-ATTN_CASES = [("flux_1gpu", 1, 24, 4608), ("flux_sp8_heads", 1, 3, 4608), ("wan_ulysses4", 1, 10, 75600 // 4)]
+ATTN_CASES = [("flux_1gpu", 1, 24, 4608), ("flux_sp8_heads", 1, 3, 4608), ("wan_ulysses4", 1, 10, 75600 // 4),
+              ("wan_ulysses4_rank", 1, 10, 75600), ("hunyuan_ulysses8_rank", 1, 3, 118800)]
 LN_CASES = [("flux_ln", 4608, 3072), ("wan_ln_sp4", 18900, 5120)]
 
 
@@ -187,7 +188,12 @@ def bench_conv(nat, iters, flush, peaks, cases, ref):
     return rows
 
 
+ATTN_KEY_TILES = [64]
+
+
 def bench_attn(nat, iters, flush, peaks, cases, ref):
+    """Flash attention at the per-rank shapes of the benchmark configs (each key-tile width in
+    ATTN_KEY_TILES), against torch SDPA (cuDNN on sm_100) with ``ref``."""
     rows = []
     for name, B, H, S in _sel(ATTN_CASES, cases):
         q = torch.randn(B, H, S, 128, device="cuda", dtype=torch.bfloat16)
@@ -195,15 +201,26 @@ def bench_attn(nat, iters, flush, peaks, cases, ref):
         v = torch.randn_like(q)
         o = torch.empty_like(q)
         sc = 1 / math.sqrt(128)
-        t_ours = time_fn(lambda: nat.attention(q, k, v, sc, out=o), iters, flush=flush)
         fl = 4.0 * B * H * S * S * 128
-        r = {"kernel": "attn_tcgen05", "shape": name, "B": B, "H": H, "S": S, "ms": round(t_ours, 4),
-             "tflops": round(fl / t_ours / 1e9, 1),
-             "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3)}
+        it = max(2, min(iters, int(2e14 / fl)))  # long sequences: fewer repeats
+        r = {"kernel": "attn_tcgen05", "shape": name, "B": B, "H": H, "S": S}
+        for kt in ATTN_KEY_TILES:
+            nat.attention_set_key_tile(kt)
+            t_ours = time_fn(lambda: nat.attention(q, k, v, sc, out=o), it, flush=flush)
+            r[f"keys{kt}_ms"] = round(t_ours, 4)
+            r[f"keys{kt}_tflops"] = round(fl / t_ours / 1e9, 1)
+        from difflet_b200 import envs
+
+        nat.attention_set_key_tile(envs.DIFFLET_ATTN_KEYS)
+        best = min(r[f"keys{kt}_ms"] for kt in ATTN_KEY_TILES)
+        r.update({"ms": best, "tflops": round(fl / best / 1e9, 1),
+                  "frac_of_measured_peak": round(fl / best / 1e9 / peaks["bf16_tflops"], 3)})
+        t_ours = best
         if ref:
-            t_ref = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=sc), iters,
+            t_ref = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=sc), it,
                             flush=flush)
-            r.update({"sdpa_ms": round(t_ref, 4), "sdpa_tflops": round(fl / t_ref / 1e9, 1)})
+            r.update({"sdpa_ms": round(t_ref, 4), "sdpa_tflops": round(fl / t_ref / 1e9, 1),
+                      "vs_sdpa": round(t_ref / t_ours, 3)})
         rows.append(r)
     return rows
 
@@ -246,7 +263,10 @@ def main(argv=None):
     ap.add_argument("--cases", default="")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-ref", action="store_true")
+    ap.add_argument("--attn-keys", default="64", help="attention key-tile widths to time (comma list of 64 / 128)")
+    ap.add_argument("--out", default=None, help="also write the rows as JSON here")
     args = ap.parse_args(argv)
+    ATTN_KEY_TILES[:] = [int(k) for k in args.attn_keys.split(",") if k]
     from difflet_b200 import _native
     from difflet_b200.ops.fused import _lib
     from difflet_b200.utils.peaks import load_peaks
@@ -275,6 +295,9 @@ def main(argv=None):
     _native.check_device_errors()
     for r in rows:
         print(json.dumps(r))
+    if args.out:
+        with open(args.out, "w") as f:
+            json.dump({"peaks": peaks, "rows": rows}, f, indent=1)
 
 
 if __name__ == "__main__":

@@ -52,7 +52,15 @@ class MiniMaxH3Engine:
                                                                                           "transformer")))
             dit.to(dev, self.dtype)
         dcfg = TINY if self.cfg.in_channels != 24 else MiniMaxDecoderConfig()
-        self.app = MiniMaxH3Application(dit, MiniMaxDecoders.random_init(dcfg, device=dev, dtype=self.dtype))
+        text_encoder = None
+        if self.model_path and not self.kw.get("random_init") and self.kw.get("load_text_encoder", True):
+            from difflet_b200.models.text_encoders import load_text_encoder
+
+            # Qwen3-VL's language model read at hidden_states[50] (the released model's conditioning)
+            text_encoder = load_text_encoder("minimax_h3", self.model_path, dev, self.dtype,
+                                             text_len=self.kw.get("text_len", 128))
+        self.app = MiniMaxH3Application(dit, MiniMaxDecoders.random_init(dcfg, device=dev, dtype=self.dtype),
+                                        text_encoder=text_encoder)
 
     def generate(self, **kw):
         for k, v in self.default_shape.items():

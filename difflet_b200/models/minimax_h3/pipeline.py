@@ -39,7 +39,11 @@ class MiniMaxH3Application:
         dev, dt = dit.device, dit.dtype
         num_frames = L.align_num_frames(num_frames)
         emb, _ = self.text_encoder([prompt])
-        n_text = max(1, min(self.text_len, len(prompt.split()) * 2 + 1))
+        valid = getattr(self.text_encoder, "last_valid", None)
+        if valid is not None:  # a real tokenizer's count of this prompt's tokens
+            n_text = max(1, min(self.text_len, int(valid[0])))
+        else:  # synthetic stand-in: a word-count estimate
+            n_text = max(1, min(self.text_len, len(prompt.split()) * 2 + 1))
         text = emb[:, :n_text]
         keyframes = list(keyframes or [])
         anchors = tuple(keyframe_anchors)

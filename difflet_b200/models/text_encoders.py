@@ -19,6 +19,13 @@ call signature of the synthetic stand-in (``SyntheticTextEncoder``): ``enc(promp
   positions are removed and the rest is padded / cut to ``max_len``; optional CLIP pooled
   vector (HunyuanVideo).
 
+* ``LayerStateEncoder``: a decoder LM read at one inner hidden state (MiniMax-H3: Qwen3-VL-32B's
+  language model, ``hidden_states[50]`` = the raw output of decoder layer 49, before any later
+  layer and without the final norm).  Only the layers up to that one are built and loaded; the
+  prompt is tokenised without special tokens, right-padded (causal attention: valid rows never
+  see the padding) and the padding rows are zeroed; the valid token count comes back as
+  ``last_valid``.
+
 ``load_text_encoder(family, model_path, ...)`` returns the family's encoder, or None when the
 checkpoint has no encoder folders (the caller keeps the synthetic stand-in).
 """
@@ -149,6 +156,99 @@ class DecoderLMTextEncoder:
         return out, pooled
 
 
+class LayerStateEncoder:
+    """``enc(prompts) -> ([B, seq_len, hidden] with zero padding rows, None)``; ``last_valid`` holds
+    the per-prompt valid token counts of the last call."""
+
+    def __init__(self, model_path, device, dtype=torch.bfloat16, *, layer: int = 50, seq_len: int = 512,
+                 lm_subdir: str = "text_encoder", tok_subdir: str = "tokenizer", weight_prefix: str | None = None):
+        import json
+
+        from safetensors import safe_open
+        from transformers import AutoConfig
+
+        root = str(model_path)
+        enc_dir = os.path.join(root, lm_subdir)
+        conf = AutoConfig.from_pretrained(enc_dir)
+        text_conf = getattr(conf, "text_config", conf)
+        if int(text_conf.num_hidden_layers) < layer:
+            raise ValueError(f"the encoder has {text_conf.num_hidden_layers} layers; hidden_states[{layer}] needed")
+        text_conf.num_hidden_layers = layer  # hidden_states[layer] is the output of layer index layer - 1
+        if getattr(text_conf, "pad_token_id", None) is None:
+            text_conf.pad_token_id = 0
+        text_conf._attn_implementation = "sdpa"
+        model_cls = _text_model_class(text_conf)
+        with torch.device("meta"):
+            model = model_cls(text_conf)
+        files = sorted(f for f in os.listdir(enc_dir) if f.endswith(".safetensors"))
+        idx = os.path.join(enc_dir, "model.safetensors.index.json")
+        if os.path.exists(idx):
+            files = sorted(set(json.load(open(idx))["weight_map"].values()))
+        state = {}
+        for f in files:
+            with safe_open(os.path.join(enc_dir, f), framework="pt") as fh:
+                for key in fh.keys():
+                    name = _strip_lm_prefix(key, weight_prefix)
+                    if name is None:
+                        continue
+                    if name.startswith("layers.") and int(name.split(".")[1]) >= layer:
+                        continue
+                    state[name] = fh.get_tensor(key).to(dtype)
+        missing, unexpected = model.load_state_dict(state, strict=False, assign=True)
+        missing = [m for m in missing if not m.endswith("inv_freq")]
+        if missing or unexpected:
+            raise RuntimeError(f"text encoder load: missing {missing[:4]}, unexpected {unexpected[:4]}")
+        for name, buf in list(model.named_buffers()):
+            if buf.is_meta:  # rotary tables: rebuilt for real from the config
+                model.rotary_emb = type(model.rotary_emb)(config=text_conf)
+                break
+        self.model = model.to(device).eval().requires_grad_(False)
+        self.tok = _tokenizer(os.path.join(root, tok_subdir))
+        if self.tok.pad_token_id is None:
+            self.tok.pad_token = self.tok.eos_token
+        self.device, self.dtype, self.layer, self.seq_len = torch.device(device), dtype, layer, seq_len
+        self.last_valid = None
+
+    @torch.no_grad()
+    def __call__(self, prompts: list[str]):
+        t = self.tok(list(prompts), add_special_tokens=False, padding="max_length", max_length=self.seq_len,
+                     truncation=True, return_attention_mask=True, return_tensors="pt")
+        ids, mask = t.input_ids.to(self.device), t.attention_mask.to(self.device)
+        captured = []
+        hook = self.model.layers[self.layer - 1].register_forward_hook(
+            lambda mod, args, out: captured.append(out[0] if isinstance(out, tuple) else out))
+        try:
+            pos = torch.arange(ids.shape[1], device=self.device)[None].expand(ids.shape[0], -1)
+            self.model(input_ids=ids, attention_mask=mask, position_ids=pos, use_cache=False)
+        finally:
+            hook.remove()
+        h = captured[-1] * mask.unsqueeze(-1).to(captured[-1].dtype)
+        self.last_valid = mask.sum(1).cpu()
+        return h.to(self.dtype), None
+
+
+def _strip_lm_prefix(key: str, prefix: str | None):
+    """The language model's own parameter name of a checkpoint key (None: not a language-model
+    weight, e.g. the vision tower or lm_head)."""
+    for p in ([prefix] if prefix else ["model.language_model.", "language_model.model.", "model.", ""]):
+        if key.startswith(p):
+            rest = key[len(p):]
+            if rest.startswith(("layers.", "embed_tokens.", "norm.")):
+                return rest
+    return None
+
+
+def _text_model_class(text_conf):
+    mt = getattr(text_conf, "model_type", "")
+    if mt.startswith("qwen3_vl"):
+        from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextModel
+
+        return Qwen3VLTextModel
+    from transformers import AutoModel
+
+    return type(AutoModel.from_config(text_conf))
+
+
 def load_text_encoder(family: str, model_path, device, dtype=torch.bfloat16, **kw):
     """The family's encoder from ``model_path`` (diffusers layout), or None without encoder folders."""
     if family == "flux":
@@ -166,8 +266,13 @@ def load_text_encoder(family: str, model_path, device, dtype=torch.bfloat16, **k
         if kw.get("max_len"):  # the pipeline's text length
             spec = dataclasses.replace(spec, max_len=int(kw["max_len"]))
         return DecoderLMTextEncoder(model_path, device, dtype, spec=spec)
+    if family == "minimax_h3":
+        if not _has(model_path, "text_encoder", "tokenizer"):
+            return None
+        return LayerStateEncoder(model_path, device, dtype, layer=int(kw.get("layer", 50)),
+                                 seq_len=int(kw.get("text_len", 512)))
     raise ValueError(f"no text encoder recipe for family {family!r}")
 
 
-__all__ = ["DecoderLMTextEncoder", "FluxTextEncoders", "HUNYUAN_VIDEO_TEMPLATE", "LMTemplate", "QWEN_IMAGE_TEMPLATE",
-           "UMT5TextEncoder", "load_text_encoder"]
+__all__ = ["DecoderLMTextEncoder", "FluxTextEncoders", "HUNYUAN_VIDEO_TEMPLATE", "LMTemplate", "LayerStateEncoder",
+           "QWEN_IMAGE_TEMPLATE", "UMT5TextEncoder", "load_text_encoder"]

@@ -94,3 +94,50 @@ def test_missing_folders_return_none(tmp_path):
     assert TE.load_text_encoder("wan", None, "cpu") is None
     with pytest.raises(ValueError):
         TE.load_text_encoder("nope", tmp_path, "cpu")
+
+
+def _tiny_qwen3vl_checkpoint(root):
+    """A random tiny Qwen3-VL checkpoint folder (text_encoder/ + tokenizer/) built offline."""
+    import json
+    import os
+
+    from safetensors.torch import save_file
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextModel
+
+    words = ["[PAD]", "[EOS]"] + [f"w{i}" for i in range(60)]
+    tk = Tokenizer(models.WordLevel({w: i for i, w in enumerate(words)}, unk_token="[PAD]"))
+    tk.pre_tokenizer = pre_tokenizers.Whitespace()
+    fast = PreTrainedTokenizerFast(tokenizer_object=tk, pad_token="[PAD]", eos_token="[EOS]")
+    fast.save_pretrained(os.path.join(root, "tokenizer"))
+    conf = Qwen3VLConfig(text_config=dict(vocab_size=64, hidden_size=64, intermediate_size=128, num_hidden_layers=6,
+                                          num_attention_heads=4, num_key_value_heads=2, head_dim=16,
+                                          rope_theta=5e6, max_position_embeddings=256, pad_token_id=0))
+    enc = os.path.join(root, "text_encoder")
+    os.makedirs(enc, exist_ok=True)
+    conf.save_pretrained(enc)
+    torch.manual_seed(0)
+    full = Qwen3VLTextModel(conf.text_config).eval()
+    save_file({"model.language_model." + k: v.contiguous() for k, v in full.state_dict().items()
+               if not k.endswith("inv_freq")}, os.path.join(enc, "model.safetensors"))
+    return full, fast
+
+
+def test_layer_state_encoder_reads_the_inner_hidden_state(tmp_path):
+    """Loading only the first `layer` layers and hooking the last one equals the full model's
+    hidden_states[layer] (pre-norm), with the padding rows zeroed and the valid counts reported."""
+    from difflet_b200.models.text_encoders import LayerStateEncoder
+
+    full, tok = _tiny_qwen3vl_checkpoint(str(tmp_path))
+    enc = LayerStateEncoder(tmp_path, "cpu", torch.float32, layer=4, seq_len=12)
+    emb, pooled = enc(["w1 w2 w3", "w5 w6 w7 w8 w9"])
+    assert pooled is None and emb.shape == (2, 12, 64) and enc.last_valid.tolist() == [3, 5]
+    t = tok(["w1 w2 w3", "w5 w6 w7 w8 w9"], add_special_tokens=False, padding="max_length", max_length=12,
+            return_tensors="pt")
+    with torch.no_grad():
+        hs = full(input_ids=t.input_ids, attention_mask=t.attention_mask, output_hidden_states=True).hidden_states
+    ref = hs[4] * t.attention_mask[..., None]
+    assert torch.allclose(emb, ref, atol=1e-5, rtol=1e-4)
+    assert emb[0, 3:].abs().sum() == 0
