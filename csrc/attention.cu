@@ -564,293 +564,6 @@ __global__ void __launch_bounds__(AttnSmem<QT>::kThreads, 1)
   if (warp == AttnSmem<QT>::kMmaWarp) tmem_dealloc(tmem, AttnSmem<QT>::kTmemCols);
 }
 
-// ------------------------------------------------------------------------------------------
-// 64-key variant with double-buffered scores.  Key tiles of 64 halve S (64 TMEM columns per Q
-// tile), so each Q tile gets TWO score buffers: S_g[0], S_g[1] (4 x 64 columns) + O_0, O_1 (2 x
-// 128) = 512 columns.  P_g(j) (bf16) is written over S_g[j % 2] and read by PV_g(j) from TMEM,
-// while QK_g(j + 1) already fills S_g[(j + 1) % 2]: the MMA warp issues QK(j + 1) for both Q
-// tiles BEFORE PV(j), so the next scores are ready when a softmax warpgroup finishes its
-// current tile and the QK -> softmax -> PV chain no longer serialises the tensor core.
-// QK_g(j + 2) overwrites the buffer of P_g(j); the PV that reads it was issued earlier by the
-// same thread, and tcgen05 operations of one thread complete in order.  A softmax that must
-// rescale O_g waits for PV_g(j - 1) first (pv_done), since S(j) being ready no longer implies it.
-constexpr int kBN64 = 64;
-constexpr int kKV64 = 64 * kD * 2;  // 16 KB: two 64-column (d) chunks of [64 keys x 128 B]
-constexpr int kChunk64 = 8192;
-
-template <int QT>
-struct Attn64Smem {
-  static constexpr int kThreads = 128 * QT + 128;
-  static constexpr int kProducerWarp = 4 * QT;
-  static constexpr int kMmaWarp = 4 * QT + 1;
-  static constexpr uint32_t kTmemCols = QT == 2 ? 512 : 256;
-  static constexpr int kRing = QT == 2 ? 10 : 12;            // K/V slots of 16 KB (224 KB of smem with Q)
-  static constexpr int kKV = QT * kTileBytes;
-  static constexpr int kBar = kKV + kRing * kKV64;
-  // q_full, kv_full[R], kv_empty[R], s_full[QT][2 buffers], p_full[QT][2 buffers][2 halves], pv_done[QT],
-  // o_full.  Score / P barriers are per buffer: a softmax warpgroup may finish P(j + 1) before the
-  // MMA warp has waited for P(j), and with one barrier that would be two phases ahead of its waiter.
-  static constexpr int kNumBars = 1 + 2 * kRing + 2 * QT + 4 * QT + QT + 1;
-  static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
-};
-
-// TMEM columns: S_g[b] at 64 (2 g + b); O_g after all score buffers.
-__device__ __forceinline__ uint32_t tmem_s64_col(int g, int b) { return 64u * (2 * g + b); }
-template <int QT>
-__device__ __forceinline__ uint32_t tmem_o64_col(int g) { return 128u * QT + 128u * g; }
-
-template <int QT>
-__global__ void __launch_bounds__(Attn64Smem<QT>::kThreads, 1)
-    attn64_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                      const __grid_constant__ CUtensorMap tv, AttnParams p, int* err) {
-  using L = Attn64Smem<QT>;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  constexpr int R = L::kRing;
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + R;
-  uint64_t* s_full = kv_empty + R;      // s_full[2 g + b]
-  uint64_t* p_full = s_full + 2 * QT;   // p_full[4 g + 2 buffer + half]
-  uint64_t* pv_done = p_full + 4 * QT;  // pv_done[g]
-  uint64_t* o_full = pv_done + QT;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int splits = p.kv_splits > 1 ? p.kv_splits : 1;
-  const int chunk = blockIdx.x % splits;
-  const int q0 = (blockIdx.x / splits) * (QT * kBM);
-  const int lo = p.kv_lo ? max(0, p.kv_lo[b]) : 0;
-  const int hi = p.kv_hi ? min(p.Sk, p.kv_hi[b]) : p.Sk;
-  const int tiles_all = hi > lo ? (hi + kBN64 - 1) / kBN64 - lo / kBN64 : 0;
-  const int per_chunk = (tiles_all + splits - 1) / splits;
-  const int t_first = lo / kBN64 + chunk * per_chunk;
-  const int n_tiles = max(0, min(per_chunk, tiles_all - chunk * per_chunk));
-  const int merge_mode = splits > 1 ? 1 : p.merge_mode;
-  const long long split_rows = (long long)p.B * p.H * p.Sq;
-  float* const acc_o = splits > 1 ? p.split_o + (long long)chunk * split_rows * kD : p.acc_o;
-  float* const acc_lse = splits > 1 ? p.split_lse + (long long)chunk * split_rows : p.acc_lse;
-  float* const lse_out = splits > 1 ? nullptr : p.lse;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < L::kNumBars; ++i) {
-      uint64_t* bar = &bars[i];
-      mbar_init(bar, (bar >= p_full && bar < p_full + 4 * QT) ? 128 : 1);
-    }
-    *abort_flag = 0;
-    fence_barrier_init();
-    fence_proxy_async_shared();
-    prefetch_tmap(&tq);
-    prefetch_tmap(&tk);
-    prefetch_tmap(&tv);
-  }
-  if (warp == L::kMmaWarp) {
-    tmem_alloc(tmem_slot, L::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == L::kProducerWarp) {
-    if constexpr (QT == 2) regs_dec_64();
-    if (lane == 0 && n_tiles > 0) {
-      mbar_arrive_expect_tx(q_full, QT * kTileBytes);
-      for (int g = 0; g < QT; ++g)
-        for (int c = 0; c < 2; ++c)
-          tma_load_4d(smem + g * kTileBytes + c * kChunk, &tq, q_full, c * 64, q0 + g * kBM, h, b);
-      bool issued[R];
-      uint32_t par_i[R];
-      for (int i = 0; i < R; ++i) issued[i] = false, par_i[i] = 0;
-      bool ok = true;
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int k0 = (t_first + j) * kBN64;
-        for (int which = 0; which < 2; ++which) {  // K_j then V_j
-          const int Ld = 2 * j + which, slot = Ld % R;
-          const uint32_t par = (Ld / R) & 1;
-          if (!mbar_wait(&kv_empty[slot], par ^ 1u, err, kKidAttn, 100 + which, abort_flag)) {
-            ok = false;
-            break;
-          }
-          uint8_t* dst = smem + L::kKV + slot * kKV64;
-          mbar_arrive_expect_tx(&kv_full[slot], kKV64);
-          for (int c = 0; c < 2; ++c)
-            tma_load_4d(dst + c * kChunk64, which == 0 ? &tk : &tv, &kv_full[slot], c * 64, k0, h, b);
-          issued[slot] = true;
-          par_i[slot] = par;
-        }
-      }
-      if (!ok) {  // our own bulk copies must land before the CTA exits
-        mbar_wait(q_full, 0, nullptr, 0, 0, nullptr, 200000000LL);
-        for (int i = 0; i < R; ++i)
-          if (issued[i]) mbar_wait(&kv_full[i], par_i[i], nullptr, 0, 0, nullptr, 200000000LL);
-      }
-    }
-  } else if (warp == L::kMmaWarp) {
-    if constexpr (QT == 2) regs_dec_64();
-    if (lane == 0 && n_tiles > 0) {
-      constexpr uint32_t idesc_qk = make_idesc_bf16_f32(kBM, kBN64, 0, 0);
-      constexpr uint32_t idesc_pv = make_idesc_bf16_f32(kBM, kD, 0, 1);
-      constexpr uint64_t kHiK = make_sdesc_sw128(0, 16, 1024);        // K-major Q / K tiles
-      constexpr uint64_t kHiV = make_sdesc_sw128(0, kChunk64, 1024);  // MN-major V tiles
-      bool ok = mbar_wait(q_full, 0, err, kKidAttn, 110, abort_flag);
-      const uint32_t q_lo = smem_u32(smem) >> 4;
-      const uint32_t kv_lo = smem_u32(smem + L::kKV) >> 4;
-      auto slot_lo = [&](int Ld) { return kv_lo + (uint32_t)(Ld % R) * (kKV64 >> 4); };
-      auto wait_load = [&](int Ld, int detail) {
-        return mbar_wait(&kv_full[Ld % R], (Ld / R) & 1, err, kKidAttn, detail, abort_flag);
-      };
-      auto issue_qk = [&](int g, int jj) {
-        const uint32_t qa = q_lo + (uint32_t)g * (kTileBytes >> 4), ka = slot_lo(2 * jj);
-        const uint32_t d_tmem = tmem + tmem_s64_col(g, jj & 1);
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t qo = (uint32_t)((((kk >> 2) * kChunk) + (kk & 3) * 32) >> 4);
-          const uint32_t ko = (uint32_t)((((kk >> 2) * kChunk64) + (kk & 3) * 32) >> 4);
-          umma_f16_ss(d_tmem, kHiK | (qa + qo), kHiK | (ka + ko), idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[2 * g + (jj & 1)]);
-      };
-      auto issue_pv = [&](int g, int jj) -> bool {
-        const uint32_t va = slot_lo(2 * jj + 1);
-        const uint32_t o_tmem = tmem + tmem_o64_col<QT>(g), p_tmem = tmem + tmem_s64_col(g, jj & 1);
-        for (int hf = 0; hf < 2; ++hf) {  // P arrives in two 32-key halves
-          if (!mbar_wait(&p_full[4 * g + 2 * (jj & 1) + hf], (jj >> 1) & 1, err, kKidAttn, 130 + 2 * g + hf,
-                         abort_flag))
-            return false;
-          tc_fence_after();
-#pragma unroll
-          for (int kq = 0; kq < 2; ++kq) {
-            const int kk = hf * 2 + kq;  // 16 keys per MMA
-            umma_f16_ts(o_tmem, p_tmem + kk * 8, kHiV | (va + (uint32_t)((kk * 2048) >> 4)), idesc_pv,
-                        (jj > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
-        umma_commit(&pv_done[g]);
-        return true;
-      };
-      if (ok && wait_load(0, 113)) {
-        tc_fence_after();
-        for (int g = 0; g < QT; ++g) issue_qk(g, 0);
-        umma_commit(&kv_empty[0 % R]);
-      } else {
-        ok = false;
-      }
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles) {  // next scores first: they fill the other buffer while softmax(j) runs
-          if (!wait_load(2 * (j + 1), 113)) { ok = false; break; }
-          tc_fence_after();
-          for (int g = 0; g < QT; ++g) issue_qk(g, j + 1);
-          umma_commit(&kv_empty[(2 * (j + 1)) % R]);  // K_{j+1} consumed
-        }
-        if (!wait_load(2 * j + 1, 114)) { ok = false; break; }
-        tc_fence_after();
-        for (int g = 0; g < QT && ok; ++g) ok = issue_pv(g, j);
-        if (!ok) break;
-        umma_commit(&kv_empty[(2 * j + 1) % R]);  // V_j consumed
-      }
-      if (ok) umma_commit(o_full);
-    }
-  } else if (warp >= L::kProducerWarp) {
-    if constexpr (QT == 2) regs_dec_64();
-  } else {
-    if constexpr (QT == 2) regs_inc_216();
-    const int g = warp / 4;
-    const int sub = warp & 3;
-    const int row = sub * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
-    const uint32_t o_t = tmem + lane_base + tmem_o64_col<QT>(g);
-    float m = -INFINITY;  // running max (log2 domain)
-    float l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int bb = j & 1;
-      const uint32_t s_t = tmem + lane_base + tmem_s64_col(g, bb);
-      if (!mbar_wait(&s_full[2 * g + bb], (j >> 1) & 1, err, kKidAttn, 120 + g, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      float s[64];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) tmem_ld_32x32b_x32(s_t + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
-      tmem_wait_ld();
-      const int k0 = (t_first + j) * kBN64;
-      if ((k0 < lo) || (k0 + kBN64 > hi)) {  // edge tile: mask keys outside [lo, hi)
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const int key = k0 + c;
-          if (key < lo || key >= hi) s[c] = -INFINITY;
-        }
-      }
-      const float sc = p.scale_log2;
-      const uint64_t sc2 = f2_pack(sc, sc);
-      float mxa[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mxa[t] = fmaxf(s[t], s[8 + t]);
-#pragma unroll
-      for (int c = 16; c < 64; c += 16) {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) mxa[t] = max3(mxa[t], s[c + t], s[c + 8 + t]);
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-      const float m_new = fmaxf(m, mx * sc);
-      const bool need = (j > 0) && __any_sync(0xffffffffu, m_new > m + 8.0f);
-      const float m_old = m;
-      if (j == 0 || need) m = m_new;
-      const float m_use = (m == -INFINITY) ? 0.f : m;
-      if (need) {  // O_g is rescaled in TMEM once PV_g(j - 1) has completed
-        if (!mbar_wait(&pv_done[g], (j - 1) & 1, err, kKidAttn, 124 + g, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const float f = (m_old == -INFINITY) ? 0.f : fast_exp2(m_old - m);
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
-          uint32_t o_raw[16];
-          tmem_ld_32x32b_x16(o_t + c * 16, o_raw);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * f);
-          tmem_st_32x32b_x16(o_t + c * 16, o_raw);
-        }
-        l *= f;
-      }
-      const uint64_t nm2 = f2_pack(-m_use, -m_use);
-      uint64_t rs[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
-#pragma unroll
-      for (int qtr = 0; qtr < 2; ++qtr) {  // keys [32 qtr, 32 qtr + 32): bf16x2 into TMEM over S
-        uint32_t pk[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint64_t x2 = f2_fma(f2_pack(s[qtr * 32 + 2 * c], s[qtr * 32 + 2 * c + 1]), sc2, nm2);
-          float x0, x1;
-          f2_unpack(x2, x0, x1);
-          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
-          rs[c & 1] = f2_add(rs[c & 1], f2_pack(e0, e1));
-          pk[c] = pack_bf16x2(e0, e1);
-        }
-        tmem_st_32x32b_x16(s_t + qtr * 16, pk);
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&p_full[4 * g + 2 * bb + qtr]);
-      }
-      float a0, a1, c0, c1;
-      f2_unpack(rs[0], a0, a1);
-      f2_unpack(rs[1], c0, c1);
-      l += (a0 + a1) + (c0 + c1);
-    }
-    attn_epilogue(p, err, b, h, q0 + g * kBM + row, o_t, ok, n_tiles, o_full, abort_flag, m, l, merge_mode,
-                  acc_o, acc_lse, lse_out);
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == L::kMmaWarp) tmem_dealloc(tmem, L::kTmemCols);
-}
-
 // Split-KV combine: one warp per query row merges the kv_splits normalised partials by
 // log-sum-exp and writes the bf16 row (Ulysses scatter included) and, if asked, the LSE.
 __global__ void __launch_bounds__(256) attn_combine_kernel(AttnParams p) {
@@ -922,40 +635,7 @@ int launch_attn(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, c
   return (int)cudaGetLastError();
 }
 
-template <int QT>
-int launch_attn64(const AttnArgs* a, const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
-                  const CUtensorMap& tv, cudaStream_t stream) {
-  static bool attr[16] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr[dev & 15]) {
-    cudaError_t e = cudaFuncSetAttribute(attn64_fwd_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Attn64Smem<QT>::kTotal);
-    if (e != cudaSuccess) return (int)e;
-    if (QT == 2) {
-      cudaFuncAttributes fa;
-      e = cudaFuncGetAttributes(&fa, attn64_fwd_kernel<QT>);
-      if (e != cudaSuccess) return (int)e;
-      if (fa.numRegs * Attn64Smem<QT>::kThreads < 128 * 64 + 256 * 216) return -11;
-    }
-    attr[dev & 15] = true;
-  }
-  const int splits = p.kv_splits > 1 ? p.kv_splits : 1;
-  dim3 grid((a->Sq + QT * kBM - 1) / (QT * kBM) * splits, a->H, a->B);
-  attn64_fwd_kernel<QT><<<grid, Attn64Smem<QT>::kThreads, Attn64Smem<QT>::kTotal, stream>>>(tq, tk, tv, p, a->err);
-  if (splits > 1) {
-    const long long rows = (long long)a->B * a->H * a->Sq;
-    attn_combine_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(p);
-  }
-  return (int)cudaGetLastError();
-}
-
-int g_attn_keys = 64;  // key-tile width of the flash kernel: 64 (double-buffered scores) or 128
-
 }  // namespace
-
-// Key-tile width of the attention kernel (64: double-buffered scores; 128: one score buffer).
-extern "C" void dfl_attention_set_key_tile(int keys) { g_attn_keys = keys == 128 ? 128 : 64; }
 
 // Key-range splits: modelled time = waves of CTAs x (one full-range CTA time / s) + the
 // split overhead (partial f32 rows written and read back by the combine, CTA start-up),
@@ -992,10 +672,9 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
   int rc = make_tmap_4d(&tq, a->q, a->Sq, a->H, a->B, a->q_ss, a->q_hs, a->q_bs);
   if (rc) return 1000 + rc;
-  const int kv_box = g_attn_keys == 64 ? kBN64 : kBN;
-  rc = make_tmap_4d(&tk, a->k, a->Sk, a->H, a->B, a->k_ss, a->k_hs, a->k_bs, kv_box);
+  rc = make_tmap_4d(&tk, a->k, a->Sk, a->H, a->B, a->k_ss, a->k_hs, a->k_bs);
   if (rc) return 2000 + rc;
-  rc = make_tmap_4d(&tv, a->v, a->Sk, a->H, a->B, a->v_ss, a->v_hs, a->v_bs, kv_box);
+  rc = make_tmap_4d(&tv, a->v, a->Sk, a->H, a->B, a->v_ss, a->v_hs, a->v_bs);
   if (rc) return 3000 + rc;
   AttnParams p;
   p.o_bs = a->o_bs;
@@ -1033,8 +712,7 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   if (p.kv_splits > 1) {
     if (a->merge_mode != 0 || !a->split_o || !a->split_lse || (reinterpret_cast<uintptr_t>(a->split_o) & 15))
       return -10;
-    // 256-row query blocks, split key ranges
-    return g_attn_keys == 64 ? launch_attn64<2>(a, p, tq, tk, tv, stream) : launch_attn<2>(a, p, tq, tk, tv, stream);
+    return launch_attn<2>(a, p, tq, tk, tv, stream);  // 256-row query blocks, split key ranges
   }
   // Two ping-pong Q tiles per CTA unless that leaves more than half the SMs idle:
   // then one Q tile per CTA doubles the CTA count while still fitting one wave.
@@ -1042,10 +720,6 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int sms = dfl_host::num_sms(dev);
   const long long ctas2 = (long long)((a->Sq + 2 * kBM - 1) / (2 * kBM)) * a->H * a->B;
-  if (g_attn_keys == 64) {
-    if (ctas2 * 2 <= sms) return launch_attn64<1>(a, p, tq, tk, tv, stream);
-    return launch_attn64<2>(a, p, tq, tk, tv, stream);
-  }
   if (ctas2 * 2 <= sms) return launch_attn<1>(a, p, tq, tk, tv, stream);
   return launch_attn<2>(a, p, tq, tk, tv, stream);
 }

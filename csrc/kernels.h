@@ -242,8 +242,6 @@ typedef struct AttnArgs {
 int dfl_attention(const AttnArgs* a, cudaStream_t stream);
 // Key-range split count that minimises the modelled time of this launch (1 = none).
 int dfl_attention_plan_splits(const AttnArgs* a);
-// Key-tile width of the flash kernel: 64 (default, double-buffered scores) or 128.
-void dfl_attention_set_key_tile(int keys);
 
 // ---------------------------------------------------------------------------
 // Peer-memory communication runtime (comm.cu)

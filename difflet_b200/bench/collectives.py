@@ -240,20 +240,44 @@ def bench_cfg(world, rank, iters, peak, hbm):
                              torch.empty(n, device="cuda", dtype=torch.bfloat16))
 
     s1, s2 = sampler(), sampler()
+    # the device work of one step: the scheduler's per-step weights are host scalars, computed
+    # once here so the loop times the exchange + update (not Python bookkeeping)
+    k_v, e, gw, _ = s1.coeffs()
     buf = peer.next_pred_buffer(pred.shape, pred.dtype)
+    buf.copy_(pred)
+    from difflet_b200.ops import fused as F
 
     def fused():
-        peer.step(pred, 5.0, s1)
+        peer.heap.barrier()  # the partner's prediction is complete
+        F.guided_step(buf, None, scale=5.0, x=s1.x, x16=s1.x16, last=s1.last, m1=s1.m1, m2=s1.m2, m_out=s1.m2,
+                      k_v=k_v, e=e, g=gw, store_last=True, b_ptr=peer.heap.peer_ptrs(buf)[1 - peer.rank],
+                      swap=peer.is_cond)
+
+    parts = [torch.empty_like(pred) for _ in range(2)]
 
     def baseline():
-        coll.step(pred, 5.0, s2)
+        dist.all_gather(parts, pred, group=group)
+        F.guided_step(parts[0], parts[1], scale=5.0, x=s2.x, x16=s2.x16, last=s2.last, m1=s2.m1, m2=s2.m2,
+                      m_out=s2.m2, k_v=k_v, e=e, g=gw, store_last=True)
 
-    del buf
     tf, tb = _timeit(fused, iters), _timeit(baseline, iters)
     link = n * 2.0
     hbm_b = n * (2 + 2 + 4 * 4 + 4 * 3 + 2.0)  # a, b, x / last / m1 / m2 in; x / last / m / x16 out
     peer.close()
     return _row(f"cfg_step (Wan 720p x 81, {n} values per rank)", tf, tb, 0.0, link, hbm_b, peak, hbm)
+
+
+def bench_barrier(world, rank, iters, peak, hbm):
+    """The device epoch barrier every fused path uses (flag stores into every peer + bounded
+    polling), against NCCL's barrier-equivalent all-reduce of one value."""
+    from difflet_b200.parallel.symm import SymmetricHeap
+
+    heap = SymmetricHeap(dist.group.WORLD, list(range(world)), torch.device("cuda", rank))
+    one = torch.ones(1, device="cuda")
+    tf = _timeit(heap.barrier, iters * 10)
+    tb = _timeit(lambda: dist.all_reduce(one), iters * 10)
+    heap.close()
+    return _row("peer_barrier", tf, tb, 0.0, 4.0 * world, 0.0, peak, hbm)
 
 
 def main(argv=None):
@@ -275,8 +299,9 @@ def main(argv=None):
     peak, hbm, src = _peaks()
     torch.manual_seed(rank)
     rows = []
-    todo = (args.only or "qkv,attn,tp,sp,cfg").split(",")
-    fns = {"qkv": bench_qkv, "attn": bench_attn, "tp": bench_tp, "sp": bench_sp, "cfg": bench_cfg}
+    todo = (args.only or "barrier,qkv,attn,tp,sp,cfg").split(",")
+    fns = {"barrier": bench_barrier, "qkv": bench_qkv, "attn": bench_attn, "tp": bench_tp, "sp": bench_sp,
+           "cfg": bench_cfg}
     for name in todo:
         rows.append(fns[name](world, rank, args.iters, peak, hbm))
         if rank == 0:

@@ -20,13 +20,24 @@ import math
 import torch
 
 GEMM_SHAPES = [
+    # FLUX.1-dev 1024^2 on one GPU: the GEMMs that dominate the step
     ("flux_qkv_img", 4096, 9216, 3072),
-    ("flux_single_fused", 4608, 21504, 3072),
-    ("flux_single_proj_out", 4608, 3072, 15360),
+    ("flux_out_img", 4096, 3072, 3072),
     ("flux_mlp_up", 4096, 12288, 3072),
     ("flux_mlp_down", 4096, 3072, 12288),
-    ("flux_sp8_fused", 576, 21504, 3072),
+    ("flux_single_fused", 4608, 21504, 3072),
+    ("flux_single_proj_out", 4608, 3072, 15360),
+    # Ulysses-8 (576 rows per rank) and tp2 x Ulysses-4 (1152 rows, half the columns / K)
+    ("flux_u8_qkv_img", 512, 9216, 3072),
+    ("flux_u8_single_fused", 576, 21504, 3072),
+    ("flux_u8_single_proj_out", 576, 3072, 15360),
+    ("flux_u8_mlp_down", 512, 3072, 12288),
+    ("flux_tp2u4_single_fused", 1152, 10752, 3072),
+    ("flux_tp2u4_single_proj_out", 1152, 3072, 7680),
+    # Wan2.2 720p x 81 (75,600 tokens; Ulysses-4 per rank 18,900)
+    ("wan_qkv_1gpu", 75600, 15360, 5120),
     ("wan_ffn_up_sp4", 18900, 13824, 5120),
+    ("wan_ffn_down_sp4", 18900, 5120, 13824),
     ("square_8192", 8192, 8192, 8192),
 ]
 ATTN_CASES = [("flux_1gpu", 1, 24, 4608), ("flux_sp8_heads", 1, 3, 4608), ("wan_ulysses4", 1, 10, 75600 // 4),
@@ -188,12 +199,9 @@ def bench_conv(nat, iters, flush, peaks, cases, ref):
     return rows
 
 
-ATTN_KEY_TILES = [64]
-
-
 def bench_attn(nat, iters, flush, peaks, cases, ref):
-    """Flash attention at the per-rank shapes of the benchmark configs (each key-tile width in
-    ATTN_KEY_TILES), against torch SDPA (cuDNN on sm_100) with ``ref``."""
+    """Flash attention at the per-rank shapes of the benchmark configs, against torch SDPA (cuDNN
+    on sm_100) with ``ref``."""
     rows = []
     for name, B, H, S in _sel(ATTN_CASES, cases):
         q = torch.randn(B, H, S, 128, device="cuda", dtype=torch.bfloat16)
@@ -203,19 +211,10 @@ def bench_attn(nat, iters, flush, peaks, cases, ref):
         sc = 1 / math.sqrt(128)
         fl = 4.0 * B * H * S * S * 128
         it = max(2, min(iters, int(2e14 / fl)))  # long sequences: fewer repeats
-        r = {"kernel": "attn_tcgen05", "shape": name, "B": B, "H": H, "S": S}
-        for kt in ATTN_KEY_TILES:
-            nat.attention_set_key_tile(kt)
-            t_ours = time_fn(lambda: nat.attention(q, k, v, sc, out=o), it, flush=flush)
-            r[f"keys{kt}_ms"] = round(t_ours, 4)
-            r[f"keys{kt}_tflops"] = round(fl / t_ours / 1e9, 1)
-        from difflet_b200 import envs
-
-        nat.attention_set_key_tile(envs.DIFFLET_ATTN_KEYS)
-        best = min(r[f"keys{kt}_ms"] for kt in ATTN_KEY_TILES)
-        r.update({"ms": best, "tflops": round(fl / best / 1e9, 1),
-                  "frac_of_measured_peak": round(fl / best / 1e9 / peaks["bf16_tflops"], 3)})
-        t_ours = best
+        t_ours = time_fn(lambda: nat.attention(q, k, v, sc, out=o), it, flush=flush)
+        r = {"kernel": "attn_tcgen05", "shape": name, "B": B, "H": H, "S": S, "ms": round(t_ours, 4),
+             "tflops": round(fl / t_ours / 1e9, 1),
+             "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3)}
         if ref:
             t_ref = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=sc), it,
                             flush=flush)
@@ -263,10 +262,8 @@ def main(argv=None):
     ap.add_argument("--cases", default="")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-ref", action="store_true")
-    ap.add_argument("--attn-keys", default="64", help="attention key-tile widths to time (comma list of 64 / 128)")
     ap.add_argument("--out", default=None, help="also write the rows as JSON here")
     args = ap.parse_args(argv)
-    ATTN_KEY_TILES[:] = [int(k) for k in args.attn_keys.split(",") if k]
     from difflet_b200 import _native
     from difflet_b200.ops.fused import _lib
     from difflet_b200.utils.peaks import load_peaks

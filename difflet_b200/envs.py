@@ -74,8 +74,6 @@ environment_variables: dict[str, Callable[[], Any]] = {
     "DIFFLET_GEMM_GROUP": lambda: _str(os.environ.get("DIFFLET_GEMM_GROUP"), "1"),
     # epilogue warps of the 2-SM GEMM: 0 = 8 for the q/k/v head-scatter epilogue and 4 otherwise; 4 or 8 = always
     "DIFFLET_GEMM_EPI_WARPS": lambda: _int(os.environ.get("DIFFLET_GEMM_EPI_WARPS"), 0),
-    # key-tile width of the flash attention kernel: 64 (double-buffered scores) or 128 (one buffer)
-    "DIFFLET_ATTN_KEYS": lambda: _int(os.environ.get("DIFFLET_ATTN_KEYS"), 64),
     # "auto": attention launches whose query blocks leave SMs idle split the key range; "0": never
     "DIFFLET_ATTN_SPLIT": lambda: _str(os.environ.get("DIFFLET_ATTN_SPLIT"), "auto"),
     # serving

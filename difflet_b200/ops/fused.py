@@ -59,7 +59,6 @@ def _lib():
         _nat = _native.require()
         _nat.gemm_set_pair_auto(envs.DIFFLET_GEMM_PAIR != "0")
         _nat.gemm_set_epi_warps(envs.DIFFLET_GEMM_EPI_WARPS)
-        _nat.attention_set_key_tile(envs.DIFFLET_ATTN_KEYS)
     _split_workspace(_nat)
     return _nat
 

@@ -123,9 +123,9 @@ class PeerSlabs(CollectiveSlabs):
         self.heap = SymmetricHeap(group, ranks, device)
 
     def empty(self, shape, dtype) -> torch.Tensor:
-        t = self.heap.empty(shape, dtype)
-        t.zero_()
-        return t
+        # zero-filled and synchronised by the allocation itself: a zero_() queued here could run
+        # after a neighbour's producer kernel has already stored halo rows into this buffer
+        return self.heap.empty(shape, dtype)
 
     def neighbours(self, buf: torch.Tensor, frame_off: int, rows: int) -> dict:
         # buf is this rank's [F, rows + 2, W, C] view from the base of its symmetric allocation;

@@ -32,6 +32,7 @@ class SymmetricHeap:
         self._local: list[torch.Tensor] = []
         self._opened: list[int] = []
         self._peers: dict[int, list[int]] = {}  # local data_ptr -> peer base pointers (index = group rank)
+        self._retired: list[torch.Tensor] = []
         self._nbytes: dict[int, int] = {}
         # barrier flags: world int32 slots; counter: local epoch
         self.flags, self.flag_ptrs = self._alloc_raw(max(self.world, 4) * 4)
@@ -67,6 +68,8 @@ class SymmetricHeap:
         n = int(math.prod(shape)) * torch.empty((), dtype=dtype).element_size()
         guard = self.CANARY_BYTES if envs.DIFFLET_BOUNDS_CHECK else 0
         raw, _ = self._alloc_raw(n + guard)
+        # _alloc_raw returns a buffer zeroed (cudaMemset + device synchronise) before the handle
+        # exchange, so no rank can see a peer's buffer before it is zero
         if guard:
             if not hasattr(self, "_canaries"):
                 self._canaries = []
@@ -95,10 +98,22 @@ class SymmetricHeap:
     def barrier(self) -> None:
         self.nat.peer_barrier(self.flag_ptrs, self.counter, self.rank, self.timeout)
 
+    def retire(self, t: torch.Tensor) -> None:
+        """Keep a symmetric buffer that is being replaced alive until ``close``: peers have it
+        mapped, and freeing an exported allocation before every importer has closed it is
+        undefined behaviour."""
+        self._retired.append(t)
+
     def close(self) -> None:
+        """Unmap the peers' buffers, wait until every rank has unmapped ours, then free ours."""
         torch.cuda.synchronize(self.device)
         for p in self._opened:
             self.nat.ipc_close(p)
         self._opened.clear()
         self._peers.clear()
+        try:
+            dist.barrier(group=self.group)
+        except Exception:  # noqa: BLE001 - a broken group: the process is going down anyway
+            pass
         self._local.clear()
+        self._retired.clear()

@@ -128,6 +128,8 @@ class PeerTP(_TPBase, PeerBase):
         key = (N, dtype)
         cur = self._slots.get(key)
         if cur is None or cur.shape[0] < self.world * rpr:
+            if cur is not None:
+                self.heap.retire(cur)  # the peers still map the smaller buffer
             cur = self.heap.empty((self.world * rpr, N), dtype)
             self._slots[key] = cur
         return cur
