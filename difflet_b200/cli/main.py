@@ -96,6 +96,7 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--queue-timeout", type=float, default=None, help="seconds a request may wait for its replica")
     s.add_argument("--request-timeout", type=float, default=600.0, help="seconds before a request is cancelled")
     s.add_argument("--heartbeat-interval", type=float, default=None, help="worker heartbeat period (s)")
+    s.add_argument("--log-dir", default=None, help="serve log files (default: ./logs), one per 5 MB and per day")
     q = sub.add_parser("quant", help="write the MXFP8 checkpoint of a model (or print its plan)")
     q.add_argument("--model-id", required=True)
     q.add_argument("--revision", default=None)

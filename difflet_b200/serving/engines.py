@@ -105,14 +105,16 @@ def _apply_env(env: dict | None) -> None:
         os.environ.update({k: str(v) for k, v in env.items()})
 
 
-def _call_run(run, req, should_cancel):
+def _call_run(run, req, should_cancel, **extra):
+    """run(req) with the keyword arguments it declares among should_cancel / on_stage / request_id."""
     import inspect
 
     try:
-        takes = "should_cancel" in inspect.signature(run).parameters
+        params = inspect.signature(run).parameters
     except (TypeError, ValueError):
-        takes = False
-    return run(req, should_cancel=should_cancel) if takes else run(req)
+        params = {}
+    kw = {k: v for k, v in dict(extra, should_cancel=should_cancel).items() if k in params}
+    return run(req, **kw)
 
 
 def _follower_main(rank, world, port, env, factory, factory_kwargs, feed, cancel_flag):
@@ -210,7 +212,7 @@ def _worker_main(conn_req, conn_resp, hb, factory, factory_kwargs, heartbeat_s, 
         for q in feeds:
             q.put(req)
         try:
-            out = _call_run(run, req, decide)
+            out = _call_run(run, req, decide, on_stage=lambda st: state.update(stage=st), request_id=rid)
             conn_resp.put(("ok", rid, out))
         except Exception as exc:  # noqa: BLE001
             kind = "cancelled" if type(exc).__name__ == "RequestCancelled" else "error"

@@ -12,40 +12,31 @@ import logging
 
 
 def pipeline_runner(model_id: str, pipeline_kwargs: dict):
-    """Runs inside every rank process of a replica: load once, return run(request, should_cancel).
+    """Runs inside every rank process of a replica: load once, return run(request, ...).
 
-    ``should_cancel()`` is polled between denoise steps (every rank of a multi-GPU replica polls
-    at the same step and gets the same answer); a cancelled request raises RequestCancelled."""
+    A request runs through the pipeline's stages (``serving/stages.py``: prepare -> denoise ->
+    decode -> output, or generate -> output), each logged with its duration; ``on_stage`` feeds
+    the worker's heartbeat.  ``should_cancel()`` is polled between denoise steps (every rank of a
+    multi-GPU replica polls at the same step and gets the same answer); a cancelled request
+    raises RequestCancelled."""
     from difflet_b200.pipeline.difflet_pipeline import DiffletPipeline
-    from difflet_b200.serving.engines import RequestCancelled
+    from difflet_b200.serving.stages import StageContext, pipeline_stages
 
     pipe = DiffletPipeline.from_pretrained(model_id, **pipeline_kwargs)
     video = pipe.model_entry.output == "video"
+    stages = pipeline_stages(pipe)
 
-    def run(req: dict, should_cancel=None):
-        if req.get("__smoke__"):
-            kw = {"prompt": "smoke", "num_inference_steps": 2}
+    def run(req: dict, should_cancel=None, on_stage=None, request_id=None):
+        smoke = bool(req.get("__smoke__"))
+        if smoke:
+            req = {"prompt": "smoke", "num_inference_steps": 2, "height": 256, "width": 256}
             if video:
-                kw["num_frames"] = 5
-            kw["height"], kw["width"] = 256, 256
-            pipe(**kw)
-            return None
-        req = dict(req)
-        if should_cancel is not None:
-            user_cb = req.pop("callback", None)
+                req["num_frames"] = 5
+        ctx = StageContext(request_id or ("smoke" if smoke else "-"), should_cancel or (lambda: False), on_stage)
+        out = stages.run(req, ctx)
+        return None if smoke else out
 
-            def callback(i, latents):
-                if should_cancel():
-                    raise RequestCancelled(f"cancelled at step {i}")
-                if user_cb is not None:
-                    user_cb(i, latents)
-
-            req["callback"] = callback
-        out = pipe(**req)
-        if out is None:
-            return None
-        return out[0].cpu()
-
+    run.stages = stages
     return run
 
 
@@ -71,7 +62,10 @@ def serve_main(a) -> int:
     from difflet_b200.serving.api import create_app
     from difflet_b200.serving.engines import ReplicatedEngine, ResidentWorkerEngine
 
-    logging.basicConfig(level=logging.INFO, format="%(asctime)s %(levelname)s %(message)s")
+    from difflet_b200.serving.logs import configure_serve_logging
+
+    log_file = configure_serve_logging(getattr(a, "log_dir", None))
+    logging.getLogger(__name__).info("serve log: %s", log_file.path)
     entry = resolve_model(a.model_id)
     kw = {"parallel": parallel_from_args(a), "backend": a.backend, "height": a.height, "width": a.width,
           "num_frames": a.num_frames, "compile_cache_dir": a.cache_dir, "random_init": a.random_weights,
@@ -93,6 +87,6 @@ def serve_main(a) -> int:
     store = make_artifact_store() if entry.output == "video" and any(k.startswith("DIFFLET_S3_") for k in os.environ) \
         else None
     app = create_app(engine, a.model_id, output=entry.output, api_key=opts.api_key, artifact_store=store)
-    uvicorn.run(app, host=opts.host, port=opts.port, log_level="info")
+    uvicorn.run(app, host=opts.host, port=opts.port, log_level="info", log_config=None)
     engine.close()
     return 0
