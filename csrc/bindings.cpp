@@ -803,6 +803,7 @@ at::Tensor rel_l1(const at::Tensor& a, const at::Tensor& b) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "difflet_b200 native sm_100a kernels";
   m.def("gemm_set_pair_auto", [](bool on) { dfl_gemm_set_pair_auto(on ? 1 : 0); });
+  m.def("gemm_set_split_force", [](int64_t s) { dfl_gemm_set_split_force((int)s); });
   m.def("gemm_set_epi_warps", [](int64_t n) { dfl_gemm_set_epi_warps((int)n); });
   m.def("gemm_set_split_workspace", [](const at::Tensor& ws, const at::Tensor& sem) {
     TORCH_CHECK(ws.is_cuda() && sem.is_cuda() && ws.device() == sem.device(), "workspace tensors on one device");

@@ -16,6 +16,7 @@
 // residual of the FLUX blocks (difflet/models/flux/modeling_flux.py:712,
 // 721-729, 844-867).
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -291,28 +292,70 @@ extern "C" void dfl_gemm_set_split_workspace(int device, void* ws, long long ws_
   g_split_sem_count[d] = sem_count;
 }
 
-// Small-M launches whose tiles fill under 60 % of the SMs split K in two (problems with at
-// least 8 K blocks): twice the items, one f32 round trip of each tile through L2.
-static void plan_split_k(GemmGroup& g, int epi, int bn, int sms, int dev) {
+// Small-M launches whose CTAs fill under 60 % of the SMs split K into s = 2..4 ranges (problems
+// with at least 4 K blocks per range).  s minimises a time model in units of one K block of one
+// CTA's 128 x 256 tile: waves(CTAs * s) * ceil(k_blocks / s) * kb_cost + (s - 1) * fixup.  The
+// fixup (one f32 partial tile written to and read back from L2 per extra range, ranges finished
+// in order) is priced at 12 K blocks (6 for 128 x 128 tiles): fitted on B200 to the measured
+// small-M shapes (576 x 3072 x 15360 fastest at 2 ranges, 512 x 3072 x 12288 at 3), where the
+// whole launch is bound by streaming the weights rather than by each SM's tensor rate.
+// kb_cost: 1 for one CTA per tile, 0.92 for a CTA pair (each SM streams half of B: 32 instead
+// of 48 KB per K block; measured 3-8 % faster per K block at these shapes).
+constexpr double kPairKbCost = 0.92;
+constexpr double kFixup256 = 12.0, kFixup128 = 6.0;
+
+static double split_model(long long tiles, int ctas, int kb_max, int sms, double kb_cost, double fixup, int* best_s) {
+  const int slots = ctas == 2 ? (sms / 2) : sms;  // pairs occupy two SMs
+  int best = 1;
+  double best_t = (double)((tiles + slots - 1) / slots) * kb_max * kb_cost;
+  if (tiles * ctas * 10 <= (long long)sms * 6) {
+    for (int sp = 2; sp <= 4; ++sp) {
+      const int per = (kb_max + sp - 1) / sp;
+      if (per < 4 || (sp - 1) * per >= kb_max) break;
+      const long long items = tiles * sp;
+      const double t = (double)((items + slots - 1) / slots) * per * kb_cost + (sp - 1) * fixup;
+      if (t < best_t) best = sp, best_t = t;
+    }
+  }
+  if (best_s) *best_s = best;
+  return best_t;
+}
+
+// Measurement switch: 0 = the model decides, 1..4 = that many K ranges wherever splitting is allowed.
+static int g_split_force = 0;
+extern "C" void dfl_gemm_set_split_force(int s) { g_split_force = (s >= 0 && s <= 4) ? s : 0; }
+
+static void plan_split_k(GemmGroup& g, int epi, int bn, int sms, int dev, int ctas) {
   const int d = dev & 15;
-  if (!g_split_ws[d] || epi == kEpiSwiGLU || epi == kEpiQkv || g.total_tiles * 10 > sms * 6) return;
+  if (!g_split_ws[d] || epi == kEpiSwiGLU || epi == kEpiQkv) return;
+  int kb_max = 0;
+  for (int i = 0; i < g.count; ++i) kb_max = std::max(kb_max, (g.p[i].K + BK - 1) / BK);
+  int best = 1;
+  split_model(g.total_tiles, ctas, kb_max, sms, ctas == 2 ? kPairKbCost : 1.0, bn >= 256 ? kFixup256 : kFixup128,
+              &best);
+  if (g_split_force) best = g_split_force;
+  if (best == 1) return;
   long long ws_off = 0;
   int sem_off = 0;
   for (int i = 0; i < g.count; ++i) {
     GemmProblem& P = g.p[i];
     const int base_tiles = P.num_m * P.num_n;
-    if ((P.K + BK - 1) / BK < 8) continue;
-    const long long need = (long long)base_tiles * BM * bn;
-    if (ws_off + need > g_split_ws_floats[d] || sem_off + base_tiles > g_split_sem_count[d]) continue;
-    P.splits = 2;
+    const int kb = (P.K + BK - 1) / BK;
+    const int per = (kb + best - 1) / best;
+    if (per < 4 || (best - 1) * per >= kb) continue;  // every range must hold K blocks
+    const long long need = (long long)base_tiles * ctas * BM * bn;  // one partial per CTA tile
+    if (ws_off + need > g_split_ws_floats[d] || sem_off + base_tiles * ctas > g_split_sem_count[d]) continue;
+    P.splits = best;
     P.ws = g_split_ws[d] + ws_off;
     P.sem = g_split_sem[d] + sem_off;
     ws_off += need;
-    sem_off += base_tiles;
-    g.total_tiles += base_tiles;  // one more item per tile
-    P.tiles = base_tiles * 2;
+    sem_off += base_tiles * ctas;
+    g.total_tiles += base_tiles * (best - 1);  // one more item per tile and extra range
+    P.tiles = base_tiles * best;
   }
 }
+
+extern "C" int dfl_gemm_pair_can_split(int epi);
 
 // One launch for `count` GEMMs that share the epilogue kind and output type.  The tile
 // shape (CTA pairs with 256 x 256 tiles, or one CTA with 128 x 256 / 128 x 128 tiles)
@@ -327,9 +370,23 @@ extern "C" int dfl_gemm_bf16_group(const GemmArgs* const* args, int count, cudaS
   }
   int dev = 0;
   cudaGetDevice(&dev);
-  bool wide = true;
+  bool wide = a0->cta_mode != 3;  // cta_mode 3: one CTA per tile, 128-column tiles (6 stages)
   for (int i = 0; i < count; ++i) wide = wide && args[i]->N >= 1024;
-  const bool pair = a0->cta_mode == 2 || (a0->cta_mode == 0 && g_pair_auto && wide && a0->M >= 1024);
+  bool pair = a0->cta_mode == 2 || (a0->cta_mode == 0 && g_pair_auto && wide && a0->M >= 1024);
+  const int sms = dfl_host::num_sms(dev);
+  if (!pair && a0->cta_mode == 0 && g_pair_auto && wide && g_split_ws[dev & 15] && dfl_gemm_pair_can_split(a0->epi)) {
+    // small M: CTA pairs (with split-K) against single CTAs (with split-K), by the model above
+    long long t1 = 0, t2 = 0;
+    int kb_max = 0;
+    for (int i = 0; i < count; ++i) {
+      const long long nn = (args[i]->N + 255) / 256;
+      t1 += (args[i]->M + BM - 1) / BM * nn;
+      t2 += (args[i]->M + 2 * BM - 1) / (2 * BM) * nn;
+      kb_max = std::max(kb_max, (args[i]->K + BK - 1) / BK);
+    }
+    pair = split_model(t2, 2, kb_max, sms, kPairKbCost, kFixup256, nullptr) <
+           split_model(t1, 1, kb_max, sms, 1.0, kFixup256, nullptr);
+  }
   const int bm = pair ? 2 * BM : BM;
   const int bn = (pair || wide) ? 256 : 128;
   GemmGroup g;
@@ -353,8 +410,11 @@ extern "C" int dfl_gemm_bf16_group(const GemmArgs* const* args, int count, cudaS
     P.splits = 1;
     g.total_tiles += P.tiles;
   }
-  if (pair) return dfl_gemm_pair_launch(&g, a0->epi, a0->out_f32, a0->err, stream, dev);
-  plan_split_k(g, a0->epi, bn, dfl_host::num_sms(dev), dev);
+  if (pair) {
+    if (dfl_gemm_pair_can_split(a0->epi)) plan_split_k(g, a0->epi, 256, sms, dev, 2);
+    return dfl_gemm_pair_launch(&g, a0->epi, a0->out_f32, a0->err, stream, dev);
+  }
+  plan_split_k(g, a0->epi, bn, sms, dev, 1);
   if (wide) return dispatch_epi<256, 4>(a0->epi, a0->out_f32, g, a0->err, stream, dev);
   return dispatch_epi<128, 6>(a0->epi, a0->out_f32, g, a0->err, stream, dev);
 }

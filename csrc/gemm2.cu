@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(PairCfg<EPI, EW>::kThreads, 1)
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* split_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // split-K wait outcome
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_rank();
@@ -153,11 +154,11 @@ __global__ void __launch_bounds__(PairCfg<EPI, EW>::kThreads, 1)
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
       bool ok = true;
       for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-        int lt, mb, nb;
+        int lt, mb, nb, kb0, kb1;
         const GemmProblem& P = group_tile(grp, t, lt);
-        tile_coords(lt, P.num_m, P.num_n, mb, nb);
-        const int num_k = (P.K + BK - 1) / BK;
-        for (int kb = 0; kb < num_k; ++kb) {
+        tile_coords(lt / P.splits, P.num_m, P.num_n, mb, nb);
+        split_k_range(P, lt % P.splits, BK, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kKidGemm, 310 + stage, abort_flag)) {
             ok = false;
             break;
@@ -193,9 +194,10 @@ __global__ void __launch_bounds__(PairCfg<EPI, EW>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        int lt;
-        const int num_k = (group_tile(grp, t, lt).K + BK - 1) / BK;
-        for (int kb = 0; kb < num_k; ++kb) {
+        int lt, kb0, kb1;
+        const GemmProblem& P = group_tile(grp, t, lt);
+        split_k_range(P, lt % P.splits, BK, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, err, kKidGemm, 330 + stage, abort_flag)) {
             ok = false;
             break;
@@ -206,7 +208,7 @@ __global__ void __launch_bounds__(PairCfg<EPI, EW>::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_f16_pair(d_tmem, make_sdesc_sw128(a_addr + k * 32, 16, 1024),
-                          make_sdesc_sw128(b_addr + k * 32, 16, 1024), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                          make_sdesc_sw128(b_addr + k * 32, 16, 1024), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           umma_commit_pair(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -232,18 +234,29 @@ __global__ void __launch_bounds__(PairCfg<EPI, EW>::kThreads, 1)
     for (int t = pair; t < num_tiles; t += num_pairs) {
       int lt, mb, nb;
       const GemmProblem& P = group_tile(grp, t, lt);
-      tile_coords(lt, P.num_m, P.num_n, mb, nb);
+      const int tile = lt / P.splits;
+      tile_coords(tile, P.num_m, P.num_n, mb, nb);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err, kKidGemm, 340 + acc, abort_flag)) break;
       tc_fence_after();
       const int row = mb * 2 * BM + (int)rank * BM + sub * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN + slice * C::kCols;
-      epilogue_tile<EPI, OUT_F32, C::kCols>(tbase, row, nb * BN + slice * C::kCols, P.M, P.N, P.ep, [&]() {
+      auto release = [&]() {
         tc_fence_before();
         if (rank == 0)
           mbar_arrive(&tempty_bar[acc]);
         else
           mbar_arrive_cta0(&tempty_bar[acc]);
-      }, stage);
+      };
+      if constexpr (EW == 4 && EPI != kEpiSwiGLU && EPI != kEpiQkv) {
+        if (P.splits > 1) {  // each CTA owns its 128 rows: partial tile / counter 2 * tile + rank
+          epilogue_tile_split<EPI, OUT_F32, BN>(tbase, sub * 32 + lane, row, nb * BN, P, 2 * tile + (int)rank,
+                                                lt % P.splits, release, err, abort_flag, split_ok);
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1u;
+          continue;
+        }
+      }
+      epilogue_tile<EPI, OUT_F32, C::kCols>(tbase, row, nb * BN + slice * C::kCols, P.M, P.N, P.ep, release, stage);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -304,6 +317,12 @@ int launch_pair(const GemmGroup& g, int* err, cudaStream_t stream, int dev) {
 }  // namespace
 
 extern "C" void dfl_gemm_set_epi_warps(int n) { g_epi_warps = (n == 4 || n == 8) ? n : 0; }
+
+// Split-K runs in the pair kernel only with four epilogue warps (the fixup's 128-thread barrier).
+extern "C" int dfl_gemm_pair_can_split(int epi) {
+  const int ew = g_epi_warps ? g_epi_warps : (epi == kEpiQkv ? 8 : 4);
+  return ew == 4 && epi != kEpiQkv && epi != kEpiSwiGLU;
+}
 
 // Grouped launch prepared by dfl_gemm_bf16_group (tiles of 256 rows, B boxes of 128 rows).
 extern "C" int dfl_gemm_pair_launch(const void* group, int epi, int out_f32, int* err, cudaStream_t stream, int dev) {

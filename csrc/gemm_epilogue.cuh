@@ -589,31 +589,46 @@ DFL_DEVICE void epilogue_tile_split(uint32_t tbase, int trow, int row, int col_b
       return;
     }
   }
-  float* wrow = P.ws + ((size_t)tile * 128 + trow) * BN;  // this thread's row of the partial tile
+  // The partial tile is stored thread-major: float4 q of chunk c of epilogue thread trow sits at
+  // ((c * 8 + q) * 128 + trow), so the 32 lanes of a warp touch 512 consecutive bytes per access
+  // (a row-major tile would give each lane its own 32-byte sector).  Loads bypass L1 (the data
+  // was written by another SM) and the next chunk's partial is loaded while this one is added.
+  float4* const wt = reinterpret_cast<float4*>(P.ws + (size_t)tile * 128 * BN) + trow;
   const int ncols = min(BN, P.N - col_base);
   const int nch = (ncols + 31) / 32;
+  float4 nxt[8];
+  if (split > 0) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) nxt[q] = __ldcg(wt + q * 128);
+  }
 #pragma unroll 1
   for (int c = 0; c < nch; ++c) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(tbase + c * 32, r);
     tmem_wait_ld();
     if (c + 1 >= nch) release();
-    float4* w4 = reinterpret_cast<float4*>(wrow + c * 32);
+    float4* const w4 = wt + (size_t)c * 8 * 128;
     if (split > 0) {
+      float4 cur[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cur[q] = nxt[q];
+      if (c + 1 < nch) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) nxt[q] = __ldcg(w4 + (8 + q) * 128);
+      }
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const float4 a = w4[q];
-        r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + a.x);
-        r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + a.y);
-        r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + a.z);
-        r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + a.w);
+        r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + cur[q].x);
+        r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + cur[q].y);
+        r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + cur[q].z);
+        r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + cur[q].w);
       }
     }
     if (!last) {
 #pragma unroll
       for (int q = 0; q < 8; ++q)
-        w4[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
-                            __uint_as_float(r[4 * q + 3]));
+        __stcg(w4 + q * 128, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                         __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
     } else {
       epilogue_chunk<EPI, OUT_F32>(r, row, col_base + c * 32, P.M, P.N, P.ep);
     }

@@ -46,7 +46,8 @@ typedef struct GemmArgs {
   int out_world;
   int rows_per_rank;
   long long peer_row_off;
-  // 0: automatic choice, 1: one CTA per 128 x BN tile, 2: CTA pairs (cta_group::2, 256 x 256 tiles)
+  // 0: automatic choice, 1: one CTA per 128 x BN tile, 2: CTA pairs (cta_group::2, 256 x 256 tiles),
+  // 3: one CTA per 128 x 128 tile (six operand stages)
   int cta_mode;
   // kEpiQkv: the head scatter applied in the epilogue (its qkv / ld / rows fields are unused;
   // the source rows are the GEMM rows).  Per-head RMS (norm_mode 0 / 1), full-width RoPE,
@@ -63,6 +64,7 @@ void dfl_gemm_set_epi_warps(int n);  // pair-kernel epilogue warps: 0 auto (8 fo
 // (their tiles share the grid; the tile shape follows args[0]).
 int dfl_gemm_bf16_group(const GemmArgs* const* args, int count, cudaStream_t stream);
 void dfl_gemm_set_pair_auto(int on);
+void dfl_gemm_set_split_force(int s);  // measurement: 0 = modelled split-K choice, 1..4 = forced K ranges
 
 // MXFP8 GEMM on the block-scaled tensor cores (tcgen05 kind::mxf8f6f4):
 //   D = epi(A . B^T), A [M, K] / B [N, K] FP8 E4M3 (K-major, row strides in

@@ -71,7 +71,7 @@ def _sel(items, cases):
     return [it for it in items if not cases or it[0] in cases]
 
 
-def bench_gemm(nat, iters, flush, peaks, cases, ref):
+def bench_gemm(nat, iters, flush, peaks, cases, ref, splits=False):
     rows = []
     for name, M, N, K in _sel(GEMM_SHAPES, cases):
         a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
@@ -79,14 +79,27 @@ def bench_gemm(nat, iters, flush, peaks, cases, ref):
         out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         t_ours = time_fn(lambda: nat.gemm(a, b, None, out=out, cta_mode=1), iters, flush=flush)
         t_pair = time_fn(lambda: nat.gemm(a, b, None, out=out, cta_mode=2), iters, flush=flush)
+        t_narrow = time_fn(lambda: nat.gemm(a, b, None, out=out, cta_mode=3), iters, flush=flush)
+        t_auto = time_fn(lambda: nat.gemm(a, b, None, out=out), iters, flush=flush)
         fl = 2.0 * M * N * K
         r = {"kernel": "gemm_tcgen05", "shape": name, "M": M, "N": N, "K": K, "ms": round(t_ours, 4),
              "tflops": round(fl / t_ours / 1e9, 1),
              "frac_of_measured_peak": round(fl / t_ours / 1e9 / peaks["bf16_tflops"], 3),
-             "pair_ms": round(t_pair, 4), "pair_tflops": round(fl / t_pair / 1e9, 1)}
+             "pair_ms": round(t_pair, 4), "pair_tflops": round(fl / t_pair / 1e9, 1),
+             "narrow_ms": round(t_narrow, 4), "narrow_tflops": round(fl / t_narrow / 1e9, 1),
+             "auto_ms": round(t_auto, 4), "auto_tflops": round(fl / t_auto / 1e9, 1)}
         if ref:
             t_ref = time_fn(lambda: torch.matmul(a, b.t(), out=out), iters, flush=flush)
             r.update({"cublas_ms": round(t_ref, 4), "cublas_tflops": round(fl / t_ref / 1e9, 1)})
+        if M <= 1152 and splits:  # small M: every split-K count, one CTA per tile and CTA pairs
+            sweep = {}
+            for sp in (1, 2, 3, 4):
+                nat.gemm_set_split_force(sp)
+                for mode, name in ((1, "single"), (2, "pair")):
+                    sweep[f"{name}_s{sp}"] = round(time_fn(lambda: nat.gemm(a, b, None, out=out, cta_mode=mode),
+                                                           iters, flush=flush), 4)
+            nat.gemm_set_split_force(0)
+            r["split_sweep_ms"] = sweep
         rows.append(r)
         del a, b, out
     return rows
@@ -262,6 +275,7 @@ def main(argv=None):
     ap.add_argument("--cases", default="")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-ref", action="store_true")
+    ap.add_argument("--split-sweep", action="store_true", help="small-M GEMMs: time every forced split-K count")
     ap.add_argument("--out", default=None, help="also write the rows as JSON here")
     args = ap.parse_args(argv)
     from difflet_b200 import _native
@@ -276,7 +290,7 @@ def main(argv=None):
     ref = not args.no_ref
     rows = []
     if "gemm" in only:
-        rows += bench_gemm(nat, args.iters, flush, peaks, cases, ref)
+        rows += bench_gemm(nat, args.iters, flush, peaks, cases, ref, args.split_sweep)
     if "attn" in only:
         rows += bench_attn(nat, args.iters, flush, peaks, cases, ref)
     if "ln" in only:

@@ -430,7 +430,10 @@ def test_row_sumsq_and_external_rms_norm(native):
     _close(v, vc.cuda())
 
 
-@pytest.mark.parametrize("M,N,K", [(300, 3072, 4096), (576, 3072, 15360), (64, 1536, 2048)])
+# the planner picks 2 ranges for (576, 3072, 15360), 3 for (512, 3072, 12288) and (256, 1024, 4096),
+# 4 for (256, 1024, 16384) and (256, 512, 8192) (128-column tiles)
+@pytest.mark.parametrize("M,N,K", [(300, 3072, 4096), (576, 3072, 15360), (64, 1536, 2048), (512, 3072, 12288),
+                                   (256, 1024, 4096), (256, 1024, 16384), (256, 512, 8192)])
 def test_gemm_split_k_small_m(native, monkeypatch, M, N, K):
     """Small-M GEMMs split K across SMs (serial f32 fixup): plain + bias and the gated residual
     epilogue against the fp32 reference, repeated calls (the counters return to 0), and a
