@@ -40,7 +40,8 @@ GEMM_SHAPES = [
     ("wan_ffn_down_sp4", 18900, 5120, 13824),
     ("square_8192", 8192, 8192, 8192),
 ]
-ATTN_CASES = [("flux_1gpu", 1, 24, 4608), ("flux_sp8_heads", 1, 3, 4608), ("wan_ulysses4", 1, 10, 75600 // 4),
+ATTN_CASES = [("flux_1gpu", 1, 24, 4608), ("flux_sp2_heads", 1, 12, 4608), ("flux_sp4_heads", 1, 6, 4608),
+              ("flux_sp8_heads", 1, 3, 4608), ("wan_ulysses4", 1, 10, 75600 // 4),
               ("wan_ulysses4_rank", 1, 10, 75600), ("hunyuan_ulysses8_rank", 1, 3, 118800)]
 LN_CASES = [("flux_ln", 4608, 3072), ("wan_ln_sp4", 18900, 5120)]
 
