@@ -175,11 +175,30 @@ def bench_tp(world, rank, iters, peak, hbm):
         dist.all_reduce(y)
 
     tf, tb = _timeit(fused, iters), _timeit(baseline, iters)
+    # where the fused path's time goes: the GEMM alone (local output), the GEMM whose epilogue
+    # stores partial rows to their owners, one device barrier, the reducer alone
+    nat = F.native()
+    rpr = -(-M // world)
+    slots = tp.slots(rpr, D, torch.bfloat16)
+    peers = tp.heap.peer_ptrs(slots)
+    rows = max(0, min(rpr, M - rank * rpr))
+    outs = tp.heap.peer_ptrs(out)
+    parts = {
+        "gemm_local_us": _timeit(lambda: F.linear(x, w, None, out=y), iters),
+        "gemm_scatter_us": _timeit(lambda: nat.gemm(x, w, None, None, 0, out_peer=peers, rows_per_rank=rpr,
+                                                    peer_row_off=rank * rpr, ldd=D), iters),
+        "barrier_us": _timeit(tp.heap.barrier, iters),
+        "reduce_us": _timeit(lambda: nat.tp_reduce(slots, rpr, world, rows, D, rank * rpr, b, gate, M, out, outs,
+                                                   out.stride(0), rank * rpr), iters),
+        "allreduce_nccl_us": _timeit(lambda: dist.all_reduce(y), iters),
+    }
     flops = 2.0 * M * D * K
     link = 2.0 * M * D * 2 * (world - 1) / world  # partial rows out + finished rows out
     hbm_b = (M * K + D * K + 3 * M * D) * 2.0
     tp.close()
-    return _row(f"tp_row_reduce (M {M}, N {D}, K {K})", tf, tb, flops, link, hbm_b, peak, hbm)
+    row = _row(f"tp_row_reduce (M {M}, N {D}, K {K})", tf, tb, flops, link, hbm_b, peak, hbm)
+    row["parts"] = {k: round(v * 1e6, 1) for k, v in parts.items()}
+    return row
 
 
 def bench_sp(world, rank, iters, peak, hbm):
