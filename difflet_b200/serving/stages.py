@@ -195,11 +195,12 @@ class StagePipeline:
 
 # ------------------------------------------------------------------ stages of a DiffletPipeline
 def _to_host(p: DecodedPayload, ctx: StageContext) -> OutputPayload:
+    """The request's result on the host: the first item of the batch (the serving API answers
+    one image / video per request)."""
     out = p.output
     if out is None:
         return OutputPayload(None)
-    if isinstance(out, (list, tuple)):
-        out = out[0]
+    out = out[0]
     return OutputPayload(out.cpu() if hasattr(out, "cpu") else out)
 
 

@@ -36,7 +36,7 @@ def test_run_records_events_and_reports_stages():
     pipe = _two_stage()
     ctx = StageContext("rid-1", on_stage=seen.append)
     out = pipe.run({"prompt": "x"}, ctx)
-    assert torch.equal(out, torch.ones(2))
+    assert torch.equal(out, torch.ones(2))  # _two_stage's own output stage passes it through
     assert seen == ["generate", "output"]
     kinds = [(e.stage, e.kind) for e in ctx.events]
     assert kinds == [("generate", "start"), ("generate", "complete"), ("output", "start"), ("output", "complete")]
@@ -121,10 +121,10 @@ def test_phase_pipeline_of_an_application():
     ctx = StageContext("r")
     video = stages.run({"prompt": "p", "num_inference_steps": 3, "unused": 1}, ctx)
     assert app.runs[0].done == [0, 1, 2]
-    assert video.dtype == torch.uint8 and video.shape == (1, 2, 2, 2, 3)
+    assert video.dtype == torch.uint8 and video.shape == (2, 2, 2, 3)  # the first video of the batch
     assert (video == 128).all()  # 0 in [-1, 1] -> 127.5 -> 128
     lat = stages.run({"prompt": "p", "num_inference_steps": 2, "output_type": "latent"}, StageContext("r2"))
-    assert torch.equal(lat, torch.full((3,), 2.0))
+    assert torch.equal(lat, torch.tensor(2.0))  # first element of the latent batch
     # cancellation polled between denoise steps
     n = {"k": 0}
 
@@ -143,12 +143,12 @@ def test_generic_pipeline_wraps_the_call():
     def call(**kw):
         seen.update(kw)
         kw["callback"](0, None)
-        return [torch.ones(1, 2)]
+        return torch.ones(1, 2)  # a batch of one
 
     stages = pipeline_stages(call)
     assert stages.stage_ids == ("generate", "output")
     out = stages.run({"prompt": "p"}, StageContext("r"))
-    assert torch.equal(out, torch.ones(1, 2)) and seen["prompt"] == "p"
+    assert torch.equal(out, torch.ones(2)) and seen["prompt"] == "p"
     answers = iter([False, True])  # the check before the stage passes; the step callback cancels
     with pytest.raises(RequestCancelled):
         stages.run({"prompt": "p"}, StageContext("r", should_cancel=lambda: next(answers)))
