@@ -241,6 +241,13 @@ def make_sequence_parallel(parallel, device, transport: str | None = None):
         from difflet_b200.parallel import ring
 
         if mode == "ring":
+            if not fused and device.type == "cuda" and parallel.tp_degree > 1:
+                # The NCCL ring baseline inside tensor parallelism (send / recv on the cp subgroup
+                # interleaved with the tp all-reduces) raised an illegal-address fault on 4 B200s,
+                # twice; its cause is not found, so it stays off the GPU.  The peer-memory ring
+                # inside TP is the product path and matched the single-GPU model.
+                raise NotImplementedError("cp_mode='ring' with the NCCL transport inside tensor parallelism is "
+                                          "disabled on CUDA; use the fused (peer-memory) transport")
             return (ring.PeerRing if fused else ring.CollectiveRing)(group, ranks, device)
         return (ring.PeerGatherKV if fused else ring.CollectiveGatherKV)(group, ranks, device)
     return (PeerUlysses if fused else CollectiveUlysses)(group, ranks, device)
