@@ -361,6 +361,20 @@ def run_mmdit(args, world, rank):
     ms = _max_over_ranks(a.elapsed_time(b) / args.steps, world)
     _native.check_device_errors()
     del F
+    decode = None
+    if args.decode and hv and app.vae is not None and rank == 0:
+        # one VAE decode of the clip's latents on rank 0 (spatially tiled, the native channels-last
+        # decoder on the GPU): latents [1, 16, T, h, w] -> frames [1, 3, Fr, H, W]
+        zlat = torch.randn(1, cfg.latent_channels, T, lh, lw, generator=gen).to(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        video = app.vae.decode(zlat)
+        t1.record()
+        torch.cuda.synchronize()
+        decode = {"ms": round(t0.elapsed_time(t1), 1), "frames": int(video.shape[2]), "shape": list(video.shape),
+                  "decoder": type(app.vae).__name__}
+        del video
+        _native.check_device_errors()
     if rank == 0:
         name = "HunyuanVideo 720x1280x129" if hv else "Qwen-Image 1328x1328 " + ("MXFP8" if kw else "bf16")
         print(json.dumps({
@@ -372,7 +386,8 @@ def run_mmdit(args, world, rank):
             "config": {"model": model_id, "global_batch": 1, "seq_len": S_img + text_len, "height": H, "width": W,
                        "frames": Fr, "true_cfg": true_cfg, "parallelism": layout, "load_s": round(load_s, 1),
                        "l2": "weights + activations stream from HBM every step; no flush"},
-            "clocks": sampler.summary(), "gpu_launches": int(launches * args.steps), "e2e": None}), flush=True)
+            "clocks": sampler.summary(), "gpu_launches": int(launches * args.steps), "e2e": None,
+            "decode": decode}), flush=True)
     torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
@@ -423,7 +438,8 @@ def main(argv=None):
                     help="wan: parallel layout (default by N: 1 batched CFG, 2 cfg2, 4 cfg2xulysses2, "
                          "8 cfg2xulysses4; also e.g. ulysses8, cfg2xtp2xulysses2)")
     ap.add_argument("--frames", type=int, default=81)
-    ap.add_argument("--decode", action="store_true", help="wan: also time one VAE decode of the final latents")
+    ap.add_argument("--decode", action="store_true",
+                    help="wan / hunyuan: also time one VAE decode of the clip's latents (rank 0 for hunyuan)")
     ap.add_argument("--e2e", action="store_true",
                     help="wan: time the full 40-step generate + decode through the public API (minutes at N=1)")
     args = ap.parse_args(argv)

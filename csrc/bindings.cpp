@@ -660,7 +660,7 @@ void tp_reduce(const at::Tensor& slots, int64_t slot_rows, int64_t world, int64_
 
 at::Tensor conv3d(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t kt,
                   int64_t kh, int64_t kw, bool causal, const c10::optional<at::Tensor>& resid, bool silu,
-                  c10::optional<at::Tensor> out, bool valid_t, bool valid_h) {
+                  c10::optional<at::Tensor> out, bool valid_t, bool valid_h, bool valid_w) {
   check_bf16_cuda(x, "x");
   check_bf16_cuda(w, "w");
   TORCH_CHECK(x.dim() == 5 && x.is_contiguous(), "x must be contiguous [N, T, H, W, Ci]");
@@ -668,10 +668,11 @@ at::Tensor conv3d(const at::Tensor& x, const at::Tensor& w, const c10::optional<
   const c10::cuda::CUDAGuard guard(x.device());
   const int64_t Co = w.size(0);
   const int64_t To = valid_t ? x.size(1) - kt + 1 : x.size(1), Ho = valid_h ? x.size(2) - kh + 1 : x.size(2);
-  TORCH_CHECK(To > 0 && Ho > 0, "valid convolution of fewer frames / rows than its kernel");
-  at::Tensor y = (out.has_value() && out->defined()) ? *out : at::empty({x.size(0), To, Ho, x.size(3), Co}, x.options());
-  TORCH_CHECK(y.is_contiguous() && y.numel() == x.size(0) * To * Ho * x.size(3) * Co,
-              "out must be contiguous [N, T_out, H_out, W, Co]");
+  const int64_t Wo = valid_w ? x.size(3) - kw + 1 : x.size(3);
+  TORCH_CHECK(To > 0 && Ho > 0 && Wo > 0, "valid convolution of fewer frames / rows / columns than its kernel");
+  at::Tensor y = (out.has_value() && out->defined()) ? *out : at::empty({x.size(0), To, Ho, Wo, Co}, x.options());
+  TORCH_CHECK(y.is_contiguous() && y.numel() == x.size(0) * To * Ho * Wo * Co,
+              "out must be contiguous [N, T_out, H_out, W_out, Co]");
   ConvArgs a{};
   a.x = x.data_ptr();
   a.w = w.data_ptr();
@@ -691,10 +692,76 @@ at::Tensor conv3d(const at::Tensor& x, const at::Tensor& w, const c10::optional<
   a.N = (int)x.size(0), a.T = (int)x.size(1), a.H = (int)x.size(2), a.W = (int)x.size(3), a.Ci = (int)x.size(4);
   a.Co = (int)Co;
   a.kt = (int)kt, a.kh = (int)kh, a.kw = (int)kw, a.causal = causal ? 1 : 0, a.silu = silu ? 1 : 0;
-  a.valid_t = valid_t ? 1 : 0, a.valid_h = valid_h ? 1 : 0;
+  a.valid_t = valid_t ? 1 : 0, a.valid_h = valid_h ? 1 : 0, a.valid_w = valid_w ? 1 : 0;
   a.err = err_ptr();
   DFL_CHECK_RC(dfl_conv3d(&a, cur_stream()), "conv3d");
   return y;
+}
+
+// HunyuanVideo-style VAE helpers (vae_gn.cu): channels-last [N, T, H, W, C] bf16 volumes.
+at::Tensor gn_stats(const at::Tensor& x, int64_t G, double eps) {
+  check_bf16_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 5 && x.is_contiguous(), "x must be contiguous [N, T, H, W, C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t N = x.size(0), C = x.size(4), P = x.size(1) * x.size(2) * x.size(3);
+  int dev = x.device().index();
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int nblk = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)sms * 4 / std::max<int64_t>(N, 1), P / 64));
+  at::Tensor partial = at::empty({nblk, N, G}, x.options().dtype(at::kFloat));
+  at::Tensor stats = at::empty({N, G, 2}, x.options().dtype(at::kFloat));
+  DFL_CHECK_RC(dfl_gn_stats(x.data_ptr(), (int)N, P, (int)C, (int)G, (float)eps, partial.data_ptr<float>(), nblk,
+                            stats.data_ptr<float>(), cur_stream()),
+               "gn_stats");
+  return stats;
+}
+
+void gn_apply(const at::Tensor& x, const at::Tensor& stats, const at::Tensor& gamma, const at::Tensor& beta,
+              int64_t G, bool silu, at::Tensor y, int64_t ot, int64_t oh, int64_t ow) {
+  check_bf16_cuda(x, "x");
+  check_bf16_cuda(y, "y");
+  TORCH_CHECK(x.dim() == 5 && x.is_contiguous() && y.dim() == 5 && y.is_contiguous(), "x, y contiguous 5-D");
+  TORCH_CHECK(y.size(0) == x.size(0) && y.size(4) == x.size(4), "y must match x in N and C");
+  TORCH_CHECK(stats.scalar_type() == at::kFloat && stats.is_contiguous() && stats.numel() == x.size(0) * G * 2,
+              "stats f32 [N, G, 2]");
+  TORCH_CHECK(gamma.scalar_type() == at::kFloat && beta.scalar_type() == at::kFloat && gamma.is_contiguous() &&
+                  beta.is_contiguous() && gamma.numel() == x.size(4) && beta.numel() == x.size(4),
+              "gamma / beta f32 [C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  GnApplyArgs a{};
+  a.x = x.data_ptr(), a.y = y.data_ptr(), a.stats = stats.data_ptr<float>();
+  a.gamma = gamma.data_ptr<float>(), a.beta = beta.data_ptr<float>();
+  a.N = (int)x.size(0), a.T = (int)x.size(1), a.H = (int)x.size(2), a.W = (int)x.size(3), a.C = (int)x.size(4);
+  a.G = (int)G;
+  a.Ty = (int)y.size(1), a.Hy = (int)y.size(2), a.Wy = (int)y.size(3);
+  a.ot = (int)ot, a.oh = (int)oh, a.ow = (int)ow, a.silu = silu ? 1 : 0;
+  DFL_CHECK_RC(dfl_gn_apply(&a, cur_stream()), "gn_apply");
+}
+
+void pad_replicate(at::Tensor y, int64_t pt, int64_t ph, int64_t pw, int64_t T, int64_t H, int64_t W) {
+  check_bf16_cuda(y, "y");
+  TORCH_CHECK(y.dim() == 5 && y.is_contiguous(), "y must be contiguous [N, Ty, Hy, Wy, C]");
+  const c10::cuda::CUDAGuard guard(y.device());
+  PadArgs a{};
+  a.y = y.data_ptr();
+  a.N = (int)y.size(0), a.Ty = (int)y.size(1), a.Hy = (int)y.size(2), a.Wy = (int)y.size(3), a.C = (int)y.size(4);
+  a.pt = (int)pt, a.ph = (int)ph, a.pw = (int)pw, a.T = (int)T, a.H = (int)H, a.W = (int)W;
+  DFL_CHECK_RC(dfl_pad_replicate(&a, cur_stream()), "pad_replicate");
+}
+
+void upsample_causal(const at::Tensor& x, bool up_t, at::Tensor y, int64_t ot, int64_t oh, int64_t ow) {
+  check_bf16_cuda(x, "x");
+  check_bf16_cuda(y, "y");
+  TORCH_CHECK(x.dim() == 5 && x.is_contiguous() && y.dim() == 5 && y.is_contiguous(), "x, y contiguous 5-D");
+  TORCH_CHECK(y.size(0) == x.size(0) && y.size(4) == x.size(4), "y must match x in N and C");
+  const c10::cuda::CUDAGuard guard(x.device());
+  UpsampleArgs a{};
+  a.x = x.data_ptr(), a.y = y.data_ptr();
+  a.N = (int)x.size(0), a.T = (int)x.size(1), a.H = (int)x.size(2), a.W = (int)x.size(3), a.C = (int)x.size(4);
+  a.up_t = up_t ? 1 : 0;
+  a.Ty = (int)y.size(1), a.Hy = (int)y.size(2), a.Wy = (int)y.size(3);
+  a.ot = (int)ot, a.oh = (int)oh, a.ow = (int)ow;
+  DFL_CHECK_RC(dfl_upsample_causal(&a, cur_stream()), "upsample_causal");
 }
 
 // VAE slab helpers: x [F, Hl, W, C]; y [F, Ho + 2 halo, Wo, C]; up / down = peer pointers (0: none).
@@ -859,7 +926,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv3d", &conv3d, "implicit-GEMM tcgen05 convolution (channels-last)", py::arg("x"), py::arg("w"),
         py::arg("bias") = py::none(), py::arg("kt") = 3, py::arg("kh") = 3, py::arg("kw") = 3,
         py::arg("causal") = true, py::arg("resid") = py::none(), py::arg("silu") = false, py::arg("out") = py::none(),
-        py::arg("valid_t") = false, py::arg("valid_h") = false);
+        py::arg("valid_t") = false, py::arg("valid_h") = false, py::arg("valid_w") = false);
   m.def("tp_reduce", &tp_reduce, py::arg("slots"), py::arg("slot_rows"), py::arg("world"), py::arg("rows"),
         py::arg("N"), py::arg("row0"), py::arg("bias") = py::none(), py::arg("gate") = py::none(),
         py::arg("rows_per_batch") = 0, py::arg("resid") = py::none(), py::arg("out") = std::vector<int64_t>{},
@@ -870,6 +937,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("vae_chan_norm", &vae_chan_norm, py::arg("x"), py::arg("gamma"), py::arg("y"), py::arg("silu"),
         py::arg("halo") = false, py::arg("up") = 0, py::arg("up_rows") = 0, py::arg("down") = 0,
         py::arg("down_rows") = 0);
+  m.def("gn_stats", &gn_stats, py::arg("x"), py::arg("G"), py::arg("eps"));
+  m.def("gn_apply", &gn_apply, py::arg("x"), py::arg("stats"), py::arg("gamma"), py::arg("beta"), py::arg("G"),
+        py::arg("silu"), py::arg("y"), py::arg("ot") = 0, py::arg("oh") = 0, py::arg("ow") = 0);
+  m.def("pad_replicate", &pad_replicate, py::arg("y"), py::arg("pt"), py::arg("ph"), py::arg("pw"), py::arg("T"),
+        py::arg("H"), py::arg("W"));
+  m.def("upsample_causal", &upsample_causal, py::arg("x"), py::arg("up_t"), py::arg("y"), py::arg("ot") = 0,
+        py::arg("oh") = 0, py::arg("ow") = 0);
   m.def("vae_upsample2x", &vae_upsample2x, py::arg("x"), py::arg("y"), py::arg("halo") = false, py::arg("up") = 0,
         py::arg("up_rows") = 0, py::arg("down") = 0, py::arg("down_rows") = 0);
   m.def("guided_step", &guided_step, py::arg("a"), py::arg("b_ptr"), py::arg("scale"), py::arg("x"),

@@ -49,8 +49,8 @@ DFL_DEVICE uint64_t make_sdesc(uint32_t addr) {
 }
 
 struct ConvGeom {
-  int N, T, H, W, Ci, Co;  // output extents (W is the same for input and output)
-  int Ti, Hi;              // input frames / rows
+  int N, T, H, W, Ci, Co;  // output extents
+  int Ti, Hi, Wi;          // input frames / rows / columns
   int kt, kh, kw, pt, ph, pw;
   int wtiles;   // ceil(W / 128)
   int csteps;   // Ci / BK
@@ -230,9 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 int make_tmap_x(CUtensorMap* map, const void* base, const ConvGeom& g, int BK) {
   auto fn = dfl_host::get_encode_tiled();
   if (!fn) return 999;
-  cuuint64_t dims[5] = {(cuuint64_t)g.Ci, (cuuint64_t)g.W, (cuuint64_t)g.Hi, (cuuint64_t)g.Ti, (cuuint64_t)g.N};
-  cuuint64_t strides[4] = {(cuuint64_t)g.Ci * 2, (cuuint64_t)g.W * g.Ci * 2, (cuuint64_t)g.Hi * g.W * g.Ci * 2,
-                           (cuuint64_t)g.Ti * g.Hi * g.W * g.Ci * 2};
+  cuuint64_t dims[5] = {(cuuint64_t)g.Ci, (cuuint64_t)g.Wi, (cuuint64_t)g.Hi, (cuuint64_t)g.Ti, (cuuint64_t)g.N};
+  cuuint64_t strides[4] = {(cuuint64_t)g.Ci * 2, (cuuint64_t)g.Wi * g.Ci * 2, (cuuint64_t)g.Hi * g.Wi * g.Ci * 2,
+                           (cuuint64_t)g.Ti * g.Hi * g.Wi * g.Ci * 2};
   cuuint32_t box[5] = {(cuuint32_t)BK, (cuuint32_t)BM, 1, 1, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   return (int)fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
@@ -293,13 +293,14 @@ int dispatch_bn(int BN, const CUtensorMap& tx, const CUtensorMap& tw, const Conv
 
 extern "C" int dfl_conv3d(const ConvArgs* a, cudaStream_t stream) {
   ConvGeom g{};
-  g.N = a->N, g.Ti = a->T, g.Hi = a->H, g.W = a->W, g.Ci = a->Ci, g.Co = a->Co;
+  g.N = a->N, g.Ti = a->T, g.Hi = a->H, g.Wi = a->W, g.Ci = a->Ci, g.Co = a->Co;
   g.kt = a->kt, g.kh = a->kh, g.kw = a->kw;
   g.pt = a->valid_t ? 0 : (a->causal ? a->kt - 1 : a->kt / 2);
   g.ph = a->valid_h ? 0 : a->kh / 2;
-  g.pw = a->kw / 2;
+  g.pw = a->valid_w ? 0 : a->kw / 2;
   g.T = a->valid_t ? g.Ti - a->kt + 1 : g.Ti;
   g.H = a->valid_h ? g.Hi - a->kh + 1 : g.Hi;
+  g.W = a->valid_w ? g.Wi - a->kw + 1 : g.Wi;
   if (g.N <= 0 || g.T <= 0 || g.H <= 0 || g.W <= 0) return -2;
   for (int k : {g.kt, g.kh, g.kw})
     if (k != 1 && k != 3) return -3;

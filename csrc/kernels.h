@@ -301,8 +301,10 @@ typedef struct ConvArgs {
   int kt, kh, kw, causal, silu;
   // valid_t: no temporal padding (the input already starts with the causal context, e.g. a
   // streaming cache), T_out = T - kt + 1; valid_h: no padding along H (the input carries halo
-  // rows from the neighbouring spatial slabs), H_out = H - kh + 1.  Otherwise T / H are kept.
-  int valid_t, valid_h;
+  // rows from the neighbouring spatial slabs), H_out = H - kh + 1; valid_w: no padding along W
+  // (the input carries its own border columns, e.g. replicate padding), W_out = W - kw + 1.
+  // Otherwise T / H / W are kept.
+  int valid_t, valid_h, valid_w;
   int* err;
 } ConvArgs;
 int dfl_conv3d(const ConvArgs* a, cudaStream_t stream);
@@ -323,6 +325,33 @@ typedef struct VaeRowArgs {
 int dfl_vae_chan_norm(const VaeRowArgs* a, cudaStream_t stream);
 // nearest 2x upsample: Ho = 2 Hl, Wo = 2 W
 int dfl_vae_upsample2x(const VaeRowArgs* a, cudaStream_t stream);
+
+// Channels-last GroupNorm / replicate padding / causal upsampling of the HunyuanVideo-style VAE
+// (vae_gn.cu).  Volumes are bf16 [N, T, H, W, C] contiguous, C a multiple of 8; destinations are
+// larger buffers [N, Ty, Hy, Wy, C] written at the offset (ot, oh, ow).
+// Clip statistics of GroupNorm(G): stats f32 [N][G][2] = {mean, 1 / sqrt(var + eps)} over the
+// P = T * H * W pixels and C / G channels of each group; partial: f32 scratch [nblk][N][G].
+int dfl_gn_stats(const void* x, int N, long long P, int C, int G, float eps, float* partial, int nblk,
+                 float* stats, cudaStream_t stream);
+typedef struct GnApplyArgs {
+  const void* x; void* y; const float* stats; const float* gamma; const float* beta;  // gamma / beta f32 [C]
+  int N, T, H, W, C, G;
+  int Ty, Hy, Wy, ot, oh, ow;
+  int silu;
+} GnApplyArgs;
+int dfl_gn_apply(const GnApplyArgs* a, cudaStream_t stream);
+typedef struct PadArgs {  // fill the border of y around its interior box (pt, ph, pw) + (T, H, W)
+  void* y;
+  int N, Ty, Hy, Wy, C;
+  int pt, ph, pw, T, H, W;
+} PadArgs;
+int dfl_pad_replicate(const PadArgs* a, cudaStream_t stream);
+typedef struct UpsampleArgs {  // nearest 2x in H, W; up_t: frame 0 once, later frames twice
+  const void* x; void* y;
+  int N, T, H, W, C, up_t;
+  int Ty, Hy, Wy, ot, oh, ow;
+} UpsampleArgs;
+int dfl_upsample_causal(const UpsampleArgs* a, cudaStream_t stream);
 
 // Copy-engine copy (peer -> local over NVLink; no SM work, no kernel).
 int dfl_memcpy_async(void* dst, const void* src, long long nbytes, cudaStream_t stream);

@@ -37,6 +37,7 @@ CUDA_SOURCES = [
     "probe_noalloc.cu",
     "sched.cu",
     "vae.cu",
+    "vae_gn.cu",
 ]
 CPP_SOURCES = ["bindings.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "probe_noalloc.h", "gemm_epilogue.cuh"]

@@ -9,7 +9,12 @@ guidance-distilled (embedded guidance 6.0, flow shift 7.0); 1.5 runs true CFG
 from __future__ import annotations
 
 from difflet_b200.models.mmdit.entry import MMDiTEngine
-from difflet_b200.models.vae.hunyuan_vae import HunyuanVAEConfig, HunyuanVAEDecoder
+from difflet_b200.models.vae.hunyuan_vae import HunyuanVAEConfig, HunyuanVAEDecoder, HunyuanVAENative
+
+
+def _vae_class(dev):
+    """Channels-last native kernels on a GPU; the PyTorch decoder on the CPU."""
+    return HunyuanVAENative if getattr(dev, "type", str(dev)) == "cuda" else HunyuanVAEDecoder
 
 
 class HunyuanVideoEngine(MMDiTEngine):
@@ -19,10 +24,10 @@ class HunyuanVideoEngine(MMDiTEngine):
 
     def make_vae(self, dev):
         if self.kw.get("random_init") or not self.model_path:
-            return HunyuanVAEDecoder.random_init(HunyuanVAEConfig(), device=dev, dtype=self.dtype, seed=5)
+            return _vae_class(dev).random_init(HunyuanVAEConfig(), device=dev, dtype=self.dtype, seed=5)
         from difflet_b200.utils.checkpoint import load_component
 
-        return HunyuanVAEDecoder(HunyuanVAEConfig(), load_component(self.model_path, "vae", dtype=self.dtype, device=dev))
+        return _vae_class(dev)(HunyuanVAEConfig(), load_component(self.model_path, "vae", dtype=self.dtype, device=dev))
 
     def app_kwargs(self):
         return {"flow_shift": float(self.kw.get("flow_shift", 7.0)), "text_len": 256}
@@ -36,10 +41,10 @@ class HunyuanVideo15Engine(HunyuanVideoEngine):
     def make_vae(self, dev):
         cfg = HunyuanVAEConfig(latent_channels=32, block_out_channels=(128, 256, 512, 1024, 1024))
         if self.kw.get("random_init") or not self.model_path:
-            return HunyuanVAEDecoder.random_init(cfg, device=dev, dtype=self.dtype, seed=6)
+            return _vae_class(dev).random_init(cfg, device=dev, dtype=self.dtype, seed=6)
         from difflet_b200.utils.checkpoint import load_component
 
-        return HunyuanVAEDecoder(cfg, load_component(self.model_path, "vae", dtype=self.dtype, device=dev))
+        return _vae_class(dev)(cfg, load_component(self.model_path, "vae", dtype=self.dtype, device=dev))
 
     def app_kwargs(self):
         return {"flow_shift": float(self.kw.get("flow_shift", 5.0)), "text_len": 256, "true_cfg": True,

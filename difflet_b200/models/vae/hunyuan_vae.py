@@ -11,7 +11,11 @@ spatially only and the rest in (t, h, w), GroupNorm + SiLU + conv out.
 
 Memory at 720p x 129 frames is bounded by decoding overlapping spatial tiles
 (whole clip in time per tile) and blending the overlaps linearly.  Weights use
-the diffusers names; convolutions run through cuDNN.
+the diffusers names.  ``HunyuanVAEDecoder`` is the PyTorch statement of the
+decoder (NCTHW, cuDNN convolutions: the oracle); ``HunyuanVAENative`` runs the
+same tiles channels-last on the engine's kernels -- the tcgen05 implicit-GEMM
+convolution (``csrc/conv.cu``, valid padding on a replicate-padded buffer),
+clip GroupNorm (+ SiLU) and the causal upsampler (``csrc/vae_gn.cu``).
 """
 
 from __future__ import annotations
@@ -197,3 +201,137 @@ class HunyuanVAEDecoder:
                 out[:, :, :, y0 * s:y1 * s, x0 * s:x1 * s] += dec * m
                 weight[:, :, :, y0 * s:y1 * s, x0 * s:x1 * s] += m
         return (out / weight).clamp(-1, 1).to(dt)
+
+
+# ------------------------------------------------------------------------------------------------
+# Channels-last decoder on the native kernels
+# ------------------------------------------------------------------------------------------------
+def _pad32(n: int) -> int:
+    return -(-n // 32) * 32
+
+
+class _NConv:
+    """A convolution in kernel layout, input / output channels padded to multiples of 32."""
+
+    def __init__(self, w, b, dt):
+        from difflet_b200.ops.fused import conv_weight
+
+        Co, Ci = w.shape[:2]
+        self.k = tuple(w.shape[2:])
+        self.ci, self.co = Ci, Co
+        self.Ci, self.Co = _pad32(Ci), _pad32(Co)
+        w5 = torch.zeros((self.Co, self.Ci) + self.k, device=w.device, dtype=torch.float32)
+        w5[:Co, :Ci] = w.float()
+        self.w2 = conv_weight(w5.to(dt))
+        bb = torch.zeros(self.Co, device=w.device, dtype=torch.float32)
+        bb[:Co] = b.float()
+        self.b = bb.to(dt)
+
+
+class HunyuanVAENative(HunyuanVAEDecoder):
+    """The HunyuanVideo decoder channels-last [N, T, H, W, C] on the native kernels (any device:
+    on the CPU every op runs its PyTorch oracle).  Each 3x3x3 causal convolution reads a buffer
+    [N, T + 2, H + 2, W + 2, C] whose interior the producer writes (GroupNorm + SiLU, the causal
+    upsampler, or a copy), then ``pad_replicate`` fills the two leading frames and the one-pixel
+    border the way the reference's replicate padding does, and the convolution runs with valid
+    padding in T, H and W.  The mid-block attention (one 512-wide head, frame-causal mask) stays
+    on PyTorch SDPA."""
+
+    def __init__(self, cfg: HunyuanVAEConfig, weights: dict):
+        super().__init__(cfg, weights)
+        self._convs = None
+        self._norms = None
+
+    def _prep(self):
+        if self._convs is None:
+            dt = self.w["decoder.conv_in.conv.weight"].dtype
+            self._convs = {n[: -len(".conv.weight")]: _NConv(self.w[n], self.w[n[: -len("weight")] + "bias"], dt)
+                           for n in self.w if n.endswith(".conv.weight")}
+            self._norms = {n[: -len(".weight")]: (self.w[n].float().contiguous(),
+                                                  self.w[n[: -len("weight")] + "bias"].float().contiguous())
+                           for n in self.w if n.endswith(".weight") and self.w[n].dim() == 1}
+        return self._convs
+
+    def _gn_into(self, x, name, silu, y, offs=(0, 0, 0)):
+        from difflet_b200.ops import fused as F
+
+        g, b = self._norms[name]
+        st = F.gn_stats(x, self.cfg.norm_groups, 1e-6)
+        return F.gn_apply(x, st, g, b, self.cfg.norm_groups, silu=silu, y=y, offs=offs)
+
+    def _conv3(self, name, fill, T, H, W, resid=None, like=None):
+        """3x3x3 causal conv of the (T, H, W) volume that ``fill(buf, offs)`` writes."""
+        from difflet_b200.ops import fused as F
+
+        cv = self._convs[name]
+        alloc = torch.zeros if cv.Ci != cv.ci else torch.empty  # padded channels must read as zero
+        buf = alloc(1, T + 2, H + 2, W + 2, cv.Ci, device=like.device, dtype=like.dtype)
+        fill(buf, (2, 1, 1))
+        F.pad_replicate(buf, (2, 1, 1), (T, H, W))
+        padded = cv.Co != cv.co
+        y = F.conv_cl(buf, cv.w2, cv.b, kt=3, kh=3, kw=3, valid_t=True, valid_h=True, valid_w=True,
+                      resid=None if padded else resid)
+        if padded:
+            y = y[..., : cv.co].contiguous()
+            if resid is not None:
+                y = y + resid
+        return y
+
+    def _pointwise(self, name, x):
+        from difflet_b200.ops import fused as F
+
+        cv = self._convs[name]
+        return F.conv_cl(x, cv.w2, cv.b, kt=1, kh=1, kw=1)[..., : cv.co].contiguous()
+
+    def _nres(self, x, n):
+        _, T, H, W, _ = x.shape
+        h = self._pointwise(n + ".conv_shortcut", x) if n + ".conv_shortcut" in self._convs else x
+        y = self._conv3(n + ".conv1", lambda buf, o: self._gn_into(x, n + ".norm1", True, buf, o), T, H, W, like=x)
+        return self._conv3(n + ".conv2", lambda buf, o: self._gn_into(y, n + ".norm2", True, buf, o), T, H, W,
+                           resid=h, like=x)
+
+    def _nattn(self, x, n):
+        _, T, H, W, C = x.shape
+        y = self._gn_into(x, n + ".group_norm", False, torch.empty_like(x)).reshape(1, T * H * W, C)
+        lin = lambda t, m: Fn.linear(t, self.w[f"{n}.{m}.weight"], self.w[f"{n}.{m}.bias"])  # noqa: E731
+        q, k, v = (lin(y, m)[:, None] for m in ("to_q", "to_k", "to_v"))
+        frame = torch.arange(T, device=x.device).repeat_interleave(H * W)
+        mask = frame[None, :] <= frame[:, None]
+        o = Fn.scaled_dot_product_attention(q, k, v, attn_mask=mask)[:, 0]
+        return x + lin(o, "to_out.0").view(1, T, H, W, C)
+
+    def _nup(self, x, n, up_t):
+        from difflet_b200.ops import fused as F
+
+        _, T, H, W, _ = x.shape
+        To = 2 * T - 1 if up_t else T
+        return self._conv3(n, lambda buf, o: F.upsample_causal(x, up_t, buf, o), To, 2 * H, 2 * W, like=x)
+
+    def _decode_tile(self, z):
+        """z [B, 16, T, h, w] -> [B, 3, T', 8h, 8w] (the parent's tiling and blending call this)."""
+        self._prep()
+        outs = []
+        for bi in range(z.shape[0]):
+            x = z[bi:bi + 1].permute(0, 2, 3, 4, 1).contiguous()  # [1, T, h, w, 16]
+            pq = self.w["post_quant_conv.weight"]
+            x = Fn.linear(x, pq.reshape(pq.shape[0], -1), self.w["post_quant_conv.bias"])
+            _, T, H, W, c = x.shape
+            x = self._conv3("decoder.conv_in", lambda buf, o: buf[:, 2:2 + T, 1:1 + H, 1:1 + W, :c].copy_(x),
+                            T, H, W, like=x)
+            x = self._nres(x, "decoder.mid_block.resnets.0")
+            x = self._nattn(x, "decoder.mid_block.attentions.0")
+            x = self._nres(x, "decoder.mid_block.resnets.1")
+            for i, (_, _, up_s, up_t) in enumerate(_plan(self.cfg)):
+                for j in range(self.cfg.layers_per_block + 1):
+                    x = self._nres(x, f"decoder.up_blocks.{i}.resnets.{j}")
+                if up_s:
+                    x = self._nup(x, f"decoder.up_blocks.{i}.upsamplers.0", up_t)
+            _, T, H, W, _ = x.shape
+            x = self._conv3("decoder.conv_out", lambda buf, o: self._gn_into(x, "decoder.conv_norm_out", True, buf, o),
+                            T, H, W, like=x)
+            outs.append(x.permute(0, 4, 1, 2, 3))
+        return torch.cat(outs, 0)
+
+
+__all__ = ["HunyuanVAEConfig", "HunyuanVAEDecoder", "HunyuanVAENative", "weight_shapes"]
+

@@ -510,14 +510,15 @@ def conv_weight(w: torch.Tensor) -> torch.Tensor:
 
 
 def conv_cl(x, w2, b=None, *, kt=3, kh=3, kw=3, causal=True, resid=None, silu=False, out=None, valid_t=False,
-            valid_h=False):
+            valid_h=False, valid_w=False):
     """Stride-1 convolution on channels-last x [N, T, H, W, Ci] with ``conv_weight`` weights;
     zero spatial padding k/2, temporal causal (kt - 1 in front) or symmetric padding;
     ``valid_t``: no temporal padding (x starts with its causal context: T_out = T - kt + 1);
-    ``valid_h``: no padding along H (x carries halo rows: H_out = H - kh + 1).
+    ``valid_h``: no padding along H (x carries halo rows: H_out = H - kh + 1); ``valid_w`` likewise
+    along W (x carries its border columns, e.g. replicate padding: W_out = W - kw + 1).
     Optional bias, SiLU, residual add (y = resid + conv).  CUDA -> tcgen05 implicit GEMM."""
     if x.is_cuda:
-        return native().conv3d(x, w2, b, kt, kh, kw, causal, resid, silu, out, valid_t, valid_h)
+        return native().conv3d(x, w2, b, kt, kh, kw, causal, resid, silu, out, valid_t, valid_h, valid_w)
     N, T, H, W, Ci = x.shape
     Co = w2.shape[0]
     ct = torch.float64 if x.dtype == torch.float64 else torch.float32
@@ -525,7 +526,8 @@ def conv_cl(x, w2, b=None, *, kt=3, kh=3, kw=3, causal=True, resid=None, silu=Fa
     xc = x.to(ct).permute(0, 4, 1, 2, 3)
     pt0, pt1 = (0, 0) if valid_t else ((kt - 1, 0) if causal else (kt // 2, kt // 2))
     ph = 0 if valid_h else kh // 2
-    xc = F.pad(xc, (kw // 2, kw // 2, ph, ph, pt0, pt1))
+    pw = 0 if valid_w else kw // 2
+    xc = F.pad(xc, (pw, pw, ph, ph, pt0, pt1))
     y = F.conv3d(xc, w5, None if b is None else b.to(ct))
     if silu:
         y = F.silu(y)
@@ -536,6 +538,65 @@ def conv_cl(x, w2, b=None, *, kt=3, kh=3, kw=3, causal=True, resid=None, silu=Fa
         out.copy_(y.to(out.dtype))
         return out
     return y.to(x.dtype)
+
+
+def gn_stats(x, G: int, eps: float = 1e-6):
+    """GroupNorm statistics of a channels-last clip x [N, T, H, W, C]: f32 [N, G, 2] = (mean,
+    1 / sqrt(var + eps)) over every frame, row, column and the group's C / G channels."""
+    if x.is_cuda:
+        return native().gn_stats(x, int(G), float(eps))
+    N, C = x.shape[0], x.shape[-1]
+    ct = torch.float64 if x.dtype == torch.float64 else torch.float32
+    v = x.to(ct).reshape(N, -1, G, C // G).transpose(1, 2).reshape(N, G, -1)
+    mean = v.mean(-1)
+    var = ((v - mean[..., None]) ** 2).mean(-1)
+    return torch.stack([mean, torch.rsqrt(var + eps)], -1).to(torch.float32 if ct == torch.float32 else ct)
+
+
+def gn_apply(x, stats, gamma, beta, G: int, *, silu: bool, y, offs=(0, 0, 0)):
+    """y[:, ot:ot+T, oh:oh+H, ow:ow+W] = GroupNorm(x) * gamma + beta (+ SiLU) with ``gn_stats``;
+    ``gamma`` / ``beta`` f32 [C]."""
+    ot, oh, ow = offs
+    if x.is_cuda:
+        native().gn_apply(x, stats, gamma, beta, int(G), bool(silu), y, int(ot), int(oh), int(ow))
+        return y
+    N, T, H, W, C = x.shape
+    ct = torch.float64 if x.dtype == torch.float64 else torch.float32
+    st = stats.to(ct).repeat_interleave(C // G, 1)  # [N, C, 2]
+    v = (x.to(ct) - st[:, None, None, None, :, 0]) * st[:, None, None, None, :, 1] * gamma.to(ct) + beta.to(ct)
+    if silu:
+        v = F.silu(v)
+    y[:, ot:ot + T, oh:oh + H, ow:ow + W] = v.to(y.dtype)
+    return y
+
+
+def pad_replicate(y, interior, size):
+    """Fill the border of y [N, Ty, Hy, Wy, C] around its interior box (offset ``interior`` =
+    (pt, ph, pw), extent ``size`` = (T, H, W)) with the nearest interior element, per dimension."""
+    (pt, ph, pw), (T, H, W) = interior, size
+    if y.is_cuda:
+        native().pad_replicate(y, int(pt), int(ph), int(pw), int(T), int(H), int(W))
+        return y
+    Ty, Hy, Wy = y.shape[1:4]
+    it = torch.arange(Ty).clamp(pt, pt + T - 1)
+    ih = torch.arange(Hy).clamp(ph, ph + H - 1)
+    iw = torch.arange(Wy).clamp(pw, pw + W - 1)
+    y.copy_(y[:, it][:, :, ih][:, :, :, iw])
+    return y
+
+
+def upsample_causal(x, up_t: bool, y, offs=(0, 0, 0)):
+    """Nearest 2x along H and W of x [N, T, H, W, C]; with ``up_t`` frame 0 stays one frame and
+    every later frame is repeated twice (T_out = 2 T - 1); written into y at offset ``offs``."""
+    ot, oh, ow = offs
+    if x.is_cuda:
+        native().upsample_causal(x, bool(up_t), y, int(ot), int(oh), int(ow))
+        return y
+    v = x.repeat_interleave(2, 2).repeat_interleave(2, 3)
+    if up_t and x.shape[1] > 1:
+        v = torch.cat([v[:, :1], v[:, 1:].repeat_interleave(2, 1)], 1)
+    y[:, ot:ot + v.shape[1], oh:oh + v.shape[2], ow:ow + v.shape[3]] = v
+    return y
 
 
 def vae_chan_norm(x, gamma, y, *, silu=True, halo=0, up=0, up_rows=0, down=0, down_rows=0):
