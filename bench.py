@@ -373,6 +373,17 @@ def run_mmdit(args, world, rank):
         torch.cuda.synchronize()
         decode = {"ms": round(t0.elapsed_time(t1), 1), "frames": int(video.shape[2]), "shape": list(video.shape),
                   "decoder": type(app.vae).__name__}
+        if args.decode_compare:  # the same decode by the PyTorch statement of the decoder (cuDNN)
+            from difflet_b200.models.vae.hunyuan_vae import HunyuanVAEDecoder
+
+            ref = HunyuanVAEDecoder(app.vae.cfg, app.vae.w)
+            t0.record()
+            vref = ref.decode(zlat)
+            t1.record()
+            torch.cuda.synchronize()
+            decode["torch_cudnn_ms"] = round(t0.elapsed_time(t1), 1)
+            decode["rel_l2_vs_torch"] = round(float((video.float() - vref.float()).norm() / vref.float().norm()), 5)
+            del vref
         del video
         _native.check_device_errors()
     if rank == 0:
@@ -438,6 +449,8 @@ def main(argv=None):
                     help="wan: parallel layout (default by N: 1 batched CFG, 2 cfg2, 4 cfg2xulysses2, "
                          "8 cfg2xulysses4; also e.g. ulysses8, cfg2xtp2xulysses2)")
     ap.add_argument("--frames", type=int, default=81)
+    ap.add_argument("--decode-compare", action="store_true",
+                    help="hunyuan --decode: also time the PyTorch (cuDNN) decoder on the same latents")
     ap.add_argument("--decode", action="store_true",
                     help="wan / hunyuan: also time one VAE decode of the clip's latents (rank 0 for hunyuan)")
     ap.add_argument("--e2e", action="store_true",
