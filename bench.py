@@ -1,5 +1,5 @@
 """Headline benchmark: FLUX.1-dev 1024x1024 DiT denoise step (and e2e s/image) on N B200s.
-``--model wan``: Wan2.2-T2V-A14B 1280x720x81 DiT step / decode / e2e s/video.
+``--model wan``: Wan2.2-T2V-A14B 1280x720x81 (40 steps, CFG 5, CFG2 x Ulysses-4 on 8 GPUs) DiT step / decode / e2e s/video.
 
 Contract (one rank per GPU; the driver launches N > 1 under torch.distributed.run):
   python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
@@ -272,8 +272,8 @@ def run_wan(args, world, rank):
 
 
 def run_mmdit(args, world, rank):
-    """BASELINE config 4 (HunyuanVideo 13B, 720x1280x129, 118,800 image tokens, embedded guidance,
-    ring-attention CP over N) or config 5 (Qwen-Image 20B, 1328^2 = 6,889 tokens, MXFP8 block
+    """The HunyuanVideo benchmark (HunyuanVideo 13B, 720x1280x129, 118,800 image tokens, embedded guidance,
+    ring-attention CP over N) or the Qwen-Image benchmark (Qwen-Image 20B, 1328^2 = 6,889 tokens, MXFP8 block
     linears, true CFG 4.0 batched on one GPU / CFG-parallel pairs, TP over the rest).
 
     ``value``: one DiT denoise step (every CFG branch, guidance combine, Euler update), device-timed

@@ -1,8 +1,8 @@
 """``difflet serve`` throughput sweep: 1..8 concurrent image requests against one server.
 
-BASELINE config 5 asks for a ``serve`` batch sweep of 1-8 concurrent requests.  The reference
+The Qwen-Image serving benchmark is a sweep of 1-8 concurrent requests.  The reference
 server answers one request per replica at a time and refuses with HTTP 429 once a request has
-waited longer than the queue timeout (``README.md:137-138``; ``--dp-degree N`` runs N replicas).
+waited longer than the queue timeout (reference ``README.md:137-138``; ``--dp-degree N`` runs N replicas).
 This tool measures the same thing here: for each concurrency level c it runs c client threads,
 each sending ``rounds`` requests back to back to ``POST /v1/images/generations``, and reports the
 completed requests per second, latency percentiles and the refusals.

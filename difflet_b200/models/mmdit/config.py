@@ -70,7 +70,7 @@ FluxConfig = MMDiTConfig
 PRESETS = {
     "flux-dev": MMDiTConfig(),
     "flux-schnell": MMDiTConfig(guidance_embed=False),
-    # tiny FLUX-style MMDiT for the CPU float64 parity check.
+    # The tiny FLUX-style MMDiT of the CPU float64 parity check (2 + 2 blocks, hidden 256, 4 heads of 64).
     "tiny": MMDiTConfig(hidden=256, heads=4, head_dim=64, double_blocks=2, single_blocks=2, text_dim=256,
                         pooled_dim=256, axes_dim=(8, 28, 28), guidance_embed=False),
     # head_dim-128 variant of the tiny model, runnable on the tcgen05 kernels.

@@ -4,7 +4,7 @@ Written from the diffusers math and independent of the fused model: it reads
 the diffusers-layout state dict, runs separate q/k/v linears, concatenates the
 two streams in the family's order, applies interleaved RoPE from position-id
 tables and plain masked softmax attention.  Used as the oracle for the fused
-MMDiT (in float64 for the tiny-model parity check of BASELINE config 1).
+MMDiT (in float64 for the tiny-model parity check: 2 + 2 blocks, hidden 256, 4 Euler steps).
 """
 
 from __future__ import annotations

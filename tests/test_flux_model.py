@@ -1,4 +1,4 @@
-"""FLUX model: fused layout vs the straight-line oracle, and BASELINE config 1 (tiny MMDiT)."""
+"""FLUX model: fused layout vs the straight-line oracle, and the tiny-MMDiT float64 parity run."""
 
 import torch
 
@@ -43,7 +43,7 @@ def test_fused_matches_oracle_float64():
 
 
 def test_tiny_mmdit_four_euler_steps_fp32_vs_float64():
-    """2+2 blocks, D=256, 4x64 heads, 256 image + 64 text tokens, 4 Euler steps."""
+    """The tiny MMDiT parity run: 2+2 blocks, D=256, 4x64 heads, 256 image + 64 text tokens, 4 Euler steps."""
     cfg = get_config("tiny")
     m64 = FluxTransformer.random_init(cfg, dtype=torch.float64, seed=0)
     m32 = FluxTransformer(cfg, {k: v.float() for k, v in m64.w.items()})
