@@ -291,7 +291,7 @@ def run_mmdit(args, world, rank):
     default = ({1: "single"}.get(world, f"ring{world}") if hv else {1: "single"}.get(world, f"tp{world}"))
     par, layout = wan_layout(world, args.layout or default)
     if hv:
-        Fr = 129 if args.frames == 81 else args.frames  # config 4: 129 frames (the Wan default is 81)
+        Fr = 129 if args.frames == 81 else args.frames  # HunyuanVideo clip: 129 frames (the Wan default is 81)
         model_id, H, W, steps_total, text_len = "hunyuanvideo-community/HunyuanVideo", 720, 1280, 50, 256
         kw = {}
     else:
