@@ -53,3 +53,38 @@ def test_flux_pipeline_gpu_vs_cpu(native):
                                                          num_inference_steps=4, output_type="latent")
     torch.cuda.synchronize()
     assert _rel(lg, lc) < 3e-2
+
+
+def test_flux_full_width_small_m_gemm_paths(native):
+    """FLUX.1-dev at full width with the token count of one Ulysses-8 rank (512 image + 64 text rows,
+    the small-M regime): the forward with the automatic GEMM choice (CTA pairs, split K) equals the
+    forward with one CTA per tile and no split, within bf16 rounding."""
+    from difflet_b200.ops import fused as F
+
+    cfg = get_config("flux-dev")
+    dit = FluxTransformer.random_init(cfg, device="cuda", dtype=torch.bfloat16, seed=21)
+    g = torch.Generator().manual_seed(4)
+    x = pack_latents(torch.randn(1, 16, 32, 64, generator=g)).cuda().bfloat16()  # 16 x 32 tokens
+    txt = torch.randn(1, 64, cfg.text_dim, generator=g).cuda().bfloat16()
+    pooled = torch.randn(1, cfg.pooled_dim, generator=g).cuda()
+    t, gd = torch.full((1,), 0.7, device="cuda"), torch.full((1,), 3.5, device="cuda")
+    auto = dit(x, txt, pooled, t, gd, img_hw=(16, 32)).float()
+    nat = F._lib()
+    try:
+        nat.gemm_set_pair_auto(False)
+        nat.gemm_set_split_force(1)
+        plain = dit(x, txt, pooled, t, gd, img_hw=(16, 32)).float()
+    finally:
+        from difflet_b200 import envs
+
+        nat.gemm_set_split_force(0)
+        nat.gemm_set_pair_auto(envs.DIFFLET_GEMM_PAIR != "0")
+    torch.cuda.synchronize()
+    assert torch.isfinite(auto).all()
+    # split K changes the fp32 summation order and so the bf16 rounding of some outputs; over 57
+    # random-init blocks that drifts by about 1.5 % (each GEMM path alone is checked against an
+    # fp32 reference in test_kernels_gpu.py); a lost K range or tile would be far larger
+    assert _rel(auto, plain) < 3e-2
+    from difflet_b200 import _native
+
+    _native.check_device_errors()
