@@ -375,6 +375,31 @@ def test_conv_cl_matches_torch(native, N, T, H, W, Ci, Co, k, causal):
     _close(y.cpu(), ref, tol=GEMM_TOL)
 
 
+@pytest.mark.parametrize("T,H,W,Ci,Co,valid", [
+    (4, 7, 24, 128, 128, "th"),    # a 5-row decode slab with its two halo rows, cached frames in front
+    (3, 12, 24, 64, 64, "th"),     # a 10-row slab
+    (2, 3, 40, 96, 96, "h"),       # one output row
+    (4, 9, 18, 64, 128, "thw"),    # replicate-padded clip (every border carried by the input)
+    (3, 6, 130, 32, 96, "tw"),     # two 128-wide column tiles of a valid-W row
+])
+def test_conv_cl_valid_padding_matches_torch(native, T, H, W, Ci, Co, valid):
+    """valid_t / valid_h / valid_w: no padding along the axis, the input already carries the
+    context (causal frames, halo rows of a slab, replicate-padded borders); small slabs included."""
+    from difflet_b200.ops import fused as F
+
+    torch.manual_seed(12)
+    vt, vh, vw = ("t" in valid), ("h" in valid), ("w" in valid)
+    x = torch.randn(1, T, H, W, Ci, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(Co, Ci, 3, 3, 3, device="cuda") / (Ci * 27) ** 0.5).bfloat16()
+    b = torch.randn(Co, device="cuda", dtype=torch.bfloat16)
+    w2 = F.conv_weight(w)
+    y = F.conv_cl(x, w2, b, valid_t=vt, valid_h=vh, valid_w=vw)
+    ref = F.conv_cl(x.cpu().float(), w2.cpu().float(), b.cpu().float(), valid_t=vt, valid_h=vh, valid_w=vw)
+    torch.cuda.synchronize()
+    assert y.shape == ref.shape == (1, T - 2 if vt else T, H - 2 if vh else H, W - 2 if vw else W, Co)
+    _close(y.cpu(), ref, tol=GEMM_TOL)
+
+
 @pytest.mark.parametrize("M,N,K", [(256, 256, 64), (1000, 1280, 512), (4608, 3072, 3072), (300, 2304, 128)])
 def test_gemm_cta_pair(native, M, N, K):
     """The 2-CTA (cta_group::2) GEMM: plain, GELU window and gated residual epilogues."""
