@@ -5,8 +5,14 @@ buffers and orders them with a device barrier.  Here the slabs of 2-4 "ranks" ru
 threads on one device: their buffers are plain device tensors, the neighbour pointers are
 computed by ``PeerSlabs.neighbours`` exactly as across GPUs, and the barrier is a host barrier
 after a device synchronise, so no kernel ever waits for another one.  The middle slabs take
-halo rows from both sides, which a 2-GPU run does not exercise.  The decode must equal the
-whole-frame decode bit for bit (each output pixel's arithmetic does not depend on the split).
+halo rows from both sides, which a 2-GPU run does not exercise.
+
+Every convolution, norm and upsample computes each output pixel the same way whatever the split,
+so with an exact attention (float64, patched in for both decodes) the slab decode must equal the
+whole-frame decode bit for bit.  With the library attention of the mid block the split changes
+only that attention's query count (a slab's rows instead of the frame's), for which the library
+picks another reduction: a few outputs move by one bf16 step, which this bf16 decoder carries to
+about 1 % relative L2 at the output -- the distance of its bf16 decode from a float32 decode.
 """
 
 import threading
@@ -67,10 +73,18 @@ class _ThreadSlabs(PeerSlabs):
         return out
 
 
-@pytest.mark.parametrize("world,rows", [(2, 20), (3, 20), (4, 20)])
-def test_peer_slab_decode_threads_one_gpu(native, world, rows):
+def _exact_attention(q, k, v, **kw):
+    assert not kw
+    s = (q.double() @ k.double().transpose(-1, -2)) / q.shape[-1] ** 0.5
+    return (torch.softmax(s, -1) @ v.double()).to(q.dtype)
+
+
+@pytest.mark.parametrize("world,rows,exact", [(2, 20, True), (3, 20, True), (4, 20, True), (4, 20, False)])
+def test_peer_slab_decode_threads_one_gpu(native, monkeypatch, world, rows, exact):
     from difflet_b200.models.vae.wan_vae import WanVAEConfig, WanVAEDecoder
 
+    if exact:
+        monkeypatch.setattr(torch.nn.functional, "scaled_dot_product_attention", _exact_attention)
     vcfg = WanVAEConfig(base_dim=32)
     vae = WanVAEDecoder.random_init(vcfg, device="cuda", dtype=torch.bfloat16, seed=6)
     z = torch.randn(1, 16, 3, rows, 24, generator=torch.Generator().manual_seed(2)).cuda().bfloat16()
@@ -101,4 +115,7 @@ def test_peer_slab_decode_threads_one_gpu(native, world, rows):
     err = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
     # where they differ: which output rows (a halo error sits at the slab boundaries)
     bad_rows = (out != ref)[0].any(0).any(0).any(-1).nonzero().flatten().tolist()  # video [1, 3, F, H, W]
-    assert torch.equal(out, ref), f"rel L2 {err:.3g}; differing output rows {bad_rows[:40]}"
+    if exact:
+        assert torch.equal(out, ref), f"rel L2 {err:.3g}; differing output rows {bad_rows[:40]}"
+    else:
+        assert err < 2e-2, f"rel L2 {err:.3g}"
