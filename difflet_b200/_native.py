@@ -54,6 +54,12 @@ NVCC_FLAGS = [
     "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
 ]
 CXX_FLAGS = ["-O3", "-std=c++17"]
+# Link the C++ runtime torch itself uses (the shared libstdc++.so.6).  A toolchain whose
+# unversioned libstdc++.so link is missing falls back to the static archive; the extension then
+# carries a second copy of the C++ runtime whose iostream / locale state is not the process's,
+# and formatting a number into an error message (TORCH_CHECK with an int) dereferences a null
+# locale facet instead of raising.
+LD_FLAGS = ["-l:libstdc++.so.6"]
 
 
 def _bounds_check() -> bool:
@@ -89,7 +95,7 @@ def source_hash(bounds: bool | None = None) -> str:
     for p in sorted(_sources() + [CSRC / n for n in HEADERS if (CSRC / n).exists()]):
         h.update(p.name.encode())
         h.update(p.read_bytes())
-    h.update(" ".join(_nvcc_flags(bounds) + CXX_FLAGS).encode())
+    h.update(" ".join(_nvcc_flags(bounds) + CXX_FLAGS + LD_FLAGS).encode())
     return h.hexdigest()[:24]
 
 
@@ -131,6 +137,7 @@ def build(verbose: bool = False, force: bool = False):
         sources=[str(p) for p in _sources()],
         extra_cflags=CXX_FLAGS,
         extra_cuda_cflags=_nvcc_flags(),
+        extra_ldflags=LD_FLAGS,
         extra_include_paths=[str(CSRC)],
         build_directory=str(bdir),
         verbose=verbose,

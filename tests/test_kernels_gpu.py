@@ -585,6 +585,19 @@ def test_peer_barrier_timeout_fails_fast(native):
     assert torch.isfinite(native.gemm(x, x, None).float()).all()  # the context is still usable
 
 
+def test_refused_launch_raises_with_its_status(native):
+    """A launch the host code refuses (an operand off its 16-byte alignment) raises a Python
+    error naming the status code; no kernel runs and the context stays usable."""
+    x = torch.randn(128 * 64 + 8, device="cuda", dtype=torch.bfloat16)
+    a = x[1:1 + 128 * 64].view(128, 64)  # 2 bytes past an aligned address
+    b = torch.randn(64, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match=r"gemm launch failed with status -3"):
+        native.gemm(a, b, None)
+    y = native.gemm(b, b, None)
+    torch.cuda.synchronize()
+    _close(y, b.float() @ b.float().t(), tol=GEMM_TOL)
+
+
 def test_vae_chan_norm_and_upsample_with_halo_stores(native):
     """Channel RMS + SiLU and the nearest upsampler write their rows at the halo offset and their
     boundary rows into the neighbouring slabs' halo rows (here local tensors stand in for the
