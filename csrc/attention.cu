@@ -694,14 +694,18 @@ extern "C" int dfl_attention(const AttnArgs* a, cudaStream_t stream) {
   p.acc_lse = a->acc_lse;
   p.merge_mode = a->merge_mode;
   if (a->merge_mode != 0 && (!a->acc_o || !a->acc_lse || (reinterpret_cast<uintptr_t>(a->acc_o) & 15))) return -9;
+  // seg0_per is also the row offset of a rank's seg1 rows in its own buffer, so it stays 0 for a
+  // single-stream sequence (seg0_len 0); only the divisors are kept nonzero (a segment without
+  // rows is never divided by)
   p.seg0_len = a->seg0_len;
-  p.seg0_per = a->seg0_per > 0 ? a->seg0_per : 1;
+  p.seg0_per = a->seg0_per;
   p.seg1_per = a->seg1_per > 0 ? a->seg1_per : 1;
   for (int r = 0; r < DFL_MAX_PEERS; ++r)
     p.o_peer[r] = reinterpret_cast<__nv_bfloat16*>(r < a->o_world ? a->o_peer[r] : nullptr);
   if (a->o_world > 1) {
     if (a->o_world > DFL_MAX_PEERS) return -6;
-    if (a->seg0_len > 0 && a->seg0_per * a->o_world != a->seg0_len) return -7;
+    if (a->seg0_len < 0 || a->seg0_per < 0 || a->seg1_per < 0) return -7;
+    if (a->seg0_per * a->o_world != a->seg0_len) return -7;  // seg0_per is 0 exactly when seg0_len is
     if (a->seg1_per * a->o_world != a->Sq - a->seg0_len) return -7;
     for (int r = 0; r < a->o_world; ++r)
       if (!a->o_peer[r] || (reinterpret_cast<uintptr_t>(a->o_peer[r]) & 15)) return -8;

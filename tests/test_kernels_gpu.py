@@ -508,6 +508,44 @@ def test_attention_split_kv(native, split):
     assert (lse - ref_lse).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("n0,n1,split", [(0, 300, 1), (0, 300, 3), (64, 236, 1), (64, 236, 2)])
+def test_attention_output_scatter_to_owning_ranks(native, n0, n1, split):
+    """The Ulysses heads->sequence exchange in the attention epilogue: each output row goes to
+    the rank that owns it (rank r owns rows [r n0, (r+1) n0) of the first segment and
+    [r n1, (r+1) n1) of the second, stored at local rows [0, n0) and [n0, n0 + n1)), at this
+    rank's head columns.  The owners' buffers are local tensors here.  n0 = 0 is a single-stream
+    sequence (Wan); the split runs the key-chunk combine pass, which stores the same way."""
+    torch.manual_seed(19)
+    world, B, Hl, dh = 3, 2, 2, 128
+    S_loc = n0 + n1
+    S = world * S_loc
+    q = torch.randn(B, Hl, S, dh, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, Hl, S, dh, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, Hl, S, dh, device="cuda", dtype=torch.bfloat16)
+    rank = 1  # this rank's heads fill columns [rank Hl dh, (rank + 1) Hl dh) of every owner's rows
+    ld = world * Hl * dh
+    owners = [torch.zeros(B * S_loc + 1, ld, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    col = rank * Hl * dh * 2
+    scale = 1 / math.sqrt(dh)
+    native.attention(q, k, v, scale, None, None, None, None, [t.data_ptr() + col for t in owners], n0 * world, n0,
+                     n1, [S_loc * ld, dh, ld], kv_split=split)
+    ref, _ = _attn_ref(q, k, v, scale, None, None)  # [B, Hl, S, dh]
+    torch.cuda.synchronize()
+    rows = torch.cat([torch.arange(r * n0, (r + 1) * n0) for r in range(world)] +
+                     [n0 * world + torch.arange(r * n1, (r + 1) * n1) for r in range(world)]).cuda()
+    own = torch.cat([torch.full((n0,), r) for r in range(world)] + [torch.full((n1,), r) for r in range(world)]).cuda()
+    lrow = torch.cat([torch.arange(n0) for _ in range(world)] + [n0 + torch.arange(n1) for _ in range(world)]).cuda()
+    for r in range(world):
+        sel = own == r
+        mine = owners[r][: B * S_loc].view(B, S_loc, world, Hl, dh)[:, :, rank]  # [B, S_loc, Hl, dh]
+        want = torch.zeros(B, S_loc, Hl, dh, device="cuda")
+        want[:, lrow[sel]] = ref[:, :, rows[sel]].permute(0, 2, 1, 3).float()
+        _close(mine, want)
+        assert owners[r][B * S_loc:].abs().sum() == 0  # nothing past the owner's rows
+        other = owners[r][: B * S_loc].view(B, S_loc, world, Hl * dh)
+        assert other[:, :, [c for c in range(world) if c != rank]].abs().sum() == 0  # other ranks' columns
+
+
 @pytest.mark.parametrize("n,swap", [(1 << 20, False), (12345, True), (7, False)])
 def test_guided_step_unipc_matches_oracle(native, n, swap):
     """The fused CFG combine + UniPC step (csrc/sched.cu) over several steps against the same
