@@ -695,6 +695,11 @@ inline int fill_epi_params(const GemmArgs& a, dfl::EpiParams& ep) {
   ep.rows_per_rank = a.rows_per_rank > 0 ? a.rows_per_rank : a.M;
   ep.peer_row_off = a.peer_row_off;
   for (int r = 0; r < DFL_MAX_PEERS; ++r) ep.out_peer[r] = r < a.out_world ? a.out_peer[r] : nullptr;
+  if (a.out_world > 0) {  // every row needs an owner (the device side does not check in release builds)
+    if ((long long)ep.rows_per_rank * a.out_world < a.M) return -10;
+    for (int r = 0; r < a.out_world; ++r)
+      if (!a.out_peer[r]) return -10;
+  }
   if (a.epi == kEpiSwiGLU && (a.N % 64 || a.out_world > 0)) return -11;
   if (a.epi == kEpiQkv) {
     const int rc = check_qkv_plan(a);

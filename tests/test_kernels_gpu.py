@@ -634,6 +634,13 @@ def test_refused_launch_raises_with_its_status(native):
     y = native.gemm(b, b, None)
     torch.cuda.synchronize()
     _close(y, b.float() @ b.float().t(), tol=GEMM_TOL)
+    # a row scatter whose owners cannot hold every row (2 owners x 40 rows for 128 rows)
+    owners = [torch.zeros(64, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    with pytest.raises(RuntimeError, match=r"gemm launch failed with status -10"):
+        native.gemm(b.repeat(2, 1), b, None, None, 0, out_peer=[t.data_ptr() for t in owners], rows_per_rank=40,
+                    peer_row_off=0, ldd=64)
+    torch.cuda.synchronize()
+    assert all(t.abs().sum() == 0 for t in owners)
 
 
 def test_vae_chan_norm_and_upsample_with_halo_stores(native):
