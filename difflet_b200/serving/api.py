@@ -11,6 +11,10 @@ Routes as in the reference (``difflet/serving/openai/api_server.py:96-515``):
   POST /v1/videos             video models: create an asynchronous job
   GET  /v1/videos/{id}        job status (queued / in_progress / completed / failed)
   GET  /v1/videos/{id}/content  the encoded video
+  POST /v1/videos/sync        video models: generate in the request and answer with the
+                              encoded video itself (``X-Request-Id``, ``X-Model``,
+                              ``X-Inference-Time-S`` headers); a client that disconnects
+                              cancels its generation (reference ``api_server.py:405-457``)
 An API key (``--api-key`` or ``DIFFLET_API_KEY``) is enforced as a Bearer token
 on every /v1 route.  A busy server answers 429.
 """
@@ -170,9 +174,9 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
             return {"created": int(time.time()), "data": [{"b64_json": base64.b64encode(png).decode()}]}
 
     else:
+        import asyncio
 
-        @app.post("/v1/videos")
-        async def create_video(payload: Any = Body(default=None)):
+        def _video_request(payload) -> dict:
             if not isinstance(payload, dict) or not payload.get("prompt"):
                 raise HTTPException(400, "prompt is required")
             req = {"prompt": payload["prompt"], **_parse_size(payload.get("size"))}
@@ -182,8 +186,43 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
             if "seconds" in payload and "num_frames" not in req:
                 req["num_frames"] = int(float(payload["seconds"]) * 16) // 4 * 4 + 1
             _validate(req)
-            job = jobs.create(req)
+            return req
+
+        @app.post("/v1/videos")
+        async def create_video(payload: Any = Body(default=None)):
+            job = jobs.create(_video_request(payload))
             return job.public()
+
+        @app.post("/v1/videos/sync")
+        async def create_video_sync(request: Request, payload: Any = Body(default=None)):
+            """Generate while the client waits and answer with the encoded video.  The generation
+            runs on a worker thread; the connection is polled meanwhile, and a client that goes
+            away cancels its request (the engine stops between denoise steps)."""
+            from fastapi.responses import Response
+
+            req = _video_request(payload)
+            rid = request.headers.get("x-request-id") or f"video_sync_{uuid.uuid4().hex}"
+            loop = asyncio.get_running_loop()
+            t0 = time.perf_counter()
+            fut = loop.run_in_executor(None, _run, req, rid)
+            while True:
+                done, _ = await asyncio.wait({fut}, timeout=0.25)
+                if done:
+                    break
+                if await request.is_disconnected():
+                    if hasattr(engine, "cancel"):
+                        engine.cancel(rid)
+                    try:
+                        await fut
+                    except Exception:  # noqa: BLE001 - the client is gone; nothing to answer
+                        pass
+                    return Response(status_code=499)
+            frames = fut.result()  # HTTP errors of the engine propagate from here
+            infer_s = time.perf_counter() - t0
+            data = frames if isinstance(frames, (bytes, bytearray)) else encode_video(frames, jobs.fps)
+            return Response(content=bytes(data), media_type="video/x-msvideo",
+                            headers={"X-Request-Id": rid, "X-Model": model_id,
+                                     "X-Inference-Time-S": f"{infer_s:.6f}"})
 
         @app.get("/v1/videos/{vid}")
         async def get_video(vid: str):

@@ -70,6 +70,31 @@ def test_video_job_lifecycle(tmp_path):
     assert data[:4] == b"RIFF" and data[8:12] == b"AVI "
 
 
+def test_video_sync_returns_the_encoded_video():
+    """POST /v1/videos/sync answers with the encoded video and its request headers; an engine
+    failure is a 500 and a missing prompt a 400 (nothing is generated for it)."""
+    calls = []
+
+    def gen(req):
+        calls.append(req)
+        if req["prompt"] == "fail":
+            raise EngineError("worker died")
+        return torch.zeros(req.get("num_frames", 5), 16, 16, 3, dtype=torch.uint8)
+
+    c = TestClient(create_app(InProcessEngine(gen), "wan", output="video"))
+    r = c.post("/v1/videos/sync", json={"prompt": "waves", "size": "16x16", "num_frames": 9},
+               headers={"X-Request-Id": "req-7"})
+    assert r.status_code == 200
+    assert r.content[:4] == b"RIFF" and r.content[8:12] == b"AVI "
+    assert r.headers["x-request-id"] == "req-7" and r.headers["x-model"] == "wan"
+    assert float(r.headers["x-inference-time-s"]) >= 0.0
+    assert calls[-1]["num_frames"] == 9 and calls[-1]["width"] == 16
+    assert c.post("/v1/videos/sync", json={"prompt": "fail"}).status_code == 500
+    n = len(calls)
+    assert c.post("/v1/videos/sync", json={"size": "16x16"}).status_code == 400
+    assert len(calls) == n
+
+
 # --- resident worker (spawned process) with fake runners ---------------------------------
 
 def fake_runner(mode="ok", delay=0.0):
