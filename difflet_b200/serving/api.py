@@ -17,6 +17,11 @@ Routes as in the reference (``difflet/serving/openai/api_server.py:96-515``):
                               cancels its generation (reference ``api_server.py:405-457``)
 An API key (``--api-key`` or ``DIFFLET_API_KEY``) is enforced as a Bearer token
 on every /v1 route.  A busy server answers 429.
+
+Errors use the OpenAI envelope ``{"error": {"message", "type", "code"}}`` with a stable
+``code`` per status (reference ``difflet/serving/errors.py:9-64``); chat-completion fields that
+ask for something an image generator does not do (streaming, tools, n > 1, sampling
+parameters) are refused with ``feature_not_supported``.
 """
 
 from __future__ import annotations
@@ -36,6 +41,31 @@ _GEN_KEYS = ("height", "width", "num_inference_steps", "seed", "guidance_scale",
              "true_cfg_scale", "negative_prompt", "num_frames")
 
 
+# status -> (OpenAI error type, stable code)
+_ERROR_CODES = {400: ("invalid_request_error", "invalid_request"), 401: ("invalid_request_error", "invalid_api_key"),
+                404: ("invalid_request_error", "not_found"), 409: ("invalid_request_error", "conflict"),
+                422: ("invalid_request_error", "invalid_request"), 429: ("server_error", "server_busy"),
+                499: ("server_error", "request_cancelled"), 500: ("server_error", "internal_error"),
+                503: ("server_error", "unavailable")}
+# chat-completion fields an image generator cannot honour
+_CHAT_UNSUPPORTED = ("stream", "tools", "tool_choice", "functions", "function_call", "temperature", "top_p", "stop",
+                     "max_tokens", "logprobs")
+
+
+class ServingError(HTTPException):
+    """An HTTP error with an explicit machine-readable ``code`` (else derived from the status)."""
+
+    def __init__(self, status_code: int, message: str, code: str | None = None):
+        super().__init__(status_code, message)
+        self.code = code
+
+
+def error_payload(status: int, message: str, code: str | None = None) -> dict:
+    etype, default = _ERROR_CODES.get(status, ("server_error" if status >= 500 else "invalid_request_error",
+                                               "error"))
+    return {"error": {"message": message, "type": etype, "code": code or default}}
+
+
 def _parse_size(size: str | None):
     if not size:
         return {}
@@ -45,7 +75,12 @@ def _parse_size(size: str | None):
 
 def normalize_chat_request(payload: dict) -> dict:
     if not isinstance(payload, dict):
-        raise HTTPException(400, "request body must be a JSON object")
+        raise ServingError(400, "request body must be a JSON object", "invalid_request")
+    for k in _CHAT_UNSUPPORTED:
+        if payload.get(k) not in (None, False):
+            raise ServingError(400, f"{k} is not supported by an image generation model", "feature_not_supported")
+    if payload.get("n") not in (None, 1):
+        raise ServingError(400, "one image per request (n = 1)", "feature_not_supported")
     msgs = payload.get("messages") or []
     prompt = None
     for m in reversed(msgs):
@@ -56,7 +91,7 @@ def normalize_chat_request(payload: dict) -> dict:
             prompt = c
             break
     if not prompt:
-        raise HTTPException(400, "no user message with text content")
+        raise ServingError(400, "no user message with text content", "invalid_prompt")
     opts = dict(payload.get("extra_body") or {})
     for k in _GEN_KEYS + ("size", "n"):
         if k in payload:
@@ -79,12 +114,23 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
     app = FastAPI(title="difflet_b200", version="0.1.0")
     jobs = VideoJobStore(engine, video_dir, encode_video, artifact_store=artifact_store) if output == "video" else None
 
+    from fastapi.exceptions import RequestValidationError
+
+    @app.exception_handler(HTTPException)
+    async def http_error(request: Request, exc: HTTPException):
+        return JSONResponse(status_code=exc.status_code,
+                            content=error_payload(exc.status_code, str(exc.detail), getattr(exc, "code", None)))
+
+    @app.exception_handler(RequestValidationError)
+    async def validation_error(request: Request, exc: RequestValidationError):
+        return JSONResponse(status_code=400, content=error_payload(400, str(exc.errors())[:2000]))
+
     @app.middleware("http")
     async def auth(request: Request, call_next):
         if api_key and request.url.path.startswith("/v1/"):
             got = request.headers.get("authorization", "")
             if got != f"Bearer {api_key}":
-                return JSONResponse(status_code=401, content={"error": {"message": "invalid api key"}})
+                return JSONResponse(status_code=401, content=error_payload(401, "invalid api key"))
         return await call_next(request)
 
     @app.get("/health")
@@ -115,10 +161,10 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
         try:
             check_generate_kwargs(spec, req)
         except SpecRefusal as exc:
-            raise HTTPException(400, str(exc))
+            raise ServingError(400, str(exc), "feature_not_supported")
         for field, why in spec.refused_video_fields:
             if req.get(field) is not None:
-                raise HTTPException(400, f"{field}: {why}")
+                raise ServingError(400, f"{field}: {why}", "feature_not_supported")
 
     def _run(req, request_id=None):
         _validate(req)
@@ -164,7 +210,7 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
         @app.post("/v1/images/generations")
         async def images(request: Request, payload: Any = Body(default=None)):
             if not isinstance(payload, dict) or not payload.get("prompt"):
-                raise HTTPException(400, "prompt is required")
+                raise ServingError(400, "prompt is required", "invalid_prompt")
             req = {"prompt": payload["prompt"], **_parse_size(payload.get("size"))}
             for k in _GEN_KEYS:
                 if k in payload:
@@ -178,7 +224,7 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
 
         def _video_request(payload) -> dict:
             if not isinstance(payload, dict) or not payload.get("prompt"):
-                raise HTTPException(400, "prompt is required")
+                raise ServingError(400, "prompt is required", "invalid_prompt")
             req = {"prompt": payload["prompt"], **_parse_size(payload.get("size"))}
             for k in _GEN_KEYS:
                 if k in payload:

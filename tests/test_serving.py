@@ -70,6 +70,28 @@ def test_video_job_lifecycle(tmp_path):
     assert data[:4] == b"RIFF" and data[8:12] == b"AVI "
 
 
+def test_errors_use_the_openai_envelope():
+    """Every error answers {"error": {"message", "type", "code"}}; chat fields an image model
+    cannot honour are refused before anything is queued."""
+    calls = []
+    c = TestClient(create_app(InProcessEngine(lambda r: calls.append(r) or _img(r)), "flux", api_key="k"))
+    r = c.get("/v1/models")
+    assert r.status_code == 401 and r.json()["error"]["code"] == "invalid_api_key"
+    h = {"Authorization": "Bearer k"}
+    msgs = [{"role": "user", "content": "a cat"}]
+    for extra in ({"stream": True}, {"tools": [{"type": "function"}]}, {"n": 2}, {"temperature": 0.7}):
+        r = c.post("/v1/chat/completions", headers=h, json={"messages": msgs, **extra})
+        err = r.json()["error"]
+        assert r.status_code == 400 and err["code"] == "feature_not_supported", (extra, r.json())
+        assert err["type"] == "invalid_request_error" and err["message"]
+    r = c.post("/v1/chat/completions", headers=h, json={"messages": [{"role": "system", "content": "x"}]})
+    assert r.status_code == 400 and r.json()["error"]["code"] == "invalid_prompt"
+    assert not calls
+    r = c.post("/v1/requests/nope/cancel", headers=h)
+    assert r.status_code == 404 and r.json()["error"]["code"] == "not_found"
+    assert c.post("/v1/chat/completions", headers=h, json={"messages": msgs, "stream": False}).status_code == 200
+
+
 def test_video_sync_returns_the_encoded_video():
     """POST /v1/videos/sync answers with the encoded video and its request headers; an engine
     failure is a 500 and a missing prompt a 400 (nothing is generated for it)."""
