@@ -12,9 +12,12 @@ from __future__ import annotations
 
 import json
 import os
+import signal
 import subprocess
 import sys
 from pathlib import Path
+
+from difflet_b200.cli.runner import die_with_parent
 
 
 def try_claim(work: Path, i: int) -> bool:
@@ -65,5 +68,7 @@ def run_router(argv_worker: list[str], dp: int, gpus_per_replica: int, work: str
         env = dict(os.environ)
         env["CUDA_VISIBLE_DEVICES"] = ",".join(str(r * gpus_per_replica + k) for k in range(gpus_per_replica))
         env["DIFFLET_DP_RANK"] = str(r)
-        procs.append(subprocess.Popen([sys.executable, "-m", "difflet_b200"] + argv_worker, env=env))
+        # a worker owns its GPUs outright: SIGKILL it if the router dies, so no orphan keeps them
+        procs.append(subprocess.Popen([sys.executable, "-m", "difflet_b200"] + argv_worker, env=env,
+                                      preexec_fn=die_with_parent(signal.SIGKILL)))
     return max(p.wait() for p in procs)

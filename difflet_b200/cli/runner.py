@@ -13,14 +13,29 @@ import subprocess
 import sys
 
 
-def _pdeathsig():
-    try:
-        import ctypes
+def die_with_parent(sig: int):
+    """A ``preexec_fn`` asking the kernel to send ``sig`` to the child when its parent exits
+    (Linux ``PR_SET_PDEATHSIG``; a no-op elsewhere).  A child whose parent already exited
+    between the fork and this call (re-parented to init) signals itself."""
 
-        libc = ctypes.CDLL("libc.so.6")
-        libc.prctl(1, signal.SIGTERM)  # PR_SET_PDEATHSIG
-    except Exception:
-        pass
+    def _preexec():
+        if not sys.platform.startswith("linux"):
+            return
+        try:
+            import ctypes
+
+            libc = ctypes.CDLL("libc.so.6", use_errno=True)
+            libc.prctl(1, int(sig), 0, 0, 0)  # PR_SET_PDEATHSIG
+        except Exception:  # noqa: BLE001 - best effort: the child still runs
+            return
+        if os.getppid() == 1:
+            os.kill(os.getpid(), int(sig))
+
+    return _preexec
+
+
+# torchrun's agent stops its ranks on SIGTERM (a SIGKILLed agent would orphan them)
+_pdeathsig = die_with_parent(signal.SIGTERM)
 
 
 def run_torchrun(argv: list[str], nproc: int, *, port: int | None = None, timeout_s: float | None = None,

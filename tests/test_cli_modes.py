@@ -2,6 +2,7 @@
 --host-vae decode on the host, --dp-schedule static assignment, difflet quant plans."""
 
 import json
+import time
 import subprocess
 import sys
 from pathlib import Path
@@ -77,3 +78,32 @@ def test_host_and_device_vae_exclusive():
 def test_work_dir_flag_parses(flag):
     a = build_parser().parse_args(["generate", "--model-id", "x", flag])
     assert a.keep_work_dir
+
+
+def test_children_die_with_their_parent():
+    """A DP worker / torchrun child is signalled when the process that started it exits, so no
+    orphan keeps holding its GPUs."""
+    import textwrap
+
+    code = textwrap.dedent("""
+        import signal, subprocess, sys
+        from difflet_b200.cli.runner import die_with_parent
+        p = subprocess.Popen([sys.executable, "-c", "import time; time.sleep(60)"],
+                             preexec_fn=die_with_parent(signal.SIGKILL))
+        print(p.pid, flush=True)
+    """)
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=60, check=True)
+    pid = int(out.stdout.split()[0])
+
+    def alive():
+        try:
+            with open(f"/proc/{pid}/status") as f:
+                state = [ln for ln in f if ln.startswith("State:")][0]
+            return "Z" not in state.split()[1]
+        except (FileNotFoundError, IndexError):
+            return False
+
+    deadline = time.time() + 10
+    while alive() and time.time() < deadline:
+        time.sleep(0.1)
+    assert not alive()
