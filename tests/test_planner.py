@@ -42,6 +42,24 @@ def test_flux_estimates_track_measured_steps(monkeypatch):
         assert abs(est_ms - measured_ms) / measured_ms < 0.2, (n, est_ms, measured_ms)
 
 
+def test_wan_estimates_track_measured_steps(monkeypatch):
+    """The cost model against Wan2.2-A14B 1280x720x81 steps (both CFG branches) measured on
+    B200 with this engine: 12076 ms on 1 GPU (batched CFG), 5953 ms on 2 (CFG-parallel), 2914 ms
+    on 4 (CFG2 x Ulysses-2)."""
+    from difflet_b200 import planner as P
+    from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
+    from difflet_b200.registry import resolve_model
+
+    monkeypatch.setattr(P, "_EFF_SCALE", [0.85])
+    e = resolve_model("Wan-AI/Wan2.2-T2V-A14B-Diffusers")
+    shape = P.model_shape(e, 720, 1280, 81)
+    layouts = ((DiffletParallelConfig(), 12076.0), (DiffletParallelConfig(cfg_parallel_enabled=True), 5953.0),
+               (DiffletParallelConfig(cfg_parallel_enabled=True, cp_degree=2, cp_mode="ulysses"), 2914.0))
+    for p, measured_ms in layouts:
+        est_ms = P.estimate_step_s(e, p, shape, 1397.4e12) * 1e3
+        assert abs(est_ms - measured_ms) / measured_ms < 0.1, (p, est_ms, measured_ms)
+
+
 class _FakeNVML:
     """A stand-in for pynvml: 8 GPUs of 183,359 MiB with 18 active NVLinks each."""
 
