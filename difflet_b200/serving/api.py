@@ -314,7 +314,7 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
                 job = jobs.cancel(vid)
                 if job.status not in TERMINAL:
                     return {"id": vid, "object": "video.deleted", "deleted": False, "status": job.status}
-            jobs.repo.delete(vid)
+            jobs.delete(vid)
             return {"id": vid, "object": "video.deleted", "deleted": True}
 
     app.state.jobs = jobs

@@ -9,11 +9,19 @@ Readers resolve the newest generation whose inventory still validates, or a pinn
 generation whose files were altered is rejected, and staging directories abandoned by a crashed
 publisher are removed on the next publication.
 
+Storage is bounded as in the reference's video storage (``difflet/serving/video_storage.py:133-604``):
+a publication larger than ``max_bytes`` (8 GiB by default) is refused before anything is written,
+and so is one that would leave less than ``reserve_bytes`` free on the file system.  ``delete``
+removes every generation of a name in one rename (readers see all of it or none) and ``sweep``
+removes the names a caller no longer knows (what a crash between a job record's deletion and
+its files' left behind) together with abandoned staging and trash directories.
+
 Layout::
 
     <root>/<name>/generations/<generation id>/files...   + inventory.json
     <root>/<name>/.staging/<random>/                       (in-flight publications)
     <root>/<name>/.lock
+    <root>/.trash/<random>/                                 (deleted names, removed after the rename)
 """
 
 from __future__ import annotations
@@ -34,6 +42,17 @@ INVENTORY = "inventory.json"
 
 class ArtifactIntegrityError(RuntimeError):
     """A generation's files no longer match its inventory."""
+
+
+class ArtifactTooLarge(ValueError):
+    """A publication above the store's size limit."""
+
+
+class ArtifactNoSpace(OSError):
+    """A publication that would leave less than the reserved free space."""
+
+DEFAULT_MAX_BYTES = 8 << 30
+DEFAULT_RESERVE_BYTES = 1 << 30
 
 
 @dataclass(frozen=True)
@@ -65,16 +84,42 @@ def _fsync_dir(p: Path) -> None:
 
 
 class ImmutableArtifacts:
-    def __init__(self, root: str | os.PathLike, *, lock_timeout: float = 300.0):
+    def __init__(self, root: str | os.PathLike, *, lock_timeout: float = 300.0, max_bytes: int = DEFAULT_MAX_BYTES,
+                 reserve_bytes: int = DEFAULT_RESERVE_BYTES):
         self.root = Path(root).resolve()
         self.lock_timeout = lock_timeout
+        self.max_bytes = int(max_bytes)
+        self.reserve_bytes = int(reserve_bytes)
         self.root.mkdir(parents=True, exist_ok=True)
+
+    def available_bytes(self) -> int:
+        st = os.statvfs(self.root)
+        return st.f_bavail * st.f_frsize
+
+    def _check_size(self, files: dict) -> int:
+        total = 0
+        for rel, content in files.items():
+            if isinstance(content, (bytes, bytearray)):
+                total += len(content)
+            else:
+                src = Path(content)
+                if src.is_symlink() or not src.is_file():
+                    raise ValueError(f"artifact source {rel!r} must be a regular file, not {src}")
+                total += src.stat().st_size
+        if total > self.max_bytes:
+            raise ArtifactTooLarge(f"{total} bytes exceed the artifact limit of {self.max_bytes}")
+        if self.available_bytes() - total < self.reserve_bytes:
+            raise ArtifactNoSpace(f"publishing {total} bytes would leave under {self.reserve_bytes} bytes free")
+        return total
 
     # ---------------------------------------------------------------------- helpers
     def _base(self, name: str) -> Path:
-        if not name or "/" in name or name.startswith("."):
+        if not name or "/" in name or name.startswith(".") or len(name) > 200:
             raise ValueError(f"bad artifact name {name!r}")
-        return self.root / name
+        base = self.root / name
+        if base.is_symlink():
+            raise ValueError(f"artifact directory {base} is a symbolic link")
+        return base
 
     @contextmanager
     def _locked(self, name: str):
@@ -112,6 +157,7 @@ class ImmutableArtifacts:
     # ---------------------------------------------------------------------- publish / resolve
     def publish(self, name: str, files: dict) -> Generation:
         """Publish ``files`` ({relative path: bytes or a source file path}) as a new generation."""
+        self._check_size(files)
         with self._locked(name) as base:
             staging_root = base / ".staging"
             if staging_root.exists():  # abandoned by a crashed publisher (we hold the lock)
@@ -175,4 +221,33 @@ class ImmutableArtifacts:
         return None
 
 
-__all__ = ["ArtifactIntegrityError", "Generation", "ImmutableArtifacts"]
+    # ---------------------------------------------------------------------- retention
+    def names(self) -> list[str]:
+        return sorted(p.name for p in self.root.iterdir() if p.is_dir() and not p.name.startswith("."))
+
+    def delete(self, name: str) -> bool:
+        """Remove every generation of ``name``; False when it had none.  The directory is renamed
+        out of the way under the publication lock first, so a reader never sees part of it."""
+        base = self._base(name)
+        if not base.exists():
+            return False
+        trash = self.root / ".trash"
+        trash.mkdir(exist_ok=True)
+        with self._locked(name):
+            dst = trash / uuid.uuid4().hex
+            os.rename(base, dst)
+            _fsync_dir(self.root)
+        shutil.rmtree(dst, ignore_errors=True)
+        return True
+
+    def sweep(self, keep) -> list[str]:
+        """Delete the names not in ``keep`` and leftover trash; returns the names removed."""
+        keep = set(keep)
+        gone = [n for n in self.names() if n not in keep]
+        for n in gone:
+            self.delete(n)
+        shutil.rmtree(self.root / ".trash", ignore_errors=True)
+        return gone
+
+
+__all__ = ["ArtifactIntegrityError", "ArtifactNoSpace", "ArtifactTooLarge", "Generation", "ImmutableArtifacts"]

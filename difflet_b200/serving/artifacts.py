@@ -56,6 +56,14 @@ class LocalArtifactStore:
         with open(self._path(ref.key), "rb") as f:
             return f.read()
 
+    def delete(self, key: str) -> bool:
+        """Remove an object; False when there was none."""
+        try:
+            os.unlink(self._path(key))
+            return True
+        except FileNotFoundError:
+            return False
+
     def get_url(self, ref: ArtifactRef, ttl_seconds: int = 3600) -> str:
         if self.base_url:
             return self.base_url.rstrip("/") + "/" + urllib.parse.quote(ref.key)
@@ -178,6 +186,22 @@ class S3ArtifactStore:
     def get_bytes(self, ref: ArtifactRef) -> bytes:
         with urllib.request.urlopen(self.get_url(ref, 300), timeout=self.timeout) as resp:
             return resp.read()
+
+    def delete(self, key: str) -> bool:
+        """DELETE through a presigned URL; a missing object (404) counts as deleted.  Raises
+        OSError on any other failure so the caller can retry later."""
+        import urllib.error
+
+        req = urllib.request.Request(self.presign("DELETE", key, 900), method="DELETE")
+        try:
+            with urllib.request.urlopen(req, timeout=self.timeout) as resp:
+                if resp.status // 100 != 2:
+                    raise OSError(f"S3 DELETE of {key!r} failed with HTTP {resp.status}")
+        except urllib.error.HTTPError as exc:
+            if exc.code == 404:
+                return False
+            raise OSError(f"S3 DELETE of {key!r} failed with HTTP {exc.code}") from exc
+        return True
 
 
 def make_artifact_store(local_dir: str | None = None):

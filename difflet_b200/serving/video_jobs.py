@@ -181,8 +181,56 @@ class VideoJobStore:
         self._running: str | None = None
         for job in self.repo.recover():
             self._q.put(job.id)
+        # files whose job record is gone (a crash between the two deletions), and remote objects
+        # whose deletion failed earlier
+        self.artifacts.sweep(keep=list(self.repo._jobs))
+        self._pending_path = os.path.join(self.dir, "pending_remote_deletes.json")
+        self.retry_remote_deletes()
         self._t = threading.Thread(target=self._loop, daemon=True)
         self._t.start()
+
+    # ------------------------------------------------------------------ deletion
+    def _pending(self) -> list:
+        try:
+            with open(self._pending_path) as f:
+                return list(json.load(f))
+        except (FileNotFoundError, ValueError):
+            return []
+
+    def _write_pending(self, keys: list) -> None:
+        tmp = self._pending_path + ".tmp"
+        with open(tmp, "w") as f:
+            json.dump(sorted(set(keys)), f)
+            f.flush()
+            os.fsync(f.fileno())
+        os.replace(tmp, self._pending_path)
+
+    def retry_remote_deletes(self) -> int:
+        """Delete the remote objects whose deletion failed before; returns how many are left."""
+        if self.remote is None or not hasattr(self.remote, "delete"):
+            return len(self._pending())
+        left = []
+        for key in self._pending():
+            try:
+                self.remote.delete(key)
+            except OSError:
+                left.append(key)
+        if left or os.path.exists(self._pending_path):
+            self._write_pending(left)
+        return len(left)
+
+    def delete(self, vid: str) -> None:
+        """Delete a finished job: its record, its local generations and its remote object.  A
+        remote deletion that fails is recorded and retried on the next delete and at start-up."""
+        self.repo.delete(vid)
+        self.artifacts.delete(vid)
+        if self.remote is not None and hasattr(self.remote, "delete"):
+            key = f"videos/{vid}.avi"
+            try:
+                self.remote.delete(key)
+            except OSError:
+                self._write_pending(self._pending() + [key])
+            self.retry_remote_deletes()
 
     @property
     def jobs(self) -> dict:

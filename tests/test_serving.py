@@ -335,6 +335,12 @@ def test_s3_store_against_a_fake_endpoint(monkeypatch):
             if data is not None:
                 self.wfile.write(data)
 
+        def do_DELETE(self):
+            ok, path = self._check()
+            code = 403 if not ok else (204 if objects.pop(path, None) is not None else 404)
+            self.send_response(code)
+            self.end_headers()
+
         def log_message(self, *a):
             pass
 
@@ -354,6 +360,11 @@ def test_s3_store_against_a_fake_endpoint(monkeypatch):
         assert urllib.request.urlopen(url, timeout=10).read() == b"RIFF-data"
         with pytest.raises(urllib.error.HTTPError):
             urllib.request.urlopen(url.replace("X-Amz-Expires=60", "X-Amz-Expires=600"), timeout=10)
+        assert store.delete("videos/v1.avi") is True and objects == {}
+        assert store.delete("videos/v1.avi") is False  # already gone (404)
+        store.secret_key = "wrong"
+        with pytest.raises(OSError):  # refused: kept for a retry
+            store.delete("videos/v1.avi")
     finally:
         srv.shutdown()
 
@@ -456,3 +467,62 @@ def _try(eng, req, rid):
         return eng.generate(req, request_id=rid)
     except Exception as exc:  # noqa: BLE001
         return exc
+
+
+def test_artifact_limits_delete_and_sweep(tmp_path):
+    """Generations are bounded (size limit, reserved free space), deleted whole, and names the
+    caller no longer knows are swept."""
+    from difflet_b200.serving.artifact_manager import ArtifactNoSpace, ArtifactTooLarge, ImmutableArtifacts
+
+    a = ImmutableArtifacts(tmp_path / "art", max_bytes=1000, reserve_bytes=0)
+    g = a.publish("v1", {"video.avi": b"x" * 100})
+    a.publish("v2", {"video.avi": b"y" * 10})
+    with pytest.raises(ArtifactTooLarge):
+        a.publish("v3", {"video.avi": b"z" * 1001})
+    assert a.names() == ["v1", "v2"]  # nothing staged for the refused one
+    link = tmp_path / "link"
+    link.symlink_to(g.file("video.avi"))
+    with pytest.raises(ValueError):
+        a.publish("v4", {"video.avi": str(link)})
+    tight = ImmutableArtifacts(tmp_path / "art", reserve_bytes=a.available_bytes() + 1)
+    with pytest.raises(ArtifactNoSpace):
+        tight.publish("v5", {"video.avi": b"w"})
+    assert a.delete("v1") and not a.delete("v1")
+    assert a.resolve("v1") is None and not g.path.exists()
+    assert a.sweep(keep=["v1"]) == ["v2"] and a.names() == []
+    assert not (tmp_path / "art" / ".trash").exists()
+
+
+def test_deleting_a_video_removes_its_files_and_remote_object(tmp_path):
+    """DELETE /v1/videos/{id} removes the record, the local generation and the remote object; a
+    remote deletion that fails is retried later; files without a record are swept at start-up."""
+    from difflet_b200.serving.artifacts import LocalArtifactStore
+
+    class Flaky(LocalArtifactStore):
+        fail = True
+
+        def delete(self, key):
+            if self.fail:
+                raise OSError("endpoint down")
+            return super().delete(key)
+
+    remote = Flaky(str(tmp_path / "remote"))
+    eng = InProcessEngine(lambda req: torch.zeros(5, 16, 16, 3, dtype=torch.uint8))
+    app = create_app(eng, "wan", output="video", video_dir=str(tmp_path / "svc"), artifact_store=remote)
+    c = TestClient(app)
+    vid = c.post("/v1/videos", json={"prompt": "waves", "size": "16x16"}).json()["id"]
+    jobs = c.app.state.jobs
+    assert jobs.wait(vid, 10).status == "completed"
+    assert (tmp_path / "remote" / "videos" / f"{vid}.avi").exists()
+    r = c.delete(f"/v1/videos/{vid}")
+    assert r.status_code == 200 and r.json()["deleted"]
+    assert jobs.artifacts.names() == [] and c.get(f"/v1/videos/{vid}").status_code == 404
+    assert (tmp_path / "remote" / "videos" / f"{vid}.avi").exists()  # the remote delete failed ...
+    Flaky.fail = False
+    assert jobs.retry_remote_deletes() == 0  # ... and is retried
+    assert not (tmp_path / "remote" / "videos" / f"{vid}.avi").exists()
+    jobs.artifacts.publish("orphan", {"video.avi": b"RIFF"})
+    from difflet_b200.serving.video_jobs import VideoJobStore
+
+    VideoJobStore(eng, str(tmp_path / "svc"), lambda f, fps: b"", artifact_store=remote)
+    assert "orphan" not in jobs.artifacts.names()
