@@ -106,13 +106,14 @@ def normalize_chat_request(payload: dict) -> dict:
 
 def create_app(engine, model_id: str, *, output: str = "image", api_key: str | None = None,
                request_timeout: float = 600.0, video_dir: str | None = None, encode_image=None,
-               encode_video=None, artifact_store=None) -> FastAPI:
+               encode_video=None, artifact_store=None, video_limits: dict | None = None) -> FastAPI:
     from difflet_b200.utils.media import encode_mjpeg_avi, encode_png
 
     encode_image = encode_image or encode_png
     encode_video = encode_video or encode_mjpeg_avi
     app = FastAPI(title="difflet_b200", version="0.1.0")
-    jobs = VideoJobStore(engine, video_dir, encode_video, artifact_store=artifact_store) if output == "video" else None
+    jobs = (VideoJobStore(engine, video_dir, encode_video, artifact_store=artifact_store, **(video_limits or {}))
+            if output == "video" else None)
 
     from fastapi.exceptions import RequestValidationError
 
@@ -236,7 +237,12 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
 
         @app.post("/v1/videos")
         async def create_video(payload: Any = Body(default=None)):
-            job = jobs.create(_video_request(payload))
+            from difflet_b200.serving.video_jobs import JobAdmissionError
+
+            try:
+                job = jobs.create(_video_request(payload))
+            except JobAdmissionError as exc:
+                raise ServingError(429, str(exc), "server_busy")
             return job.public()
 
         @app.post("/v1/videos/sync")

@@ -161,15 +161,35 @@ class VideoJobRepository:
         return self.list(status="queued", limit=1 << 30)
 
 
+class JobAdmissionError(RuntimeError):
+    """A job the service cannot take now (its queue or its job table is full)."""
+
+
 class VideoJobStore:
     """The video service: repository + dispatcher thread + artifact publication + cancellation.
 
     ``engine.generate(request)`` returns uint8 frames (or encoded bytes); ``engine.cancel(id)``,
-    when the engine has it, stops a running request between denoise steps."""
+    when the engine has it, stops a running request between denoise steps.
 
-    def __init__(self, engine, directory: str | None, encode_video, fps: int = 16, artifact_store=None):
+    Bounds, as in the reference service (``difflet/serving/video_service.py:165-260``): at most
+    ``max_queued`` jobs wait behind the running one and at most ``max_jobs`` records exist (a
+    new job beyond either is refused); a job that waited longer than ``queue_timeout_s`` fails
+    without running, one that runs longer than ``request_timeout_s`` is cancelled and fails as
+    timed out; finished jobs older than ``retention_s`` are deleted with their files by a sweep
+    every ``sweep_interval_s``."""
+
+    def __init__(self, engine, directory: str | None, encode_video, fps: int = 16, artifact_store=None, *,
+                 max_queued: int = 64, max_jobs: int = 4096, queue_timeout_s: float | None = None,
+                 request_timeout_s: float | None = None, retention_s: float = 25 * 3600.0,
+                 sweep_interval_s: float = 300.0):
         from difflet_b200.serving.artifact_manager import ImmutableArtifacts
 
+        if max_queued < 0 or max_jobs < 1 or retention_s <= 0 or sweep_interval_s <= 0:
+            raise ValueError("max_queued >= 0, max_jobs >= 1 and positive retention / sweep interval required")
+        self.max_queued, self.max_jobs = int(max_queued), int(max_jobs)
+        self.queue_timeout_s, self.request_timeout_s = queue_timeout_s, request_timeout_s
+        self.retention_s, self.sweep_interval_s = float(retention_s), float(sweep_interval_s)
+        self._timed_out: set = set()
         self.engine = engine
         self.dir = directory or tempfile.mkdtemp(prefix="difflet_videos_")
         self.repo = VideoJobRepository(os.path.join(self.dir, "jobs"))
@@ -188,6 +208,33 @@ class VideoJobStore:
         self.retry_remote_deletes()
         self._t = threading.Thread(target=self._loop, daemon=True)
         self._t.start()
+        self._stop = threading.Event()
+        self._sweeper = threading.Thread(target=self._sweep_loop, daemon=True)
+        self._sweeper.start()
+
+    def close(self) -> None:
+        self._stop.set()
+
+    # ------------------------------------------------------------------ retention
+    def sweep_expired(self, now: float | None = None) -> list:
+        """Delete finished jobs older than the retention (record, local and remote files)."""
+        now = time.time() if now is None else now
+        gone = []
+        for job in list(self.repo._jobs.values()):
+            if job.status in TERMINAL and now - (job.completed_at or job.created_at) > self.retention_s:
+                try:
+                    self.delete(job.id)
+                    gone.append(job.id)
+                except (VideoJobNotFound, InvalidTransition):
+                    pass
+        return gone
+
+    def _sweep_loop(self):
+        while not self._stop.wait(self.sweep_interval_s):
+            try:
+                self.sweep_expired()
+            except Exception:  # noqa: BLE001 - the next sweep tries again
+                pass
 
     # ------------------------------------------------------------------ deletion
     def _pending(self) -> list:
@@ -236,7 +283,16 @@ class VideoJobStore:
     def jobs(self) -> dict:
         return self.repo._jobs
 
+    def queued(self) -> int:
+        return sum(1 for j in self.repo._jobs.values() if j.status == "queued")
+
     def create(self, request: dict) -> VideoJob:
+        if self.queued() >= self.max_queued:
+            raise JobAdmissionError(f"{self.max_queued} video jobs are already waiting")
+        if len(self.repo._jobs) >= self.max_jobs:
+            self.sweep_expired()
+            if len(self.repo._jobs) >= self.max_jobs:
+                raise JobAdmissionError(f"the service holds {self.max_jobs} jobs; delete finished ones")
         job = self.repo.create(request)
         self._q.put(job.id)
         return job
@@ -259,11 +315,29 @@ class VideoJobStore:
     def _loop(self):
         while True:
             vid = self._q.get()
+            job = self.repo.get(vid)
+            if job is not None and job.status == "queued" and self.queue_timeout_s is not None \
+                    and time.time() - job.created_at > self.queue_timeout_s:
+                try:
+                    self.repo.transition(vid, "failed", expect="queued",
+                                         error=f"timed out after {self.queue_timeout_s:g} s in the queue")
+                except InvalidTransition:
+                    pass
+                continue
             try:
                 self.repo.transition(vid, "in_progress", expect="queued")
             except (InvalidTransition, VideoJobNotFound):
                 continue  # cancelled while queued
             self._running = vid
+            watch = None
+            if self.request_timeout_s is not None and hasattr(self.engine, "cancel"):
+                def _expire(v=vid):
+                    self._timed_out.add(v)
+                    self.engine.cancel(v)
+
+                watch = threading.Timer(self.request_timeout_s, _expire)
+                watch.daemon = True
+                watch.start()
             try:
                 req = dict(self.repo.require(vid).request)
                 frames = self.engine.generate(req, request_id=vid) if _takes_request_id(self.engine) \
@@ -278,12 +352,18 @@ class VideoJobStore:
                                      digest=gen.digest, url=url)
             except Exception as exc:  # noqa: BLE001
                 cancelled = type(exc).__name__ in ("RequestCancelled",) or "cancelled" in str(exc).lower()
+                timed_out = vid in self._timed_out
+                to = "failed" if timed_out or not cancelled else "cancelled"
+                err = (f"timed out after {self.request_timeout_s:g} s" if timed_out
+                       else None if cancelled else repr(exc))
                 try:
-                    self.repo.transition(vid, "cancelled" if cancelled else "failed", expect="in_progress",
-                                         error=None if cancelled else repr(exc))
+                    self.repo.transition(vid, to, expect="in_progress", error=err)
                 except InvalidTransition:
                     pass
             finally:
+                if watch is not None:
+                    watch.cancel()
+                self._timed_out.discard(vid)
                 self._running = None
 
     def wait(self, vid: str, timeout: float = 60.0) -> VideoJob:
@@ -305,4 +385,4 @@ def _takes_request_id(engine) -> bool:
         return False
 
 
-__all__ = ["InvalidTransition", "STATES", "VideoJob", "VideoJobNotFound", "VideoJobRepository", "VideoJobStore"]
+__all__ = ["InvalidTransition", "JobAdmissionError", "STATES", "VideoJob", "VideoJobNotFound", "VideoJobRepository", "VideoJobStore"]

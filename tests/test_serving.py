@@ -526,3 +526,62 @@ def test_deleting_a_video_removes_its_files_and_remote_object(tmp_path):
 
     VideoJobStore(eng, str(tmp_path / "svc"), lambda f, fps: b"", artifact_store=remote)
     assert "orphan" not in jobs.artifacts.names()
+
+
+def test_video_service_bounds_timeouts_and_retention(tmp_path):
+    """Jobs beyond the queue bound are refused (429); a job that waited past the queue timeout
+    fails without running; a running one past the request timeout is cancelled and fails as
+    timed out; finished jobs past the retention are deleted with their files."""
+    from difflet_b200.serving.video_jobs import VideoJobStore
+
+    gate = threading.Event()
+    ran = []
+
+    class Eng(InProcessEngine):
+        def __init__(self):
+            super().__init__(self._gen)
+            self.cancelled = set()
+
+        def _gen(self, req):
+            ran.append(req["prompt"])
+            if req["prompt"] == "slow":
+                gate.wait(10)
+            if req["prompt"] == "hang":
+                for _ in range(200):  # a generation that polls its cancellation between steps
+                    if "hang-id" in self.cancelled or self.cancelled:
+                        raise RuntimeError("request cancelled")
+                    time.sleep(0.02)
+            return torch.zeros(5, 16, 16, 3, dtype=torch.uint8)
+
+        def cancel(self, rid):
+            self.cancelled.add(rid)
+            return True
+
+    eng = Eng()
+    app = create_app(eng, "wan", output="video", video_dir=str(tmp_path / "a"),
+                     video_limits={"max_queued": 1, "queue_timeout_s": 0.2})
+    c = TestClient(app)
+    jobs = c.app.state.jobs
+    slow = c.post("/v1/videos", json={"prompt": "slow", "size": "16x16"}).json()["id"]
+    t0 = time.time()
+    while jobs.get(slow).status != "in_progress" and time.time() - t0 < 5:
+        time.sleep(0.01)
+    waiting = c.post("/v1/videos", json={"prompt": "late", "size": "16x16"}).json()["id"]
+    r = c.post("/v1/videos", json={"prompt": "third", "size": "16x16"})
+    assert r.status_code == 429 and r.json()["error"]["code"] == "server_busy"
+    time.sleep(0.4)
+    gate.set()
+    assert jobs.wait(slow, 10).status == "completed"
+    late = jobs.wait(waiting, 10)
+    assert late.status == "failed" and "queue" in late.error and "late" not in ran
+
+    svc = VideoJobStore(Eng(), str(tmp_path / "b"), lambda f, fps: b"RIFF", request_timeout_s=0.2, retention_s=60)
+    hung = svc.create({"prompt": "hang"})
+    j = svc.wait(hung.id, 10)
+    assert j.status == "failed" and "timed out" in j.error
+    done = svc.create({"prompt": "ok"})
+    assert svc.wait(done.id, 10).status == "completed" and done.id in svc.artifacts.names()
+    assert svc.sweep_expired(now=time.time() + 30) == []
+    assert set(svc.sweep_expired(now=time.time() + 120)) == {hung.id, done.id}
+    assert svc.get(done.id) is None and svc.artifacts.names() == []
+    svc.close()
