@@ -118,6 +118,11 @@ def build_parser() -> argparse.ArgumentParser:
     b.add_argument("--out", default="bench_results", help="suite results directory (JSONL per suite)")
     b.add_argument("--dry-run", action="store_true", help="print the suite's launches without running them")
     b.add_argument("--no-idle-check", action="store_true", help="skip the GPU idle check before each launch")
+    b.add_argument("--compare", nargs=2, metavar=("A", "B"), default=None,
+                   help="compare result B against result A (bench.py lines or suite JSONL)")
+    b.add_argument("--report", metavar="DIR", default=None, help="write DIR/SUMMARY.md from the results under DIR")
+    b.add_argument("--timing", metavar="DIR", default=None,
+                   help="summarise a launch's telemetry (DIFFLET_BENCH_TIMING_DIR files)")
     return ap
 
 
@@ -362,6 +367,20 @@ def cmd_serve(a) -> int:
 
 
 def cmd_bench(a) -> int:
+    if a.compare:
+        from difflet_b200.bench.compare import main as cmain
+
+        return cmain(list(a.compare))
+    if a.report:
+        from difflet_b200.bench.report import report
+
+        print(report(a.report))
+        return 0
+    if a.timing:
+        from difflet_b200.bench import timing
+
+        print(json.dumps(timing.summarize(timing.read_launch(a.timing)), indent=1))
+        return 0
     if a.suite:
         from difflet_b200.bench import suite as S
 
