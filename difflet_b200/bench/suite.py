@@ -144,8 +144,11 @@ def _result_line(stdout: str) -> dict | None:
 
 def run(suite: Suite, launches: list[Launch], out_dir: Path | str, *,
         launcher: Callable[..., Any] = subprocess.run, idle: Callable[[list[int]], Any] | None = None,
-        dry_run: bool = False, timeout_s: float = 3600.0) -> list[dict]:
-    """Execute ``launches``; one JSONL record per launch in ``<out_dir>/<suite>.jsonl``."""
+        dry_run: bool = False, timeout_s: float = 3600.0, memory_sampler: Callable[[list[int]], Any] | None = None
+        ) -> list[dict]:
+    """Execute ``launches``; one JSONL record per launch in ``<out_dir>/<suite>.jsonl``.
+    ``memory_sampler(devices)``: a context manager with ``summary()`` (``bench/memory.py``) run
+    around each launch; its per-GPU and per-process peaks go into the record."""
     from difflet_b200.bench import provenance
 
     out_dir = Path(out_dir)
@@ -171,7 +174,10 @@ def run(suite: Suite, launches: list[Launch], out_dir: Path | str, *,
                 _append(results_path, rec)
                 continue
         t0 = time.perf_counter()
+        sampler = memory_sampler(devices) if memory_sampler is not None else None
         try:
+            if sampler is not None:
+                sampler.__enter__()
             proc = launcher(cmd, capture_output=True, text=True, timeout=timeout_s,
                             env=ln.recipe.env(os.environ))
             rec["wall_s"] = round(time.perf_counter() - t0, 3)
@@ -181,6 +187,10 @@ def run(suite: Suite, launches: list[Launch], out_dir: Path | str, *,
                 rec["error"] = (proc.stderr or "")[-2000:]
         except subprocess.TimeoutExpired:
             rec["error"] = f"timeout after {timeout_s} s"
+        finally:
+            if sampler is not None:
+                sampler.__exit__(None, None, None)
+                rec["device_memory"] = sampler.summary()
         rec["provenance"] = prov
         records.append(rec)
         _append(results_path, rec)

@@ -391,7 +391,12 @@ def cmd_bench(a) -> int:
             from difflet_b200.bench.host import check_idle
 
             idle = check_idle
-        recs = S.run(su, launches, a.out, idle=idle, dry_run=a.dry_run)
+        sampler = None
+        if not a.dry_run:
+            from difflet_b200.bench.memory import DeviceMemorySampler
+
+            sampler = DeviceMemorySampler
+        recs = S.run(su, launches, a.out, idle=idle, dry_run=a.dry_run, memory_sampler=sampler)
         if a.dry_run:
             for r in recs:
                 print(json.dumps({"run": r["run"], "launch": r["launch"], "argv": r["argv"]}))

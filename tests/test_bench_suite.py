@@ -134,8 +134,22 @@ order: ABBA
                                            stderr="")
 
     idle = lambda devs: H.check_idle(devs, FakeNVML({0: (0, 0, 10)}))  # noqa: E731
-    recs = S.run(su, ls, tmp_path / "out", launcher=launcher, idle=idle)
+    class Mem:  # stands in for bench.memory.DeviceMemorySampler
+        def __init__(self, devices):
+            self.devices = devices
+
+        def __enter__(self):
+            return self
+
+        def __exit__(self, *exc):
+            pass
+
+        def summary(self):
+            return {"gpu_peak_gib": {str(d): 1.5 for d in self.devices}}
+
+    recs = S.run(su, ls, tmp_path / "out", launcher=launcher, idle=idle, memory_sampler=Mem)
     assert len(recs) == 4 and all(r["returncode"] == 0 and r["idle_check"]["idle"] for r in recs)
+    assert recs[0]["device_memory"] == {"gpu_peak_gib": {"0": 1.5}}
     assert seen[0][1]["DIFFLET_GEMM_PAIR"] == "1"
     lines = (tmp_path / "out" / "ab.jsonl").read_text().splitlines()
     assert len(lines) == 4 and json.loads(lines[0])["run"] == "one/a"

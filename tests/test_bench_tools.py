@@ -102,3 +102,33 @@ def test_page_cache_evict_warm_residency(tmp_path):
     assert pc.warm(files) == 4 << 20
     hot = pc.residency(files)
     assert hot["fraction"] == 1.0 and cold["fraction"] <= hot["fraction"] and hot["bytes"] == 4 << 20
+
+
+def test_device_memory_sampler_with_a_fake_nvml():
+    """Peaks per GPU and per process from NVML samples (a fake with the three queries used)."""
+    import time
+    from types import SimpleNamespace
+
+    from difflet_b200.bench.memory import DeviceMemorySampler
+
+    class FakeNVML:
+        def __init__(self):
+            self.tick = 0
+
+        def nvmlDeviceGetHandleByIndex(self, i):
+            return i
+
+        def nvmlDeviceGetComputeRunningProcesses(self, h):
+            self.tick += 1
+            grow = min(self.tick, 5) << 30
+            return [SimpleNamespace(pid=100 + h, usedGpuMemory=grow), SimpleNamespace(pid=999, usedGpuMemory=None)]
+
+        def nvmlDeviceGetMemoryInfo(self, h):
+            return SimpleNamespace(used=(min(self.tick, 5) + 1) << 30)
+
+    with DeviceMemorySampler([0, 1], interval_s=0.01, nvml=FakeNVML()) as s:
+        time.sleep(0.2)
+    out = s.summary()
+    assert out["error"] is None and out["samples"] >= 4
+    assert out["gpu_peak_gib"] == {"0": 6.0, "1": 6.0}
+    assert out["process_peak_gib"]["100"] == {"gpu": 0, "peak_gib": 5.0} and "999" not in out["process_peak_gib"]
