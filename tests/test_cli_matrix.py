@@ -36,3 +36,19 @@ def test_generate_writes_the_output(tmp_path, model_id, preset, shape, suffix):
     assert path.suffix == suffix and path.exists() and path.stat().st_size > 0
     head = path.read_bytes()[:12]
     assert head[:4] == (b"\x89PNG" if suffix == ".png" else b"RIFF")
+
+
+def test_dp_batch_writes_every_output(tmp_path):
+    """``--dp 2 --requests batch.jsonl``: two replica processes claim the requests; every output
+    is written once and the work directory is removed after a successful batch."""
+    env = dict(os.environ, PYTHONPATH=str(REPO) + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    reqs = tmp_path / "batch.jsonl"
+    reqs.write_text("".join(json.dumps({"prompt": p, "output": str(tmp_path / p)}) + "\n" for p in "abc"))
+    cmd = [sys.executable, "-m", "difflet_b200", "generate", "--model-id", "black-forest-labs/FLUX.1-dev",
+           "--backend", "cpu", "--random-weights", "--preset", "tiny128", "--height", "64", "--width", "64",
+           "--steps", "2", "--dp", "2", "--requests", str(reqs), "--work-dir", str(tmp_path / "work"),
+           "--cache-dir", str(tmp_path / "cache")]
+    proc = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env, cwd=str(tmp_path))
+    assert proc.returncode == 0, proc.stderr[-3000:]
+    assert all((tmp_path / f"{p}.png").exists() for p in "abc")
+    assert not (tmp_path / "work").exists()
