@@ -66,11 +66,53 @@ def error_payload(status: int, message: str, code: str | None = None) -> dict:
     return {"error": {"message": message, "type": etype, "code": code or default}}
 
 
+MAX_PROMPT_CHARS = 10000
+
+
 def _parse_size(size: str | None):
     if not size:
         return {}
-    w, h = str(size).lower().split("x")
-    return {"width": int(w), "height": int(h)}
+    try:
+        w, h = str(size).lower().split("x")
+        return {"width": int(w), "height": int(h)}
+    except ValueError:
+        raise ServingError(400, f"size must be WIDTHxHEIGHT, got {size!r}", "invalid_request") from None
+
+
+def _int_field(req, key, lo, hi, multiple=1):
+    v = req.get(key)
+    if v is None:
+        return
+    if isinstance(v, bool) or not isinstance(v, int) or not lo <= v <= hi or v % multiple:
+        extra = f", a multiple of {multiple}" if multiple > 1 else ""
+        raise ServingError(400, f"{key} must be an integer in [{lo}, {hi}]{extra}, got {v!r}", "invalid_request")
+
+
+def check_request_fields(req: dict) -> None:
+    """Types and ranges of the generation fields, checked before a request is queued (a bad value
+    answers 400 instead of failing inside the engine)."""
+    import math
+
+    prompt = req.get("prompt")
+    if not isinstance(prompt, str) or not prompt.strip():
+        raise ServingError(400, "prompt must be a non-empty string", "invalid_prompt")
+    if len(prompt) > MAX_PROMPT_CHARS:
+        raise ServingError(400, f"prompt has {len(prompt)} characters (at most {MAX_PROMPT_CHARS})",
+                           "prompt_too_long")
+    neg = req.get("negative_prompt")
+    if neg is not None and not isinstance(neg, str):
+        raise ServingError(400, "negative_prompt must be a string", "invalid_prompt")
+    _int_field(req, "height", 16, 8192, 16)
+    _int_field(req, "width", 16, 8192, 16)
+    _int_field(req, "num_inference_steps", 1, 1000)
+    _int_field(req, "num_frames", 1, 1024)
+    _int_field(req, "seed", 0, (1 << 63) - 1)
+    for key in ("guidance_scale", "guidance_scale_2", "true_cfg_scale"):
+        v = req.get(key)
+        if v is None:
+            continue
+        if isinstance(v, bool) or not isinstance(v, (int, float)) or not math.isfinite(v) or not 0 <= v <= 100:
+            raise ServingError(400, f"{key} must be a number in [0, 100], got {v!r}", "invalid_request")
 
 
 def normalize_chat_request(payload: dict) -> dict:
@@ -156,7 +198,8 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
     spec = spec_for_model_id(model_id)
 
     def _validate(req):
-        """Options the model does not take answer 400 before the request is queued."""
+        """Bad values and options the model does not take answer 400 before the request is queued."""
+        check_request_fields(req)
         if spec is None:
             return
         try:

@@ -28,7 +28,7 @@ def test_sweep_counts_completions_and_refusals():
     try:
         url = f"http://127.0.0.1:{port}"
         assert wait_ready(url, 30)
-        rows = sweep(url, levels=(1, 8), rounds=2, payload={"prompt": "x", "size": "8x8"}, timeout=30)
+        rows = sweep(url, levels=(1, 8), rounds=2, payload={"prompt": "x", "size": "16x16"}, timeout=30)
     finally:
         server.should_exit = True
         th.join(timeout=10)

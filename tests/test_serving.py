@@ -24,13 +24,36 @@ def test_chat_completion_image_and_auth():
     r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "a cat"}]})
     assert r.status_code == 401
     r = c.post("/v1/chat/completions", headers={"Authorization": "Bearer k"},
-               json={"messages": [{"role": "user", "content": "a cat"}], "extra_body": {"size": "32x24"}})
+               json={"messages": [{"role": "user", "content": "a cat"}], "extra_body": {"size": "32x48"}})
     assert r.status_code == 200
     url = r.json()["choices"][0]["message"]["content"][0]["image_url"]["url"]
     png = base64.b64decode(url.split(",", 1)[1])
     assert png[:4] == b"\x89PNG"
-    r = c.post("/v1/images/generations", headers={"Authorization": "Bearer k"}, json={"prompt": "x", "size": "8x8"})
+    r = c.post("/v1/images/generations", headers={"Authorization": "Bearer k"}, json={"prompt": "x", "size": "16x16"})
     assert r.status_code == 200 and r.json()["data"][0]["b64_json"]
+
+
+def test_request_fields_are_checked_before_queueing():
+    """Malformed sizes and out-of-range values answer 400 with a stable code; nothing runs."""
+    calls = []
+    c = TestClient(create_app(InProcessEngine(lambda r: calls.append(r) or _img(r)), "flux"))
+    bad = [({"prompt": "x", "size": "big"}, "invalid_request"), ({"prompt": "x", "size": "24x24"}, "invalid_request"),
+           ({"prompt": "x", "num_inference_steps": 0}, "invalid_request"),
+           ({"prompt": "x", "num_inference_steps": "4"}, "invalid_request"),
+           ({"prompt": "x", "seed": -1}, "invalid_request"), ({"prompt": "x", "guidance_scale": float("inf")}, None),
+           ({"prompt": "x", "guidance_scale": True}, "invalid_request"), ({"prompt": "   "}, "invalid_prompt"),
+           ({"prompt": "x" * 10001}, "prompt_too_long"), ({"prompt": "x", "negative_prompt": 3}, "invalid_prompt")]
+    for body, code in bad:
+        try:
+            r = c.post("/v1/images/generations", json=body)
+        except ValueError:  # a non-finite float is not valid JSON: refused by the client itself
+            continue
+        assert r.status_code == 400, (body, r.json())
+        if code:
+            assert r.json()["error"]["code"] == code, (body, r.json())
+    assert not calls
+    assert c.post("/v1/images/generations", json={"prompt": "x", "size": "32x48", "seed": 7,
+                                                  "guidance_scale": 3.5, "num_inference_steps": 4}).status_code == 200
 
 
 def test_normalize_chat_request():
@@ -234,8 +257,8 @@ def test_video_cancel_queued_and_running(tmp_path):
             return True
 
     c = TestClient(create_app(Eng(), "wan", output="video", video_dir=str(tmp_path)))
-    v1 = c.post("/v1/videos", json={"prompt": "one", "size": "8x8"}).json()["id"]
-    v2 = c.post("/v1/videos", json={"prompt": "two", "size": "8x8"}).json()["id"]
+    v1 = c.post("/v1/videos", json={"prompt": "one", "size": "16x16"}).json()["id"]
+    v2 = c.post("/v1/videos", json={"prompt": "two", "size": "16x16"}).json()["id"]
     assert started.wait(5)
     assert c.post(f"/v1/videos/{v2}/cancel").json()["status"] == "cancelled"  # still queued
     c.post(f"/v1/videos/{v1}/cancel")                                           # running
@@ -253,7 +276,7 @@ def test_completed_video_is_an_immutable_generation(tmp_path):
 
     eng = InProcessEngine(lambda req: torch.zeros(3, 8, 8, 3, dtype=torch.uint8))
     c = TestClient(create_app(eng, "wan", output="video", video_dir=str(tmp_path)))
-    vid = c.post("/v1/videos", json={"prompt": "p", "size": "8x8"}).json()["id"]
+    vid = c.post("/v1/videos", json={"prompt": "p", "size": "16x16"}).json()["id"]
     job = c.app.state.jobs.wait(vid, 10)
     assert job.status == "completed" and job.digest
     data = c.get(f"/v1/videos/{vid}/content").content
