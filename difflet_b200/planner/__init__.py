@@ -73,6 +73,13 @@ def _eff(rows: int) -> float:
 
 
 ATTN_EFF = 0.80  # flash attention's measured fraction of the sustained GEMM peak (FLUX 24 x 4608)
+ATTN_EFF_LONG = 0.89  # ... at video lengths (HunyuanVideo 118,800 tokens: per-tile overheads amortised)
+
+
+def _attn_eff(seq: int) -> float:
+    """Attention efficiency rising with the key length, log-linear from 5,120 to 118,800 keys."""
+    x = math.log(max(seq, 5120) / 5120) / math.log(118800 / 5120)
+    return ATTN_EFF + (ATTN_EFF_LONG - ATTN_EFF) * min(1.0, x)
 KERNEL_TAIL_S = 3e-6  # fill / drain of one launch inside the CUDA graph
 KERNELS_PER_LAYER = 8
 N_SMS = 148
@@ -97,7 +104,7 @@ def estimate_step_s(entry, p: DiffletParallelConfig, shape: dict, peak_flops: fl
     rows = S // p.cp_degree
     heads_rank = max(1, shape["heads"] // (p.tp_degree * p.cp_degree))
     t_comp = gemm_flops / (world_model * peak_flops * _eff(rows)) + attn_flops / (
-        world_model * peak_flops * ATTN_EFF * _attn_occupancy(heads_rank, S))
+        world_model * peak_flops * _attn_eff(S) * _attn_occupancy(heads_rank, S))
     act = S * D * 2 / max(1, p.cp_degree)  # bytes of one activation shard
     comm = 0.0
     syncs = 0

@@ -60,6 +60,22 @@ def test_wan_estimates_track_measured_steps(monkeypatch):
         assert abs(est_ms - measured_ms) / measured_ms < 0.1, (p, est_ms, measured_ms)
 
 
+def test_hunyuan_estimates_track_measured_steps(monkeypatch):
+    """HunyuanVideo 720x1280x129 (119,056 tokens, attention-bound) under ring CP: 10606 / 5304 /
+    2713 ms measured on 1 / 2 / 4 B200s."""
+    from difflet_b200 import planner as P
+    from difflet_b200.pipeline.parallel_config import DiffletParallelConfig
+    from difflet_b200.registry import resolve_model
+
+    monkeypatch.setattr(P, "_EFF_SCALE", [0.85])
+    e = resolve_model("hunyuanvideo-community/HunyuanVideo")
+    shape = P.model_shape(e, 720, 1280, 129)
+    for cp, measured_ms in ((1, 10606.0), (2, 5304.0), (4, 2713.0)):
+        p = DiffletParallelConfig(cp_degree=cp, cp_mode="ring") if cp > 1 else DiffletParallelConfig()
+        est_ms = P.estimate_step_s(e, p, shape, 1397.4e12) * 1e3
+        assert abs(est_ms - measured_ms) / measured_ms < 0.1, (cp, est_ms, measured_ms)
+
+
 class _FakeNVML:
     """A stand-in for pynvml: 8 GPUs of 183,359 MiB with 18 active NVLinks each."""
 
