@@ -19,7 +19,6 @@ the fused peer kernel; Ulysses shards the tokens.
 
 from __future__ import annotations
 
-import math
 
 import torch
 

@@ -26,7 +26,7 @@ halo rows over NVLink, the mid-block attention all-gathers K / V, and rank 0 ass
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 import torch.nn.functional as Fn

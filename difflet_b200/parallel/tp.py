@@ -28,7 +28,6 @@ TP-aware q/k norms; the TPU collective-matmul design precedent
 
 from __future__ import annotations
 
-import math
 
 import torch
 import torch.distributed as dist

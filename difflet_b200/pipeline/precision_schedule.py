@@ -24,7 +24,7 @@ import json
 import re
 from dataclasses import dataclass
 from pathlib import Path
-from typing import Any, Iterable
+from typing import Iterable
 
 PRECISION_BF16 = "bf16"
 PRECISION_MXFP8_E4M3 = "mxfp8_e4m3"
