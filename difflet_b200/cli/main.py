@@ -97,6 +97,10 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--request-timeout", type=float, default=600.0, help="seconds before a request is cancelled")
     s.add_argument("--heartbeat-interval", type=float, default=None, help="worker heartbeat period (s)")
     s.add_argument("--log-dir", default=None, help="serve log files (default: ./logs), one per 5 MB and per day")
+    s.add_argument("--video-retention-hours", type=float, default=25.0,
+                   help="video models: finished jobs and their files are deleted after this long")
+    s.add_argument("--max-video-jobs", type=int, default=4096,
+                   help="video models: job records kept at most (new jobs beyond: HTTP 429)")
     q = sub.add_parser("quant", help="write the MXFP8 checkpoint of a model (or print its plan)")
     q.add_argument("--model-id", required=True)
     q.add_argument("--revision", default=None)

@@ -87,7 +87,9 @@ def serve_main(a) -> int:
     store = make_artifact_store() if entry.output == "video" and any(k.startswith("DIFFLET_S3_") for k in os.environ) \
         else None
     app = create_app(engine, a.model_id, output=entry.output, api_key=opts.api_key, artifact_store=store,
-                     video_limits={"max_queued": opts.max_queued_requests, "request_timeout_s": opts.request_timeout})
+                     video_limits={"max_queued": opts.max_queued_requests, "request_timeout_s": opts.request_timeout,
+                                   "retention_s": 3600.0 * getattr(a, "video_retention_hours", 25.0),
+                                   "max_jobs": getattr(a, "max_video_jobs", 4096)})
     uvicorn.run(app, host=opts.host, port=opts.port, log_level="info", log_config=None)
     engine.close()
     return 0
