@@ -132,3 +132,31 @@ def test_device_memory_sampler_with_a_fake_nvml():
     assert out["error"] is None and out["samples"] >= 4
     assert out["gpu_peak_gib"] == {"0": 6.0, "1": 6.0}
     assert out["process_peak_gib"]["100"] == {"gpu": 0, "peak_gib": 5.0} and "999" not in out["process_peak_gib"]
+
+
+def test_timing_reader_reads_what_the_engine_writes(tmp_path):
+    """Round trip through the real writer, in a fresh process (its sink opens on first use)."""
+    import subprocess
+    import sys
+    import textwrap
+    from pathlib import Path
+
+    from difflet_b200.bench import timing
+
+    code = textwrap.dedent("""
+        from difflet_b200.utils import telemetry as t
+        t.event("process", role="driver")
+        with t.span("request", request="r0"):
+            for i in range(3):
+                t.event("step", index=i)
+            t.event("forward", seconds=0.25)
+    """)
+    repo = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, DIFFLET_BENCH_TIMING_DIR=str(tmp_path), PYTHONPATH=str(repo), RANK="0", WORLD_SIZE="1")
+    subprocess.run([sys.executable, "-c", code], env=env, check=True, timeout=120)
+    logs = timing.read_launch(tmp_path)
+    assert len(logs) == 1 and logs[0].role == "driver" and logs[0].forwards == [0.25]
+    sp = logs[0].spans[0]
+    assert sp.name == "request" and sp.ok is True and sp.seconds >= 0 and sp.fields.get("request") == "r0"
+    s = timing.summarize(logs)
+    assert s["steps"] == 3 and s["bad_lines"] == 0 and s["unfinished_spans"] == []
