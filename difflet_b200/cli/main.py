@@ -114,6 +114,9 @@ def build_parser() -> argparse.ArgumentParser:
     cl = sub.add_parser("clean", help="remove cache entries")
     cl.add_argument("--cache-dir", default=None)
     cl.add_argument("--model", default=None)
+    cl.add_argument("--key", default=None, help="one entry (its hash directory name)")
+    cl.add_argument("--older-than-days", type=float, default=None, help="entries whose manifest is older")
+    cl.add_argument("--dry-run", action="store_true", help="list what would be removed")
     cl.add_argument("--all", action="store_true")
     b = sub.add_parser("bench", help="kernel microbenchmarks (or the headline bench with --headline)")
     b.add_argument("--only", default="gemm,attn,ln")
@@ -265,32 +268,87 @@ def cmd_generate(a) -> int:
     return 0
 
 
+def _dir_size(path: Path) -> int:
+    """Bytes under ``path``, each inode once (weight shards hard-linked between entries are
+    counted in every entry that links them, but once within one)."""
+    seen, total = set(), 0
+    for root, _dirs, files in os.walk(path):
+        for f in files:
+            try:
+                st = os.lstat(os.path.join(root, f))
+            except OSError:
+                continue
+            if st.st_ino not in seen:
+                seen.add(st.st_ino)
+                total += st.st_size
+    return total
+
+
+def _cache_entries(root: Path) -> list[dict]:
+    """Every cache entry (a ``<model>/<key>`` directory holding a manifest), never following links."""
+    rows = []
+    for m in sorted(root.glob("*/*/manifest.json")):
+        entry = m.parent
+        if entry.is_symlink() or entry.parent.is_symlink():
+            continue
+        try:
+            doc = json.loads(m.read_text())
+        except (OSError, ValueError):
+            doc = {}
+        inputs = doc.get("inputs", {})
+        rows.append({"model": entry.parent.name, "key": entry.name, "path": str(entry),
+                     "parallel": inputs.get("parallel"), "shapes": inputs.get("shapes"), "dtype": inputs.get("dtype"),
+                     "bytes": _dir_size(entry), "mtime": m.stat().st_mtime})
+    return rows
+
+
 def cmd_cache(a) -> int:
     from difflet_b200 import envs
 
     root = Path(a.cache_dir or envs.DIFFLET_COMPILE_CACHE)
-    rows = []
-    for m in sorted(root.glob("*/*/manifest.json")):
-        doc = json.loads(m.read_text())
-        rows.append({"model": m.parent.parent.name, "key": m.parent.name,
-                     "parallel": doc.get("inputs", {}).get("parallel"), "shapes": doc.get("inputs", {}).get("shapes"),
-                     "dtype": doc.get("inputs", {}).get("dtype")})
+    rows = _cache_entries(root) if root.exists() else []
     if a.json:
         print(json.dumps(rows, indent=2))
     else:
         for r in rows:
-            print(f"{r['model']:20s} {r['key']}  {r['dtype']}  {r['parallel']}  {r['shapes']}")
+            print(f"{r['model']:20s} {r['key']}  {r['bytes'] / 2**20:9.1f} MiB  {r['dtype']}  {r['parallel']}  "
+                  f"{r['shapes']}")
+        print(f"{len(rows)} entries, {sum(r['bytes'] for r in rows) / 2**30:.2f} GiB")
     return 0
 
 
 def cmd_clean(a) -> int:
+    """Remove cache entries: all, one model's, one key, or those older than N days.  Only
+    directories holding a manifest are removed, links are never followed, and names are plain
+    directory names (no path can reach outside the cache)."""
     from difflet_b200 import envs
 
     root = Path(a.cache_dir or envs.DIFFLET_COMPILE_CACHE)
-    if a.all:
-        shutil.rmtree(root, ignore_errors=True)
-    elif a.model:
-        shutil.rmtree(root / a.model, ignore_errors=True)
+    for name, val in (("--model", a.model), ("--key", a.key)):
+        if val is not None and (not val or "/" in val or os.sep in val or val in (".", "..")):
+            print(f"{name} must be a plain name, got {val!r}", file=sys.stderr)
+            return 2
+    if not (a.all or a.model or a.key or a.older_than_days is not None):
+        print("nothing selected: give --all, --model, --key or --older-than-days", file=sys.stderr)
+        return 2
+    now = time.time()
+    doomed = []
+    for r in (_cache_entries(root) if root.exists() else []):
+        if a.model and r["model"] != a.model:
+            continue
+        if a.key and r["key"] != a.key:
+            continue
+        if a.older_than_days is not None and now - r["mtime"] < a.older_than_days * 86400:
+            continue
+        doomed.append(r)
+    for r in doomed:
+        print(("would remove " if a.dry_run else "removing ") + r["path"])
+        if not a.dry_run:
+            shutil.rmtree(r["path"], ignore_errors=True)
+            try:
+                Path(r["path"]).parent.rmdir()  # the model directory, once empty
+            except OSError:
+                pass
     return 0
 
 

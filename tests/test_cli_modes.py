@@ -2,9 +2,10 @@
 --host-vae decode on the host, --dp-schedule static assignment, difflet quant plans."""
 
 import json
-import time
+import os
 import subprocess
 import sys
+import time
 from pathlib import Path
 
 import pytest
@@ -107,3 +108,40 @@ def test_children_die_with_their_parent():
     while alive() and time.time() < deadline:
         time.sleep(0.1)
     assert not alive()
+
+
+def test_cache_listing_and_clean_selection(tmp_path, capsys):
+    """``cache`` lists entries with their sizes (hard links counted once per entry); ``clean``
+    removes only manifest-holding entries chosen by model / key / age, refuses path-like names
+    and never follows links out of the cache."""
+    from difflet_b200.cli.main import main
+
+    root = tmp_path / "cache"
+    outside = tmp_path / "precious"
+    outside.mkdir()
+    (outside / "keep.txt").write_text("x")
+    for model, key, age_days in (("flux", "aaaa", 0), ("flux", "bbbb", 10), ("wan", "cccc", 0)):
+        d = root / model / key
+        d.mkdir(parents=True)
+        (d / "manifest.json").write_text(json.dumps({"inputs": {"dtype": "bf16", "parallel": {}, "shapes": []}}))
+        (d / "w.bin").write_bytes(b"0" * 1000)
+        t = time.time() - age_days * 86400
+        os.utime(d / "manifest.json", (t, t))
+    os.link(root / "flux" / "aaaa" / "w.bin", root / "flux" / "aaaa" / "w2.bin")
+    (root / "linked").mkdir()
+    (root / "linked" / "evil").symlink_to(outside, target_is_directory=True)
+    (outside / "manifest.json").write_text("{}")
+    assert main(["cache", "--cache-dir", str(root), "--json"]) == 0
+    rows = json.loads(capsys.readouterr().out)
+    sizes = {r["key"]: r["bytes"] for r in rows}
+    assert set(sizes) == {"aaaa", "bbbb", "cccc"} and sizes["aaaa"] == sizes["bbbb"]  # the hard link once
+    assert main(["clean", "--cache-dir", str(root), "--model", "../precious"]) == 2
+    assert main(["clean", "--cache-dir", str(root)]) == 2
+    assert main(["clean", "--cache-dir", str(root), "--older-than-days", "5", "--dry-run"]) == 0
+    assert (root / "flux" / "bbbb").exists()
+    assert main(["clean", "--cache-dir", str(root), "--older-than-days", "5"]) == 0
+    assert not (root / "flux" / "bbbb").exists() and (root / "flux" / "aaaa").exists()
+    assert main(["clean", "--cache-dir", str(root), "--key", "cccc"]) == 0
+    assert not (root / "wan").exists()
+    assert main(["clean", "--cache-dir", str(root), "--all"]) == 0
+    assert not (root / "flux").exists() and (outside / "keep.txt").exists()
