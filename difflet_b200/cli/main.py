@@ -231,9 +231,14 @@ def cmd_generate(a) -> int:
         from difflet_b200.cli.dp import run_router
 
         work = a.work_dir or (a.output + ".work")
+        # a directory that held files before this batch is not the batch's to delete
+        foreign = Path(work).is_symlink() or (Path(work).is_dir() and any(Path(work).iterdir()))
         rc = run_router(sys.argv[1:], a.dp, world, work, schedule=a.dp_schedule)
         if rc == 0 and not a.keep_work_dir:
-            shutil.rmtree(work, ignore_errors=True)
+            if foreign:
+                print(f"difflet: keeping {work}: it was not empty before this batch", file=sys.stderr)
+            else:
+                shutil.rmtree(work, ignore_errors=True)
         return rc
     if world > 1 and not os.environ.get("DIFFLET_UNDER_TORCHRUN"):
         from difflet_b200.cli.runner import run_torchrun

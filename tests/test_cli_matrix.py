@@ -52,3 +52,20 @@ def test_dp_batch_writes_every_output(tmp_path):
     assert proc.returncode == 0, proc.stderr[-3000:]
     assert all((tmp_path / f"{p}.png").exists() for p in "abc")
     assert not (tmp_path / "work").exists()
+
+
+def test_dp_batch_keeps_a_work_dir_that_held_files(tmp_path):
+    """A ``--work-dir`` that already held files is left in place after the batch."""
+    env = dict(os.environ, PYTHONPATH=str(REPO) + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    work = tmp_path / "mine"
+    work.mkdir()
+    (work / "notes.txt").write_text("keep me")
+    reqs = tmp_path / "batch.jsonl"
+    reqs.write_text(json.dumps({"prompt": "a", "output": str(tmp_path / "a")}) + "\n")
+    cmd = [sys.executable, "-m", "difflet_b200", "generate", "--model-id", "black-forest-labs/FLUX.1-dev",
+           "--backend", "cpu", "--random-weights", "--preset", "tiny128", "--height", "64", "--width", "64",
+           "--steps", "2", "--dp", "2", "--requests", str(reqs), "--work-dir", str(work),
+           "--cache-dir", str(tmp_path / "cache")]
+    proc = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env, cwd=str(tmp_path))
+    assert proc.returncode == 0, proc.stderr[-3000:]
+    assert (tmp_path / "a.png").exists() and (work / "notes.txt").read_text() == "keep me"
