@@ -164,6 +164,11 @@ def write_quantized_dir(sd_or_dir, out_dir: str | Path, spec: QuantSpec, *, conf
     from safetensors.torch import save_file
 
     out = Path(out_dir)
+    if out.is_symlink() or (out.exists() and not out.is_dir()):
+        raise ValueError(f"{out} exists and is not a directory this writer may replace")
+    if out.is_dir() and any(out.iterdir()) and not (out / MANIFEST).is_file():
+        # only an earlier quantized checkpoint (or an empty directory) is replaced
+        raise ValueError(f"{out} holds files that are not a quantized checkpoint; choose another --out")
     tmp = out.parent / f".{out.name}.tmp{os.getpid()}"
     if tmp.exists():
         shutil.rmtree(tmp)

@@ -76,6 +76,14 @@ def test_writer_reader_roundtrip(tmp_path):
     assert torch.equal(back[k], fake_quant(sd[k]))
     k = "transformer_blocks.0.attn.to_out.0.weight"
     assert torch.equal(back[k], sd[k])
+    # an earlier quantized checkpoint is replaced; a directory holding anything else is refused
+    assert qc.write_quantized_dir(sd, out, spec) == out
+    other = tmp_path / "mine"
+    other.mkdir()
+    (other / "notes.txt").write_text("keep")
+    with pytest.raises(ValueError):
+        qc.write_quantized_dir(sd, other, spec)
+    assert (other / "notes.txt").read_text() == "keep"
 
 
 def test_writer_refuses_dead_and_fused_patterns():
