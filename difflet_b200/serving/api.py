@@ -363,7 +363,12 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
                 job = jobs.cancel(vid)
                 if job.status not in TERMINAL:
                     return {"id": vid, "object": "video.deleted", "deleted": False, "status": job.status}
-            jobs.delete(vid)
+            from difflet_b200.serving.video_jobs import VideoJobNotFound
+
+            try:
+                jobs.delete(vid)
+            except VideoJobNotFound:  # deleted meanwhile (the retention sweep or another client)
+                raise HTTPException(404, "no such video")
             return {"id": vid, "object": "video.deleted", "deleted": True}
 
     app.state.jobs = jobs

@@ -235,7 +235,10 @@ class ImmutableArtifacts:
         trash.mkdir(exist_ok=True)
         with self._locked(name):
             dst = trash / uuid.uuid4().hex
-            os.rename(base, dst)
+            try:
+                os.rename(base, dst)
+            except FileNotFoundError:  # a concurrent delete (the retention sweep) got there first
+                return False
             _fsync_dir(self.root)
         shutil.rmtree(dst, ignore_errors=True)
         return True
