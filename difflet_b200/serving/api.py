@@ -45,7 +45,7 @@ _GEN_KEYS = ("height", "width", "num_inference_steps", "seed", "guidance_scale",
 _ERROR_CODES = {400: ("invalid_request_error", "invalid_request"), 401: ("invalid_request_error", "invalid_api_key"),
                 404: ("invalid_request_error", "not_found"), 409: ("invalid_request_error", "conflict"),
                 422: ("invalid_request_error", "invalid_request"), 429: ("server_error", "server_busy"),
-                499: ("server_error", "request_cancelled"), 500: ("server_error", "internal_error"),
+                410: ("invalid_request_error", "gone"), 499: ("server_error", "request_cancelled"), 500: ("server_error", "internal_error"),
                 503: ("server_error", "unavailable")}
 # chat-completion fields an image generator cannot honour
 _CHAT_UNSUPPORTED = ("stream", "tools", "tool_choice", "functions", "function_call", "temperature", "top_p", "stop",
@@ -343,6 +343,10 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
                 from fastapi.responses import RedirectResponse
 
                 return RedirectResponse(job.url, status_code=307)
+            import os
+
+            if not job.path or not os.path.isfile(job.path):
+                raise ServingError(410, "the video file is no longer available", "gone")
             return FileResponse(job.path, media_type="video/x-msvideo")
 
         @app.post("/v1/videos/{vid}/cancel")

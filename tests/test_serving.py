@@ -91,6 +91,11 @@ def test_video_job_lifecycle(tmp_path):
     assert c.get(f"/v1/videos/{vid}").json()["status"] == "completed"
     data = c.get(f"/v1/videos/{vid}/content").content
     assert data[:4] == b"RIFF" and data[8:12] == b"AVI "
+    import os
+
+    os.unlink(c.app.state.jobs.get(vid).path)  # the file vanished behind the service's back
+    r = c.get(f"/v1/videos/{vid}/content")
+    assert r.status_code == 410 and r.json()["error"]["code"] == "gone"
 
 
 def test_errors_use_the_openai_envelope():
