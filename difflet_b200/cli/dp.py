@@ -20,16 +20,47 @@ from pathlib import Path
 from difflet_b200.cli.runner import die_with_parent
 
 
+def _pid_alive(pid: int) -> bool:
+    try:
+        os.kill(pid, 0)
+    except ProcessLookupError:
+        return False
+    except PermissionError:
+        return True
+    return True
+
+
+def _stale(claim: Path) -> bool:
+    """A claim whose worker no longer runs (a crashed or killed earlier batch)."""
+    try:
+        pid = int(claim.read_text().strip() or "0")
+    except (OSError, ValueError):
+        return False  # being written right now, or not ours to judge
+    return pid > 0 and not _pid_alive(pid)
+
+
 def try_claim(work: Path, i: int) -> bool:
+    """Claim request ``i`` (an exclusive create).  A rerun after a crash takes over the claims
+    whose worker is gone: the stale claim is renamed away first, so of several workers that
+    find it at once exactly one takes it over."""
     if (work / f"{i}.done").exists():
         return False
-    try:
-        fd = os.open(str(work / f"{i}.claim"), os.O_CREAT | os.O_EXCL | os.O_WRONLY, 0o644)
-    except FileExistsError:
-        return False
-    os.write(fd, str(os.getpid()).encode())
-    os.close(fd)
-    return True
+    claim = work / f"{i}.claim"
+    for _ in range(2):
+        try:
+            fd = os.open(str(claim), os.O_CREAT | os.O_EXCL | os.O_WRONLY, 0o644)
+        except FileExistsError:
+            if not _stale(claim):
+                return False
+            try:
+                os.rename(claim, work / f"{i}.claim.stale.{os.getpid()}")
+            except FileNotFoundError:
+                return False  # another worker took it over first
+            continue
+        os.write(fd, str(os.getpid()).encode())
+        os.close(fd)
+        return True
+    return False
 
 
 def mark(work: Path, i: int, ok: bool, info: dict | None = None) -> None:

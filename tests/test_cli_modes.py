@@ -145,3 +145,20 @@ def test_cache_listing_and_clean_selection(tmp_path, capsys):
     assert not (root / "wan").exists()
     assert main(["clean", "--cache-dir", str(root), "--all"]) == 0
     assert not (root / "flux").exists() and (outside / "keep.txt").exists()
+
+
+def test_dp_claims_of_a_dead_worker_are_taken_over(tmp_path):
+    """A rerun after a crash claims the requests whose worker is gone; a live worker's claim
+    and a finished request are left alone."""
+    from difflet_b200.cli.dp import try_claim
+
+    dead = subprocess.Popen([sys.executable, "-c", "pass"])
+    dead.wait()
+    (tmp_path / "0.claim").write_text(str(dead.pid))      # crashed earlier batch
+    (tmp_path / "1.claim").write_text(str(os.getpid()))   # still running
+    (tmp_path / "2.claim").write_text(str(dead.pid))
+    (tmp_path / "2.done").write_text("{}")
+    assert try_claim(tmp_path, 0) and (tmp_path / "0.claim").read_text() == str(os.getpid())
+    assert not try_claim(tmp_path, 0)  # now ours: not claimed twice
+    assert not try_claim(tmp_path, 1) and not try_claim(tmp_path, 2)
+    assert try_claim(tmp_path, 3)
