@@ -18,6 +18,17 @@ from difflet_b200.models.flux.pipeline import FluxApplication
 from difflet_b200.models.vae.autoencoder_kl import KLDecoder, KLDecoderConfig
 
 
+def _graph_default() -> bool:
+    """``DIFFLET_EXEC_MODE``: "graph" (default) replays the denoise step as a CUDA graph,
+    "eager" launches its kernels one by one (profiling, debugging)."""
+    from difflet_b200 import envs
+
+    mode = str(envs.DIFFLET_EXEC_MODE or "graph").lower()
+    if mode not in ("graph", "eager"):
+        raise ValueError(f"DIFFLET_EXEC_MODE must be graph or eager, got {mode!r}")
+    return mode == "graph"
+
+
 class FluxEngine:
     def __init__(self, *, entry, model_path, parallel, dtype, shape, backend, application_kwargs):
         self.entry = entry
@@ -105,7 +116,7 @@ class FluxEngine:
             text_encoder = load_text_encoder("flux", self.model_path, dev, self.dtype,
                                              max_sequence_length=256 if "schnell" in str(self.model_path).lower() else 512)
         self.app = FluxApplication(dit, vae, text_encoder=text_encoder,
-                                   use_cuda_graph=(self.backend == "cuda" and self.kw.get("cuda_graph", True)))
+                                   use_cuda_graph=(self.backend == "cuda" and self.kw.get("cuda_graph", _graph_default())))
         if self.kw.get("teacache_speedup"):
             from difflet_b200.pipeline.teacache import build_controller
 

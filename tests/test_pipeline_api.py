@@ -58,3 +58,18 @@ def test_parallel_config_rules():
     p = DiffletParallelConfig(tp_degree=2, cp_degree=2, cfg_parallel_enabled=True, cp_mode="ulysses")
     assert p.world_size == 8 and p.mesh_spec.rank_of(cfg=1, cp=1, tp=1) == 7
     assert p.to_cache_dict() == {"tp_degree": 2, "cp_degree": 2, "cfg_parallel_enabled": True, "cp_mode": "ulysses"}
+
+
+def test_exec_mode_selects_graph_or_eager(monkeypatch):
+    """``DIFFLET_EXEC_MODE`` decides whether the FLUX denoise step replays as a CUDA graph."""
+    import pytest as _pytest
+
+    from difflet_b200.models.flux.entry import _graph_default
+
+    monkeypatch.delenv("DIFFLET_EXEC_MODE", raising=False)
+    assert _graph_default() is True
+    monkeypatch.setenv("DIFFLET_EXEC_MODE", "eager")
+    assert _graph_default() is False
+    monkeypatch.setenv("DIFFLET_EXEC_MODE", "sometimes")
+    with _pytest.raises(ValueError):
+        _graph_default()
