@@ -74,3 +74,17 @@ def test_cache_key_semantics():
     assert cc.cache_key(_spec(parallel=DiffletParallelConfig(tp_degree=2))) != k0
     assert cc.cache_key(_spec(height=768)) != k0
     assert cc.cache_key(_spec(toolchain={"nvcc": "13.0"})) != k0
+
+
+def test_every_env_variable_is_read_somewhere():
+    """No variable in the env registry is declared and then ignored (a silently dead knob)."""
+    import re
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1] / "difflet_b200"
+    names = set(re.findall(r'"(DIFFLET_[A-Z0-9_]+)"\s*:', (root / "envs.py").read_text()))
+    assert names
+    other = "\n".join(p.read_text() for p in root.rglob("*.py") if p.name != "envs.py")
+    other += (root.parent / "bench.py").read_text()
+    dead = sorted(n for n in names if n not in other)
+    assert not dead, dead
