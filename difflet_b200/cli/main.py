@@ -491,6 +491,9 @@ def main(argv=None) -> int:
         from difflet_b200.cli.modes import apply_mode
 
         apply_mode(a)
+        if getattr(a, "torch_compile", False):
+            print("difflet: --torch-compile has no effect here: the hot ops are sm_100a kernels and the "
+                  "denoise step already replays as a CUDA graph", file=sys.stderr)
     if a.cmd == "download":
         from difflet_b200.pipeline.path_resolver import resolve_model_path
         from difflet_b200.registry import resolve_model

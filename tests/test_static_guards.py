@@ -88,3 +88,18 @@ def test_every_env_variable_is_read_somewhere():
     other += (root.parent / "bench.py").read_text()
     dead = sorted(n for n in names if n not in other)
     assert not dead, dead
+
+
+def test_every_cli_flag_is_read_somewhere():
+    """Every flag the CLI parses is read by some code path (no silently ignored flags)."""
+    import re
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1] / "difflet_b200"
+    flags = set(re.findall(r'add_argument\("--([a-z0-9-]+)"', (root / "cli" / "main.py").read_text()))
+    assert flags
+    pkg = "\n".join(p.read_text() for p in root.rglob("*.py"))
+    dead = sorted(f for f in flags if not any(p in pkg for p in (f"a.{f.replace('-', '_')}",
+                                                                   f"args.{f.replace('-', '_')}",
+                                                                   f'"{f.replace("-", "_")}"')))
+    assert not dead, dead
