@@ -168,11 +168,21 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
     async def validation_error(request: Request, exc: RequestValidationError):
         return JSONResponse(status_code=400, content=error_payload(400, str(exc.errors())[:2000]))
 
+    import hashlib
+    import hmac
+
+    key_digest = hashlib.sha256(api_key.encode()).digest() if api_key else None
+
     @app.middleware("http")
     async def auth(request: Request, call_next):
-        if api_key and request.url.path.startswith("/v1/"):
-            got = request.headers.get("authorization", "")
-            if got != f"Bearer {api_key}":
+        """Bearer-token check on the versioned routes (health and readiness stay open for
+        probes; CORS preflights pass).  The token is compared by digest in constant time."""
+        path = request.url.path
+        if key_digest is not None and request.method != "OPTIONS" and (path == "/v1" or path.startswith("/v1/")):
+            scheme, _, token = request.headers.get("authorization", "").partition(" ")
+            ok = scheme.lower() == "bearer" and hmac.compare_digest(
+                hashlib.sha256(token.strip().encode()).digest(), key_digest)
+            if not ok:
                 return JSONResponse(status_code=401, content=error_payload(401, "invalid api key"))
         return await call_next(request)
 

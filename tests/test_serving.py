@@ -33,6 +33,18 @@ def test_chat_completion_image_and_auth():
     assert r.status_code == 200 and r.json()["data"][0]["b64_json"]
 
 
+def test_api_key_check():
+    """The key guards /v1 and everything under it (scheme case-insensitive); probes stay open."""
+    c = TestClient(create_app(InProcessEngine(_img), "flux", api_key="s3cret"))
+    assert c.get("/health").status_code == 200 and c.get("/ready").status_code == 200
+    assert c.get("/v1/models").status_code == 401
+    assert c.get("/v1").status_code == 401
+    assert c.get("/v1/models", headers={"Authorization": "Bearer wrong"}).status_code == 401
+    assert c.get("/v1/models", headers={"Authorization": "s3cret"}).status_code == 401
+    assert c.get("/v1/models", headers={"Authorization": "bearer s3cret"}).status_code == 200
+    assert c.get("/v1/models", headers={"Authorization": "Bearer s3cret"}).json()["data"][0]["id"] == "flux"
+
+
 def test_request_fields_are_checked_before_queueing():
     """Malformed sizes and out-of-range values answer 400 with a stable code; nothing runs."""
     calls = []
