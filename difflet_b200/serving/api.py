@@ -124,6 +124,10 @@ def normalize_chat_request(payload: dict) -> dict:
     if payload.get("n") not in (None, 1):
         raise ServingError(400, "one image per request (n = 1)", "feature_not_supported")
     msgs = payload.get("messages") or []
+    if not isinstance(msgs, list) or not all(isinstance(m, dict) for m in msgs):
+        raise ServingError(400, "messages must be a list of message objects", "invalid_request")
+    if payload.get("extra_body") is not None and not isinstance(payload["extra_body"], dict):
+        raise ServingError(400, "extra_body must be an object", "invalid_extra_body")
     prompt = None
     for m in reversed(msgs):
         if m.get("role") == "user":

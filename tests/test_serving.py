@@ -127,6 +127,9 @@ def test_errors_use_the_openai_envelope():
     r = c.post("/v1/chat/completions", headers=h, json={"messages": [{"role": "system", "content": "x"}]})
     assert r.status_code == 400 and r.json()["error"]["code"] == "invalid_prompt"
     assert not calls
+    for body in ({"messages": "a cat"}, {"messages": ["a cat"]}, {"messages": msgs, "extra_body": "x"}):
+        r = c.post("/v1/chat/completions", headers=h, json=body)
+        assert r.status_code == 400 and r.json()["error"]["code"] in ("invalid_request", "invalid_extra_body")
     r = c.post("/v1/requests/nope/cancel", headers=h)
     assert r.status_code == 404 and r.json()["error"]["code"] == "not_found"
     assert c.post("/v1/chat/completions", headers=h, json={"messages": msgs, "stream": False}).status_code == 200
