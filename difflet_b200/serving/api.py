@@ -288,7 +288,14 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
                 if k in payload:
                     req[k] = payload[k]
             if "seconds" in payload and "num_frames" not in req:
-                req["num_frames"] = int(float(payload["seconds"]) * 16) // 4 * 4 + 1
+                sec = payload["seconds"]
+                try:
+                    sec = float(sec)
+                except (TypeError, ValueError):
+                    raise ServingError(400, f"seconds must be a number, got {sec!r}", "invalid_request") from None
+                if not 0 < sec <= 60:
+                    raise ServingError(400, f"seconds must be in (0, 60], got {sec}", "invalid_request")
+                req["num_frames"] = int(sec * 16) // 4 * 4 + 1
             _validate(req)
             return req
 

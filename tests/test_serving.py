@@ -157,7 +157,11 @@ def test_video_sync_returns_the_encoded_video():
     assert c.post("/v1/videos/sync", json={"prompt": "fail"}).status_code == 500
     n = len(calls)
     assert c.post("/v1/videos/sync", json={"size": "16x16"}).status_code == 400
+    for sec in ("soon", -1, 600):
+        assert c.post("/v1/videos/sync", json={"prompt": "waves", "size": "16x16", "seconds": sec}).status_code == 400
     assert len(calls) == n
+    assert c.post("/v1/videos/sync", json={"prompt": "waves", "size": "16x16", "seconds": 2}).status_code == 200
+    assert calls[-1]["num_frames"] == 33
 
 
 # --- resident worker (spawned process) with fake runners ---------------------------------
