@@ -235,7 +235,12 @@ def create_app(engine, model_id: str, *, output: str = "image", api_key: str | N
         except RequestCancelled as exc:
             raise HTTPException(499, str(exc))
         except EngineError as exc:
-            raise HTTPException(500, str(exc)[-2000:])
+            # the engine's message can hold paths and tracebacks: logged here, not sent to clients
+            import logging
+
+            logging.getLogger("difflet_b200.serving.api").error("request %s failed: %s", request_id, str(exc)[-4000:])
+            raise ServingError(500, "internal model execution error"
+                               + (f" (request {request_id})" if request_id else ""), "internal_error")
 
     @app.post("/v1/requests/{rid}/cancel")
     async def cancel_request(rid: str):

@@ -154,7 +154,9 @@ def test_video_sync_returns_the_encoded_video():
     assert r.headers["x-request-id"] == "req-7" and r.headers["x-model"] == "wan"
     assert float(r.headers["x-inference-time-s"]) >= 0.0
     assert calls[-1]["num_frames"] == 9 and calls[-1]["width"] == 16
-    assert c.post("/v1/videos/sync", json={"prompt": "fail"}).status_code == 500
+    r = c.post("/v1/videos/sync", json={"prompt": "fail"})
+    assert r.status_code == 500 and r.json()["error"]["code"] == "internal_error"
+    assert "worker died" not in r.text  # engine internals stay in the server log
     n = len(calls)
     assert c.post("/v1/videos/sync", json={"size": "16x16"}).status_code == 400
     for sec in ("soon", -1, 600):
