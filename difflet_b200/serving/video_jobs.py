@@ -354,8 +354,12 @@ class VideoJobStore:
                 cancelled = type(exc).__name__ in ("RequestCancelled",) or "cancelled" in str(exc).lower()
                 timed_out = vid in self._timed_out
                 to = "failed" if timed_out or not cancelled else "cancelled"
+                if not (timed_out or cancelled):  # the detail stays in the server log
+                    import logging
+
+                    logging.getLogger("difflet_b200.serving.video").error("video %s failed: %r", vid, exc)
                 err = (f"timed out after {self.request_timeout_s:g} s" if timed_out
-                       else None if cancelled else repr(exc))
+                       else None if cancelled else f"generation failed: {type(exc).__name__}")
                 try:
                     self.repo.transition(vid, to, expect="in_progress", error=err)
                 except InvalidTransition:
